@@ -1,0 +1,446 @@
+"""The eagle-shaped Python face of the B200 engine.
+
+Mirrors the until-done surface of eagle (paths relative to the eagle source tree):
+
+* :func:`simulate` / :class:`SimResult` -- python/eagle/_simulate.py:451-483, :777
+  (bind the model's planes like a call, allocate the ``terminated`` mask, run until
+  every sample finishes or ``max_steps``; ``status`` is ``"finished"`` or ``"max_steps"``);
+* :func:`until_done` / :class:`Runner` / :class:`RunReport` -- python/eagle/_until_done.py:120-171,
+  :528, :1775 (``run()`` continues from the current mask and state, ``reset()`` clears
+  the mask);
+* :func:`reduce` -- python/eagle/_graph_reduce.py:98 (the canonical reduction);
+* :func:`compact` / :func:`mask_count` -- python/eagle/_active_set.py:482-525 and
+  _until_done.py:374-387.
+
+Planes are torch CUDA tensors (the engine works on them in place) or host arrays
+(numpy / CPU tensors), which are staged through the device and written back. Every
+computation runs in ``libeagle_b200.so`` on the GPU; there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import time
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _abi
+
+_torch = None
+
+
+def _t():
+    global _torch
+    if _torch is None:
+        import torch
+
+        _torch = torch
+    return _torch
+
+
+def _stream_handle(stream=None) -> int:
+    torch = _t()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def _ptr(x) -> int:
+    return int(x.data_ptr())
+
+
+# ------------------------------------------------------------------------- models
+
+@dataclass(frozen=True)
+class Model:
+    """A built-in step body: its plane and Param names in the engine's order."""
+
+    name: str
+    planes: tuple      # per-sample planes, read-only first then mutable
+    mutable: tuple
+    params: tuple
+
+
+class _Oscillator(Model):
+    """The Euler oscillator of eagle's README (README.md:89-97)::
+
+        x = x0 + dt * v0; v = v0 - dt * omega * omega * x0; t += dt; terminated = t >= t_end
+
+    ``t_end`` may be a number (a Param) or a per-sample plane."""
+
+
+oscillator = _Oscillator(name="oscillator", planes=("omega", "t_end", "x", "v", "t"), mutable=("x", "v", "t"),
+                         params=("t_end", "dt"))
+
+_MODES = {"band": _abi.MODE_BAND, "persist": _abi.MODE_PERSIST, "fused": _abi.MODE_FUSED}
+
+
+# ------------------------------------------------------------------------- reports
+
+@dataclass(frozen=True)
+class RunReport:
+    """What one :meth:`Runner.run` did (python/eagle/_until_done.py:120-171).
+
+    ``finished`` counts set mask bytes at the end, ``done`` is ``finished == n``,
+    ``steps`` the longest sample's steps in this run (exact), ``launches`` the loop
+    passes, ``compactions`` the compactions run, ``step_sum`` the steps executed."""
+
+    n: int
+    finished: int
+    done: bool
+    steps: int
+    launches: int
+    compactions: int
+    step_sum: int
+    mode: str
+    exact_steps: bool = True
+
+
+class SimResult:
+    """What one :meth:`Simulation.run` produced (python/eagle/_simulate.py:451-483):
+    ``state`` maps each mutable plane to its array; each is also an attribute and an
+    item. ``finished`` is the mask, ``done``/``status``/``steps``/``report``/``wall_s``."""
+
+    __slots__ = ("state", "finished", "done", "steps", "status", "report", "n", "wall_s")
+
+    def __init__(self, *, state, finished, report, wall_s):
+        put = object.__setattr__
+        put(self, "state", dict(state))
+        put(self, "finished", finished)
+        put(self, "report", report)
+        put(self, "done", bool(report.done))
+        put(self, "steps", int(report.steps))
+        put(self, "status", "finished" if report.done else "max_steps")
+        put(self, "n", int(report.n))
+        put(self, "wall_s", float(wall_s))
+
+    def __setattr__(self, name, value):
+        raise AttributeError("a SimResult is read-only")
+
+    def __getattr__(self, name):
+        state = object.__getattribute__(self, "state")
+        if name in state:
+            return state[name]
+        raise AttributeError(f"the result has no field or state plane {name!r} (state: {sorted(state)})")
+
+    def __getitem__(self, name):
+        return self.state[name]
+
+    def __repr__(self) -> str:
+        return f"SimResult(status={self.status!r}, n={self.n}, steps={self.steps}, state={list(self.state)})"
+
+
+# ------------------------------------------------------------------------- runner
+
+def _as_device_plane(name, value, n, device, *, staged):
+    """A contiguous float64 CUDA tensor for ``value``; host arrays are staged
+    (copied in, and remembered in ``staged`` for the copy back)."""
+    torch = _t()
+    if isinstance(value, torch.Tensor) and value.is_cuda:
+        if value.dtype != torch.float64 or not value.is_contiguous() or value.numel() != n:
+            raise ValueError(f"plane {name!r} must be a contiguous float64 tensor of {n} samples")
+        return value
+    host = torch.as_tensor(np.asarray(value) if not isinstance(value, torch.Tensor) else value)
+    if host.dtype != torch.float64 or host.numel() != n:
+        raise ValueError(f"plane {name!r} must hold {n} float64 samples")
+    dev = host.reshape(-1).to(device, non_blocking=True)
+    staged.append((name, value, dev))
+    return dev
+
+
+class Runner:
+    """The until-done loop of one model over one batch (python/eagle/_until_done.py:528).
+
+    ``run()`` runs every live sample until it terminates or has taken ``max_steps``
+    steps in this run and returns a :class:`RunReport`; a second ``run()`` continues
+    from the current mask and state; ``reset()`` clears the mask. ``mode`` picks the
+    schedule: ``"band"`` (one CUDA graph: WHILE over the fused step + compaction
+    kernel), ``"persist"`` (one persistent launch) or ``"fused"`` (one lane per sample,
+    one launch); ``"auto"`` takes ``"band"``. All modes leave identical bits. ``fma``
+    contracts the model's multiply-adds as a device compiler does by default."""
+
+    def __init__(self, model: Model, *, max_steps: int, mode: str = "auto", fma: bool = False, terminated=None,
+                 device=None, k_first: int = 0, k_min: int = 0, k_max: int = 0, chunk: int = 0,
+                 overhead_steps: float = 0.0, interval_steps: float = 0.0, **planes):
+        torch = _t()
+        if model is not oscillator:
+            raise ValueError(f"eagle_b200: unknown model {model!r}")
+        if max_steps is None or int(max_steps) < 0:
+            raise ValueError("max_steps must be >= 0")
+        mode = "band" if mode == "auto" else mode
+        if mode not in _MODES:
+            raise ValueError(f"mode must be one of {sorted(_MODES)} or 'auto'")
+        missing = {"omega", "t_end", "dt", "x", "v", "t"} - set(planes)
+        if missing:
+            raise TypeError(f"oscillator needs {sorted(missing)}")
+        extra = set(planes) - {"omega", "t_end", "dt", "x", "v", "t"}
+        if extra:
+            raise TypeError(f"oscillator takes no plane(s) {sorted(extra)}")
+        n = int(np.asarray(planes["omega"]).size) if not isinstance(planes["omega"], torch.Tensor) \
+            else planes["omega"].numel()
+        self.device = torch.device(device) if device is not None else (
+            planes["x"].device if isinstance(planes["x"], torch.Tensor) and planes["x"].is_cuda
+            else torch.device("cuda", torch.cuda.current_device()))
+        self._staged = []
+        self.n = n
+        self.mode = mode
+        self.max_steps = int(max_steps)
+        self.fma = bool(fma)
+        spread = not np.isscalar(planes["t_end"]) and not (isinstance(planes["t_end"], torch.Tensor)
+                                                           and planes["t_end"].dim() == 0)
+        self.spread = spread
+        dev_planes = {}
+        for name in ("omega", "x", "v", "t") + (("t_end",) if spread else ()):
+            dev_planes[name] = _as_device_plane(name, planes[name], n, self.device, staged=self._staged)
+        self.planes = dev_planes
+        if terminated is None:
+            terminated = torch.zeros(n, dtype=torch.bool, device=self.device)
+        elif not (isinstance(terminated, torch.Tensor) and terminated.is_cuda):
+            raise ValueError("terminated must be a CUDA tensor (bool or uint8)")
+        if terminated.dtype not in (torch.bool, torch.uint8) or not terminated.is_contiguous():
+            raise ValueError("terminated must be a contiguous bool/uint8 CUDA tensor")
+        self.terminated = terminated
+        d = _abi.new(_abi.EngineDesc)
+        d.flags = _abi.FLAG_FMA if self.fma else 0
+        d.device = self.device.index if self.device.index is not None else -1
+        d.model = _abi.MODEL_OSCILLATOR_SPREAD if spread else _abi.MODEL_OSCILLATOR
+        d.mode = _MODES[mode]
+        d.n = n
+        d.max_steps = self.max_steps
+        order = ("omega", "t_end", "x", "v", "t") if spread else ("omega", "x", "v", "t")
+        for i, name in enumerate(order):
+            d.planes[i] = _ptr(dev_planes[name])
+        if spread:
+            d.uniforms[0] = float(planes["dt"])
+        else:
+            d.uniforms[0] = float(planes["t_end"])
+            d.uniforms[1] = float(planes["dt"])
+        d.terminated = _ptr(terminated)
+        d.k_first, d.k_min, d.k_max, d.chunk = int(k_first), int(k_min), int(k_max), int(chunk)
+        d.overhead_steps, d.interval_steps = float(overhead_steps), float(interval_steps)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _abi.check(_abi.lib().eagle_backend_x_b200_engine_create(ctypes.byref(d), ctypes.byref(h)))
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                _abi.lib().eagle_backend_x_b200_engine_release(h)
+            except Exception:
+                pass
+            self._h = None
+
+    def launch(self, stream=None) -> None:
+        """Enqueue one run on ``stream`` (default: torch's current stream); no sync."""
+        torch = _t()
+        with torch.cuda.device(self.device):
+            _abi.check(_abi.lib().eagle_backend_x_b200_engine_launch(self._h, _stream_handle(stream)))
+
+    def report(self, stream=None) -> RunReport:
+        """Wait for ``stream`` and read the last run's report (one small copy)."""
+        torch = _t()
+        r = _abi.new(_abi.Report)
+        with torch.cuda.device(self.device):
+            _abi.check(_abi.lib().eagle_backend_x_b200_engine_report(self._h, _stream_handle(stream),
+                                                                     ctypes.byref(r)))
+        return RunReport(n=int(r.n), finished=int(r.finished), done=bool(r.done), steps=int(r.steps),
+                         launches=int(r.launches), compactions=int(r.compactions), step_sum=int(r.step_sum),
+                         mode=self.mode)
+
+    def run(self, stream=None) -> RunReport:
+        self.launch(stream)
+        rep = self.report(stream)
+        self._copy_back(stream)
+        return rep
+
+    def reset(self) -> None:
+        """Clear the mask: every sample is live again (its state is kept)."""
+        self.terminated.zero_()
+
+    def _copy_back(self, stream=None) -> None:
+        torch = _t()
+        for name, host, dev in self._staged:
+            if name in ("x", "v", "t"):
+                if isinstance(host, torch.Tensor):
+                    host.copy_(dev.reshape(host.shape))
+                else:
+                    np.copyto(host, dev.cpu().numpy().reshape(np.shape(host)))
+
+
+def until_done(model: Model, *, max_steps: int, **kwargs) -> Runner:
+    """The :class:`Runner` of ``model`` over the given planes (python/eagle/_until_done.py:1775)."""
+    return Runner(model, max_steps=max_steps, **kwargs)
+
+
+def simulate(model: Model, *, max_steps: int, mode: str = "auto", fma: bool = False, **planes) -> SimResult:
+    """Run ``model`` on every sample until each finishes or ``max_steps`` (python/eagle/_simulate.py:777).
+
+    ``planes`` bind the model's arguments by name (numbers for Params, arrays for
+    per-sample planes); the mutable planes are updated in place and returned in the
+    :class:`SimResult` together with the ``finished`` mask."""
+    t0 = time.perf_counter()
+    runner = Runner(model, max_steps=max_steps, mode=mode, fma=fma, **planes)
+    report = runner.run()
+    wall = time.perf_counter() - t0
+    state = {}
+    for name in model.mutable:
+        host = planes[name]
+        state[name] = host if not (hasattr(host, "is_cuda") and host.is_cuda) else runner.planes[name]
+    return SimResult(state=state, finished=runner.terminated, report=report, wall_s=wall)
+
+
+# ------------------------------------------------------------------------- reduction
+
+_REDUCE_DTYPES = None
+
+
+def _reduce_dtype(x):
+    torch = _t()
+    global _REDUCE_DTYPES
+    if _REDUCE_DTYPES is None:
+        _REDUCE_DTYPES = {torch.float32: _abi.REDUCE_F32, torch.float64: _abi.REDUCE_F64,
+                          torch.int32: _abi.REDUCE_I32, torch.int64: _abi.REDUCE_I64, torch.uint8: _abi.REDUCE_U8,
+                          torch.bool: _abi.REDUCE_U8}
+    if x.dtype not in _REDUCE_DTYPES:
+        raise TypeError(f"eagle_b200.reduce: dtype {x.dtype} is not reducible")
+    return _REDUCE_DTYPES[x.dtype]
+
+
+_OPS = {"sum": _abi.REDUCE_OP_SUM, "max": _abi.REDUCE_OP_MAX, "all": _abi.REDUCE_OP_ALL, "min": _abi.REDUCE_OP_MIN}
+_POLICIES = {"compensated": _abi.REDUCE_COMPENSATED, "ordered": _abi.REDUCE_ORDERED, "auto": _abi.REDUCE_AUTO}
+
+
+class Reducer:
+    """A prepared canonical reduction of one (n, columns) CUDA plane: work buffers
+    allocated once (the seam's query), so :meth:`__call__` only enqueues (and can be
+    captured in a CUDA graph)."""
+
+    def __init__(self, x, op: str = "sum", *, policy: str = "ordered", comp=None, pair_out: bool = False,
+                 out=None):
+        torch = _t()
+        if not (isinstance(x, torch.Tensor) and x.is_cuda and x.is_contiguous()):
+            raise ValueError("eagle_b200.reduce takes a contiguous CUDA tensor")
+        self.x = x
+        n = x.shape[0] if x.dim() > 0 else 1
+        cols = x.numel() // n if n else 1
+        d = _abi.new(_abi.ReduceDesc)
+        d.dtype = _reduce_dtype(x)
+        d.op = _OPS[op]
+        d.device = x.device.index
+        d.n = n
+        d.policy = _POLICIES[policy]
+        d.flags = _abi.REDUCE_PAIR_OUT if pair_out else 0
+        d.columns = cols
+        self.comp = comp
+        if comp is not None:
+            d.comp_in = _ptr(comp)
+        _abi.check(_abi.lib().eagle_backend_x_reduce_canonical(ctypes.byref(d)))  # query
+        elem = x.element_size()
+        self.work_a = torch.empty(int(d.work_elems) * elem, dtype=torch.uint8, device=x.device)
+        self.work_b = torch.empty(int(d.work_elems) * elem, dtype=torch.uint8, device=x.device)
+        self.out = out if out is not None else torch.empty(cols * (2 if pair_out else 1), dtype=x.dtype,
+                                                           device=x.device)
+        d.in_ = _ptr(x)
+        d.out = _ptr(self.out)
+        d.work_a = _ptr(self.work_a)
+        d.work_b = _ptr(self.work_b)
+        self.desc = d
+
+    def __call__(self, stream=None):
+        self.desc.stream = _stream_handle(stream)
+        _abi.check(_abi.lib().eagle_backend_x_reduce_canonical(ctypes.byref(self.desc)))
+        return self.out
+
+
+def reduce(x, op: str = "sum", *, policy: str = "ordered", comp=None, pair_out: bool = False, stream=None):
+    """The canonical reduction of each column of the CUDA plane ``x`` (python/eagle/_graph_reduce.py:98):
+    a tensor of ``columns`` results (``2 * columns`` with ``pair_out``: hi then comp)."""
+    return Reducer(x, op, policy=policy, comp=comp, pair_out=pair_out)(stream)
+
+
+# ------------------------------------------------------------------------- filtering
+
+class Compactor:
+    """A prepared active-set compaction of an ``n``-sample mask (scratch from the
+    seam's query, allocated once): :meth:`__call__` only enqueues."""
+
+    def __init__(self, mask, *, drop: bool = True, trigger: bool = False, theta: float = 0.5, span=None):
+        torch = _t()
+        if not (isinstance(mask, torch.Tensor) and mask.is_cuda and mask.dtype in (torch.bool, torch.uint8)):
+            raise ValueError("compact takes a bool/uint8 CUDA mask")
+        n = mask.numel()
+        dev = mask.device
+        self.mask = mask
+        self.index_map = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+        self.count = torch.zeros(1, dtype=torch.int32, device=dev)
+        d = _abi.new(_abi.CompactDesc)
+        d.flags = _abi.COMPACT_MASK_IS_DROP if drop else 0
+        d.device = dev.index
+        d.n = n
+        _abi.check(_abi.lib().eagle_backend_compact_device(ctypes.byref(d)))  # query
+        self.scratch = torch.empty(max(int(d.scratch_bytes), 1), dtype=torch.uint8, device=dev)
+        d.mask = _ptr(mask)
+        d.index_map = _ptr(self.index_map)
+        d.count = _ptr(self.count)
+        d.scratch = _ptr(self.scratch)
+        self.trigger = trigger
+        if trigger:
+            self.live32 = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.fire = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.span = span if span is not None else torch.full((1,), n, dtype=torch.int32, device=dev)
+            d.live32, d.fire, d.span = _ptr(self.live32), _ptr(self.fire), _ptr(self.span)
+            d.theta = float(theta)
+        self.desc = d
+
+    def __call__(self, stream=None):
+        self.desc.stream = _stream_handle(stream)
+        _abi.check(_abi.lib().eagle_backend_compact_device(ctypes.byref(self.desc)))
+        return self.index_map, self.count
+
+
+def compact(mask, *, drop: bool = True, stream=None):
+    """``(index_map, count)``: the ascending indices of the samples ``mask`` keeps
+    (``drop=True``: the unset bytes, a ``terminated`` mask). ``index_map[:count]`` is
+    valid; ``count`` is a one-element device tensor."""
+    return Compactor(mask, drop=drop)(stream)
+
+
+def mask_count(mask, cell=None, stream=None):
+    """``cell[0] = number of set bytes of mask`` (memset, then the MASK_COUNT cell op)."""
+    torch = _t()
+    if cell is None:
+        cell = torch.zeros(1, dtype=torch.int32, device=mask.device)
+    s = _stream_handle(stream)
+    _abi.check(_abi.lib().eagle_backend_memset_device(_ptr(cell), 4, s))
+    d = _abi.new(_abi.CellOpDesc)
+    d.op = _abi.CELL_MASK_COUNT
+    d.device = mask.device.index
+    d.stream = s
+    d.n = mask.numel()
+    d.p[0] = _ptr(mask)
+    d.p[1] = _ptr(cell)
+    _abi.check(_abi.lib().eagle_backend_cell_op(ctypes.byref(d)))
+    return cell
+
+
+def cell_op(op: int, n: int, pointers, ints=(), device: int = -1, stream=None) -> None:
+    """Enqueue one of the seam's built-in cell ops (BUMP, MASK_COUNT, POLICY, ...)."""
+    d = _abi.new(_abi.CellOpDesc)
+    d.op = int(op)
+    d.device = int(device)
+    d.stream = _stream_handle(stream)
+    d.n = int(n)
+    for k, p in enumerate(pointers):
+        d.p[k] = int(p)
+    for k, v in enumerate(ints):
+        d.i[k] = int(v)
+    _abi.check(_abi.lib().eagle_backend_cell_op(ctypes.byref(d)))
+
+
+def entry(name: str, device: int = -1) -> int:
+    """The raw CUfunction handle of a built-in step entry (for run_device / launch_raw)."""
+    f = ctypes.c_uint64()
+    _abi.check(_abi.lib().eagle_backend_x_b200_entry(name.encode(), int(device), ctypes.byref(f)))
+    return int(f.value)

@@ -1,0 +1,449 @@
+// Active-set compaction and the until-done loop's cell ops, on B200.
+//
+// compact_device keeps eagle's contract (eagle/filtering/Compact.h:23-47,
+// python/src/seam/eagle_backend.h:666-701): index_map[0, count) = the kept sample
+// indices, ascending; count; optionally the reorder trigger (live32, fire) of
+// Compact.h:113-118. Eagle runs predicate -> multi-level int64 scan -> scatter
+// (about 2 log256(n) + 2 launches over 8-byte planes). Here it is ONE kernel
+// after a memset of its scratch: each CTA takes the next 4096-sample tile off a
+// counter (so every tile it waits on is already owned by a running CTA), turns
+// 16 mask bytes per thread into a keep bit-set, scans the counts across the CTA,
+// finds the tile's global offset by a decoupled look-back over the earlier
+// tiles' status words, stages the kept indices in shared memory and writes them
+// with coalesced stores. The trigger's live32 rides in the same status words, so
+// the last tile alone knows count and live32 and writes count, live32 and fire.
+#include "common.cuh"
+
+namespace eb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kPer = 16;
+constexpr int64_t kTile = int64_t(kThreads) * kPer;
+
+struct CompactArgs {
+    const uint8_t* mask;
+    int64_t n;
+    int32_t* map;
+    uint32_t* count;
+    uint64_t* status;      // one word per tile, zero on entry
+    uint32_t* tileNext;    // zero on entry
+    uint32_t* err;         // zero on entry
+    uint32_t* live32;      // trigger outputs (Trigger only)
+    const uint32_t* span;
+    uint32_t* fire;
+    float theta;
+    uint32_t tiles;
+};
+
+/** Keep bits of 16 consecutive mask bytes starting at sample ``i0``. */
+template <bool Drop, bool Aligned>
+__device__ __forceinline__ uint32_t keepBits(const uint8_t* __restrict__ mask, int64_t i0, int64_t n)
+{
+    uint32_t set = 0;  // bit j: mask byte i0 + j is non-zero
+    if (Aligned && i0 + kPer <= n) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(mask + i0));
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t nz = __vcmpne4(words[q], 0u);  // 0xff per non-zero byte
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                set |= ((nz >> (8 * b)) & 1u) << (4 * q + b);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+            if (i0 + j < n && mask[i0 + j] != 0)
+                set |= 1u << j;
+    }
+    const uint32_t valid = i0 >= n ? 0u : (i0 + kPer <= n ? 0xffffu : ((1u << uint32_t(n - i0)) - 1u));
+    return (Drop ? ~set : set) & valid;
+}
+
+template <bool Drop, bool Trigger, bool Aligned>
+__global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
+{
+    __shared__ uint32_t sTile;
+    __shared__ uint32_t scan[33];
+    __shared__ uint64_t sPrefix;
+    __shared__ int32_t stage[kTile];
+    const int t = int(threadIdx.x);
+    if (t == 0)
+        sTile = atomicAdd(a.tileNext, 1u);
+    __syncthreads();
+    const uint32_t tile = sTile;
+    const int64_t i0 = int64_t(tile) * kTile + int64_t(t) * kPer;
+    const uint32_t bits = keepBits<Drop, Aligned>(a.mask, i0, a.n);
+    const uint32_t cnt = __popc(bits);
+    uint32_t total = 0;
+    const uint32_t excl = blockExclusiveSum(cnt, total, scan);
+    uint32_t groups = 0;
+    if constexpr (Trigger) {
+        // a 32-sample group is two neighbouring threads (tiles start on a multiple of 32)
+        const uint32_t pair = bits | __shfl_xor_sync(kFull, bits, 1);
+        const uint32_t mine = ((t & 1) == 0 && pair != 0) ? 1u : 0u;
+        blockExclusiveSum(mine, groups, scan);
+    }
+    const uint64_t payload = (uint64_t(groups) << 32) | uint64_t(total);
+    if (t < 32) {
+        uint64_t prefix = 0;
+        if (tile == 0) {
+            if (t == 0)
+                lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, payload);
+        } else {
+            if (t == 0)
+                lbPublish<PlainCodec>(a.status, tile, 0, kLbAggregate, payload);
+            prefix = lbExclusivePrefix<PlainCodec>(a.status, tile, 0, a.err);
+            if (t == 0)
+                lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, prefix + payload);
+        }
+        if (t == 0)
+            sPrefix = prefix;
+    }
+    // stage the kept indices of the tile in order
+    uint32_t k = excl;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+        if ((bits >> j) & 1u)
+            stage[k++] = int32_t(i0 + j);
+    __syncthreads();
+    const uint64_t prefix = sPrefix;
+    const uint32_t at = uint32_t(prefix);
+    for (uint32_t q = uint32_t(t); q < total; q += kThreads)
+        a.map[size_t(at) + q] = stage[q];
+    if (tile == a.tiles - 1 && t == 0) {
+        const uint32_t c = at + total;
+        const bool broken = *a.err != 0u;
+        *a.count = broken ? 0xffffffffu : c;  // a count above n reports a failed compaction
+        if constexpr (Trigger) {
+            const uint32_t live32 = uint32_t(prefix >> 32) + groups;
+            *a.live32 = live32;
+            const uint32_t span = *a.span;
+            const double limit = double(a.theta) * 32.0 * double(live32);
+            *a.fire = (double(c) < limit && c < span && span >= 4096u) ? 1u : 0u;
+        }
+    }
+}
+
+__global__ void compactEmptyKernel(uint32_t* count, uint32_t* live32, uint32_t* fire)
+{
+    *count = 0u;
+    if (live32 != nullptr) {
+        *live32 = 0u;
+        *fire = 0u;
+    }
+}
+
+template <bool Drop, bool Trigger>
+void launchCompact(const CompactArgs& a, bool aligned, cudaStream_t s)
+{
+    if (aligned)
+        compactKernel<Drop, Trigger, true><<<a.tiles, kThreads, 0, s>>>(a);
+    else
+        compactKernel<Drop, Trigger, false><<<a.tiles, kThreads, 0, s>>>(a);
+}
+
+size_t compactScratchBytes(int64_t n)
+{
+    const int64_t tiles = n > 0 ? (n + kTile - 1) / kTile : 1;
+    const size_t bytes = size_t(tiles) * sizeof(uint64_t) + 2 * sizeof(uint32_t);
+    return (bytes + 255) & ~size_t(255);
+}
+
+// ------------------------------------------------------------------- cell ops
+
+__global__ void bumpKernel(uint32_t* cell) { cell[0] += 1u; }
+
+/** ``cell += number of non-zero bytes``: 16 bytes per thread per step, one atomic per CTA. */
+template <bool Aligned>
+__global__ __launch_bounds__(256) void maskCountKernel(const uint8_t* __restrict__ mask, int64_t n, uint32_t* cell)
+{
+    __shared__ uint32_t part[8];
+    uint32_t c = 0;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x * 16;
+    for (int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 16; i < n; i += stride) {
+        if (Aligned && i + 16 <= n) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(mask + i));
+            c += __popc(__vcmpne4(w.x, 0u)) / 8 + __popc(__vcmpne4(w.y, 0u)) / 8 + __popc(__vcmpne4(w.z, 0u)) / 8
+                + __popc(__vcmpne4(w.w, 0u)) / 8;
+        } else {
+            for (int j = 0; j < 16 && i + j < n; ++j)
+                c += mask[i + j] != 0 ? 1u : 0u;
+        }
+    }
+    c = warpSum(c);
+    if ((threadIdx.x & 31) == 0)
+        part[threadIdx.x >> 5] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t s = 0;
+        for (int w = 0; w < int(blockDim.x >> 5); ++w)
+            s += part[w];
+        if (s != 0)
+            atomicAdd(cell, s);
+    }
+}
+
+__global__ void identityKernel(int32_t* a, int64_t n)
+{
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        a[i] = int32_t(i);
+}
+
+__global__ void countFiredKernel(const uint32_t* fire, uint32_t* reorders) { reorders[0] += fire[0] != 0u ? 1u : 0u; }
+
+__global__ void groupAndKernel(const uint8_t* m, uint8_t* d, int64_t lanes, int group, int64_t groups)
+{
+    for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < groups;
+         g += int64_t(gridDim.x) * blockDim.x) {
+        uint8_t all = 1;
+        const int64_t s = g * group;
+        for (int j = 0; j < group && s + j < lanes; ++j)
+            all &= uint8_t(m[s + j] != 0);
+        d[g] = all;
+    }
+}
+
+__global__ void scaleCountKernel(const uint32_t* c, uint32_t* o, int group) { o[0] = c[0] * uint32_t(group); }
+
+/** One step of the until-done band policy: eagle's POLICY cell op
+ *  (python/src/plugin/eagle_cuda.cu:1990-2025; bandK of eagle/policy/Launch.h:184-190),
+ *  the same expressions in the same order, so a host twin rounds identically. */
+__global__ void policyKernel(const uint32_t* finished, const uint32_t* total, int64_t* cells, int64_t* word,
+    uint32_t* go, int64_t* hist, int64_t kmin, int64_t kmax, int iK, int iFin, int iDone, int iCap, int iR,
+    int iMapped, int scale)
+{
+    const int64_t fin = finished[0], all = total[0];
+    const int64_t live = all - fin, newly = fin - cells[iFin];
+    const int64_t done = cells[iDone] + word[0];
+    cells[iMapped] += all - cells[iFin];
+    cells[iFin] = fin;
+    cells[iDone] = done;
+    const int64_t k = cells[iK];
+    const double rate = double(cells[iR]) / double(scale);
+    int64_t kNext = k;
+    if (newly <= 0) {
+        kNext = kmax;
+    } else {
+        const double e2 = 2.0 * rate * double(live) * double(k) / double(newly);
+        int64_t p = 1;
+        while (p < (INT64_C(1) << 30) && e2 >= 2.0 * double(p) * double(p))
+            p *= 2;
+        kNext = p < kmin ? kmin : (p > kmax ? kmax : p);
+    }
+    cells[iK] = kNext;
+    const int64_t left = cells[iCap] - done;
+    const uint32_t g = (fin != all) && (left > 0);
+    go[0] = g;
+    if (g) {
+        const int64_t w = kNext < left ? kNext : left;
+        word[0] = w;
+        hist[w] += 1;
+    }
+}
+
+__global__ void resetKernel(int32_t* perm, int32_t* inv, int32_t* map, uint32_t* count, uint32_t* span, int64_t n)
+{
+    const int64_t i0 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (int64_t i = i0; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        perm[i] = int32_t(i);
+        inv[i] = int32_t(i);
+        if (map != nullptr)
+            map[i] = int32_t(i);
+    }
+    if (i0 == 0) {
+        *count = uint32_t(n);
+        *span = uint32_t(n);
+    }
+}
+
+unsigned gridFor(int64_t n, int64_t perThread = 1)
+{
+    const int64_t threads = (n + perThread - 1) / perThread;
+    const int64_t blocks = (threads + 255) / 256;
+    const int64_t cap = int64_t(smCount()) * 16;
+    return unsigned(std::max<int64_t>(1, std::min(blocks, cap)));
+}
+
+void need(const eagle_backend_cell_op_desc& d, int pointers, const char* who)
+{
+    for (int k = 0; k < pointers; ++k)
+        if (d.p[k] == 0)
+            invalid(std::string(who) + ": p" + std::to_string(k) + " must be a device address");
+}
+
+uint64_t firstPointer(const eagle_backend_cell_op_desc& d)
+{
+    for (uint64_t p : d.p)
+        if (p != 0)
+            return p;
+    return 0;
+}
+
+}  // namespace
+
+/** Enqueue ``cell[0] = number of set bytes of mask[0, n)`` (memset + count) on ``s``. */
+void enqueueMaskCount(const uint8_t* mask, int64_t n, uint32_t* cell, cudaStream_t s, bool zeroFirst)
+{
+    if (zeroFirst)
+        cudaCheck(cudaMemsetAsync(cell, 0, sizeof(uint32_t), s), "cudaMemsetAsync");
+    if (n == 0)
+        return;
+    const bool aligned = (reinterpret_cast<uintptr_t>(mask) & 15u) == 0;
+    if (aligned)
+        maskCountKernel<true><<<gridFor(n, 16), 256, 0, s>>>(mask, n, cell);
+    else
+        maskCountKernel<false><<<gridFor(n, 16), 256, 0, s>>>(mask, n, cell);
+    launchCheck("mask count");
+}
+
+}  // namespace eb
+
+using namespace eb;
+
+#define EB_API extern "C" __attribute__((visibility("default")))
+
+EB_API eagle_backend_status eagle_backend_compact_device(struct eagle_backend_compact_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_compact_device";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        if (d.n < 0)
+            invalid(std::string(who) + ": n must be >= 0");
+        if (d.n > INT64_C(2147483647))
+            unsupported(std::string(who) + ": the int32 index map addresses at most 2^31-1 samples, got n = "
+                + std::to_string(d.n));
+        if (d.scratch == 0) {
+            constexpr size_t end = offsetof(eagle_backend_compact_desc, scratch_bytes) + sizeof(int64_t);
+            if (desc->struct_size < end)
+                invalid(std::string(who) + ": the scratch query needs a desc carrying scratch_bytes");
+            desc->scratch_bytes = int64_t(compactScratchBytes(d.n));
+            return;
+        }
+        if (d.count == 0 || (d.n > 0 && (d.mask == 0 || d.index_map == 0)))
+            invalid(std::string(who) + ": mask, index_map and count must be device addresses");
+        const bool trigger = d.live32 != 0;
+        if (trigger) {
+            if (d.span == 0 || d.fire == 0)
+                invalid(std::string(who) + ": a trigger needs live32, span and fire");
+            if (d.reserved2 != 0)
+                invalid(std::string(who) + ": reserved2 must be zero");
+            if (!(d.theta > 0.0f && d.theta < 1.0f))
+                invalid(std::string(who) + ": the trigger's theta must lie in (0, 1)");
+        }
+        const int dev = resolveDevice(d.device, d.mask != 0 ? d.mask : d.count);
+        DeviceScope scope(dev);
+        const cudaStream_t s = seamStream(d.stream);
+        if (d.n == 0) {
+            compactEmptyKernel<<<1, 1, 0, s>>>(reinterpret_cast<uint32_t*>(d.count),
+                trigger ? reinterpret_cast<uint32_t*>(d.live32) : nullptr,
+                trigger ? reinterpret_cast<uint32_t*>(d.fire) : nullptr);
+            launchCheck(who);
+            return;
+        }
+        const size_t scratchBytes = compactScratchBytes(d.n);
+        CompactArgs a{};
+        a.mask = reinterpret_cast<const uint8_t*>(d.mask);
+        a.n = d.n;
+        a.map = reinterpret_cast<int32_t*>(d.index_map);
+        a.count = reinterpret_cast<uint32_t*>(d.count);
+        a.tiles = uint32_t((d.n + kTile - 1) / kTile);
+        a.status = reinterpret_cast<uint64_t*>(d.scratch);
+        a.tileNext = reinterpret_cast<uint32_t*>(d.scratch + size_t(a.tiles) * sizeof(uint64_t));
+        a.err = a.tileNext + 1;
+        a.live32 = reinterpret_cast<uint32_t*>(d.live32);
+        a.span = reinterpret_cast<const uint32_t*>(d.span);
+        a.fire = reinterpret_cast<uint32_t*>(d.fire);
+        a.theta = d.theta;
+        cudaCheck(cudaMemsetAsync(reinterpret_cast<void*>(d.scratch), 0, scratchBytes, s), "cudaMemsetAsync");
+        const bool aligned = (d.mask & 15u) == 0;
+        const bool drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
+        if (drop)
+            trigger ? launchCompact<true, true>(a, aligned, s) : launchCompact<true, false>(a, aligned, s);
+        else
+            trigger ? launchCompact<false, true>(a, aligned, s) : launchCompact<false, false>(a, aligned, s);
+        launchCheck(who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_reset_device(struct eagle_backend_reorder_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_reset_device";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        if (d.n < 0 || d.n > INT64_C(2147483647))
+            invalid(std::string(who) + ": n must lie in [0, 2^31 - 1]");
+        if (d.perm == 0 || d.inv == 0 || d.count == 0 || d.span == 0)
+            invalid(std::string(who) + ": perm, inv, count and span must be device addresses");
+        DeviceScope scope(resolveDevice(d.device, d.perm));
+        const cudaStream_t s = seamStream(d.stream);
+        resetKernel<<<gridFor(std::max<int64_t>(d.n, 1)), 256, 0, s>>>(reinterpret_cast<int32_t*>(d.perm),
+            reinterpret_cast<int32_t*>(d.inv), reinterpret_cast<int32_t*>(d.index_map),
+            reinterpret_cast<uint32_t*>(d.count), reinterpret_cast<uint32_t*>(d.span), d.n);
+        launchCheck(who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_cell_op(const struct eagle_backend_cell_op_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_cell_op";
+        const auto d = readDesc(desc, 0u, who);
+        if (d.n < 0)
+            invalid(std::string(who) + ": n must be >= 0");
+        if (d.op > EAGLE_BACKEND_CELL_SCALE_COUNT)
+            unsupported(std::string(who) + ": op " + std::to_string(d.op)
+                + " is an array op this backend does not carry (it serves the until-done loop's ops 0-6)");
+        DeviceScope scope(resolveDevice(d.device, firstPointer(d)));
+        const cudaStream_t s = seamStream(d.stream);
+        switch (d.op) {
+        case EAGLE_BACKEND_CELL_BUMP:
+            need(d, 1, who);
+            bumpKernel<<<1, 1, 0, s>>>(reinterpret_cast<uint32_t*>(d.p[0]));
+            break;
+        case EAGLE_BACKEND_CELL_MASK_COUNT:
+            if (d.n == 0)
+                return;
+            need(d, 2, who);
+            enqueueMaskCount(reinterpret_cast<const uint8_t*>(d.p[0]), d.n, reinterpret_cast<uint32_t*>(d.p[1]), s,
+                false);
+            break;
+        case EAGLE_BACKEND_CELL_POLICY:
+            need(d, 6, who);
+            if (d.i[8] == 0)
+                invalid(std::string(who) + ": POLICY rate scale (i8) must be non-zero");
+            policyKernel<<<1, 1, 0, s>>>(reinterpret_cast<const uint32_t*>(d.p[0]),
+                reinterpret_cast<const uint32_t*>(d.p[1]), reinterpret_cast<int64_t*>(d.p[2]),
+                reinterpret_cast<int64_t*>(d.p[3]), reinterpret_cast<uint32_t*>(d.p[4]),
+                reinterpret_cast<int64_t*>(d.p[5]), d.i[0], d.i[1], int(d.i[2]), int(d.i[3]), int(d.i[4]), int(d.i[5]),
+                int(d.i[6]), int(d.i[7]), int(d.i[8]));
+            break;
+        case EAGLE_BACKEND_CELL_IDENTITY:
+            if (d.n == 0)
+                return;
+            need(d, 1, who);
+            identityKernel<<<gridFor(d.n), 256, 0, s>>>(reinterpret_cast<int32_t*>(d.p[0]), d.n);
+            break;
+        case EAGLE_BACKEND_CELL_COUNT_FIRED:
+            need(d, 2, who);
+            countFiredKernel<<<1, 1, 0, s>>>(reinterpret_cast<const uint32_t*>(d.p[0]),
+                reinterpret_cast<uint32_t*>(d.p[1]));
+            break;
+        case EAGLE_BACKEND_CELL_GROUP_AND:
+            if (d.n == 0)
+                return;
+            need(d, 2, who);
+            if (d.i[1] < 1)
+                invalid(std::string(who) + ": GROUP_AND group must be >= 1");
+            groupAndKernel<<<gridFor(d.n), 256, 0, s>>>(reinterpret_cast<const uint8_t*>(d.p[0]),
+                reinterpret_cast<uint8_t*>(d.p[1]), d.i[0], int(d.i[1]), d.n);
+            break;
+        default:  // SCALE_COUNT
+            need(d, 2, who);
+            scaleCountKernel<<<1, 1, 0, s>>>(reinterpret_cast<const uint32_t*>(d.p[0]),
+                reinterpret_cast<uint32_t*>(d.p[1]), int(d.i[0]));
+        }
+        launchCheck(who);
+    });
+}

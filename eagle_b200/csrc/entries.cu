@@ -1,0 +1,265 @@
+// The oscillator's step entries in the hawk kernel ABI, so eagle's own launch
+// path (run_device, launch_raw, BoundPlan.launch/_range/_persist) can drive them.
+//
+// Argument order: the role arguments of the kernel's arg_spec, packed as eagle's
+// registry packs them (plugin/plugin_registry/registry.h:605-710): a 32-byte
+// handle per per-sample / terminated / mutable / lookup plane, float64 uniforms
+// by value. The arg_spec of the oscillator (README.md:89-97 plus the two planes
+// a finishing, automatic kernel binds, python/eagle/_until_done.py:58-66):
+//
+//   ("per_sample", "omega"), ("uniform", "t_end"), ("uniform", "dt"),
+//   ("terminated", "terminated"), ("mutable", "x"), ("mutable", "v"),
+//   ("mutable", "t"), ("lookup", "finished_count"), ("lookup", "fused_steps")
+//
+// (the "_spread" entries take t_end as ("per_sample", "t_end") instead). Then the
+// partition triple ``int64 base, count, nSamples`` (eagle/exec/DeviceKernel.h:47-84),
+// then the fast-entry tails of python/eagle/_plan_binding.py:455-460 / :582-591:
+//   _range:   uint32* hawk_steps, uint64* hawk_stepsum
+//   _persist: uint32* hawk_next, uint64* hawk_util, uint32* hawk_steps,
+//             uint64* hawk_stepsum, uint32 hawk_chunk
+// ``fused_steps`` (int64) is the steps one launch may take per sample.
+#include "models.cuh"
+
+#include <map>
+#include <mutex>
+#include <string>
+
+namespace eb {
+
+/** t_end as a Param (by value) or a per-sample plane (a handle). */
+template <bool Spread>
+struct TEnd;
+template <>
+struct TEnd<false> {
+    double v;
+    __device__ __forceinline__ double at(int64_t) const { return v; }
+};
+template <>
+struct TEnd<true> {
+    ScalarHandle h;
+    __device__ __forceinline__ double at(int64_t i) const { return static_cast<const double*>(h.data)[i]; }
+};
+
+__device__ __forceinline__ double* dplane(const ScalarHandle& h) { return static_cast<double*>(h.data); }
+
+/** Flush a thread's run counters with one atomic per block and counter:
+ *  finished count (u32), longest steps (u32 max) and executed steps (u64 sum);
+ *  a null cell is skipped. Every thread of the block calls it. */
+__device__ __forceinline__ void blockFlush(uint32_t fin, uint32_t longest, unsigned long long sum,
+    uint32_t* finished, uint32_t* steps, unsigned long long* stepsum)
+{
+    __shared__ uint32_t sFin[32], sMax[32];
+    __shared__ unsigned long long sSum[32];
+    fin = warpSum(fin);
+    longest = warpMax(longest);
+    sum = warpSum(sum);
+    const unsigned lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sFin[warp] = fin;
+        sMax[warp] = longest;
+        sSum[warp] = sum;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t f = 0, m = 0;
+        unsigned long long u = 0;
+        for (unsigned w = 0; w < (blockDim.x + 31) / 32; ++w) {
+            f += sFin[w];
+            m = sMax[w] > m ? sMax[w] : m;
+            u += sSum[w];
+        }
+        if (finished != nullptr && f != 0)
+            atomicAdd(finished, f);
+        if (steps != nullptr && m != 0)
+            atomicMax(steps, m);
+        if (stepsum != nullptr && u != 0)
+            atomicAdd(stepsum, u);
+    }
+}
+
+/** The plain and range entries: one lane per sample of [base, base + count). */
+template <bool Fma, bool Spread>
+__device__ __forceinline__ void rangeBody(const ScalarHandle& omega, const TEnd<Spread>& tEnd, double dt,
+    const ScalarHandle& terminated, const ScalarHandle& x, const ScalarHandle& v, const ScalarHandle& t,
+    const ScalarHandle& finished, const ScalarHandle& fused, int64_t base, int64_t count, uint32_t* steps,
+    unsigned long long* stepsum)
+{
+    const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t i = base + j;
+    uint8_t* term = static_cast<uint8_t*>(terminated.data);
+    const int64_t budget = *static_cast<const int64_t*>(fused.data);
+    int64_t taken = 0;
+    bool fin = false;
+    if (j < count && term[i] == 0) {
+        Oscillator<Fma> s;
+        s.x = dplane(x)[i];
+        s.v = dplane(v)[i];
+        s.t = dplane(t)[i];
+        s.c = Oscillator<Fma>::coeff(dt, static_cast<const double*>(omega.data)[i]);
+        s.te = tEnd.at(i);
+        fin = s.run(dt, budget, taken);
+        dplane(x)[i] = s.x;
+        dplane(v)[i] = s.v;
+        dplane(t)[i] = s.t;
+        if (fin)
+            term[i] = 1;
+    }
+    blockFlush(fin ? 1u : 0u, uint32_t(taken), (unsigned long long)taken, static_cast<uint32_t*>(finished.data),
+        steps, stepsum);
+}
+
+#define EB_OSC_ROLES(TEND_T)                                                                                  \
+    ScalarHandle omega, TEND_T tEnd, double dt, ScalarHandle terminated, ScalarHandle x, ScalarHandle v,     \
+        ScalarHandle t, ScalarHandle finished, ScalarHandle fused, int64_t base, int64_t count, int64_t nSamples
+
+template <bool Fma, bool Spread>
+__global__ __launch_bounds__(256) void oscillatorPlain(EB_OSC_ROLES(TEnd<Spread>))
+{
+    (void)nSamples;
+    rangeBody<Fma, Spread>(omega, tEnd, dt, terminated, x, v, t, finished, fused, base, count, nullptr, nullptr);
+}
+
+template <bool Fma, bool Spread>
+__global__ __launch_bounds__(256) void oscillatorRange(EB_OSC_ROLES(TEnd<Spread>), uint32_t* hawkSteps,
+    unsigned long long* hawkStepsum)
+{
+    (void)nSamples;
+    rangeBody<Fma, Spread>(omega, tEnd, dt, terminated, x, v, t, finished, fused, base, count, hawkSteps,
+        hawkStepsum);
+}
+
+/** The persistent entry: at each chunk head the lanes of a warp without a
+ *  sample claim the next ones together off ``hawk_next`` (one atomic per warp),
+ *  skipping samples already terminated, until the partition is exhausted; each
+ *  lane then runs up to ``chunk`` steps of its sample, within the budget. A lane
+ *  whose sample ends mid-chunk waits, masked, for the next head. */
+template <bool Fma, bool Spread>
+__global__ __launch_bounds__(256) void oscillatorPersist(EB_OSC_ROLES(TEnd<Spread>), uint32_t* hawkNext,
+    unsigned long long* hawkUtil, uint32_t* hawkSteps, unsigned long long* hawkStepsum, uint32_t hawkChunk)
+{
+    (void)nSamples;
+    const unsigned lane = threadIdx.x & 31u;
+    uint8_t* term = static_cast<uint8_t*>(terminated.data);
+    const int64_t budget = *static_cast<const int64_t*>(fused.data);
+    const int64_t chunk = hawkChunk == 0 ? 32 : int64_t(hawkChunk);
+    uint32_t* finished_ = static_cast<uint32_t*>(finished.data);
+    Oscillator<Fma> s{};
+    int64_t i = -1;       // the lane's sample, -1: none
+    int64_t taken = 0;    // steps of the lane's sample so far
+    bool exhausted = false;
+    uint32_t finCount = 0, longest = 0;  // the lane's run counters, flushed once at the end
+    unsigned long long ranSum = 0, slots = 0;
+    for (;;) {
+        // claim: every lane without a sample takes the next unclaimed index
+        for (;;) {
+            const bool needs = i < 0 && !exhausted;
+            const unsigned want = __ballot_sync(kFull, needs);
+            if (want == 0)
+                break;
+            const unsigned leader = __ffs(want) - 1;
+            uint32_t first = 0;
+            if (lane == leader)
+                first = atomicAdd(hawkNext, uint32_t(__popc(want)));
+            first = __shfl_sync(kFull, first, leader);
+            if (needs) {
+                const int64_t k = int64_t(first) + __popc(want & ((1u << lane) - 1u));
+                if (k >= count) {
+                    exhausted = true;
+                } else if (term[base + k] == 0) {
+                    i = base + k;
+                    s.x = dplane(x)[i];
+                    s.v = dplane(v)[i];
+                    s.t = dplane(t)[i];
+                    s.c = Oscillator<Fma>::coeff(dt, static_cast<const double*>(omega.data)[i]);
+                    s.te = tEnd.at(i);
+                    taken = 0;
+                }
+            }
+        }
+        if (__ballot_sync(kFull, i >= 0) == 0)
+            break;
+        int64_t ran = 0;
+        bool fin = false;
+        if (i >= 0) {
+            const int64_t room = budget - taken;
+            fin = s.run(dt, room < chunk ? room : chunk, ran);
+            taken += ran;
+        }
+        ranSum += (unsigned long long)ran;
+        slots += (unsigned long long)chunk;
+        const bool ends = i >= 0 && (fin || taken >= budget);
+        if (ends) {
+            dplane(x)[i] = s.x;
+            dplane(v)[i] = s.v;
+            dplane(t)[i] = s.t;
+            if (fin) {
+                term[i] = 1;
+                ++finCount;
+            }
+            longest = uint32_t(taken) > longest ? uint32_t(taken) : longest;
+            i = -1;
+        }
+    }
+    blockFlush(finCount, longest, ranSum, finished_, hawkSteps, hawkStepsum);
+    if (hawkUtil != nullptr) {
+        const unsigned long long r = warpSum(ranSum), sl = warpSum(slots);
+        if (lane == 0) {
+            atomicAdd(&hawkUtil[0], r);
+            atomicAdd(&hawkUtil[1], sl);
+        }
+    }
+}
+
+namespace {
+
+template <bool Fma, bool Spread>
+void addEntries(std::map<std::string, const void*>& m, const std::string& stem)
+{
+    const std::string suffix = Fma ? "_fma" : "";
+    m[stem + suffix] = reinterpret_cast<const void*>(&oscillatorPlain<Fma, Spread>);
+    m[stem + "_range" + suffix] = reinterpret_cast<const void*>(&oscillatorRange<Fma, Spread>);
+    m[stem + "_persist" + suffix] = reinterpret_cast<const void*>(&oscillatorPersist<Fma, Spread>);
+}
+
+const std::map<std::string, const void*>& entryTable()
+{
+    static const std::map<std::string, const void*> table = [] {
+        std::map<std::string, const void*> m;
+        addEntries<false, false>(m, "oscillator");
+        addEntries<true, false>(m, "oscillator");
+        addEntries<false, true>(m, "oscillator_spread");
+        addEntries<true, true>(m, "oscillator_spread");
+        return m;
+    }();
+    return table;
+}
+
+}  // namespace
+
+/** The host stub of a built-in entry by name (nullptr if unknown). */
+const void* entryStub(const std::string& name)
+{
+    const auto& t = entryTable();
+    const auto it = t.find(name);
+    return it == t.end() ? nullptr : it->second;
+}
+
+}  // namespace eb
+
+using namespace eb;
+
+extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_backend_x_b200_entry(
+    const char* name, int32_t device, uint64_t* function)
+{
+    return guarded([&] {
+        if (name == nullptr || function == nullptr)
+            invalid("eagle_backend_x_b200_entry: null name or output");
+        const void* stub = entryStub(name);
+        if (stub == nullptr)
+            fail(EAGLE_BACKEND_INDEX, std::string("eagle_backend_x_b200_entry: no built-in entry named '") + name + "'");
+        DeviceScope scope(resolveDevice(device, 0));
+        cudaFunction_t f = nullptr;
+        cudaCheck(cudaGetFuncBySymbol(&f, stub), "cudaGetFuncBySymbol");
+        *function = reinterpret_cast<uint64_t>(f);
+    });
+}

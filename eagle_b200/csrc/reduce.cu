@@ -1,0 +1,412 @@
+// The canonical ``ordered`` reduction on B200: one kernel per call.
+//
+// The tree is eagle's (eagle/reduce/canonical.h:10-32): leaves of 256 slots x 16
+// terms, slot t folding samples t, t+256, ... of its leaf (a Neumaier walk for a
+// floating sum), the in-leaf tree at offsets 128, 64, ..., 1 with an absent partner
+// carried, then level-by-level pairwise over the leaf partials with an odd last
+// node carried. The bits are a function of the values in sample order only.
+//
+// B200 mapping. A CTA of 256 threads owns an aligned group of 2^q consecutive
+// leaves: thread t holds slot t (its 16 loads issued together, each a coalesced
+// 2 KB row across the CTA), the offsets 128..32 go through shared memory and
+// 16..1 through warp shuffles inside warp 0, and the group's leaf partials are
+// joined by the same pairwise levels (an aligned group is a subtree of them).
+// The last CTA to finish (a device-scope counter) runs the remaining levels over
+// the group partials in aligned chunks of 512 and stores the value. One memset
+// node zeroes the counters before the launch, so the call stays capturable.
+#include "common.cuh"
+
+#include <cmath>
+
+namespace eb {
+namespace {
+
+constexpr int kSlots = 256;
+constexpr int kTerms = 16;
+constexpr int64_t kLeaf = int64_t(kSlots) * kTerms;
+constexpr int kChunk = 512;         // nodes one pass of the final levels joins
+constexpr int kMaxGroupLeaves = 64;  // leaves one CTA owns at most
+
+// ------------------------------------------------------------------- partials
+
+template <class T>
+struct CompP {  // a floating-point sum's partial (hi, comp)
+    T h, c;
+    static __device__ __forceinline__ CompP of(T x) { return {x, T(0)}; }
+    static __device__ __forceinline__ CompP of(T x, T xc) { return {x, isfinite(x) ? xc : T(0)}; }
+    static __device__ __forceinline__ CompP join(const CompP& a, const CompP& b)
+    {
+        const T s = a.h + b.h;
+        const T bb = s - a.h;
+        const T e = (a.h - (s - bb)) + (b.h - bb);
+        return {s, isfinite(s) ? (a.c + b.c) + e : T(0)};
+    }
+    __device__ __forceinline__ void add(T x) { *this = join(*this, CompP{x, T(0)}); }
+    __device__ __forceinline__ void add(T x, T xc)
+    {
+        add(x);
+        c = isfinite(h) ? c + xc : T(0);
+    }
+    __device__ __forceinline__ T value() const { return isfinite(h) ? h + c : h; }
+    __device__ __forceinline__ CompP shflDown(unsigned off) const
+    {
+        return {__shfl_down_sync(kFull, h, off), __shfl_down_sync(kFull, c, off)};
+    }
+};
+
+template <class T>
+struct SumOp {
+    __device__ __forceinline__ T operator()(T a, T b) const
+    {
+        if constexpr (std::is_integral_v<T>) {
+            using U = std::make_unsigned_t<T>;
+            return T(U(a) + U(b));
+        } else {
+            return a + b;
+        }
+    }
+};
+template <class T>
+struct MaxOp {
+    __device__ __forceinline__ T operator()(T a, T b) const { return a > b ? a : b; }
+};
+template <class T>
+struct MinOp {
+    __device__ __forceinline__ T operator()(T a, T b) const { return a < b ? a : b; }
+};
+struct AllOp {
+    __device__ __forceinline__ uint8_t operator()(uint8_t a, uint8_t b) const { return uint8_t(a != 0 && b != 0); }
+};
+
+template <class T, class Op>
+struct PlainP {  // the partial of an exact operator: one value
+    T h;
+    static __device__ __forceinline__ PlainP of(T x) { return {x}; }
+    static __device__ __forceinline__ PlainP of(T x, T) { return {x}; }
+    static __device__ __forceinline__ PlainP join(const PlainP& a, const PlainP& b) { return {Op{}(a.h, b.h)}; }
+    __device__ __forceinline__ void add(T x) { h = Op{}(h, x); }
+    __device__ __forceinline__ void add(T x, T) { add(x); }
+    __device__ __forceinline__ T value() const { return h; }
+    __device__ __forceinline__ PlainP shflDown(unsigned off) const
+    {
+        if constexpr (sizeof(T) < 4)
+            return {T(__shfl_down_sync(kFull, int(h), off))};
+        else
+            return {__shfl_down_sync(kFull, h, off)};
+    }
+};
+
+template <class P>
+struct IsComp : std::false_type {};
+template <class T>
+struct IsComp<CompP<T>> : std::true_type {};
+
+// ------------------------------------------------------------------- kernels
+
+struct ReduceArgs {
+    const void* in;
+    const void* comp;
+    int64_t rows, cols, col0;
+    int64_t leaves, groupLeaves, groups;
+    void* partials;      // cols * groups partials
+    uint32_t* counters;  // cols words, zero on entry
+    void* out;
+    int pairOut;
+};
+
+/** One leaf's partial (valid in thread 0): the slot walk, then the in-leaf tree. */
+template <class P, class T, bool HasComp>
+__device__ __forceinline__ P leafPartial(const T* __restrict__ in, const T* __restrict__ comp, int64_t cols,
+    int64_t col, int64_t base, int64_t cnt, P* s)
+{
+    const int t = int(threadIdx.x);
+    const int live = cnt < kSlots ? int(cnt) : kSlots;
+    if (t < live) {
+        T v[kTerms];
+        T vc[HasComp ? kTerms : 1];
+#pragma unroll
+        for (int k = 0; k < kTerms; ++k) {
+            const int64_t i = int64_t(t) + int64_t(k) * kSlots;
+            v[k] = i < cnt ? in[(base + i) * cols + col] : T(0);
+            if constexpr (HasComp)
+                vc[k] = i < cnt ? comp[(base + i) * cols + col] : T(0);
+        }
+        P p;
+        if constexpr (HasComp)
+            p = P::of(v[0], vc[0]);
+        else
+            p = P::of(v[0]);
+#pragma unroll
+        for (int k = 1; k < kTerms; ++k) {
+            if (int64_t(t) + int64_t(k) * kSlots < cnt) {
+                if constexpr (HasComp)
+                    p.add(v[k], vc[k]);
+                else
+                    p.add(v[k]);
+            }
+        }
+        s[t] = p;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int off = kSlots / 2; off >= 32; off >>= 1) {
+        if (t < off && t + off < live)
+            s[t] = P::join(s[t], s[t + off]);
+        __syncthreads();
+    }
+    P q{};
+    if (t < 32) {
+        q = s[t];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const P o = q.shflDown(unsigned(off));
+            if (t < off && t + off < live)
+                q = P::join(q, o);
+        }
+    }
+    __syncthreads();  // s is reused by the next leaf
+    return q;
+}
+
+/** Pairwise levels over ``v[0, m)`` in shared memory (an aligned subtree): node i
+ *  of level L sits at i * 2^L; its right child, if present, at + 2^(L-1). */
+template <class P>
+__device__ __forceinline__ void levels(P* v, int m)
+{
+    for (int off = 1; off < m; off <<= 1) {
+        for (int i = int(threadIdx.x) * 2 * off; i < m; i += int(blockDim.x) * 2 * off)
+            if (i + off < m)
+                v[i] = P::join(v[i], v[i + off]);
+        __syncthreads();
+    }
+}
+
+template <class P, class T, bool HasComp>
+__global__ __launch_bounds__(kSlots) void canonicalKernel(ReduceArgs a)
+{
+    __shared__ P s[kSlots];
+    __shared__ P group[kChunk > kMaxGroupLeaves ? kChunk : kMaxGroupLeaves];
+    __shared__ int amLast;
+    const T* in = static_cast<const T*>(a.in);
+    const T* comp = static_cast<const T*>(a.comp);
+    P* partials = static_cast<P*>(a.partials);
+    const int64_t col = a.col0 + int64_t(blockIdx.y);
+    const int64_t g = int64_t(blockIdx.x);
+    const int64_t l0 = g * a.groupLeaves;
+    const int64_t l1 = l0 + a.groupLeaves < a.leaves ? l0 + a.groupLeaves : a.leaves;
+    for (int64_t l = l0; l < l1; ++l) {
+        const int64_t base = l * kLeaf;
+        const int64_t cnt = a.rows - base < kLeaf ? a.rows - base : kLeaf;
+        const P p = leafPartial<P, T, HasComp>(in, comp, a.cols, col, base, cnt, s);
+        if (threadIdx.x == 0)
+            group[l - l0] = p;
+    }
+    __syncthreads();
+    levels(group, int(l1 - l0));
+    if (threadIdx.x == 0) {
+        partials[col * a.groups + g] = group[0];
+        __threadfence();
+        amLast = atomicAdd(&a.counters[col], 1u) == uint32_t(a.groups - 1);
+    }
+    __syncthreads();
+    if (!amLast)
+        return;
+    __threadfence();
+    // the last CTA of this column: the remaining levels over the group partials,
+    // in aligned chunks of kChunk nodes, written back in place
+    P* v = partials + col * a.groups;
+    int64_t m = a.groups;
+    while (m > 1) {
+        const int64_t chunks = (m + kChunk - 1) / kChunk;
+        for (int64_t c = 0; c < chunks; ++c) {
+            const int cnt = int(m - c * kChunk < kChunk ? m - c * kChunk : kChunk);
+            for (int i = int(threadIdx.x); i < cnt; i += int(blockDim.x))
+                group[i] = v[c * kChunk + i];
+            __syncthreads();
+            levels(group, cnt);
+            if (threadIdx.x == 0)
+                v[c] = group[0];
+            __syncthreads();
+        }
+        m = chunks;
+    }
+    if (threadIdx.x == 0) {
+        const P r = v[0];
+        T* out = static_cast<T*>(a.out);
+        if constexpr (IsComp<P>::value) {
+            if (a.pairOut) {
+                out[col] = r.h;
+                out[a.cols + col] = isfinite(r.h) ? r.c : T(0);
+            } else {
+                out[col] = r.value();
+            }
+        } else {
+            out[col] = r.value();
+        }
+        a.counters[col] = 0u;  // ready for a replay
+    }
+}
+
+// ------------------------------------------------------------------- host side
+
+int64_t leafCount(int64_t rows) { return (rows + kLeaf - 1) / kLeaf; }
+
+/** Leaves per CTA: a power of two that keeps about eight CTAs per SM busy. */
+int64_t groupLeavesFor(int64_t leaves, int sms)
+{
+    const int64_t target = int64_t(sms) * 8;
+    int64_t g = 1;
+    while (g < kMaxGroupLeaves && (leaves + g - 1) / g > target)
+        g *= 2;
+    return g;
+}
+
+template <class P, class T>
+int64_t workElemsFor(int64_t rows, int64_t cols, int sms)
+{
+    const int64_t leaves = leafCount(rows);
+    const int64_t groups = (leaves + groupLeavesFor(leaves, sms) - 1) / groupLeavesFor(leaves, sms);
+    const int64_t partialBytes = groups * cols * int64_t(sizeof(P));
+    const int64_t counterBytes = cols * int64_t(sizeof(uint32_t));
+    const int64_t need = (std::max(partialBytes, counterBytes) + int64_t(sizeof(T)) - 1) / int64_t(sizeof(T));
+    // never less than eagle's own formula (3 elements per leaf and column), so a
+    // caller that sized its buffers by it stays valid
+    return std::max(need, 3 * leaves * cols);
+}
+
+template <class P, class T>
+void enqueueReduce(const eagle_backend_reduce_desc& d, int64_t cols, int pairOut, cudaStream_t stream)
+{
+    const int sms = smCount();
+    ReduceArgs a{};
+    a.in = reinterpret_cast<const void*>(d.in);
+    a.rows = d.n;
+    a.cols = cols;
+    a.leaves = leafCount(d.n);
+    a.groupLeaves = groupLeavesFor(a.leaves, sms);
+    a.groups = (a.leaves + a.groupLeaves - 1) / a.groupLeaves;
+    a.partials = reinterpret_cast<void*>(d.work_a);
+    a.counters = reinterpret_cast<uint32_t*>(d.work_b);
+    a.out = reinterpret_cast<void*>(d.out);
+    a.pairOut = pairOut;
+    cudaCheck(cudaMemsetAsync(a.counters, 0, size_t(cols) * sizeof(uint32_t), stream), "cudaMemsetAsync");
+    const bool hasComp = d.comp_in != 0;
+    a.comp = reinterpret_cast<const void*>(d.comp_in);
+    if (a.groups > INT64_C(2147483647))
+        unsupported("eagle_backend_x_reduce_canonical: too many leaf groups");
+    for (int64_t c0 = 0; c0 < cols; c0 += 65535) {
+        a.col0 = c0;
+        const dim3 grid(unsigned(a.groups), unsigned(std::min<int64_t>(cols - c0, 65535)));
+        if constexpr (IsComp<P>::value) {
+            if (hasComp)
+                canonicalKernel<P, T, true><<<grid, kSlots, 0, stream>>>(a);
+            else
+                canonicalKernel<P, T, false><<<grid, kSlots, 0, stream>>>(a);
+        } else {
+            canonicalKernel<P, T, false><<<grid, kSlots, 0, stream>>>(a);
+        }
+        launchCheck("eagle_backend_x_reduce_canonical");
+    }
+}
+
+template <class T>
+void dispatchOp(const eagle_backend_reduce_desc& d, int64_t cols, int pairOut, cudaStream_t stream, bool query,
+    int64_t* workElems)
+{
+    switch (d.op) {
+    case EAGLE_BACKEND_REDUCE_OP_SUM:
+        if constexpr (std::is_floating_point_v<T>) {
+            if (query)
+                *workElems = workElemsFor<CompP<T>, T>(d.n, cols, smCount());
+            else
+                enqueueReduce<CompP<T>, T>(d, cols, pairOut, stream);
+        } else {
+            if (query)
+                *workElems = workElemsFor<PlainP<T, SumOp<T>>, T>(d.n, cols, smCount());
+            else
+                enqueueReduce<PlainP<T, SumOp<T>>, T>(d, cols, pairOut, stream);
+        }
+        break;
+    case EAGLE_BACKEND_REDUCE_OP_MAX:
+        if (query)
+            *workElems = workElemsFor<PlainP<T, MaxOp<T>>, T>(d.n, cols, smCount());
+        else
+            enqueueReduce<PlainP<T, MaxOp<T>>, T>(d, cols, pairOut, stream);
+        break;
+    default:
+        if (query)
+            *workElems = workElemsFor<PlainP<T, MinOp<T>>, T>(d.n, cols, smCount());
+        else
+            enqueueReduce<PlainP<T, MinOp<T>>, T>(d, cols, pairOut, stream);
+    }
+}
+
+}  // namespace
+}  // namespace eb
+
+using namespace eb;
+
+extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_backend_x_reduce_canonical(
+    struct eagle_backend_reduce_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_reduce_canonical";
+        constexpr size_t base = offsetof(eagle_backend_reduce_desc, work_elems) + sizeof(int64_t);
+        if (desc == nullptr || desc->struct_size < base)
+            invalid(std::string(who) + ": null desc or struct_size too small");
+        eagle_backend_reduce_desc d{};
+        std::memcpy(&d, desc, std::min<size_t>(desc->struct_size, sizeof d));
+        const bool ext = desc->struct_size >= offsetof(eagle_backend_reduce_desc, comp_in) + sizeof(uint64_t);
+        if (!ext) {
+            d.policy = EAGLE_BACKEND_REDUCE_ORDERED;
+            d.flags = 0;
+            d.columns = 1;
+            d.comp_in = 0;
+        }
+        if (d.n < 1)
+            invalid(std::string(who) + ": n must be >= 1");
+        if (d.op > EAGLE_BACKEND_REDUCE_OP_MIN || d.dtype > EAGLE_BACKEND_REDUCE_U8)
+            invalid(std::string(who) + ": unknown dtype or op");
+        const bool all = d.op == EAGLE_BACKEND_REDUCE_OP_ALL;
+        if (all != (d.dtype == EAGLE_BACKEND_REDUCE_U8))
+            invalid(std::string(who) + ": the U8 element type goes with OP_ALL, and only with it");
+        if (d.columns < 1 || d.policy > EAGLE_BACKEND_REDUCE_AUTO || d.flags > EAGLE_BACKEND_REDUCE_PAIR_OUT)
+            invalid(std::string(who) + ": columns must be >= 1; unknown policy or flags");
+        const bool fsum = d.op == EAGLE_BACKEND_REDUCE_OP_SUM
+            && (d.dtype == EAGLE_BACKEND_REDUCE_F32 || d.dtype == EAGLE_BACKEND_REDUCE_F64);
+        if ((d.comp_in != 0 || d.flags != 0) && !fsum)
+            invalid(std::string(who) + ": comp_in and PAIR_OUT take a float32/float64 sum");
+        const bool query = d.work_a == 0;
+        if (!query && (d.in == 0 || d.out == 0 || d.work_b == 0))
+            invalid(std::string(who) + ": in, out, work_a and work_b must be device addresses");
+        const int dev = resolveDevice(d.device, query ? 0 : d.in);
+        DeviceScope scope(dev);
+        if (!query && d.dtype == EAGLE_BACKEND_REDUCE_F64 && d.op == EAGLE_BACKEND_REDUCE_OP_SUM && d.flags == 0) {
+            // eagle takes a 128-bit fixed-point leaf on devices whose FP32:FP64 rate
+            // is 8:1 or worse (canonical.h:304-313); this build carries the (hi, comp)
+            // leaf only, so such a device is refused rather than given other bits
+            int ratio = 0;
+            if (cudaDeviceGetAttribute(&ratio, cudaDevAttrSingleToDoublePrecisionPerfRatio, dev) == cudaSuccess
+                && ratio >= 8)
+                unsupported(std::string(who) + ": this device's FP32:FP64 ratio is " + std::to_string(ratio)
+                    + ":1; eagle reduces float64 sums there with the fixed-point leaf, which this build lacks");
+            (void)cudaGetLastError();
+        }
+        const cudaStream_t stream = seamStream(d.stream);
+        const int pairOut = (d.flags & EAGLE_BACKEND_REDUCE_PAIR_OUT) != 0;
+        int64_t workElems = 0;
+        switch (d.dtype) {
+        case EAGLE_BACKEND_REDUCE_F32: dispatchOp<float>(d, d.columns, pairOut, stream, query, &workElems); break;
+        case EAGLE_BACKEND_REDUCE_F64: dispatchOp<double>(d, d.columns, pairOut, stream, query, &workElems); break;
+        case EAGLE_BACKEND_REDUCE_I32: dispatchOp<int32_t>(d, d.columns, pairOut, stream, query, &workElems); break;
+        case EAGLE_BACKEND_REDUCE_I64: dispatchOp<int64_t>(d, d.columns, pairOut, stream, query, &workElems); break;
+        default:
+            if (query)
+                workElems = workElemsFor<PlainP<uint8_t, AllOp>, uint8_t>(d.n, d.columns, smCount());
+            else
+                enqueueReduce<PlainP<uint8_t, AllOp>, uint8_t>(d, d.columns, 0, stream);
+        }
+        if (query)
+            desc->work_elems = workElems;
+    });
+}

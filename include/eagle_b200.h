@@ -1,0 +1,409 @@
+/* eagle_b200: a B200 (sm_100a) backend for eagle's until-done hot path, behind
+ * eagle's ``eagle-backend/1`` C seam.
+ *
+ * Every declaration below is ``extern "C"``, takes plain pointers, integers and
+ * POD descs (no C++ or torch types), and keeps the name, argument meaning, struct
+ * layout and status behaviour of the seam entry it replaces. Each carries the
+ * reference declaration it stands in for as ``python/src/seam/eagle_backend.h:LINE``
+ * (paths relative to the eagle source tree). Entries named ``eagle_backend_x_b200_*``
+ * are this backend's own additions; each says so.
+ *
+ * Conventions (eagle_backend.h:59-88): every desc starts with ``uint32_t
+ * struct_size``; an input desc is read up to min(caller, callee) size, the rest
+ * taken as zero; unknown flag bits return EAGLE_BACKEND_UNSUPPORTED; ``device ==
+ * -1`` is the device owning the desc's buffers (else the current one); a raw
+ * stream 0 is the legacy default stream; a non-OK status leaves its message in
+ * the calling thread's ``eagle_backend_last_error()``, valid until the next call.
+ */
+#ifndef EAGLE_B200_H
+#define EAGLE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- versions, statuses, capability bits (eagle_backend.h:104-141) ---------- */
+
+#define EAGLE_BACKEND_VERSION_MAJOR 1u
+#define EAGLE_BACKEND_VERSION_MINOR 8u
+#define EAGLE_BACKEND_VERSION ((EAGLE_BACKEND_VERSION_MAJOR << 16) | EAGLE_BACKEND_VERSION_MINOR)
+
+typedef int32_t eagle_backend_status;
+
+#define EAGLE_BACKEND_OK 0
+#define EAGLE_BACKEND_ERROR 1
+#define EAGLE_BACKEND_INVALID_ARGUMENT 2
+#define EAGLE_BACKEND_INDEX 3
+#define EAGLE_BACKEND_INTEROP 4
+#define EAGLE_BACKEND_UNAVAILABLE 5
+#define EAGLE_BACKEND_CALLBACK_FAILED 6
+#define EAGLE_BACKEND_BAD_HANDLE 7
+#define EAGLE_BACKEND_UNSUPPORTED 8
+
+#define EAGLE_BACKEND_CAP_STREAM (UINT64_C(1) << 0)
+#define EAGLE_BACKEND_CAP_EXEC (UINT64_C(1) << 9)
+#define EAGLE_BACKEND_CAP_DEVICE (UINT64_C(1) << 10)
+#define EAGLE_BACKEND_CAP_FILTERING (UINT64_C(1) << 12)
+
+typedef struct eagle_backend_stream_s* eagle_backend_stream;
+
+/* ---- structs ------------------------------------------------------------------ */
+
+/* eagle_backend.h:171-179 */
+struct eagle_backend_build_info {
+    uint32_t struct_size;
+    uint32_t abi_version;
+    int32_t cudart_version;
+    int32_t reserved0;
+    char eagle_version[32];
+    char archs[128];
+    char backend_kind[16];
+};
+
+/* eagle_backend.h:181-192 */
+struct eagle_backend_device_props {
+    uint32_t struct_size;
+    int32_t device;
+    char name[256];
+    int32_t cc_major, cc_minor, sm_count, clock_rate_khz, memory_clock_rate_khz, memory_bus_width_bits;
+    int32_t regs_per_block, regs_per_sm, warp_size, reserved0;
+    int64_t shared_mem_per_block, shared_mem_per_sm;
+    double peak_bytes_per_s, peak_flops_sp, peak_flops_dp, fp64_ratio;
+    double ridge_flops_per_byte_sp, ridge_flops_per_byte_dp;
+    int64_t total_mem_bytes, free_mem_bytes;
+};
+
+/* eagle_backend.h:194-199 */
+struct eagle_backend_stream_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    int32_t reserved0;
+};
+#define EAGLE_BACKEND_STREAM_NON_BLOCKING 1u
+
+/* eagle_backend.h:244-256: one kernel launch over one partition */
+struct eagle_backend_launch_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    uint32_t block;
+    uint64_t function;
+    const uint64_t* params;
+    const uint64_t* param_sizes;
+    int64_t nparams;
+    int64_t base, count, n_samples;
+    uint64_t stream;
+};
+
+/* eagle_backend.h:480-493 */
+struct eagle_backend_launch_raw_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    uint32_t shared_bytes;
+    uint64_t function;
+    uint64_t stream;
+    uint32_t grid[3];
+    uint32_t block[3];
+    uint64_t args;
+    uint32_t arg_count;
+    uint32_t reserved;
+};
+
+/* cell ops (eagle_backend.h:497-523): integer kernels, bit-equal to the plain C expression */
+#define EAGLE_BACKEND_CELL_BUMP 0u
+#define EAGLE_BACKEND_CELL_MASK_COUNT 1u
+#define EAGLE_BACKEND_CELL_POLICY 2u
+#define EAGLE_BACKEND_CELL_IDENTITY 3u
+#define EAGLE_BACKEND_CELL_COUNT_FIRED 4u
+#define EAGLE_BACKEND_CELL_GROUP_AND 5u
+#define EAGLE_BACKEND_CELL_SCALE_COUNT 6u
+
+/* eagle_backend.h:576-587 */
+struct eagle_backend_cell_op_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    uint32_t op;
+    int32_t device;
+    uint64_t stream;
+    int64_t n;
+    uint64_t p[6];
+    int64_t i[10];
+    double f[2];
+    int64_t j[4];
+};
+
+/* filtering (eagle_backend.h:666-691) */
+#define EAGLE_BACKEND_COMPACT_MASK_IS_DROP (UINT32_C(1) << 0)
+
+struct eagle_backend_compact_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    uint32_t reserved;
+    uint64_t mask;
+    uint64_t index_map;
+    uint64_t count;
+    uint64_t scratch;
+    int64_t n;
+    uint64_t stream;
+    int64_t scratch_bytes;
+    uint64_t live32;
+    uint64_t span;
+    uint64_t fire;
+    float theta;
+    uint32_t reserved2;
+};
+
+/* eagle_backend.h:705-730 (reset_device reads device, perm, inv, index_map, count, span, n, stream) */
+struct eagle_backend_reorder_plane {
+    uint64_t data;
+    uint32_t elem_bytes;
+    uint32_t reserved;
+};
+
+struct eagle_backend_reorder_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    uint32_t n_planes;
+    uint64_t planes;
+    uint64_t mask;
+    uint64_t perm;
+    uint64_t inv;
+    uint64_t index_map;
+    uint64_t count;
+    uint64_t span;
+    uint64_t fire;
+    uint64_t scratch;
+    int64_t n;
+    uint64_t stream;
+    int64_t scratch_bytes;
+};
+
+/* canonical reduction (eagle_backend.h:861-894) */
+#define EAGLE_BACKEND_REDUCE_F32 0u
+#define EAGLE_BACKEND_REDUCE_F64 1u
+#define EAGLE_BACKEND_REDUCE_I32 2u
+#define EAGLE_BACKEND_REDUCE_I64 3u
+#define EAGLE_BACKEND_REDUCE_U8 4u
+#define EAGLE_BACKEND_REDUCE_OP_SUM 0u
+#define EAGLE_BACKEND_REDUCE_OP_MAX 1u
+#define EAGLE_BACKEND_REDUCE_OP_ALL 2u
+#define EAGLE_BACKEND_REDUCE_OP_MIN 3u
+#define EAGLE_BACKEND_REDUCE_COMPENSATED 0u
+#define EAGLE_BACKEND_REDUCE_ORDERED 1u
+#define EAGLE_BACKEND_REDUCE_AUTO 2u
+#define EAGLE_BACKEND_REDUCE_PAIR_OUT 1u
+
+struct eagle_backend_reduce_desc {
+    uint32_t struct_size;
+    uint32_t dtype;
+    uint32_t op;
+    int32_t device;
+    uint64_t in;
+    uint64_t out;
+    uint64_t work_a;
+    uint64_t work_b;
+    int64_t n;
+    uint64_t stream;
+    int64_t work_elems;
+    uint32_t policy;
+    uint32_t flags;
+    int64_t columns;
+    uint64_t comp_in;
+};
+
+/* ---- mandatory core (eagle_backend.h:268-277) --------------------------------- */
+
+/* eagle_backend.h:268: (1 << 16) | 8 */
+uint32_t eagle_backend_version(void);
+/* eagle_backend.h:269: the calling thread's message of its last failed call */
+const char* eagle_backend_last_error(void);
+/* eagle_backend.h:270 */
+eagle_backend_status eagle_backend_build_info(struct eagle_backend_build_info* info);
+/* eagle_backend.h:272: OK when a CUDA device is usable, UNAVAILABLE otherwise */
+eagle_backend_status eagle_backend_probe(void);
+/* eagle_backend.h:273: frees a buffer this backend allocated (NULL-safe) */
+void eagle_backend_free(void* p);
+/* eagle_backend.h:274 */
+eagle_backend_status eagle_backend_capabilities(uint64_t* groups);
+/* eagle_backend.h:277: the DLPack device types served (kDLCUDA = 2) */
+eagle_backend_status eagle_backend_device_types(int32_t* types, int32_t cap, int32_t* count);
+
+/* ---- stream (bit 0; eagle_backend.h:281-284) ---------------------------------- */
+
+eagle_backend_status eagle_backend_stream_create(const struct eagle_backend_stream_desc* desc, eagle_backend_stream* out);
+eagle_backend_status eagle_backend_stream_ptr(eagle_backend_stream h, uint64_t* stream);
+eagle_backend_status eagle_backend_stream_synchronize(eagle_backend_stream h);
+void eagle_backend_stream_release(eagle_backend_stream h);
+
+/* ---- exec (bit 9; eagle_backend.h:389) ----------------------------------------- */
+
+/* One launch of ``desc->function`` over the partition (base, count, n_samples): the
+ * packed role arguments, then the partition triple appended by value (the hawk
+ * kernel ABI, eagle/exec/DeviceKernel.h:47-84); grid = ceil(count / block).
+ * ``*launched`` = 0 for an empty partition. */
+eagle_backend_status eagle_backend_run_device(const struct eagle_backend_launch_desc* desc, int32_t* launched);
+
+/* ---- device (bit 10; eagle_backend.h:393) -------------------------------------- */
+
+eagle_backend_status eagle_backend_device_props(int32_t device, struct eagle_backend_device_props* props);
+
+/* ---- memory, per symbol (eagle_backend.h:405-424) ------------------------------ */
+
+#define EAGLE_BACKEND_COPY_H2D 0
+#define EAGLE_BACKEND_COPY_D2H 1
+#define EAGLE_BACKEND_COPY_D2D 2
+#define EAGLE_BACKEND_COPY_H2H 3
+
+/* eagle_backend.h:405: zero ``bytes`` at device ``ptr`` on ``stream`` (capture-legal) */
+eagle_backend_status eagle_backend_memset_device(uint64_t ptr, uint64_t bytes, uint64_t stream);
+/* eagle_backend.h:409 */
+eagle_backend_status eagle_backend_memcpy_device(uint64_t dst, uint64_t src, uint64_t bytes, uint64_t stream);
+/* eagle_backend.h:424 */
+eagle_backend_status eagle_backend_memcpy(uint64_t dst, uint64_t src, uint64_t bytes, int32_t kind, uint64_t stream);
+
+/* ---- device scope, raw launch, cell ops, events (minor 7; eagle_backend.h:442-662) */
+
+/* eagle_backend.h:442 */
+eagle_backend_status eagle_backend_device_count(int32_t* count);
+/* eagle_backend.h:444 */
+eagle_backend_status eagle_backend_set_device(int32_t device);
+/* eagle_backend.h:447 */
+eagle_backend_status eagle_backend_get_device(int32_t* device);
+/* eagle_backend.h:451: read and clear the thread's pending launch error */
+eagle_backend_status eagle_backend_launch_status(int32_t device);
+/* eagle_backend.h:453 */
+eagle_backend_status eagle_backend_device_synchronize(int32_t device);
+/* eagle_backend.h:455 */
+eagle_backend_status eagle_backend_stream_is_capturing(uint64_t stream, int32_t* capturing);
+/* eagle_backend.h:478: one CUfunction attribute (cuFuncGetAttribute codes) */
+eagle_backend_status eagle_backend_function_attribute(uint64_t function, int32_t attribute, int32_t* value);
+/* eagle_backend.h:495: cuLaunchKernel of desc->function; enqueue only, capture-legal */
+eagle_backend_status eagle_backend_launch_raw(const struct eagle_backend_launch_raw_desc* desc);
+/* eagle_backend.h:590: ops BUMP, MASK_COUNT, POLICY, IDENTITY, COUNT_FIRED,
+ * GROUP_AND, SCALE_COUNT (the until-done loop's ops); the array ops 7-35 return
+ * UNSUPPORTED. Capture-legal: enqueue only. */
+eagle_backend_status eagle_backend_cell_op(const struct eagle_backend_cell_op_desc* desc);
+/* eagle_backend.h:648 */
+eagle_backend_status eagle_backend_stream_sync(int32_t device, uint64_t stream);
+/* eagle_backend.h:651-662 */
+eagle_backend_status eagle_backend_event_create(int32_t device, uint64_t* event);
+eagle_backend_status eagle_backend_event_create_timed(int32_t device, uint64_t* event);
+eagle_backend_status eagle_backend_event_elapsed(uint64_t start, uint64_t end, float* ms);
+eagle_backend_status eagle_backend_event_record(uint64_t event, uint64_t stream);
+eagle_backend_status eagle_backend_event_wait(uint64_t stream, uint64_t event);
+void eagle_backend_event_release(uint64_t event, int32_t device);
+
+/* ---- filtering (bit 12; eagle_backend.h:701, :832) ----------------------------- */
+
+/* eagle_backend.h:693-701: compact the samples ``mask`` keeps into
+ * index_map[0, *count), ascending. ``scratch == 0`` is the query (writes
+ * scratch_bytes only). Otherwise enqueue only: no allocation, no synchronisation,
+ * no host read (capturable). n > 2^31 - 1 returns UNSUPPORTED. One single-pass
+ * kernel (warp ballots, decoupled look-back) after a memset of its scratch. */
+eagle_backend_status eagle_backend_compact_device(struct eagle_backend_compact_desc* desc);
+/* eagle_backend.h:826-832: perm, inv and (non-zero) index_map become 0..n-1,
+ * *count = *span = n, in one kernel; capture-legal */
+eagle_backend_status eagle_backend_reset_device(struct eagle_backend_reorder_desc* desc);
+
+/* ---- canonical reduction (experimental; eagle_backend.h:896-906) -------------- */
+
+/* The canonical fixed-order reduction of each column of the row-major (n, columns)
+ * device plane ``in`` into ``out``: leaves of 256 slots x 16 strided samples, the
+ * fixed in-leaf tree, level-by-level pairwise over the leaves. ``work_a == 0`` is
+ * the query (writes work_elems). Every policy runs the ordered tree (bitwise
+ * deterministic; the ordered result also meets the compensated contract). One
+ * kernel per 65535 columns after a memset: enqueue only, capturable. */
+eagle_backend_status eagle_backend_x_reduce_canonical(struct eagle_backend_reduce_desc* desc);
+
+/* ---- this backend's additions (no counterpart entry in the seam) --------------- */
+
+/* eagle_backend_x_b200_entry: the CUfunction (as uint64) of one of this backend's
+ * built-in step kernels by name, for run_device / launch_raw. The kernels take the
+ * hawk argument ABI: role arguments packed as eagle's registry packs them
+ * (plugin/plugin_registry/registry.h:605-710: a 32-byte handle per per-sample,
+ * mutable, terminated and lookup plane, float64 uniforms by value), then
+ * ``int64 base, count, nSamples`` (eagle/exec/DeviceKernel.h:47-84), then the
+ * fast-entry tails of python/eagle/_plan_binding.py:455-460 (``_persist``) and
+ * :582-591 (``_range``). Names: "oscillator", "oscillator_range", "oscillator_persist"
+ * (t_end a Param) and "oscillator_spread", "..._range", "..._persist" (t_end per
+ * sample); a "_fma" suffix selects the contracted multiply-adds. */
+eagle_backend_status eagle_backend_x_b200_entry(const char* name, int32_t device, uint64_t* function);
+
+/* The until-done engine (this backend's addition; it stands in for the loop that
+ * python/eagle/_until_done.py:528-1845 builds from seam calls). One engine runs one
+ * model over n samples resident on one device. */
+#define EAGLE_B200_MODEL_OSCILLATOR 0u        /* README.md:89-97, t_end a Param */
+#define EAGLE_B200_MODEL_OSCILLATOR_SPREAD 1u /* the same body, t_end per sample */
+
+#define EAGLE_B200_MODE_BAND 0u    /* one CUDA graph: WHILE { fused step + compaction + policy } */
+#define EAGLE_B200_MODE_PERSIST 1u /* one persistent launch: lanes claim samples off a counter */
+#define EAGLE_B200_MODE_FUSED 2u   /* one launch, one lane per sample, the whole budget */
+
+#define EAGLE_B200_FLAG_FMA 1u /* contract x0 + dt*v0 and v0 - c*x0 into fused multiply-adds */
+
+struct eagle_b200_engine_desc {
+    uint32_t struct_size;
+    uint32_t flags;      /* EAGLE_B200_FLAG_* */
+    int32_t device;      /* -1: the device owning the planes */
+    uint32_t model;      /* EAGLE_B200_MODEL_* */
+    uint32_t mode;       /* EAGLE_B200_MODE_* */
+    uint32_t reserved0;
+    int64_t n;           /* samples, 0 <= n <= 2^31 - 1 */
+    int64_t max_steps;   /* steps a sample may take per run, >= 0 */
+    uint64_t planes[8];  /* device addresses of the model's planes, in the model's order */
+    double uniforms[4];  /* the model's Params, in the model's order */
+    uint64_t terminated; /* u8[n] mask: a set byte is a finished sample */
+    int64_t k_first;     /* band: steps of the first launch (0: 16) */
+    int64_t k_min;       /* band: fewest steps per launch but the last (0: 8) */
+    int64_t k_max;       /* band: most steps per launch (0: 4096) */
+    uint32_t chunk;      /* persist: steps between claims, a power of two (0: 32) */
+    uint32_t block;      /* threads per block (0: 256) */
+    double overhead_steps; /* band: a launch's fixed cost in sample-steps (0: built-in) */
+    double interval_steps; /* band: a launch's per-sample memory cost in steps (0: built-in) */
+};
+
+/* What one run did (python/eagle/_until_done.py:120-171, RunReport). */
+struct eagle_b200_report {
+    uint32_t struct_size;
+    uint32_t done;        /* finished == n */
+    int64_t n;
+    int64_t finished;     /* samples whose mask is set when the run ends */
+    int64_t steps;        /* the longest sample's steps in this run (exact) */
+    int64_t launches;     /* loop iterations (band) or 1 */
+    int64_t compactions;  /* compactions run (band) */
+    uint64_t step_sum;    /* steps executed by all samples in this run */
+    uint32_t error;       /* device error word: 0 = none (bit 0: a look-back wait gave up) */
+    uint32_t mode;
+};
+
+/* The models' plane orders: OSCILLATOR planes = {omega, x, v, t}, uniforms = {t_end,
+ * dt}; OSCILLATOR_SPREAD planes = {omega, t_end, x, v, t}, uniforms = {dt}. */
+typedef struct eagle_b200_engine_s* eagle_b200_engine;
+
+/* Allocate the engine's device state (compacted state, look-back words, cells) on
+ * its device and, for the band mode, build its graph. Allocates: call outside any
+ * stream capture. */
+eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagle_b200_engine_desc* desc,
+    eagle_b200_engine* out);
+/* Enqueue one run on ``stream`` (continuing from the current mask and state);
+ * no host synchronisation. */
+eagle_backend_status eagle_backend_x_b200_engine_launch(eagle_b200_engine h, uint64_t stream);
+/* Wait for ``stream`` and read the last run's report (one device-to-host copy). */
+eagle_backend_status eagle_backend_x_b200_engine_report(eagle_b200_engine h, uint64_t stream,
+    struct eagle_b200_report* report);
+/* launch + report. */
+eagle_backend_status eagle_backend_x_b200_engine_run(eagle_b200_engine h, uint64_t stream,
+    struct eagle_b200_report* report);
+void eagle_backend_x_b200_engine_release(eagle_b200_engine h);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* EAGLE_B200_H */

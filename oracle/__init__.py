@@ -1,0 +1,194 @@
+"""Test infrastructure: NumPy face of the CPU restatement in ``oracle.cpp``.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
+import this package; the engine in ``eagle_b200`` never does. Each function says
+which part of eagle it restates (paths relative to the eagle source tree).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+F32, F64, I32, I64, U8 = 0, 1, 2, 3, 4
+OP_SUM, OP_MAX, OP_ALL, OP_MIN = 0, 1, 2, 3
+MASK_IS_DROP = 1
+_DTYPE_CODE = {np.dtype(np.float32): F32, np.dtype(np.float64): F64, np.dtype(np.int32): I32,
+               np.dtype(np.int64): I64, np.dtype(np.uint8): U8, np.dtype(np.bool_): U8}
+_OPS = {"sum": OP_SUM, "max": OP_MAX, "all": OP_ALL, "min": OP_MIN}
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+
+
+def build() -> str:
+    """Compile ``liboracle.so`` with the committed Makefile (g++ -ffp-contract=off)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.oracle_threads.argtypes = [ctypes.c_int]
+        L.oracle_reduce.argtypes = [_P, _I64, _I64, ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int]
+        L.oracle_leaf_partials_f64.argtypes = [_P, _I64, _P]
+        L.oracle_leaf_partials_f64.restype = _I64
+        L.oracle_pairwise_f64.argtypes = [_P, _I64, _P]
+        L.oracle_partial_value_f64.argtypes = [ctypes.c_double, ctypes.c_double]
+        L.oracle_partial_value_f64.restype = ctypes.c_double
+        L.oracle_compact.argtypes = [_P, _I64, ctypes.c_uint32, _P, _P, ctypes.c_uint32, ctypes.c_float, _P, _P]
+        L.oracle_mask_count.argtypes = [_P, _I64]
+        L.oracle_mask_count.restype = ctypes.c_uint32
+        L.oracle_band_k.argtypes = [ctypes.c_double, _I64, _I64, _I64, _I64, _I64]
+        L.oracle_band_k.restype = _I64
+        L.oracle_policy_step.argtypes = [ctypes.c_uint32, ctypes.c_uint32, _P, _P, _P, _P, _I64, _I64] + \
+            [ctypes.c_int] * 7
+        L.oracle_oscillator_run.argtypes = [_I64, _P, _P, ctypes.c_double, ctypes.c_double, _P, _P, _P, _P, _P,
+                                            _I64, ctypes.c_int, _I64, _P]
+        L.oracle_corpus_f64.argtypes = [_I64, ctypes.c_uint64, _P]
+        L.oracle_corpus_f32.argtypes = [_I64, ctypes.c_uint64, _P]
+        L.oracle_fixture_f64.argtypes = [_I64, ctypes.c_double, _P, _P]
+        L.oracle_fixture_f64.restype = ctypes.c_double
+        L.oracle_fixture_f32.argtypes = [_I64, ctypes.c_double, _P, _P]
+        L.oracle_fixture_f32.restype = ctypes.c_double
+        _lib = L
+    return _lib
+
+
+def _ptr(a) -> int:
+    return 0 if a is None else a.ctypes.data
+
+
+def threads(n: int = 0) -> int:
+    """Set (n > 0) and return the OpenMP team size."""
+    return lib().oracle_threads(int(n))
+
+
+def reduce(x, op: str = "sum", *, columns: int = 1, comp=None, pair_out: bool = False):
+    """The canonical ``ordered`` reduction (eagle/reduce/canonical.h:10-32, :340-408)
+    of each column of the row-major ``(n, columns)`` array ``x``."""
+    x = np.ascontiguousarray(x)
+    code = _DTYPE_CODE[x.dtype]
+    if x.dtype == np.bool_:
+        x = x.view(np.uint8)
+    n = x.size // columns
+    out = np.zeros(columns * (2 if pair_out else 1), dtype=x.dtype)
+    c = None if comp is None else np.ascontiguousarray(comp, dtype=x.dtype)
+    rc = lib().oracle_reduce(_ptr(x), n, columns, code, _OPS[op], _ptr(c), _ptr(out), int(pair_out))
+    if rc != 0:
+        raise ValueError(f"oracle_reduce refused (status {rc})")
+    return out
+
+
+def leaf_partials(x):
+    """Per-leaf (hi, comp) partials of a float64 sum, leaf order: shape (leaves, 2)."""
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    m = (x.size + 4095) // 4096
+    hc = np.zeros((m, 2), dtype=np.float64)
+    lib().oracle_leaf_partials_f64(_ptr(x), x.size, _ptr(hc))
+    return hc
+
+
+def pairwise(hc):
+    """Level-by-level pairwise root of (hi, comp) partials (canonical.h:358-381)."""
+    hc = np.ascontiguousarray(hc, dtype=np.float64).reshape(-1, 2)
+    root = np.zeros(2, dtype=np.float64)
+    lib().oracle_pairwise_f64(_ptr(hc), hc.shape[0], _ptr(root))
+    return root
+
+
+def partial_value(h: float, c: float) -> float:
+    return lib().oracle_partial_value_f64(h, c)
+
+
+def compact(mask, *, drop: bool = True, span: int = 0, theta: float = 0.0, trigger: bool = False):
+    """Ascending map of the kept samples and its count (eagle/filtering/Compact.h:23-47);
+    with ``trigger`` also ``(live32, fire)`` (Compact.h:113-118)."""
+    m = np.ascontiguousarray(mask).view(np.uint8) if np.asarray(mask).dtype == np.bool_ \
+        else np.ascontiguousarray(mask, dtype=np.uint8)
+    n = m.size
+    index_map = np.zeros(max(n, 1), dtype=np.int32)
+    count = np.zeros(1, dtype=np.uint32)
+    live32 = np.zeros(1, dtype=np.uint32) if trigger else None
+    fire = np.zeros(1, dtype=np.uint32) if trigger else None
+    rc = lib().oracle_compact(_ptr(m), n, MASK_IS_DROP if drop else 0, _ptr(index_map), _ptr(count), span,
+                              theta, _ptr(live32), _ptr(fire))
+    if rc != 0:
+        raise ValueError(f"oracle_compact refused (status {rc})")
+    c = int(count[0])
+    if trigger:
+        return index_map[:c].copy(), c, int(live32[0]), int(fire[0])
+    return index_map[:c].copy(), c
+
+
+def mask_count(mask) -> int:
+    m = np.ascontiguousarray(mask).view(np.uint8)
+    return int(lib().oracle_mask_count(_ptr(m), m.size))
+
+
+def band_k(rate, newly, live, k, k_max, k_min=8) -> int:
+    """eagle/policy/Launch.h:184-190."""
+    return int(lib().oracle_band_k(float(rate), int(newly), int(live), int(k), int(k_max), int(k_min)))
+
+
+def policy_step(finished, total, cells, word, go, hist, k_min, k_max, idx=(0, 1, 2, 3, 4, 5), scale=1000):
+    """One POLICY cell op (python/src/plugin/eagle_cuda.cu:1990-2025) on int64 host cells, in place."""
+    lib().oracle_policy_step(int(finished), int(total), _ptr(cells), _ptr(word), _ptr(go), _ptr(hist),
+                             int(k_min), int(k_max), *[int(i) for i in idx], int(scale))
+
+
+def oscillator_run(omega, x, v, t, terminated, *, t_end, dt, max_steps, fused=False, tile=1024,
+                   steps_out=True):
+    """Run every live sample of the README Euler oscillator (README.md:89-97) until its
+    ``t >= t_end`` or ``max_steps`` steps, in place. ``t_end`` is a number (a Param) or a
+    per-sample array. Returns ``(steps_per_sample or None, finished, longest, total)``."""
+    n = omega.size
+    for a in (omega, x, v, t):
+        assert a.dtype == np.float64 and a.flags.c_contiguous and a.size == n
+    assert terminated.dtype in (np.uint8, np.bool_) and terminated.size == n
+    te_arr = None
+    te_uniform = 0.0
+    if np.ndim(t_end) == 0:
+        te_uniform = float(t_end)
+    else:
+        te_arr = np.ascontiguousarray(t_end, dtype=np.float64)
+    steps = np.zeros(n, dtype=np.int32) if steps_out else None
+    stats = np.zeros(3, dtype=np.int64)
+    rc = lib().oracle_oscillator_run(n, _ptr(omega), _ptr(te_arr), te_uniform, float(dt), _ptr(x), _ptr(v),
+                                     _ptr(t), _ptr(terminated.view(np.uint8)), _ptr(steps), int(max_steps),
+                                     int(bool(fused)), int(tile), _ptr(stats))
+    if rc != 0:
+        raise ValueError(f"oracle_oscillator_run refused (status {rc})")
+    return steps, int(stats[0]), int(stats[1]), int(stats[2])
+
+
+def corpus(n: int, seed: int, dtype=np.float64):
+    """The adversarial corpus of eagle's reduction tests (tests/CanonicalReduceCases.h:49-60):
+    normal values scaled by 10^U{-8..8}, std::mt19937_64(seed)."""
+    out = np.zeros(n, dtype=dtype)
+    if dtype == np.float64:
+        lib().oracle_corpus_f64(n, seed, _ptr(out))
+    else:
+        lib().oracle_corpus_f32(n, seed, _ptr(out))
+    return out
+
+
+def fixture(n: int, kappa: float, dtype=np.float64):
+    """The exact-sum fixture of eagle's reduction tests (tests/CanonicalReduceCases.h:141-176):
+    returns (values, exact sum, reached condition number)."""
+    x = np.zeros(n, dtype=dtype)
+    reached = np.zeros(1, dtype=np.float64)
+    f = lib().oracle_fixture_f64 if dtype == np.float64 else lib().oracle_fixture_f32
+    exact = f(n, float(kappa), _ptr(x), _ptr(reached))
+    return x, float(exact), float(reached[0])

@@ -1,0 +1,494 @@
+// Test infrastructure: the CPU restatement of eagle's until-done hot path that the
+// parity tests check the CUDA engine against. Nothing in the product links or calls
+// this file; only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg do.
+//
+// What it restates (paths relative to the eagle source tree):
+//   * the canonical ``ordered`` reduction tree: eagle/reduce/canonical.h:10-32
+//     (definition), :115-151 (Partial: of / add / join / value), :340-353 (leaf),
+//     :358-381 (pairwise), :397-408 (partialRange). The join arithmetic is the one
+//     the reference's own independent test oracle pins, tests/CanonicalReduceCases.h:73-78
+//     ("a Neumaier step is a join with (x, 0)", :94); MinOp is canonical.h:110-113.
+//   * active-set compaction: eagle/filtering/Compact.h:23-47 (ascending map of the
+//     kept samples, count), :113-118 (reorder trigger), :233-236 (n == 0).
+//   * the band policy: eagle/policy/Launch.h:184-190 (bandK) and the POLICY cell op,
+//     python/src/plugin/eagle_cuda.cu:1990-2025.
+//   * the until-done semantics of a finishing step kernel:
+//     docs/content/modules/filtering/run_until_done.rst:4-24,36-75 (a live sample steps,
+//     assigns ``terminated``, stops and is counted once when it is set); the fast-path
+//     step count (python/eagle/_until_done.py:1345-1352: the longest sample's steps);
+//     the Euler oscillator body of README.md:89-97 in its written expression order.
+//   * the host twin's team schedule: python/eagle/_host_loop.py:400-455 (tiles of
+//     contiguous samples, each run to completion), eagle/exec/HostTeam.h:23-27.
+//
+// Built with -ffp-contract=off: every floating-point operation below rounds once,
+// exactly as written. The ``fma`` variants call std::fma explicitly where the device
+// compiler would contract a multiply-add (x0 + dt*v0, v0 - c*x0).
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include <omp.h>
+#include <random>
+
+#include "oracle.h"
+
+namespace {
+
+// ---------------------------------------------------------------- canonical tree
+
+constexpr int64_t kSlots = 256;
+constexpr int64_t kTerms = 16;
+constexpr int64_t kLeaf = kSlots * kTerms;
+
+template <class T>
+struct Comp {  // a floating-point sum's partial: (hi, comp)
+    T h, c;
+    static Comp of(T x) { return {x, T(0)}; }
+    static Comp join(const Comp& a, const Comp& b)
+    {
+        const T s = a.h + b.h;
+        const T bb = s - a.h;
+        const T e = (a.h - (s - bb)) + (b.h - bb);
+        return {s, std::isfinite(s) ? (a.c + b.c) + e : T(0)};
+    }
+    // a Neumaier step is a join with (x, 0)
+    void add(T x) { *this = join(*this, Comp{x, T(0)}); }
+    // a term with a companion: canonical.h:139-143 (Neumaier step, then the companion)
+    void add(T x, T xc)
+    {
+        add(x);
+        c = std::isfinite(h) ? c + xc : T(0);
+    }
+    static Comp of(T x, T xc) { return {x, std::isfinite(x) ? xc : T(0)}; }
+    T value() const { return std::isfinite(h) ? h + c : h; }
+};
+
+template <class T, class Op>
+struct Plain {  // every exact operator folds plainly
+    T h;
+    static Plain of(T x) { return {x}; }
+    static Plain of(T x, T) { return {x}; }
+    static Plain join(const Plain& a, const Plain& b) { return {Op{}(a.h, b.h)}; }
+    void add(T x) { h = Op{}(h, x); }
+    void add(T x, T) { add(x); }
+    T value() const { return h; }
+};
+
+template <class T>
+struct SumOp {
+    T operator()(T a, T b) const
+    {
+        if constexpr (std::is_integral_v<T>) {
+            using U = std::make_unsigned_t<T>;
+            return T(U(a) + U(b));  // two's-complement wrap, as the device adds
+        } else {
+            return a + b;
+        }
+    }
+};
+template <class T>
+struct MaxOp {
+    T operator()(T a, T b) const { return a > b ? a : b; }
+};
+template <class T>
+struct MinOp {
+    T operator()(T a, T b) const { return a < b ? a : b; }
+};
+struct AllOp {
+    uint8_t operator()(uint8_t a, uint8_t b) const { return uint8_t((a != 0) && (b != 0)); }
+};
+
+// A column of a row-major (rows, cols) plane, with an optional companion plane.
+template <class T>
+struct ColumnIn {
+    const T* in;
+    const T* comp;
+    int64_t cols, col;
+    T x(int64_t i) const { return in[i * cols + col]; }
+    T xc(int64_t i) const { return comp[i * cols + col]; }
+};
+
+template <class P, class T>
+P leaf(const ColumnIn<T>& in, int64_t base, int64_t cnt)
+{
+    const int64_t live = std::min(cnt, kSlots);
+    P s[kSlots];
+    for (int64_t t = 0; t < live; ++t) {
+        for (int64_t k = t; k < cnt; k += kSlots) {
+            if (in.comp == nullptr) {
+                if (k == t)
+                    s[t] = P::of(in.x(base + k));
+                else
+                    s[t].add(in.x(base + k));
+            } else {
+                if (k == t)
+                    s[t] = P::of(in.x(base + k), in.xc(base + k));
+                else
+                    s[t].add(in.x(base + k), in.xc(base + k));
+            }
+        }
+    }
+    for (int64_t off = kSlots / 2; off > 0; off >>= 1)
+        for (int64_t t = 0; t < off; ++t)
+            if (t + off < live)
+                s[t] = P::join(s[t], s[t + off]);
+    return s[0];
+}
+
+// Level-by-level pairwise reduction of v[0, m), an odd last node carried.
+template <class P>
+P pairwise(std::vector<P>& v)
+{
+    int64_t m = int64_t(v.size());
+    while (m > 1) {
+        const int64_t pairs = m / 2;
+        for (int64_t i = 0; i < pairs; ++i)
+            v[i] = P::join(v[2 * i], v[2 * i + 1]);
+        if (m & 1)
+            v[pairs] = v[m - 1];
+        m = (m + 1) / 2;
+    }
+    return v[0];
+}
+
+template <class P, class T>
+std::vector<P> leafPartials(const ColumnIn<T>& in, int64_t rows)
+{
+    const int64_t nl = (rows + kLeaf - 1) / kLeaf;
+    std::vector<P> parts(static_cast<size_t>(nl));
+#pragma omp parallel for schedule(static)
+    for (int64_t l = 0; l < nl; ++l)
+        parts[size_t(l)] = leaf<P>(in, l * kLeaf, std::min(kLeaf, rows - l * kLeaf));
+    return parts;
+}
+
+template <class P, class T>
+P reduceColumn(const ColumnIn<T>& in, int64_t rows)
+{
+    auto parts = leafPartials<P>(in, rows);
+    return pairwise(parts);
+}
+
+template <class T, class Op>
+int reducePlainTyped(const void* in, int64_t n, int64_t cols, void* out)
+{
+    auto* o = static_cast<T*>(out);
+    for (int64_t j = 0; j < cols; ++j) {
+        ColumnIn<T> ci{static_cast<const T*>(in), nullptr, cols, j};
+        o[j] = reduceColumn<Plain<T, Op>>(ci, n).value();
+    }
+    return 0;
+}
+
+template <class T>
+int reduceSumFloat(const void* in, int64_t n, int64_t cols, const void* comp, void* out, int pairOut)
+{
+    auto* o = static_cast<T*>(out);
+    for (int64_t j = 0; j < cols; ++j) {
+        ColumnIn<T> ci{static_cast<const T*>(in), static_cast<const T*>(comp), cols, j};
+        const Comp<T> r = reduceColumn<Comp<T>>(ci, n);
+        if (pairOut) {
+            o[j] = r.h;
+            o[cols + j] = std::isfinite(r.h) ? r.c : T(0);
+        } else {
+            o[j] = r.value();
+        }
+    }
+    return 0;
+}
+
+// the exact-sum fixture of tests/CanonicalReduceCases.h:141-176 (used below)
+template <class T>
+double fixtureOf(int64_t n, double kappa, T* x, double* reached)
+{
+    std::mt19937_64 rng{static_cast<uint64_t>(n)};
+    std::uniform_int_distribution<int> unit(1, 8);
+    std::uniform_real_distribution<double> mag(1.0, 2.0);
+    std::vector<double> big(static_cast<size_t>(n));
+    long long units = 0;
+    int64_t nbig = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t j = std::min(i, n - 1 - i);
+        big[size_t(j)] = mag(rng);
+        if (j % 4 == 0 || i == n - 1 - i) {
+            const int u = unit(rng);
+            units += u;
+            x[i] = T(std::ldexp(double(u), -10));
+        } else {
+            ++nbig;
+        }
+    }
+    const double exact = std::ldexp(double(units), -10);
+    const double scale = kappa * exact / (1.5 * double(std::max<int64_t>(nbig, 1)));
+    double abs = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t j = std::min(i, n - 1 - i);
+        if (!(j % 4 == 0 || i == n - 1 - i))
+            x[i] = (i < n - 1 - i) ? T(big[size_t(j)] * scale) : -T(big[size_t(j)] * scale);
+        abs += std::fabs(double(x[i]));
+    }
+    *reached = abs / exact;
+    return exact;
+}
+
+}  // namespace
+
+extern "C" {
+
+int oracle_threads(int threads)
+{
+    if (threads > 0)
+        omp_set_num_threads(threads);
+    return omp_get_max_threads();
+}
+
+int oracle_reduce(const void* in, int64_t n, int64_t cols, int dtype, int op, const void* comp_in,
+    void* out, int pair_out)
+{
+    if (n < 1 || cols < 1 || in == nullptr || out == nullptr)
+        return 2;
+    const bool fsum = op == ORACLE_OP_SUM && (dtype == ORACLE_F32 || dtype == ORACLE_F64);
+    if ((comp_in != nullptr || pair_out) && !fsum)
+        return 2;
+    if ((op == ORACLE_OP_ALL) != (dtype == ORACLE_U8))
+        return 2;
+    switch (dtype) {
+    case ORACLE_F32:
+        if (op == ORACLE_OP_SUM)
+            return reduceSumFloat<float>(in, n, cols, comp_in, out, pair_out);
+        if (op == ORACLE_OP_MAX)
+            return reducePlainTyped<float, MaxOp<float>>(in, n, cols, out);
+        return reducePlainTyped<float, MinOp<float>>(in, n, cols, out);
+    case ORACLE_F64:
+        if (op == ORACLE_OP_SUM)
+            return reduceSumFloat<double>(in, n, cols, comp_in, out, pair_out);
+        if (op == ORACLE_OP_MAX)
+            return reducePlainTyped<double, MaxOp<double>>(in, n, cols, out);
+        return reducePlainTyped<double, MinOp<double>>(in, n, cols, out);
+    case ORACLE_I32:
+        if (op == ORACLE_OP_SUM)
+            return reducePlainTyped<int32_t, SumOp<int32_t>>(in, n, cols, out);
+        if (op == ORACLE_OP_MAX)
+            return reducePlainTyped<int32_t, MaxOp<int32_t>>(in, n, cols, out);
+        return reducePlainTyped<int32_t, MinOp<int32_t>>(in, n, cols, out);
+    case ORACLE_I64:
+        if (op == ORACLE_OP_SUM)
+            return reducePlainTyped<int64_t, SumOp<int64_t>>(in, n, cols, out);
+        if (op == ORACLE_OP_MAX)
+            return reducePlainTyped<int64_t, MaxOp<int64_t>>(in, n, cols, out);
+        return reducePlainTyped<int64_t, MinOp<int64_t>>(in, n, cols, out);
+    case ORACLE_U8:
+        return reducePlainTyped<uint8_t, AllOp>(in, n, cols, out);
+    default:
+        return 2;
+    }
+}
+
+int64_t oracle_leaf_partials_f64(const double* x, int64_t n, double* hc)
+{
+    if (n < 1)
+        return 0;
+    ColumnIn<double> ci{x, nullptr, 1, 0};
+    const auto parts = leafPartials<Comp<double>>(ci, n);
+    for (size_t i = 0; i < parts.size(); ++i) {
+        hc[2 * i] = parts[i].h;
+        hc[2 * i + 1] = parts[i].c;
+    }
+    return int64_t(parts.size());
+}
+
+void oracle_pairwise_f64(const double* hc, int64_t m, double* root_hc)
+{
+    std::vector<Comp<double>> v(static_cast<size_t>(m));
+    for (int64_t i = 0; i < m; ++i)
+        v[size_t(i)] = {hc[2 * i], hc[2 * i + 1]};
+    const auto r = pairwise(v);
+    root_hc[0] = r.h;
+    root_hc[1] = r.c;
+}
+
+double oracle_partial_value_f64(double h, double c)
+{
+    return std::isfinite(h) ? h + c : h;
+}
+
+// ------------------------------------------------------------------- compaction
+
+int oracle_compact(const uint8_t* mask, int64_t n, uint32_t flags, int32_t* index_map, uint32_t* count,
+    uint32_t span, float theta, uint32_t* live32, uint32_t* fire)
+{
+    if (n < 0 || n > INT64_C(2147483647))
+        return 8;
+    const bool drop = (flags & ORACLE_MASK_IS_DROP) != 0;
+    uint32_t c = 0, groups = 0;
+    for (int64_t g = 0; g * 32 < n; ++g) {
+        bool any = false;
+        for (int64_t i = g * 32; i < std::min<int64_t>(n, (g + 1) * 32); ++i) {
+            const bool set = mask[i] != 0;
+            if (drop ? !set : set) {
+                index_map[c++] = int32_t(i);
+                any = true;
+            }
+        }
+        groups += any ? 1u : 0u;
+    }
+    *count = c;
+    if (live32 != nullptr) {
+        *live32 = groups;
+        const double limit = double(theta) * 32.0 * double(groups);
+        *fire = (double(c) < limit && c < span && span >= 4096u) ? 1u : 0u;
+    }
+    return 0;
+}
+
+uint32_t oracle_mask_count(const uint8_t* mask, int64_t n)
+{
+    uint32_t c = 0;
+    for (int64_t i = 0; i < n; ++i)
+        c += mask[i] != 0 ? 1u : 0u;
+    return c;
+}
+
+// ----------------------------------------------------------------------- policy
+
+int64_t oracle_band_k(double rate, int64_t newly, int64_t live, int64_t k, int64_t k_max, int64_t k_min)
+{
+    if (newly <= 0)
+        return k_max;
+    const double e2 = 2.0 * rate * double(live) * double(k) / double(newly);
+    int64_t p = 1;
+    while (p < (INT64_C(1) << 30) && e2 >= 2.0 * double(p) * double(p))
+        p *= 2;
+    return std::min(std::max(p, k_min), k_max);
+}
+
+void oracle_policy_step(uint32_t finished, uint32_t total, int64_t* cells, int64_t* word, uint32_t* go,
+    int64_t* hist, int64_t k_min, int64_t k_max, int iK, int iFin, int iDone, int iCap, int iR, int iMapped,
+    int scale)
+{
+    const int64_t fin = finished, all = total;
+    const int64_t live = all - fin, newly = fin - cells[iFin];
+    const int64_t done = cells[iDone] + word[0];
+    cells[iMapped] += all - cells[iFin];
+    cells[iFin] = fin;
+    cells[iDone] = done;
+    const int64_t k = cells[iK];
+    const double rate = double(cells[iR]) / double(scale);
+    const int64_t k_next = oracle_band_k(rate, newly, live, k, k_max, k_min);
+    cells[iK] = k_next;
+    const int64_t left = cells[iCap] - done;
+    const uint32_t g = (fin != all) && (left > 0);
+    go[0] = g;
+    if (g) {
+        const int64_t w = k_next < left ? k_next : left;
+        word[0] = w;
+        hist[w] += 1;
+    }
+}
+
+// ------------------------------------------------------------ Euler oscillator
+
+// One sample of the README oscillator run until it terminates or has taken
+// ``max_steps`` steps in this run; returns the steps taken.
+static inline int64_t oscillatorSample(double omega, double t_end, double dt, double& x, double& v, double& t,
+    uint8_t& term, int64_t max_steps, bool fused)
+{
+    if (term != 0)
+        return 0;
+    const double c = (dt * omega) * omega;  // ((dt*omega)*omega), hoisted: the same product every step
+    double x0 = x, v0 = v, tt = t;
+    int64_t s = 0;
+    while (s < max_steps) {
+        double x1, v1;
+        if (fused) {
+            x1 = std::fma(dt, v0, x0);
+            v1 = std::fma(-c, x0, v0);
+        } else {
+            x1 = x0 + dt * v0;
+            v1 = v0 - c * x0;
+        }
+        x0 = x1;
+        v0 = v1;
+        tt = tt + dt;
+        ++s;
+        if (tt >= t_end) {
+            term = 1;
+            break;
+        }
+    }
+    x = x0;
+    v = v0;
+    t = tt;
+    return s;
+}
+
+int oracle_oscillator_run(int64_t n, const double* omega, const double* t_end, double t_end_uniform, double dt,
+    double* x, double* v, double* t, uint8_t* term, int32_t* steps_out, int64_t max_steps, int fused,
+    int64_t tile, int64_t* stats)
+{
+    if (n < 0 || max_steps < 0)
+        return 2;
+    if (tile <= 0)
+        tile = 1024;
+    const int64_t tiles = (n + tile - 1) / tile;
+    int64_t finished = 0, longest = 0, total = 0;
+#pragma omp parallel for schedule(dynamic, 1) reduction(+ : finished, total) reduction(max : longest)
+    for (int64_t b = 0; b < tiles; ++b) {
+        const int64_t end = std::min(n, (b + 1) * tile);
+        for (int64_t i = b * tile; i < end; ++i) {
+            const double te = t_end != nullptr ? t_end[i] : t_end_uniform;
+            const int64_t s = oscillatorSample(omega[i], te, dt, x[i], v[i], t[i], term[i], max_steps, fused != 0);
+            if (steps_out != nullptr)
+                steps_out[i] = int32_t(s);
+            finished += term[i] != 0 ? 1 : 0;
+            longest = std::max(longest, s);
+            total += s;
+        }
+    }
+    if (stats != nullptr) {
+        stats[0] = finished;
+        stats[1] = longest;
+        stats[2] = total;
+    }
+    return 0;
+}
+
+// ------------------------------------------------------- reference test corpora
+//
+// The inputs of eagle's canonical-reduction tests, regenerated with the same
+// standard-library engines and distributions (libstdc++): the adversarial corpus
+// of tests/CanonicalReduceCases.h:49-60 and the exact-sum fixture of :141-176
+// (mirrored +-x pairs that cancel exactly, plus a residual on a 2^-10 grid whose
+// exact sum is known).
+
+void oracle_corpus_f64(int64_t n, uint64_t seed, double* out)
+{
+    std::mt19937_64 rng(seed);
+    std::normal_distribution<double> nd(0.0, 1.0);
+    std::uniform_int_distribution<int> ex(-8, 8);
+    for (int64_t i = 0; i < n; ++i)
+        out[i] = nd(rng) * std::pow(10.0, ex(rng));
+}
+
+void oracle_corpus_f32(int64_t n, uint64_t seed, float* out)
+{
+    std::mt19937_64 rng(seed);
+    std::normal_distribution<double> nd(0.0, 1.0);
+    std::uniform_int_distribution<int> ex(-8, 8);
+    for (int64_t i = 0; i < n; ++i)
+        out[i] = float(nd(rng) * std::pow(10.0, ex(rng)));
+}
+
+double oracle_fixture_f64(int64_t n, double kappa, double* x, double* reached)
+{
+    return fixtureOf<double>(n, kappa, x, reached);
+}
+
+double oracle_fixture_f32(int64_t n, double kappa, float* x, double* reached)
+{
+    return fixtureOf<float>(n, kappa, x, reached);
+}
+
+}  // extern "C"

@@ -1,0 +1,150 @@
+"""The C-ABI library without a GPU: it loads, exports exactly the seam symbols the
+header declares, its desc layouts match the C header, and the calls that need no
+device (queries, argument refusals, the probe) behave as the seam specifies
+(python/src/seam/eagle_backend.h of the eagle source tree)."""
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from eagle_b200 import _abi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "eagle_b200.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(eagle_backend_\w+)\s*\(", text)))
+
+
+def _exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", _abi.LIB_PATH], capture_output=True, text=True, check=True)
+    return sorted(line.split()[-1] for line in out.stdout.splitlines() if " T " in line)
+
+
+def test_library_loads_and_reports_its_version():
+    L = _abi.lib()
+    assert L.eagle_backend_version() == (1 << 16) | 8
+    groups = ctypes.c_uint64()
+    assert L.eagle_backend_capabilities(ctypes.byref(groups)) == _abi.OK
+    assert groups.value == _abi.CAP_STREAM | _abi.CAP_EXEC | _abi.CAP_DEVICE | _abi.CAP_FILTERING
+    info = _abi.new(_abi.BuildInfo)
+    assert L.eagle_backend_build_info(ctypes.byref(info)) == _abi.OK
+    assert info.backend_kind == b"cuda" and info.abi_version == (1 << 16) | 8
+
+
+def test_exports_are_exactly_the_declared_seam():
+    declared = _declared()
+    exported = _exported()
+    assert declared, "no declarations parsed"
+    assert set(declared) == set(exported), (set(declared) ^ set(exported))
+    assert all(name.startswith("eagle_backend_") for name in exported)
+    assert set(_abi.SIGNATURES) == set(declared)
+
+
+_LAYOUTS = {
+    "eagle_backend_build_info": _abi.BuildInfo,
+    "eagle_backend_device_props": _abi.DeviceProps,
+    "eagle_backend_launch_desc": _abi.LaunchDesc,
+    "eagle_backend_launch_raw_desc": _abi.LaunchRawDesc,
+    "eagle_backend_cell_op_desc": _abi.CellOpDesc,
+    "eagle_backend_compact_desc": _abi.CompactDesc,
+    "eagle_backend_reorder_desc": _abi.ReorderDesc,
+    "eagle_backend_reduce_desc": _abi.ReduceDesc,
+    "eagle_b200_engine_desc": _abi.EngineDesc,
+    "eagle_b200_report": _abi.Report,
+}
+
+
+def test_desc_layouts_match_the_header(tmp_path):
+    """Compile the header with gcc and compare every struct's size and field offsets
+    with the ctypes mirrors (and the seam's sizes of eagle_backend.h:171-906)."""
+    lines = ['#include <stddef.h>', '#include <stdio.h>', f'#include "{HEADER}"', "int main(void) {"]
+    for cname, ct in _LAYOUTS.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof(struct {cname}));')
+        for fname, _ in ct._fields_:
+            cf = "in" if fname == "in_" else fname
+            lines.append(f'printf("{cname}.{fname} %zu\\n", offsetof(struct {cname}, {cf}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-o", str(exe), str(src)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                               check=True).stdout.splitlines())
+    for cname, ct in _LAYOUTS.items():
+        assert int(got[cname]) == ctypes.sizeof(ct), cname
+        for fname, _ in ct._fields_:
+            assert int(got[f"{cname}.{fname}"]) == getattr(ct, fname).offset, (cname, fname)
+    # the seam's own struct sizes
+    assert int(got["eagle_backend_compact_desc"]) == 104
+    assert int(got["eagle_backend_reduce_desc"]) == 96
+    assert int(got["eagle_backend_cell_op_desc"]) == 208
+
+
+def test_compact_query_needs_no_device():
+    d = _abi.new(_abi.CompactDesc, n=100_003, flags=_abi.COMPACT_MASK_IS_DROP)
+    assert _abi.lib().eagle_backend_compact_device(ctypes.byref(d)) == _abi.OK
+    assert d.scratch_bytes >= 8 * ((100_003 + 4095) // 4096)
+
+
+def test_compact_refuses_past_int32_and_negative():
+    L = _abi.lib()
+    d = _abi.new(_abi.CompactDesc, n=2 ** 31, scratch=1, mask=1, index_map=1, count=1)
+    assert L.eagle_backend_compact_device(ctypes.byref(d)) == _abi.UNSUPPORTED
+    assert "2^31-1" in _abi.last_error()
+    d = _abi.new(_abi.CompactDesc, n=-1)
+    assert L.eagle_backend_compact_device(ctypes.byref(d)) == _abi.INVALID_ARGUMENT
+
+
+def test_unknown_flag_bits_are_refused():
+    d = _abi.new(_abi.CompactDesc, n=10, flags=1 << 7)
+    assert _abi.lib().eagle_backend_compact_device(ctypes.byref(d)) == _abi.UNSUPPORTED
+
+
+def test_reduce_argument_refusals():
+    L = _abi.lib()
+    d = _abi.new(_abi.ReduceDesc, n=0)
+    assert L.eagle_backend_x_reduce_canonical(ctypes.byref(d)) == _abi.INVALID_ARGUMENT
+    d = _abi.new(_abi.ReduceDesc, n=10, dtype=_abi.REDUCE_F64, op=_abi.REDUCE_OP_ALL)
+    assert L.eagle_backend_x_reduce_canonical(ctypes.byref(d)) == _abi.INVALID_ARGUMENT
+    d = _abi.new(_abi.ReduceDesc, n=10, dtype=_abi.REDUCE_I64, op=_abi.REDUCE_OP_SUM, flags=_abi.REDUCE_PAIR_OUT,
+                 columns=1)
+    assert L.eagle_backend_x_reduce_canonical(ctypes.byref(d)) == _abi.INVALID_ARGUMENT
+
+
+def test_cell_op_array_ops_unsupported():
+    d = _abi.new(_abi.CellOpDesc, op=7, n=4)
+    assert _abi.lib().eagle_backend_cell_op(ctypes.byref(d)) == _abi.UNSUPPORTED
+
+
+def test_entry_lookup_unknown_name():
+    f = ctypes.c_uint64()
+    assert _abi.lib().eagle_backend_x_b200_entry(b"no_such_kernel", -1, ctypes.byref(f)) == _abi.INDEX
+
+
+def test_probe_without_a_device():
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            pytest.skip("a device is visible")
+    except ImportError:
+        pass
+    assert _abi.lib().eagle_backend_probe() == _abi.UNAVAILABLE
+    assert "no CUDA device" in _abi.last_error()
+
+
+def test_last_error_clears_on_success():
+    L = _abi.lib()
+    d = _abi.new(_abi.CompactDesc, n=-1)
+    L.eagle_backend_compact_device(ctypes.byref(d))
+    assert _abi.last_error()
+    d = _abi.new(_abi.CompactDesc, n=5)
+    assert L.eagle_backend_compact_device(ctypes.byref(d)) == _abi.OK
+    assert _abi.last_error() == ""
