@@ -1,0 +1,401 @@
+"""Benchmark: sample-steps/s of eagle's until-done loop on the 16M-sample
+heterogeneous-stop Euler oscillator, per GPU shard, with the HBM roofline figures.
+
+Workload (one "step" = one until-done run of the whole batch, from its initial
+state, then the canonical sum of the final x): n = 16,777,216 fp64 samples per GPU,
+omega ~ U[1, 3], x ~ N(1, 0.1), v = t = 0, dt = 1e-3, t_end log-uniform in
+[0.01, 10] per sample, max_steps = 10,000 (about 1446 steps per sample on average,
+2.4e10 sample-steps per run). Synthetic, seeded (numpy default_rng: seed 1 omega,
+2 x, 3 t_end; rank r > 0 uses [seed, r]). Under torchrun every rank runs its own
+contiguous shard of N x 16M samples (weak scaling); the rank partials of the
+canonical sum are all-gathered over NCCL and folded in rank order on the device.
+
+``--impl reference`` times the CPU restatement of eagle's host path (the oracle,
+OpenMP over all host cores) on a bounded prefix of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sample-steps/s, 16M heterogeneous-stop oscillator; HBM GB/s vs roofline"
+UNIT = "sample-steps/s"
+N_PER_GPU = 1 << 24
+MAX_STEPS = 10_000
+DT = 1e-3
+B_STEP = 66  # bytes one sample-step of eagle's unfused kernel reads and writes (omega, t_end, x, v, t, mask)
+WORKLOAD = "euler-oscillator-heterogeneous-stop"
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="engine", choices=("engine", "reference"))
+    p.add_argument("--mode", default="auto", choices=("auto", "band", "band_eager", "persist", "fused"))
+    p.add_argument("--n", type=int, default=N_PER_GPU, help="samples per GPU")
+    p.add_argument("--no-fma", action="store_true", help="exact (uncontracted) arithmetic profile")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=15.0)
+    return p.parse_args()
+
+
+def _inputs(rank: int, n: int):
+    def rng(seed):
+        return np.random.default_rng(seed if rank == 0 else [seed, rank])
+
+    omega = rng(1).uniform(1.0, 3.0, n)
+    x0 = rng(2).normal(1.0, 0.1, n)
+    t_end = 10.0 ** rng(3).uniform(-2.0, 1.0, n)
+    return omega, x0, t_end
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class _Clocks:
+    """nvidia-smi samples (SM clock, reasons) taken during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [q.strip() for q in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _cpu_baseline(omega, x0, t_end, budget_s: float):
+    """The oracle (CPU restatement of eagle's host path, OpenMP, all host threads)
+    on a contiguous prefix of the workload sized to about ``budget_s`` seconds."""
+    import oracle
+
+    oracle.build()
+    cores = oracle.threads()
+    n = omega.size
+
+    def run(m):
+        st = [x0[:m].copy(), np.zeros(m), np.zeros(m), np.zeros(m, np.uint8)]
+        t0 = time.perf_counter()
+        _, fin, longest, total = oracle.oscillator_run(omega[:m], *st, t_end=t_end[:m], dt=DT, max_steps=MAX_STEPS,
+                                                       steps_out=False)
+        return total, time.perf_counter() - t0
+
+    m = min(n, 1 << 16)
+    total, sec = run(m)
+    rate = total / max(sec, 1e-9)
+    per_sample = total / m
+    m = int(min(n, max(m, budget_s * rate / per_sample)))
+    m = max(4096, m // 4096 * 4096) if m < n else n
+    total, sec = run(m)
+    return {"value": total / sec, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"the first {m} of the {n} samples of one GPU shard ({total} sample-steps, {sec:.2f} s), "
+                      f"run to completion on {cores} OpenMP threads"}
+
+
+def reference(args):
+    """The CPU arm: the oracle on the host cores, on bounded samples of the workload."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    omega, x0, t_end = _inputs(0, args.n)
+    import oracle
+
+    oracle.build()
+    cores = oracle.threads()
+    per_step = max(2.0, 150.0 / max(1, args.steps + args.warmup))
+    # size one step's prefix from a calibration run
+    m = 1 << 16
+    st = [x0[:m].copy(), np.zeros(m), np.zeros(m), np.zeros(m, np.uint8)]
+    t0 = time.perf_counter()
+    _, _, _, total = oracle.oscillator_run(omega[:m], *st, t_end=t_end[:m], dt=DT, max_steps=MAX_STEPS,
+                                           steps_out=False)
+    rate = total / max(time.perf_counter() - t0, 1e-9)
+    m = int(min(args.n, max(4096, per_step * rate / (total / m))))
+    m = m // 4096 * 4096 if m < args.n else args.n
+    times, totals = [], []
+    for i in range(args.warmup + args.steps):
+        st = [x0[:m].copy(), np.zeros(m), np.zeros(m), np.zeros(m, np.uint8)]
+        t0 = time.perf_counter()
+        _, fin, longest, total = oracle.oscillator_run(omega[:m], *st, t_end=t_end[:m], dt=DT, max_steps=MAX_STEPS,
+                                                       steps_out=False)
+        s = oracle.reduce(st[0])
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+            totals.append(total)
+    value = sum(totals) / sum(times)
+    sample = (f"the first {m} of the {args.n} samples per GPU shard ({totals[0]} sample-steps per step), "
+              f"{cores} OpenMP threads, each sample run to completion then the canonical sum of x")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded numpy)",
+            "config": {"workload": WORKLOAD, "n_per_gpu": args.n, "max_steps": MAX_STEPS, "dt": DT,
+                       "sampled_n": m},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def engine(args):
+    import torch
+
+    import eagle_b200 as eb
+    from eagle_b200 import _abi
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    n = args.n
+    mode = "persist" if args.mode == "auto" else args.mode
+    fma = not args.no_fma
+    omega, x0, t_end = _inputs(rank, n)
+    dev = torch.device("cuda", local)
+    d_om = torch.from_numpy(omega).to(dev)
+    d_te = torch.from_numpy(t_end).to(dev)
+    d_x0 = torch.from_numpy(x0).to(dev)
+    x = torch.empty_like(d_x0)
+    v = torch.zeros_like(d_x0)
+    t = torch.zeros_like(d_x0)
+    mask = torch.zeros(n, dtype=torch.uint8, device=dev)
+    runner = eb.until_done(eb.oscillator, max_steps=MAX_STEPS, mode=mode, fma=fma, terminated=mask, omega=d_om,
+                           t_end=d_te, dt=DT, x=x, v=v, t=t)
+    red = eb.Reducer(x, pair_out=True)
+    gathered = torch.zeros(2 * world, dtype=torch.float64, device=dev)
+    combine_work = torch.zeros(2 * world + 2, dtype=torch.float64, device=dev)
+    result = torch.zeros(3, dtype=torch.float64, device=dev)
+    lib = _abi.lib()
+
+    def step(stream):
+        x.copy_(d_x0)
+        v.zero_()
+        t.zero_()
+        mask.zero_()
+        runner.launch(stream)
+        red(stream)
+        if dist is not None:
+            dist.all_gather_into_tensor(gathered, red.out)
+            src = gathered
+        else:
+            src = red.out
+        _abi.check(lib.eagle_backend_x_b200_combine_partials(src.data_ptr(), world, combine_work.data_ptr(),
+                                                             result.data_ptr(), stream.cuda_stream))
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step(stream)
+    rep = runner.report(stream)  # raises if the device reported an error word
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _Clocks(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step(stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        dist.barrier()
+    rep = runner.report(stream)
+    steps_per_run = rep.step_sum
+    # engine-only time per run (the dominant kernel's launches), for the roofline
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    eng_ms = []
+    for _ in range(3):
+        x.copy_(d_x0)
+        v.zero_()
+        t.zero_()
+        mask.zero_()
+        f0.record(stream)
+        runner.launch(stream)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        eng_ms.append(f0.elapsed_time(f1))
+    eng = statistics.median(eng_ms)
+    mx = torch.tensor([ms, eng], dtype=torch.float64, device=dev)
+    tot = torch.tensor([float(steps_per_run)], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    ms, eng = float(mx[0]), float(mx[1])
+    all_steps = float(tot[0])
+    value = all_steps * args.steps / (ms / 1e3)
+
+    # e2e: the same runs through the C-ABI with the inputs in pinned host memory
+    e2e = None
+    if not args.no_e2e:
+        h_om = torch.from_numpy(omega).pin_memory()
+        h_te = torch.from_numpy(t_end).pin_memory()
+        h_x0 = torch.from_numpy(x0).pin_memory()
+        h_zero = torch.zeros(n, dtype=torch.float64).pin_memory()
+        h_res = torch.zeros(3, dtype=torch.float64).pin_memory()
+        s = stream.cuda_stream
+        plane_bytes = 8 * n
+
+        def e2e_step():
+            for dst, src in ((d_om, h_om), (d_te, h_te), (x, h_x0), (v, h_zero), (t, h_zero)):
+                _abi.check(lib.eagle_backend_memcpy(dst.data_ptr(), src.data_ptr(), plane_bytes, _abi.COPY_H2D, s))
+            _abi.check(lib.eagle_backend_memset_device(mask.data_ptr(), n, s))
+            runner.launch(stream)
+            red(stream)
+            if dist is not None:
+                dist.all_gather_into_tensor(gathered, red.out)
+                src = gathered
+            else:
+                src = red.out
+            _abi.check(lib.eagle_backend_x_b200_combine_partials(src.data_ptr(), world, combine_work.data_ptr(),
+                                                                 result.data_ptr(), s))
+            _abi.check(lib.eagle_backend_memcpy(h_res.data_ptr(), result.data_ptr(), 24, _abi.COPY_D2H, s))
+            return runner.report(stream)  # the run report: one more small device-to-host read
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            r2 = e2e_step()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        ems = torch.tensor([g0.elapsed_time(g1)], dtype=torch.float64, device=dev)
+        if dist is not None:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e = {"value": all_steps * args.steps / (float(ems[0]) / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": 5 * plane_bytes, "d2h_bytes_per_step": 24 + int(r2.report_bytes),
+               "ms_per_step": float(ems[0]) / args.steps}
+
+    if rank != 0:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    peak, peak_kind = _peaks()
+    achieved = B_STEP * steps_per_run / (eng / 1e3) / 1e9
+    passes = rep.launches
+    launches_per_step = (passes + 2 if mode == "band" else 2) + 1 + 1  # engine kernels, the sum, the combine
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                traffic = json.load(f).get(f"{mode}_{'fma' if fma else 'exact'}")
+        except Exception:
+            traffic = None
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded numpy, see bench.py)",
+        "config": {"workload": WORKLOAD, "n_per_gpu": n, "n_total": n * world, "max_steps": MAX_STEPS, "dt": DT,
+                   "mode": mode, "arith": "fma" if fma else "exact", "sample_steps_per_gpu_step": steps_per_run,
+                   "status": "finished" if rep.done else "max_steps", "passes": passes,
+                   "l2": "inputs larger than L2 (5 x 128 MiB planes per GPU, re-initialised every step)",
+                   "parallelism": f"shard{world}"},
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                     "basis": "66 B per sample-step (eagle's unfused per-step plane traffic) x sample-steps "
+                              "per run / engine time per run; the fused kernel keeps state in registers, so "
+                              "this effective figure exceeds the physical DRAM rate"},
+        "clocks": clocks.summary(),
+    }
+    res = result.cpu().numpy()
+    line["result"] = {"sum_x": float(res[2]), "mean_x": float(res[2]) / (n * world), "finished": rep.finished,
+                      "steps": rep.steps}
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = _cpu_baseline(omega, x0, t_end, args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        reference(args)
+    else:
+        engine(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -27,7 +27,7 @@ REDUCE_PAIR_OUT = 1
 COPY_H2D, COPY_D2H, COPY_D2D, COPY_H2H = range(4)
 
 MODEL_OSCILLATOR, MODEL_OSCILLATOR_SPREAD = 0, 1
-MODE_BAND, MODE_PERSIST, MODE_FUSED = 0, 1, 2
+MODE_BAND, MODE_PERSIST, MODE_FUSED, MODE_BAND_EAGER = 0, 1, 2, 3
 FLAG_FMA = 1
 
 
@@ -120,7 +120,8 @@ class ScalarHandle(ctypes.Structure):
 
 class Report(ctypes.Structure):
     _fields_ = [("struct_size", _u32), ("done", _u32), ("n", _i64), ("finished", _i64), ("steps", _i64),
-                ("launches", _i64), ("compactions", _i64), ("step_sum", _u64), ("error", _u32), ("mode", _u32)]
+                ("launches", _i64), ("compactions", _i64), ("step_sum", _u64), ("error", _u32), ("mode", _u32),
+                ("report_bytes", _u32), ("reserved0", _u32)]
 
 
 def new(struct_type, **fields):
@@ -173,6 +174,7 @@ SIGNATURES = {
     "eagle_backend_reset_device": (_i32, [ctypes.POINTER(ReorderDesc)]),
     "eagle_backend_x_reduce_canonical": (_i32, [ctypes.POINTER(ReduceDesc)]),
     "eagle_backend_x_b200_entry": (_i32, [ctypes.c_char_p, _i32, ctypes.POINTER(_u64)]),
+    "eagle_backend_x_b200_combine_partials": (_i32, [_u64, _i64, _u64, _u64, _u64]),
     "eagle_backend_x_b200_engine_create": (_i32, [ctypes.POINTER(EngineDesc), ctypes.POINTER(_P)]),
     "eagle_backend_x_b200_engine_launch": (_i32, [_P, _u64]),
     "eagle_backend_x_b200_engine_report": (_i32, [_P, _u64, ctypes.POINTER(Report)]),

@@ -72,7 +72,8 @@ class _Oscillator(Model):
 oscillator = _Oscillator(name="oscillator", planes=("omega", "t_end", "x", "v", "t"), mutable=("x", "v", "t"),
                          params=("t_end", "dt"))
 
-_MODES = {"band": _abi.MODE_BAND, "persist": _abi.MODE_PERSIST, "fused": _abi.MODE_FUSED}
+_MODES = {"band": _abi.MODE_BAND, "persist": _abi.MODE_PERSIST, "fused": _abi.MODE_FUSED,
+          "band_eager": _abi.MODE_BAND_EAGER}
 
 
 # ------------------------------------------------------------------------- reports
@@ -94,6 +95,7 @@ class RunReport:
     step_sum: int
     mode: str
     exact_steps: bool = True
+    report_bytes: int = 0
 
 
 class SimResult:
@@ -247,7 +249,7 @@ class Runner:
                                                                      ctypes.byref(r)))
         return RunReport(n=int(r.n), finished=int(r.finished), done=bool(r.done), steps=int(r.steps),
                          launches=int(r.launches), compactions=int(r.compactions), step_sum=int(r.step_sum),
-                         mode=self.mode)
+                         mode=self.mode, report_bytes=int(r.report_bytes))
 
     def run(self, stream=None) -> RunReport:
         self.launch(stream)

@@ -94,8 +94,8 @@ __device__ __forceinline__ int64_t bandK(double rate, int64_t newly, int64_t liv
     return p < kMin ? kMin : (p > kMax ? kMax : p);
 }
 
-template <bool Fma, bool Spread>
-__global__ __launch_bounds__(kBandThreads) void bandKernel(BandArgs a)
+template <bool Fma, bool Spread, bool Graph>
+__global__ __launch_bounds__(kBandThreads, 6) void bandKernel(BandArgs a)
 {
     __shared__ uint32_t sTile;
     __shared__ uint32_t scan[33];
@@ -111,7 +111,9 @@ __global__ __launch_bounds__(kBandThreads) void bandKernel(BandArgs a)
         const unsigned long long started = atomicAdd(&c->guard, 1ull) + 1ull;
         if (started > (unsigned long long)c->cap + 1ull) {
             atomicOr(&c->err, 2u);
-            cudaGraphSetConditional(a.cond, 0u);
+            c->go = 0;
+            if constexpr (Graph)
+                cudaGraphSetConditional(a.cond, 0u);
         }
     }
     const uint32_t iter = c->iter;
@@ -162,7 +164,7 @@ __global__ __launch_bounds__(kBandThreads) void bandKernel(BandArgs a)
         int64_t taken = 0;
         bool fin = false;
         if (valid)
-            fin = s.run(a.dt, word, taken);
+            taken = s.run(a.dt, int(word), fin);
         bool keep = valid && !fin;
         if (valid && (fin || last)) {
             // a sample leaving the loop: its state goes home
@@ -265,10 +267,12 @@ __global__ __launch_bounds__(kBandThreads) void bandKernel(BandArgs a)
     c->tileNext = 0;
     c->ctasDone = 0;
     __threadfence();
-    cudaGraphSetConditional(a.cond, go);
+    if constexpr (Graph)
+        cudaGraphSetConditional(a.cond, go);
 }
 
 /** Reset the run cells and arm the WHILE condition (one thread). */
+template <bool Graph>
 __global__ void bandInitKernel(Cells* c, int64_t n, cudaGraphConditionalHandle cond)
 {
     c->iter = 0;
@@ -288,7 +292,8 @@ __global__ void bandInitKernel(Cells* c, int64_t n, cudaGraphConditionalHandle c
     c->epoch = c->epoch + 1;
     const uint32_t go = (c->cap > 0 && n > 0) ? 1u : 0u;
     c->go = go;
-    cudaGraphSetConditional(cond, go);
+    if constexpr (Graph)
+        cudaGraphSetConditional(cond, go);
 }
 
 /** After the loop: a run that took no pass still reports its mask count. */
@@ -317,22 +322,29 @@ struct Engine {
     void* records = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    BandArgs band{};
+    uint32_t* goHost = nullptr;  // pinned: the eager band loop's condition word
     int bandGrid = 0, persistGrid = 0;
     uint32_t chunk = 32, block = 256;
     bool fma = false, spread = false;
 };
 
-template <bool Fma, bool Spread>
+template <bool Fma, bool Spread, bool Graph>
 void* bandKernelPtr()
 {
-    return reinterpret_cast<void*>(&bandKernel<Fma, Spread>);
+    return reinterpret_cast<void*>(&bandKernel<Fma, Spread, Graph>);
 }
 
-void* pickBand(bool fma, bool spread)
+void* pickBand(bool fma, bool spread, bool graph = true)
 {
+    if (graph) {
+        if (fma)
+            return spread ? bandKernelPtr<true, true, true>() : bandKernelPtr<true, false, true>();
+        return spread ? bandKernelPtr<false, true, true>() : bandKernelPtr<false, false, true>();
+    }
     if (fma)
-        return spread ? bandKernelPtr<true, true>() : bandKernelPtr<true, false>();
-    return spread ? bandKernelPtr<false, true>() : bandKernelPtr<false, false>();
+        return spread ? bandKernelPtr<true, true, false>() : bandKernelPtr<true, false, false>();
+    return spread ? bandKernelPtr<false, true, false>() : bandKernelPtr<false, false, false>();
 }
 
 void buildBandGraph(Engine& e, BandArgs& args)
@@ -347,7 +359,7 @@ void buildBandGraph(Engine& e, BandArgs& args)
         int64_t n = e.n;
         void* params[] = {&e.cells, &n, &cond};
         cudaKernelNodeParams p{};
-        p.func = reinterpret_cast<void*>(&bandInitKernel);
+        p.func = reinterpret_cast<void*>(&bandInitKernel<true>);
         p.gridDim = dim3(1);
         p.blockDim = dim3(1);
         p.kernelParams = params;
@@ -392,6 +404,25 @@ void launchEngine(Engine& e, cudaStream_t s)
 {
     if (e.mode == EAGLE_B200_MODE_BAND) {
         cudaCheck(cudaGraphLaunch(e.exec, s), "cudaGraphLaunch");
+        return;
+    }
+    if (e.mode == EAGLE_B200_MODE_BAND_EAGER) {
+        // the same passes, driven from the host: one condition read per pass
+        bandInitKernel<false><<<1, 1, 0, s>>>(e.cells, e.n, cudaGraphConditionalHandle{});
+        launchCheck("band init");
+        void* pass = pickBand(e.fma, e.spread, false);
+        for (;;) {
+            cudaCheck(cudaMemcpyAsync(e.goHost, &e.cells->go, sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
+                "cudaMemcpyAsync");
+            cudaCheck(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+            if (*e.goHost == 0)
+                break;
+            void* params[] = {&e.band};
+            cudaCheck(cudaLaunchKernel(pass, dim3(unsigned(e.bandGrid)), dim3(kBandThreads), params, 0, s),
+                "cudaLaunchKernel");
+        }
+        bandFinishKernel<<<unsigned(std::max(1, smCount())), 256, 0, s>>>(e.cells, e.term, e.n);
+        launchCheck("band finish");
         return;
     }
     // persist / fused: zero the run words, count the mask, one launch
@@ -469,7 +500,8 @@ void readReport(Engine& e, cudaStream_t s, eagle_b200_report* out)
     r.finished = c.finished;
     r.done = uint32_t(int64_t(c.finished) == e.n);
     r.mode = e.mode;
-    if (e.mode == EAGLE_B200_MODE_BAND) {
+    r.report_bytes = uint32_t(sizeof(Cells));
+    if (e.mode == EAGLE_B200_MODE_BAND || e.mode == EAGLE_B200_MODE_BAND_EAGER) {
         r.steps = int64_t(c.longest);
         r.launches = c.iter;
         r.compactions = c.iter;
@@ -502,6 +534,7 @@ void destroy(Engine* e)
     (void)cudaFree(e->status);
     (void)cudaFree(e->records);
     (void)cudaFreeHost(e->host);
+    (void)cudaFreeHost(e->goHost);
     (void)cudaSetDevice(prev);
     delete e;
 }
@@ -523,13 +556,13 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
             invalid(std::string(who) + ": null output");
         if (d.model > EAGLE_B200_MODEL_OSCILLATOR_SPREAD)
             unsupported(std::string(who) + ": unknown model " + std::to_string(d.model));
-        if (d.mode > EAGLE_B200_MODE_FUSED)
+        if (d.mode > EAGLE_B200_MODE_BAND_EAGER)
             unsupported(std::string(who) + ": unknown mode " + std::to_string(d.mode));
         if (d.n < 0 || d.n > INT64_C(2147483647))
             unsupported(std::string(who) + ": n must lie in [0, 2^31 - 1]");
         if (d.max_steps < 0)
             invalid(std::string(who) + ": max_steps must be >= 0");
-        if (d.mode != EAGLE_B200_MODE_BAND && d.max_steps > INT64_C(4294967295))
+        if ((d.mode == EAGLE_B200_MODE_PERSIST || d.mode == EAGLE_B200_MODE_FUSED) && d.max_steps > INT64_C(4294967295))
             unsupported(std::string(who) + ": the persist and fused entries count steps in 32 bits");
         const bool spread = d.model == EAGLE_B200_MODEL_OSCILLATOR_SPREAD;
         const int nPlanes = spread ? 5 : 4;
@@ -564,16 +597,17 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
             init.cap = d.max_steps;
             init.kFirst = d.k_first > 0 ? d.k_first : 16;
             init.kMin = d.k_min > 0 ? d.k_min : 8;
-            init.kMax = d.k_max > 0 ? d.k_max : 4096;
+            init.kMax = d.k_max > 0 ? std::min<int64_t>(d.k_max, INT64_C(1) << 30) : 4096;
             init.overheadSteps = d.overhead_steps > 0 ? d.overhead_steps : 2.0e7;
             init.intervalSteps = d.interval_steps > 0 ? d.interval_steps : 16.0;
             init.budget = d.max_steps;
             init.total = uint32_t(d.n);
             cudaCheck(cudaMemcpy(e->cells, &init, sizeof init, cudaMemcpyHostToDevice), "cudaMemcpy");
             int occ = 0;
-            if (e->mode == EAGLE_B200_MODE_BAND) {
-                cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, pickBand(e->fma, spread),
-                              kBandThreads, 0),
+            const bool band = e->mode == EAGLE_B200_MODE_BAND || e->mode == EAGLE_B200_MODE_BAND_EAGER;
+            if (band) {
+                cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ,
+                              pickBand(e->fma, spread, e->mode == EAGLE_B200_MODE_BAND), kBandThreads, 0),
                     "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
                 e->bandGrid = std::max(1, occ) * smCount();
                 const int64_t tiles = std::max<int64_t>(1, (d.n + kBandThreads - 1) / kBandThreads);
@@ -614,7 +648,11 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
                     args.rte[b] = spread ? p + 4 * cap : nullptr;
                     args.ridx[b] = reinterpret_cast<int32_t*>(p + size_t(doubles) * size_t(cap));
                 }
-                buildBandGraph(*e, args);
+                e->band = args;
+                if (e->mode == EAGLE_B200_MODE_BAND)
+                    buildBandGraph(*e, e->band);
+                else
+                    cudaCheck(cudaMallocHost(&e->goHost, sizeof(uint32_t)), "cudaMallocHost");
             } else {
                 const void* stub = entryStub(std::string(spread ? "oscillator_spread" : "oscillator") + "_persist"
                     + (e->fma ? "_fma" : ""));

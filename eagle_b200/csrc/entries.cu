@@ -97,7 +97,7 @@ __device__ __forceinline__ void rangeBody(const ScalarHandle& omega, const TEnd<
         s.t = dplane(t)[i];
         s.c = Oscillator<Fma>::coeff(dt, static_cast<const double*>(omega.data)[i]);
         s.te = tEnd.at(i);
-        fin = s.run(dt, budget, taken);
+        taken = s.runLong(dt, budget, fin);
         dplane(x)[i] = s.x;
         dplane(v)[i] = s.v;
         dplane(t)[i] = s.t;
@@ -128,11 +128,14 @@ __global__ __launch_bounds__(256) void oscillatorRange(EB_OSC_ROLES(TEnd<Spread>
         hawkStepsum);
 }
 
-/** The persistent entry: at each chunk head the lanes of a warp without a
- *  sample claim the next ones together off ``hawk_next`` (one atomic per warp),
- *  skipping samples already terminated, until the partition is exhausted; each
- *  lane then runs up to ``chunk`` steps of its sample, within the budget. A lane
- *  whose sample ends mid-chunk waits, masked, for the next head. */
+/** The persistent entry. Every lane holds its current sample and, one chunk
+ *  ahead, the NEXT one: at each chunk head the lanes of a warp lacking a next
+ *  sample claim the following indices together off ``hawk_next`` (one atomic per
+ *  warp) and issue its loads, which complete while the chunk runs; a lane whose
+ *  sample ended takes its prefetched one without waiting. A claimed sample
+ *  already terminated is skipped (python/eagle/_plan_binding.py:431-446). Each
+ *  lane runs up to ``chunk`` steps of its sample per head, within the budget; a
+ *  lane whose sample ends mid-chunk waits, masked, for the next head. */
 template <bool Fma, bool Spread>
 __global__ __launch_bounds__(256) void oscillatorPersist(EB_OSC_ROLES(TEnd<Spread>), uint32_t* hawkNext,
     unsigned long long* hawkUtil, uint32_t* hawkSteps, unsigned long long* hawkStepsum, uint32_t hawkChunk)
@@ -140,58 +143,77 @@ __global__ __launch_bounds__(256) void oscillatorPersist(EB_OSC_ROLES(TEnd<Sprea
     (void)nSamples;
     const unsigned lane = threadIdx.x & 31u;
     uint8_t* term = static_cast<uint8_t*>(terminated.data);
+    const double* om = static_cast<const double*>(omega.data);
     const int64_t budget = *static_cast<const int64_t*>(fused.data);
-    const int64_t chunk = hawkChunk == 0 ? 32 : int64_t(hawkChunk);
+    const int chunk = hawkChunk == 0 ? 32 : int(hawkChunk < (1u << 20) ? hawkChunk : (1u << 20));
     uint32_t* finished_ = static_cast<uint32_t*>(finished.data);
-    Oscillator<Fma> s{};
-    int64_t i = -1;       // the lane's sample, -1: none
-    int64_t taken = 0;    // steps of the lane's sample so far
+    Oscillator<Fma> cur{}, nxt{};
+    int64_t i = -1, ni = -1;  // the lane's current and prefetched samples (-1: none)
+    uint8_t nterm = 0;        // the prefetched sample's mask byte
+    int64_t taken = 0;        // steps of the current sample so far
     bool exhausted = false;
     uint32_t finCount = 0, longest = 0;  // the lane's run counters, flushed once at the end
     unsigned long long ranSum = 0, slots = 0;
-    for (;;) {
-        // claim: every lane without a sample takes the next unclaimed index
-        for (;;) {
-            const bool needs = i < 0 && !exhausted;
-            const unsigned want = __ballot_sync(kFull, needs);
-            if (want == 0)
-                break;
-            const unsigned leader = __ffs(want) - 1;
-            uint32_t first = 0;
-            if (lane == leader)
-                first = atomicAdd(hawkNext, uint32_t(__popc(want)));
-            first = __shfl_sync(kFull, first, leader);
-            if (needs) {
-                const int64_t k = int64_t(first) + __popc(want & ((1u << lane) - 1u));
-                if (k >= count) {
-                    exhausted = true;
-                } else if (term[base + k] == 0) {
-                    i = base + k;
-                    s.x = dplane(x)[i];
-                    s.v = dplane(v)[i];
-                    s.t = dplane(t)[i];
-                    s.c = Oscillator<Fma>::coeff(dt, static_cast<const double*>(omega.data)[i]);
-                    s.te = tEnd.at(i);
-                    taken = 0;
-                }
+
+    // lanes without a next sample claim one and issue its loads (no wait here)
+    auto prefetch = [&]() {
+        const bool needs = ni < 0 && !exhausted;
+        const unsigned want = __ballot_sync(kFull, needs);
+        if (want == 0)
+            return;
+        const unsigned leader = __ffs(want) - 1;
+        uint32_t first = 0;
+        if (lane == leader)
+            first = atomicAdd(hawkNext, uint32_t(__popc(want)));
+        first = __shfl_sync(kFull, first, leader);
+        if (needs) {
+            const int64_t k = int64_t(first) + __popc(want & ((1u << lane) - 1u));
+            if (k >= count) {
+                exhausted = true;
+            } else {
+                ni = base + k;
+                nterm = term[ni];
+                nxt.x = dplane(x)[ni];
+                nxt.v = dplane(v)[ni];
+                nxt.t = dplane(t)[ni];
+                nxt.c = om[ni];  // the coefficient is formed at the swap
+                nxt.te = tEnd.at(ni);
             }
         }
-        if (__ballot_sync(kFull, i >= 0) == 0)
+    };
+    // lanes without a current sample take the prefetched one (a terminated one is skipped)
+    auto swap = [&]() {
+        if (i < 0 && ni >= 0) {
+            if (nterm == 0) {
+                cur = nxt;
+                cur.c = Oscillator<Fma>::coeff(dt, nxt.c);
+                i = ni;
+                taken = 0;
+            }
+            ni = -1;
+        }
+    };
+
+    prefetch();
+    for (;;) {
+        swap();
+        prefetch();
+        const bool active = i >= 0;
+        if (__ballot_sync(kFull, active || ni >= 0) == 0)
             break;
-        int64_t ran = 0;
+        int ran = 0;
         bool fin = false;
-        if (i >= 0) {
+        if (active) {
             const int64_t room = budget - taken;
-            fin = s.run(dt, room < chunk ? room : chunk, ran);
+            ran = cur.run(dt, int(room < chunk ? room : chunk), fin);
             taken += ran;
         }
         ranSum += (unsigned long long)ran;
         slots += (unsigned long long)chunk;
-        const bool ends = i >= 0 && (fin || taken >= budget);
-        if (ends) {
-            dplane(x)[i] = s.x;
-            dplane(v)[i] = s.v;
-            dplane(t)[i] = s.t;
+        if (active && (fin || taken >= budget)) {
+            dplane(x)[i] = cur.x;
+            dplane(v)[i] = cur.v;
+            dplane(t)[i] = cur.t;
             if (fin) {
                 term[i] = 1;
                 ++finCount;

@@ -30,7 +30,8 @@ struct Oscillator {
         return __dmul_rn(__dmul_rn(dt, omega), omega);
     }
 
-    __device__ __forceinline__ bool step(double dt)
+    /** x and v one step on (t is advanced by the caller). */
+    __device__ __forceinline__ void stepXV(double dt)
     {
         double x1, v1;
         if constexpr (Fma) {
@@ -42,26 +43,64 @@ struct Oscillator {
         }
         x = x1;
         v = v1;
-        t = __dadd_rn(t, dt);
-        return t >= te;
     }
 
-    /** Run at most ``budget`` steps; ``taken`` = steps run; true if the sample
-     *  terminated on its last step. */
-    __device__ __forceinline__ bool run(double dt, int64_t budget, int64_t& taken)
+    __device__ __forceinline__ void step(double dt)
     {
-        int64_t s = 0;
-        bool fin = false;
-#pragma unroll 4
-        for (; s < budget;) {
-            ++s;
-            if (step(dt)) {
-                fin = true;
-                break;
+        stepXV(dt);
+        t = __dadd_rn(t, dt);
+    }
+
+    static constexpr int kBlock = 8;
+
+    /** Run at most ``budget`` (>= 0) steps; returns the steps run, ``fin`` true if
+     *  the sample terminated on the last of them.
+     *
+     *  The stop test reads t only, and t advances by dt alone. With dt >= 0 the
+     *  rounded sums t, t + dt, ... never decrease, so when t after a whole block of
+     *  kBlock steps is still below t_end no step inside the block stopped: the
+     *  block's t is formed first (the same additions, in the same order) and, if it
+     *  stays below t_end, x and v take the block's steps with no per-step test.
+     *  The block holding the stop, and any dt that is negative or NaN, take the
+     *  steps one at a time with the test after each, as the model is written. */
+    __device__ __forceinline__ int run(double dt, int budget, bool& fin)
+    {
+        int s = 0;
+        fin = false;
+        if (dt >= 0.0) {
+            for (; s + kBlock <= budget; s += kBlock) {
+                double tb = t;
+#pragma unroll
+                for (int k = 0; k < kBlock; ++k)
+                    tb = __dadd_rn(tb, dt);
+                if (tb >= te)
+                    break;
+#pragma unroll
+                for (int k = 0; k < kBlock; ++k)
+                    stepXV(dt);
+                t = tb;
             }
         }
-        taken = s;
-        return fin;
+        for (; s < budget; ++s) {
+            step(dt);
+            if (t >= te) {
+                fin = true;
+                return s + 1;
+            }
+        }
+        return s;
+    }
+
+    /** ``run`` for a 64-bit budget, in pieces of at most 2^30 steps. */
+    __device__ __forceinline__ int64_t runLong(double dt, int64_t budget, bool& fin)
+    {
+        int64_t total = 0;
+        fin = false;
+        while (total < budget && !fin) {
+            const int64_t left = budget - total;
+            total += run(dt, left < (INT64_C(1) << 30) ? int(left) : (1 << 30), fin);
+        }
+        return total;
     }
 };
 

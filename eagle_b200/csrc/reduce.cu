@@ -247,6 +247,39 @@ __global__ __launch_bounds__(kSlots) void canonicalKernel(ReduceArgs a)
     }
 }
 
+/** Pairwise levels over m (hi, comp) partials -- chunk results in chunk order,
+ *  e.g. one per rank -- into out = {hi, comp, value}. One CTA. */
+__global__ __launch_bounds__(kSlots) void combinePairsKernel(const double* __restrict__ hc, int64_t m,
+    double* __restrict__ work, double* __restrict__ out)
+{
+    __shared__ CompP<double> v[kChunk];
+    const double* src = hc;
+    int64_t count = m;
+    while (count > 1) {
+        const int64_t chunks = (count + kChunk - 1) / kChunk;
+        for (int64_t c = 0; c < chunks; ++c) {
+            const int cnt = int(count - c * kChunk < kChunk ? count - c * kChunk : kChunk);
+            for (int i = int(threadIdx.x); i < cnt; i += int(blockDim.x))
+                v[i] = CompP<double>{src[2 * (c * kChunk + i)], src[2 * (c * kChunk + i) + 1]};
+            __syncthreads();
+            levels(v, cnt);
+            if (threadIdx.x == 0) {
+                work[2 * c] = v[0].h;
+                work[2 * c + 1] = v[0].c;
+            }
+            __syncthreads();
+        }
+        src = work;
+        count = chunks;
+    }
+    if (threadIdx.x == 0) {
+        const CompP<double> r{src[0], src[1]};
+        out[0] = r.h;
+        out[1] = r.c;
+        out[2] = r.value();
+    }
+}
+
 // ------------------------------------------------------------------- host side
 
 int64_t leafCount(int64_t rows) { return (rows + kLeaf - 1) / kLeaf; }
@@ -408,5 +441,21 @@ extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_bac
         }
         if (query)
             desc->work_elems = workElems;
+    });
+}
+
+extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_backend_x_b200_combine_partials(
+    uint64_t hc, int64_t m, uint64_t work, uint64_t out, uint64_t stream)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_combine_partials";
+        if (m < 1)
+            invalid(std::string(who) + ": m must be >= 1");
+        if (hc == 0 || out == 0 || (m > 1 && work == 0))
+            invalid(std::string(who) + ": hc, out and (for m > 1) work must be device addresses");
+        DeviceScope scope(resolveDevice(-1, hc));
+        combinePairsKernel<<<1, kSlots, 0, seamStream(stream)>>>(reinterpret_cast<const double*>(hc), m,
+            reinterpret_cast<double*>(work), reinterpret_cast<double*>(out));
+        launchCheck(who);
     });
 }

@@ -323,6 +323,16 @@ eagle_backend_status eagle_backend_x_reduce_canonical(struct eagle_backend_reduc
 
 /* ---- this backend's additions (no counterpart entry in the seam) --------------- */
 
+/* eagle_backend_x_b200_combine_partials: combine ``m`` float64 (hi, comp) partials
+ * ``hc[2m]`` (chunk roots in chunk order, e.g. one per rank; each chunk
+ * leafSize * 2^q samples) by the canonical pairwise levels into ``out[3]`` = {hi,
+ * comp, value}: the bits of the reduction over the concatenated chunks
+ * (eagle/reduce/canonical.h:30-32, :424-439, the rank-order fold of
+ * eagle/exec/RankPartition.h:230-241). ``work`` holds 2 * ceil(m / 512) doubles
+ * (unused for m == 1). One single-CTA kernel; enqueue only. */
+eagle_backend_status eagle_backend_x_b200_combine_partials(uint64_t hc, int64_t m, uint64_t work, uint64_t out,
+    uint64_t stream);
+
 /* eagle_backend_x_b200_entry: the CUfunction (as uint64) of one of this backend's
  * built-in step kernels by name, for run_device / launch_raw. The kernels take the
  * hawk argument ABI: role arguments packed as eagle's registry packs them
@@ -344,6 +354,7 @@ eagle_backend_status eagle_backend_x_b200_entry(const char* name, int32_t device
 #define EAGLE_B200_MODE_BAND 0u    /* one CUDA graph: WHILE { fused step + compaction + policy } */
 #define EAGLE_B200_MODE_PERSIST 1u /* one persistent launch: lanes claim samples off a counter */
 #define EAGLE_B200_MODE_FUSED 2u   /* one launch, one lane per sample, the whole budget */
+#define EAGLE_B200_MODE_BAND_EAGER 3u /* the band passes launched from the host, one condition read per pass */
 
 #define EAGLE_B200_FLAG_FMA 1u /* contract x0 + dt*v0 and v0 - c*x0 into fused multiply-adds */
 
@@ -378,8 +389,11 @@ struct eagle_b200_report {
     int64_t launches;     /* loop iterations (band) or 1 */
     int64_t compactions;  /* compactions run (band) */
     uint64_t step_sum;    /* steps executed by all samples in this run */
-    uint32_t error;       /* device error word: 0 = none (bit 0: a look-back wait gave up) */
+    uint32_t error;       /* device error word: 0 = none (bit 0: a look-back wait gave up,
+                           * bit 1: the band loop was stopped by its pass guard) */
     uint32_t mode;
+    uint32_t report_bytes; /* bytes the report read moved device -> host */
+    uint32_t reserved0;
 };
 
 /* The models' plane orders: OSCILLATOR planes = {omega, x, v, t}, uniforms = {t_end,

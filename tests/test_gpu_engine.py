@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
 
-MODES = ("band", "persist", "fused")
+MODES = ("band", "band_eager", "persist", "fused")
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "golden.json")
 
 
@@ -63,7 +63,8 @@ def test_uniform_stop_readme_batch(eb, orc, mode, fma):
     ref, ((_, fin, longest, total),) = _oracle_run(orc, om, 1.0, n, 10_000, fma)
     _assert_same(dev, ref)
     assert rep.done and rep.finished == n and rep.steps == 1000 == longest and rep.step_sum == total
-    assert np.array_equal(np.round(dev[0][:3], 8), [0.54057281, 0.54057112, 0.54056944])
+    # sample 0 (omega = 1 exactly) does not depend on n: README.md:105's x[0]
+    assert round(float(dev[0][0]), 8) == 0.54057281
 
 
 @pytest.mark.parametrize("mode", MODES)
