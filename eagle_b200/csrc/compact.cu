@@ -14,6 +14,8 @@
 // the last tile alone knows count and live32 and writes count, live32 and fire.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace eb {
 namespace {
 
@@ -444,6 +446,109 @@ EB_API eagle_backend_status eagle_backend_cell_op(const struct eagle_backend_cel
             scaleCountKernel<<<1, 1, 0, s>>>(reinterpret_cast<const uint32_t*>(d.p[0]),
                 reinterpret_cast<uint32_t*>(d.p[1]), int(d.i[0]));
         }
+        launchCheck(who);
+    });
+}
+
+// ---------------------------------------------------------- allocation-free form
+//
+// Some callers of the compaction cannot allocate device memory: code that runs
+// where an allocation would break its guarantees (inside a latency-critical
+// loop, where cudaMalloc may synchronise the device), bindings from a host
+// language that has no handle on the process's CUDA allocator, or a runtime
+// whose device memory is fixed at start-up. For them the scratch of one
+// compaction lives in a file-scope device array instead of a caller buffer.
+
+namespace eb {
+namespace {
+
+/** The largest batch the allocation-free compaction serves (2^28 samples). */
+constexpr int64_t kNoAllocMaxSamples = INT64_C(1) << 28;
+/** One status word per 4096-sample tile, then the tile counter and the error word. */
+constexpr size_t kNoAllocScratchBytes = size_t(kNoAllocMaxSamples / kTile) * sizeof(uint64_t) + 256;
+
+/** The scratch every allocation-free call shares (each device that loads this
+ *  library holds its own copy until the process exits). Host code must not use
+ *  this name as an address: see noAllocScratch. */
+static __device__ __align__(256) unsigned char g_noAllocScratch[kNoAllocScratchBytes];
+
+/** The device address of g_noAllocScratch on ``device`` (current when called),
+ *  looked up on the first call for that device and kept. */
+void* noAllocScratch(int device)
+{
+    static std::mutex mu;
+    static void* addr[256] = {};
+    if (device < 0 || device >= 256)
+        invalid("eagle_backend_x_b200_compact_device_noalloc: device ordinal out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[device] == nullptr) {
+        void* p = nullptr;
+        cudaCheck(cudaGetSymbolAddress(&p, g_noAllocScratch), "cudaGetSymbolAddress");
+        addr[device] = p;
+    }
+    return addr[device];
+}
+
+}  // namespace
+}  // namespace eb
+
+EB_API eagle_backend_status eagle_backend_x_b200_compact_device_noalloc(struct eagle_backend_compact_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_compact_device_noalloc";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        if (d.n < 0)
+            invalid(std::string(who) + ": n must be >= 0");
+        if (d.n > kNoAllocMaxSamples)
+            unsupported(std::string(who) + ": n = " + std::to_string(d.n) + " exceeds the "
+                + std::to_string(kNoAllocMaxSamples) + " samples its built-in scratch serves; use "
+                "eagle_backend_compact_device with caller scratch");
+        if (d.scratch != 0)
+            invalid(std::string(who) + ": takes no scratch (leave the field 0)");
+        if (d.count == 0 || (d.n > 0 && (d.mask == 0 || d.index_map == 0)))
+            invalid(std::string(who) + ": mask, index_map and count must be device addresses");
+        const bool trigger = d.live32 != 0;
+        if (trigger) {
+            if (d.span == 0 || d.fire == 0)
+                invalid(std::string(who) + ": a trigger needs live32, span and fire");
+            if (d.reserved2 != 0)
+                invalid(std::string(who) + ": reserved2 must be zero");
+            if (!(d.theta > 0.0f && d.theta < 1.0f))
+                invalid(std::string(who) + ": the trigger's theta must lie in (0, 1)");
+        }
+        const int dev = resolveDevice(d.device, d.mask != 0 ? d.mask : d.count);
+        DeviceScope scope(dev);
+        const cudaStream_t s = seamStream(d.stream);
+        if (d.n == 0) {
+            compactEmptyKernel<<<1, 1, 0, s>>>(reinterpret_cast<uint32_t*>(d.count),
+                trigger ? reinterpret_cast<uint32_t*>(d.live32) : nullptr,
+                trigger ? reinterpret_cast<uint32_t*>(d.fire) : nullptr);
+            launchCheck(who);
+            return;
+        }
+        char* scratch = static_cast<char*>(noAllocScratch(dev));
+        CompactArgs a{};
+        a.mask = reinterpret_cast<const uint8_t*>(d.mask);
+        a.n = d.n;
+        a.map = reinterpret_cast<int32_t*>(d.index_map);
+        a.count = reinterpret_cast<uint32_t*>(d.count);
+        a.tiles = uint32_t((d.n + kTile - 1) / kTile);
+        a.status = reinterpret_cast<uint64_t*>(scratch);
+        a.tileNext = reinterpret_cast<uint32_t*>(scratch + size_t(a.tiles) * sizeof(uint64_t));
+        a.err = a.tileNext + 1;
+        a.live32 = reinterpret_cast<uint32_t*>(d.live32);
+        a.span = reinterpret_cast<const uint32_t*>(d.span);
+        a.fire = reinterpret_cast<uint32_t*>(d.fire);
+        a.theta = d.theta;
+        // the status words, the tile counter and the error word start at zero on every call
+        cudaCheck(cudaMemsetAsync(scratch, 0, size_t(a.tiles) * sizeof(uint64_t) + 2 * sizeof(uint32_t), s),
+            "cudaMemsetAsync");
+        const bool aligned = (d.mask & 15u) == 0;
+        const bool drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
+        if (drop)
+            trigger ? launchCompact<true, true>(a, aligned, s) : launchCompact<true, false>(a, aligned, s);
+        else
+            trigger ? launchCompact<false, true>(a, aligned, s) : launchCompact<false, false>(a, aligned, s);
         launchCheck(who);
     });
 }

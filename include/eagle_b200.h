@@ -311,6 +311,19 @@ eagle_backend_status eagle_backend_compact_device(struct eagle_backend_compact_d
  * *count = *span = n, in one kernel; capture-legal */
 eagle_backend_status eagle_backend_reset_device(struct eagle_backend_reorder_desc* desc);
 
+/* eagle_backend_x_b200_compact_device_noalloc: compact_device for callers that
+ * cannot allocate device memory (no counterpart in the reference: eagle's
+ * compaction always takes caller scratch). Same desc, same outputs, same flags and
+ * trigger; ``scratch`` must be 0 and no query is needed. Its working memory is a
+ * fixed 512 KiB + 256 B array inside this library on every device that loads it,
+ * enough for n <= 2^28 samples; a larger n returns UNSUPPORTED. It allocates
+ * nothing: it enqueues one memset of that array and the compaction kernel. The
+ * first call on a device looks the array's address up (cudaGetSymbolAddress), so
+ * make that first call before any stream capture. Every call shares the one array:
+ * calls that may overlap on the GPU (other streams, other threads) race and must
+ * be serialised by the caller. */
+eagle_backend_status eagle_backend_x_b200_compact_device_noalloc(struct eagle_backend_compact_desc* desc);
+
 /* ---- canonical reduction (experimental; eagle_backend.h:896-906) -------------- */
 
 /* The canonical fixed-order reduction of each column of the row-major (n, columns)
