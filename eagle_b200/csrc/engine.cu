@@ -589,7 +589,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
             std::memcpy(e->planes, d.planes, sizeof e->planes);
             std::memcpy(e->uniforms, d.uniforms, sizeof e->uniforms);
             e->term = reinterpret_cast<uint8_t*>(d.terminated);
-            e->chunk = d.chunk == 0 ? 32u : d.chunk;
+            e->chunk = d.chunk == 0 ? 256u : d.chunk;
             e->block = 256;
             cudaCheck(cudaMalloc(&e->cells, sizeof(Cells)), "cudaMalloc");
             cudaCheck(cudaMallocHost(&e->host, sizeof(Cells)), "cudaMallocHost");

@@ -386,7 +386,7 @@ struct eagle_b200_engine_desc {
     int64_t k_first;     /* band: steps of the first launch (0: 16) */
     int64_t k_min;       /* band: fewest steps per launch but the last (0: 8) */
     int64_t k_max;       /* band: most steps per launch (0: 4096) */
-    uint32_t chunk;      /* persist: steps between claims, a power of two (0: 32) */
+    uint32_t chunk;      /* persist: steps between claims, a power of two (0: 256) */
     uint32_t block;      /* threads per block (0: 256) */
     double overhead_steps; /* band: a launch's fixed cost in sample-steps (0: built-in) */
     double interval_steps; /* band: a launch's per-sample memory cost in steps (0: built-in) */
