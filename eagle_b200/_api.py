@@ -446,3 +446,48 @@ def entry(name: str, device: int = -1) -> int:
     f = ctypes.c_uint64()
     _abi.check(_abi.lib().eagle_backend_x_b200_entry(name.encode(), int(device), ctypes.byref(f)))
     return int(f.value)
+
+
+class CompactSum:
+    """Compact the samples ``mask`` keeps and take the canonical sum of their
+    ``values`` (float64), in two kernels with no host read in between: the
+    compaction writes the kept values in sample order (``eagle_backend_x_b200_compact_gather``)
+    and the reduction reads the kept count on the device
+    (``eagle_backend_x_b200_reduce_counted``). Buffers are allocated once;
+    :meth:`__call__` only enqueues. ``drop=True`` treats set bytes as dropped (a
+    ``terminated`` mask), ``drop=False`` as kept."""
+
+    def __init__(self, mask, values, *, drop: bool = False, pair_out: bool = False):
+        torch = _t()
+        if not (isinstance(mask, torch.Tensor) and mask.is_cuda and mask.dtype in (torch.bool, torch.uint8)):
+            raise ValueError("CompactSum takes a bool/uint8 CUDA mask")
+        if not (isinstance(values, torch.Tensor) and values.is_cuda and values.dtype == torch.float64
+                and values.is_contiguous() and values.numel() == mask.numel()):
+            raise ValueError("CompactSum takes contiguous float64 CUDA values, one per mask byte")
+        n = mask.numel()
+        dev = mask.device
+        self.mask, self.values = mask, values
+        self.kept = torch.empty(max(n, 1), dtype=torch.float64, device=dev)
+        self.count = torch.zeros(1, dtype=torch.int32, device=dev)
+        d = _abi.new(_abi.CompactDesc, flags=_abi.COMPACT_MASK_IS_DROP if drop else 0, device=dev.index, n=n)
+        _abi.check(_abi.lib().eagle_backend_x_b200_compact_gather(ctypes.byref(d), 0, 0, 8))  # query
+        self.scratch = torch.empty(max(int(d.scratch_bytes), 1), dtype=torch.uint8, device=dev)
+        d.mask, d.count, d.scratch = _ptr(mask), _ptr(self.count), _ptr(self.scratch)
+        self.cdesc = d
+        r = _abi.new(_abi.ReduceDesc, dtype=_abi.REDUCE_F64, op=_abi.REDUCE_OP_SUM, device=dev.index, n=max(n, 1),
+                     policy=_abi.REDUCE_ORDERED, flags=_abi.REDUCE_PAIR_OUT if pair_out else 0, columns=1)
+        _abi.check(_abi.lib().eagle_backend_x_b200_reduce_counted(ctypes.byref(r), 0))  # query
+        self.work_a = torch.empty(int(r.work_elems), dtype=torch.float64, device=dev)
+        self.work_b = torch.empty(int(r.work_elems), dtype=torch.float64, device=dev)
+        self.out = torch.empty(2 if pair_out else 1, dtype=torch.float64, device=dev)
+        r.in_, r.out, r.work_a, r.work_b = _ptr(self.kept), _ptr(self.out), _ptr(self.work_a), _ptr(self.work_b)
+        self.rdesc = r
+
+    def __call__(self, stream=None):
+        s = _stream_handle(stream)
+        self.cdesc.stream = s
+        self.rdesc.stream = s
+        _abi.check(_abi.lib().eagle_backend_x_b200_compact_gather(ctypes.byref(self.cdesc), _ptr(self.values),
+                                                                   _ptr(self.kept), 8))
+        _abi.check(_abi.lib().eagle_backend_x_b200_reduce_counted(ctypes.byref(self.rdesc), _ptr(self.count)))
+        return self.out

@@ -36,6 +36,9 @@ struct CompactArgs {
     uint32_t* fire;
     float theta;
     uint32_t tiles;
+    const void* values;  // Gather: the samples' values (elemBytes each)
+    void* outValues;     // Gather: the kept samples' values, in sample order
+    uint32_t elemBytes;  // Gather: 4 or 8
 };
 
 /** Keep bits of 16 consecutive mask bytes starting at sample ``i0``. */
@@ -63,7 +66,7 @@ __device__ __forceinline__ uint32_t keepBits(const uint8_t* __restrict__ mask, i
     return (Drop ? ~set : set) & valid;
 }
 
-template <bool Drop, bool Trigger, bool Aligned>
+template <bool Drop, bool Trigger, bool Aligned, bool Gather = false>
 __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
 {
     __shared__ uint32_t sTile;
@@ -112,8 +115,23 @@ __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
     __syncthreads();
     const uint64_t prefix = sPrefix;
     const uint32_t at = uint32_t(prefix);
-    for (uint32_t q = uint32_t(t); q < total; q += kThreads)
-        a.map[size_t(at) + q] = stage[q];
+    if (a.map != nullptr)
+        for (uint32_t q = uint32_t(t); q < total; q += kThreads)
+            a.map[size_t(at) + q] = stage[q];
+    if constexpr (Gather) {
+        // the kept samples' values, in sample order, next to the map
+        if (a.elemBytes == 8) {
+            const uint64_t* src = static_cast<const uint64_t*>(a.values);
+            uint64_t* dst = static_cast<uint64_t*>(a.outValues);
+            for (uint32_t q = uint32_t(t); q < total; q += kThreads)
+                dst[size_t(at) + q] = src[stage[q]];
+        } else {
+            const uint32_t* src = static_cast<const uint32_t*>(a.values);
+            uint32_t* dst = static_cast<uint32_t*>(a.outValues);
+            for (uint32_t q = uint32_t(t); q < total; q += kThreads)
+                dst[size_t(at) + q] = src[stage[q]];
+        }
+    }
     if (tile == a.tiles - 1 && t == 0) {
         const uint32_t c = at + total;
         const bool broken = *a.err != 0u;
@@ -137,13 +155,13 @@ __global__ void compactEmptyKernel(uint32_t* count, uint32_t* live32, uint32_t* 
     }
 }
 
-template <bool Drop, bool Trigger>
+template <bool Drop, bool Trigger, bool Gather = false>
 void launchCompact(const CompactArgs& a, bool aligned, cudaStream_t s)
 {
     if (aligned)
-        compactKernel<Drop, Trigger, true><<<a.tiles, kThreads, 0, s>>>(a);
+        compactKernel<Drop, Trigger, true, Gather><<<a.tiles, kThreads, 0, s>>>(a);
     else
-        compactKernel<Drop, Trigger, false><<<a.tiles, kThreads, 0, s>>>(a);
+        compactKernel<Drop, Trigger, false, Gather><<<a.tiles, kThreads, 0, s>>>(a);
 }
 
 size_t compactScratchBytes(int64_t n)
@@ -446,6 +464,60 @@ EB_API eagle_backend_status eagle_backend_cell_op(const struct eagle_backend_cel
             scaleCountKernel<<<1, 1, 0, s>>>(reinterpret_cast<const uint32_t*>(d.p[0]),
                 reinterpret_cast<uint32_t*>(d.p[1]), int(d.i[0]));
         }
+        launchCheck(who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_compact_gather(struct eagle_backend_compact_desc* desc,
+    uint64_t values, uint64_t out_values, uint32_t elem_bytes)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_compact_gather";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        if (d.n < 0)
+            invalid(std::string(who) + ": n must be >= 0");
+        if (d.n > INT64_C(2147483647))
+            unsupported(std::string(who) + ": at most 2^31-1 samples, got n = " + std::to_string(d.n));
+        if (elem_bytes != 4 && elem_bytes != 8)
+            invalid(std::string(who) + ": elem_bytes must be 4 or 8");
+        if (d.scratch == 0) {
+            constexpr size_t end = offsetof(eagle_backend_compact_desc, scratch_bytes) + sizeof(int64_t);
+            if (desc->struct_size < end)
+                invalid(std::string(who) + ": the scratch query needs a desc carrying scratch_bytes");
+            desc->scratch_bytes = int64_t(compactScratchBytes(d.n));
+            return;
+        }
+        if (d.count == 0 || (d.n > 0 && (d.mask == 0 || values == 0 || out_values == 0)))
+            invalid(std::string(who) + ": mask, values, out_values and count must be device addresses");
+        if (d.live32 != 0)
+            unsupported(std::string(who) + ": the reorder trigger is not offered with the value gather");
+        const int dev = resolveDevice(d.device, d.mask != 0 ? d.mask : d.count);
+        DeviceScope scope(dev);
+        const cudaStream_t s = seamStream(d.stream);
+        if (d.n == 0) {
+            compactEmptyKernel<<<1, 1, 0, s>>>(reinterpret_cast<uint32_t*>(d.count), nullptr, nullptr);
+            launchCheck(who);
+            return;
+        }
+        CompactArgs a{};
+        a.mask = reinterpret_cast<const uint8_t*>(d.mask);
+        a.n = d.n;
+        a.map = reinterpret_cast<int32_t*>(d.index_map);  // may be 0: no map written
+        a.count = reinterpret_cast<uint32_t*>(d.count);
+        a.tiles = uint32_t((d.n + kTile - 1) / kTile);
+        a.status = reinterpret_cast<uint64_t*>(d.scratch);
+        a.tileNext = reinterpret_cast<uint32_t*>(d.scratch + size_t(a.tiles) * sizeof(uint64_t));
+        a.err = a.tileNext + 1;
+        a.values = reinterpret_cast<const void*>(values);
+        a.outValues = reinterpret_cast<void*>(out_values);
+        a.elemBytes = elem_bytes;
+        cudaCheck(cudaMemsetAsync(reinterpret_cast<void*>(d.scratch), 0, compactScratchBytes(d.n), s),
+            "cudaMemsetAsync");
+        const bool aligned = (d.mask & 15u) == 0;
+        if (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP)
+            launchCompact<true, false, true>(a, aligned, s);
+        else
+            launchCompact<false, false, true>(a, aligned, s);
         launchCheck(who);
     });
 }

@@ -247,6 +247,100 @@ __global__ __launch_bounds__(kSlots) void canonicalKernel(ReduceArgs a)
     }
 }
 
+/** Leaves per CTA for ``leaves`` leaves: a power of two keeping the group count at
+ *  most ``target`` (any aligned power-of-two grouping gives the same bits). */
+__device__ __forceinline__ int64_t groupLeavesDevice(int64_t leaves, int64_t target)
+{
+    int64_t g = 1;
+    while (g < kMaxGroupLeaves && (leaves + g - 1) / g > target)
+        g *= 2;
+    return g;
+}
+
+/** The canonical reduction of the first ``*count`` elements of ``in`` (at most
+ *  ``a.rows``): the element count is read on the device, so a reduction can follow
+ *  a compaction with no host round trip. One column. ``gridDim.x`` CTAs (the group
+ *  target); CTAs past the groups the count needs only take part in the last-CTA
+ *  count. An empty input stores the operator's identity (0 for a sum). */
+template <class P, class T>
+__global__ __launch_bounds__(kSlots) void canonicalCountedKernel(ReduceArgs a, const uint32_t* count)
+{
+    __shared__ P s[kSlots];
+    __shared__ P group[kChunk > kMaxGroupLeaves ? kChunk : kMaxGroupLeaves];
+    __shared__ int amLast;
+    const T* in = static_cast<const T*>(a.in);
+    P* partials = static_cast<P*>(a.partials);
+    const int64_t cap = a.rows;
+    const int64_t c = int64_t(*count);
+    const int64_t rows = c < cap ? c : cap;
+    const int64_t leaves = (rows + kLeaf - 1) / kLeaf;
+    const int64_t gl = groupLeavesDevice(leaves, int64_t(gridDim.x));
+    const int64_t groups = (leaves + gl - 1) / gl;
+    const int64_t g = int64_t(blockIdx.x);
+    if (g < groups) {
+        const int64_t l0 = g * gl;
+        const int64_t l1 = l0 + gl < leaves ? l0 + gl : leaves;
+        for (int64_t l = l0; l < l1; ++l) {
+            const int64_t base = l * kLeaf;
+            const int64_t cnt = rows - base < kLeaf ? rows - base : kLeaf;
+            const P p = leafPartial<P, T, false>(in, nullptr, 1, 0, base, cnt, s);
+            if (threadIdx.x == 0)
+                group[l - l0] = p;
+        }
+        __syncthreads();
+        levels(group, int(l1 - l0));
+    }
+    if (threadIdx.x == 0) {
+        if (g < groups)
+            partials[g] = group[0];
+        __threadfence();
+        amLast = atomicAdd(&a.counters[0], 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!amLast)
+        return;
+    __threadfence();
+    P* v = partials;
+    int64_t m = groups;
+    while (m > 1) {
+        const int64_t chunks = (m + kChunk - 1) / kChunk;
+        for (int64_t cc = 0; cc < chunks; ++cc) {
+            const int cnt = int(m - cc * kChunk < kChunk ? m - cc * kChunk : kChunk);
+            for (int i = int(threadIdx.x); i < cnt; i += int(blockDim.x))
+                group[i] = v[cc * kChunk + i];
+            __syncthreads();
+            levels(group, cnt);
+            if (threadIdx.x == 0)
+                v[cc] = group[0];
+            __syncthreads();
+        }
+        m = chunks;
+    }
+    if (threadIdx.x == 0) {
+        T* out = static_cast<T*>(a.out);
+        if (groups == 0) {
+            out[0] = T(0);
+            if constexpr (IsComp<P>::value) {
+                if (a.pairOut)
+                    out[1] = T(0);
+            }
+        } else {
+            const P r = v[0];
+            if constexpr (IsComp<P>::value) {
+                if (a.pairOut) {
+                    out[0] = r.h;
+                    out[1] = isfinite(r.h) ? r.c : T(0);
+                } else {
+                    out[0] = r.value();
+                }
+            } else {
+                out[0] = r.value();
+            }
+        }
+        a.counters[0] = 0u;
+    }
+}
+
 /** Pairwise levels over m (hi, comp) partials -- chunk results in chunk order,
  *  e.g. one per rank -- into out = {hi, comp, value}. One CTA. */
 __global__ __launch_bounds__(kSlots) void combinePairsKernel(const double* __restrict__ hc, int64_t m,
@@ -457,5 +551,85 @@ extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_bac
         combinePairsKernel<<<1, kSlots, 0, seamStream(stream)>>>(reinterpret_cast<const double*>(hc), m,
             reinterpret_cast<double*>(work), reinterpret_cast<double*>(out));
         launchCheck(who);
+    });
+}
+
+namespace eb {
+namespace {
+
+/** CTAs of a counted reduction of up to ``capacity`` elements: about eight per SM,
+ *  and never fewer than the groups the largest count needs. */
+int64_t countedGrid(int64_t capacity)
+{
+    const int64_t leaves = (capacity + kLeaf - 1) / kLeaf;
+    return std::max<int64_t>(int64_t(smCount()) * 8, (leaves + kMaxGroupLeaves - 1) / kMaxGroupLeaves);
+}
+
+template <class P, class T>
+void enqueueCounted(const eagle_backend_reduce_desc& d, const uint32_t* count, int pairOut, cudaStream_t stream)
+{
+    const int64_t target = countedGrid(d.n);
+    ReduceArgs a{};
+    a.in = reinterpret_cast<const void*>(d.in);
+    a.rows = d.n;
+    a.cols = 1;
+    a.partials = reinterpret_cast<void*>(d.work_a);
+    a.counters = reinterpret_cast<uint32_t*>(d.work_b);
+    a.out = reinterpret_cast<void*>(d.out);
+    a.pairOut = pairOut;
+    cudaCheck(cudaMemsetAsync(a.counters, 0, sizeof(uint32_t), stream), "cudaMemsetAsync");
+    canonicalCountedKernel<P, T><<<unsigned(target), kSlots, 0, stream>>>(a, count);
+    launchCheck("eagle_backend_x_b200_reduce_counted");
+}
+
+}  // namespace
+}  // namespace eb
+
+extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_backend_x_b200_reduce_counted(
+    struct eagle_backend_reduce_desc* desc, uint64_t count)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_reduce_counted";
+        constexpr size_t base = offsetof(eagle_backend_reduce_desc, work_elems) + sizeof(int64_t);
+        if (desc == nullptr || desc->struct_size < base)
+            invalid(std::string(who) + ": null desc or struct_size too small");
+        eagle_backend_reduce_desc d{};
+        std::memcpy(&d, desc, std::min<size_t>(desc->struct_size, sizeof d));
+        if (desc->struct_size < offsetof(eagle_backend_reduce_desc, comp_in) + sizeof(uint64_t)) {
+            d.policy = EAGLE_BACKEND_REDUCE_ORDERED;
+            d.flags = 0;
+            d.columns = 1;
+            d.comp_in = 0;
+        }
+        if (d.n < 1)
+            invalid(std::string(who) + ": n (the capacity) must be >= 1");
+        if (d.op != EAGLE_BACKEND_REDUCE_OP_SUM || d.dtype > EAGLE_BACKEND_REDUCE_I64)
+            unsupported(std::string(who) + ": sums of F32 / F64 / I32 / I64 only");
+        if (d.columns != 1 || d.comp_in != 0 || d.flags > EAGLE_BACKEND_REDUCE_PAIR_OUT)
+            unsupported(std::string(who) + ": one column, no companion input");
+        const bool fsum = d.dtype == EAGLE_BACKEND_REDUCE_F32 || d.dtype == EAGLE_BACKEND_REDUCE_F64;
+        if (d.flags != 0 && !fsum)
+            invalid(std::string(who) + ": PAIR_OUT takes a float sum");
+        const int dev = resolveDevice(d.device, d.work_a == 0 ? 0 : d.in);
+        DeviceScope scope(dev);
+        const int64_t target = countedGrid(d.n);
+        if (d.work_a == 0) {
+            // partials: one per group (at most target of them); the counter word
+            const int64_t elemBytes = (d.dtype == EAGLE_BACKEND_REDUCE_F32 || d.dtype == EAGLE_BACKEND_REDUCE_I32) ? 4 : 8;
+            const int64_t partialBytes = target * 2 * elemBytes;
+            desc->work_elems = std::max<int64_t>((partialBytes + elemBytes - 1) / elemBytes, 4);
+            return;
+        }
+        if (d.in == 0 || d.out == 0 || d.work_b == 0 || count == 0)
+            invalid(std::string(who) + ": in, out, work_a, work_b and count must be device addresses");
+        const cudaStream_t stream = seamStream(d.stream);
+        const uint32_t* cnt = reinterpret_cast<const uint32_t*>(count);
+        const int pairOut = d.flags != 0;
+        switch (d.dtype) {
+        case EAGLE_BACKEND_REDUCE_F32: enqueueCounted<CompP<float>, float>(d, cnt, pairOut, stream); break;
+        case EAGLE_BACKEND_REDUCE_F64: enqueueCounted<CompP<double>, double>(d, cnt, pairOut, stream); break;
+        case EAGLE_BACKEND_REDUCE_I32: enqueueCounted<PlainP<int32_t, SumOp<int32_t>>, int32_t>(d, cnt, 0, stream); break;
+        default: enqueueCounted<PlainP<int64_t, SumOp<int64_t>>, int64_t>(d, cnt, 0, stream);
+        }
     });
 }

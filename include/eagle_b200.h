@@ -336,6 +336,24 @@ eagle_backend_status eagle_backend_x_reduce_canonical(struct eagle_backend_reduc
 
 /* ---- this backend's additions (no counterpart entry in the seam) --------------- */
 
+/* eagle_backend_x_b200_compact_gather: compact_device (same desc, query and
+ * capturability) that also writes the kept samples' values, ``elem_bytes`` (4 or 8)
+ * each from ``values``, in sample order to ``out_values[0, *count)``; ``index_map``
+ * may be 0 (no map written). The compaction half of "compact the survivors, then
+ * reduce them" (eagle: ActiveSet.compact, python/eagle/_active_set.py:482-525, then
+ * a gather through the map) in one kernel. No reorder trigger. */
+eagle_backend_status eagle_backend_x_b200_compact_gather(struct eagle_backend_compact_desc* desc, uint64_t values,
+    uint64_t out_values, uint32_t elem_bytes);
+
+/* eagle_backend_x_b200_reduce_counted: x_reduce_canonical (sums of F32 / F64 / I32 /
+ * I64, one column, optional PAIR_OUT) of the first ``*count`` elements of ``in``
+ * (``count`` a device uint32; ``desc->n`` the capacity, count is clipped to it),
+ * read on the device: the reduction can follow compact_gather with no host read of
+ * the count (eagle reads it back to size its reduce, python/eagle/_graph_reduce.py
+ * :204-222). Same bits as x_reduce_canonical over that many elements; 0 elements
+ * give 0. Query with work_a == 0. One kernel after a memset; capturable. */
+eagle_backend_status eagle_backend_x_b200_reduce_counted(struct eagle_backend_reduce_desc* desc, uint64_t count);
+
 /* eagle_backend_x_b200_combine_partials: combine ``m`` float64 (hi, comp) partials
  * ``hc[2m]`` (chunk roots in chunk order, e.g. one per rank; each chunk
  * leafSize * 2^q samples) by the canonical pairwise levels into ``out[3]`` = {hi,

@@ -1,0 +1,54 @@
+"""One rank of the multi-GPU check (launched by tests/test_gpu_multi.py under
+torchrun): the engine on this rank's shard of a 2^22-sample batch, the canonical
+partial of x, an NCCL all-gather and the device fold; rank 0 compares the bits
+with the oracle's one-device run of the whole batch."""
+
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import eagle_b200 as eb  # noqa: E402
+from eagle_b200 import shard  # noqa: E402
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    n = 1 << 22
+    rng = np.random.default_rng(42)
+    om, x0, te = rng.uniform(1, 3, n), rng.normal(1, 0.1, n), 10.0 ** rng.uniform(-2, 1, n)
+    begin, count = shard.shard_range(n, rank, world)
+    sl = slice(begin, begin + count)
+    dev = dict(omega=torch.from_numpy(om[sl].copy()).cuda(), t_end=torch.from_numpy(te[sl].copy()).cuda(),
+               x=torch.from_numpy(x0[sl].copy()).cuda(), v=torch.zeros(count, dtype=torch.float64, device="cuda"),
+               t=torch.zeros(count, dtype=torch.float64, device="cuda"))
+    res = eb.simulate(eb.oscillator, max_steps=10_000, fma=True, mode="persist", dt=1e-3, **dev)
+    pair = eb.reduce(res.x, pair_out=True)
+    folded = shard.fold_partials(shard.gather_partials(pair))
+    torch.cuda.synchronize()
+    if rank == 0:
+        import oracle
+
+        st = [x0.copy(), np.zeros(n), np.zeros(n), np.zeros(n, np.uint8)]
+        oracle.oscillator_run(om, *st, t_end=te, dt=1e-3, max_steps=10_000, fused=True)
+        want = oracle.reduce(st[0])[0]
+        got = folded[2].item()
+        if np.float64(got).tobytes() != np.float64(want).tobytes():
+            print(f"MISMATCH folded {got!r} whole {want!r}", flush=True)
+            sys.exit(1)
+        print("RANK-ORDER FOLD OK", world, got, flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

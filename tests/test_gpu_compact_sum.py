@@ -1,0 +1,83 @@
+"""Compact the survivors, then their canonical ordered sum (the 2^28-value
+microbenchmark configuration: N(0, 1) values with one in 10^6 replaced by +-1e12,
+Bernoulli(p) keep-masks for p in {0.9, 0.5, 0.1, 0.01}): the count, the kept
+values in sample order and the sum's bits against the oracle (flatnonzero and
+the canonical tree of eagle/reduce/canonical.h over the kept values)."""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+PS = (0.9, 0.5, 0.1, 0.01)
+
+
+def microbench_inputs(n, i):
+    """Values (seed 4), outlier positions (seed 5) and signs (seed 6), mask i (seed 7 + i)."""
+    x = np.random.default_rng(4).standard_normal(n)
+    k = max(1, n // 1_000_000)
+    pos = np.random.default_rng(5).choice(n, size=k, replace=False)
+    sign = np.where(np.random.default_rng(6).random(k) < 0.5, -1.0, 1.0)
+    x[pos] = sign * 1e12
+    keep = np.random.default_rng(7 + i).random(n) < PS[i]
+    return x, keep
+
+
+@pytest.mark.parametrize("n", (1, 4097, (1 << 20) + 37, 1 << 24))
+@pytest.mark.parametrize("i", range(4))
+def test_compact_then_sum(eb, orc, n, i):
+    x, keep = microbench_inputs(n, i)
+    cs = eb.CompactSum(torch.from_numpy(keep).cuda(), torch.from_numpy(x).cuda())
+    got = cs().cpu().numpy()
+    kept = x[keep]
+    c = int(cs.count.item())
+    assert c == kept.size
+    assert cs.kept[:c].cpu().numpy().tobytes() == kept.tobytes()
+    want = orc.reduce(kept) if kept.size else np.zeros(1)
+    assert got.tobytes() == want.tobytes(), (n, PS[i])
+
+
+def test_drop_mask_and_pair_out(eb, orc):
+    n = 100_003
+    x, keep = microbench_inputs(n, 1)
+    cs = eb.CompactSum(torch.from_numpy(~keep).cuda(), torch.from_numpy(x).cuda(), drop=True, pair_out=True)
+    got = cs().cpu().numpy()
+    assert got.tobytes() == orc.reduce(x[keep], pair_out=True).tobytes()
+
+
+def test_nothing_kept_sums_to_zero(eb):
+    n = 5000
+    cs = eb.CompactSum(torch.zeros(n, dtype=torch.bool, device="cuda"),
+                       torch.ones(n, dtype=torch.float64, device="cuda"))
+    assert cs().item() == 0.0 and int(cs.count.item()) == 0
+
+
+def test_captured_replay(eb, orc):
+    n = 300_007
+    x, keep = microbench_inputs(n, 2)
+    md, xd = torch.from_numpy(keep).cuda(), torch.from_numpy(x).cuda()
+    cs = eb.CompactSum(md, xd)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        cs(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        cs(s)
+    for j in (0, 3):
+        x2, keep2 = microbench_inputs(n, j)
+        md.copy_(torch.from_numpy(keep2))
+        xd.copy_(torch.from_numpy(x2))
+        g.replay()
+        torch.cuda.synchronize()
+        assert cs.out.cpu().numpy().tobytes() == orc.reduce(x2[keep2]).tobytes()
+
+
+def test_full_size_one_mask(eb, orc):
+    n = 1 << 28
+    x, keep = microbench_inputs(n, 2)
+    cs = eb.CompactSum(torch.from_numpy(keep).cuda(), torch.from_numpy(x).cuda())
+    got = cs().cpu().numpy()
+    assert got.tobytes() == orc.reduce(x[keep]).tobytes()
