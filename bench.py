@@ -22,7 +22,6 @@ import datetime
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -44,7 +43,7 @@ WORKLOAD = "euler-oscillator-heterogeneous-stop"
 def _args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="engine", choices=("engine", "reference"))
     p.add_argument("--mode", default="auto", choices=("auto", "band", "band_eager", "persist", "fused"))
@@ -77,58 +76,59 @@ def _peaks():
 
 
 class _Clocks:
-    """nvidia-smi samples (SM clock, reasons) taken during the timed region."""
+    """SM clock and clock-event reasons sampled through NVML every 10 ms during the
+    timed region (reading only; nothing is set)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
-    def __init__(self, gpu: int):
-        self.gpu = gpu
-        self.proc = None
-        self.lines = []
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []
+        self.smax = None
+        self._stop = threading.Event()
+        self._thread = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            bus = torch.cuda.get_device_properties(self.cuda_index).pci_bus_id
+            try:
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode() if isinstance(bus, str) else bus)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.smax = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        clk = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        reasons = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((clk, reasons))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.01)
+
+            self._thread = threading.Thread(target=poll, daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._thread = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self):
-        sm, smax, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
-            parts = [q.strip() for q in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.smax, "reasons": [], "samples": 0}
+        reasons = sorted(name for name, bit in self.REASONS.items() if any(r & bit for _, r in self.samples))
+        return {"sm_mhz": statistics.median(c for c, _ in self.samples), "sm_max_mhz": self.smax,
+                "reasons": reasons, "samples": len(self.samples)}
 
 
 def _cpu_baseline(omega, x0, t_end, budget_s: float):
@@ -379,8 +379,8 @@ def engine(args):
         "clocks": clocks.summary(),
     }
     res = result.cpu().numpy()
-    line["result"] = {"sum_x": float(res[2]), "mean_x": float(res[2]) / (n * world), "finished": rep.finished,
-                      "steps": rep.steps}
+    line["result"] = {"sum_x": float(res[2]), "mean_x": float(res[2]) / (n * world),
+                      "finished_rank0": rep.finished, "steps_rank0": rep.steps}
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = _cpu_baseline(omega, x0, t_end, args.cpu_seconds)
     print(json.dumps(line), flush=True)

@@ -7,9 +7,9 @@ library and fails loudly (``BackendUnavailable``) when it is not built.
 """
 
 from ._abi import BackendError, BackendUnavailable, BackendUnsupported
-from ._api import (Compactor, CompactSum, Model, Reducer, Runner, RunReport, SimResult, cell_op, compact, entry, mask_count,
-                   oscillator, reduce, simulate, until_done)
+from ._api import (Compactor, CompactSum, Model, Reducer, Runner, RunReport, SimResult, cell_op, compact, entry, gambler,
+                   mask_count, oscillator, reduce, simulate, until_done)
 
 __all__ = ["BackendError", "BackendUnavailable", "BackendUnsupported", "Compactor", "CompactSum", "Model", "Reducer", "Runner",
-           "RunReport", "SimResult", "cell_op", "compact", "entry", "mask_count", "oscillator", "reduce",
+           "RunReport", "SimResult", "cell_op", "compact", "entry", "gambler", "mask_count", "oscillator", "reduce",
            "simulate", "until_done"]

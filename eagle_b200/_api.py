@@ -72,6 +72,16 @@ class _Oscillator(Model):
 oscillator = _Oscillator(name="oscillator", planes=("omega", "t_end", "x", "v", "t"), mutable=("x", "v", "t"),
                          params=("t_end", "dt"))
 
+
+class _Gambler(Model):
+    """The gambler's-ruin walk: ``pos`` (int32) moves +1 or -1 per step and the sample
+    stops at 0 or 100; ``time`` (int64) counts its steps. Step s of sample i moves +1
+    when bit (s mod 128) of Philox-4x32-10(counter = (s // 128, id_base + i), key =
+    seed) is set. Params: ``seed`` and ``id_base`` (default 0)."""
+
+
+gambler = _Gambler(name="gambler", planes=("pos", "time"), mutable=("pos", "time"), params=("seed", "id_base"))
+
 _MODES = {"band": _abi.MODE_BAND, "persist": _abi.MODE_PERSIST, "fused": _abi.MODE_FUSED,
           "band_eager": _abi.MODE_BAND_EAGER}
 
@@ -134,17 +144,18 @@ class SimResult:
 
 # ------------------------------------------------------------------------- runner
 
-def _as_device_plane(name, value, n, device, *, staged):
-    """A contiguous float64 CUDA tensor for ``value``; host arrays are staged
-    (copied in, and remembered in ``staged`` for the copy back)."""
+def _as_device_plane(name, value, n, device, *, staged, dtype=None):
+    """A contiguous CUDA tensor (float64 unless ``dtype``) for ``value``; host arrays
+    are staged (copied in, and remembered in ``staged`` for the copy back)."""
     torch = _t()
+    dtype = dtype or torch.float64
     if isinstance(value, torch.Tensor) and value.is_cuda:
-        if value.dtype != torch.float64 or not value.is_contiguous() or value.numel() != n:
-            raise ValueError(f"plane {name!r} must be a contiguous float64 tensor of {n} samples")
+        if value.dtype != dtype or not value.is_contiguous() or value.numel() != n:
+            raise ValueError(f"plane {name!r} must be a contiguous {dtype} tensor of {n} samples")
         return value
     host = torch.as_tensor(np.asarray(value) if not isinstance(value, torch.Tensor) else value)
-    if host.dtype != torch.float64 or host.numel() != n:
-        raise ValueError(f"plane {name!r} must hold {n} float64 samples")
+    if host.dtype != dtype or host.numel() != n:
+        raise ValueError(f"plane {name!r} must hold {n} {dtype} samples")
     dev = host.reshape(-1).to(device, non_blocking=True)
     staged.append((name, value, dev))
     return dev
@@ -165,10 +176,15 @@ class Runner:
                  device=None, k_first: int = 0, k_min: int = 0, k_max: int = 0, chunk: int = 0,
                  overhead_steps: float = 0.0, interval_steps: float = 0.0, **planes):
         torch = _t()
-        if model is not oscillator:
+        if model not in (oscillator, gambler):
             raise ValueError(f"eagle_b200: unknown model {model!r}")
         if max_steps is None or int(max_steps) < 0:
             raise ValueError("max_steps must be >= 0")
+        if model is gambler:
+            mode = "persist" if mode == "auto" else mode
+            self._init_gambler(max_steps=max_steps, mode=mode, terminated=terminated, device=device, chunk=chunk,
+                               **planes)
+            return
         mode = "band" if mode == "auto" else mode
         if mode not in _MODES:
             raise ValueError(f"mode must be one of {sorted(_MODES)} or 'auto'")
@@ -225,6 +241,50 @@ class Runner:
             _abi.check(_abi.lib().eagle_backend_x_b200_engine_create(ctypes.byref(d), ctypes.byref(h)))
         self._h = h
 
+    def _init_gambler(self, *, max_steps, mode, terminated, device, chunk, **planes):
+        torch = _t()
+        if mode not in ("persist", "fused"):
+            raise ValueError("the gambler model runs under mode 'persist' or 'fused'")
+        missing = {"pos", "time", "seed"} - set(planes)
+        if missing:
+            raise TypeError(f"gambler needs {sorted(missing)}")
+        extra = set(planes) - {"pos", "time", "seed", "id_base"}
+        if extra:
+            raise TypeError(f"gambler takes no plane(s) {sorted(extra)}")
+        pos = planes["pos"]
+        n = pos.numel() if isinstance(pos, torch.Tensor) else int(np.asarray(pos).size)
+        self.device = torch.device(device) if device is not None else (
+            pos.device if isinstance(pos, torch.Tensor) and pos.is_cuda
+            else torch.device("cuda", torch.cuda.current_device()))
+        self._staged = []
+        self.n, self.mode, self.max_steps, self.fma, self.spread = n, mode, int(max_steps), False, False
+        self.planes = {"pos": _as_device_plane("pos", pos, n, self.device, staged=self._staged, dtype=torch.int32),
+                       "time": _as_device_plane("time", planes["time"], n, self.device, staged=self._staged,
+                                                dtype=torch.int64)}
+        if terminated is None:
+            terminated = torch.zeros(n, dtype=torch.bool, device=self.device)
+        elif not (isinstance(terminated, torch.Tensor) and terminated.is_cuda
+                  and terminated.dtype in (torch.bool, torch.uint8) and terminated.is_contiguous()):
+            raise ValueError("terminated must be a contiguous bool/uint8 CUDA tensor")
+        self.terminated = terminated
+        d = _abi.new(_abi.EngineDesc)
+        d.device = self.device.index if self.device.index is not None else -1
+        d.model = _abi.MODEL_GAMBLER
+        d.mode = _MODES[mode]
+        d.n = n
+        d.max_steps = self.max_steps
+        d.planes[0] = _ptr(self.planes["pos"])
+        d.planes[1] = _ptr(self.planes["time"])
+        seed = int(planes["seed"]) & ((1 << 64) - 1)
+        d.iuniforms[0] = seed - (1 << 64) if seed >= (1 << 63) else seed
+        d.iuniforms[1] = int(planes.get("id_base", 0))
+        d.terminated = _ptr(terminated)
+        d.chunk = int(chunk)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _abi.check(_abi.lib().eagle_backend_x_b200_engine_create(ctypes.byref(d), ctypes.byref(h)))
+        self._h = h
+
     def __del__(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value:
@@ -264,7 +324,7 @@ class Runner:
     def _copy_back(self, stream=None) -> None:
         torch = _t()
         for name, host, dev in self._staged:
-            if name in ("x", "v", "t"):
+            if name in ("x", "v", "t", "pos", "time"):
                 if isinstance(host, torch.Tensor):
                     host.copy_(dev.reshape(host.shape))
                 else:

@@ -315,6 +315,7 @@ struct Engine {
     int64_t n = 0, maxSteps = 0;
     uint64_t planes[8] = {};
     double uniforms[4] = {};
+    int64_t iuniforms[4] = {};
     uint8_t* term = nullptr;
     Cells* cells = nullptr;
     Cells* host = nullptr;  // pinned mirror for the report
@@ -395,6 +396,15 @@ void buildBandGraph(Engine& e, BandArgs& args)
     cudaCheck(cudaGraphInstantiate(&e.exec, e.graph, 0), "cudaGraphInstantiate");
 }
 
+/** The built-in entry a persist / fused engine launches. */
+std::string entryName(const Engine& e, bool persist)
+{
+    const std::string stem = e.model == EAGLE_B200_MODEL_GAMBLER ? "gambler"
+        : (e.spread ? "oscillator_spread" : "oscillator");
+    const std::string fma = (e.fma && e.model != EAGLE_B200_MODEL_GAMBLER) ? "_fma" : "";
+    return stem + (persist ? "_persist" : "_range") + fma;
+}
+
 ScalarHandle handle(uint64_t p, int64_t n, int dev)
 {
     return ScalarHandle{reinterpret_cast<void*>(p), uint64_t(n), 1, 2, dev};
@@ -434,46 +444,51 @@ void launchEngine(Engine& e, cudaStream_t s)
     if (e.n == 0 || e.maxSteps == 0)
         return;
     const bool persist = e.mode == EAGLE_B200_MODE_PERSIST;
-    const std::string name = std::string(e.spread ? "oscillator_spread" : "oscillator")
-        + (persist ? "_persist" : "_range") + (e.fma ? "_fma" : "");
+    const std::string name = entryName(e, persist);
     const void* stub = entryStub(name);
     const int dev = e.device;
     // role arguments in the arg_spec order, then the partition triple and the tail
-    ScalarHandle omega, tendH, term, x, v, t, fin, fused;
-    double tendU = 0.0, dt = 0.0;
-    if (e.spread) {
-        omega = handle(e.planes[0], e.n, dev);
-        tendH = handle(e.planes[1], e.n, dev);
-        x = handle(e.planes[2], e.n, dev);
-        v = handle(e.planes[3], e.n, dev);
-        t = handle(e.planes[4], e.n, dev);
-        dt = e.uniforms[0];
+    ScalarHandle h[8];
+    double du[4];
+    int64_t iu[4];
+    std::vector<void*> args;
+    ScalarHandle term = handle(reinterpret_cast<uint64_t>(e.term), e.n, dev);
+    ScalarHandle fin = handle(reinterpret_cast<uint64_t>(&c->finished), 1, dev);
+    ScalarHandle fused = handle(reinterpret_cast<uint64_t>(&c->budget), 1, dev);
+    if (e.model == EAGLE_B200_MODEL_GAMBLER) {
+        h[0] = handle(e.planes[0], e.n, dev);  // pos
+        h[1] = handle(e.planes[1], e.n, dev);  // time
+        iu[0] = e.iuniforms[0];
+        iu[1] = e.iuniforms[1];
+        for (void* p : {static_cast<void*>(&h[0]), static_cast<void*>(&h[1]), static_cast<void*>(&term),
+                 static_cast<void*>(&iu[0]), static_cast<void*>(&iu[1])})
+            args.push_back(p);
+    } else if (e.spread) {
+        for (int k = 0; k < 5; ++k)
+            h[k] = handle(e.planes[k], e.n, dev);  // omega, t_end, x, v, t
+        du[0] = e.uniforms[0];
+        for (void* p : {static_cast<void*>(&h[0]), static_cast<void*>(&h[1]), static_cast<void*>(&du[0]),
+                 static_cast<void*>(&term), static_cast<void*>(&h[2]), static_cast<void*>(&h[3]),
+                 static_cast<void*>(&h[4])})
+            args.push_back(p);
     } else {
-        omega = handle(e.planes[0], e.n, dev);
-        x = handle(e.planes[1], e.n, dev);
-        v = handle(e.planes[2], e.n, dev);
-        t = handle(e.planes[3], e.n, dev);
-        tendU = e.uniforms[0];
-        dt = e.uniforms[1];
+        for (int k = 0; k < 4; ++k)
+            h[k] = handle(e.planes[k], e.n, dev);  // omega, x, v, t
+        du[0] = e.uniforms[0];
+        du[1] = e.uniforms[1];
+        for (void* p : {static_cast<void*>(&h[0]), static_cast<void*>(&du[0]), static_cast<void*>(&du[1]),
+                 static_cast<void*>(&term), static_cast<void*>(&h[1]), static_cast<void*>(&h[2]),
+                 static_cast<void*>(&h[3])})
+            args.push_back(p);
     }
-    term = handle(reinterpret_cast<uint64_t>(e.term), e.n, dev);
-    fin = handle(reinterpret_cast<uint64_t>(&c->finished), 1, dev);
-    fused = handle(reinterpret_cast<uint64_t>(&c->budget), 1, dev);
     int64_t base = 0, count = e.n, nSamples = e.n;
     uint32_t* next = &c->next;
     unsigned long long* util = nullptr;
     uint32_t* steps = &c->steps32;
     unsigned long long* stepsum = &c->stepsum64;
     uint32_t chunk = e.chunk;
-    std::vector<void*> args;
-    args.push_back(&omega);
-    if (e.spread)
-        args.push_back(&tendH);
-    else
-        args.push_back(&tendU);
-    for (void* p : {static_cast<void*>(&dt), static_cast<void*>(&term), static_cast<void*>(&x),
-             static_cast<void*>(&v), static_cast<void*>(&t), static_cast<void*>(&fin), static_cast<void*>(&fused),
-             static_cast<void*>(&base), static_cast<void*>(&count), static_cast<void*>(&nSamples)})
+    for (void* p : {static_cast<void*>(&fin), static_cast<void*>(&fused), static_cast<void*>(&base),
+             static_cast<void*>(&count), static_cast<void*>(&nSamples)})
         args.push_back(p);
     unsigned grid = 0;
     if (persist) {
@@ -554,8 +569,11 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
         const auto d = readDesc(desc, EAGLE_B200_FLAG_FMA, who);
         if (out == nullptr)
             invalid(std::string(who) + ": null output");
-        if (d.model > EAGLE_B200_MODEL_OSCILLATOR_SPREAD)
+        if (d.model > EAGLE_B200_MODEL_GAMBLER)
             unsupported(std::string(who) + ": unknown model " + std::to_string(d.model));
+        if (d.model == EAGLE_B200_MODEL_GAMBLER
+            && (d.mode == EAGLE_B200_MODE_BAND || d.mode == EAGLE_B200_MODE_BAND_EAGER))
+            unsupported(std::string(who) + ": the band schedule is built for the oscillator only; use persist or fused");
         if (d.mode > EAGLE_B200_MODE_BAND_EAGER)
             unsupported(std::string(who) + ": unknown mode " + std::to_string(d.mode));
         if (d.n < 0 || d.n > INT64_C(2147483647))
@@ -565,7 +583,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
         if ((d.mode == EAGLE_B200_MODE_PERSIST || d.mode == EAGLE_B200_MODE_FUSED) && d.max_steps > INT64_C(4294967295))
             unsupported(std::string(who) + ": the persist and fused entries count steps in 32 bits");
         const bool spread = d.model == EAGLE_B200_MODEL_OSCILLATOR_SPREAD;
-        const int nPlanes = spread ? 5 : 4;
+        const int nPlanes = d.model == EAGLE_B200_MODEL_GAMBLER ? 2 : (spread ? 5 : 4);
         if (d.n > 0) {
             for (int i = 0; i < nPlanes; ++i)
                 if (d.planes[i] == 0)
@@ -588,6 +606,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
             e->maxSteps = d.max_steps;
             std::memcpy(e->planes, d.planes, sizeof e->planes);
             std::memcpy(e->uniforms, d.uniforms, sizeof e->uniforms);
+            std::memcpy(e->iuniforms, d.iuniforms, sizeof e->iuniforms);
             e->term = reinterpret_cast<uint8_t*>(d.terminated);
             e->chunk = d.chunk == 0 ? 256u : d.chunk;
             e->block = 256;
@@ -654,8 +673,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
                 else
                     cudaCheck(cudaMallocHost(&e->goHost, sizeof(uint32_t)), "cudaMallocHost");
             } else {
-                const void* stub = entryStub(std::string(spread ? "oscillator_spread" : "oscillator") + "_persist"
-                    + (e->fma ? "_fma" : ""));
+                const void* stub = entryStub(entryName(*e, true));
                 cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, stub, 256, 0),
                     "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
                 e->persistGrid = std::max(1, occ) * smCount();

@@ -18,7 +18,7 @@
 //   _persist: uint32* hawk_next, uint64* hawk_util, uint32* hawk_steps,
 //             uint64* hawk_stepsum, uint32 hawk_chunk
 // ``fused_steps`` (int64) is the steps one launch may take per sample.
-#include "models.cuh"
+#include "schedule.cuh"
 
 #include <map>
 #include <mutex>
@@ -41,41 +41,6 @@ struct TEnd<true> {
 };
 
 __device__ __forceinline__ double* dplane(const ScalarHandle& h) { return static_cast<double*>(h.data); }
-
-/** Flush a thread's run counters with one atomic per block and counter:
- *  finished count (u32), longest steps (u32 max) and executed steps (u64 sum);
- *  a null cell is skipped. Every thread of the block calls it. */
-__device__ __forceinline__ void blockFlush(uint32_t fin, uint32_t longest, unsigned long long sum,
-    uint32_t* finished, uint32_t* steps, unsigned long long* stepsum)
-{
-    __shared__ uint32_t sFin[32], sMax[32];
-    __shared__ unsigned long long sSum[32];
-    fin = warpSum(fin);
-    longest = warpMax(longest);
-    sum = warpSum(sum);
-    const unsigned lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    if (lane == 0) {
-        sFin[warp] = fin;
-        sMax[warp] = longest;
-        sSum[warp] = sum;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        uint32_t f = 0, m = 0;
-        unsigned long long u = 0;
-        for (unsigned w = 0; w < (blockDim.x + 31) / 32; ++w) {
-            f += sFin[w];
-            m = sMax[w] > m ? sMax[w] : m;
-            u += sSum[w];
-        }
-        if (finished != nullptr && f != 0)
-            atomicAdd(finished, f);
-        if (steps != nullptr && m != 0)
-            atomicMax(steps, m);
-        if (stepsum != nullptr && u != 0)
-            atomicAdd(stepsum, u);
-    }
-}
 
 /** The plain and range entries: one lane per sample of [base, base + count). */
 template <bool Fma, bool Spread>
@@ -232,6 +197,8 @@ __global__ __launch_bounds__(256) void oscillatorPersist(EB_OSC_ROLES(TEnd<Sprea
     }
 }
 
+void addGamblerEntries(std::map<std::string, const void*>& m);  // walks.cu
+
 namespace {
 
 template <bool Fma, bool Spread>
@@ -251,6 +218,7 @@ const std::map<std::string, const void*>& entryTable()
         addEntries<true, false>(m, "oscillator");
         addEntries<false, true>(m, "oscillator_spread");
         addEntries<true, true>(m, "oscillator_spread");
+        addGamblerEntries(m);
         return m;
     }();
     return table;

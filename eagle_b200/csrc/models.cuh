@@ -105,3 +105,97 @@ struct Oscillator {
 };
 
 }  // namespace eb
+
+namespace eb {
+
+/** Philox-4x32-10 (Salmon, Moraes, Dror and Shaw, SC'11): ten rounds of two
+ *  32x32->64 multiplies and xors over a 4-word counter, the 2-word key bumped by
+ *  the Weyl constants between rounds. */
+__device__ __forceinline__ void philox4x32_10(uint32_t& c0, uint32_t& c1, uint32_t& c2, uint32_t& c3, uint32_t k0,
+    uint32_t k1)
+{
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        if (r > 0) {
+            k0 += 0x9E3779B9u;
+            k1 += 0xBB67AE85u;
+        }
+        const uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
+        const uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
+        const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+        c0 = n0;
+        c1 = lo1;
+        c2 = n2;
+        c3 = lo0;
+    }
+}
+
+/** The gambler's-ruin walk: a position in (0, 100) moves +1 or -1 per step and the
+ *  sample stops when it reaches 0 or 100; ``time`` counts its steps over its whole
+ *  life. Step s (0-based) moves +1 when bit (s mod 128) of Philox-4x32-10 with
+ *  counter (s / 128, id) and key ``seed`` is set (word s/32 mod 4, bit s mod 32). */
+struct GamblerModel {
+    int32_t* pos;
+    int64_t* time;
+    uint8_t* term;
+    uint64_t seed;
+    int64_t idBase;
+
+    struct Sample {
+        int32_t pos;
+        int64_t time;
+        uint64_t id;
+    };
+
+    __device__ __forceinline__ Sample load(int64_t i) const { return Sample{pos[i], time[i], uint64_t(idBase + i)}; }
+    __device__ __forceinline__ void store(int64_t i, const Sample& s) const
+    {
+        pos[i] = s.pos;
+        time[i] = s.time;
+    }
+    __device__ __forceinline__ void prepare(Sample&) const {}
+
+    /** At most ``budget`` steps; returns the steps run, ``fin`` when it reached 0 or 100. */
+    __device__ __forceinline__ int run(Sample& s, int budget, bool& fin) const
+    {
+        int done = 0;
+        fin = false;
+        int32_t p = s.pos;
+        int64_t tm = s.time;
+        while (done < budget) {
+            const uint64_t blk = uint64_t(tm) >> 7;
+            uint32_t c0 = uint32_t(blk), c1 = uint32_t(blk >> 32), c2 = uint32_t(s.id), c3 = uint32_t(s.id >> 32);
+            philox4x32_10(c0, c1, c2, c3, uint32_t(seed), uint32_t(seed >> 32));
+            // the block's remaining bits, one 32-bit word at a time
+            int bit = int(tm & 127);
+            while (bit < 128 && done < budget) {
+                const int w = bit >> 5;
+                uint32_t word = w == 0 ? c0 : (w == 1 ? c1 : (w == 2 ? c2 : c3));
+                word >>= (bit & 31);
+                int lim = 32 - (bit & 31);
+                if (lim > budget - done)
+                    lim = budget - done;
+                for (int k = 0; k < lim; ++k) {
+                    p += int32_t((word & 1u) << 1) - 1;
+                    word >>= 1;
+                    if (p == 0 || p == 100) {
+                        fin = true;
+                        done += k + 1;
+                        tm += k + 1;
+                        s.pos = p;
+                        s.time = tm;
+                        return done;
+                    }
+                }
+                done += lim;
+                tm += lim;
+                bit += lim;
+            }
+        }
+        s.pos = p;
+        s.time = tm;
+        return done;
+    }
+};
+
+}  // namespace eb

@@ -381,6 +381,7 @@ eagle_backend_status eagle_backend_x_b200_entry(const char* name, int32_t device
  * model over n samples resident on one device. */
 #define EAGLE_B200_MODEL_OSCILLATOR 0u        /* README.md:89-97, t_end a Param */
 #define EAGLE_B200_MODEL_OSCILLATOR_SPREAD 1u /* the same body, t_end per sample */
+#define EAGLE_B200_MODEL_GAMBLER 2u           /* +-1 walk absorbed at 0 and 100, Philox-4x32-10 steps */
 
 #define EAGLE_B200_MODE_BAND 0u    /* one CUDA graph: WHILE { fused step + compaction + policy } */
 #define EAGLE_B200_MODE_PERSIST 1u /* one persistent launch: lanes claim samples off a counter */
@@ -408,6 +409,7 @@ struct eagle_b200_engine_desc {
     uint32_t block;      /* threads per block (0: 256) */
     double overhead_steps; /* band: a launch's fixed cost in sample-steps (0: built-in) */
     double interval_steps; /* band: a launch's per-sample memory cost in steps (0: built-in) */
+    int64_t iuniforms[4];  /* the model's integer Params, in the model's order */
 };
 
 /* What one run did (python/eagle/_until_done.py:120-171, RunReport). */
@@ -428,7 +430,9 @@ struct eagle_b200_report {
 };
 
 /* The models' plane orders: OSCILLATOR planes = {omega, x, v, t}, uniforms = {t_end,
- * dt}; OSCILLATOR_SPREAD planes = {omega, t_end, x, v, t}, uniforms = {dt}. */
+ * dt}; OSCILLATOR_SPREAD planes = {omega, t_end, x, v, t}, uniforms = {dt};
+ * GAMBLER planes = {pos (int32), time (int64)}, iuniforms = {seed, id_base}, band
+ * mode not offered. */
 typedef struct eagle_b200_engine_s* eagle_b200_engine;
 
 /* Allocate the engine's device state (compacted state, look-back words, cells) on

@@ -56,6 +56,8 @@ def lib():
             [ctypes.c_int] * 7
         L.oracle_oscillator_run.argtypes = [_I64, _P, _P, ctypes.c_double, ctypes.c_double, _P, _P, _P, _P, _P,
                                             _I64, ctypes.c_int, _I64, _P]
+        L.oracle_philox4x32_10.argtypes = [_P, ctypes.c_uint64, _P]
+        L.oracle_gambler_run.argtypes = [_I64, _P, _P, _P, _I64, ctypes.c_uint64, _I64, _P]
         L.oracle_corpus_f64.argtypes = [_I64, ctypes.c_uint64, _P]
         L.oracle_corpus_f32.argtypes = [_I64, ctypes.c_uint64, _P]
         L.oracle_fixture_f64.argtypes = [_I64, ctypes.c_double, _P, _P]
@@ -192,3 +194,24 @@ def fixture(n: int, kappa: float, dtype=np.float64):
     f = lib().oracle_fixture_f64 if dtype == np.float64 else lib().oracle_fixture_f32
     exact = f(n, float(kappa), _ptr(x), _ptr(reached))
     return x, float(exact), float(reached[0])
+
+
+def philox4x32_10(counter, seed: int):
+    """Philox-4x32-10 (Salmon et al., SC'11) of a 4-word counter under a 64-bit seed."""
+    c = np.ascontiguousarray(counter, dtype=np.uint32)
+    out = np.zeros(4, dtype=np.uint32)
+    lib().oracle_philox4x32_10(_ptr(c), int(seed), _ptr(out))
+    return out
+
+
+def gambler_run(pos, time, terminated, *, seed: int, max_steps: int, id_base: int = 0):
+    """Every live sample's walk until it reaches 0 or 100 or has taken ``max_steps``
+    steps in this run, in place. Returns ``(finished, longest, total)``."""
+    n = pos.size
+    assert pos.dtype == np.int32 and time.dtype == np.int64 and terminated.dtype in (np.uint8, np.bool_)
+    stats = np.zeros(3, dtype=np.int64)
+    rc = lib().oracle_gambler_run(n, _ptr(pos), _ptr(time), _ptr(terminated.view(np.uint8)), int(id_base),
+                                  int(seed), int(max_steps), _ptr(stats))
+    if rc != 0:
+        raise ValueError(f"oracle_gambler_run refused (status {rc})")
+    return int(stats[0]), int(stats[1]), int(stats[2])

@@ -455,6 +455,94 @@ int oracle_oscillator_run(int64_t n, const double* omega, const double* t_end, d
     return 0;
 }
 
+// ------------------------------------------------------------ gambler's ruin
+//
+// The random-walk configuration: a position in (0, 100) moves +1 or -1 per step
+// and the sample stops when it reaches 0 or 100; the output is its absorption
+// time. eagle has no code for it (its random numbers come from the absent aether
+// library), so the random stream is this build's definition: Philox-4x32-10
+// (Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1, 2, 3",
+// SC'11) with key = the 64-bit seed and counter = (step / 128, sample id), both as
+// two 32-bit words, low word first; step s of a sample (0-based, counted over its
+// whole life) moves +1 when bit (s mod 128) of the 128-bit output (word s/32 mod 4,
+// bit s mod 32) is set, else -1.
+
+static inline void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1)
+{
+    for (int r = 0; r < 10; ++r) {
+        if (r > 0) {
+            k0 += 0x9E3779B9u;
+            k1 += 0xBB67AE85u;
+        }
+        const uint64_t p0 = uint64_t(0xD2511F53u) * c[0];
+        const uint64_t p1 = uint64_t(0xCD9E8D57u) * c[2];
+        const uint32_t hi0 = uint32_t(p0 >> 32), lo0 = uint32_t(p0);
+        const uint32_t hi1 = uint32_t(p1 >> 32), lo1 = uint32_t(p1);
+        const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+        c[0] = n0;
+        c[1] = lo1;
+        c[2] = n2;
+        c[3] = lo0;
+    }
+}
+
+void oracle_philox4x32_10(const uint32_t counter[4], uint64_t seed, uint32_t out[4])
+{
+    uint32_t c[4] = {counter[0], counter[1], counter[2], counter[3]};
+    philox4x32_10(c, uint32_t(seed), uint32_t(seed >> 32));
+    for (int q = 0; q < 4; ++q)
+        out[q] = c[q];
+}
+
+int oracle_gambler_run(int64_t n, int32_t* pos, int64_t* time, uint8_t* term, int64_t id_base, uint64_t seed,
+    int64_t max_steps, int64_t* stats)
+{
+    if (n < 0 || max_steps < 0)
+        return 2;
+    int64_t finished = 0, longest = 0, total = 0;
+#pragma omp parallel for schedule(dynamic, 1024) reduction(+ : finished, total) reduction(max : longest)
+    for (int64_t i = 0; i < n; ++i) {
+        int64_t s = 0;
+        if (term[i] == 0) {
+            const uint64_t id = uint64_t(id_base + i);
+            int32_t p = pos[i];
+            int64_t tm = time[i];
+            uint32_t block[4] = {0, 0, 0, 0};
+            int64_t have = -1;  // the 128-step block held in ``block``
+            while (s < max_steps) {
+                const int64_t blk = tm >> 7;
+                if (blk != have) {
+                    uint32_t c[4] = {uint32_t(uint64_t(blk)), uint32_t(uint64_t(blk) >> 32), uint32_t(id),
+                        uint32_t(id >> 32)};
+                    philox4x32_10(c, uint32_t(seed), uint32_t(seed >> 32));
+                    for (int q = 0; q < 4; ++q)
+                        block[q] = c[q];
+                    have = blk;
+                }
+                const int b = int(tm & 127);
+                p += ((block[b >> 5] >> (b & 31)) & 1u) ? 1 : -1;
+                ++tm;
+                ++s;
+                if (p == 0 || p == 100) {
+                    term[i] = 1;
+                    break;
+                }
+            }
+            pos[i] = p;
+            time[i] = tm;
+        }
+        finished += term[i] != 0 ? 1 : 0;
+        longest = std::max(longest, s);
+        total += s;
+    }
+    if (stats != nullptr) {
+        stats[0] = finished;
+        stats[1] = longest;
+        stats[2] = total;
+    }
+    return 0;
+}
+
 // ------------------------------------------------------- reference test corpora
 //
 // The inputs of eagle's canonical-reduction tests, regenerated with the same

@@ -35,6 +35,9 @@ void oracle_policy_step(uint32_t finished, uint32_t total, int64_t* cells, int64
 int oracle_oscillator_run(int64_t n, const double* omega, const double* t_end, double t_end_uniform, double dt,
     double* x, double* v, double* t, uint8_t* term, int32_t* steps_out, int64_t max_steps, int fused,
     int64_t tile, int64_t* stats);
+void oracle_philox4x32_10(const uint32_t counter[4], uint64_t seed, uint32_t out[4]);
+int oracle_gambler_run(int64_t n, int32_t* pos, int64_t* time, uint8_t* term, int64_t id_base, uint64_t seed,
+    int64_t max_steps, int64_t* stats);
 void oracle_corpus_f64(int64_t n, uint64_t seed, double* out);
 void oracle_corpus_f32(int64_t n, uint64_t seed, float* out);
 double oracle_fixture_f64(int64_t n, double kappa, double* x, double* reached);

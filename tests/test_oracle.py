@@ -332,3 +332,34 @@ def test_golden_fixtures(orc):
         assert (fin, longest, total) == (case["finished"], case["longest"], case["total"])
         xs = orc.reduce(st[0])[0]
         assert int(_bits(xs)) == int(case["sum_x_bits"], 16)
+
+
+# --------------------------------------------------------------- Philox / walk
+
+def test_philox_statistics(orc):
+    """Philox-4x32-10 as restated (Salmon et al., SC'11): distinct counters and keys give
+    distinct words, bits are balanced, and one flipped counter bit changes about half
+    of the 128 output bits."""
+    outs = np.stack([orc.philox4x32_10([k, 0, 7, 0], 99) for k in range(4096)])
+    assert len({tuple(o) for o in outs}) == 4096
+    bits = np.unpackbits(outs.view(np.uint8))
+    assert abs(bits.mean() - 0.5) < 0.01
+    flips = []
+    for k in range(256):
+        a = orc.philox4x32_10([k, 1, 2, 3], 5)
+        b = orc.philox4x32_10([k ^ 1, 1, 2, 3], 5)
+        flips.append(int(np.unpackbits((a ^ b).view(np.uint8)).sum()))
+    assert 60 < np.mean(flips) < 68
+    assert not np.array_equal(orc.philox4x32_10([1, 2, 3, 4], 5), orc.philox4x32_10([1, 2, 3, 4], 6))
+
+
+def test_gambler_mean_absorption_time(orc):
+    """E[T] = s (100 - s) for a fair walk from s; averaged over s ~ U{1..99} it is 1683.3."""
+    n = 1 << 18
+    pos = np.random.default_rng(3).integers(1, 100, n).astype(np.int32)
+    want = float(np.mean(pos.astype(np.float64) * (100 - pos)))
+    time, term = np.zeros(n, np.int64), np.zeros(n, np.uint8)
+    fin, longest, total = orc.gambler_run(pos, time, term, seed=1, max_steps=1_000_000)
+    assert fin == n and total == int(time.sum())
+    assert abs(time.mean() - want) < 0.02 * want
+    assert set(np.unique(pos)) <= {0, 100}
