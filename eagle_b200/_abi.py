@@ -26,7 +26,7 @@ REDUCE_COMPENSATED, REDUCE_ORDERED, REDUCE_AUTO = range(3)
 REDUCE_PAIR_OUT = 1
 COPY_H2D, COPY_D2H, COPY_D2D, COPY_H2H = range(4)
 
-MODEL_OSCILLATOR, MODEL_OSCILLATOR_SPREAD, MODEL_GAMBLER = 0, 1, 2
+MODEL_OSCILLATOR, MODEL_OSCILLATOR_SPREAD, MODEL_GAMBLER, MODEL_LORENZ = 0, 1, 2, 3
 MODE_BAND, MODE_PERSIST, MODE_FUSED, MODE_BAND_EAGER = 0, 1, 2, 3
 FLAG_FMA = 1
 
@@ -110,7 +110,7 @@ class EngineDesc(ctypes.Structure):
                 ("reserved0", _u32), ("n", _i64), ("max_steps", _i64), ("planes", _u64 * 8),
                 ("uniforms", _f64 * 4), ("terminated", _u64), ("k_first", _i64), ("k_min", _i64),
                 ("k_max", _i64), ("chunk", _u32), ("block", _u32), ("overhead_steps", _f64),
-                ("interval_steps", _f64), ("iuniforms", _i64 * 4)]
+                ("interval_steps", _f64), ("iuniforms", _i64 * 4), ("uniforms_ext", _f64 * 4)]
 
 
 class ScalarHandle(ctypes.Structure):

@@ -82,6 +82,17 @@ class _Gambler(Model):
 
 gambler = _Gambler(name="gambler", planes=("pos", "time"), mutable=("pos", "time"), params=("seed", "id_base"))
 
+
+class _Lorenz(Model):
+    """Lorenz-63 under eagle's perf-card adaptive RKF7(8) attempt: per-sample ``rho``;
+    state ``x, y, z, t, h`` (float64) and ``n_acc, n_rej`` (uint32 counts); Params
+    ``sigma, beta, t_final, rtol, atol``. One until-done step is one attempt."""
+
+
+lorenz = _Lorenz(name="lorenz", planes=("rho", "x", "y", "z", "t", "h", "n_acc", "n_rej"),
+                 mutable=("x", "y", "z", "t", "h", "n_acc", "n_rej"),
+                 params=("sigma", "beta", "t_final", "rtol", "atol"))
+
 _MODES = {"band": _abi.MODE_BAND, "persist": _abi.MODE_PERSIST, "fused": _abi.MODE_FUSED,
           "band_eager": _abi.MODE_BAND_EAGER}
 
@@ -176,10 +187,15 @@ class Runner:
                  device=None, k_first: int = 0, k_min: int = 0, k_max: int = 0, chunk: int = 0,
                  overhead_steps: float = 0.0, interval_steps: float = 0.0, **planes):
         torch = _t()
-        if model not in (oscillator, gambler):
+        if model not in (oscillator, gambler, lorenz):
             raise ValueError(f"eagle_b200: unknown model {model!r}")
         if max_steps is None or int(max_steps) < 0:
             raise ValueError("max_steps must be >= 0")
+        if model is lorenz:
+            mode = "persist" if mode == "auto" else mode
+            self._init_lorenz(max_steps=max_steps, mode=mode, terminated=terminated, device=device, chunk=chunk,
+                              **planes)
+            return
         if model is gambler:
             mode = "persist" if mode == "auto" else mode
             self._init_gambler(max_steps=max_steps, mode=mode, terminated=terminated, device=device, chunk=chunk,
@@ -285,6 +301,52 @@ class Runner:
             _abi.check(_abi.lib().eagle_backend_x_b200_engine_create(ctypes.byref(d), ctypes.byref(h)))
         self._h = h
 
+    def _init_lorenz(self, *, max_steps, mode, terminated, device, chunk, **planes):
+        torch = _t()
+        if mode not in ("persist", "fused"):
+            raise ValueError("the lorenz model runs under mode 'persist' or 'fused'")
+        names = ("rho", "x", "y", "z", "t", "h", "n_acc", "n_rej")
+        params = ("sigma", "beta", "t_final", "rtol", "atol")
+        missing = (set(names) | set(params)) - set(planes)
+        if missing:
+            raise TypeError(f"lorenz needs {sorted(missing)}")
+        extra = set(planes) - set(names) - set(params)
+        if extra:
+            raise TypeError(f"lorenz takes no plane(s) {sorted(extra)}")
+        x = planes["x"]
+        n = x.numel() if isinstance(x, torch.Tensor) else int(np.asarray(x).size)
+        self.device = torch.device(device) if device is not None else (
+            x.device if isinstance(x, torch.Tensor) and x.is_cuda else torch.device("cuda", torch.cuda.current_device()))
+        self._staged = []
+        self.n, self.mode, self.max_steps, self.fma, self.spread = n, mode, int(max_steps), False, False
+        self.planes = {}
+        for name in names:
+            dt = torch.int32 if name in ("n_acc", "n_rej") else torch.float64
+            self.planes[name] = _as_device_plane(name, planes[name], n, self.device, staged=self._staged, dtype=dt)
+        if terminated is None:
+            terminated = torch.zeros(n, dtype=torch.bool, device=self.device)
+        elif not (isinstance(terminated, torch.Tensor) and terminated.is_cuda
+                  and terminated.dtype in (torch.bool, torch.uint8) and terminated.is_contiguous()):
+            raise ValueError("terminated must be a contiguous bool/uint8 CUDA tensor")
+        self.terminated = terminated
+        d = _abi.new(_abi.EngineDesc)
+        d.device = self.device.index if self.device.index is not None else -1
+        d.model = _abi.MODEL_LORENZ
+        d.mode = _MODES[mode]
+        d.n = n
+        d.max_steps = self.max_steps
+        for k, name in enumerate(names):
+            d.planes[k] = _ptr(self.planes[name])
+        for k, name in enumerate(params[:4]):
+            d.uniforms[k] = float(planes[name])
+        d.uniforms_ext[0] = float(planes["atol"])
+        d.terminated = _ptr(terminated)
+        d.chunk = int(chunk)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _abi.check(_abi.lib().eagle_backend_x_b200_engine_create(ctypes.byref(d), ctypes.byref(h)))
+        self._h = h
+
     def __del__(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value:
@@ -324,7 +386,7 @@ class Runner:
     def _copy_back(self, stream=None) -> None:
         torch = _t()
         for name, host, dev in self._staged:
-            if name in ("x", "v", "t", "pos", "time"):
+            if name in ("x", "v", "t", "pos", "time", "y", "z", "h", "n_acc", "n_rej"):
                 if isinstance(host, torch.Tensor):
                     host.copy_(dev.reshape(host.shape))
                 else:

@@ -316,6 +316,7 @@ struct Engine {
     uint64_t planes[8] = {};
     double uniforms[4] = {};
     int64_t iuniforms[4] = {};
+    double uext[4] = {};
     uint8_t* term = nullptr;
     Cells* cells = nullptr;
     Cells* host = nullptr;  // pinned mirror for the report
@@ -400,8 +401,10 @@ void buildBandGraph(Engine& e, BandArgs& args)
 std::string entryName(const Engine& e, bool persist)
 {
     const std::string stem = e.model == EAGLE_B200_MODEL_GAMBLER ? "gambler"
+        : e.model == EAGLE_B200_MODEL_LORENZ ? "lorenz"
         : (e.spread ? "oscillator_spread" : "oscillator");
-    const std::string fma = (e.fma && e.model != EAGLE_B200_MODEL_GAMBLER) ? "_fma" : "";
+    const bool oscillator = e.model == EAGLE_B200_MODEL_OSCILLATOR || e.model == EAGLE_B200_MODEL_OSCILLATOR_SPREAD;
+    const std::string fma = (e.fma && oscillator) ? "_fma" : "";
     return stem + (persist ? "_persist" : "_range") + fma;
 }
 
@@ -455,7 +458,19 @@ void launchEngine(Engine& e, cudaStream_t s)
     ScalarHandle term = handle(reinterpret_cast<uint64_t>(e.term), e.n, dev);
     ScalarHandle fin = handle(reinterpret_cast<uint64_t>(&c->finished), 1, dev);
     ScalarHandle fused = handle(reinterpret_cast<uint64_t>(&c->budget), 1, dev);
-    if (e.model == EAGLE_B200_MODEL_GAMBLER) {
+    if (e.model == EAGLE_B200_MODEL_LORENZ) {
+        for (int k = 0; k < 8; ++k)
+            h[k] = handle(e.planes[k], e.n, dev);  // rho, x, y, z, t, h, n_acc, n_rej
+        for (int k = 0; k < 4; ++k)
+            du[k] = e.uniforms[k];  // sigma, beta, t_final, rtol
+        args.push_back(&h[0]);
+        for (int k = 0; k < 4; ++k)
+            args.push_back(&du[k]);
+        args.push_back(&e.uext[0]);  // atol
+        args.push_back(&term);
+        for (int k = 1; k < 8; ++k)
+            args.push_back(&h[k]);
+    } else if (e.model == EAGLE_B200_MODEL_GAMBLER) {
         h[0] = handle(e.planes[0], e.n, dev);  // pos
         h[1] = handle(e.planes[1], e.n, dev);  // time
         iu[0] = e.iuniforms[0];
@@ -499,9 +514,9 @@ void launchEngine(Engine& e, cudaStream_t s)
     } else {
         args.push_back(&steps);
         args.push_back(&stepsum);
-        grid = unsigned((e.n + 255) / 256);
+        grid = unsigned((e.n + e.block - 1) / e.block);
     }
-    cudaCheck(cudaLaunchKernel(stub, dim3(grid), dim3(256), args.data(), 0, s), "cudaLaunchKernel");
+    cudaCheck(cudaLaunchKernel(stub, dim3(grid), dim3(e.block), args.data(), 0, s), "cudaLaunchKernel");
 }
 
 void readReport(Engine& e, cudaStream_t s, eagle_b200_report* out)
@@ -569,9 +584,9 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
         const auto d = readDesc(desc, EAGLE_B200_FLAG_FMA, who);
         if (out == nullptr)
             invalid(std::string(who) + ": null output");
-        if (d.model > EAGLE_B200_MODEL_GAMBLER)
+        if (d.model > EAGLE_B200_MODEL_LORENZ)
             unsupported(std::string(who) + ": unknown model " + std::to_string(d.model));
-        if (d.model == EAGLE_B200_MODEL_GAMBLER
+        if ((d.model == EAGLE_B200_MODEL_GAMBLER || d.model == EAGLE_B200_MODEL_LORENZ)
             && (d.mode == EAGLE_B200_MODE_BAND || d.mode == EAGLE_B200_MODE_BAND_EAGER))
             unsupported(std::string(who) + ": the band schedule is built for the oscillator only; use persist or fused");
         if (d.mode > EAGLE_B200_MODE_BAND_EAGER)
@@ -583,7 +598,8 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
         if ((d.mode == EAGLE_B200_MODE_PERSIST || d.mode == EAGLE_B200_MODE_FUSED) && d.max_steps > INT64_C(4294967295))
             unsupported(std::string(who) + ": the persist and fused entries count steps in 32 bits");
         const bool spread = d.model == EAGLE_B200_MODEL_OSCILLATOR_SPREAD;
-        const int nPlanes = d.model == EAGLE_B200_MODEL_GAMBLER ? 2 : (spread ? 5 : 4);
+        const int nPlanes = d.model == EAGLE_B200_MODEL_LORENZ ? 8
+            : d.model == EAGLE_B200_MODEL_GAMBLER ? 2 : (spread ? 5 : 4);
         if (d.n > 0) {
             for (int i = 0; i < nPlanes; ++i)
                 if (d.planes[i] == 0)
@@ -607,9 +623,10 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
             std::memcpy(e->planes, d.planes, sizeof e->planes);
             std::memcpy(e->uniforms, d.uniforms, sizeof e->uniforms);
             std::memcpy(e->iuniforms, d.iuniforms, sizeof e->iuniforms);
+            std::memcpy(e->uext, d.uniforms_ext, sizeof e->uext);
             e->term = reinterpret_cast<uint8_t*>(d.terminated);
-            e->chunk = d.chunk == 0 ? 256u : d.chunk;
-            e->block = 256;
+            e->chunk = d.chunk != 0 ? d.chunk : d.model == EAGLE_B200_MODEL_LORENZ ? 8u : 256u;
+            e->block = d.model == EAGLE_B200_MODEL_LORENZ ? 128u : 256u;
             cudaCheck(cudaMalloc(&e->cells, sizeof(Cells)), "cudaMalloc");
             cudaCheck(cudaMallocHost(&e->host, sizeof(Cells)), "cudaMallocHost");
             Cells init{};
@@ -674,7 +691,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
                     cudaCheck(cudaMallocHost(&e->goHost, sizeof(uint32_t)), "cudaMallocHost");
             } else {
                 const void* stub = entryStub(entryName(*e, true));
-                cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, stub, 256, 0),
+                cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, stub, int(e->block), 0),
                     "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
                 e->persistGrid = std::max(1, occ) * smCount();
             }

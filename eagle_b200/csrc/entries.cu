@@ -198,6 +198,7 @@ __global__ __launch_bounds__(256) void oscillatorPersist(EB_OSC_ROLES(TEnd<Sprea
 }
 
 void addGamblerEntries(std::map<std::string, const void*>& m);  // walks.cu
+void addLorenzEntries(std::map<std::string, const void*>& m);   // lorenz.cu
 
 namespace {
 
@@ -219,6 +220,7 @@ const std::map<std::string, const void*>& entryTable()
         addEntries<false, true>(m, "oscillator_spread");
         addEntries<true, true>(m, "oscillator_spread");
         addGamblerEntries(m);
+        addLorenzEntries(m);
         return m;
     }();
     return table;

@@ -382,6 +382,7 @@ eagle_backend_status eagle_backend_x_b200_entry(const char* name, int32_t device
 #define EAGLE_B200_MODEL_OSCILLATOR 0u        /* README.md:89-97, t_end a Param */
 #define EAGLE_B200_MODEL_OSCILLATOR_SPREAD 1u /* the same body, t_end per sample */
 #define EAGLE_B200_MODEL_GAMBLER 2u           /* +-1 walk absorbed at 0 and 100, Philox-4x32-10 steps */
+#define EAGLE_B200_MODEL_LORENZ 3u            /* Lorenz-63 under adaptive RKF7(8); a step is one attempt */
 
 #define EAGLE_B200_MODE_BAND 0u    /* one CUDA graph: WHILE { fused step + compaction + policy } */
 #define EAGLE_B200_MODE_PERSIST 1u /* one persistent launch: lanes claim samples off a counter */
@@ -405,11 +406,12 @@ struct eagle_b200_engine_desc {
     int64_t k_first;     /* band: steps of the first launch (0: 16) */
     int64_t k_min;       /* band: fewest steps per launch but the last (0: 8) */
     int64_t k_max;       /* band: most steps per launch (0: 4096) */
-    uint32_t chunk;      /* persist: steps between claims, a power of two (0: 256) */
+    uint32_t chunk;      /* persist: steps between claims, a power of two (0: 256; LORENZ 8) */
     uint32_t block;      /* threads per block (0: 256) */
     double overhead_steps; /* band: a launch's fixed cost in sample-steps (0: built-in) */
     double interval_steps; /* band: a launch's per-sample memory cost in steps (0: built-in) */
     int64_t iuniforms[4];  /* the model's integer Params, in the model's order */
+    double uniforms_ext[4]; /* the model's float Params past the first four */
 };
 
 /* What one run did (python/eagle/_until_done.py:120-171, RunReport). */
@@ -431,8 +433,10 @@ struct eagle_b200_report {
 
 /* The models' plane orders: OSCILLATOR planes = {omega, x, v, t}, uniforms = {t_end,
  * dt}; OSCILLATOR_SPREAD planes = {omega, t_end, x, v, t}, uniforms = {dt};
- * GAMBLER planes = {pos (int32), time (int64)}, iuniforms = {seed, id_base}, band
- * mode not offered. */
+ * GAMBLER planes = {pos (int32), time (int64)}, iuniforms = {seed, id_base};
+ * LORENZ planes = {rho, x, y, z, t, h, n_acc (uint32), n_rej (uint32)}, uniforms =
+ * {sigma, beta, t_final, rtol}, uniforms_ext = {atol}. GAMBLER and LORENZ run under
+ * the persist and fused modes. */
 typedef struct eagle_b200_engine_s* eagle_b200_engine;
 
 /* Allocate the engine's device state (compacted state, look-back words, cells) on

@@ -58,6 +58,9 @@ def lib():
                                             _I64, ctypes.c_int, _I64, _P]
         L.oracle_philox4x32_10.argtypes = [_P, ctypes.c_uint64, _P]
         L.oracle_gambler_run.argtypes = [_I64, _P, _P, _P, _I64, ctypes.c_uint64, _I64, _P]
+        L.oracle_det_pow.argtypes = [ctypes.c_double, ctypes.c_double]
+        L.oracle_det_pow.restype = ctypes.c_double
+        L.oracle_lorenz_run.argtypes = [_I64, _P] + [ctypes.c_double] * 5 + [_P] * 8 + [_I64, _P]
         L.oracle_corpus_f64.argtypes = [_I64, ctypes.c_uint64, _P]
         L.oracle_corpus_f32.argtypes = [_I64, ctypes.c_uint64, _P]
         L.oracle_fixture_f64.argtypes = [_I64, ctypes.c_double, _P, _P]
@@ -214,4 +217,30 @@ def gambler_run(pos, time, terminated, *, seed: int, max_steps: int, id_base: in
                                   int(seed), int(max_steps), _ptr(stats))
     if rc != 0:
         raise ValueError(f"oracle_gambler_run refused (status {rc})")
+    return int(stats[0]), int(stats[1]), int(stats[2])
+
+
+def det_pow(r: float, e: float) -> float:
+    """The controller's deterministic power r^e (ln by the atanh series, exp by Taylor)."""
+    return lib().oracle_det_pow(float(r), float(e))
+
+
+LORENZ = dict(sigma=10.0, beta=8.0 / 3.0, t_final=10.0, rtol=1e-9, atol=1e-12)
+
+
+def lorenz_run(rho, x, y, z, t, h, n_acc, n_rej, terminated, *, max_steps, sigma=10.0, beta=8.0 / 3.0,
+               t_final=10.0, rtol=1e-9, atol=1e-12):
+    """Adaptive RKF7(8) attempts of Lorenz-63 (benchmarks/perf_card/perf_card.py:131-348
+    with the Lorenz right-hand side) until t reaches t_final or ``max_steps`` attempts,
+    in place. Returns ``(finished, longest, total)`` in attempts."""
+    n = rho.size
+    for a in (rho, x, y, z, t, h):
+        assert a.dtype == np.float64 and a.flags.c_contiguous and a.size == n
+    assert n_acc.dtype == np.uint32 and n_rej.dtype == np.uint32
+    stats = np.zeros(3, dtype=np.int64)
+    rc = lib().oracle_lorenz_run(n, _ptr(rho), sigma, beta, t_final, rtol, atol, _ptr(x), _ptr(y), _ptr(z), _ptr(t),
+                                 _ptr(h), _ptr(n_acc), _ptr(n_rej), _ptr(terminated.view(np.uint8)), int(max_steps),
+                                 _ptr(stats))
+    if rc != 0:
+        raise ValueError(f"oracle_lorenz_run refused (status {rc})")
     return int(stats[0]), int(stats[1]), int(stats[2])

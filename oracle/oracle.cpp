@@ -543,6 +543,241 @@ int oracle_gambler_run(int64_t n, int32_t* pos, int64_t* time, uint8_t* term, in
     return 0;
 }
 
+// ------------------------------------------------------------ Lorenz, RKF7(8)
+//
+// Lorenz-63 (dx = sigma (y - x), dy = x (rho - z) - y, dz = x y - beta z) integrated
+// by the adaptive Runge-Kutta-Fehlberg 7(8) attempt of eagle's perf card
+// (benchmarks/perf_card/perf_card.py:131-138 controller constants, :255-278
+// Fehlberg's tableau from NASA TR R-287, :289-309 stages with left-to-right term
+// sums skipping zero coefficients and the mixed max-norm error ratio, :313-317
+// sum_terms, :330-348 the attempt: clip the last step onto t_final, accept or reject,
+// scale h by min(5, max(0.2, 0.9 ratio^expo)), count, stop at t_final).
+//
+// The controller's power ratio^expo is this build's deterministic pow (the library
+// pow rounds differently on CPU and GPU): ln by exponent extraction and the series
+// ln m = 2 atanh((m-1)/(m+1)) on m in [sqrt(1/2), sqrt(2)), exp by reduction to
+// f = y - n ln2 and the Taylor series of e^f, then scaling by 2^n; every operation
+// rounds once, in the same order on the device.
+
+}  // extern "C"
+
+namespace {
+
+const double kLn2 = 0.6931471805599453;
+
+double detLog(double r)
+{
+    uint64_t b;
+    std::memcpy(&b, &r, sizeof b);
+    int k = 0;
+    if (((b >> 52) & 0x7ff) == 0) {  // subnormal: scale up exactly
+        r = r * 18014398509481984.0;  // 2^54
+        std::memcpy(&b, &r, sizeof b);
+        k = -54;
+    }
+    k += int((b >> 52) & 0x7ff) - 1023;
+    b = (b & 0x800FFFFFFFFFFFFFull) | (uint64_t(1023) << 52);  // m in [1, 2)
+    double m;
+    std::memcpy(&m, &b, sizeof m);
+    if (m > 1.4142135623730951) {
+        m = m * 0.5;
+        k += 1;
+    }
+    const double u = (m - 1.0) / (m + 1.0);
+    const double u2 = u * u;
+    double p = 1.0 / 23.0;
+    p = p * u2 + 1.0 / 21.0;
+    p = p * u2 + 1.0 / 19.0;
+    p = p * u2 + 1.0 / 17.0;
+    p = p * u2 + 1.0 / 15.0;
+    p = p * u2 + 1.0 / 13.0;
+    p = p * u2 + 1.0 / 11.0;
+    p = p * u2 + 1.0 / 9.0;
+    p = p * u2 + 1.0 / 7.0;
+    p = p * u2 + 1.0 / 5.0;
+    p = p * u2 + 1.0 / 3.0;
+    p = p * u2 + 1.0;
+    const double lnm = (2.0 * u) * p;
+    return lnm + double(k) * kLn2;
+}
+
+double detExp(double y)
+{
+    const double n = std::nearbyint(y / kLn2);
+    const double f = y - n * kLn2;
+    double p = 1.0 / 6402373705728000.0;  // 1/18!
+    p = p * f + 1.0 / 355687428096000.0;
+    p = p * f + 1.0 / 20922789888000.0;
+    p = p * f + 1.0 / 1307674368000.0;
+    p = p * f + 1.0 / 87178291200.0;
+    p = p * f + 1.0 / 6227020800.0;
+    p = p * f + 1.0 / 479001600.0;
+    p = p * f + 1.0 / 39916800.0;
+    p = p * f + 1.0 / 3628800.0;
+    p = p * f + 1.0 / 362880.0;
+    p = p * f + 1.0 / 40320.0;
+    p = p * f + 1.0 / 5040.0;
+    p = p * f + 1.0 / 720.0;
+    p = p * f + 1.0 / 120.0;
+    p = p * f + 1.0 / 24.0;
+    p = p * f + 1.0 / 6.0;
+    p = p * f + 1.0 / 2.0;
+    p = p * f + 1.0;
+    p = p * f + 1.0;
+    const int e = int(n);
+    if (e > 1000 || e < -1000)
+        return e > 0 ? INFINITY : 0.0;
+    const uint64_t sb = uint64_t(e + 1023) << 52;
+    double scale;
+    std::memcpy(&scale, &sb, sizeof scale);
+    return p * scale;
+}
+
+double detPow(double r, double e)  // r >= 0 (or NaN), e < 0: the controller's power
+{
+    if (std::isnan(r))
+        return r;
+    if (r == 0.0)
+        return INFINITY;
+    if (std::isinf(r))
+        return 0.0;
+    return detExp(e * detLog(r));
+}
+
+// Fehlberg 7(8) (NASA TR R-287): the lower-triangular a, the 8th-order weights b, the
+// error weights be (b_hat - b), as eagle's perf card lists them.
+const double kA[12][12] = {
+    {2. / 27},
+    {1. / 36, 1. / 12},
+    {1. / 24, 0, 1. / 8},
+    {5. / 12, 0, -25. / 16, 25. / 16},
+    {1. / 20, 0, 0, 1. / 4, 1. / 5},
+    {-25. / 108, 0, 0, 125. / 108, -65. / 27, 125. / 54},
+    {31. / 300, 0, 0, 0, 61. / 225, -2. / 9, 13. / 900},
+    {2.0, 0, 0, -53. / 6, 704. / 45, -107. / 9, 67. / 90, 3.0},
+    {-91. / 108, 0, 0, 23. / 108, -976. / 135, 311. / 54, -19. / 60, 17. / 6, -1. / 12},
+    {2383. / 4100, 0, 0, -341. / 164, 4496. / 1025, -301. / 82, 2133. / 4100, 45. / 82, 45. / 164, 18. / 41},
+    {3. / 205, 0, 0, 0, 0, -6. / 41, -3. / 205, -3. / 41, 3. / 41, 6. / 41, 0},
+    {-1777. / 4100, 0, 0, -341. / 164, 4496. / 1025, -289. / 82, 2193. / 4100, 51. / 82, 33. / 164, 12. / 41, 0,
+        1.0},
+};
+const double kB[13] = {0, 0, 0, 0, 0, 34. / 105, 9. / 35, 9. / 35, 9. / 280, 9. / 280, 0, 41. / 840, 41. / 840};
+const double kBE[13] = {41. / 840, 0, 0, 0, 0, 0, 0, 0, 0, 0, 41. / 840, -41. / 840, -41. / 840};
+
+inline void lorenzRhs(const double s[3], double sigma, double rho, double beta, double out[3])
+{
+    out[0] = sigma * (s[1] - s[0]);
+    out[1] = s[0] * (rho - s[2]) - s[1];
+    out[2] = s[0] * s[1] - beta * s[2];
+}
+
+// the weighted left-to-right sum of k[j][d] over the non-zero coefficients
+inline double termSum(const double* coef, int count, double k[][3], int d)
+{
+    double total = 0.0;
+    bool first = true;
+    for (int j = 0; j < count; ++j) {
+        if (coef[j] == 0.0)
+            continue;
+        const double term = coef[j] * k[j][d];
+        total = first ? term : total + term;
+        first = false;
+    }
+    return total;
+}
+
+// One attempt; returns true when it was accepted.
+bool lorenzAttempt(double s[3], double& t, double& h, double rho, double sigma, double beta, double tFinal,
+    double rtol, double atol)
+{
+    const double s0[3] = {s[0], s[1], s[2]};
+    const double t0 = t;
+    const bool last = h >= tFinal - t0;
+    const double step = last ? tFinal - t0 : h;
+    double k[13][3];
+    lorenzRhs(s0, sigma, rho, beta, k[0]);
+    for (int i = 0; i < 12; ++i) {
+        double si[3];
+        for (int d = 0; d < 3; ++d)
+            si[d] = s0[d] + step * termSum(kA[i], i + 1, k, d);
+        lorenzRhs(si, sigma, rho, beta, k[i + 1]);
+    }
+    double s8[3], err[3];
+    for (int d = 0; d < 3; ++d) {
+        s8[d] = s0[d] + step * termSum(kB, 13, k, d);
+        err[d] = step * termSum(kBE, 13, k, d);
+    }
+    double ratio = 0.0;
+    for (int d = 0; d < 3; ++d) {
+        const double r = std::fabs(err[d]) / (atol + rtol * std::fmax(std::fabs(s8[d]), std::fabs(s0[d])));
+        ratio = d == 0 ? r : std::fmax(ratio, r);
+    }
+    const bool accept = ratio < 1.0;
+    const double expo = accept ? -1.0 / 9.0 : -1.0 / 8.0;
+    h = step * std::fmin(5.0, std::fmax(0.2, 0.9 * detPow(ratio, expo)));
+    if (accept) {
+        s[0] = s8[0];
+        s[1] = s8[1];
+        s[2] = s8[2];
+        t = last ? tFinal : t0 + step;
+    }
+    return accept;
+}
+
+}  // namespace
+
+extern "C" {
+
+double oracle_det_pow(double r, double e) { return detPow(r, e); }
+
+int oracle_lorenz_run(int64_t n, const double* rho, double sigma, double beta, double t_final, double rtol,
+    double atol, double* x, double* y, double* z, double* t, double* h, uint32_t* n_acc, uint32_t* n_rej,
+    uint8_t* term, int64_t max_steps, int64_t* stats)
+{
+    if (n < 0 || max_steps < 0)
+        return 2;
+    int64_t finished = 0, longest = 0, total = 0;
+#pragma omp parallel for schedule(dynamic, 64) reduction(+ : finished, total) reduction(max : longest)
+    for (int64_t i = 0; i < n; ++i) {
+        int64_t a = 0;
+        if (term[i] == 0) {
+            double s[3] = {x[i], y[i], z[i]};
+            double tt = t[i], hh = h[i];
+            uint32_t na = n_acc[i], nr = n_rej[i];
+            while (a < max_steps) {
+                const bool acc = lorenzAttempt(s, tt, hh, rho[i], sigma, beta, t_final, rtol, atol);
+                na += acc ? 1u : 0u;
+                nr += acc ? 0u : 1u;
+                ++a;
+                if (tt >= t_final) {
+                    term[i] = 1;
+                    break;
+                }
+            }
+            x[i] = s[0];
+            y[i] = s[1];
+            z[i] = s[2];
+            t[i] = tt;
+            h[i] = hh;
+            n_acc[i] = na;
+            n_rej[i] = nr;
+        }
+        finished += term[i] != 0 ? 1 : 0;
+        longest = std::max(longest, a);
+        total += a;
+    }
+    if (stats != nullptr) {
+        stats[0] = finished;
+        stats[1] = longest;
+        stats[2] = total;
+    }
+    return 0;
+}
+
+}  // extern "C"
+
+extern "C" {
+
 // ------------------------------------------------------- reference test corpora
 //
 // The inputs of eagle's canonical-reduction tests, regenerated with the same

@@ -38,6 +38,10 @@ int oracle_oscillator_run(int64_t n, const double* omega, const double* t_end, d
 void oracle_philox4x32_10(const uint32_t counter[4], uint64_t seed, uint32_t out[4]);
 int oracle_gambler_run(int64_t n, int32_t* pos, int64_t* time, uint8_t* term, int64_t id_base, uint64_t seed,
     int64_t max_steps, int64_t* stats);
+double oracle_det_pow(double r, double e);
+int oracle_lorenz_run(int64_t n, const double* rho, double sigma, double beta, double t_final, double rtol,
+    double atol, double* x, double* y, double* z, double* t, double* h, uint32_t* n_acc, uint32_t* n_rej,
+    uint8_t* term, int64_t max_steps, int64_t* stats);
 void oracle_corpus_f64(int64_t n, uint64_t seed, double* out);
 void oracle_corpus_f32(int64_t n, uint64_t seed, float* out);
 double oracle_fixture_f64(int64_t n, double kappa, double* x, double* reached);

@@ -363,3 +363,36 @@ def test_gambler_mean_absorption_time(orc):
     assert fin == n and total == int(time.sum())
     assert abs(time.mean() - want) < 0.02 * want
     assert set(np.unique(pos)) <= {0, 100}
+
+
+def test_det_pow_tracks_pow(orc):
+    """The controller's deterministic power stays within 5e-14 relative of libm's pow
+    over r in [1e-300, 1e300], e = -1/8, -1/9 (the k * ln 2 terms of the reductions
+    round in double). What the controller needs is the same bits on host and device,
+    which the GPU tests check; its accuracy only keeps the step sizes sensible."""
+    import math
+    g = np.random.default_rng(1)
+    for r in np.concatenate([10.0 ** g.uniform(-300, 300, 4000), g.uniform(0.5, 2.0, 1000), [1.0, 2.0, 0.5]]):
+        for e in (-1.0 / 8.0, -1.0 / 9.0):
+            want = math.pow(r, e)
+            got = orc.det_pow(r, e)
+            assert abs(got / want - 1.0) <= 5e-14, (r, e, got, want)
+    assert orc.det_pow(0.0, -0.125) == math.inf and orc.det_pow(math.inf, -0.125) == 0.0
+    assert math.isnan(orc.det_pow(math.nan, -0.125))
+
+
+def test_lorenz_reaches_t_final_and_counts(orc):
+    """Every sample of the Lorenz configuration reaches t_final well inside the cap;
+    accepted + rejected attempts equal the per-sample attempt count the run reports."""
+    n = 512
+    g = np.random.default_rng(2)
+    rho = g.uniform(20.0, 40.0, n)
+    x, y, z = (g.normal(1.0, 0.1, n) for _ in range(3))
+    t, h = np.zeros(n), np.full(n, 1e-3)
+    na, nr = np.zeros(n, np.uint32), np.zeros(n, np.uint32)
+    term = np.zeros(n, np.uint8)
+    fin, longest, total = orc.lorenz_run(rho, x, y, z, t, h, na, nr, term, max_steps=200_000)
+    assert fin == n and np.all(t == 10.0) and np.all(term == 1)
+    att = na.astype(np.int64) + nr
+    assert int(att.sum()) == total and int(att.max()) == longest
+    assert 100 < att.mean() < 2000 and np.all(np.isfinite(z))
