@@ -17,6 +17,10 @@ LIB_PATH = os.path.join(HERE, "libeagle_b200.so")
 OK, ERROR, INVALID_ARGUMENT, INDEX, INTEROP, UNAVAILABLE, CALLBACK_FAILED, BAD_HANDLE, UNSUPPORTED = range(9)
 
 CAP_STREAM, CAP_EXEC, CAP_DEVICE, CAP_FILTERING = 1 << 0, 1 << 9, 1 << 10, 1 << 12
+CAP_CAPTURER, CAP_CAPTURED, CAP_FORK, CAP_CONDITIONAL, CAP_ATTRIBUTION, CAP_GRAPH, CAP_LAUNCHER = (1 << k for k in range(1, 8))
+CAP_CONDITIONAL_IF_ELSE, CAP_CONDITIONAL_SWITCH = 1 << 13, 1 << 14
+COND_IF, COND_IF_ELSE, COND_WHILE, COND_SWITCH = 1, 2, 3, 4
+LOOP_UNCAPPED = 0xFFFFFFFF
 
 CELL_BUMP, CELL_MASK_COUNT, CELL_POLICY, CELL_IDENTITY, CELL_COUNT_FIRED, CELL_GROUP_AND, CELL_SCALE_COUNT = range(7)
 COMPACT_MASK_IS_DROP = 1
@@ -124,6 +128,25 @@ class Report(ctypes.Structure):
                 ("report_bytes", _u32), ("reserved0", _u32)]
 
 
+class CapturerDesc(ctypes.Structure):
+    _fields_ = [("struct_size", _u32), ("flags", _u32), ("device", _i32), ("reserved0", _i32), ("stream", _u64)]
+
+
+class ForkDesc(ctypes.Structure):
+    _fields_ = [("struct_size", _u32), ("flags", _u32), ("device", _i32), ("reserved0", _i32), ("origin", _u64),
+                ("branch_count", _u64), ("wait_count", _u64)]
+
+
+class ConditionalDesc(ctypes.Structure):
+    _fields_ = [("struct_size", _u32), ("flags", _u32), ("device", _i32), ("loop_cap", _u32), ("origin", _u64),
+                ("count_ptr", _u64), ("baseline_ptr", _u64), ("counter_ptr", _u64), ("kind", _u32), ("arms", _u32),
+                ("negate", _u32), ("reserved1", _u32), ("brk_ptr", _u64), ("limit_ptr", _u64)]
+
+
+class GraphDesc(ctypes.Structure):
+    _fields_ = [("struct_size", _u32), ("flags", _u32), ("device", _i32), ("reserved0", _i32)]
+
+
 def new(struct_type, **fields):
     """A zero-filled desc with ``struct_size`` set, then ``fields``."""
     s = struct_type()
@@ -149,6 +172,54 @@ SIGNATURES = {
     "eagle_backend_stream_ptr": (_i32, [_P, ctypes.POINTER(_u64)]),
     "eagle_backend_stream_synchronize": (_i32, [_P]),
     "eagle_backend_stream_release": (None, [_P]),
+    "eagle_backend_capturer_create": (_i32, [ctypes.POINTER(CapturerDesc), ctypes.POINTER(_P)]),
+    "eagle_backend_capturer_begin": (_i32, [_P]),
+    "eagle_backend_capturer_end": (_i32, [_P, ctypes.POINTER(_P)]),
+    "eagle_backend_capturer_graph": (_i32, [_P, ctypes.POINTER(_u64)]),
+    "eagle_backend_capturer_release": (None, [_P]),
+    "eagle_backend_captured_is_valid": (_i32, [_P, ctypes.POINTER(_i32)]),
+    "eagle_backend_captured_release": (None, [_P]),
+    "eagle_backend_fork_create": (_i32, [ctypes.POINTER(ForkDesc), ctypes.POINTER(_P)]),
+    "eagle_backend_fork_fork": (_i32, [_P]),
+    "eagle_backend_fork_join": (_i32, [_P]),
+    "eagle_backend_fork_branch": (_i32, [_P, _u64, ctypes.POINTER(_u64)]),
+    "eagle_backend_fork_origin": (_i32, [_P, ctypes.POINTER(_u64)]),
+    "eagle_backend_fork_forked": (_i32, [_P, ctypes.POINTER(_i32)]),
+    "eagle_backend_fork_size": (_i32, [_P, ctypes.POINTER(_u64)]),
+    "eagle_backend_fork_release": (None, [_P]),
+    "eagle_backend_fork_mark": (_i32, [_P, _u64, ctypes.POINTER(_u64)]),
+    "eagle_backend_fork_wait": (_i32, [_P, _u64, _u64]),
+    "eagle_backend_conditional_create": (_i32, [ctypes.POINTER(ConditionalDesc), ctypes.POINTER(_P)]),
+    "eagle_backend_conditional_begin": (_i32, [_P, ctypes.POINTER(_u64)]),
+    "eagle_backend_conditional_body_stream": (_i32, [_P, ctypes.POINTER(_u64)]),
+    "eagle_backend_conditional_is_loop": (_i32, [_P, ctypes.POINTER(_i32)]),
+    "eagle_backend_conditional_end": (_i32, [_P]),
+    "eagle_backend_conditional_release": (None, [_P]),
+    "eagle_backend_conditional_arm_stream": (_i32, [_P, _u64, ctypes.POINTER(_u64)]),
+    "eagle_backend_conditional_nodes": (_i32, [_P, _i64, ctypes.POINTER(ctypes.POINTER(_u64)), ctypes.POINTER(_i64)]),
+    "eagle_backend_capture_snapshot_nodes": (_i32, [_u64, ctypes.POINTER(ctypes.POINTER(_u64)),
+                                                    ctypes.POINTER(_i64)]),
+    "eagle_backend_is_node_toggleable": (_i32, [_u64, ctypes.POINTER(_i32)]),
+    "eagle_backend_capture_add_child": (_i32, [_u64, _u64, _i32]),
+    "eagle_backend_graph_create": (_i32, [ctypes.POINTER(GraphDesc), ctypes.POINTER(_P)]),
+    "eagle_backend_graph_from_captured": (_i32, [_P, ctypes.POINTER(_P)]),
+    "eagle_backend_graph_stream": (_i32, [_P, _u64]),
+    "eagle_backend_graph_add_node": (_i32, [_P, _P]),
+    "eagle_backend_graph_launcher": (_i32, [_P, ctypes.POINTER(_P)]),
+    "eagle_backend_graph_last_node": (_i32, [_P, ctypes.POINTER(_i64)]),
+    "eagle_backend_graph_release": (None, [_P]),
+    "eagle_backend_launcher_launch": (_i32, [_P]),
+    "eagle_backend_launcher_synchronize": (_i32, [_P]),
+    "eagle_backend_launcher_stream": (_i32, [_P, _u64]),
+    "eagle_backend_launcher_set_logical_size": (_i32, [_P, _i64]),
+    "eagle_backend_launcher_kernel_node_count": (_i32, [_P, ctypes.POINTER(_i64)]),
+    "eagle_backend_launcher_set_node_enabled": (_i32, [_P, _u64, _i32]),
+    "eagle_backend_launcher_release": (None, [_P]),
+    "eagle_backend_launcher_set_kernel_params": (_i32, [_P, _u64, ctypes.POINTER(_u64), _i64]),
+    "eagle_backend_launcher_set_memcpy_source": (_i32, [_P, _u64, _u64]),
+    "eagle_backend_launcher_exec_update": (_i32, [_P, _P, ctypes.POINTER(_i32)]),
+    "eagle_backend_launcher_clone_graph": (_i32, [_P, ctypes.POINTER(_u64)]),
+    "eagle_backend_launcher_graph_destroy": (_i32, [_u64]),
     "eagle_backend_run_device": (_i32, [ctypes.POINTER(LaunchDesc), ctypes.POINTER(_i32)]),
     "eagle_backend_device_props": (_i32, [_i32, ctypes.POINTER(DeviceProps)]),
     "eagle_backend_memset_device": (_i32, [_u64, _u64, _u64]),

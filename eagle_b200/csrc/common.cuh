@@ -136,6 +136,9 @@ inline void launchCheck(const char* who)
             + cudaGetErrorString(e) + ")");
 }
 
+/** UNAVAILABLE unless a CUDA device is visible. */
+void requireDevice();
+
 /** SMs of the current device (cached per device). */
 int smCount();
 

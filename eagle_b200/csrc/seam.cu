@@ -72,8 +72,6 @@ int smCount()
     return cache[size_t(dev)];
 }
 
-namespace {
-
 void requireDevice()
 {
     int count = 0;
@@ -84,6 +82,8 @@ void requireDevice()
             + (e != cudaSuccess ? std::string(" (") + cudaGetErrorName(e) + ")" : std::string()));
     }
 }
+
+namespace {
 
 void copyText(char* dst, size_t n, const char* src)
 {
@@ -157,8 +157,15 @@ EB_API eagle_backend_status eagle_backend_capabilities(uint64_t* groups)
     return guarded([&] {
         if (groups == nullptr)
             invalid("eagle_backend_capabilities: null output");
-        *groups = EAGLE_BACKEND_CAP_STREAM | EAGLE_BACKEND_CAP_EXEC | EAGLE_BACKEND_CAP_DEVICE
+        *groups = EAGLE_BACKEND_CAP_STREAM | EAGLE_BACKEND_CAP_CAPTURER | EAGLE_BACKEND_CAP_CAPTURED
+            | EAGLE_BACKEND_CAP_FORK | EAGLE_BACKEND_CAP_CONDITIONAL | EAGLE_BACKEND_CAP_ATTRIBUTION
+            | EAGLE_BACKEND_CAP_GRAPH | EAGLE_BACKEND_CAP_LAUNCHER | EAGLE_BACKEND_CAP_EXEC | EAGLE_BACKEND_CAP_DEVICE
             | EAGLE_BACKEND_CAP_FILTERING;
+        // IF/ELSE and SWITCH nodes exist from driver 12.8 on: the driver's version is their capability.
+        int v = 0;
+        if (cudaDriverGetVersion(&v) == cudaSuccess && v >= 12080)
+            *groups |= EAGLE_BACKEND_CAP_CONDITIONAL_IF_ELSE | EAGLE_BACKEND_CAP_CONDITIONAL_SWITCH;
+        (void)cudaGetLastError();
     });
 }
 

@@ -43,11 +43,35 @@ typedef int32_t eagle_backend_status;
 #define EAGLE_BACKEND_UNSUPPORTED 8
 
 #define EAGLE_BACKEND_CAP_STREAM (UINT64_C(1) << 0)
+#define EAGLE_BACKEND_CAP_CAPTURER (UINT64_C(1) << 1)
+#define EAGLE_BACKEND_CAP_CAPTURED (UINT64_C(1) << 2)
+#define EAGLE_BACKEND_CAP_FORK (UINT64_C(1) << 3)
+#define EAGLE_BACKEND_CAP_CONDITIONAL (UINT64_C(1) << 4)
+#define EAGLE_BACKEND_CAP_ATTRIBUTION (UINT64_C(1) << 5)
+#define EAGLE_BACKEND_CAP_GRAPH (UINT64_C(1) << 6)
+#define EAGLE_BACKEND_CAP_LAUNCHER (UINT64_C(1) << 7)
 #define EAGLE_BACKEND_CAP_EXEC (UINT64_C(1) << 9)
 #define EAGLE_BACKEND_CAP_DEVICE (UINT64_C(1) << 10)
 #define EAGLE_BACKEND_CAP_FILTERING (UINT64_C(1) << 12)
+#define EAGLE_BACKEND_CAP_CONDITIONAL_IF_ELSE (UINT64_C(1) << 13)
+#define EAGLE_BACKEND_CAP_CONDITIONAL_SWITCH (UINT64_C(1) << 14)
+
+/* Conditional node kinds (eagle_backend.h:144-147); 0 = WHILE when counter_ptr
+ * is set, else IF. */
+#define EAGLE_BACKEND_COND_IF 1u
+#define EAGLE_BACKEND_COND_IF_ELSE 2u
+#define EAGLE_BACKEND_COND_WHILE 3u
+#define EAGLE_BACKEND_COND_SWITCH 4u
+/* A WHILE's loop_cap for a loop the guard alone ends. */
+#define EAGLE_BACKEND_LOOP_UNCAPPED 0xFFFFFFFFu
 
 typedef struct eagle_backend_stream_s* eagle_backend_stream;
+typedef struct eagle_backend_capturer_s* eagle_backend_capturer;
+typedef struct eagle_backend_captured_s* eagle_backend_captured;
+typedef struct eagle_backend_fork_s* eagle_backend_fork;
+typedef struct eagle_backend_conditional_s* eagle_backend_conditional;
+typedef struct eagle_backend_graph_s* eagle_backend_graph;
+typedef struct eagle_backend_launcher_s* eagle_backend_launcher;
 
 /* ---- structs ------------------------------------------------------------------ */
 
@@ -77,6 +101,54 @@ struct eagle_backend_device_props {
 
 /* eagle_backend.h:194-199 */
 struct eagle_backend_stream_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    int32_t reserved0;
+};
+
+/* eagle_backend.h:200-206 */
+struct eagle_backend_capturer_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    int32_t reserved0;
+    uint64_t stream; /* the stream to capture */
+};
+
+/* eagle_backend.h:208-216 */
+struct eagle_backend_fork_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    int32_t reserved0;
+    uint64_t origin;       /* the stream the branches fork from */
+    uint64_t branch_count;
+    uint64_t wait_count;   /* marks fork_mark may make */
+};
+
+/* eagle_backend.h:218-234. The guard is ``(*count != (baseline ? *baseline : 0))
+ * != negate`` (a null count always holds); a WHILE keeps ``counter_ptr[2] =
+ * {remaining, ran}``, reset by its head setter every replay. */
+struct eagle_backend_conditional_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    uint32_t loop_cap;     /* WHILE iteration cap per replay, >= 1 */
+    uint64_t origin;       /* the capturing stream the node is woven into */
+    uint64_t count_ptr;    /* device uint32* (SWITCH: the arm index) */
+    uint64_t baseline_ptr; /* device uint32*, 0 = none */
+    uint64_t counter_ptr;  /* device uint32[2] for a WHILE, 0 = IF */
+    uint32_t kind;         /* EAGLE_BACKEND_COND_*, 0 = from counter_ptr */
+    uint32_t arms;         /* 0 = the kind's own; SWITCH: the arm count */
+    uint32_t negate;
+    uint32_t reserved1;
+    uint64_t brk_ptr;      /* WHILE: device uint32 break cell, 0 = none */
+    uint64_t limit_ptr;    /* WHILE: device uint32 trip count, 0 = none */
+};
+
+/* eagle_backend.h:236-241 */
+struct eagle_backend_graph_desc {
     uint32_t struct_size;
     uint32_t flags;
     int32_t device;
@@ -240,6 +312,95 @@ eagle_backend_status eagle_backend_stream_create(const struct eagle_backend_stre
 eagle_backend_status eagle_backend_stream_ptr(eagle_backend_stream h, uint64_t* stream);
 eagle_backend_status eagle_backend_stream_synchronize(eagle_backend_stream h);
 void eagle_backend_stream_release(eagle_backend_stream h);
+
+/* ---- capturer (bit 1; eagle_backend.h:288-294): a thread-local stream capture - */
+
+eagle_backend_status eagle_backend_capturer_create(const struct eagle_backend_capturer_desc* desc, eagle_backend_capturer* out);
+eagle_backend_status eagle_backend_capturer_begin(eagle_backend_capturer h);
+eagle_backend_status eagle_backend_capturer_end(eagle_backend_capturer h, eagle_backend_captured* out);
+/* eagle_backend.h:292: the graph the in-flight capture records into (0: none) */
+eagle_backend_status eagle_backend_capturer_graph(eagle_backend_capturer h, uint64_t* graph);
+void eagle_backend_capturer_release(eagle_backend_capturer h);
+
+/* ---- captured (bit 2; eagle_backend.h:298-299) --------------------------------- */
+
+eagle_backend_status eagle_backend_captured_is_valid(eagle_backend_captured h, int32_t* valid);
+void eagle_backend_captured_release(eagle_backend_captured h);
+
+/* ---- fork (bit 3; eagle_backend.h:303-318): branch streams made at create ------ */
+
+eagle_backend_status eagle_backend_fork_create(const struct eagle_backend_fork_desc* desc, eagle_backend_fork* out);
+eagle_backend_status eagle_backend_fork_fork(eagle_backend_fork h);
+eagle_backend_status eagle_backend_fork_join(eagle_backend_fork h);
+/* INDEX when ``i`` is out of range */
+eagle_backend_status eagle_backend_fork_branch(eagle_backend_fork h, uint64_t i, uint64_t* stream);
+eagle_backend_status eagle_backend_fork_origin(eagle_backend_fork h, uint64_t* stream);
+eagle_backend_status eagle_backend_fork_forked(eagle_backend_fork h, int32_t* forked);
+eagle_backend_status eagle_backend_fork_size(eagle_backend_fork h, uint64_t* n);
+void eagle_backend_fork_release(eagle_backend_fork h);
+/* eagle_backend.h:314-318: mark branch ``producer``'s tip; branch ``waiter`` waits on a mark */
+eagle_backend_status eagle_backend_fork_mark(eagle_backend_fork h, uint64_t producer, uint64_t* mark);
+eagle_backend_status eagle_backend_fork_wait(eagle_backend_fork h, uint64_t waiter, uint64_t mark);
+
+/* ---- conditional (bit 4, + 13 IF/ELSE, 14 SWITCH; eagle_backend.h:322-333) -----
+ * create makes the arm streams (call it before the capture begins); begin weaves a
+ * 1x1 setter kernel and the conditional node at the origin's capture tip and opens
+ * the arm captures; end closes them (a WHILE first captures its tail setter as the
+ * body's last node). An arm that launched nothing is refused at end. */
+
+eagle_backend_status eagle_backend_conditional_create(const struct eagle_backend_conditional_desc* desc, eagle_backend_conditional* out);
+eagle_backend_status eagle_backend_conditional_begin(eagle_backend_conditional h, uint64_t* body_stream);
+eagle_backend_status eagle_backend_conditional_body_stream(eagle_backend_conditional h, uint64_t* body_stream);
+eagle_backend_status eagle_backend_conditional_is_loop(eagle_backend_conditional h, int32_t* is_loop);
+eagle_backend_status eagle_backend_conditional_end(eagle_backend_conditional h);
+void eagle_backend_conditional_release(eagle_backend_conditional h);
+eagle_backend_status eagle_backend_conditional_arm_stream(eagle_backend_conditional h, uint64_t k, uint64_t* stream);
+/* ``which`` >= 0: arm ``which``'s body nodes; -1: the setter nodes (head, + a
+ * WHILE's tail). ``*nodes`` is freed with eagle_backend_free. */
+eagle_backend_status eagle_backend_conditional_nodes(eagle_backend_conditional h, int64_t which, uint64_t** nodes,
+    int64_t* count);
+
+/* ---- attribution (bit 5; eagle_backend.h:339-346) ------------------------------ */
+
+eagle_backend_status eagle_backend_capture_snapshot_nodes(uint64_t stream, uint64_t** nodes, int64_t* count);
+eagle_backend_status eagle_backend_is_node_toggleable(uint64_t node, int32_t* toggleable);
+eagle_backend_status eagle_backend_capture_add_child(uint64_t stream, uint64_t child, int32_t conditional_body);
+
+/* ---- graph (bit 6; eagle_backend.h:350-358): a created graph starts with one
+ * empty node; add_node chains a captured graph after the last node -------------- */
+
+eagle_backend_status eagle_backend_graph_create(const struct eagle_backend_graph_desc* desc, eagle_backend_graph* out);
+/* CONSUMES ``captured`` on OK; INVALID_ARGUMENT for an empty capture */
+eagle_backend_status eagle_backend_graph_from_captured(eagle_backend_captured captured, eagle_backend_graph* out);
+eagle_backend_status eagle_backend_graph_stream(eagle_backend_graph h, uint64_t stream);
+/* CONSUMES ``captured`` on OK */
+eagle_backend_status eagle_backend_graph_add_node(eagle_backend_graph h, eagle_backend_captured captured);
+eagle_backend_status eagle_backend_graph_launcher(eagle_backend_graph h, eagle_backend_launcher* out);
+eagle_backend_status eagle_backend_graph_last_node(eagle_backend_graph h, int64_t* index);
+void eagle_backend_graph_release(eagle_backend_graph h);
+
+/* ---- launcher (bit 7; eagle_backend.h:362-383): an instantiated graph ---------- */
+
+eagle_backend_status eagle_backend_launcher_launch(eagle_backend_launcher h);
+eagle_backend_status eagle_backend_launcher_synchronize(eagle_backend_launcher h);
+eagle_backend_status eagle_backend_launcher_stream(eagle_backend_launcher h, uint64_t stream);
+/* Re-grid every kernel node add_node gathered to ceil(logical_size / block); 0 keeps them */
+eagle_backend_status eagle_backend_launcher_set_logical_size(eagle_backend_launcher h, int64_t logical_size);
+eagle_backend_status eagle_backend_launcher_kernel_node_count(eagle_backend_launcher h, int64_t* count);
+eagle_backend_status eagle_backend_launcher_set_node_enabled(eagle_backend_launcher h, uint64_t node, int32_t enabled);
+void eagle_backend_launcher_release(eagle_backend_launcher h);
+/* Patch kernel node ``node``'s first ``n`` arguments from ``params`` (0 keeps the
+ * captured value); the source graph's node is patched too */
+eagle_backend_status eagle_backend_launcher_set_kernel_params(eagle_backend_launcher h, uint64_t node,
+    const uint64_t* params, int64_t n);
+eagle_backend_status eagle_backend_launcher_set_memcpy_source(eagle_backend_launcher h, uint64_t node, uint64_t src);
+/* ``*accepted`` = 0 when the driver rejects the update (the exec is unchanged) */
+eagle_backend_status eagle_backend_launcher_exec_update(eagle_backend_launcher h, eagle_backend_captured captured,
+    int32_t* accepted);
+/* An owned clone of the source graph (a cudaGraph_t); refuses host-function,
+ * conditional and memory-allocation nodes */
+eagle_backend_status eagle_backend_launcher_clone_graph(eagle_backend_launcher h, uint64_t* graph);
+eagle_backend_status eagle_backend_launcher_graph_destroy(uint64_t graph);
 
 /* ---- exec (bit 9; eagle_backend.h:389) ----------------------------------------- */
 

@@ -32,7 +32,11 @@ def test_library_loads_and_reports_its_version():
     assert L.eagle_backend_version() == (1 << 16) | 8
     groups = ctypes.c_uint64()
     assert L.eagle_backend_capabilities(ctypes.byref(groups)) == _abi.OK
-    assert groups.value == _abi.CAP_STREAM | _abi.CAP_EXEC | _abi.CAP_DEVICE | _abi.CAP_FILTERING
+    base = (_abi.CAP_STREAM | _abi.CAP_CAPTURER | _abi.CAP_CAPTURED | _abi.CAP_FORK | _abi.CAP_CONDITIONAL
+            | _abi.CAP_ATTRIBUTION | _abi.CAP_GRAPH | _abi.CAP_LAUNCHER | _abi.CAP_EXEC | _abi.CAP_DEVICE
+            | _abi.CAP_FILTERING)
+    arms = _abi.CAP_CONDITIONAL_IF_ELSE | _abi.CAP_CONDITIONAL_SWITCH
+    assert groups.value & ~arms == base  # the arm kinds follow the driver's version
     info = _abi.new(_abi.BuildInfo)
     assert L.eagle_backend_build_info(ctypes.byref(info)) == _abi.OK
     assert info.backend_kind == b"cuda" and info.abi_version == (1 << 16) | 8
@@ -58,6 +62,10 @@ _LAYOUTS = {
     "eagle_backend_reduce_desc": _abi.ReduceDesc,
     "eagle_b200_engine_desc": _abi.EngineDesc,
     "eagle_b200_report": _abi.Report,
+    "eagle_backend_capturer_desc": _abi.CapturerDesc,
+    "eagle_backend_fork_desc": _abi.ForkDesc,
+    "eagle_backend_conditional_desc": _abi.ConditionalDesc,
+    "eagle_backend_graph_desc": _abi.GraphDesc,
 }
 
 
@@ -85,6 +93,7 @@ def test_desc_layouts_match_the_header(tmp_path):
     assert int(got["eagle_backend_compact_desc"]) == 104
     assert int(got["eagle_backend_reduce_desc"]) == 96
     assert int(got["eagle_backend_cell_op_desc"]) == 208
+    assert int(got["eagle_backend_conditional_desc"]) == 80
 
 
 def test_compact_query_needs_no_device():
