@@ -114,7 +114,8 @@ class EngineDesc(ctypes.Structure):
                 ("reserved0", _u32), ("n", _i64), ("max_steps", _i64), ("planes", _u64 * 8),
                 ("uniforms", _f64 * 4), ("terminated", _u64), ("k_first", _i64), ("k_min", _i64),
                 ("k_max", _i64), ("chunk", _u32), ("block", _u32), ("overhead_steps", _f64),
-                ("interval_steps", _f64), ("iuniforms", _i64 * 4), ("uniforms_ext", _f64 * 4)]
+                ("interval_steps", _f64), ("iuniforms", _i64 * 4), ("uniforms_ext", _f64 * 4),
+                ("ctas_per_sm", _u32), ("reserved1", _u32)]
 
 
 class ScalarHandle(ctypes.Structure):

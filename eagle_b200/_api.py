@@ -185,8 +185,9 @@ class Runner:
 
     def __init__(self, model: Model, *, max_steps: int, mode: str = "auto", fma: bool = False, terminated=None,
                  device=None, k_first: int = 0, k_min: int = 0, k_max: int = 0, chunk: int = 0,
-                 overhead_steps: float = 0.0, interval_steps: float = 0.0, **planes):
+                 overhead_steps: float = 0.0, interval_steps: float = 0.0, ctas_per_sm: int = 0, **planes):
         torch = _t()
+        self._ctas_per_sm = int(ctas_per_sm)
         if model not in (oscillator, gambler, lorenz):
             raise ValueError(f"eagle_b200: unknown model {model!r}")
         if max_steps is None or int(max_steps) < 0:
@@ -252,6 +253,7 @@ class Runner:
         d.terminated = _ptr(terminated)
         d.k_first, d.k_min, d.k_max, d.chunk = int(k_first), int(k_min), int(k_max), int(chunk)
         d.overhead_steps, d.interval_steps = float(overhead_steps), float(interval_steps)
+        d.ctas_per_sm = self._ctas_per_sm
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             _abi.check(_abi.lib().eagle_backend_x_b200_engine_create(ctypes.byref(d), ctypes.byref(h)))
@@ -296,6 +298,7 @@ class Runner:
         d.iuniforms[1] = int(planes.get("id_base", 0))
         d.terminated = _ptr(terminated)
         d.chunk = int(chunk)
+        d.ctas_per_sm = self._ctas_per_sm
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             _abi.check(_abi.lib().eagle_backend_x_b200_engine_create(ctypes.byref(d), ctypes.byref(h)))
@@ -342,6 +345,7 @@ class Runner:
         d.uniforms_ext[0] = float(planes["atol"])
         d.terminated = _ptr(terminated)
         d.chunk = int(chunk)
+        d.ctas_per_sm = self._ctas_per_sm
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             _abi.check(_abi.lib().eagle_backend_x_b200_engine_create(ctypes.byref(d), ctypes.byref(h)))
@@ -396,6 +400,89 @@ class Runner:
 def until_done(model: Model, *, max_steps: int, **kwargs) -> Runner:
     """The :class:`Runner` of ``model`` over the given planes (python/eagle/_until_done.py:1775)."""
     return Runner(model, max_steps=max_steps, **kwargs)
+
+
+class StagedRunner:
+    """The until-done loop fed from host memory in chunks: chunk k's host-to-device
+    copies run on a copy stream while chunk k-1 steps on the compute stream, so the
+    transfer of a run overlaps its work instead of preceding it. Samples are
+    independent, so the chunked runs leave the bits of one run over all samples.
+
+    ``planes`` are the device planes and Params as for :class:`Runner` (CUDA
+    tensors of ``n`` samples); :meth:`launch` takes the per-sample inputs to copy
+    in, as pinned host tensors keyed by plane name, and zeroes the mask. The chunk
+    runs rotate over ``streams`` compute streams, each persistent run holding
+    ``ctas_per_sm`` CTAs per SM: a run lasts at least as long as its longest sample
+    whatever its size, and its resident CTAs wait out that tail, so narrower runs
+    side by side keep the tails of one chunk under the work of the others."""
+
+    def __init__(self, model: Model, *, max_steps: int, chunks: int = 16, streams: int = 4, ctas_per_sm: int = 1,
+                 terminated=None, device=None, **kwargs):
+        torch = _t()
+        per_sample = {k: v for k, v in kwargs.items() if isinstance(v, torch.Tensor) and v.is_cuda and v.dim() == 1}
+        if not per_sample:
+            raise ValueError("StagedRunner needs the device planes")
+        n = next(iter(per_sample.values())).numel()
+        if any(v.numel() != n or not v.is_contiguous() for v in per_sample.values()):
+            raise ValueError("every device plane must be a contiguous tensor of the same length")
+        chunks = max(1, min(int(chunks), n))
+        self.n, self.device = n, next(iter(per_sample.values())).device
+        if terminated is None:
+            terminated = torch.zeros(n, dtype=torch.uint8, device=self.device)
+        self.terminated = terminated
+        self.planes = per_sample
+        bounds = [n * k // chunks for k in range(chunks + 1)]
+        self.bounds = list(zip(bounds[:-1], bounds[1:]))
+        self.runners = []
+        for lo, hi in self.bounds:
+            sub = {k: (v[lo:hi] if k in per_sample else v) for k, v in kwargs.items()}
+            self.runners.append(Runner(model, max_steps=max_steps, terminated=terminated[lo:hi], device=self.device,
+                                       ctas_per_sm=ctas_per_sm, **sub))
+        self.mode = self.runners[0].mode
+        self.copy_stream = torch.cuda.Stream(self.device)
+        self.streams = [torch.cuda.Stream(self.device) for _ in range(max(1, int(streams)))]
+        self._start = torch.cuda.Event()
+        self._ready = [torch.cuda.Event() for _ in self.bounds]
+        self._done = [torch.cuda.Event() for _ in self.streams]
+
+    def launch(self, host: dict, stream=None) -> None:
+        """Enqueue one run whose inputs come from the pinned host tensors ``host``."""
+        torch = _t()
+        lib = _abi.lib()
+        stream = stream or torch.cuda.current_stream(self.device)
+        for name, h in host.items():
+            dev = self.planes[name]
+            if h.numel() != self.n or h.element_size() != dev.element_size() or h.is_cuda:
+                raise ValueError(f"host plane {name!r} must be {self.n} host samples of {dev.dtype}")
+        self._start.record(stream)  # the previous run is done with the buffers
+        self.copy_stream.wait_event(self._start)
+        for cs in self.streams:
+            cs.wait_event(self._start)
+        cs = self.copy_stream.cuda_stream
+        msize = self.terminated.element_size()
+        for k, (lo, hi) in enumerate(self.bounds):
+            for name, h in host.items():
+                dev = self.planes[name]
+                es = dev.element_size()
+                _abi.check(lib.eagle_backend_memcpy(dev.data_ptr() + lo * es, h.data_ptr() + lo * es,
+                                                    (hi - lo) * es, _abi.COPY_H2D, cs))
+            _abi.check(lib.eagle_backend_memset_device(self.terminated.data_ptr() + lo * msize, (hi - lo) * msize, cs))
+            self._ready[k].record(self.copy_stream)
+            run_on = self.streams[k % len(self.streams)]
+            run_on.wait_event(self._ready[k])
+            self.runners[k].launch(run_on)
+        for ev, cs_ in zip(self._done, self.streams):
+            ev.record(cs_)
+            stream.wait_event(ev)
+
+    def report(self, stream=None) -> RunReport:
+        """The run's report over all chunks (one small read per chunk)."""
+        reps = [r.report(stream) for r in self.runners]
+        fin = sum(r.finished for r in reps)
+        return RunReport(n=self.n, finished=fin, done=fin == self.n, steps=max(r.steps for r in reps),
+                         launches=sum(r.launches for r in reps), compactions=sum(r.compactions for r in reps),
+                         step_sum=sum(r.step_sum for r in reps), mode=self.mode,
+                         report_bytes=sum(r.report_bytes for r in reps))
 
 
 def simulate(model: Model, *, max_steps: int, mode: str = "auto", fma: bool = False, **planes) -> SimResult:

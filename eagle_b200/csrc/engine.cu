@@ -693,7 +693,8 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
                 const void* stub = entryStub(entryName(*e, true));
                 cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, stub, int(e->block), 0),
                     "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-                e->persistGrid = std::max(1, occ) * smCount();
+                const int perSm = d.ctas_per_sm > 0 ? std::min(int(d.ctas_per_sm), std::max(1, occ)) : std::max(1, occ);
+                e->persistGrid = perSm * smCount();
             }
         } catch (...) {
             destroy(e);

@@ -573,6 +573,9 @@ struct eagle_b200_engine_desc {
     double interval_steps; /* band: a launch's per-sample memory cost in steps (0: built-in) */
     int64_t iuniforms[4];  /* the model's integer Params, in the model's order */
     double uniforms_ext[4]; /* the model's float Params past the first four */
+    uint32_t ctas_per_sm;   /* persist: resident CTAs per SM (0: as many as fit); fewer leave room
+                             * for runs on other streams to overlap this run's tail */
+    uint32_t reserved1;
 };
 
 /* What one run did (python/eagle/_until_done.py:120-171, RunReport). */
