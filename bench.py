@@ -47,7 +47,11 @@ def _args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="engine", choices=("engine", "reference"))
     p.add_argument("--mode", default="auto", choices=("auto", "band", "band_eager", "persist", "fused"))
-    p.add_argument("--n", type=int, default=N_PER_GPU, help="samples per GPU")
+    p.add_argument("--n", type=int, default=None, help="samples per GPU (default: the workload's)")
+    p.add_argument("--workload", default="oscillator", choices=("oscillator", "lorenz", "gambler", "compact_sum"),
+                   help="oscillator: the headline 16M heterogeneous-stop run; the others time the other "
+                        "configurations' kernels (Lorenz RKF7(8) 2^22, gambler's ruin 2^26, compact-then-sum "
+                        "2^28) for their own lines")
     p.add_argument("--no-fma", action="store_true", help="exact (uncontracted) arithmetic profile")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-chunks", type=int, default=16)
@@ -396,8 +400,214 @@ def engine(args):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------- the other configurations
+
+def _timed(fn, steps, warmup, stream, reset=None):
+    """CUDA-event time of ``steps`` calls of ``fn`` after ``warmup`` (``reset`` runs
+    before every call, inside the timed region, as a run's re-initialisation)."""
+    import torch
+
+    for _ in range(warmup):
+        if reset:
+            reset()
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        if reset:
+            reset()
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _profile_value(key):
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(key)
+    except Exception:
+        return None
+
+
+def side_workload(args):
+    """One JSON line for the Lorenz, gambler or compact-then-sum configuration on
+    one GPU, with its CPU baseline (the oracle on a bounded prefix)."""
+    import torch
+
+    import eagle_b200 as eb
+    import oracle
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    oracle.build()
+    cores = oracle.threads()
+    line = {"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "data": "synthetic (seeded numpy, see bench.py)"}
+    if args.workload == "lorenz":
+        n = args.n or (1 << 22)
+        rng = np.random.default_rng
+        rho = rng(1).uniform(20.0, 40.0, n)
+        xyz = [rng(s).normal(1.0, 0.1, n) for s in (2, 3, 4)]
+        init = {"rho": rho, "x": xyz[0], "y": xyz[1], "z": xyz[2], "t": np.zeros(n), "h": np.full(n, 1e-3)}
+        d0 = {k: torch.from_numpy(v).to(dev) for k, v in init.items()}
+        planes = {k: v.clone() for k, v in d0.items()}
+        planes["n_acc"] = torch.zeros(n, dtype=torch.int32, device=dev)
+        planes["n_rej"] = torch.zeros(n, dtype=torch.int32, device=dev)
+        mask = torch.zeros(n, dtype=torch.uint8, device=dev)
+        prm = dict(sigma=10.0, beta=8.0 / 3.0, t_final=10.0, rtol=1e-9, atol=1e-12)
+        runner = eb.until_done(eb.lorenz, max_steps=200_000, mode="persist", terminated=mask, **planes, **prm)
+        red = eb.Reducer(planes["z"])
+
+        def reset():
+            for k in ("x", "y", "z", "t", "h"):
+                planes[k].copy_(d0[k])
+            planes["n_acc"].zero_()
+            planes["n_rej"].zero_()
+            mask.zero_()
+
+        def step():
+            runner.launch(stream)
+            red(stream)
+
+        with _Clocks(0) as clocks:
+            ms = _timed(step, args.steps, args.warmup, stream, reset)
+        rep = runner.report(stream)
+        instr = _profile_value("lorenz_fp64_instr_per_attempt")
+        achieved = instr * rep.step_sum / (ms / 1e3) / 1e12 if instr else None
+        props = torch.cuda.get_device_properties(0)
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                mhz = float(json.load(f)["sm_max_mhz"])
+        except Exception:
+            mhz = 1965.0
+        fp64_peak = 64 * props.multi_processor_count * mhz * 1e6 / 1e12  # FP64 lanes per SM per cycle
+        m = min(n, 1 << 15)
+        host = {k: v[:m].copy() for k, v in init.items()}
+        na, nr, term = np.zeros(m, np.uint32), np.zeros(m, np.uint32), np.zeros(m, np.uint8)
+        t0 = time.perf_counter()
+        _, _, total = oracle.lorenz_run(host["rho"], host["x"], host["y"], host["z"], host["t"], host["h"], na, nr,
+                                        term, max_steps=200_000, **prm)
+        sec = time.perf_counter() - t0
+        line.update({"metric": "attempts/s, 4M-sample Lorenz-63 adaptive RKF7(8)", "value": rep.step_sum / (ms / 1e3),
+                     "unit": "attempts/s", "ms_per_step": ms, "dtype": "f64",
+                     "config": {"workload": "lorenz63-rkf78", "n": n, "max_steps": 200_000, **prm, "h0": 1e-3,
+                                "attempts_per_run": rep.step_sum, "longest": rep.steps,
+                                "status": "finished" if rep.done else "max_steps",
+                                "l2": "state 8 planes x 32 MiB, re-initialised every step (the kernel is FP64-bound)"},
+                     "result": {"sum_z": float(red.out[0].item())},
+                     "roofline": {"bound": "fp64", "achieved": achieved, "peak": fp64_peak,
+                                  "unit": "T FP64 lane-instructions/s",
+                                  "frac": achieved / fp64_peak if achieved else None, "traffic": None,
+                                  "peak_kind": "derived: 64 FP64 lanes per SM per cycle x SMs x the measured max SM "
+                                               "clock (no FP64 figure is measured on this pool)",
+                                  "basis": "FP64 thread instructions per attempt counted by ncu (profiles/"
+                                           "traffic.json) x attempts per run / run time"},
+                     "cpu_baseline": {"value": total / sec, "unit": "attempts/s", "cores": cores, "kind": "port",
+                                      "sample": f"the first {m} samples run to t_final ({total} attempts, {sec:.2f} s)"},
+                     "gpu_launches": 4 * args.steps, "clocks": clocks.summary()})
+    elif args.workload == "gambler":
+        n = args.n or (1 << 26)
+        pos0 = np.random.default_rng(1).integers(1, 100, n).astype(np.int32)
+        seed = 2026
+        d_pos0 = torch.from_numpy(pos0).to(dev)
+        pos, tm = d_pos0.clone(), torch.zeros(n, dtype=torch.int64, device=dev)
+        mask = torch.zeros(n, dtype=torch.uint8, device=dev)
+        runner = eb.until_done(eb.gambler, max_steps=1_000_000, mode="persist", terminated=mask, pos=pos, time=tm,
+                               seed=seed)
+        red = eb.Reducer(tm)
+
+        def reset():
+            pos.copy_(d_pos0)
+            tm.zero_()
+            mask.zero_()
+
+        def step():
+            runner.launch(stream)
+            red(stream)
+
+        with _Clocks(0) as clocks:
+            ms = _timed(step, args.steps, args.warmup, stream, reset)
+        rep = runner.report(stream)
+        m = min(n, 1 << 18)
+        hp, ht, term = pos0[:m].copy(), np.zeros(m, np.int64), np.zeros(m, np.uint8)
+        t0 = time.perf_counter()
+        _, _, total = oracle.gambler_run(hp, ht, term, seed=seed, max_steps=1_000_000)
+        sec = time.perf_counter() - t0
+        line.update({"metric": "sample-steps/s, 64M gambler's-ruin walk (Philox-4x32-10)",
+                     "value": rep.step_sum / (ms / 1e3), "unit": "sample-steps/s", "ms_per_step": ms,
+                     "dtype": "int32 position, int64 time",
+                     "config": {"workload": "gamblers-ruin-philox", "n": n, "max_steps": 1_000_000, "seed": seed,
+                                "absorb": [0, 100], "sample_steps_per_run": rep.step_sum, "longest": rep.steps,
+                                "status": "finished" if rep.done else "max_steps",
+                                "l2": "inputs 768 MiB, re-initialised every step"},
+                     "result": {"sum_time": int(red.out[0].item()), "mean_time": float(red.out[0].item()) / n},
+                     "roofline": {"bound": "integer ALU", "achieved": None, "peak": None, "unit": None,
+                                  "frac": None, "traffic": None,
+                                  "basis": "Philox-4x32-10 per 128 steps plus a compare per step: integer-issue "
+                                           "bound; the ncu pipe shares are in profiles/"},
+                     "cpu_baseline": {"value": total / sec, "unit": "sample-steps/s", "cores": cores, "kind": "port",
+                                      "sample": f"the first {m} samples run to absorption ({total} steps, {sec:.2f} s)"},
+                     "gpu_launches": 4 * args.steps, "clocks": clocks.summary()})
+    else:
+        n = args.n or (1 << 28)
+        rng = np.random.default_rng(4)
+        vals = rng.standard_normal(n)
+        big = np.random.default_rng(5).choice(n, size=max(1, n // 1_000_000), replace=False)
+        sign = np.where(np.random.default_rng(6).random(big.size) < 0.5, -1.0, 1.0)
+        vals[big] = sign * 1e12
+        x = torch.from_numpy(vals).to(dev)
+        ps = (0.9, 0.5, 0.1, 0.01)
+        masks = [torch.from_numpy(np.random.default_rng(7 + i).random(n) < p).to(dev) for i, p in enumerate(ps)]
+        sums = [eb.CompactSum(mk, x) for mk in masks]
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MiB: evicts the 126 MB L2
+
+        def step():
+            for cs in sums:
+                flush.zero_()
+                cs(stream)
+
+        with _Clocks(0) as clocks:
+            ms = _timed(step, args.steps, args.warmup, stream)
+        flush_ms = _timed(lambda: [flush.zero_() for _ in ps], 3, 1, stream)
+        work_ms = max(ms - flush_ms, 1e-6)
+        counts = [int(cs.count.item()) for cs in sums]
+        alg = sum(n + 8 * n * (1 - (1 - p) ** 4) for p in ps)  # mask + every 32 B value sector with a survivor
+        peak, peak_kind = _peaks()
+        m = min(n, 1 << 24)
+        t0 = time.perf_counter()
+        for i, p in enumerate(ps):
+            keep = np.random.default_rng(7 + i).random(m) < p
+            idx, _ = oracle.compact(keep, drop=False)
+            oracle.reduce(vals[:m][idx])
+        sec = time.perf_counter() - t0
+        line.update({"metric": "GB/s, 2^28 compact-then-sum vs the HBM roofline", "value": alg / (work_ms / 1e3) / 1e9,
+                     "unit": "GB/s", "ms_per_step": ms, "dtype": "f64 values, u8 mask",
+                     "config": {"workload": "compact-then-sum", "n": n, "p": list(ps), "kept": counts,
+                                "l2": "a 256 MiB buffer is written before every compaction (its time is measured "
+                                      "apart and taken out)", "flush_ms_per_step": flush_ms},
+                     "result": {"sums": [float(cs.out[0].item()) for cs in sums]},
+                     "roofline": {"bound": "hbm", "achieved": alg / (work_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                                  "frac": alg / (work_ms / 1e3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
+                                  "basis": "n mask bytes + 8 n (1 - (1 - p)^4) value bytes per mask (the sectors "
+                                           "holding a survivor), summed over the four masks / compaction time"},
+                     "cpu_baseline": {"value": 4 * (m + 8 * m) / sec / 1e9, "unit": "GB/s", "cores": cores,
+                                      "kind": "port",
+                                      "sample": f"the first {m} samples of each mask: compaction then canonical "
+                                                f"sum ({sec:.2f} s; mask + values read)"},
+                     "gpu_launches": 4 * 3 * args.steps, "clocks": clocks.summary()})
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = _args()
+    if args.workload != "oscillator":
+        side_workload(args)
+        return
+    if args.n is None:
+        args.n = N_PER_GPU
     if args.impl == "reference":
         reference(args)
     else:
