@@ -96,6 +96,10 @@ class CompactDesc(ctypes.Structure):
                 ("reserved2", _u32)]
 
 
+class ReorderPlane(ctypes.Structure):
+    _fields_ = [("data", _u64), ("elem_bytes", _u32), ("reserved", _u32)]
+
+
 class ReorderDesc(ctypes.Structure):
     _fields_ = [("struct_size", _u32), ("flags", _u32), ("device", _i32), ("n_planes", _u32), ("planes", _u64),
                 ("mask", _u64), ("perm", _u64), ("inv", _u64), ("index_map", _u64), ("count", _u64),
@@ -173,6 +177,9 @@ SIGNATURES = {
     "eagle_backend_stream_ptr": (_i32, [_P, ctypes.POINTER(_u64)]),
     "eagle_backend_stream_synchronize": (_i32, [_P]),
     "eagle_backend_stream_release": (None, [_P]),
+    "eagle_backend_reorder_device": (_i32, [ctypes.POINTER(ReorderDesc)]),
+    "eagle_backend_x_restore_device": (_i32, [ctypes.POINTER(ReorderDesc)]),
+    "eagle_backend_pointer_residency": (_i32, [_i32, _u64, ctypes.POINTER(_i32)]),
     "eagle_backend_capturer_create": (_i32, [ctypes.POINTER(CapturerDesc), ctypes.POINTER(_P)]),
     "eagle_backend_capturer_begin": (_i32, [_P]),
     "eagle_backend_capturer_end": (_i32, [_P, ctypes.POINTER(_P)]),

@@ -700,3 +700,54 @@ class CompactSum:
                                                                    _ptr(self.kept), 8))
         _abi.check(_abi.lib().eagle_backend_x_b200_reduce_counted(ctypes.byref(self.rdesc), _ptr(self.count)))
         return self.out
+
+
+# ------------------------------------------------------------------------- physical reorder
+
+def _plane_table(planes):
+    torch = _t()
+    tab = (_abi.ReorderPlane * max(1, len(planes)))()
+    for k, p in enumerate(planes):
+        if not (isinstance(p, torch.Tensor) and p.is_cuda and p.is_contiguous()):
+            raise ValueError("reorder planes must be contiguous CUDA tensors")
+        tab[k].data = _ptr(p)
+        tab[k].elem_bytes = p.element_size()
+    return tab
+
+
+def reorder(planes, mask, perm, inv, index_map, count, span, *, fire=None, drop: bool = True, stream=None):
+    """Physically reorder ``planes`` (the ``mask`` among them) in place over
+    ``[0, span)``: the kept samples first in ascending order, the dropped ones after
+    (eagle/filtering/Reorder.h; ``eagle_backend_reorder_device``). ``perm`` / ``inv``
+    (int32) follow the moves, ``index_map`` becomes the identity over ``[0, count)``;
+    ``count``, ``span`` (and ``fire``, which gates the whole call on the device) are
+    one-element uint32/int32 CUDA cells. Enqueue only; the scratch is allocated here."""
+    torch = _t()
+    n = perm.numel()
+    tab = _plane_table(planes)
+    d = _abi.new(_abi.ReorderDesc, flags=_abi.COMPACT_MASK_IS_DROP if drop else 0, device=perm.device.index,
+                 n_planes=len(planes), planes=ctypes.addressof(tab), mask=_ptr(mask), perm=_ptr(perm), inv=_ptr(inv),
+                 index_map=_ptr(index_map), count=_ptr(count), span=_ptr(span),
+                 fire=_ptr(fire) if fire is not None else 0, n=n)
+    _abi.check(_abi.lib().eagle_backend_reorder_device(ctypes.byref(d)))  # query
+    scratch = torch.empty(max(1, int(d.scratch_bytes)), dtype=torch.uint8, device=perm.device)
+    d.scratch = _ptr(scratch)
+    d.stream = _stream_handle(stream)
+    _abi.check(_abi.lib().eagle_backend_reorder_device(ctypes.byref(d)))
+    return scratch  # keep alive until the stream is past the call
+
+
+def restore(planes, perm, inv, *, stream=None):
+    """Undo every reorder since the last restore (``eagle_backend_x_restore_device``):
+    each plane back in sample order, ``perm`` and ``inv`` the identity."""
+    torch = _t()
+    n = perm.numel()
+    tab = _plane_table(planes)
+    d = _abi.new(_abi.ReorderDesc, device=perm.device.index, n_planes=len(planes), planes=ctypes.addressof(tab),
+                 perm=_ptr(perm), inv=_ptr(inv), n=n)
+    _abi.check(_abi.lib().eagle_backend_x_restore_device(ctypes.byref(d)))  # query
+    scratch = torch.empty(max(1, int(d.scratch_bytes)), dtype=torch.uint8, device=perm.device)
+    d.scratch = _ptr(scratch)
+    d.stream = _stream_handle(stream)
+    _abi.check(_abi.lib().eagle_backend_x_restore_device(ctypes.byref(d)))
+    return scratch

@@ -1,0 +1,493 @@
+// The physical reorder of the active set (eagle/filtering/Reorder.h; seam
+// python/src/seam/eagle_backend.h:705-740) and its undo (x_restore_device,
+// :855-859).
+//
+// reorder_device moves every plane IN PLACE over [0, *span) so that the samples
+// the mask keeps fill [0, *count) in ascending sample order and the dropped ones
+// follow, also in ascending order (a stable partition: slot i goes to
+// incl(i) - 1 when kept, to count + i - incl(i) when dropped, incl being the
+// inclusive kept count, Reorder.h reorderDst); perm moves with the planes, inv is
+// rebuilt for the moved slots, index_map becomes the identity over [0, *count)
+// and *span = *count. With a fire word, every kernel returns at once while
+// *fire == 0, and the last one clears it, so the whole reorder can sit in a
+// captured loop and run only when the reorder trigger fired.
+//
+// Here: ONE scan kernel (16 mask bytes per thread, CTA scan, decoupled look-back
+// over 4096-slot tiles) records each tile's keep bits and its exclusive kept
+// prefix in the scratch, since the mask itself is one of the planes that move.
+// Each plane then takes two kernels: a copy of [0, *span) into the stage, and a
+// tile kernel that reads its 4096 staged elements, places them in shared memory
+// in their new order (kept run first, dropped run after) and writes both runs
+// with coalesced stores. Nothing reads *span or *fire on the host, so every
+// launch is capturable.
+#include "common.cuh"
+
+#include <cstdlib>
+#include <mutex>
+#include <set>
+#include <string>
+#include <utility>
+#include <vector>
+
+#define EB_API extern "C" __attribute__((visibility("default")))
+
+namespace eb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kPer = 16;
+constexpr int64_t kTile = int64_t(kThreads) * kPer;
+
+struct alignas(16) Elem16 {
+    uint64_t lo, hi;
+};
+
+/** The scratch layout of a reorder of n samples whose widest moved element is
+ *  ``elem`` bytes: tile status words, three counters, tile prefixes, tile keep
+ *  bits (one uint16 per thread), then the stage. */
+struct Layout {
+    size_t status, words, prefix, bits, stage, total;
+};
+
+Layout layoutFor(int64_t n, uint32_t elem)
+{
+    const size_t tiles = size_t(n > 0 ? (n + kTile - 1) / kTile : 1);
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    Layout l{};
+    l.status = 0;
+    l.words = up(tiles * sizeof(uint64_t));
+    l.prefix = l.words + 256;
+    l.bits = up(l.prefix + tiles * sizeof(uint32_t));
+    l.stage = up(l.bits + tiles * kThreads * sizeof(uint16_t));
+    l.total = up(l.stage + size_t(n > 0 ? n : 1) * (elem > 4 ? elem : 4));
+    return l;
+}
+
+struct ScanArgs {
+    const uint8_t* mask;
+    int64_t n;
+    const uint32_t* span;
+    const uint32_t* fire;
+    uint64_t* status;
+    uint32_t* tileNext;
+    uint32_t* err;
+    uint32_t* cnt;
+    uint32_t* prefix;
+    uint16_t* bits;
+    uint32_t tiles;
+};
+
+__device__ __forceinline__ int64_t spanOf(const uint32_t* span, int64_t n)
+{
+    const int64_t s = int64_t(*span);
+    return s < n ? s : n;
+}
+
+template <bool Drop>
+__global__ __launch_bounds__(kThreads) void reorderScanKernel(ScanArgs a)
+{
+    if (a.fire != nullptr && *a.fire == 0u)
+        return;
+    __shared__ uint32_t sTile;
+    __shared__ uint32_t scan[33];
+    const int t = int(threadIdx.x);
+    if (t == 0)
+        sTile = atomicAdd(a.tileNext, 1u);
+    __syncthreads();
+    const uint32_t tile = sTile;
+    const int64_t sp = spanOf(a.span, a.n);
+    const int64_t i0 = int64_t(tile) * kTile + int64_t(t) * kPer;
+    uint32_t keep = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int64_t i = i0 + j;
+        if (i < sp) {
+            const bool set = a.mask[i] != 0;
+            keep |= uint32_t(set != Drop) << j;
+        }
+    }
+    a.bits[size_t(tile) * kThreads + size_t(t)] = uint16_t(keep);
+    uint32_t total = 0;
+    blockExclusiveSum(uint32_t(__popc(keep)), total, scan);
+    if (t < 32) {
+        uint64_t prefix = 0;
+        if (tile == 0) {
+            if (t == 0)
+                lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, total);
+        } else {
+            if (t == 0)
+                lbPublish<PlainCodec>(a.status, tile, 0, kLbAggregate, total);
+            prefix = lbExclusivePrefix<PlainCodec>(a.status, tile, 0, a.err);
+            if (t == 0)
+                lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, prefix + total);
+        }
+        if (t == 0) {
+            a.prefix[tile] = uint32_t(prefix);
+            if (tile == a.tiles - 1)
+                *a.cnt = *a.err != 0u ? 0xffffffffu : uint32_t(prefix + total);
+        }
+    }
+}
+
+/** stage[i] = plane[i] over [0, *span) (or [0, n) without a span). */
+template <class T>
+__global__ __launch_bounds__(kThreads) void copySpanKernel(const T* __restrict__ src, T* __restrict__ dst,
+    const uint32_t* span, const uint32_t* fire, int64_t n)
+{
+    if (fire != nullptr && *fire == 0u)
+        return;
+    const int64_t end = span != nullptr ? spanOf(span, n) : n;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < end; i += int64_t(gridDim.x) * blockDim.x)
+        dst[i] = src[i];
+}
+
+struct PlaceArgs {
+    const void* stage;
+    void* plane;
+    const uint16_t* bits;
+    const uint32_t* prefix;
+    const uint32_t* cnt;
+    const uint32_t* span;
+    const uint32_t* fire;
+    const uint32_t* err;
+    int32_t* inv;       // Perm only
+    int32_t* indexMap;  // Perm only
+    int64_t n;
+};
+
+/** One 4096-slot tile of one plane into its new places. With ``Perm`` the plane
+ *  is perm: inv[v] = new slot for each moved value v, and index_map is the
+ *  identity over the tile's part of [0, count). */
+template <class T, bool Perm>
+__global__ __launch_bounds__(kThreads) void placeKernel(PlaceArgs a)
+{
+    if (a.fire != nullptr && *a.fire == 0u)
+        return;
+    if (*a.err != 0u)
+        return;  // the scan gave up: leave the planes as they were
+    extern __shared__ __align__(16) unsigned char smem[];
+    T* out = reinterpret_cast<T*>(smem);
+    __shared__ uint32_t scan[33];
+    const int t = int(threadIdx.x);
+    const uint32_t tile = blockIdx.x;
+    const int64_t sp = spanOf(a.span, a.n);
+    const int64_t tile0 = int64_t(tile) * kTile;
+    if (tile0 >= sp)
+        return;  // the whole CTA: nothing of this tile moves
+    const int64_t len = sp - tile0 < kTile ? sp - tile0 : kTile;
+    const uint32_t keep = a.bits[size_t(tile) * kThreads + size_t(t)];
+    uint32_t kept = 0;
+    const uint32_t excl = blockExclusiveSum(uint32_t(__popc(keep)), kept, scan);
+    const int64_t pre = int64_t(a.prefix[tile]);  // kept slots before the tile
+    const int64_t cnt = int64_t(*a.cnt);
+    const T* src = static_cast<const T*>(a.stage);
+    // tile-local places: kept ones at [0, kept), dropped ones at [kept, len)
+    uint32_t k = excl;
+    uint32_t dpos = kept + uint32_t(t * kPer) - excl;  // dropped before this thread's run
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int64_t i = tile0 + int64_t(t) * kPer + j;
+        if (i < sp) {
+            const T v = src[i];
+            if ((keep >> j) & 1u)
+                out[k++] = v;
+            else
+                out[dpos++] = v;
+        }
+    }
+    __syncthreads();
+    T* dst = static_cast<T*>(a.plane);
+    // the kept run lands at [pre, pre + kept), the dropped run at [cnt + tile0 - pre, ...)
+    const int64_t dropAt = cnt + tile0 - pre;
+    for (int q = t; q < int(len); q += kThreads) {
+        const int64_t d = q < int(kept) ? pre + q : dropAt + (q - int(kept));
+        const T v = out[q];
+        dst[d] = v;
+        if constexpr (Perm) {
+            a.inv[static_cast<int32_t>(v)] = int32_t(d);
+            if (q < int(kept))
+                a.indexMap[d] = int32_t(d);
+        }
+    }
+}
+
+__global__ void reorderFinishKernel(const uint32_t* cnt, const uint32_t* err, uint32_t* count, uint32_t* span,
+    uint32_t* fire)
+{
+    if (fire != nullptr && *fire == 0u)
+        return;
+    const uint32_t c = *err != 0u ? 0xffffffffu : *cnt;  // a count above n reports a failed reorder
+    *count = c;
+    if (*err == 0u)
+        *span = c;
+    if (fire != nullptr)
+        *fire = 0u;
+}
+
+__global__ void reorderEmptyKernel(uint32_t* count, uint32_t* span, uint32_t* fire)
+{
+    if (fire != nullptr && *fire == 0u)
+        return;
+    *count = 0u;
+    *span = 0u;
+    if (fire != nullptr)
+        *fire = 0u;
+}
+
+/** plane[perm[s]] = stage[s] over [0, n): back to sample order. */
+template <class T>
+__global__ __launch_bounds__(kThreads) void restoreScatterKernel(const T* __restrict__ stage, T* plane,
+    const int32_t* __restrict__ perm, int64_t n)
+{
+    for (int64_t s = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; s < n; s += int64_t(gridDim.x) * blockDim.x)
+        plane[perm[s]] = stage[s];
+}
+
+__global__ void identityPairKernel(int32_t* perm, int32_t* inv, int64_t n)
+{
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        perm[i] = int32_t(i);
+        inv[i] = int32_t(i);
+    }
+}
+
+/** Opt the place kernel of ``kernel`` into ``bytes`` of dynamic shared memory, once
+ *  per kernel and device (a function attribute, not a stream operation). */
+void allowShared(const void* kernel, size_t bytes)
+{
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaCheck(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({kernel, dev}) != 0)
+        return;
+    cudaCheck(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)),
+        "cudaFuncSetAttribute");
+    done.insert({kernel, dev});
+}
+
+unsigned streamGrid(int64_t n)
+{
+    const int64_t want = (n + kThreads - 1) / kThreads;
+    const int64_t cap = int64_t(smCount()) * 8;
+    return unsigned(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+template <class F>
+void withElem(uint32_t bytes, F&& f)
+{
+    switch (bytes) {
+    case 1: f(uint8_t{}); break;
+    case 2: f(uint16_t{}); break;
+    case 4: f(uint32_t{}); break;
+    case 8: f(uint64_t{}); break;
+    default: f(Elem16{}); break;
+    }
+}
+
+/** The plane table, checked as eagle checks it (Reorder.h checkReorder). */
+std::vector<eagle_backend_reorder_plane> planesOf(const eagle_backend_reorder_desc& d, const char* who,
+    bool needMask)
+{
+    if (d.n_planes > 0 && d.planes == 0)
+        invalid(std::string(who) + ": a null plane table");
+    if (d.n_planes > 4096)
+        invalid(std::string(who) + ": at most 4096 planes");
+    std::vector<eagle_backend_reorder_plane> p(d.n_planes);
+    if (d.n_planes > 0)
+        std::memcpy(p.data(), reinterpret_cast<const void*>(d.planes), d.n_planes * sizeof p[0]);
+    bool maskSeen = false;
+    for (size_t k = 0; k < p.size(); ++k) {
+        const uint32_t e = p[k].elem_bytes;
+        if (e != 1 && e != 2 && e != 4 && e != 8 && e != 16)
+            invalid(std::string(who) + ": plane " + std::to_string(k) + " has " + std::to_string(e)
+                + "-byte elements; supported are 1, 2, 4, 8 and 16");
+        if (d.n > 0 && p[k].data == 0)
+            invalid(std::string(who) + ": plane " + std::to_string(k) + " is null");
+        if (p[k].data % e != 0)
+            invalid(std::string(who) + ": plane " + std::to_string(k) + " is not aligned to its element size");
+        const uint64_t lo = p[k].data, hi = lo + uint64_t(d.n) * e;
+        for (size_t q = 0; q < k; ++q) {
+            const uint64_t qlo = p[q].data, qhi = qlo + uint64_t(d.n) * p[q].elem_bytes;
+            if (d.n > 0 && lo < qhi && qlo < hi)
+                invalid(std::string(who) + ": planes " + std::to_string(q) + " and " + std::to_string(k) + " overlap");
+        }
+        if (p[k].data == d.mask && e == 1)
+            maskSeen = true;
+    }
+    if (needMask && d.n > 0 && !maskSeen)
+        invalid(std::string(who) + ": the mask must be one of the planes (it moves with them)");
+    return p;
+}
+
+uint32_t widestOf(const std::vector<eagle_backend_reorder_plane>& p)
+{
+    uint32_t w = 4;  // perm
+    for (const auto& q : p)
+        w = q.elem_bytes > w ? q.elem_bytes : w;
+    return w;
+}
+
+}  // namespace
+}  // namespace eb
+
+using namespace eb;
+
+EB_API eagle_backend_status eagle_backend_reorder_device(struct eagle_backend_reorder_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_reorder_device";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        if (d.n < 0)
+            invalid(std::string(who) + ": n must be >= 0");
+        if (d.n > INT64_C(2147483647))
+            unsupported(std::string(who) + ": the int32 perm addresses at most 2^31-1 samples, got n = "
+                + std::to_string(d.n));
+        const auto planes = planesOf(d, who, true);
+        const Layout l = layoutFor(d.n, widestOf(planes));
+        if (d.scratch == 0) {
+            constexpr size_t end = offsetof(eagle_backend_reorder_desc, scratch_bytes) + sizeof(int64_t);
+            if (desc->struct_size < end)
+                invalid(std::string(who) + ": the scratch query needs a desc carrying scratch_bytes");
+            desc->scratch_bytes = int64_t(l.total);
+            return;
+        }
+        if (d.count == 0 || d.span == 0 || (d.n > 0 && (d.mask == 0 || d.perm == 0 || d.inv == 0 || d.index_map == 0)))
+            invalid(std::string(who) + ": mask, perm, inv, index_map, count and span must be device addresses");
+        DeviceScope scope(resolveDevice(d.device, d.n > 0 ? d.mask : d.count));
+        const cudaStream_t s = seamStream(d.stream);
+        auto* count = reinterpret_cast<uint32_t*>(d.count);
+        auto* span = reinterpret_cast<uint32_t*>(d.span);
+        auto* fire = reinterpret_cast<uint32_t*>(d.fire);
+        if (d.n == 0) {
+            reorderEmptyKernel<<<1, 1, 0, s>>>(count, span, fire);
+            launchCheck(who);
+            return;
+        }
+        char* base = reinterpret_cast<char*>(d.scratch);
+        ScanArgs a{};
+        a.mask = reinterpret_cast<const uint8_t*>(d.mask);
+        a.n = d.n;
+        a.span = span;
+        a.fire = fire;
+        a.tiles = uint32_t((d.n + kTile - 1) / kTile);
+        a.status = reinterpret_cast<uint64_t*>(base + l.status);
+        a.tileNext = reinterpret_cast<uint32_t*>(base + l.words);
+        a.err = a.tileNext + 1;
+        a.cnt = a.tileNext + 2;
+        a.prefix = reinterpret_cast<uint32_t*>(base + l.prefix);
+        a.bits = reinterpret_cast<uint16_t*>(base + l.bits);
+        cudaCheck(cudaMemsetAsync(base, 0, l.prefix, s), "cudaMemsetAsync");  // status words and counters
+        if (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP)
+            reorderScanKernel<true><<<a.tiles, kThreads, 0, s>>>(a);
+        else
+            reorderScanKernel<false><<<a.tiles, kThreads, 0, s>>>(a);
+        launchCheck(who);
+        PlaceArgs p{};
+        p.stage = base + l.stage;
+        p.bits = a.bits;
+        p.prefix = a.prefix;
+        p.cnt = a.cnt;
+        p.span = span;
+        p.fire = fire;
+        p.err = a.err;
+        p.n = d.n;
+        auto move = [&](uint64_t data, uint32_t elem, bool perm) {
+            withElem(elem, [&](auto tag) {
+                using T = decltype(tag);
+                copySpanKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(data),
+                    reinterpret_cast<T*>(base + l.stage), span, fire, d.n);
+                launchCheck(who);
+                p.plane = reinterpret_cast<void*>(data);
+                const size_t shared = size_t(kTile) * sizeof(T);
+                if (perm) {
+                    p.inv = reinterpret_cast<int32_t*>(d.inv);
+                    p.indexMap = reinterpret_cast<int32_t*>(d.index_map);
+                    allowShared(reinterpret_cast<const void*>(&placeKernel<int32_t, true>), shared);
+                    placeKernel<int32_t, true><<<a.tiles, kThreads, shared, s>>>(p);
+                } else {
+                    allowShared(reinterpret_cast<const void*>(&placeKernel<T, false>), shared);
+                    placeKernel<T, false><<<a.tiles, kThreads, shared, s>>>(p);
+                }
+                launchCheck(who);
+            });
+        };
+        for (const auto& q : planes)
+            move(q.data, q.elem_bytes, false);
+        move(d.perm, 4, true);
+        reorderFinishKernel<<<1, 1, 0, s>>>(a.cnt, a.err, count, span, fire);
+        launchCheck(who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_restore_device(struct eagle_backend_reorder_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_restore_device";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        if (d.n < 0 || d.n > INT64_C(2147483647))
+            invalid(std::string(who) + ": n must lie in [0, 2^31 - 1]");
+        const auto planes = planesOf(d, who, false);
+        const Layout l = layoutFor(d.n, widestOf(planes));
+        if (d.scratch == 0) {
+            constexpr size_t end = offsetof(eagle_backend_reorder_desc, scratch_bytes) + sizeof(int64_t);
+            if (desc->struct_size < end)
+                invalid(std::string(who) + ": the scratch query needs a desc carrying scratch_bytes");
+            desc->scratch_bytes = int64_t(l.total);
+            return;
+        }
+        if (d.n == 0)
+            return;
+        if (d.perm == 0 || d.inv == 0)
+            invalid(std::string(who) + ": perm and inv must be device addresses");
+        DeviceScope scope(resolveDevice(d.device, d.perm));
+        const cudaStream_t s = seamStream(d.stream);
+        char* stage = reinterpret_cast<char*>(d.scratch) + l.stage;
+        const auto* perm = reinterpret_cast<const int32_t*>(d.perm);
+        for (const auto& q : planes) {
+            withElem(q.elem_bytes, [&](auto tag) {
+                using T = decltype(tag);
+                copySpanKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(q.data),
+                    reinterpret_cast<T*>(stage), nullptr, nullptr, d.n);
+                launchCheck(who);
+                restoreScatterKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(stage),
+                    reinterpret_cast<T*>(q.data), perm, d.n);
+                launchCheck(who);
+            });
+        }
+        identityPairKernel<<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<int32_t*>(d.perm),
+            reinterpret_cast<int32_t*>(d.inv), d.n);
+        launchCheck(who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_pointer_residency(int32_t device, uint64_t ptr, int32_t* cls)
+{
+    return guarded([&] {
+        if (cls == nullptr)
+            invalid("eagle_backend_pointer_residency: null output");
+        int dev = device;
+        if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) {
+            (void)cudaGetLastError();
+            *cls = EAGLE_BACKEND_RESIDENCY_PAGEABLE;
+            return;
+        }
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, reinterpret_cast<const void*>(ptr)) != cudaSuccess) {
+            (void)cudaGetLastError();
+            *cls = EAGLE_BACKEND_RESIDENCY_PAGEABLE;
+            return;
+        }
+        switch (at.type) {
+        case cudaMemoryTypeDevice:
+            *cls = at.device == dev ? EAGLE_BACKEND_RESIDENCY_DEVICE : EAGLE_BACKEND_RESIDENCY_OTHER_DEVICE;
+            break;
+        case cudaMemoryTypeManaged: *cls = EAGLE_BACKEND_RESIDENCY_MANAGED; break;
+        case cudaMemoryTypeHost:
+            *cls = at.devicePointer != nullptr ? EAGLE_BACKEND_RESIDENCY_MAPPED_HOST : EAGLE_BACKEND_RESIDENCY_PAGEABLE;
+            break;
+        default: *cls = EAGLE_BACKEND_RESIDENCY_PAGEABLE; break;
+        }
+    });
+}

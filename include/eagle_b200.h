@@ -471,6 +471,27 @@ eagle_backend_status eagle_backend_compact_device(struct eagle_backend_compact_d
 /* eagle_backend.h:826-832: perm, inv and (non-zero) index_map become 0..n-1,
  * *count = *span = n, in one kernel; capture-legal */
 eagle_backend_status eagle_backend_reset_device(struct eagle_backend_reorder_desc* desc);
+/* eagle_backend.h:705-740: permute every plane IN PLACE over [0, *span) so the kept
+ * samples fill [0, *count) in ascending sample order and the dropped ones follow in
+ * ascending order; perm moves with them, inv is rebuilt for the moved slots,
+ * index_map becomes the identity over [0, *count), *span = *count. The mask is one
+ * of the planes. With fire != 0 every kernel returns while *fire == 0 and the last
+ * clears it. Query with scratch == 0 (scratch_bytes). Enqueue only, capturable. */
+eagle_backend_status eagle_backend_reorder_device(struct eagle_backend_reorder_desc* desc);
+/* eagle_backend.h:855-859: undo every reorder since the last restore: each plane back
+ * in sample order, perm and inv the identity (mask, index_map, count, span and fire
+ * are not read). Query with scratch == 0. Enqueue only. */
+eagle_backend_status eagle_backend_x_restore_device(struct eagle_backend_reorder_desc* desc);
+
+/* Residency classes of eagle_backend_pointer_residency (eagle_backend.h:833-839). */
+#define EAGLE_BACKEND_RESIDENCY_HOST 0
+#define EAGLE_BACKEND_RESIDENCY_DEVICE 1
+#define EAGLE_BACKEND_RESIDENCY_MANAGED 2
+#define EAGLE_BACKEND_RESIDENCY_MAPPED_HOST 3
+#define EAGLE_BACKEND_RESIDENCY_PAGEABLE 4
+#define EAGLE_BACKEND_RESIDENCY_OTHER_DEVICE 5
+/* eagle_backend.h:847: classify ``ptr`` as seen from ``device`` (-1: the current one) */
+eagle_backend_status eagle_backend_pointer_residency(int32_t device, uint64_t ptr, int32_t* cls);
 
 /* eagle_backend_x_b200_compact_device_noalloc: compact_device for callers that
  * cannot allocate device memory (no counterpart in the reference: eagle's

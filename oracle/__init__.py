@@ -244,3 +244,36 @@ def lorenz_run(rho, x, y, z, t, h, n_acc, n_rej, terminated, *, max_steps, sigma
     if rc != 0:
         raise ValueError(f"oracle_lorenz_run refused (status {rc})")
     return int(stats[0]), int(stats[1]), int(stats[2])
+
+
+def reorder(planes, mask_plane: int, perm, inv, index_map, span: int, *, drop: bool = True, fire=None):
+    """The physical reorder of eagle/filtering/Reorder.h (reorderDst :171-175; the
+    stage / place / fin kernels :177-430): over slots [0, span) the kept samples move
+    to [0, count) in ascending order and the dropped ones follow in ascending order,
+    every plane (the mask among them, ``planes[mask_plane]``) and ``perm`` in place;
+    ``inv[perm[s]] = s`` for the moved slots; ``index_map[0:count]`` is the identity.
+    With ``fire == 0`` nothing happens. Returns ``(count, span, fire)`` after."""
+    if fire is not None and fire == 0:
+        return None, span, fire
+    n = perm.size
+    sp = min(int(span), n)
+    mask = planes[mask_plane][:sp].copy()
+    keep = (mask == 0) if drop else (mask != 0)
+    order = np.concatenate([np.flatnonzero(keep), np.flatnonzero(~keep)])
+    for p in planes:
+        p[:sp] = p[:sp][order]
+    perm[:sp] = perm[:sp][order]
+    inv[perm[:sp]] = np.arange(sp, dtype=inv.dtype)
+    cnt = int(keep.sum())
+    index_map[:cnt] = np.arange(cnt, dtype=index_map.dtype)
+    return cnt, cnt, (0 if fire is not None else None)
+
+
+def restore(planes, perm, inv):
+    """Reorder.h restoreDevice (:612-629): each plane back in sample order
+    (``plane[perm[s]] = stage[s]``), then ``perm`` and ``inv`` the identity."""
+    for p in planes:
+        stage = p.copy()
+        p[perm] = stage
+    perm[:] = np.arange(perm.size, dtype=perm.dtype)
+    inv[:] = np.arange(inv.size, dtype=inv.dtype)

@@ -157,3 +157,32 @@ def test_last_error_clears_on_success():
     d = _abi.new(_abi.CompactDesc, n=5)
     assert L.eagle_backend_compact_device(ctypes.byref(d)) == _abi.OK
     assert _abi.last_error() == ""
+
+
+def _reorder_desc(n, planes, mask, **kw):
+    tab = (_abi.ReorderPlane * max(1, len(planes)))()
+    for k, (addr, e) in enumerate(planes):
+        tab[k].data, tab[k].elem_bytes = addr, e
+    d = _abi.new(_abi.ReorderDesc, n=n, n_planes=len(planes), planes=ctypes.addressof(tab), mask=mask, **kw)
+    return d, tab
+
+
+def test_reorder_query_and_refusals():
+    L = _abi.lib()
+    d, tab = _reorder_desc(100_000, [(1 << 20, 8), (1 << 30, 1)], 1 << 30)
+    assert L.eagle_backend_reorder_device(ctypes.byref(d)) == _abi.OK
+    assert d.scratch_bytes >= 8 * 100_000  # the stage holds the widest plane
+    d, tab = _reorder_desc(100, [(1 << 20, 3), (1 << 30, 1)], 1 << 30)
+    assert L.eagle_backend_reorder_device(ctypes.byref(d)) == _abi.INVALID_ARGUMENT
+    assert "3-byte" in _abi.last_error()
+    d, tab = _reorder_desc(100, [(1 << 20, 8)], 1 << 30)
+    assert L.eagle_backend_reorder_device(ctypes.byref(d)) == _abi.INVALID_ARGUMENT
+    assert "mask must be one of the planes" in _abi.last_error()
+    d, tab = _reorder_desc(100, [(1 << 20, 8), ((1 << 20) + 8, 8), (1 << 30, 1)], 1 << 30)
+    assert L.eagle_backend_reorder_device(ctypes.byref(d)) == _abi.INVALID_ARGUMENT
+    assert "overlap" in _abi.last_error()
+    d, tab = _reorder_desc(100, [((1 << 20) + 4, 8), (1 << 30, 1)], 1 << 30)
+    assert L.eagle_backend_reorder_device(ctypes.byref(d)) == _abi.INVALID_ARGUMENT
+    assert "aligned" in _abi.last_error()
+    d, tab = _reorder_desc(2 ** 31, [(1 << 20, 8), (1 << 30, 1)], 1 << 30)
+    assert L.eagle_backend_reorder_device(ctypes.byref(d)) == _abi.UNSUPPORTED
