@@ -8,9 +8,9 @@ library and fails loudly (``BackendUnavailable``) when it is not built.
 
 from ._abi import BackendError, BackendUnavailable, BackendUnsupported
 from ._api import (Compactor, CompactSum, Model, Reducer, Runner, RunReport, SimResult, StagedRunner, cell_op,
-                   compact, entry, gambler, lorenz, mask_count, oscillator, reduce, reorder, restore, simulate,
+                   compact, entry, gambler, lorenz, mask_count, oscillator, reduce, reorder, reorder_classes, restore, simulate,
                    until_done)
 
 __all__ = ["BackendError", "BackendUnavailable", "BackendUnsupported", "Compactor", "CompactSum", "Model", "Reducer",
            "Runner", "RunReport", "SimResult", "StagedRunner", "cell_op", "compact", "entry", "gambler", "lorenz",
-           "mask_count", "oscillator", "reduce", "reorder", "restore", "simulate", "until_done"]
+           "mask_count", "oscillator", "reduce", "reorder", "reorder_classes", "restore", "simulate", "until_done"]

@@ -24,6 +24,7 @@ LOOP_UNCAPPED = 0xFFFFFFFF
 
 CELL_BUMP, CELL_MASK_COUNT, CELL_POLICY, CELL_IDENTITY, CELL_COUNT_FIRED, CELL_GROUP_AND, CELL_SCALE_COUNT = range(7)
 COMPACT_MASK_IS_DROP = 1
+CLASSES_WITHIN_LIVE = 2
 REDUCE_F32, REDUCE_F64, REDUCE_I32, REDUCE_I64, REDUCE_U8 = range(5)
 REDUCE_OP_SUM, REDUCE_OP_MAX, REDUCE_OP_ALL, REDUCE_OP_MIN = range(4)
 REDUCE_COMPENSATED, REDUCE_ORDERED, REDUCE_AUTO = range(3)
@@ -133,6 +134,23 @@ class Report(ctypes.Structure):
                 ("report_bytes", _u32), ("reserved0", _u32)]
 
 
+class CompactClassesDesc(ctypes.Structure):
+    _fields_ = [("struct_size", _u32), ("flags", _u32), ("device", _i32), ("reserved", _u32), ("mask", _u64),
+                ("index_map", _u64), ("count", _u64), ("scratch", _u64), ("n", _i64), ("stream", _u64),
+                ("scratch_bytes", _i64), ("live32", _u64), ("span", _u64), ("fire", _u64), ("theta", _f32),
+                ("reserved2", _u32), ("class_plane", _u64), ("classes", _u32), ("class_theta", _f32),
+                ("offsets", _u64), ("mixed32", _u64), ("stale_count", _u64), ("class_fire", _u64),
+                ("reserved3", _u64)]
+
+
+class ReorderClassesDesc(ctypes.Structure):
+    _fields_ = [("struct_size", _u32), ("flags", _u32), ("device", _i32), ("n_planes", _u32), ("planes", _u64),
+                ("mask", _u64), ("perm", _u64), ("inv", _u64), ("index_map", _u64), ("count", _u64),
+                ("span", _u64), ("fire", _u64), ("scratch", _u64), ("n", _i64), ("stream", _u64),
+                ("scratch_bytes", _i64), ("class_plane", _u64), ("classes", _u32), ("reserved3", _u32),
+                ("offsets", _u64), ("class_sorts", _u64)]
+
+
 class CapturerDesc(ctypes.Structure):
     _fields_ = [("struct_size", _u32), ("flags", _u32), ("device", _i32), ("reserved0", _i32), ("stream", _u64)]
 
@@ -180,6 +198,8 @@ SIGNATURES = {
     "eagle_backend_reorder_device": (_i32, [ctypes.POINTER(ReorderDesc)]),
     "eagle_backend_x_restore_device": (_i32, [ctypes.POINTER(ReorderDesc)]),
     "eagle_backend_pointer_residency": (_i32, [_i32, _u64, ctypes.POINTER(_i32)]),
+    "eagle_backend_compact_classes_device": (_i32, [ctypes.POINTER(CompactClassesDesc)]),
+    "eagle_backend_reorder_classes_device": (_i32, [ctypes.POINTER(ReorderClassesDesc)]),
     "eagle_backend_capturer_create": (_i32, [ctypes.POINTER(CapturerDesc), ctypes.POINTER(_P)]),
     "eagle_backend_capturer_begin": (_i32, [_P]),
     "eagle_backend_capturer_end": (_i32, [_P, ctypes.POINTER(_P)]),

@@ -751,3 +751,26 @@ def restore(planes, perm, inv, *, stream=None):
     d.stream = _stream_handle(stream)
     _abi.check(_abi.lib().eagle_backend_x_restore_device(ctypes.byref(d)))
     return scratch
+
+
+def reorder_classes(planes, mask, class_plane, perm, inv, index_map, count, span, offsets, class_sorts, classes: int,
+                    *, fire=None, drop: bool = True, within: bool = False, stream=None):
+    """Stable counting sort of ``planes`` in place by ``(live, class)`` over
+    ``[0, span)`` (dead last), or by class over ``[0, count)`` with ``within``
+    (eagle/filtering/ReorderClasses.h; ``eagle_backend_reorder_classes_device``).
+    ``offsets`` (uint32[classes + 1]) receives each key's first slot; ``class_sorts``
+    counts the sorts that ran. Enqueue only; returns the scratch to keep alive."""
+    torch = _t()
+    tab = _plane_table(planes)
+    flags = (_abi.COMPACT_MASK_IS_DROP if drop else 0) | (_abi.CLASSES_WITHIN_LIVE if within else 0)
+    d = _abi.new(_abi.ReorderClassesDesc, flags=flags, device=perm.device.index, n_planes=len(planes),
+                 planes=ctypes.addressof(tab), mask=_ptr(mask), perm=_ptr(perm), inv=_ptr(inv),
+                 index_map=_ptr(index_map), count=_ptr(count), span=_ptr(span),
+                 fire=_ptr(fire) if fire is not None else 0, n=perm.numel(), class_plane=_ptr(class_plane),
+                 classes=int(classes), offsets=_ptr(offsets), class_sorts=_ptr(class_sorts))
+    _abi.check(_abi.lib().eagle_backend_reorder_classes_device(ctypes.byref(d)))  # query
+    scratch = torch.empty(max(1, int(d.scratch_bytes)), dtype=torch.uint8, device=perm.device)
+    d.scratch = _ptr(scratch)
+    d.stream = _stream_handle(stream)
+    _abi.check(_abi.lib().eagle_backend_reorder_classes_device(ctypes.byref(d)))
+    return scratch

@@ -324,6 +324,107 @@ using namespace eb;
 
 #define EB_API extern "C" __attribute__((visibility("default")))
 
+namespace eb {
+namespace {
+
+/** compact_device's whole enqueue (after the query), shared with the class trigger entry. */
+void enqueueCompactDevice(const eagle_backend_compact_desc& d, const char* who)
+{
+    if (d.count == 0 || (d.n > 0 && (d.mask == 0 || d.index_map == 0)))
+        invalid(std::string(who) + ": mask, index_map and count must be device addresses");
+    const bool trigger = d.live32 != 0;
+    if (trigger) {
+        if (d.span == 0 || d.fire == 0)
+            invalid(std::string(who) + ": a trigger needs live32, span and fire");
+        if (d.reserved2 != 0)
+            invalid(std::string(who) + ": reserved2 must be zero");
+        if (!(d.theta > 0.0f && d.theta < 1.0f))
+            invalid(std::string(who) + ": the trigger's theta must lie in (0, 1)");
+    }
+    const cudaStream_t s = seamStream(d.stream);
+    if (d.n == 0) {
+        compactEmptyKernel<<<1, 1, 0, s>>>(reinterpret_cast<uint32_t*>(d.count),
+            trigger ? reinterpret_cast<uint32_t*>(d.live32) : nullptr,
+            trigger ? reinterpret_cast<uint32_t*>(d.fire) : nullptr);
+        launchCheck(who);
+        return;
+    }
+    const size_t scratchBytes = compactScratchBytes(d.n);
+    CompactArgs a{};
+    a.mask = reinterpret_cast<const uint8_t*>(d.mask);
+    a.n = d.n;
+    a.map = reinterpret_cast<int32_t*>(d.index_map);
+    a.count = reinterpret_cast<uint32_t*>(d.count);
+    a.tiles = uint32_t((d.n + kTile - 1) / kTile);
+    a.status = reinterpret_cast<uint64_t*>(d.scratch);
+    a.tileNext = reinterpret_cast<uint32_t*>(d.scratch + size_t(a.tiles) * sizeof(uint64_t));
+    a.err = a.tileNext + 1;
+    a.live32 = reinterpret_cast<uint32_t*>(d.live32);
+    a.span = reinterpret_cast<const uint32_t*>(d.span);
+    a.fire = reinterpret_cast<uint32_t*>(d.fire);
+    a.theta = d.theta;
+    cudaCheck(cudaMemsetAsync(reinterpret_cast<void*>(d.scratch), 0, scratchBytes, s), "cudaMemsetAsync");
+    const bool aligned = (d.mask & 15u) == 0;
+    const bool drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
+    if (drop)
+        trigger ? launchCompact<true, true>(a, aligned, s) : launchCompact<true, false>(a, aligned, s);
+    else
+        trigger ? launchCompact<false, true>(a, aligned, s) : launchCompact<false, false>(a, aligned, s);
+    launchCheck(who);
+}
+
+/** Per 32-slot group of [0, n): does it hold two or more live classes
+ *  (ReorderClasses.h classMixed32)? One atomic per CTA. */
+__global__ __launch_bounds__(256) void mixed32Kernel(const uint8_t* __restrict__ mask, const uint8_t* __restrict__ cls,
+    uint32_t* mixed32, bool drop, int64_t n)
+{
+    __shared__ uint32_t part[8];
+    uint32_t mine = 0;
+    for (int64_t i0 = int64_t(blockIdx.x) * blockDim.x; i0 < n; i0 += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t i = i0 + threadIdx.x;
+        bool live = false;
+        unsigned c = 0u;
+        if (i < n) {
+            const bool set = mask[i] != 0;
+            live = drop ? !set : set;
+            c = cls[i];
+        }
+        unsigned lo = live ? c : 255u, hi = live ? c : 0u;
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            lo = min(lo, __shfl_xor_sync(kFull, lo, d));
+            hi = max(hi, __shfl_xor_sync(kFull, hi, d));
+        }
+        if ((threadIdx.x & 31u) == 0u && lo < hi)
+            ++mine;
+    }
+    if ((threadIdx.x & 31u) == 0u)
+        part[threadIdx.x >> 5] = mine;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t t = 0;
+        for (int w = 0; w < int(blockDim.x >> 5); ++w)
+            t += part[w];
+        if (t != 0)
+            atomicAdd(mixed32, t);
+    }
+}
+
+/** ReorderClasses.h classTriggerFires: a mixing, a class drift or the liveness trigger. */
+__global__ void classFireKernel(const uint32_t* count, const uint32_t* live32, const uint32_t* span,
+    const uint32_t* mixed32, const uint32_t* stale, const uint32_t* liveFire, float classTheta, uint32_t* classFire)
+{
+    const uint32_t mixed = *mixed32;
+    const bool warpMix = mixed > 0u && double(mixed) >= double(classTheta) * double(*live32) && *span >= 4096u;
+    const bool drift = double(stale != nullptr ? *stale : 0u) > 0.05 * double(*count);
+    *classFire = (warpMix || drift || (liveFire != nullptr && *liveFire != 0u)) ? 1u : 0u;
+}
+
+__global__ void zeroWordKernel(uint32_t* w) { *w = 0u; }
+
+}  // namespace
+}  // namespace eb
+
 EB_API eagle_backend_status eagle_backend_compact_device(struct eagle_backend_compact_desc* desc)
 {
     return guarded([&] {
@@ -341,48 +442,57 @@ EB_API eagle_backend_status eagle_backend_compact_device(struct eagle_backend_co
             desc->scratch_bytes = int64_t(compactScratchBytes(d.n));
             return;
         }
-        if (d.count == 0 || (d.n > 0 && (d.mask == 0 || d.index_map == 0)))
-            invalid(std::string(who) + ": mask, index_map and count must be device addresses");
-        const bool trigger = d.live32 != 0;
-        if (trigger) {
-            if (d.span == 0 || d.fire == 0)
-                invalid(std::string(who) + ": a trigger needs live32, span and fire");
-            if (d.reserved2 != 0)
-                invalid(std::string(who) + ": reserved2 must be zero");
-            if (!(d.theta > 0.0f && d.theta < 1.0f))
-                invalid(std::string(who) + ": the trigger's theta must lie in (0, 1)");
-        }
-        const int dev = resolveDevice(d.device, d.mask != 0 ? d.mask : d.count);
-        DeviceScope scope(dev);
-        const cudaStream_t s = seamStream(d.stream);
-        if (d.n == 0) {
-            compactEmptyKernel<<<1, 1, 0, s>>>(reinterpret_cast<uint32_t*>(d.count),
-                trigger ? reinterpret_cast<uint32_t*>(d.live32) : nullptr,
-                trigger ? reinterpret_cast<uint32_t*>(d.fire) : nullptr);
-            launchCheck(who);
+        DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
+        enqueueCompactDevice(d, who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_compact_classes_device(struct eagle_backend_compact_classes_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_compact_classes_device";
+        if (desc == nullptr)
+            invalid(std::string(who) + ": null desc");
+        constexpr size_t need = offsetof(eagle_backend_compact_classes_desc, reserved3) + sizeof(uint64_t);
+        if (desc->struct_size < need)
+            invalid(std::string(who) + ": the desc must carry the class fields");
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        if (d.n < 0)
+            invalid(std::string(who) + ": n must be >= 0");
+        if (d.n > INT64_C(2147483647))
+            unsupported(std::string(who) + ": the int32 index map addresses at most 2^31-1 samples, got n = "
+                + std::to_string(d.n));
+        if (d.scratch == 0) {
+            desc->scratch_bytes = int64_t(compactScratchBytes(d.n));
             return;
         }
-        const size_t scratchBytes = compactScratchBytes(d.n);
-        CompactArgs a{};
-        a.mask = reinterpret_cast<const uint8_t*>(d.mask);
-        a.n = d.n;
-        a.map = reinterpret_cast<int32_t*>(d.index_map);
-        a.count = reinterpret_cast<uint32_t*>(d.count);
-        a.tiles = uint32_t((d.n + kTile - 1) / kTile);
-        a.status = reinterpret_cast<uint64_t*>(d.scratch);
-        a.tileNext = reinterpret_cast<uint32_t*>(d.scratch + size_t(a.tiles) * sizeof(uint64_t));
-        a.err = a.tileNext + 1;
-        a.live32 = reinterpret_cast<uint32_t*>(d.live32);
-        a.span = reinterpret_cast<const uint32_t*>(d.span);
-        a.fire = reinterpret_cast<uint32_t*>(d.fire);
-        a.theta = d.theta;
-        cudaCheck(cudaMemsetAsync(reinterpret_cast<void*>(d.scratch), 0, scratchBytes, s), "cudaMemsetAsync");
-        const bool aligned = (d.mask & 15u) == 0;
-        const bool drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
-        if (drop)
-            trigger ? launchCompact<true, true>(a, aligned, s) : launchCompact<true, false>(a, aligned, s);
-        else
-            trigger ? launchCompact<false, true>(a, aligned, s) : launchCompact<false, false>(a, aligned, s);
+        if (d.live32 == 0 || d.span == 0 || d.fire == 0 || d.mixed32 == 0 || d.class_fire == 0
+            || (d.n > 0 && d.class_plane == 0))
+            invalid(std::string(who) + ": live32, span, fire, class_plane, mixed32 and class_fire are required");
+        if (d.reserved2 != 0 || d.reserved3 != 0)
+            invalid(std::string(who) + ": reserved fields must be zero");
+        if (d.classes < 2 || d.classes > EAGLE_BACKEND_MAX_CLASSES)
+            invalid(std::string(who) + ": classes must lie in [2, 255]");
+        if (!(d.class_theta > 0.0f && d.class_theta < 1.0f))
+            invalid(std::string(who) + ": class_theta must lie in (0, 1)");
+        DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
+        eagle_backend_compact_desc base{};
+        std::memcpy(&base, &d, sizeof base);  // the first block repeats compact_desc field for field
+        base.struct_size = sizeof base;
+        enqueueCompactDevice(base, who);
+        const cudaStream_t s = seamStream(d.stream);
+        auto* mixed = reinterpret_cast<uint32_t*>(d.mixed32);
+        zeroWordKernel<<<1, 1, 0, s>>>(mixed);
+        if (d.n > 0) {
+            const int64_t blocks = std::min<int64_t>((d.n + 255) / 256, int64_t(smCount()) * 16);
+            mixed32Kernel<<<unsigned(blocks), 256, 0, s>>>(reinterpret_cast<const uint8_t*>(d.mask),
+                reinterpret_cast<const uint8_t*>(d.class_plane), mixed,
+                (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0, d.n);
+        }
+        classFireKernel<<<1, 1, 0, s>>>(reinterpret_cast<const uint32_t*>(d.count),
+            reinterpret_cast<const uint32_t*>(d.live32), reinterpret_cast<const uint32_t*>(d.span), mixed,
+            reinterpret_cast<const uint32_t*>(d.stale_count), reinterpret_cast<const uint32_t*>(d.fire), d.class_theta,
+            reinterpret_cast<uint32_t*>(d.class_fire));
         launchCheck(who);
     });
 }

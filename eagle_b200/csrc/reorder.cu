@@ -329,6 +329,279 @@ uint32_t widestOf(const std::vector<eagle_backend_reorder_plane>& p)
     return w;
 }
 
+
+// ------------------------------------------------------------------ K classes
+//
+// reorder_classes_device (ReorderClasses.h reorderClassesDevice; seam
+// eagle_backend.h:793-824): a stable counting sort of the slots [0, lim) by key,
+// key = class (clamped to K-1) for a live sample and K for a dead one (dead
+// last), or by class alone over the live prefix with CLASSES_WITHIN_LIVE; lim is
+// *span, or *count within the live prefix. A tile of 4096 slots is ranked by its
+// 8 warps, 16 rounds of 32 consecutive slots each: __match_any_sync groups the
+// round's lanes by key, a lane's rank is its peers below it plus its warp's count
+// of that key so far, and a prefix over the warps gives each warp's start per key.
+// The first kernel writes each tile's count per key (key-major) and the slots'
+// keys (the mask and class planes move later); one look-back scan turns the
+// counts into each (key, tile)'s first destination; then every plane is staged
+// and placed (dst = base[key][tile] + warp start + rank).
+
+constexpr int kWarps = kThreads / 32;
+constexpr int kRounds = int(kTile) / kThreads;
+constexpr uint32_t kNoKey = 0x100u;
+
+__device__ __forceinline__ uint32_t classKeyOf(uint8_t m, uint8_t c, bool drop, bool within, uint32_t classes)
+{
+    const uint32_t cc = uint32_t(c) < classes ? uint32_t(c) : classes - 1u;
+    if (within)
+        return cc;
+    const bool set = m != 0;
+    return (drop ? !set : set) ? cc : classes;
+}
+
+struct ClassArgs {
+    const uint8_t* mask;
+    const uint8_t* cls;
+    int64_t n;
+    const uint32_t* lim;
+    const uint32_t* fire;
+    uint32_t classes, nKeys;
+    int drop, within;
+    uint8_t* keys;   // n: each slot's key, kept while the planes move
+    uint32_t* hist;  // nKeys x tiles, key-major: counts, then the first destinations
+    uint32_t tiles;
+};
+
+/** Per-warp counts of each key over the tile's rounds; a lane's ranks come back
+ *  in ``rank`` (its round-r slot's rank among the warp's earlier slots of its key). */
+__device__ __forceinline__ void rankTile(const uint8_t* keys, int64_t tile0, int64_t lim, uint16_t (*cnt)[256],
+    uint32_t (&key)[kRounds], uint32_t (&rank)[kRounds])
+{
+    const unsigned lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+        const int64_t i = tile0 + int64_t(w) * (kRounds * 32) + int64_t(r) * 32 + lane;
+        const uint32_t k = i < lim ? uint32_t(keys[i]) : kNoKey;
+        const unsigned peers = __match_any_sync(kFull, k);
+        const uint32_t below = __popc(peers & ((1u << lane) - 1u));
+        uint32_t base = 0;
+        if (k != kNoKey)
+            base = cnt[w][k];
+        __syncwarp();
+        if (k != kNoKey && below == 0)
+            cnt[w][k] = uint16_t(base + __popc(peers));
+        __syncwarp();
+        key[r] = k;
+        rank[r] = base + below;
+    }
+}
+
+__global__ __launch_bounds__(kThreads) void classHistKernel(ClassArgs a)
+{
+    if (a.fire != nullptr && *a.fire == 0u)
+        return;
+    __shared__ uint16_t cnt[kWarps][256];
+    const int t = int(threadIdx.x);
+    for (int q = t; q < kWarps * 256; q += kThreads)
+        (&cnt[0][0])[q] = 0;
+    __syncthreads();
+    const int64_t lim = spanOf(a.lim, a.n);
+    const int64_t tile0 = int64_t(blockIdx.x) * kTile;
+    const unsigned lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
+    // the keys of the tile's slots, saved for the place kernels
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+        const int64_t i = tile0 + int64_t(w) * (kRounds * 32) + int64_t(r) * 32 + lane;
+        if (i < lim)
+            a.keys[i] = uint8_t(classKeyOf(a.mask[i], a.cls[i], a.drop != 0, a.within != 0, a.classes));
+    }
+    __syncwarp();
+    uint32_t key[kRounds], rank[kRounds];
+    rankTile(a.keys, tile0, lim, cnt, key, rank);
+    __syncthreads();
+    if (uint32_t(t) < a.nKeys) {
+        uint32_t total = 0;
+#pragma unroll
+        for (int q = 0; q < kWarps; ++q)
+            total += cnt[q][t];
+        a.hist[size_t(t) * a.tiles + blockIdx.x] = total;
+    }
+}
+
+struct ScanU32Args {
+    uint32_t* data;  // in: counts; out: exclusive prefixes
+    int64_t m;
+    const uint32_t* fire;
+    uint64_t* status;
+    uint32_t* tileNext;
+    uint32_t* err;
+    uint32_t* total;
+    uint32_t tiles;
+};
+
+/** Exclusive prefix sum of m uint32 counts in place: 16 per thread, CTA scan,
+ *  decoupled look-back over 4096-element tiles. */
+__global__ __launch_bounds__(kThreads) void scanU32Kernel(ScanU32Args a)
+{
+    if (a.fire != nullptr && *a.fire == 0u)
+        return;
+    __shared__ uint32_t sTile;
+    __shared__ uint32_t scan[33];
+    __shared__ uint64_t sPrefix;
+    const int t = int(threadIdx.x);
+    if (t == 0)
+        sTile = atomicAdd(a.tileNext, 1u);
+    __syncthreads();
+    const uint32_t tile = sTile;
+    const int64_t i0 = int64_t(tile) * kTile + int64_t(t) * kPer;
+    uint32_t v[kPer];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        v[j] = i0 + j < a.m ? a.data[i0 + j] : 0u;
+        sum += v[j];
+    }
+    uint32_t total = 0;
+    const uint32_t excl = blockExclusiveSum(sum, total, scan);
+    if (t < 32) {
+        uint64_t prefix = 0;
+        if (tile == 0) {
+            if (t == 0)
+                lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, total);
+        } else {
+            if (t == 0)
+                lbPublish<PlainCodec>(a.status, tile, 0, kLbAggregate, total);
+            prefix = lbExclusivePrefix<PlainCodec>(a.status, tile, 0, a.err);
+            if (t == 0)
+                lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, prefix + total);
+        }
+        if (t == 0) {
+            sPrefix = prefix;
+            if (tile == a.tiles - 1)
+                *a.total = uint32_t(prefix + total);
+        }
+    }
+    __syncthreads();
+    uint32_t run = uint32_t(sPrefix) + excl;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        if (i0 + j < a.m)
+            a.data[i0 + j] = run;
+        run += v[j];
+    }
+}
+
+struct ClassPlaceArgs {
+    const void* stage;
+    void* plane;
+    const uint8_t* keys;
+    const uint32_t* base;  // nKeys x tiles first destinations
+    const uint32_t* lim;
+    const uint32_t* fire;
+    const uint32_t* err;
+    int32_t* inv;  // Perm only
+    int64_t n;
+    uint32_t tiles;
+};
+
+template <class T, bool Perm>
+__global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
+{
+    if (a.fire != nullptr && *a.fire == 0u)
+        return;
+    if (*a.err != 0u)
+        return;
+    __shared__ uint16_t cnt[kWarps][256];
+    const int t = int(threadIdx.x);
+    for (int q = t; q < kWarps * 256; q += kThreads)
+        (&cnt[0][0])[q] = 0;
+    __syncthreads();
+    const int64_t lim = spanOf(a.lim, a.n);
+    const int64_t tile0 = int64_t(blockIdx.x) * kTile;
+    if (tile0 >= lim)
+        return;
+    uint32_t key[kRounds], rank[kRounds];
+    rankTile(a.keys, tile0, lim, cnt, key, rank);
+    __syncthreads();
+    // each warp's first rank per key: the counts of the warps before it
+    if (t < 256) {
+        uint32_t run = 0;
+#pragma unroll
+        for (int q = 0; q < kWarps; ++q) {
+            const uint32_t c = cnt[q][t];
+            cnt[q][t] = uint16_t(run);
+            run += c;
+        }
+    }
+    __syncthreads();
+    const unsigned lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
+    const T* src = static_cast<const T*>(a.stage);
+    T* dst = static_cast<T*>(a.plane);
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+        if (key[r] == kNoKey)
+            continue;
+        const int64_t i = tile0 + int64_t(w) * (kRounds * 32) + int64_t(r) * 32 + lane;
+        const int64_t d = int64_t(a.base[size_t(key[r]) * a.tiles + blockIdx.x]) + cnt[w][key[r]] + rank[r];
+        const T v = src[i];
+        dst[d] = v;
+        if constexpr (Perm)
+            a.inv[static_cast<int32_t>(v)] = int32_t(d);
+    }
+}
+
+__global__ void classIdentityKernel(int32_t* indexMap, const uint32_t* live, const uint32_t* fire, const uint32_t* err)
+{
+    if (fire != nullptr && *fire == 0u)
+        return;
+    if (*err != 0u)
+        return;
+    const int64_t end = int64_t(*live);
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < end; i += int64_t(gridDim.x) * blockDim.x)
+        indexMap[i] = int32_t(i);
+}
+
+__global__ void classFinishKernel(const uint32_t* base, uint32_t tiles, uint32_t nKeys, const uint32_t* total,
+    uint32_t classes, int within, const uint32_t* err, uint32_t* offsets, uint32_t* count, uint32_t* span,
+    uint32_t* fire, uint32_t* classSorts)
+{
+    if (fire != nullptr && *fire == 0u)
+        return;
+    if (*err != 0u) {
+        *count = 0xffffffffu;  // a count above n reports a failed sort
+        return;
+    }
+    for (uint32_t c = 0; c <= classes; ++c)
+        offsets[c] = c < nKeys ? base[size_t(c) * tiles] : *total;
+    if (!within) {
+        const uint32_t live = base[size_t(classes) * tiles];  // the dead key's first slot
+        *count = live;
+        *span = live;
+    }
+    if (fire != nullptr)
+        *fire = 0u;
+    *classSorts += 1u;
+}
+
+struct ClassLayout {
+    size_t keys, hist, status, words, stage, total;
+};
+
+ClassLayout classLayoutFor(int64_t n, uint32_t elem, uint32_t classes)
+{
+    const size_t m = size_t(n > 0 ? n : 1);
+    const size_t tiles = (m + size_t(kTile) - 1) / size_t(kTile);
+    const size_t histN = size_t(classes + 1) * tiles;
+    const size_t scanTiles = (histN + size_t(kTile) - 1) / size_t(kTile);
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    ClassLayout l{};
+    l.keys = 0;
+    l.hist = up(m);
+    l.status = up(l.hist + histN * sizeof(uint32_t));
+    l.words = up(l.status + scanTiles * sizeof(uint64_t));
+    l.stage = l.words + 256;
+    l.total = up(l.stage + m * (elem > 4 ? elem : 4));
+    return l;
+}
 }  // namespace
 }  // namespace eb
 
@@ -417,6 +690,124 @@ EB_API eagle_backend_status eagle_backend_reorder_device(struct eagle_backend_re
             move(q.data, q.elem_bytes, false);
         move(d.perm, 4, true);
         reorderFinishKernel<<<1, 1, 0, s>>>(a.cnt, a.err, count, span, fire);
+        launchCheck(who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_reorder_classes_device(struct eagle_backend_reorder_classes_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_reorder_classes_device";
+        if (desc == nullptr)
+            invalid(std::string(who) + ": null desc");
+        constexpr size_t need = offsetof(eagle_backend_reorder_classes_desc, class_sorts) + sizeof(uint64_t);
+        if (desc->struct_size < need)
+            invalid(std::string(who) + ": the desc must carry the class fields");
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP | EAGLE_BACKEND_CLASSES_WITHIN_LIVE, who);
+        if (d.classes < 2 || d.classes > EAGLE_BACKEND_MAX_CLASSES)
+            invalid(std::string(who) + ": classes must lie in [2, 255]");
+        if (d.reserved3 != 0)
+            invalid(std::string(who) + ": reserved3 must be zero");
+        if (d.n < 0)
+            invalid(std::string(who) + ": n must be >= 0");
+        if (d.n > INT64_C(2147483647))
+            unsupported(std::string(who) + ": the int32 perm addresses at most 2^31-1 samples, got n = "
+                + std::to_string(d.n));
+        eagle_backend_reorder_desc base{};
+        std::memcpy(&base, &d, sizeof base);
+        const auto planes = planesOf(base, who, true);
+        bool classSeen = false;
+        for (const auto& q : planes)
+            classSeen = classSeen || (q.data == d.class_plane && q.elem_bytes == 1);
+        if (d.n > 0 && !classSeen)
+            invalid(std::string(who) + ": the class plane must be one of the planes (it moves with them)");
+        const ClassLayout l = classLayoutFor(d.n, widestOf(planes), d.classes);
+        if (d.scratch == 0) {
+            desc->scratch_bytes = int64_t(l.total);
+            return;
+        }
+        if (d.n > 0
+            && (d.mask == 0 || d.perm == 0 || d.inv == 0 || d.index_map == 0 || d.count == 0 || d.span == 0
+                || d.class_plane == 0 || d.offsets == 0 || d.class_sorts == 0))
+            invalid(std::string(who) + ": mask, perm, inv, index_map, count, span, class_plane, offsets and "
+                                       "class_sorts must be device addresses");
+        DeviceScope scope(resolveDevice(d.device, d.n > 0 ? d.mask : d.count));
+        const cudaStream_t s = seamStream(d.stream);
+        auto* count = reinterpret_cast<uint32_t*>(d.count);
+        auto* span = reinterpret_cast<uint32_t*>(d.span);
+        auto* fire = reinterpret_cast<uint32_t*>(d.fire);
+        if (d.n == 0) {
+            reorderEmptyKernel<<<1, 1, 0, s>>>(count, span, fire);
+            launchCheck(who);
+            return;
+        }
+        const bool within = (d.flags & EAGLE_BACKEND_CLASSES_WITHIN_LIVE) != 0;
+        const uint32_t* lim = within ? count : span;
+        char* raw = reinterpret_cast<char*>(d.scratch);
+        ClassArgs c{};
+        c.mask = reinterpret_cast<const uint8_t*>(d.mask);
+        c.cls = reinterpret_cast<const uint8_t*>(d.class_plane);
+        c.n = d.n;
+        c.lim = lim;
+        c.fire = fire;
+        c.classes = d.classes;
+        c.nKeys = within ? d.classes : d.classes + 1;
+        c.drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
+        c.within = within;
+        c.keys = reinterpret_cast<uint8_t*>(raw + l.keys);
+        c.hist = reinterpret_cast<uint32_t*>(raw + l.hist);
+        c.tiles = uint32_t((d.n + kTile - 1) / kTile);
+        ScanU32Args sa{};
+        sa.data = c.hist;
+        sa.m = int64_t(c.nKeys) * c.tiles;
+        sa.fire = fire;
+        sa.status = reinterpret_cast<uint64_t*>(raw + l.status);
+        sa.tileNext = reinterpret_cast<uint32_t*>(raw + l.words);
+        sa.err = sa.tileNext + 1;
+        sa.total = sa.tileNext + 2;
+        sa.tiles = uint32_t((sa.m + kTile - 1) / kTile);
+        cudaCheck(cudaMemsetAsync(raw + l.status, 0, l.stage - l.status, s), "cudaMemsetAsync");
+        // tiles past lim still write zero counts, so the whole count matrix is defined
+        cudaCheck(cudaMemsetAsync(c.hist, 0, size_t(sa.m) * sizeof(uint32_t), s), "cudaMemsetAsync");
+        classHistKernel<<<c.tiles, kThreads, 0, s>>>(c);
+        launchCheck(who);
+        scanU32Kernel<<<sa.tiles, kThreads, 0, s>>>(sa);
+        launchCheck(who);
+        ClassPlaceArgs p{};
+        p.stage = raw + l.stage;
+        p.keys = c.keys;
+        p.base = c.hist;
+        p.lim = lim;
+        p.fire = fire;
+        p.err = sa.err;
+        p.n = d.n;
+        p.tiles = c.tiles;
+        auto move = [&](uint64_t data, uint32_t elem, bool perm) {
+            withElem(elem, [&](auto tag) {
+                using T = decltype(tag);
+                copySpanKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(data),
+                    reinterpret_cast<T*>(raw + l.stage), lim, fire, d.n);
+                launchCheck(who);
+                p.plane = reinterpret_cast<void*>(data);
+                if (perm) {
+                    p.inv = reinterpret_cast<int32_t*>(d.inv);
+                    classPlaceKernel<int32_t, true><<<c.tiles, kThreads, 0, s>>>(p);
+                } else {
+                    classPlaceKernel<T, false><<<c.tiles, kThreads, 0, s>>>(p);
+                }
+                launchCheck(who);
+            });
+        };
+        for (const auto& q : planes)
+            move(q.data, q.elem_bytes, false);
+        move(d.perm, 4, true);
+        // the live count: *count within the live prefix, else the dead key's first slot
+        const uint32_t* live = within ? count : c.hist + size_t(d.classes) * c.tiles;
+        classIdentityKernel<<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<int32_t*>(d.index_map), live, fire,
+            sa.err);
+        launchCheck(who);
+        classFinishKernel<<<1, 1, 0, s>>>(c.hist, c.tiles, c.nKeys, sa.total, d.classes, within ? 1 : 0, sa.err,
+            reinterpret_cast<uint32_t*>(d.offsets), count, span, fire, reinterpret_cast<uint32_t*>(d.class_sorts));
         launchCheck(who);
     });
 }

@@ -483,6 +483,76 @@ eagle_backend_status eagle_backend_reorder_device(struct eagle_backend_reorder_d
  * are not read). Query with scratch == 0. Enqueue only. */
 eagle_backend_status eagle_backend_x_restore_device(struct eagle_backend_reorder_desc* desc);
 
+/* ---- filtering: K classes (eagle_backend.h:742-824) ---------------------------- */
+
+/* reorder_classes flags: sort [0, *count) by class only (the live prefix) */
+#define EAGLE_BACKEND_CLASSES_WITHIN_LIVE (UINT32_C(1) << 1)
+#define EAGLE_BACKEND_MAX_CLASSES 255
+
+/* eagle_backend.h:755-781: compact_device plus the K-class trigger; live32, span and
+ * fire are required here */
+struct eagle_backend_compact_classes_desc {
+    uint32_t struct_size;
+    uint32_t flags;
+    int32_t device;
+    uint32_t reserved;
+    uint64_t mask;
+    uint64_t index_map;
+    uint64_t count;
+    uint64_t scratch;
+    int64_t n;
+    uint64_t stream;
+    int64_t scratch_bytes;
+    uint64_t live32;
+    uint64_t span;
+    uint64_t fire;
+    float theta;
+    uint32_t reserved2;
+    uint64_t class_plane;   /* uint8_t[n], each sample's class in [0, classes) */
+    uint32_t classes;       /* K, in [2, 255] */
+    float class_theta;      /* the mixed-group threshold, in (0, 1) */
+    uint64_t offsets;       /* not written here */
+    uint64_t mixed32;       /* uint32_t[1]: OUT, 32-slot groups holding two or more live classes */
+    uint64_t stale_count;   /* uint32_t[1]: IN, samples whose class changed since the last sort; 0 = none */
+    uint64_t class_fire;    /* uint32_t[1]: OUT, (mixed32 > 0 && mixed32 >= class_theta * live32 &&
+                             * span >= 4096) || stale_count > 0.05 * count || fire */
+    uint64_t reserved3;
+};
+
+/* eagle_backend.h:787: compaction with the class trigger (query and capture as compact_device) */
+eagle_backend_status eagle_backend_compact_classes_device(struct eagle_backend_compact_classes_desc* desc);
+
+/* eagle_backend.h:792-812: reorder_device generalised to K classes */
+struct eagle_backend_reorder_classes_desc {
+    uint32_t struct_size;
+    uint32_t flags;         /* COMPACT_MASK_IS_DROP | CLASSES_WITHIN_LIVE */
+    int32_t device;
+    uint32_t n_planes;
+    uint64_t planes;
+    uint64_t mask;
+    uint64_t perm;
+    uint64_t inv;
+    uint64_t index_map;
+    uint64_t count;
+    uint64_t span;
+    uint64_t fire;
+    uint64_t scratch;
+    int64_t n;
+    uint64_t stream;
+    int64_t scratch_bytes;
+    uint64_t class_plane;   /* uint8_t[n], one of the planes */
+    uint32_t classes;       /* K, in [2, 255] */
+    uint32_t reserved3;
+    uint64_t offsets;       /* uint32_t[classes + 1]: OUT, exclusive prefix over the live samples */
+    uint64_t class_sorts;   /* uint32_t[1]: incremented once when the permutation ran */
+};
+
+/* eagle_backend.h:814-824: permute every plane IN PLACE by a stable counting sort on
+ * (live, class) over [0, *span) (dead last), then *count = *span = live; with
+ * CLASSES_WITHIN_LIVE over [0, *count) by class only. perm moves, inv is rebuilt,
+ * index_map is the identity over [0, live), offsets is written. */
+eagle_backend_status eagle_backend_reorder_classes_device(struct eagle_backend_reorder_classes_desc* desc);
+
 /* Residency classes of eagle_backend_pointer_residency (eagle_backend.h:833-839). */
 #define EAGLE_BACKEND_RESIDENCY_HOST 0
 #define EAGLE_BACKEND_RESIDENCY_DEVICE 1

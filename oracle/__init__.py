@@ -277,3 +277,58 @@ def restore(planes, perm, inv):
         p[perm] = stage
     perm[:] = np.arange(perm.size, dtype=perm.dtype)
     inv[:] = np.arange(inv.size, dtype=inv.dtype)
+
+
+def class_key(mask, cls, classes: int, *, drop: bool = True, within: bool = False):
+    """ReorderClasses.h classKey (:58-67): the class clamped to K-1; with ``within``
+    that alone, else K for a dead sample (dead sorts last)."""
+    cc = np.minimum(cls.astype(np.int64), classes - 1)
+    if within:
+        return cc
+    live = (mask == 0) if drop else (mask != 0)
+    return np.where(live, cc, classes)
+
+
+def reorder_classes(planes, mask_plane: int, class_plane: int, perm, inv, index_map, count: int, span: int,
+                    classes: int, *, drop: bool = True, within: bool = False, fire=None):
+    """ReorderClasses.h reorderClassesHost (:303-360): a stable counting sort of slots
+    [0, lim) by key (lim = count within the live prefix, else span), every plane and
+    perm in place; inv rebuilt for the moved slots; index_map the identity over the
+    live samples; offsets[0..K] the keys' first slots. Returns
+    ``(offsets, count, span, fire, sorted)``."""
+    if fire is not None and fire == 0:
+        return None, count, span, fire, False
+    n = perm.size
+    lim = min(int(count if within else span), n)
+    key = class_key(planes[mask_plane][:lim], planes[class_plane][:lim], classes, drop=drop, within=within)
+    order = np.argsort(key, kind="stable")
+    nkeys = classes if within else classes + 1
+    counts = np.bincount(key, minlength=nkeys)
+    off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+    for p in planes:
+        p[:lim] = p[:lim][order]
+    perm[:lim] = perm[:lim][order]
+    inv[perm[:lim]] = np.arange(lim, dtype=inv.dtype)
+    live = int(count) if within else int(off[classes])
+    index_map[:live] = np.arange(live, dtype=index_map.dtype)
+    offsets = off[:classes + 1].copy()
+    if not within:
+        count = span = live
+    return offsets, count, span, (0 if fire is not None else None), True
+
+
+def class_trigger(mask, cls, *, drop: bool, live32: int, span: int, count: int, live_fire: int, class_theta: float,
+                  stale: int = 0):
+    """ReorderClasses.h classTriggerHost (:262-281) and classTriggerFires (:46-52):
+    ``mixed32`` = 32-slot groups of [0, n) holding two or more live classes, and the
+    class trigger."""
+    n = mask.size
+    live = (mask == 0) if drop else (mask != 0)
+    mixed = 0
+    for g in range(0, n, 32):
+        c = cls[g:g + 32][live[g:g + 32]]
+        if c.size and c.min() < c.max():
+            mixed += 1
+    warp_mix = mixed > 0 and float(mixed) >= float(np.float32(class_theta)) * float(live32) and span >= 4096
+    drift = float(stale) > 0.05 * float(count)
+    return mixed, int(warp_mix or drift or live_fire != 0)

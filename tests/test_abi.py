@@ -66,6 +66,8 @@ _LAYOUTS = {
     "eagle_backend_fork_desc": _abi.ForkDesc,
     "eagle_backend_conditional_desc": _abi.ConditionalDesc,
     "eagle_backend_graph_desc": _abi.GraphDesc,
+    "eagle_backend_compact_classes_desc": _abi.CompactClassesDesc,
+    "eagle_backend_reorder_classes_desc": _abi.ReorderClassesDesc,
 }
 
 
