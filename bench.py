@@ -48,10 +48,10 @@ def _args():
     p.add_argument("--impl", default="engine", choices=("engine", "reference"))
     p.add_argument("--mode", default="auto", choices=("auto", "band", "band_eager", "persist", "fused"))
     p.add_argument("--n", type=int, default=None, help="samples per GPU (default: the workload's)")
-    p.add_argument("--workload", default="oscillator", choices=("oscillator", "lorenz", "gambler", "compact_sum"),
+    p.add_argument("--workload", default="oscillator", choices=("oscillator", "lorenz", "gambler", "compact_sum", "reorder"),
                    help="oscillator: the headline 16M heterogeneous-stop run; the others time the other "
                         "configurations' kernels (Lorenz RKF7(8) 2^22, gambler's ruin 2^26, compact-then-sum "
-                        "2^28) for their own lines")
+                        "2^28, the physical reorder and the K-class sort of 2^24) for their own lines")
     p.add_argument("--no-fma", action="store_true", help="exact (uncontracted) arithmetic profile")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-chunks", type=int, default=16)
@@ -551,6 +551,75 @@ def side_workload(args):
                      "cpu_baseline": {"value": total / sec, "unit": "sample-steps/s", "cores": cores, "kind": "port",
                                       "sample": f"the first {m} samples run to absorption ({total} steps, {sec:.2f} s)"},
                      "gpu_launches": 4 * args.steps, "clocks": clocks.summary()})
+    elif args.workload == "reorder":
+        n = args.n or (1 << 24)
+        g = np.random.default_rng(11)
+        names = ("omega", "t_end", "x", "v", "t")
+        planes = [torch.from_numpy(g.standard_normal(n)).to(dev) for _ in names]
+        mask0 = torch.from_numpy((g.random(n) < 0.5).astype(np.uint8)).to(dev)
+        cls0 = torch.from_numpy(g.integers(0, 8, n).astype(np.uint8)).to(dev)
+        mask, cls = mask0.clone(), cls0.clone()
+        perm = torch.arange(n, dtype=torch.int32, device=dev)
+        inv = perm.clone()
+        im = torch.zeros(n, dtype=torch.int32, device=dev)
+        cells = torch.zeros(8, dtype=torch.int32, device=dev)
+        offsets = torch.zeros(9, dtype=torch.int32, device=dev)
+        count, span, sorts = cells[0:1], cells[1:2], cells[2:3]
+        every = planes + [mask, cls]
+
+        def reset():
+            eb.restore(every, perm, inv)
+            span.fill_(n)
+
+        times = {"reorder": [], "classes": []}
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with _Clocks(0) as clocks:
+            for step in range(args.warmup + args.steps):
+                for kind in ("reorder", "classes"):
+                    reset()
+                    torch.cuda.synchronize()
+                    e0.record(stream)
+                    if kind == "reorder":
+                        keep = eb.reorder(every, mask, perm, inv, im, count, span, stream=stream)
+                    else:
+                        keep = eb.reorder_classes(every, mask, cls, perm, inv, im, count, span, offsets, sorts, 8,
+                                                  stream=stream)
+                    e1.record(stream)
+                    torch.cuda.synchronize()
+                    if step >= args.warmup:
+                        times[kind].append(e0.elapsed_time(e1))
+                    del keep
+        ms = {k: statistics.median(v) for k, v in times.items()}
+        # the in-place minimum: every moved plane read once and written once, the mask (and the class plane)
+        # read for the keys, perm read and written, inv and index_map written
+        moved = 5 * 8 + 1 + 1
+        alg = {"reorder": n * (2 * moved + 1 + 8 + 4 + 4 * 0.5),
+               "classes": n * (2 * moved + 2 + 8 + 4 + 4 * 0.5)}
+        peak, peak_kind = _peaks()
+        rate = {k: alg[k] / (ms[k] / 1e3) / 1e9 for k in ms}
+        m = min(n, 1 << 22)
+        hp = [p[:m].cpu().numpy().copy() for p in planes] + [mask0[:m].cpu().numpy().copy(),
+                                                            cls0[:m].cpu().numpy().copy()]
+        hperm, hinv, him = np.arange(m, dtype=np.int32), np.arange(m, dtype=np.int32), np.zeros(m, np.int32)
+        t0 = time.perf_counter()
+        oracle.reorder(hp, 5, hperm, hinv, him, m)
+        sec = time.perf_counter() - t0
+        line.update({"metric": "GB/s, 2^24-slot physical reorder (5 f64 planes + mask + class plane) vs HBM",
+                     "value": rate["reorder"], "unit": "GB/s", "ms_per_step": ms["reorder"] + ms["classes"],
+                     "dtype": "f64 planes, u8 mask and class, int32 perm",
+                     "config": {"workload": "physical-reorder", "n": n, "p_keep": 0.5, "classes": 8,
+                                "reorder_ms": ms["reorder"], "class_sort_ms": ms["classes"],
+                                "class_sort_GBps": rate["classes"],
+                                "l2": "7 planes of 16-128 MiB, restored to sample order before every timed call"},
+                     "roofline": {"bound": "hbm", "achieved": rate["reorder"], "peak": peak, "unit": "GB/s",
+                                  "frac": rate["reorder"] / peak, "traffic": None, "peak_kind": peak_kind,
+                                  "basis": "the in-place minimum: each moved plane read and written once, the keys "
+                                           "read, perm read and written, inv and index_map written; the stage copy "
+                                           "that makes the move in place doubles the plane traffic by design"},
+                     "cpu_baseline": {"value": m * (2 * moved + 13) / sec / 1e9, "unit": "GB/s", "cores": 1,
+                                      "kind": "port", "sample": f"the first {m} slots, numpy stable partition "
+                                                                f"({sec:.2f} s)"},
+                     "gpu_launches": (2 + 2 * 8 + 1) + (3 + 2 * 8 + 2), "clocks": clocks.summary()})
     else:
         n = args.n or (1 << 28)
         rng = np.random.default_rng(4)
