@@ -102,7 +102,7 @@ __global__ __launch_bounds__(256) void oscillatorRange(EB_OSC_ROLES(TEnd<Spread>
  *  lane runs up to ``chunk`` steps of its sample per head, within the budget; a
  *  lane whose sample ends mid-chunk waits, masked, for the next head. */
 template <bool Fma, bool Spread>
-__global__ __launch_bounds__(256) void oscillatorPersist(EB_OSC_ROLES(TEnd<Spread>), uint32_t* hawkNext,
+__global__ __launch_bounds__(256, 4) void oscillatorPersist(EB_OSC_ROLES(TEnd<Spread>), uint32_t* hawkNext,
     unsigned long long* hawkUtil, uint32_t* hawkSteps, unsigned long long* hawkStepsum, uint32_t hawkChunk)
 {
     (void)nSamples;
