@@ -175,24 +175,29 @@ __global__ __launch_bounds__(kThreads) void placeKernel(PlaceArgs a)
     if (tile0 >= sp)
         return;  // the whole CTA: nothing of this tile moves
     const int64_t len = sp - tile0 < kTile ? sp - tile0 : kTile;
+    __shared__ uint16_t sKeep[kThreads];
+    __shared__ uint32_t sExcl[kThreads];
     const uint32_t keep = a.bits[size_t(tile) * kThreads + size_t(t)];
     uint32_t kept = 0;
     const uint32_t excl = blockExclusiveSum(uint32_t(__popc(keep)), kept, scan);
+    sKeep[t] = uint16_t(keep);
+    sExcl[t] = excl;
+    __syncthreads();
     const int64_t pre = int64_t(a.prefix[tile]);  // kept slots before the tile
     const int64_t cnt = int64_t(*a.cnt);
     const T* src = static_cast<const T*>(a.stage);
-    // tile-local places: kept ones at [0, kept), dropped ones at [kept, len)
-    uint32_t k = excl;
-    uint32_t dpos = kept + uint32_t(t * kPer) - excl;  // dropped before this thread's run
-#pragma unroll
+    // element e of the tile is the (e % 16)-th of thread e / 16's keep bits: read the
+    // stage coalesced (lane-consecutive e) and put each element at its tile-local place,
+    // the kept ones at [0, kept), the dropped ones at [kept, len)
+#pragma unroll 4
     for (int j = 0; j < kPer; ++j) {
-        const int64_t i = tile0 + int64_t(t) * kPer + j;
-        if (i < sp) {
-            const T v = src[i];
-            if ((keep >> j) & 1u)
-                out[k++] = v;
-            else
-                out[dpos++] = v;
+        const int e = t + j * kThreads;
+        if (int64_t(e) < len) {
+            const T v = src[tile0 + e];
+            const uint32_t kb = sKeep[e >> 4], bit = uint32_t(e & 15);
+            const uint32_t before = sExcl[e >> 4] + __popc(kb & ((1u << bit) - 1u));  // kept before e
+            const uint32_t pos = ((kb >> bit) & 1u) ? before : kept + uint32_t(e) - before;
+            out[pos] = v;
         }
     }
     __syncthreads();
@@ -371,10 +376,11 @@ struct ClassArgs {
     uint32_t tiles;
 };
 
-/** Per-warp counts of each key over the tile's rounds; a lane's ranks come back
- *  in ``rank`` (its round-r slot's rank among the warp's earlier slots of its key). */
+/** Per-warp counts of each key over the tile's rounds; a lane's round-r slot comes
+ *  back in ``kr[r]`` as key << 16 | its rank among the warp's earlier slots of that
+ *  key (kNoKey past lim). */
 __device__ __forceinline__ void rankTile(const uint8_t* keys, int64_t tile0, int64_t lim, uint16_t (*cnt)[256],
-    uint32_t (&key)[kRounds], uint32_t (&rank)[kRounds])
+    uint32_t (&kr)[kRounds])
 {
     const unsigned lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
 #pragma unroll
@@ -390,8 +396,7 @@ __device__ __forceinline__ void rankTile(const uint8_t* keys, int64_t tile0, int
         if (k != kNoKey && below == 0)
             cnt[w][k] = uint16_t(base + __popc(peers));
         __syncwarp();
-        key[r] = k;
-        rank[r] = base + below;
+        kr[r] = (k << 16) | (base + below);
     }
 }
 
@@ -415,8 +420,8 @@ __global__ __launch_bounds__(kThreads) void classHistKernel(ClassArgs a)
             a.keys[i] = uint8_t(classKeyOf(a.mask[i], a.cls[i], a.drop != 0, a.within != 0, a.classes));
     }
     __syncwarp();
-    uint32_t key[kRounds], rank[kRounds];
-    rankTile(a.keys, tile0, lim, cnt, key, rank);
+    uint32_t kr[kRounds];
+    rankTile(a.keys, tile0, lim, cnt, kr);
     __syncthreads();
     if (uint32_t(t) < a.nKeys) {
         uint32_t total = 0;
@@ -510,7 +515,12 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
         return;
     if (*a.err != 0u)
         return;
+    extern __shared__ __align__(16) unsigned char smem[];
+    T* out = reinterpret_cast<T*>(smem);                               // the tile in key order
+    uint8_t* outKey = reinterpret_cast<uint8_t*>(smem + kTile * sizeof(T));  // each place's key
     __shared__ uint16_t cnt[kWarps][256];
+    __shared__ uint32_t sStart[256];
+    __shared__ uint32_t scan[33];
     const int t = int(threadIdx.x);
     for (int q = t; q < kWarps * 256; q += kThreads)
         (&cnt[0][0])[q] = 0;
@@ -519,30 +529,41 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
     const int64_t tile0 = int64_t(blockIdx.x) * kTile;
     if (tile0 >= lim)
         return;
-    uint32_t key[kRounds], rank[kRounds];
-    rankTile(a.keys, tile0, lim, cnt, key, rank);
+    const int64_t len = lim - tile0 < kTile ? lim - tile0 : kTile;
+    uint32_t kr[kRounds];
+    rankTile(a.keys, tile0, lim, cnt, kr);
     __syncthreads();
-    // each warp's first rank per key: the counts of the warps before it
-    if (t < 256) {
-        uint32_t run = 0;
+    // each warp's first rank per key (the counts of the warps before it), and the
+    // tile's count of each key
+    uint32_t total = 0;
 #pragma unroll
-        for (int q = 0; q < kWarps; ++q) {
-            const uint32_t c = cnt[q][t];
-            cnt[q][t] = uint16_t(run);
-            run += c;
-        }
+    for (int q = 0; q < kWarps; ++q) {
+        const uint32_t c = cnt[q][t];
+        cnt[q][t] = uint16_t(total);
+        total += c;
     }
+    uint32_t all = 0;
+    sStart[t] = blockExclusiveSum(total, all, scan);  // the key's first place in the tile
     __syncthreads();
     const unsigned lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
     const T* src = static_cast<const T*>(a.stage);
-    T* dst = static_cast<T*>(a.plane);
 #pragma unroll
     for (int r = 0; r < kRounds; ++r) {
-        if (key[r] == kNoKey)
+        const uint32_t k = kr[r] >> 16;
+        if (k == kNoKey)
             continue;
         const int64_t i = tile0 + int64_t(w) * (kRounds * 32) + int64_t(r) * 32 + lane;
-        const int64_t d = int64_t(a.base[size_t(key[r]) * a.tiles + blockIdx.x]) + cnt[w][key[r]] + rank[r];
-        const T v = src[i];
+        const uint32_t pos = sStart[k] + cnt[w][k] + (kr[r] & 0xffffu);
+        out[pos] = src[i];
+        outKey[pos] = uint8_t(k);
+    }
+    __syncthreads();
+    // each key's run of the tile is contiguous in the plane: coalesced stores
+    T* dst = static_cast<T*>(a.plane);
+    for (int q = t; q < int(len); q += kThreads) {
+        const uint32_t k = outKey[q];
+        const int64_t d = int64_t(a.base[size_t(k) * a.tiles + blockIdx.x]) + (q - int64_t(sStart[k]));
+        const T v = out[q];
         dst[d] = v;
         if constexpr (Perm)
             a.inv[static_cast<int32_t>(v)] = int32_t(d);
@@ -789,11 +810,14 @@ EB_API eagle_backend_status eagle_backend_reorder_classes_device(struct eagle_ba
                     reinterpret_cast<T*>(raw + l.stage), lim, fire, d.n);
                 launchCheck(who);
                 p.plane = reinterpret_cast<void*>(data);
+                const size_t shared = size_t(kTile) * (sizeof(T) + 1);
                 if (perm) {
                     p.inv = reinterpret_cast<int32_t*>(d.inv);
-                    classPlaceKernel<int32_t, true><<<c.tiles, kThreads, 0, s>>>(p);
+                    allowShared(reinterpret_cast<const void*>(&classPlaceKernel<int32_t, true>), shared);
+                    classPlaceKernel<int32_t, true><<<c.tiles, kThreads, shared, s>>>(p);
                 } else {
-                    classPlaceKernel<T, false><<<c.tiles, kThreads, 0, s>>>(p);
+                    allowShared(reinterpret_cast<const void*>(&classPlaceKernel<T, false>), shared);
+                    classPlaceKernel<T, false><<<c.tiles, kThreads, shared, s>>>(p);
                 }
                 launchCheck(who);
             });
