@@ -5,9 +5,9 @@
 // indices, ascending; count; optionally the reorder trigger (live32, fire) of
 // Compact.h:113-118. Eagle runs predicate -> multi-level int64 scan -> scatter
 // (about 2 log256(n) + 2 launches over 8-byte planes). Here it is ONE kernel
-// after a memset of its scratch: each CTA takes the next 4096-sample tile off a
+// after a memset of its scratch: each CTA takes the next 16384-sample tile off a
 // counter (so every tile it waits on is already owned by a running CTA), turns
-// 16 mask bytes per thread into a keep bit-set, scans the counts across the CTA,
+// 4 x 16 mask bytes per thread into keep bit-sets, scans the counts across the CTA,
 // finds the tile's global offset by a decoupled look-back over the earlier
 // tiles' status words, stages the kept indices in shared memory and writes them
 // with coalesced stores. The trigger's live32 rides in the same status words, so
@@ -20,8 +20,10 @@ namespace eb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kPer = 16;
-constexpr int64_t kTile = int64_t(kThreads) * kPer;
+constexpr int kRows = 4;                               // a tile is four rows of 4096 samples
+constexpr int64_t kRow = int64_t(kThreads) * 16;       // 16 mask bytes per thread per row
+constexpr int64_t kTile = kRow * kRows;                // 16384 samples per CTA
+constexpr uint32_t kStage = uint32_t(kRow);            // one row's kept indices at most
 
 struct CompactArgs {
     const uint8_t* mask;
@@ -41,53 +43,83 @@ struct CompactArgs {
     uint32_t elemBytes;  // Gather: 4 or 8
 };
 
-/** Keep bits of 16 consecutive mask bytes starting at sample ``i0``. */
+/** Bits of the non-zero bytes among the 16 in ``w`` (bit j: byte j). */
+__device__ __forceinline__ uint32_t nonZero16(uint4 w)
+{
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    uint32_t set = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t nz = __vcmpne4(words[q], 0u);  // 0xff per non-zero byte
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+            set |= ((nz >> (8 * b)) & 1u) << (4 * q + b);
+    }
+    return set;
+}
+
+/** Keep bits of the 16 mask bytes of samples [i0, i0 + 16): one 16-byte load when
+ *  the run is whole and the mask 16-byte aligned. */
 template <bool Drop, bool Aligned>
-__device__ __forceinline__ uint32_t keepBits(const uint8_t* __restrict__ mask, int64_t i0, int64_t n)
+__device__ __forceinline__ uint32_t keepBits16(const uint8_t* __restrict__ mask, int64_t i0, int64_t n)
 {
     uint32_t set = 0;  // bit j: mask byte i0 + j is non-zero
-    if (Aligned && i0 + kPer <= n) {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(mask + i0));
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const uint32_t nz = __vcmpne4(words[q], 0u);  // 0xff per non-zero byte
-#pragma unroll
-            for (int b = 0; b < 4; ++b)
-                set |= ((nz >> (8 * b)) & 1u) << (4 * q + b);
-        }
+    if (Aligned && i0 + 16 <= n) {
+        set = nonZero16(__ldg(reinterpret_cast<const uint4*>(mask + i0)));
     } else {
 #pragma unroll
-        for (int j = 0; j < kPer; ++j)
+        for (int j = 0; j < 16; ++j)
             if (i0 + j < n && mask[i0 + j] != 0)
                 set |= 1u << j;
     }
-    const uint32_t valid = i0 >= n ? 0u : (i0 + kPer <= n ? 0xffffu : ((1u << uint32_t(n - i0)) - 1u));
+    const uint32_t valid = i0 >= n ? 0u : (i0 + 16 <= n ? 0xffffu : ((1u << uint32_t(n - i0)) - 1u));
     return (Drop ? ~set : set) & valid;
 }
 
+/** One 16384-sample tile per CTA, as four rows of 4096: thread t holds the 16
+ *  mask bytes at t * 16 of every row (four coalesced 16-byte loads). One CTA scan
+ *  of the four rows' counts packed as 16-bit lanes of a 64-bit word gives each
+ *  thread's place in every row, one decoupled look-back the tile's offset; each
+ *  row's kept indices then go through shared memory to coalesced stores (the
+ *  Gather values are read through the staged indices at the store). Four rows per
+ *  look-back keep four times the bytes in flight per round trip, which is what a
+ *  sparse mask (few kept, so little else to do) is bound by. */
 template <bool Drop, bool Trigger, bool Aligned, bool Gather = false>
 __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
 {
     __shared__ uint32_t sTile;
+    __shared__ uint64_t scan64[33];
     __shared__ uint32_t scan[33];
     __shared__ uint64_t sPrefix;
-    __shared__ int32_t stage[kTile];
+    __shared__ int32_t stage[kStage];
     const int t = int(threadIdx.x);
     if (t == 0)
         sTile = atomicAdd(a.tileNext, 1u);
     __syncthreads();
     const uint32_t tile = sTile;
-    const int64_t i0 = int64_t(tile) * kTile + int64_t(t) * kPer;
-    const uint32_t bits = keepBits<Drop, Aligned>(a.mask, i0, a.n);
-    const uint32_t cnt = __popc(bits);
+    const int64_t tile0 = int64_t(tile) * kTile;
+    uint32_t bits[kRows];
+    uint64_t packed = 0;  // row q's count in bits [16q, 16q + 16)
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+        bits[q] = keepBits16<Drop, Aligned>(a.mask, tile0 + int64_t(q) * kRow + int64_t(t) * 16, a.n);
+        packed |= uint64_t(__popc(bits[q])) << (16 * q);
+    }
+    uint64_t rowTotals = 0;
+    const uint64_t excl = blockExclusiveSum(packed, rowTotals, scan64);
     uint32_t total = 0;
-    const uint32_t excl = blockExclusiveSum(cnt, total, scan);
+#pragma unroll
+    for (int q = 0; q < kRows; ++q)
+        total += uint32_t(rowTotals >> (16 * q)) & 0xffffu;
     uint32_t groups = 0;
     if constexpr (Trigger) {
-        // a 32-sample group is two neighbouring threads (tiles start on a multiple of 32)
-        const uint32_t pair = bits | __shfl_xor_sync(kFull, bits, 1);
-        const uint32_t mine = ((t & 1) == 0 && pair != 0) ? 1u : 0u;
+        // a 32-sample group is two neighbouring threads of a row (rows start on a multiple of 32)
+        uint32_t mine = 0;
+#pragma unroll
+        for (int q = 0; q < kRows; ++q) {
+            const uint32_t pair = bits[q] | __shfl_xor_sync(kFull, bits[q], 1);
+            mine += ((t & 1) == 0 && pair != 0) ? 1u : 0u;
+        }
         blockExclusiveSum(mine, groups, scan);
     }
     const uint64_t payload = (uint64_t(groups) << 32) | uint64_t(total);
@@ -106,34 +138,47 @@ __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
         if (t == 0)
             sPrefix = prefix;
     }
-    // stage the kept indices of the tile in order
-    uint32_t k = excl;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j)
-        if ((bits >> j) & 1u)
-            stage[k++] = int32_t(i0 + j);
     __syncthreads();
     const uint64_t prefix = sPrefix;
-    const uint32_t at = uint32_t(prefix);
-    if (a.map != nullptr)
-        for (uint32_t q = uint32_t(t); q < total; q += kThreads)
-            a.map[size_t(at) + q] = stage[q];
-    if constexpr (Gather) {
-        // the kept samples' values, in sample order, next to the map
-        if (a.elemBytes == 8) {
-            const uint64_t* src = static_cast<const uint64_t*>(a.values);
-            uint64_t* dst = static_cast<uint64_t*>(a.outValues);
-            for (uint32_t q = uint32_t(t); q < total; q += kThreads)
-                dst[size_t(at) + q] = src[stage[q]];
-        } else {
-            const uint32_t* src = static_cast<const uint32_t*>(a.values);
-            uint32_t* dst = static_cast<uint32_t*>(a.outValues);
-            for (uint32_t q = uint32_t(t); q < total; q += kThreads)
-                dst[size_t(at) + q] = src[stage[q]];
+    // the rows' kept indices gather in shared memory in output order; they are written
+    // out whenever the next row would not fit (a sparse tile: once; a dense one: per row)
+    uint32_t flushAt = uint32_t(prefix);  // the output index of stage[0]
+    uint32_t fill = 0;                    // staged so far (uniform across the CTA)
+    auto flush = [&]() {
+        __syncthreads();
+        for (uint32_t r = uint32_t(t); r < fill; r += kThreads) {
+            const int32_t idx = stage[r];
+            const size_t out = size_t(flushAt) + r;
+            if (a.map != nullptr)
+                a.map[out] = idx;
+            if constexpr (Gather) {
+                if (a.elemBytes == 8)
+                    static_cast<uint64_t*>(a.outValues)[out] = static_cast<const uint64_t*>(a.values)[idx];
+                else
+                    static_cast<uint32_t*>(a.outValues)[out] = static_cast<const uint32_t*>(a.values)[idx];
+            }
         }
+        __syncthreads();
+        flushAt += fill;
+        fill = 0;
+    };
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+        const uint32_t rowTotal = uint32_t(rowTotals >> (16 * q)) & 0xffffu;
+        if (fill + rowTotal > kStage)
+            flush();
+        uint32_t k = fill + (uint32_t(excl >> (16 * q)) & 0xffffu);
+        const int64_t i0 = tile0 + int64_t(q) * kRow + int64_t(t) * 16;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if ((bits[q] >> j) & 1u)
+                stage[k++] = int32_t(i0 + j);
+        fill += rowTotal;
     }
+    if (fill != 0)
+        flush();
     if (tile == a.tiles - 1 && t == 0) {
-        const uint32_t c = at + total;
+        const uint32_t c = uint32_t(prefix) + total;
         const bool broken = *a.err != 0u;
         *a.count = broken ? 0xffffffffu : c;  // a count above n reports a failed compaction
         if constexpr (Trigger) {

@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
 
-SIZES = (0, 1, 7, 31, 32, 33, 256, 257, 4095, 4096, 4097, 100_003, (1 << 20) + 37, 1 << 24)
+SIZES = (0, 1, 7, 31, 32, 33, 63, 64, 65, 256, 257, 4095, 4096, 4097, 16383, 16384, 16385, 100_003, (1 << 20) + 37,
+         1 << 24)
 
 
 def _mask(n, seed, p):
