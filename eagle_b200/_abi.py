@@ -19,6 +19,8 @@ OK, ERROR, INVALID_ARGUMENT, INDEX, INTEROP, UNAVAILABLE, CALLBACK_FAILED, BAD_H
 CAP_STREAM, CAP_EXEC, CAP_DEVICE, CAP_FILTERING = 1 << 0, 1 << 9, 1 << 10, 1 << 12
 CAP_CAPTURER, CAP_CAPTURED, CAP_FORK, CAP_CONDITIONAL, CAP_ATTRIBUTION, CAP_GRAPH, CAP_LAUNCHER = (1 << k for k in range(1, 8))
 CAP_CONDITIONAL_IF_ELSE, CAP_CONDITIONAL_SWITCH = 1 << 13, 1 << 14
+CAP_INTEROP = 1 << 11
+STREAM_NONE = -(1 << 63)
 COND_IF, COND_IF_ELSE, COND_WHILE, COND_SWITCH = 1, 2, 3, 4
 LOOP_UNCAPPED = 0xFFFFFFFF
 
@@ -195,6 +197,11 @@ SIGNATURES = {
     "eagle_backend_stream_ptr": (_i32, [_P, ctypes.POINTER(_u64)]),
     "eagle_backend_stream_synchronize": (_i32, [_P]),
     "eagle_backend_stream_release": (None, [_P]),
+    "eagle_backend_fence": (_i32, [_i32, _i32, _i64, _i64]),
+    "eagle_backend_event_pool_created": (_i32, [ctypes.POINTER(_i64)]),
+    "eagle_backend_host_alloc": (_i32, [_u64, ctypes.POINTER(_u64)]),
+    "eagle_backend_host_free": (_i32, [_u64]),
+    "eagle_backend_host_func": (_i32, [_u64, _P, _P]),
     "eagle_backend_reorder_device": (_i32, [ctypes.POINTER(ReorderDesc)]),
     "eagle_backend_x_restore_device": (_i32, [ctypes.POINTER(ReorderDesc)]),
     "eagle_backend_pointer_residency": (_i32, [_i32, _u64, ctypes.POINTER(_i32)]),

@@ -417,7 +417,7 @@ class StagedRunner:
     side by side keep the tails of one chunk under the work of the others."""
 
     def __init__(self, model: Model, *, max_steps: int, chunks: int = 16, streams: int = 4, ctas_per_sm: int = 1,
-                 terminated=None, device=None, **kwargs):
+                 full_tail: int = 2, terminated=None, device=None, **kwargs):
         torch = _t()
         per_sample = {k: v for k, v in kwargs.items() if isinstance(v, torch.Tensor) and v.is_cuda and v.dim() == 1}
         if not per_sample:
@@ -434,10 +434,12 @@ class StagedRunner:
         bounds = [n * k // chunks for k in range(chunks + 1)]
         self.bounds = list(zip(bounds[:-1], bounds[1:]))
         self.runners = []
-        for lo, hi in self.bounds:
-            sub = {k: (v[lo:hi] if k in per_sample else v) for k, v in kwargs.items()}
+        for k, (lo, hi) in enumerate(self.bounds):
+            sub = {key: (v[lo:hi] if key in per_sample else v) for key, v in kwargs.items()}
+            # the last ``full_tail`` chunks run alone at the end: let them fill the GPU
+            cps = 0 if k >= len(self.bounds) - int(full_tail) else ctas_per_sm
             self.runners.append(Runner(model, max_steps=max_steps, terminated=terminated[lo:hi], device=self.device,
-                                       ctas_per_sm=ctas_per_sm, **sub))
+                                       ctas_per_sm=cps, **sub))
         self.mode = self.runners[0].mode
         self.copy_stream = torch.cuda.Stream(self.device)
         self.streams = [torch.cuda.Stream(self.device) for _ in range(max(1, int(streams)))]

@@ -4,6 +4,7 @@
 #include "common.cuh"
 
 #include <mutex>
+#include <unordered_map>
 #include <vector>
 
 namespace eb {
@@ -160,7 +161,7 @@ EB_API eagle_backend_status eagle_backend_capabilities(uint64_t* groups)
         *groups = EAGLE_BACKEND_CAP_STREAM | EAGLE_BACKEND_CAP_CAPTURER | EAGLE_BACKEND_CAP_CAPTURED
             | EAGLE_BACKEND_CAP_FORK | EAGLE_BACKEND_CAP_CONDITIONAL | EAGLE_BACKEND_CAP_ATTRIBUTION
             | EAGLE_BACKEND_CAP_GRAPH | EAGLE_BACKEND_CAP_LAUNCHER | EAGLE_BACKEND_CAP_EXEC | EAGLE_BACKEND_CAP_DEVICE
-            | EAGLE_BACKEND_CAP_FILTERING;
+            | EAGLE_BACKEND_CAP_INTEROP | EAGLE_BACKEND_CAP_FILTERING;
         // IF/ELSE and SWITCH nodes exist from driver 12.8 on: the driver's version is their capability.
         int v = 0;
         if (cudaDriverGetVersion(&v) == cudaSuccess && v >= 12080)
@@ -402,6 +403,145 @@ EB_API eagle_backend_status eagle_backend_memcpy(uint64_t dst, uint64_t src, uin
         cudaCheck(cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes, k,
                       seamStream(stream)),
             "cudaMemcpyAsync");
+    });
+}
+
+// ---- interop (bit 11): the DLPack stream fence and host memory ---------------------
+
+namespace {
+
+constexpr int64_t kStreamNone = INT64_MIN;  // no stream argument given: the type's default
+constexpr int32_t kDLCUDA = 2;
+
+/** A DLPack ``__dlpack__(stream=)`` value of a CUDA buffer: 1 the legacy default
+ *  stream, 2 the per-thread default, -1 no ordering, 0 refused, else a raw stream
+ *  (python/src/seam/eagle_backend.h:90-93). ``order`` is false for -1. */
+struct DlStream {
+    bool order;
+    cudaStream_t s;
+    int64_t code;
+};
+
+DlStream dlStream(int64_t code, const char* who)
+{
+    if (code == kStreamNone)
+        code = 1;
+    if (code == 0)
+        invalid(std::string(who) + ": stream 0 is ambiguous and refused by DLPack; pass 1 for the legacy default "
+                                   "stream or 2 for the per-thread default stream");
+    if (code == -1)
+        return DlStream{false, nullptr, code};
+    if (code < -1)
+        invalid(std::string(who) + ": a stream must be -1, 1, 2 or a stream handle, got " + std::to_string(code));
+    cudaStream_t s = code == 1 ? cudaStreamLegacy
+        : code == 2            ? cudaStreamPerThread
+                               : reinterpret_cast<cudaStream_t>(code);
+    return DlStream{true, s, code};
+}
+
+/** Timing-free events reused per device; never destroyed (the process may outlive
+ *  its contexts' teardown order). */
+struct FenceEvents {
+    std::mutex mu;
+    std::unordered_map<int, std::vector<cudaEvent_t>> free;
+    int64_t created = 0;
+
+    cudaEvent_t acquire(int device)
+    {
+        {
+            std::lock_guard<std::mutex> lock(mu);
+            auto& f = free[device];
+            if (!f.empty()) {
+                cudaEvent_t e = f.back();
+                f.pop_back();
+                return e;
+            }
+            ++created;
+        }
+        cudaEvent_t e = nullptr;
+        cudaCheck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreateWithFlags");
+        return e;
+    }
+    void release(int device, cudaEvent_t e)
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        free[device].push_back(e);
+    }
+};
+
+FenceEvents& fenceEvents()
+{
+    static FenceEvents* pool = new FenceEvents();
+    return *pool;
+}
+
+}  // namespace
+
+EB_API eagle_backend_status eagle_backend_fence(int32_t dl_device_type, int32_t device_id, int64_t producer,
+    int64_t consumer)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_fence";
+        if (dl_device_type != kDLCUDA)
+            unsupported(std::string(who) + ": this backend serves DLPack device type 2 (CUDA), not "
+                + std::to_string(dl_device_type));
+        const DlStream p = dlStream(producer, who), c = dlStream(consumer, who);
+        if (!p.order || !c.order || p.code == c.code)
+            return;  // no ordering asked for, or one stream orders itself
+        requireDevice();
+        const int dev = resolveDevice(device_id, 0);
+        DeviceScope scope(dev);
+        FenceEvents& pool = fenceEvents();
+        cudaEvent_t e = pool.acquire(dev);
+        const cudaError_t rec = cudaEventRecord(e, p.s);
+        const cudaError_t wait = rec == cudaSuccess ? cudaStreamWaitEvent(c.s, e, 0) : rec;
+        pool.release(dev, e);  // a recorded event may be recorded again: the wait keeps its own snapshot
+        cudaCheck(rec, "cudaEventRecord");
+        cudaCheck(wait, "cudaStreamWaitEvent");
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_event_pool_created(int64_t* count)
+{
+    return guarded([&] {
+        if (count == nullptr)
+            invalid("eagle_backend_event_pool_created: null output");
+        FenceEvents& pool = fenceEvents();
+        std::lock_guard<std::mutex> lock(pool.mu);
+        *count = pool.created;
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_host_alloc(uint64_t bytes, uint64_t* out)
+{
+    return guarded([&] {
+        if (out == nullptr)
+            invalid("eagle_backend_host_alloc: null output");
+        *out = 0;
+        if (bytes == 0)
+            return;
+        requireDevice();
+        void* p = nullptr;
+        cudaCheck(cudaHostAlloc(&p, size_t(bytes), cudaHostAllocPortable), "cudaHostAlloc");
+        *out = reinterpret_cast<uint64_t>(p);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_host_free(uint64_t ptr)
+{
+    return guarded([&] {
+        if (ptr != 0)
+            cudaCheck(cudaFreeHost(reinterpret_cast<void*>(ptr)), "cudaFreeHost");
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_host_func(uint64_t stream, void (*fn)(void*), void* arg)
+{
+    return guarded([&] {
+        if (fn == nullptr)
+            invalid("eagle_backend_host_func: null function");
+        requireDevice();
+        cudaCheck(cudaLaunchHostFunc(seamStream(stream), fn, arg), "cudaLaunchHostFunc");
     });
 }
 

@@ -52,6 +52,7 @@ typedef int32_t eagle_backend_status;
 #define EAGLE_BACKEND_CAP_LAUNCHER (UINT64_C(1) << 7)
 #define EAGLE_BACKEND_CAP_EXEC (UINT64_C(1) << 9)
 #define EAGLE_BACKEND_CAP_DEVICE (UINT64_C(1) << 10)
+#define EAGLE_BACKEND_CAP_INTEROP (UINT64_C(1) << 11)
 #define EAGLE_BACKEND_CAP_FILTERING (UINT64_C(1) << 12)
 #define EAGLE_BACKEND_CAP_CONDITIONAL_IF_ELSE (UINT64_C(1) << 13)
 #define EAGLE_BACKEND_CAP_CONDITIONAL_SWITCH (UINT64_C(1) << 14)
@@ -413,6 +414,23 @@ eagle_backend_status eagle_backend_run_device(const struct eagle_backend_launch_
 /* ---- device (bit 10; eagle_backend.h:393) -------------------------------------- */
 
 eagle_backend_status eagle_backend_device_props(int32_t device, struct eagle_backend_device_props* props);
+
+/* ---- interop (bit 11; eagle_backend.h:396-440) --------------------------------- */
+
+/* eagle_backend.h:150: "no stream given" in a fence stream argument */
+#define EAGLE_BACKEND_STREAM_NONE INT64_MIN
+/* eagle_backend.h:399: order everything queued on ``producer`` before what is queued
+ * later on ``consumer`` (DLPack stream codes: 1 legacy default, 2 per-thread default,
+ * -1 no ordering, 0 refused, else a raw stream), without blocking the host */
+eagle_backend_status eagle_backend_fence(int32_t dl_device_type, int32_t device_id, int64_t producer, int64_t consumer);
+/* eagle_backend.h:400: events the fence pool has created */
+eagle_backend_status eagle_backend_event_pool_created(int64_t* count);
+/* eagle_backend.h:429-433: page-locked host memory the device can DMA from (0 for 0 bytes) */
+eagle_backend_status eagle_backend_host_alloc(uint64_t bytes, uint64_t* out);
+eagle_backend_status eagle_backend_host_free(uint64_t ptr);
+/* eagle_backend.h:438-440: call fn(arg) once the work enqueued before it on ``stream``
+ * is done; capture-legal (a host node); fn must not call the backend */
+eagle_backend_status eagle_backend_host_func(uint64_t stream, void (*fn)(void*), void* arg);
 
 /* ---- memory, per symbol (eagle_backend.h:405-424) ------------------------------ */
 

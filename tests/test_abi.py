@@ -34,7 +34,7 @@ def test_library_loads_and_reports_its_version():
     assert L.eagle_backend_capabilities(ctypes.byref(groups)) == _abi.OK
     base = (_abi.CAP_STREAM | _abi.CAP_CAPTURER | _abi.CAP_CAPTURED | _abi.CAP_FORK | _abi.CAP_CONDITIONAL
             | _abi.CAP_ATTRIBUTION | _abi.CAP_GRAPH | _abi.CAP_LAUNCHER | _abi.CAP_EXEC | _abi.CAP_DEVICE
-            | _abi.CAP_FILTERING)
+            | _abi.CAP_INTEROP | _abi.CAP_FILTERING)
     arms = _abi.CAP_CONDITIONAL_IF_ELSE | _abi.CAP_CONDITIONAL_SWITCH
     assert groups.value & ~arms == base  # the arm kinds follow the driver's version
     info = _abi.new(_abi.BuildInfo)
@@ -188,3 +188,17 @@ def test_reorder_query_and_refusals():
     assert "aligned" in _abi.last_error()
     d, tab = _reorder_desc(2 ** 31, [(1 << 20, 8), (1 << 30, 1)], 1 << 30)
     assert L.eagle_backend_reorder_device(ctypes.byref(d)) == _abi.UNSUPPORTED
+
+
+def test_fence_refusals_need_no_device():
+    L = _abi.lib()
+    assert L.eagle_backend_fence(1, 0, 1, 2) == _abi.UNSUPPORTED  # a CPU buffer has no CUDA fence
+    assert L.eagle_backend_fence(2, 0, 0, 2) == _abi.INVALID_ARGUMENT  # stream 0 is refused by DLPack
+    assert "ambiguous" in _abi.last_error()
+    assert L.eagle_backend_fence(2, 0, -5, 2) == _abi.INVALID_ARGUMENT
+    assert L.eagle_backend_fence(2, 0, -1, 2) == _abi.OK  # no ordering asked for
+    assert L.eagle_backend_fence(2, 0, 2, 2) == _abi.OK   # one stream orders itself
+    assert L.eagle_backend_fence(2, 0, _abi.STREAM_NONE, 1) == _abi.OK  # none given: the legacy default
+    out = ctypes.c_uint64(7)
+    assert L.eagle_backend_host_alloc(0, ctypes.byref(out)) == _abi.OK and out.value == 0
+    assert L.eagle_backend_host_free(0) == _abi.OK
