@@ -32,6 +32,7 @@ REDUCE_OP_SUM, REDUCE_OP_MAX, REDUCE_OP_ALL, REDUCE_OP_MIN = range(4)
 REDUCE_COMPENSATED, REDUCE_ORDERED, REDUCE_AUTO = range(3)
 REDUCE_PAIR_OUT = 1
 COPY_H2D, COPY_D2H, COPY_D2D, COPY_H2H = range(4)
+MEM_DEVICE, MEM_PINNED = 0, 1
 
 MODEL_OSCILLATOR, MODEL_OSCILLATOR_SPREAD, MODEL_GAMBLER, MODEL_LORENZ = 0, 1, 2, 3
 MODE_BAND, MODE_PERSIST, MODE_FUSED, MODE_BAND_EAGER = 0, 1, 2, 3
@@ -197,6 +198,16 @@ SIGNATURES = {
     "eagle_backend_stream_ptr": (_i32, [_P, ctypes.POINTER(_u64)]),
     "eagle_backend_stream_synchronize": (_i32, [_P]),
     "eagle_backend_stream_release": (None, [_P]),
+    "eagle_backend_module_load": (_i32, [_P, _u64, _i32, ctypes.POINTER(_u64)]),
+    "eagle_backend_module_load_jit": (_i32, [_P, _u64, _i32, _u32, ctypes.POINTER(_u64)]),
+    "eagle_backend_link_ptx": (_i32, [_P, _u64, _i32, _u32, _P, _u64, ctypes.POINTER(_u64)]),
+    "eagle_backend_module_function": (_i32, [_u64, ctypes.c_char_p, ctypes.POINTER(_u64)]),
+    "eagle_backend_module_release": (None, [_u64, _i32]),
+    "eagle_backend_memcpy_strided": (_i32, [_u64, _u64, _u64, _u64, _u64, _u64, _i32, _u64]),
+    "eagle_backend_mem_alloc": (_i32, [_i32, _i32, _u64, _u64, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
+    "eagle_backend_mem_release": (None, [_u64]),
+    "eagle_backend_mem_drain": (_i32, [ctypes.POINTER(_i64)]),
+    "eagle_backend_pointer_device": (_i32, [_u64, ctypes.POINTER(_i32)]),
     "eagle_backend_fence": (_i32, [_i32, _i32, _i64, _i64]),
     "eagle_backend_event_pool_created": (_i32, [ctypes.POINTER(_i64)]),
     "eagle_backend_host_alloc": (_i32, [_u64, ctypes.POINTER(_u64)]),

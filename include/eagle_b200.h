@@ -460,6 +460,36 @@ eagle_backend_status eagle_backend_launch_status(int32_t device);
 eagle_backend_status eagle_backend_device_synchronize(int32_t device);
 /* eagle_backend.h:455 */
 eagle_backend_status eagle_backend_stream_is_capturing(uint64_t stream, int32_t* capturing);
+/* eagle_backend.h:461: load a cubin, fatbin or PTX image in the primary context of
+ * ``device`` (-1: the current one) -- how a hawk artifact's kernels arrive */
+eagle_backend_status eagle_backend_module_load(const void* image, uint64_t bytes, int32_t device, uint64_t* module);
+/* eagle_backend.h:464: module_load of PTX under a cap of max_registers per thread (0: none) */
+eagle_backend_status eagle_backend_module_load_jit(const void* image, uint64_t bytes, int32_t device,
+    uint32_t max_registers, uint64_t* module);
+/* eagle_backend.h:469: link PTX for ``device`` and copy the cubin to ``out`` (null: size only) */
+eagle_backend_status eagle_backend_link_ptx(const void* image, uint64_t bytes, int32_t device, uint32_t max_registers,
+    void* out, uint64_t capacity, uint64_t* size);
+/* eagle_backend.h:473: the function ``name`` of ``module`` (INDEX when absent) */
+eagle_backend_status eagle_backend_module_function(uint64_t module, const char* name, uint64_t* function);
+/* eagle_backend.h:475 */
+void eagle_backend_module_release(uint64_t module, int32_t device);
+/* eagle_backend.h:622: cudaMemcpy2DAsync of ``height`` rows of ``width_bytes`` (not H2H) */
+eagle_backend_status eagle_backend_memcpy_strided(uint64_t dst, uint64_t dst_pitch, uint64_t src, uint64_t src_pitch,
+    uint64_t width_bytes, uint64_t height, int32_t kind, uint64_t stream);
+
+/* eagle_backend.h:627-644: stream-ordered memory (eagle's array layer) */
+#define EAGLE_BACKEND_MEM_DEVICE 0
+#define EAGLE_BACKEND_MEM_PINNED 1
+/* a device allocation is stream-ordered on ``stream`` and 256-byte aligned; refused
+ * while the stream is capturing; bytes == 0 gives null ptr and chunk */
+eagle_backend_status eagle_backend_mem_alloc(int32_t kind, int32_t device, uint64_t bytes, uint64_t stream,
+    uint64_t* chunk, uint64_t* ptr);
+/* stream-ordered free; deferred while the allocation stream is capturing */
+void eagle_backend_mem_release(uint64_t chunk);
+/* run the deferred frees; ``*left`` (may be null) = frees still queued */
+eagle_backend_status eagle_backend_mem_drain(int64_t* left);
+/* the device of the allocation holding ``ptr`` (-1: host or unknown) */
+eagle_backend_status eagle_backend_pointer_device(uint64_t ptr, int32_t* device);
 /* eagle_backend.h:478: one CUfunction attribute (cuFuncGetAttribute codes) */
 eagle_backend_status eagle_backend_function_attribute(uint64_t function, int32_t attribute, int32_t* value);
 /* eagle_backend.h:495: cuLaunchKernel of desc->function; enqueue only, capture-legal */
