@@ -198,6 +198,7 @@ SIGNATURES = {
     "eagle_backend_stream_ptr": (_i32, [_P, ctypes.POINTER(_u64)]),
     "eagle_backend_stream_synchronize": (_i32, [_P]),
     "eagle_backend_stream_release": (None, [_P]),
+    "eagle_backend_x_b200_leaf_partials": (_i32, [_u64, _i64, _u64, _u64]),
     "eagle_backend_module_load": (_i32, [_P, _u64, _i32, ctypes.POINTER(_u64)]),
     "eagle_backend_module_load_jit": (_i32, [_P, _u64, _i32, _u32, ctypes.POINTER(_u64)]),
     "eagle_backend_link_ptx": (_i32, [_P, _u64, _i32, _u32, _P, _u64, ctypes.POINTER(_u64)]),

@@ -694,6 +694,12 @@ class CompactSum:
         r.in_, r.out, r.work_a, r.work_b = _ptr(self.kept), _ptr(self.out), _ptr(self.work_a), _ptr(self.work_b)
         self.rdesc = r
 
+    def gather(self, stream=None):
+        """Enqueue the compaction alone: the kept values in ``kept``, their count in ``count``."""
+        self.cdesc.stream = _stream_handle(stream)
+        _abi.check(_abi.lib().eagle_backend_x_b200_compact_gather(ctypes.byref(self.cdesc), _ptr(self.values),
+                                                                   _ptr(self.kept), 8))
+
     def __call__(self, stream=None):
         s = _stream_handle(stream)
         self.cdesc.stream = s

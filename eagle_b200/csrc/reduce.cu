@@ -374,6 +374,23 @@ __global__ __launch_bounds__(kSlots) void combinePairsKernel(const double* __res
     }
 }
 
+/** Every leaf's (hi, comp) partial of a float64 sum, leaf order, one CTA per leaf
+ *  (the last leaf over the remainder): the leaves of the canonical tree
+ *  (canonical.h:340-353), for callers that join leaves from several places. */
+__global__ __launch_bounds__(kSlots) void leafPartialsKernel(const double* __restrict__ in, int64_t n,
+    double* __restrict__ out)
+{
+    __shared__ CompP<double> s[kSlots];
+    const int64_t l = blockIdx.x;
+    const int64_t base = l * kLeaf;
+    const int64_t cnt = n - base < kLeaf ? n - base : kLeaf;
+    const CompP<double> p = leafPartial<CompP<double>, double, false>(in, nullptr, 1, 0, base, cnt, s);
+    if (threadIdx.x == 0) {
+        out[2 * l] = p.h;
+        out[2 * l + 1] = p.c;
+    }
+}
+
 // ------------------------------------------------------------------- host side
 
 int64_t leafCount(int64_t rows) { return (rows + kLeaf - 1) / kLeaf; }
@@ -631,5 +648,26 @@ extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_bac
         case EAGLE_BACKEND_REDUCE_I32: enqueueCounted<PlainP<int32_t, SumOp<int32_t>>, int32_t>(d, cnt, 0, stream); break;
         default: enqueueCounted<PlainP<int64_t, SumOp<int64_t>>, int64_t>(d, cnt, 0, stream);
         }
+    });
+}
+
+extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_backend_x_b200_leaf_partials(
+    uint64_t in, int64_t n, uint64_t out, uint64_t stream)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_leaf_partials";
+        if (n < 0)
+            invalid(std::string(who) + ": n must be >= 0");
+        if (n == 0)
+            return;
+        if (in == 0 || out == 0)
+            invalid(std::string(who) + ": in and out must be device addresses");
+        const int64_t leaves = (n + kLeaf - 1) / kLeaf;
+        if (leaves > INT64_C(2147483647))
+            unsupported(std::string(who) + ": too many leaves for one grid");
+        DeviceScope scope(resolveDevice(-1, in));
+        leafPartialsKernel<<<unsigned(leaves), kSlots, 0, seamStream(stream)>>>(reinterpret_cast<const double*>(in), n,
+            reinterpret_cast<double*>(out));
+        launchCheck(who);
     });
 }

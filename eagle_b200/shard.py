@@ -11,11 +11,21 @@ the until-done loop on it with no traffic to the others, reduces its shard to a
 device. A shard of ``4096 * 2^q`` samples is a subtree of the canonical tree
 (eagle/reduce/canonical.h:30-32), so with a power-of-two rank count the folded
 bits equal the one-device reduction of the concatenated shards.
+
+A compaction's survivors are ragged: rank r keeps ``c_r`` values, so its part of
+the concatenated survivors starts at an arbitrary offset and its partial is no
+subtree. :func:`compact_sum_sharded` makes the one exchange that needs: the
+counts are all-gathered (offsets by prefix), every rank shares its first
+``LEAF - 1`` survivors, each rank forms the partials of the leaves that START in
+its part (completing its last leaf from the later ranks' heads), and the leaf
+partials are all-gathered and joined by the canonical pairwise levels -- the bits
+of the one-device canonical sum over the concatenated survivors.
 """
 
 from __future__ import annotations
 
 import ctypes
+from dataclasses import dataclass, field
 
 from . import _abi
 
@@ -68,3 +78,123 @@ def fold_partials(pairs, stream=None):
     _abi.check(_abi.lib().eagle_backend_x_b200_combine_partials(pairs.data_ptr(), m, work.data_ptr(),
                                                                 out.data_ptr(), s))
     return out
+
+
+@dataclass
+class RaggedPlan:
+    """Rank ``rank``'s share of the canonical tree over ragged survivors."""
+
+    offset: int          # the rank's first survivor in the concatenation
+    total: int           # all ranks' survivors
+    first_leaf: int      # the first leaf starting in the rank's part
+    leaves: int          # leaves starting in the rank's part
+    local_start: int     # the first such leaf's start, in the rank's own survivors
+    full_end: int        # local end of the leaves complete within the rank
+    straddle: list = field(default_factory=list)  # (rank q, lo, hi): head pieces completing the last leaf
+    straddle_len: int = 0  # elements of the straddling leaf (0: none)
+
+
+def ragged_plan(counts, rank: int) -> RaggedPlan:
+    """Which leaves of the canonical tree over the concatenation of every rank's
+    survivors (``counts[q]`` on rank q, in rank order) rank ``rank`` forms, and the
+    pieces of later ranks' heads its last leaf needs."""
+    counts = [int(c) for c in counts]
+    offsets = [0]
+    for c in counts:
+        offsets.append(offsets[-1] + c)
+    total = offsets[-1]
+    o, c = offsets[rank], counts[rank]
+    plan = RaggedPlan(offset=o, total=total, first_leaf=0, leaves=0, local_start=0, full_end=0)
+    if c == 0:
+        return plan
+    first = -(-o // LEAF)
+    last = (o + c - 1) // LEAF
+    if first > last:
+        return plan  # every survivor here belongs to a leaf an earlier rank forms
+    plan.first_leaf, plan.leaves = first, last - first + 1
+    plan.local_start = first * LEAF - o
+    end = min((last + 1) * LEAF, total)  # the last leaf's global end
+    if end <= o + c:
+        plan.full_end = end - o
+        return plan
+    plan.full_end = last * LEAF - o
+    plan.straddle_len = end - last * LEAF
+    for q in range(rank + 1, len(counts)):
+        lo, hi = max(offsets[q], o + c), min(offsets[q + 1], end)
+        if lo < hi:
+            plan.straddle.append((q, lo - offsets[q], hi - offsets[q]))
+        if offsets[q + 1] >= end:
+            break
+    return plan
+
+
+def ragged_fold(kept, count: int, *, group=None, leaf_partials=None, combine=None):
+    """The canonical sum over every rank's survivors ``kept[:count]`` (1-D float64
+    tensors, any device), joined in rank order: ``(hi, comp, value)`` on every rank.
+    ``leaf_partials`` maps a 1-D tensor to its ``(leaves, 2)`` partials and
+    ``combine`` a ``(m, 2)`` tensor of pairs to ``(hi, comp, value)``; both default
+    to this library's device entries."""
+    import torch
+    import torch.distributed as dist
+
+    leaf_partials = leaf_partials or device_leaf_partials
+    combine = combine or (lambda pairs: fold_partials(pairs.reshape(-1)))
+    dev = kept.device
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    cnt = torch.tensor([int(count)], dtype=torch.int64, device=dev)
+    gathered = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(world)]
+    dist.all_gather(gathered, cnt, group=group)
+    counts = [int(g.item()) for g in gathered]
+    total = sum(counts)
+    if total == 0:
+        return torch.zeros(3, dtype=torch.float64, device=dev)
+    # every rank's first LEAF - 1 survivors
+    head = torch.zeros(LEAF - 1, dtype=torch.float64, device=dev)
+    h = min(int(count), LEAF - 1)
+    head[:h] = kept[:h]
+    heads = [torch.zeros(LEAF - 1, dtype=torch.float64, device=dev) for _ in range(world)]
+    dist.all_gather(heads, head, group=group)
+    plan = ragged_plan(counts, rank)
+    pairs = []
+    if plan.full_end > plan.local_start:
+        pairs.append(leaf_partials(kept[plan.local_start:plan.full_end].contiguous()))
+    if plan.straddle_len:
+        parts = [kept[plan.full_end:int(count)]] + [heads[q][lo:hi] for q, lo, hi in plan.straddle]
+        leaf = torch.cat(parts).contiguous()
+        assert leaf.numel() == plan.straddle_len
+        pairs.append(leaf_partials(leaf))
+    mine = torch.cat(pairs) if pairs else torch.zeros((0, 2), dtype=torch.float64, device=dev)
+    # all-gather the leaf partials, each rank's padded to the most any rank forms
+    sizes = [ragged_plan(counts, q).leaves for q in range(world)]
+    width = max(sizes)
+    padded = torch.zeros((width, 2), dtype=torch.float64, device=dev)
+    padded[:mine.shape[0]] = mine
+    every = [torch.zeros((width, 2), dtype=torch.float64, device=dev) for _ in range(world)]
+    dist.all_gather(every, padded, group=group)
+    ordered = torch.cat([every[q][:sizes[q]] for q in range(world)]).contiguous()
+    return combine(ordered)
+
+
+def device_leaf_partials(x):
+    """``(leaves, 2)`` (hi, comp) leaf partials of a CUDA float64 tensor."""
+    import torch
+
+    n = x.numel()
+    out = torch.empty(((n + LEAF - 1) // LEAF, 2), dtype=torch.float64, device=x.device)
+    if n:
+        _abi.check(_abi.lib().eagle_backend_x_b200_leaf_partials(x.data_ptr(), n, out.data_ptr(),
+                                                                  torch.cuda.current_stream(x.device).cuda_stream))
+    return out
+
+
+def compact_sum_sharded(mask, values, *, drop: bool = False, group=None):
+    """Compact each rank's shard and take the canonical sum of every rank's
+    survivors as ONE concatenation in rank order: ``(hi, comp, value)`` on every
+    rank, the bits of the one-device compact-then-sum of the concatenated shards."""
+    from ._api import CompactSum
+
+    cs = CompactSum(mask, values, drop=drop)
+    cs.gather()
+    count = int(cs.count.item())
+    return ragged_fold(cs.kept, count, group=group)

@@ -654,6 +654,13 @@ eagle_backend_status eagle_backend_x_b200_compact_gather(struct eagle_backend_co
  * give 0. Query with work_a == 0. One kernel after a memset; capturable. */
 eagle_backend_status eagle_backend_x_b200_reduce_counted(struct eagle_backend_reduce_desc* desc, uint64_t count);
 
+/* No counterpart in the reference: every leaf's (hi, comp) partial of a float64 sum
+ * of ``n`` elements into ``out[2 * leaves]`` (the last leaf over the remainder) --
+ * the leaves of the canonical tree (canonical.h:340-353), so that leaves whose
+ * elements live on several ranks (a compaction's ragged survivors) can be formed
+ * where their elements meet and then joined by x_b200_combine_partials. */
+eagle_backend_status eagle_backend_x_b200_leaf_partials(uint64_t in, int64_t n, uint64_t out, uint64_t stream);
+
 /* eagle_backend_x_b200_combine_partials: combine ``m`` float64 (hi, comp) partials
  * ``hc[2m]`` (chunk roots in chunk order, e.g. one per rank; each chunk
  * leafSize * 2^q samples) by the canonical pairwise levels into ``out[3]`` = {hi,

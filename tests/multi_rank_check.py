@@ -1,7 +1,8 @@
 """One rank of the multi-GPU check (launched by tests/test_gpu_multi.py under
 torchrun): the engine on this rank's shard of a 2^22-sample batch, the canonical
-partial of x, an NCCL all-gather and the device fold; rank 0 compares the bits
-with the oracle's one-device run of the whole batch."""
+partial of x, an NCCL all-gather and the device fold; then a compaction of this
+rank's shard of an uneven batch and the ragged exchange of its survivors. Rank 0
+compares both results' bits with the oracle's one-device runs of the whole batch."""
 
 import datetime
 import os
@@ -46,6 +47,22 @@ def main():
             print(f"MISMATCH folded {got!r} whole {want!r}", flush=True)
             sys.exit(1)
         print("RANK-ORDER FOLD OK", world, got, flush=True)
+    # compact-then-sum over ragged survivors: an uneven batch, so no shard is a subtree
+    nv = (1 << 22) + 12_345
+    g = np.random.default_rng(7)
+    vals, keep = g.standard_normal(nv), g.random(nv) < 0.37
+    b, c = shard.shard_range(nv, rank, world)
+    got = shard.compact_sum_sharded(torch.from_numpy(keep[b:b + c].copy()).cuda(),
+                                    torch.from_numpy(vals[b:b + c].copy()).cuda())
+    torch.cuda.synchronize()
+    if rank == 0:
+        import oracle
+
+        want = oracle.reduce(vals[keep])[0]
+        if np.float64(got[2].item()).tobytes() != np.float64(want).tobytes():
+            print(f"MISMATCH ragged {got[2].item()!r} whole {want!r}", flush=True)
+            sys.exit(1)
+        print("RAGGED COMPACT-SUM OK", world, want, flush=True)
     dist.barrier()
     dist.destroy_process_group()
 

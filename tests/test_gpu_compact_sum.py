@@ -81,3 +81,16 @@ def test_full_size_one_mask(eb, orc):
     cs = eb.CompactSum(torch.from_numpy(keep).cuda(), torch.from_numpy(x).cuda())
     got = cs().cpu().numpy()
     assert got.tobytes() == orc.reduce(x[keep]).tobytes()
+
+
+def test_leaf_partials_join_to_the_canonical_sum(orc):
+    """The leaf-partial entry gives the oracle's leaves, and joining them with the
+    pairwise levels gives the canonical sum's bits."""
+    from eagle_b200 import shard
+
+    for n in (1, 4095, 4096, 4097, 100_003):
+        x = orc.corpus(n, n)
+        got = shard.device_leaf_partials(torch.from_numpy(x).cuda())
+        assert got.cpu().numpy().tobytes() == orc.leaf_partials(x).tobytes()
+        folded = shard.fold_partials(got.reshape(-1))
+        assert folded[2].item() == orc.reduce(x)[0]

@@ -1,8 +1,10 @@
 """Multi-GPU: every rank runs the until-done engine on its contiguous shard, the
 per-rank canonical partials of x are all-gathered over NCCL and folded in rank
 order on the device; the result's bits equal the one-device run over the whole
-batch (checked against the oracle). Runs under torchrun when two or more GPUs are
-visible; skipped otherwise."""
+batch (checked against the oracle); and a compaction's ragged survivors, summed
+across ranks by the head and leaf-partial exchange, give the bits of the one-device
+compact-then-sum. Runs under torchrun when two or more GPUs are visible; skipped
+otherwise."""
 
 import os
 import subprocess
@@ -29,3 +31,4 @@ def test_shards_fold_to_the_whole(world):
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "RANK-ORDER FOLD OK" in r.stdout
+    assert "RAGGED COMPACT-SUM OK" in r.stdout

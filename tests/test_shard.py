@@ -62,3 +62,47 @@ def test_rank_order_fold_is_the_whole(orc, world):
         folded, whole, his, mine = res[r]
         assert np.float64(folded).tobytes() == np.float64(whole).tobytes()
         assert his[r] == mine  # the gather is in rank order
+
+
+def _ragged_rank(rank, world, port, counts, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import oracle
+
+        whole = oracle.corpus(sum(counts), 7)
+        begin = sum(counts[:rank])
+        kept = torch.zeros(counts[rank] + 3, dtype=torch.float64)  # capacity past the count, as a compaction leaves
+        kept[:counts[rank]] = torch.from_numpy(whole[begin:begin + counts[rank]])
+
+        def leaves(x):
+            return torch.from_numpy(oracle.leaf_partials(x.numpy()))
+
+        def combine(pairs):
+            h, c = oracle.pairwise(pairs.numpy())
+            return torch.tensor([h, c, oracle.partial_value(h, c)], dtype=torch.float64)
+
+        r = shard.ragged_fold(kept, counts[rank], leaf_partials=leaves, combine=combine)
+        want = oracle.reduce(whole, pair_out=True) if sum(counts) else np.zeros(2)
+        out[rank] = (r.numpy().tobytes(), np.float64(oracle.reduce(whole)[0] if sum(counts) else 0.0).tobytes(),
+                     np.asarray(want, dtype=np.float64)[:2].tobytes())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("counts", ([5000, 3000], [0, 9000, 1, 4095], [4096, 4096, 8192, 10], [1, 2, 3],
+                                    [20000, 0, 0, 123]))
+def test_ragged_survivors_fold_to_the_whole(orc, counts):
+    """Ragged per-rank survivors (zeros, fragments smaller than a leaf, exact leaves):
+    the exchange of heads and leaf partials gives the bits of the one-rank canonical
+    sum over the concatenation."""
+    world = len(counts)
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_ragged_rank, args=(world, _free_port(), counts, out), nprocs=world, join=True)
+        res = dict(out)
+    for r in range(world):
+        got, want_value, want_pair = res[r]
+        got = np.frombuffer(got, dtype=np.float64)
+        assert got[2:3].tobytes() == want_value
+        assert got[:2].tobytes() == want_pair
