@@ -666,7 +666,7 @@ def side_workload(args):
                                       "kind": "port",
                                       "sample": f"the first {m} samples of each mask: compaction then canonical "
                                                 f"sum ({sec:.2f} s; mask + values read)"},
-                     "gpu_launches": 4 * 3 * args.steps, "clocks": clocks.summary()})
+                     "gpu_launches": 4 * 2 * args.steps, "clocks": clocks.summary()})
     print(json.dumps(line), flush=True)
 
 

@@ -660,12 +660,15 @@ def entry(name: str, device: int = -1) -> int:
 
 
 class CompactSum:
-    """Compact the samples ``mask`` keeps and take the canonical sum of their
-    ``values`` (float64), in two kernels with no host read in between: the
-    compaction writes the kept values in sample order (``eagle_backend_x_b200_compact_gather``)
-    and the reduction reads the kept count on the device
-    (``eagle_backend_x_b200_reduce_counted``). Buffers are allocated once;
-    :meth:`__call__` only enqueues. ``drop=True`` treats set bytes as dropped (a
+    """The canonical ordered sum of the float64 ``values`` that ``mask`` keeps, in
+    sample order (eagle: ActiveSet.compact, python/eagle/_active_set.py:482-525, then
+    the ``ordered`` reduction of python/eagle/_graph_reduce.py:98-173 over the
+    compacted plane). :meth:`__call__` is one call of
+    ``eagle_backend_x_b200_compact_sum``: a keep bitmap and the leaf starts, then each
+    4096-survivor leaf summed straight from ``values``; the kept values are never
+    written. :meth:`gather` writes them instead (``eagle_backend_x_b200_compact_gather``
+    into ``kept``), for callers that need the compacted plane itself. Buffers are
+    allocated once; calls only enqueue. ``drop=True`` treats set bytes as dropped (a
     ``terminated`` mask), ``drop=False`` as kept."""
 
     def __init__(self, mask, values, *, drop: bool = False, pair_out: bool = False):
@@ -677,36 +680,41 @@ class CompactSum:
             raise ValueError("CompactSum takes contiguous float64 CUDA values, one per mask byte")
         n = mask.numel()
         dev = mask.device
-        self.mask, self.values = mask, values
-        self.kept = torch.empty(max(n, 1), dtype=torch.float64, device=dev)
+        self.mask, self.values, self.n, self.drop = mask, values, n, drop
         self.count = torch.zeros(1, dtype=torch.int32, device=dev)
-        d = _abi.new(_abi.CompactDesc, flags=_abi.COMPACT_MASK_IS_DROP if drop else 0, device=dev.index, n=n)
-        _abi.check(_abi.lib().eagle_backend_x_b200_compact_gather(ctypes.byref(d), 0, 0, 8))  # query
+        self.out = torch.empty(2 if pair_out else 1, dtype=torch.float64, device=dev)
+        self.flags = _abi.REDUCE_PAIR_OUT if pair_out else 0
+        flags = _abi.COMPACT_MASK_IS_DROP if drop else 0
+        d = _abi.new(_abi.CompactDesc, flags=flags, device=dev.index, n=n)
+        with torch.cuda.device(dev):
+            _abi.check(_abi.lib().eagle_backend_x_b200_compact_sum(ctypes.byref(d), 0, 0, self.flags))  # query
         self.scratch = torch.empty(max(int(d.scratch_bytes), 1), dtype=torch.uint8, device=dev)
         d.mask, d.count, d.scratch = _ptr(mask), _ptr(self.count), _ptr(self.scratch)
-        self.cdesc = d
-        r = _abi.new(_abi.ReduceDesc, dtype=_abi.REDUCE_F64, op=_abi.REDUCE_OP_SUM, device=dev.index, n=max(n, 1),
-                     policy=_abi.REDUCE_ORDERED, flags=_abi.REDUCE_PAIR_OUT if pair_out else 0, columns=1)
-        _abi.check(_abi.lib().eagle_backend_x_b200_reduce_counted(ctypes.byref(r), 0))  # query
-        self.work_a = torch.empty(int(r.work_elems), dtype=torch.float64, device=dev)
-        self.work_b = torch.empty(int(r.work_elems), dtype=torch.float64, device=dev)
-        self.out = torch.empty(2 if pair_out else 1, dtype=torch.float64, device=dev)
-        r.in_, r.out, r.work_a, r.work_b = _ptr(self.kept), _ptr(self.out), _ptr(self.work_a), _ptr(self.work_b)
-        self.rdesc = r
+        self.sdesc = d
+        self.kept = None
+        self._gdesc = None
 
     def gather(self, stream=None):
-        """Enqueue the compaction alone: the kept values in ``kept``, their count in ``count``."""
-        self.cdesc.stream = _stream_handle(stream)
-        _abi.check(_abi.lib().eagle_backend_x_b200_compact_gather(ctypes.byref(self.cdesc), _ptr(self.values),
+        """Enqueue the compaction that writes the kept values in sample order into
+        ``kept`` and their number into ``count`` (no sum)."""
+        torch = _t()
+        if self._gdesc is None:
+            dev = self.mask.device
+            self.kept = torch.empty(max(self.n, 1), dtype=torch.float64, device=dev)
+            d = _abi.new(_abi.CompactDesc, flags=_abi.COMPACT_MASK_IS_DROP if self.drop else 0, device=dev.index,
+                         n=self.n)
+            _abi.check(_abi.lib().eagle_backend_x_b200_compact_gather(ctypes.byref(d), 0, 0, 8))  # query
+            self._gscratch = torch.empty(max(int(d.scratch_bytes), 1), dtype=torch.uint8, device=dev)
+            d.mask, d.count, d.scratch = _ptr(self.mask), _ptr(self.count), _ptr(self._gscratch)
+            self._gdesc = d
+        self._gdesc.stream = _stream_handle(stream)
+        _abi.check(_abi.lib().eagle_backend_x_b200_compact_gather(ctypes.byref(self._gdesc), _ptr(self.values),
                                                                    _ptr(self.kept), 8))
 
     def __call__(self, stream=None):
-        s = _stream_handle(stream)
-        self.cdesc.stream = s
-        self.rdesc.stream = s
-        _abi.check(_abi.lib().eagle_backend_x_b200_compact_gather(ctypes.byref(self.cdesc), _ptr(self.values),
-                                                                   _ptr(self.kept), 8))
-        _abi.check(_abi.lib().eagle_backend_x_b200_reduce_counted(ctypes.byref(self.rdesc), _ptr(self.count)))
+        self.sdesc.stream = _stream_handle(stream)
+        _abi.check(_abi.lib().eagle_backend_x_b200_compact_sum(ctypes.byref(self.sdesc), _ptr(self.values),
+                                                               _ptr(self.out), self.flags))
         return self.out
 
 

@@ -43,39 +43,6 @@ struct CompactArgs {
     uint32_t elemBytes;  // Gather: 4 or 8
 };
 
-/** Bits of the non-zero bytes among the 16 in ``w`` (bit j: byte j). */
-__device__ __forceinline__ uint32_t nonZero16(uint4 w)
-{
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    uint32_t set = 0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const uint32_t nz = __vcmpne4(words[q], 0u);  // 0xff per non-zero byte
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-            set |= ((nz >> (8 * b)) & 1u) << (4 * q + b);
-    }
-    return set;
-}
-
-/** Keep bits of the 16 mask bytes of samples [i0, i0 + 16): one 16-byte load when
- *  the run is whole and the mask 16-byte aligned. */
-template <bool Drop, bool Aligned>
-__device__ __forceinline__ uint32_t keepBits16(const uint8_t* __restrict__ mask, int64_t i0, int64_t n)
-{
-    uint32_t set = 0;  // bit j: mask byte i0 + j is non-zero
-    if (Aligned && i0 + 16 <= n) {
-        set = nonZero16(__ldg(reinterpret_cast<const uint4*>(mask + i0)));
-    } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if (i0 + j < n && mask[i0 + j] != 0)
-                set |= 1u << j;
-    }
-    const uint32_t valid = i0 >= n ? 0u : (i0 + 16 <= n ? 0xffffu : ((1u << uint32_t(n - i0)) - 1u));
-    return (Drop ? ~set : set) & valid;
-}
-
 /** One 16384-sample tile per CTA, as four rows of 4096: thread t holds the 16
  *  mask bytes at t * 16 of every row (four coalesced 16-byte loads). One CTA scan
  *  of the four rows' counts packed as 16-bit lanes of a 64-bit word gives each

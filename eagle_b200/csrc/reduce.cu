@@ -14,45 +14,16 @@
 // The last CTA to finish (a device-scope counter) runs the remaining levels over
 // the group partials in aligned chunks of 512 and stores the value. One memset
 // node zeroes the counters before the launch, so the call stays capturable.
-#include "common.cuh"
+#include "canonical.cuh"
 
 #include <cmath>
 
 namespace eb {
 namespace {
 
-constexpr int kSlots = 256;
-constexpr int kTerms = 16;
-constexpr int64_t kLeaf = int64_t(kSlots) * kTerms;
-constexpr int kChunk = 512;         // nodes one pass of the final levels joins
 constexpr int kMaxGroupLeaves = 64;  // leaves one CTA owns at most
 
 // ------------------------------------------------------------------- partials
-
-template <class T>
-struct CompP {  // a floating-point sum's partial (hi, comp)
-    T h, c;
-    static __device__ __forceinline__ CompP of(T x) { return {x, T(0)}; }
-    static __device__ __forceinline__ CompP of(T x, T xc) { return {x, isfinite(x) ? xc : T(0)}; }
-    static __device__ __forceinline__ CompP join(const CompP& a, const CompP& b)
-    {
-        const T s = a.h + b.h;
-        const T bb = s - a.h;
-        const T e = (a.h - (s - bb)) + (b.h - bb);
-        return {s, isfinite(s) ? (a.c + b.c) + e : T(0)};
-    }
-    __device__ __forceinline__ void add(T x) { *this = join(*this, CompP{x, T(0)}); }
-    __device__ __forceinline__ void add(T x, T xc)
-    {
-        add(x);
-        c = isfinite(h) ? c + xc : T(0);
-    }
-    __device__ __forceinline__ T value() const { return isfinite(h) ? h + c : h; }
-    __device__ __forceinline__ CompP shflDown(unsigned off) const
-    {
-        return {__shfl_down_sync(kFull, h, off), __shfl_down_sync(kFull, c, off)};
-    }
-};
 
 template <class T>
 struct SumOp {
@@ -113,73 +84,6 @@ struct ReduceArgs {
     void* out;
     int pairOut;
 };
-
-/** One leaf's partial (valid in thread 0): the slot walk, then the in-leaf tree. */
-template <class P, class T, bool HasComp>
-__device__ __forceinline__ P leafPartial(const T* __restrict__ in, const T* __restrict__ comp, int64_t cols,
-    int64_t col, int64_t base, int64_t cnt, P* s)
-{
-    const int t = int(threadIdx.x);
-    const int live = cnt < kSlots ? int(cnt) : kSlots;
-    if (t < live) {
-        T v[kTerms];
-        T vc[HasComp ? kTerms : 1];
-#pragma unroll
-        for (int k = 0; k < kTerms; ++k) {
-            const int64_t i = int64_t(t) + int64_t(k) * kSlots;
-            v[k] = i < cnt ? in[(base + i) * cols + col] : T(0);
-            if constexpr (HasComp)
-                vc[k] = i < cnt ? comp[(base + i) * cols + col] : T(0);
-        }
-        P p;
-        if constexpr (HasComp)
-            p = P::of(v[0], vc[0]);
-        else
-            p = P::of(v[0]);
-#pragma unroll
-        for (int k = 1; k < kTerms; ++k) {
-            if (int64_t(t) + int64_t(k) * kSlots < cnt) {
-                if constexpr (HasComp)
-                    p.add(v[k], vc[k]);
-                else
-                    p.add(v[k]);
-            }
-        }
-        s[t] = p;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int off = kSlots / 2; off >= 32; off >>= 1) {
-        if (t < off && t + off < live)
-            s[t] = P::join(s[t], s[t + off]);
-        __syncthreads();
-    }
-    P q{};
-    if (t < 32) {
-        q = s[t];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            const P o = q.shflDown(unsigned(off));
-            if (t < off && t + off < live)
-                q = P::join(q, o);
-        }
-    }
-    __syncthreads();  // s is reused by the next leaf
-    return q;
-}
-
-/** Pairwise levels over ``v[0, m)`` in shared memory (an aligned subtree): node i
- *  of level L sits at i * 2^L; its right child, if present, at + 2^(L-1). */
-template <class P>
-__device__ __forceinline__ void levels(P* v, int m)
-{
-    for (int off = 1; off < m; off <<= 1) {
-        for (int i = int(threadIdx.x) * 2 * off; i < m; i += int(blockDim.x) * 2 * off)
-            if (i + off < m)
-                v[i] = P::join(v[i], v[i + off]);
-        __syncthreads();
-    }
-}
 
 template <class P, class T, bool HasComp>
 __global__ __launch_bounds__(kSlots) void canonicalKernel(ReduceArgs a)

@@ -32,11 +32,62 @@ def test_compact_then_sum(eb, orc, n, i):
     cs = eb.CompactSum(torch.from_numpy(keep).cuda(), torch.from_numpy(x).cuda())
     got = cs().cpu().numpy()
     kept = x[keep]
+    assert int(cs.count.item()) == kept.size
+    want = orc.reduce(kept) if kept.size else np.zeros(1)
+    assert got.tobytes() == want.tobytes(), (n, PS[i])
+    cs.gather()  # the compacted plane itself
     c = int(cs.count.item())
     assert c == kept.size
     assert cs.kept[:c].cpu().numpy().tobytes() == kept.tobytes()
-    want = orc.reduce(kept) if kept.size else np.zeros(1)
-    assert got.tobytes() == want.tobytes(), (n, PS[i])
+
+
+def _patterns(n):
+    """Masks whose survivors put leaf starts on word, row and tile edges."""
+    i = np.arange(n)
+    yield "all", np.ones(n, bool)
+    yield "even", i % 2 == 0
+    yield "every 33rd", i % 33 == 0
+    yield "one run", (i >= n // 3) & (i < n // 3 + 3 * 4096 + 5)
+    yield "first and last", (i == 0) | (i == n - 1)
+    yield "runs of 4096", (i // 4096) % 2 == 1
+    yield "tile edges", (i % 16384 == 16383) | (i % 16384 == 0)
+
+
+@pytest.mark.parametrize("n", (31, 4096, 16384, 3 * 16384 + 7, 8 * 4096 * 33 + 1, (1 << 20) + 3))
+def test_fused_sum_on_edge_masks(eb, orc, n):
+    x = orc.corpus(n, n + 1)
+    xd = torch.from_numpy(x).cuda()
+    for name, keep in _patterns(n):
+        cs = eb.CompactSum(torch.from_numpy(keep).cuda(), xd)
+        got = cs().cpu().numpy()
+        want = orc.reduce(x[keep]) if keep.any() else np.zeros(1)
+        assert int(cs.count.item()) == int(keep.sum()), name
+        assert got.tobytes() == want.tobytes(), (n, name)
+
+
+def test_fused_sum_unaligned_mask(eb, orc):
+    """A mask that does not start on a 16-byte boundary takes the byte-wise loads."""
+    n = 200_003
+    x, keep = microbench_inputs(n, 1)
+    buf = torch.zeros(n + 1, dtype=torch.uint8, device="cuda")
+    buf[1:] = torch.from_numpy(keep.astype(np.uint8)).cuda()
+    cs = eb.CompactSum(buf[1:], torch.from_numpy(x).cuda())
+    assert cs().cpu().numpy().tobytes() == orc.reduce(x[keep]).tobytes()
+
+
+def test_fused_sum_refusals(eb):
+    from eagle_b200 import _abi
+    import ctypes
+    d = _abi.new(_abi.CompactDesc, device=0, n=10)
+    with pytest.raises(eb.BackendUnsupported):
+        _abi.check(_abi.lib().eagle_backend_x_b200_compact_sum(ctypes.byref(d), 0, 0, 4))
+    d.index_map = 256
+    with pytest.raises(eb.BackendUnsupported):
+        _abi.check(_abi.lib().eagle_backend_x_b200_compact_sum(ctypes.byref(d), 0, 0, 0))
+    d.index_map = 0
+    d.n = 1 << 31
+    with pytest.raises(eb.BackendUnsupported):
+        _abi.check(_abi.lib().eagle_backend_x_b200_compact_sum(ctypes.byref(d), 0, 0, 0))
 
 
 def test_drop_mask_and_pair_out(eb, orc):
