@@ -42,39 +42,15 @@ struct CompP {  // a floating-point sum's partial (hi, comp)
     }
 };
 
-/** One leaf's partial (valid in thread 0): the slot walk, then the in-leaf tree. */
-template <class P, class T, bool HasComp>
-__device__ __forceinline__ P leafPartial(const T* __restrict__ in, const T* __restrict__ comp, int64_t cols,
-    int64_t col, int64_t base, int64_t cnt, P* s)
+/** The in-leaf tree over the slot partials (thread t < ``live`` holds slot t in
+ *  ``mine``): offsets 128..32 through shared memory, 16..1 by warp shuffles, an
+ *  absent partner carried. The leaf's partial is valid in thread 0. */
+template <class P>
+__device__ __forceinline__ P leafTree(const P& mine, int live, P* s)
 {
     const int t = int(threadIdx.x);
-    const int live = cnt < kSlots ? int(cnt) : kSlots;
-    if (t < live) {
-        T v[kTerms];
-        T vc[HasComp ? kTerms : 1];
-#pragma unroll
-        for (int k = 0; k < kTerms; ++k) {
-            const int64_t i = int64_t(t) + int64_t(k) * kSlots;
-            v[k] = i < cnt ? in[(base + i) * cols + col] : T(0);
-            if constexpr (HasComp)
-                vc[k] = i < cnt ? comp[(base + i) * cols + col] : T(0);
-        }
-        P p;
-        if constexpr (HasComp)
-            p = P::of(v[0], vc[0]);
-        else
-            p = P::of(v[0]);
-#pragma unroll
-        for (int k = 1; k < kTerms; ++k) {
-            if (int64_t(t) + int64_t(k) * kSlots < cnt) {
-                if constexpr (HasComp)
-                    p.add(v[k], vc[k]);
-                else
-                    p.add(v[k]);
-            }
-        }
-        s[t] = p;
-    }
+    if (t < live)
+        s[t] = mine;
     __syncthreads();
 #pragma unroll
     for (int off = kSlots / 2; off >= 32; off >>= 1) {
@@ -94,6 +70,41 @@ __device__ __forceinline__ P leafPartial(const T* __restrict__ in, const T* __re
     }
     __syncthreads();  // s is reused by the next leaf
     return q;
+}
+
+/** One leaf's partial (valid in thread 0): the slot walk, then the in-leaf tree. */
+template <class P, class T, bool HasComp>
+__device__ __forceinline__ P leafPartial(const T* __restrict__ in, const T* __restrict__ comp, int64_t cols,
+    int64_t col, int64_t base, int64_t cnt, P* s)
+{
+    const int t = int(threadIdx.x);
+    const int live = cnt < kSlots ? int(cnt) : kSlots;
+    P p{};
+    if (t < live) {
+        T v[kTerms];
+        T vc[HasComp ? kTerms : 1];
+#pragma unroll
+        for (int k = 0; k < kTerms; ++k) {
+            const int64_t i = int64_t(t) + int64_t(k) * kSlots;
+            v[k] = i < cnt ? in[(base + i) * cols + col] : T(0);
+            if constexpr (HasComp)
+                vc[k] = i < cnt ? comp[(base + i) * cols + col] : T(0);
+        }
+        if constexpr (HasComp)
+            p = P::of(v[0], vc[0]);
+        else
+            p = P::of(v[0]);
+#pragma unroll
+        for (int k = 1; k < kTerms; ++k) {
+            if (int64_t(t) + int64_t(k) * kSlots < cnt) {
+                if constexpr (HasComp)
+                    p.add(v[k], vc[k]);
+                else
+                    p.add(v[k]);
+            }
+        }
+    }
+    return leafTree(p, live, s);
 }
 
 /** Pairwise levels over ``v[0, m)`` in shared memory (an aligned subtree): node i

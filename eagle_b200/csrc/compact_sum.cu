@@ -37,8 +37,9 @@ constexpr int kRows = 4;
 constexpr int64_t kRow = int64_t(kThreads) * 16;  // 4096 samples: 16 mask bytes per thread
 constexpr int64_t kTile = kRow * kRows;           // 16384 samples per keepBits CTA
 constexpr int64_t kTileWords = kTile / 32;        // its bitmap words
-constexpr int kChunkWords = kThreads;             // bitmap words one pass of a leaf scans
-constexpr int kBatch = 16;                        // value loads a thread issues together
+constexpr int kMaxK = 4;                          // bitmap words per thread per chunk, at most
+constexpr int kCap = 8192;                        // kept sample indices one pass stages
+constexpr int kRowBatch = 16;                     // rows whose values a thread loads together
 constexpr int kMaxGroup = 128;                    // leaves a group holds at most
 constexpr int kGroupsPerCta = 8;                  // groups per CTA the claim aims at
 
@@ -141,66 +142,45 @@ struct LeafArgs {
     int pairOut;
 };
 
-/** The kept values of leaf ``l`` (samples [s0, s1), ``cnt`` survivors) into
- *  ``stage`` at their in-leaf rank. */
-__device__ __forceinline__ void stageLeaf(const LeafArgs& a, int64_t s0, int64_t s1, int64_t cnt, double* stage,
-    uint32_t* sWord, uint32_t* sRank, uint32_t* scan)
+/** Bitmap words [cw + t K, cw + t K + K) of a group whose samples are [s0, s1):
+ *  bits outside the group cleared (they belong to the leaves on either side). */
+__device__ __forceinline__ void groupWords(const uint32_t* __restrict__ bitmap, int64_t cw, int K, int64_t s0,
+    int64_t s1, uint32_t (&wd)[kMaxK])
 {
-    const int t = int(threadIdx.x), lane = t & 31, warp = t >> 5;
     const int64_t w0 = s0 >> 5, wEnd = ((s1 - 1) >> 5) + 1;
-    uint32_t base = 0;
-    for (int64_t cw = w0; cw < wEnd; cw += kChunkWords) {
-        const int64_t w = cw + t;
-        uint32_t word = 0;
-        if (w < wEnd) {
-            word = a.bitmap[w];
+#pragma unroll
+    for (int k = 0; k < kMaxK; ++k) {
+        uint32_t x = 0;
+        const int64_t w = cw + int64_t(threadIdx.x) * K + k;
+        if (k < K && w < wEnd) {
+            x = bitmap[w];
             if (w == w0)
-                word &= ~0u << (s0 & 31);  // earlier survivors belong to the leaf before
+                x &= ~0u << (s0 & 31);
             if (w == wEnd - 1) {
-                const int e = int((s1 - 1) & 31);  // later ones to the leaf after
-                word &= e == 31 ? ~0u : ((2u << e) - 1u);
+                const int e = int((s1 - 1) & 31);
+                x &= e == 31 ? ~0u : ((2u << e) - 1u);
             }
         }
-        uint32_t chunkTotal = 0;
-        const uint32_t ex = blockExclusiveSum(uint32_t(__popc(word)), chunkTotal, scan);
-        sWord[t] = word;
-        sRank[t] = base + ex;
-        __syncthreads();
-        const int nw = int(wEnd - cw < kChunkWords ? wEnd - cw : kChunkWords);
-        for (int j0 = 0; j0 < nw; j0 += 8 * kBatch) {
-            double v[kBatch];
-            int r[kBatch];
-#pragma unroll
-            for (int k = 0; k < kBatch; ++k) {
-                const int j = j0 + 8 * k + warp;  // warp w reads word j: 32 consecutive samples
-                r[k] = -1;
-                v[k] = 0.0;
-                if (j < nw) {
-                    const uint32_t wd = sWord[j];
-                    if ((wd >> lane) & 1u) {
-                        r[k] = int(sRank[j] + uint32_t(__popc(wd & ((1u << lane) - 1u))));
-                        v[k] = __ldg(a.values + (cw + j) * 32 + lane);
-                    }
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < kBatch; ++k)
-                if (r[k] >= 0 && r[k] < int(kLeaf))
-                    stage[r[k]] = v[k];
-        }
-        base += chunkTotal;
-        __syncthreads();  // sWord / sRank are rewritten by the next pass
+        wd[k] = x;
     }
-    if (t == 0 && int64_t(base) != cnt)
-        atomicOr(a.err, 2u);  // the bitmap and the leaf starts disagree
 }
 
-__global__ __launch_bounds__(kThreads) void keptLeavesKernel(LeafArgs a)
+/** CTAs claim groups of 2^q consecutive leaves off a counter. A group's survivors
+ *  are one stream: positions 0, 1, ... in rank order, leaf = position / 4096, row =
+ *  position / 256, slot = position % 256, so thread t owns slot t of every row and
+ *  folds its values into its slot's partial in row order -- the leaf walk, term by
+ *  term, with no value ever staged. Per chunk of 256 K bitmap words (K grows as the
+ *  group thins out, so a chunk holds about 8192 survivors): a CTA scan of the
+ *  words' counts, the kept sample indices staged in shared memory by rank, then
+ *  rows in batches of 16, each thread loading its slot's value of every row
+ *  together (consecutive threads, consecutive survivors: coalesced where the mask
+ *  is dense). A row that ends a leaf runs the in-leaf tree. The next chunk's words
+ *  are in flight while the current one is summed. */
+__global__ __launch_bounds__(kThreads, 4) void keptLeavesKernel(LeafArgs a)
 {
-    __shared__ double stage[kLeaf];  // one leaf's kept values by rank (32 KB); the final levels reuse it
+    __shared__ int32_t idx[kCap];  // a pass's kept samples by rank; the final levels reuse it
     __shared__ P s[kSlots];
     __shared__ P group[kMaxGroup];
-    __shared__ uint32_t sWord[kChunkWords], sRank[kChunkWords];
     __shared__ uint32_t scan[33];
     __shared__ uint32_t sGroup;
     __shared__ int amLast;
@@ -224,18 +204,94 @@ __global__ __launch_bounds__(kThreads) void keptLeavesKernel(LeafArgs a)
             break;
         const int64_t l0 = g * gl;
         const int64_t l1 = l0 + gl < leaves ? l0 + gl : leaves;
-        for (int64_t l = l0; l < l1; ++l) {
-            const int64_t cnt = rows - l * kLeaf < kLeaf ? rows - l * kLeaf : kLeaf;
-            // kept inside [0, n) whatever the starts hold, so a failed pass reads in bounds
-            int64_t s0 = a.leafStart[l];
-            s0 = s0 < 0 ? 0 : (s0 >= a.n ? a.n - 1 : s0);
-            int64_t s1 = l + 1 < leaves ? int64_t(a.leafStart[l + 1]) : a.n;
-            s1 = s1 <= s0 ? s0 + 1 : (s1 > a.n ? a.n : s1);
-            stageLeaf(a, s0, s1, cnt, stage, sWord, sRank, scan);
-            const P p = leafPartial<P, double, false>(stage, nullptr, 1, 0, 0, cnt, s);
-            if (t == 0)
-                group[l - l0] = p;
+        const int64_t want = rows - l0 * kLeaf < (l1 - l0) * kLeaf ? rows - l0 * kLeaf : (l1 - l0) * kLeaf;
+        // kept inside [0, n) whatever the starts hold, so a failed pass reads in bounds
+        int64_t s0 = a.leafStart[l0];
+        s0 = s0 < 0 ? 0 : (s0 >= a.n ? a.n - 1 : s0);
+        int64_t s1 = l1 < leaves ? int64_t(a.leafStart[l1]) : a.n;
+        s1 = s1 <= s0 ? s0 + 1 : (s1 > a.n ? a.n : s1);
+        const int64_t w0 = s0 >> 5, wEnd = ((s1 - 1) >> 5) + 1;
+        int K = 1;
+        while (K < kMaxK && int64_t(2 * K) * want <= s1 - s0)
+            K *= 2;
+        const int64_t chunkWords = int64_t(kThreads) * K;
+        P slot{};
+        int done = 0;          // survivors of the group folded so far (at most 128 leaves' worth)
+        int64_t leaf = l0;     // the leaf being folded
+        uint32_t word[kMaxK];
+        groupWords(a.bitmap, w0, K, s0, s1, word);
+        for (int64_t cw = w0; cw < wEnd; cw += chunkWords) {
+            uint32_t next[kMaxK];
+            groupWords(a.bitmap, cw + chunkWords, K, s0, s1, next);
+            uint32_t mine = 0;
+#pragma unroll
+            for (int k = 0; k < kMaxK; ++k)
+                mine += uint32_t(__popc(word[k]));
+            uint32_t total = 0;
+            const uint32_t base = blockExclusiveSum(mine, total, scan);
+            for (uint32_t p0 = 0; p0 < total; p0 += kCap) {
+                if (mine != 0 && base < p0 + kCap && base + mine > p0) {
+                    uint32_t r = base;
+#pragma unroll
+                    for (int k = 0; k < kMaxK; ++k) {
+                        uint32_t x = word[k];
+                        const int64_t sample0 = (cw + int64_t(t) * K + k) * 32;
+                        while (x != 0) {
+                            const int j = __ffs(int(x)) - 1;
+                            x &= x - 1u;
+                            if (r >= p0 && r < p0 + kCap)
+                                idx[r - p0] = int32_t(sample0 + j);
+                            ++r;
+                        }
+                    }
+                }
+                __syncthreads();
+                const int m = total - p0 < uint32_t(kCap) ? int(total - p0) : kCap;
+                const int rowEnd = (done + m - 1) / kSlots;  // the last row this pass touches
+                for (int rowA = done / kSlots; rowA <= rowEnd; rowA += kRowBatch) {
+                    double v[kRowBatch];
+                    const int first = rowA * kSlots + t - done;  // this thread's value of row rowA, by pass rank
+#pragma unroll
+                    for (int i = 0; i < kRowBatch; ++i) {
+                        const int local = first + i * kSlots;
+                        v[i] = (local >= 0 && local < m) ? __ldg(a.values + idx[local]) : 0.0;
+                    }
+#pragma unroll
+                    for (int i = 0; i < kRowBatch; ++i) {
+                        const int row = rowA + i;
+                        if (row > rowEnd)
+                            break;
+                        const int local = first + i * kSlots;
+                        if (local >= 0 && local < m) {
+                            if ((row & (kTerms - 1)) == 0)
+                                slot = P::of(v[i]);
+                            else
+                                slot.add(v[i]);
+                        }
+                        if ((row & (kTerms - 1)) == kTerms - 1 && (row + 1) * kSlots <= done + m) {
+                            const P q = leafTree(slot, kSlots, s);  // the row that ends a leaf
+                            if (t == 0 && leaf < l1)
+                                group[leaf - l0] = q;
+                            ++leaf;
+                        }
+                    }
+                }
+                done += m;
+                __syncthreads();  // idx is rewritten by the next pass
+            }
+#pragma unroll
+            for (int k = 0; k < kMaxK; ++k)
+                word[k] = next[k];
         }
+        if (want % kLeaf != 0) {  // the last leaf of all, short of 4096
+            const int cnt = int(want % kLeaf);
+            const P q = leafTree(slot, cnt < kSlots ? int(cnt) : kSlots, s);
+            if (t == 0 && leaf < l1)
+                group[leaf - l0] = q;
+            ++leaf;
+        }
+        if (t == 0 && (done != want || leaf != l1))
+            atomicOr(a.err, 2u);  // the bitmap and the leaf starts disagree
         __syncthreads();
         levels(group, int(l1 - l0));
         if (t == 0)
@@ -250,7 +306,7 @@ __global__ __launch_bounds__(kThreads) void keptLeavesKernel(LeafArgs a)
     if (!amLast)
         return;
     __threadfence();
-    P* buf = reinterpret_cast<P*>(stage);
+    P* buf = reinterpret_cast<P*>(idx);
     P* v = a.partials;
     int64_t m = groups;
     while (m > 1) {
