@@ -72,6 +72,45 @@ __device__ __forceinline__ P leafTree(const P& mine, int live, P* s)
     return q;
 }
 
+/** leafTree with one barrier: every thread stores its slot, then warp 0 alone runs
+ *  the offsets 128, 64 and 32 (lane t joins slots t + 32 i in registers, the same
+ *  pairs in the same order) and the shuffles, while the other warps go on. ``s``
+ *  must not be written again before the CTA's next barrier after this call:
+ *  callers alternate two buffers. The leaf's partial is valid in thread 0. */
+template <class P>
+__device__ __forceinline__ P leafTreeWarp0(const P& mine, int live, P* s)
+{
+    const int t = int(threadIdx.x);
+    if (t < live)
+        s[t] = mine;
+    __syncthreads();
+    P q{};
+    if (t < 32) {
+        P x[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = t + 32 * i;
+            x[i] = j < live ? s[j] : P{};
+            if (j + 128 < live)
+                x[i] = P::join(x[i], s[j + 128]);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+            if (t + 32 * i + 64 < live)
+                x[i] = P::join(x[i], x[i + 2]);
+        if (t + 32 < live)
+            x[0] = P::join(x[0], x[1]);
+        q = x[0];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const P o = q.shflDown(unsigned(off));
+            if (t < off && t + off < live)
+                q = P::join(q, o);
+        }
+    }
+    return q;
+}
+
 /** One leaf's partial (valid in thread 0): the slot walk, then the in-leaf tree. */
 template <class P, class T, bool HasComp>
 __device__ __forceinline__ P leafPartial(const T* __restrict__ in, const T* __restrict__ comp, int64_t cols,

@@ -39,7 +39,6 @@ constexpr int64_t kTile = kRow * kRows;           // 16384 samples per keepBits 
 constexpr int64_t kTileWords = kTile / 32;        // its bitmap words
 constexpr int kMaxK = 4;                          // bitmap words per thread per chunk, at most
 constexpr int kCap = 8192;                        // kept sample indices one pass stages
-constexpr int kRowBatch = 16;                     // rows whose values a thread loads together
 constexpr int kMaxGroup = 128;                    // leaves a group holds at most
 constexpr int kGroupsPerCta = 8;                  // groups per CTA the claim aims at
 
@@ -62,7 +61,7 @@ __global__ __launch_bounds__(kThreads) void keepBitsKernel(KeepArgs a)
 {
     __shared__ uint32_t sTile;
     __shared__ uint64_t scan64[33];
-    __shared__ uint64_t sPrefix;
+    __shared__ uint32_t firstOf[32];
     const int t = int(threadIdx.x);
     if (t == 0)
         sTile = atomicAdd(a.tileNext, 1u);
@@ -89,23 +88,17 @@ __global__ __launch_bounds__(kThreads) void keepBitsKernel(KeepArgs a)
 #pragma unroll
     for (int q = 0; q < kRows; ++q)
         total += uint32_t(rowTotals >> (16 * q)) & 0xffffu;
-    if (t < 32) {
-        uint64_t prefix = 0;
-        if (tile == 0) {
-            if (t == 0)
-                lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, total);
-        } else {
-            if (t == 0)
-                lbPublish<PlainCodec>(a.status, tile, 0, kLbAggregate, total);
-            prefix = lbExclusivePrefix<PlainCodec>(a.status, tile, 0, a.err);
-            if (t == 0)
-                lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, prefix + total);
-        }
+    uint64_t prefix = 0;
+    if (tile == 0) {
         if (t == 0)
-            sPrefix = prefix;
+            lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, total);
+    } else {
+        if (t == 0)
+            lbPublish<PlainCodec>(a.status, tile, 0, kLbAggregate, total);
+        prefix = lbExclusivePrefixBlock<PlainCodec>(a.status, tile, 0, a.err, firstOf, scan64);
+        if (t == 0)
+            lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, prefix + total);
     }
-    __syncthreads();
-    const uint64_t prefix = sPrefix;
     // a leaf starts at every kept rank that is a multiple of 4096; a thread's 16
     // samples of a row hold at most one such rank
     uint64_t rowBase = prefix;
@@ -179,7 +172,7 @@ __device__ __forceinline__ void groupWords(const uint32_t* __restrict__ bitmap, 
 __global__ __launch_bounds__(kThreads, 4) void keptLeavesKernel(LeafArgs a)
 {
     __shared__ int32_t idx[kCap];  // a pass's kept samples by rank; the final levels reuse it
-    __shared__ P s[kSlots];
+    __shared__ P s[2][kSlots];     // the slot partials of the last two leaves
     __shared__ P group[kMaxGroup];
     __shared__ uint32_t scan[33];
     __shared__ uint32_t sGroup;
@@ -216,6 +209,7 @@ __global__ __launch_bounds__(kThreads, 4) void keptLeavesKernel(LeafArgs a)
             K *= 2;
         const int64_t chunkWords = int64_t(kThreads) * K;
         P slot{};
+        int parity = 0;        // the slot buffer the next in-leaf tree takes
         int done = 0;          // survivors of the group folded so far (at most 128 leaves' worth)
         int64_t leaf = l0;     // the leaf being folded
         uint32_t word[kMaxK];
@@ -248,32 +242,32 @@ __global__ __launch_bounds__(kThreads, 4) void keptLeavesKernel(LeafArgs a)
                 __syncthreads();
                 const int m = total - p0 < uint32_t(kCap) ? int(total - p0) : kCap;
                 const int rowEnd = (done + m - 1) / kSlots;  // the last row this pass touches
-                for (int rowA = done / kSlots; rowA <= rowEnd; rowA += kRowBatch) {
-                    double v[kRowBatch];
+                // one leaf's 16 rows per batch (a group starts on a leaf), so only the
+                // batch's last row can end a leaf
+                for (int rowA = (done / kSlots) & ~(kTerms - 1); rowA <= rowEnd; rowA += kTerms) {
+                    double v[kTerms];
                     const int first = rowA * kSlots + t - done;  // this thread's value of row rowA, by pass rank
 #pragma unroll
-                    for (int i = 0; i < kRowBatch; ++i) {
+                    for (int i = 0; i < kTerms; ++i) {
                         const int local = first + i * kSlots;
                         v[i] = (local >= 0 && local < m) ? __ldg(a.values + idx[local]) : 0.0;
                     }
 #pragma unroll
-                    for (int i = 0; i < kRowBatch; ++i) {
-                        const int row = rowA + i;
-                        if (row > rowEnd)
-                            break;
+                    for (int i = 0; i < kTerms; ++i) {
                         const int local = first + i * kSlots;
                         if (local >= 0 && local < m) {
-                            if ((row & (kTerms - 1)) == 0)
+                            if (i == 0)
                                 slot = P::of(v[i]);
                             else
                                 slot.add(v[i]);
                         }
-                        if ((row & (kTerms - 1)) == kTerms - 1 && (row + 1) * kSlots <= done + m) {
-                            const P q = leafTree(slot, kSlots, s);  // the row that ends a leaf
-                            if (t == 0 && leaf < l1)
-                                group[leaf - l0] = q;
-                            ++leaf;
-                        }
+                    }
+                    if ((rowA + kTerms) * kSlots <= done + m) {  // the leaf's last row is in
+                        const P q = leafTreeWarp0(slot, kSlots, s[parity]);
+                        parity ^= 1;
+                        if (t == 0 && leaf < l1)
+                            group[leaf - l0] = q;
+                        ++leaf;
                     }
                 }
                 done += m;
@@ -285,7 +279,8 @@ __global__ __launch_bounds__(kThreads, 4) void keptLeavesKernel(LeafArgs a)
         }
         if (want % kLeaf != 0) {  // the last leaf of all, short of 4096
             const int cnt = int(want % kLeaf);
-            const P q = leafTree(slot, cnt < kSlots ? int(cnt) : kSlots, s);
+            const P q = leafTreeWarp0(slot, cnt < kSlots ? int(cnt) : kSlots, s[parity]);
+            parity ^= 1;
             if (t == 0 && leaf < l1)
                 group[leaf - l0] = q;
             ++leaf;
