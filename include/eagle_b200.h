@@ -656,16 +656,17 @@ eagle_backend_status eagle_backend_x_b200_reduce_counted(struct eagle_backend_re
 
 /* eagle_backend_x_b200_compact_sum: the canonical ordered sum of the float64
  * ``values`` the mask keeps, in sample order -- the bits of compact_gather followed
- * by reduce_counted -- without writing the kept values anywhere: one pass turns the
- * mask into a keep bitmap and the sample where every 4096-survivor leaf begins, a
- * second sums each leaf straight from ``values``. Writes ``*count`` (the survivors)
- * and ``out[0]`` (the sum), or with ``flags`` = EAGLE_BACKEND_REDUCE_PAIR_OUT
- * ``out[0..1]`` = (hi, comp). Same desc as compact_device: ``index_map`` and the
- * trigger fields must be 0 (no map is written), MASK_IS_DROP honoured, ``scratch ==
- * 0`` is the query (scratch_bytes; the size depends on the device's SM count),
- * scratch 256-byte aligned, n <= 2^31-1. A failed pass (a look-back that gave up)
- * stores count 0xffffffff and a NaN sum. One memset and two kernels: enqueue only,
- * capturable. */
+ * by reduce_counted -- without writing the kept values anywhere: the mask becomes a
+ * keep bitmap with per-tile counts, a scan of the counts gives the sample where every
+ * 4096-survivor leaf begins, and each leaf is summed straight from ``values``. Writes
+ * ``*count`` (the survivors) and ``out[0]`` (the sum), or with ``flags`` =
+ * EAGLE_BACKEND_REDUCE_PAIR_OUT ``out[0..1]`` = (hi, comp). Same desc as
+ * compact_device: ``index_map`` and the trigger fields must be 0 (no map is
+ * written), MASK_IS_DROP honoured, ``scratch == 0`` is the query (scratch_bytes; the
+ * size depends on the device's SM count), scratch 256-byte aligned, n <= 2^31-1. A
+ * leaf whose bitmap and start disagree (the mask changed under the call) stores
+ * count 0xffffffff and a NaN sum. One memset and four kernels, no wait on another
+ * CTA: enqueue only, capturable. */
 eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backend_compact_desc* desc, uint64_t values,
     uint64_t out, uint32_t flags);
 
