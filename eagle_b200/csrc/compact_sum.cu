@@ -42,9 +42,6 @@ constexpr int kRows = 4;
 constexpr int64_t kRow = int64_t(kThreads) * 16;  // 4096 samples: 16 mask bytes per thread
 constexpr int64_t kTile = kRow * kRows;           // 16384 samples per keepCount CTA
 constexpr int64_t kTileWords = kTile / 32;        // its bitmap words
-constexpr int kMaxK = 4;                          // bitmap words per thread per chunk, at most
-constexpr int kMaxGroup = 128;                    // leaves a group holds at most
-constexpr int kGroupsPerCta = 8;                  // groups per CTA the claim aims at
 constexpr int kScanThreads = 1024;
 constexpr int kScanPer = 16;                      // tile counts per scan thread per round
 
@@ -95,12 +92,24 @@ __global__ __launch_bounds__(kScanThreads) void tileScanKernel(const uint32_t* _
     for (int64_t r0 = 0; r0 < tiles; r0 += int64_t(kScanThreads) * kScanPer) {
         const int64_t i0 = r0 + int64_t(t) * kScanPer;
         uint32_t v[kScanPer];
+        if (i0 + kScanPer <= tiles) {  // four 16-byte loads (the counts start 256-byte aligned)
+#pragma unroll
+            for (int k = 0; k < kScanPer / 4; ++k) {
+                const uint4 x = reinterpret_cast<const uint4*>(tileCount + i0)[k];
+                v[4 * k] = x.x;
+                v[4 * k + 1] = x.y;
+                v[4 * k + 2] = x.z;
+                v[4 * k + 3] = x.w;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < kScanPer; ++k)
+                v[k] = i0 + k < tiles ? tileCount[i0 + k] : 0u;
+        }
         uint32_t mine = 0;
 #pragma unroll
-        for (int k = 0; k < kScanPer; ++k) {
-            v[k] = i0 + k < tiles ? tileCount[i0 + k] : 0u;
+        for (int k = 0; k < kScanPer; ++k)
             mine += v[k];
-        }
         uint32_t total = 0;
         uint32_t run = carry + blockExclusiveSum(mine, total, scan);
 #pragma unroll
@@ -169,202 +178,281 @@ __global__ __launch_bounds__(kThreads) void leafStartKernel(const uint32_t* __re
     }
 }
 
+
+/** Pulls the values of samples [s0, s1) into L2 (128-byte lines spread over the
+ *  warp) when the range is dense enough that nearly all of its sectors will be
+ *  read: at most two samples per survivor. The lines stay inside the values. */
+__device__ __forceinline__ void prefetchLeafWarp(const double* values, int64_t n, int64_t s0, int64_t s1, int cnt)
+{
+    if (s1 - s0 > 2 * int64_t(cnt))
+        return;
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(values);
+    const uintptr_t hi = lo + uintptr_t(n) * sizeof(double);
+    uintptr_t p = reinterpret_cast<uintptr_t>(values + s0) & ~uintptr_t(127);
+    const uintptr_t e = reinterpret_cast<uintptr_t>(values + s1);
+    for (p += uintptr_t(threadIdx.x & 31) * 128; p < e; p += 32 * 128)
+        if (p >= lo && p < hi)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 struct LeafArgs {
     const uint32_t* bitmap;
     const int32_t* leafStart;
     const uint32_t* count;
     const double* values;
     int64_t n;
-    P* partials;          // one per claimed group
-    uint32_t groupCap;    // partials' capacity
-    uint32_t* groupNext;  // zero on entry
-    uint32_t* done;       // zero on entry
+    P* leafPart;          // one partial per leaf
+    P* chunkPart;         // one per aligned chunk of kChunk leaves
+    uint32_t* chunkDone;  // leaves finished per chunk, zero on entry
+    uint32_t* topDone;    // chunks finished, zero on entry
+    uint32_t* leafNext;   // the leaf claim counter, zero on entry
     uint32_t* err;        // zero on entry
     double* out;
     int pairOut;
 };
 
-/** Bitmap words [cw + t K, cw + t K + K) of a leaf whose samples are [s0, s1):
- *  bits outside the leaf cleared (they belong to its neighbours). */
-__device__ __forceinline__ void leafWords(const uint32_t* __restrict__ bitmap, int64_t cw, int K, int64_t s0,
-    int64_t s1, uint32_t (&wd)[kMaxK])
+constexpr int kLeafWarps = kThreads / 32;
+constexpr int kRing = 512;      // a warp's staged values: under 256 waiting + 8 words' worth
+constexpr int kBatchWords = 8;  // non-empty bitmap words whose values a lane loads together
+constexpr int kSlotsPerLane = kSlots / 32;
+
+/** Pairwise levels over ``m <= 512`` partials at ``in`` (an aligned 512-node
+ *  subtree), by one warp: lane l takes nodes [16 l, 16 l + 16) and joins them in
+ *  registers (offsets 1..8), then lanes pair up by shuffles (offsets 16..256): the
+ *  pairs and order of ``levels``. Result in lane 0. Reads through L2, so partials
+ *  that other CTAs published before their counter increment are seen. */
+__device__ __forceinline__ P warpLevels(const P* in, int m)
 {
-    const int64_t w0 = s0 >> 5, wEnd = ((s1 - 1) >> 5) + 1;
+    const int lane = int(threadIdx.x & 31);
+    P x[16];
 #pragma unroll
-    for (int k = 0; k < kMaxK; ++k) {
-        uint32_t x = 0;
-        const int64_t w = cw + int64_t(threadIdx.x) * K + k;
-        if (k < K && w < wEnd) {
-            x = bitmap[w];
+    for (int j = 0; j < 16; ++j) {
+        const int i = lane * 16 + j;
+        x[j] = i < m ? P{__ldcg(&in[i].h), __ldcg(&in[i].c)} : P{};
+    }
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1)
+#pragma unroll
+        for (int j = 0; j < 16; j += 2 * off)
+            if (lane * 16 + j + off < m)
+                x[j] = P::join(x[j], x[j + off]);
+    P q = x[0];
+#pragma unroll
+    for (int lo = 1; lo < 32; lo <<= 1) {
+        const P o = q.shflDown(unsigned(lo));
+        if ((lane & (2 * lo - 1)) == 0 && (lane + lo) * 16 < m)
+            q = P::join(q, o);
+    }
+    return q;
+}
+
+/** One warp sums one leaf: the samples [s0, s1) hold its ``cnt`` survivors. Lane l
+ *  owns slots l + 32 i (i < 8). The bitmap words go 32 at a time (one per lane); the
+ *  non-empty ones 8 at a time, each lane loading the value of its bit in each (one
+ *  coalesced 256-byte row per word), into a ring at the value's rank; every full
+ *  row of 256 ranks is folded, slot by slot, in rank order. The fold skips the
+ *  non-finite test of each step and applies it once at the end: once a slot's hi
+ *  is infinite or NaN it stays so, and its comp ends zero either way; while hi is
+ *  finite the comp of a join with (x, 0) is never -0, so adding that 0 is exact. */
+__device__ __forceinline__ P sumLeaf(const LeafArgs& a, int64_t s0, int64_t s1, int cnt, double* ring)
+{
+    const int lane = int(threadIdx.x & 31);
+    const uint32_t below = (1u << lane) - 1u;
+    const int64_t w0 = s0 >> 5, wEnd = ((s1 - 1) >> 5) + 1;
+    double h[kSlotsPerLane], c[kSlotsPerLane];
+#pragma unroll
+    for (int i = 0; i < kSlotsPerLane; ++i)
+        h[i] = c[i] = 0.0;
+    uint32_t have = 0, used = 0;  // ranks staged, ranks folded (warp-uniform)
+    auto fold = [&](int live) {   // the row at ``used``: slots below ``live`` take a term
+        const bool first = used == 0;
+#pragma unroll
+        for (int i = 0; i < kSlotsPerLane; ++i) {
+            if (lane + 32 * i < live) {
+                const double x = ring[(used + uint32_t(lane + 32 * i)) & (kRing - 1)];
+                if (first) {
+                    h[i] = x;
+                } else {
+                    const double sum = h[i] + x;
+                    const double bb = sum - h[i];
+                    const double e = (h[i] - (sum - bb)) + (x - bb);
+                    c[i] = c[i] + e;
+                    h[i] = sum;
+                }
+            }
+        }
+    };
+    for (int64_t wb = w0; wb < wEnd; wb += 32) {
+        uint32_t word = 0;
+        const int64_t w = wb + lane;
+        if (w < wEnd) {
+            word = a.bitmap[w];
             if (w == w0)
-                x &= ~0u << (s0 & 31);
+                word &= ~0u << (s0 & 31);
             if (w == wEnd - 1) {
                 const int e = int((s1 - 1) & 31);
-                x &= e == 31 ? ~0u : ((2u << e) - 1u);
+                word &= e == 31 ? ~0u : ((2u << e) - 1u);
             }
         }
-        wd[k] = x;
+        uint32_t nz = __ballot_sync(kFull, word != 0);
+        while (nz != 0) {
+            double v[kBatchWords];
+            uint32_t r[kBatchWords];
+#pragma unroll
+            for (int b = 0; b < kBatchWords; ++b) {
+                const int src = nz != 0 ? __ffs(int(nz)) - 1 : 0;
+                const uint32_t wd = __shfl_sync(kFull, word, src) & (nz != 0 ? ~0u : 0u);
+                nz &= nz - 1u;
+                const bool mine = (wd >> lane) & 1u;
+                r[b] = mine ? have + uint32_t(__popc(wd & below)) : 0xffffffffu;
+                v[b] = mine ? __ldg(a.values + (wb + src) * 32 + lane) : 0.0;
+                have += uint32_t(__popc(wd));
+            }
+#pragma unroll
+            for (int b = 0; b < kBatchWords; ++b)
+                if (r[b] < uint32_t(kLeaf))
+                    ring[r[b] & (kRing - 1)] = v[b];
+            __syncwarp();
+            while (have - used >= uint32_t(kSlots) && used < uint32_t(kLeaf)) {
+                fold(kSlots);
+                used += kSlots;
+            }
+            __syncwarp();
+        }
     }
+    if (have != uint32_t(cnt) && lane == 0)
+        atomicOr(a.err, 2u);  // the bitmap and the leaf starts disagree
+    if (have > used && used < uint32_t(kLeaf))
+        fold(int(have - used));  // the last leaf's short row
+    __syncwarp();
+    // the in-leaf tree over slots l + 32 i: offsets 128, 64, 32 in registers, then shuffles
+    const int live = cnt < kSlots ? cnt : kSlots;
+    P x[kSlotsPerLane];
+#pragma unroll
+    for (int i = 0; i < kSlotsPerLane; ++i)
+        x[i] = P{h[i], isfinite(h[i]) ? c[i] : 0.0};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        if (lane + 32 * i + 128 < live)
+            x[i] = P::join(x[i], x[i + 4]);
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        if (lane + 32 * i + 64 < live)
+            x[i] = P::join(x[i], x[i + 2]);
+    if (lane + 32 < live)
+        x[0] = P::join(x[0], x[1]);
+    P q = x[0];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const P o = q.shflDown(unsigned(off));
+        if (lane < off && lane + off < live)
+            q = P::join(q, o);
+    }
+    return q;
 }
 
-/** Words per thread for a leaf over [s0, s1): one chunk of 256 K words covers it
- *  when K <= kMaxK does. */
-__device__ __forceinline__ int wordsPerThread(int64_t s0, int64_t s1)
+/** Warps claim leaves off a counter and sum each alone (no CTA barrier anywhere).
+ *  A leaf's partial goes to leafPart; the warp that finishes the last leaf of an
+ *  aligned chunk of 512 runs the chunk's pairwise levels, and the warp that
+ *  finishes the last chunk the levels above, and stores the value. The next leaf's
+ *  value range, when dense, is pulled toward L2 while the current one is summed. */
+__global__ __launch_bounds__(kThreads, 3) void keptLeavesKernel(LeafArgs a)
 {
-    const int64_t words = ((s1 - 1) >> 5) - (s0 >> 5) + 1;
-    int K = 1;
-    while (K < kMaxK && int64_t(K) * kThreads < words)
-        K *= 2;
-    return K;
-}
-
-__global__ __launch_bounds__(kThreads, 4) void keptLeavesKernel(LeafArgs a)
-{
-    __shared__ __align__(16) int32_t idx[kLeaf];  // the leaf's kept samples by rank; the final levels reuse it
-    __shared__ P s[2][kSlots];      // the slot partials of the last two leaves
-    __shared__ P group[kMaxGroup];
-    __shared__ int32_t sStart[kMaxGroup + 1];
-    __shared__ uint32_t scan[33];
-    __shared__ uint32_t sGroup;
-    __shared__ int amLast;
-    const int t = int(threadIdx.x);
+    __shared__ double rings[kLeafWarps][kRing];
+    const int lane = int(threadIdx.x & 31), warp = int(threadIdx.x >> 5);
+    double* ring = rings[warp];
     const int64_t rows = int64_t(*a.count) > a.n ? 0 : int64_t(*a.count);
     const int64_t leaves = (rows + kLeaf - 1) / kLeaf;
-    int64_t gl = 1;  // leaves per group: a power of two, so a group is a subtree of the levels
-    while (gl < kMaxGroup && (leaves + gl - 1) / gl > int64_t(a.groupCap))
-        gl *= 2;
-    while (gl < kMaxGroup && (leaves + gl - 1) / gl > int64_t(gridDim.x) * kGroupsPerCta)
-        gl *= 2;
-    const int64_t groups = (leaves + gl - 1) / gl;
-    int parity = 0;  // the slot buffer the next in-leaf tree takes
-    for (;;) {
-        if (t == 0)
-            sGroup = atomicAdd(a.groupNext, 1u);
-        __syncthreads();
-        const int64_t g = int64_t(sGroup);
-        if (g >= groups)
-            break;
-        const int64_t l0 = g * gl;
-        const int64_t l1 = l0 + gl < leaves ? l0 + gl : leaves;
-        // the group's leaf starts, kept inside [0, n] so that any start reads in bounds
-        for (int64_t i = t; i <= l1 - l0; i += kThreads) {
-            int64_t v = l0 + i < leaves ? int64_t(a.leafStart[l0 + i]) : a.n;
-            v = v < 0 ? 0 : (v > a.n ? a.n : v);
-            sStart[i] = int32_t(v);
+    if (leaves == 0) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) {
+            a.out[0] = 0.0;
+            if (a.pairOut)
+                a.out[1] = 0.0;
         }
-        __syncthreads();  // sStart is read below; sGroup is rewritten only after a later barrier
-        uint32_t word[kMaxK];
-        {
-            const int64_t s0 = sStart[0] < a.n ? sStart[0] : a.n - 1;
-            const int64_t s1 = sStart[1] > s0 ? sStart[1] : s0 + 1;
-            leafWords(a.bitmap, s0 >> 5, wordsPerThread(s0, s1), s0, s1, word);
-        }
-        for (int64_t l = l0; l < l1; ++l) {
-            const int64_t s0 = sStart[l - l0] < a.n ? sStart[l - l0] : a.n - 1;
-            const int64_t s1 = sStart[l - l0 + 1] > s0 ? sStart[l - l0 + 1] : s0 + 1;
-            const int cnt = int(rows - l * kLeaf < kLeaf ? rows - l * kLeaf : kLeaf);
-            const int K = wordsPerThread(s0, s1);
-            const int64_t wEnd = ((s1 - 1) >> 5) + 1;
-            uint32_t base = 0;
-            for (int64_t cw = s0 >> 5;;) {
-                uint32_t mine = 0;
-#pragma unroll
-                for (int k = 0; k < kMaxK; ++k)
-                    mine += uint32_t(__popc(word[k]));
-                uint32_t total = 0;
-                uint32_t r = base + blockExclusiveSum(mine, total, scan);
-#pragma unroll
-                for (int k = 0; k < kMaxK; ++k) {
-                    uint32_t x = word[k];
-                    const int64_t sample0 = (cw + int64_t(t) * K + k) * 32;
-                    while (x != 0) {
-                        if (r < uint32_t(kLeaf))
-                            idx[r] = int32_t(sample0 + __ffs(int(x)) - 1);
-                        x &= x - 1u;
-                        ++r;
-                    }
-                }
-                base += total;
-                cw += int64_t(kThreads) * K;
-                if (cw >= wEnd)
-                    break;
-                leafWords(a.bitmap, cw, K, s0, s1, word);  // a sparse leaf's next chunk
-            }
-            if (t == 0 && int(base) != cnt)
-                atomicOr(a.err, 2u);  // the bitmap and the leaf starts disagree
-            __syncthreads();          // idx holds the leaf
-            if (l + 1 < l1) {         // the next leaf's first words go out now
-                const int64_t n0 = sStart[l - l0 + 1] < a.n ? sStart[l - l0 + 1] : a.n - 1;
-                const int64_t n1 = sStart[l - l0 + 2] > n0 ? sStart[l - l0 + 2] : n0 + 1;
-                leafWords(a.bitmap, n0 >> 5, wordsPerThread(n0, n1), n0, n1, word);
-            }
-            double v[kTerms];
-            if (cnt == int(kLeaf) && int(base) == cnt) {
-#pragma unroll
-                for (int i = 0; i < kTerms; ++i)
-                    v[i] = __ldg(a.values + idx[t + i * kSlots]);
-            } else {
-                const int have = int(base) < cnt ? int(base) : cnt;  // staged entries only
-#pragma unroll
-                for (int i = 0; i < kTerms; ++i)
-                    v[i] = t + i * kSlots < have ? __ldg(a.values + idx[t + i * kSlots]) : 0.0;
-            }
-            P slot = P::of(v[0]);
-#pragma unroll
-            for (int i = 1; i < kTerms; ++i)
-                if (t + i * kSlots < cnt)
-                    slot.add(v[i]);
-            const P q = leafTreeWarp0(slot, cnt < kSlots ? cnt : kSlots, s[parity]);
-            parity ^= 1;
-            if (t == 0)
-                group[l - l0] = q;
-        }
-        __syncthreads();
-        levels(group, int(l1 - l0));
-        if (t == 0)
-            a.partials[g] = group[0];
-    }
-    if (t == 0) {
-        __threadfence();
-        amLast = atomicAdd(a.done, 1u) == gridDim.x - 1;
-    }
-    __syncthreads();
-    if (!amLast)
         return;
-    __threadfence();
-    P* buf = reinterpret_cast<P*>(idx);
-    P* v = a.partials;
-    int64_t m = groups;
-    while (m > 1) {
-        const int64_t chunks = (m + kChunk - 1) / kChunk;
-        for (int64_t cc = 0; cc < chunks; ++cc) {
-            const int cnt = int(m - cc * kChunk < kChunk ? m - cc * kChunk : kChunk);
-            for (int i = t; i < cnt; i += kThreads)
-                buf[i] = v[cc * kChunk + i];
-            __syncthreads();
-            levels(buf, cnt);
-            if (t == 0)
-                v[cc] = buf[0];
-            __syncthreads();
-        }
-        m = chunks;
     }
-    if (t == 0) {
-        const bool failed = *a.err != 0u;
-        P r{0.0, 0.0};
-        if (groups > 0)
-            r = v[0];
-        const double nan = __longlong_as_double(0x7ff8000000000000ll);
-        if (a.pairOut) {
-            a.out[0] = failed ? nan : r.h;
-            a.out[1] = failed ? nan : (isfinite(r.h) ? r.c : 0.0);
-        } else {
-            a.out[0] = failed ? nan : (groups > 0 ? r.value() : 0.0);
+    const int64_t chunks = (leaves + kChunk - 1) / kChunk;
+    auto range = [&](int64_t l, int64_t& s0, int64_t& s1) {
+        // kept inside [0, n) whatever the starts hold, so a failed pass reads in bounds
+        s0 = a.leafStart[l];
+        s0 = s0 < 0 ? 0 : (s0 >= a.n ? a.n - 1 : s0);
+        s1 = l + 1 < leaves ? int64_t(a.leafStart[l + 1]) : a.n;
+        s1 = s1 <= s0 ? s0 + 1 : (s1 > a.n ? a.n : s1);
+    };
+    auto claim = [&]() -> int64_t {
+        uint32_t l = 0;
+        if (lane == 0)
+            l = atomicAdd(a.leafNext, 1u);
+        return int64_t(__shfl_sync(kFull, l, 0));
+    };
+    auto cntOf = [&](int64_t l) { return int(rows - l * kLeaf < kLeaf ? rows - l * kLeaf : kLeaf); };
+    int64_t l = claim();
+    if (l < leaves) {
+        int64_t s0, s1;
+        range(l, s0, s1);
+        prefetchLeafWarp(a.values, a.n, s0, s1, cntOf(l));
+    }
+    while (l < leaves) {
+        const int64_t next = claim();
+        if (next < leaves) {
+            int64_t n0, n1;
+            range(next, n0, n1);
+            prefetchLeafWarp(a.values, a.n, n0, n1, cntOf(next));
         }
-        if (failed)
-            *const_cast<uint32_t*>(a.count) = 0xffffffffu;
-        *a.groupNext = 0u;
-        *a.done = 0u;
+        int64_t s0, s1;
+        range(l, s0, s1);
+        const P q = sumLeaf(a, s0, s1, cntOf(l), ring);
+        const int64_t ch = l / kChunk;
+        const int inChunk = int(leaves - ch * kChunk < kChunk ? leaves - ch * kChunk : kChunk);
+        uint32_t last = 0;
+        if (lane == 0) {
+            a.leafPart[l] = q;
+            __threadfence();
+            last = atomicAdd(&a.chunkDone[ch], 1u) == uint32_t(inChunk - 1) ? 1u : 0u;
+        }
+        if (__shfl_sync(kFull, last, 0)) {
+            __threadfence();
+            const P cp = warpLevels(a.leafPart + ch * kChunk, inChunk);
+            uint32_t top = 0;
+            if (lane == 0) {
+                a.chunkPart[ch] = cp;
+                __threadfence();
+                top = atomicAdd(a.topDone, 1u) == uint32_t(chunks - 1) ? 1u : 0u;
+            }
+            if (__shfl_sync(kFull, top, 0)) {
+                __threadfence();
+                // the levels above the chunks: aligned runs of 512, then the level above
+                int64_t m = chunks;
+                P* v = a.chunkPart;
+                while (m > 1) {
+                    const int64_t runs = (m + kChunk - 1) / kChunk;
+                    for (int64_t rr = 0; rr < runs; ++rr) {
+                        const int cnt = int(m - rr * kChunk < kChunk ? m - rr * kChunk : kChunk);
+                        const P r = warpLevels(v + rr * kChunk, cnt);
+                        __syncwarp();
+                        if (lane == 0)
+                            v[rr] = r;
+                        __threadfence();
+                        __syncwarp();
+                    }
+                    m = runs;
+                }
+                if (lane == 0) {
+                    const P r{__ldcg(&v[0].h), __ldcg(&v[0].c)};
+                    const bool failed = *reinterpret_cast<volatile uint32_t*>(a.err) != 0u;
+                    const double nan = __longlong_as_double(0x7ff8000000000000ll);
+                    if (a.pairOut) {
+                        a.out[0] = failed ? nan : r.h;
+                        a.out[1] = failed ? nan : (isfinite(r.h) ? r.c : 0.0);
+                    } else {
+                        a.out[0] = failed ? nan : r.value();
+                    }
+                    if (failed)
+                        *const_cast<uint32_t*>(a.count) = 0xffffffffu;
+                }
+            }
+        }
+        l = next;
     }
 }
 
@@ -376,14 +464,15 @@ __global__ void compactSumEmptyKernel(uint32_t* count, double* out, int pairOut)
         out[1] = 0.0;
 }
 
-/** Scratch of one call over n samples: [3 counter words | pad] (zeroed by the
- *  call's memset), then the tile counts and offsets, the bitmap, the leaf starts
- *  and the group partials. */
+/** Scratch of one call over n samples: [leaf claim, chunks finished, error, pad |
+ *  leaves finished per chunk] (zeroed by the call's memset), then the tile counts
+ *  and offsets, the bitmap, the leaf starts, the leaf partials and the chunk
+ *  partials. */
 struct SumLayout {
     int64_t tiles = 0;
-    int64_t maxLeaves = 0;
-    uint32_t groupCap = 0;
-    size_t zeroed = 0, tileCount = 0, tileOff = 0, bitmap = 0, leafStart = 0, partials = 0, total = 0;
+    int64_t maxLeaves = 0, maxChunks = 0;
+    size_t zeroed = 0, tileCount = 0, tileOff = 0, bitmap = 0, leafStart = 0, leafPart = 0, chunkPart = 0,
+           total = 0;
 };
 
 size_t up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -405,21 +494,20 @@ int leavesGrid()
     return k * smCount();
 }
 
-SumLayout sumLayout(int64_t n, int grid)
+SumLayout sumLayout(int64_t n)
 {
     SumLayout L;
     L.tiles = n > 0 ? (n + kTile - 1) / kTile : 1;
     L.maxLeaves = (n + kLeaf - 1) / kLeaf;
-    const int64_t byGroup = (L.maxLeaves + kMaxGroup - 1) / kMaxGroup;
-    const int64_t target = int64_t(grid) * kGroupsPerCta;
-    L.groupCap = uint32_t((byGroup > target ? byGroup : target) + 1);
-    L.zeroed = 4 * sizeof(uint32_t);
-    L.tileCount = 256;
+    L.maxChunks = (L.maxLeaves + kChunk - 1) / kChunk;
+    L.zeroed = up(size_t(4 + L.maxChunks) * sizeof(uint32_t), 16);
+    L.tileCount = up(L.zeroed, 256);
     L.tileOff = up(L.tileCount + size_t(L.tiles) * sizeof(uint32_t), 256);
     L.bitmap = up(L.tileOff + size_t(L.tiles) * sizeof(uint32_t), 256);
     L.leafStart = up(L.bitmap + size_t(L.tiles) * kTileWords * sizeof(uint32_t), 256);
-    L.partials = up(L.leafStart + size_t(L.maxLeaves + 1) * sizeof(int32_t), 256);
-    L.total = up(L.partials + size_t(L.groupCap) * sizeof(P), 256);
+    L.leafPart = up(L.leafStart + size_t(L.maxLeaves + 1) * sizeof(int32_t), 256);
+    L.chunkPart = up(L.leafPart + size_t(L.maxLeaves > 0 ? L.maxLeaves : 1) * sizeof(P), 256);
+    L.total = up(L.chunkPart + size_t(L.maxChunks > 0 ? L.maxChunks : 1) * sizeof(P), 256);
     return L;
 }
 
@@ -446,9 +534,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
             unsupported(std::string(who) + ": writes no index map (eagle_backend_compact_device does)");
         if (d.live32 != 0)
             unsupported(std::string(who) + ": the reorder trigger is not offered with the fused sum");
-        const int dev = resolveDevice(d.device, d.mask != 0 ? d.mask : (d.count != 0 ? d.count : out));
-        DeviceScope scope(dev);
-        const SumLayout L = sumLayout(d.n, leavesGrid());
+        const SumLayout L = sumLayout(d.n);
         if (d.scratch == 0) {
             constexpr size_t end = offsetof(eagle_backend_compact_desc, scratch_bytes) + sizeof(int64_t);
             if (desc->struct_size < end)
@@ -462,6 +548,8 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
             invalid(std::string(who) + ": values and out must be 8-byte aligned float64 arrays");
         if ((d.scratch & 255u) != 0)
             invalid(std::string(who) + ": scratch must be 256-byte aligned");
+        const int dev = resolveDevice(d.device, d.mask != 0 ? d.mask : d.count);
+        DeviceScope scope(dev);
         const cudaStream_t s = seamStream(d.stream);
         const int pairOut = (flags & EAGLE_BACKEND_REDUCE_PAIR_OUT) ? 1 : 0;
         if (d.n == 0) {
@@ -483,11 +571,12 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
         la.count = count;
         la.values = reinterpret_cast<const double*>(values);
         la.n = d.n;
-        la.partials = reinterpret_cast<P*>(base + L.partials);
-        la.groupCap = L.groupCap;
-        la.groupNext = words;
-        la.done = words + 1;
+        la.leafPart = reinterpret_cast<P*>(base + L.leafPart);
+        la.chunkPart = reinterpret_cast<P*>(base + L.chunkPart);
+        la.leafNext = words;
+        la.topDone = words + 1;
         la.err = words + 2;
+        la.chunkDone = words + 4;
         la.out = reinterpret_cast<double*>(out);
         la.pairOut = pairOut;
         cudaCheck(cudaMemsetAsync(base, 0, L.zeroed, s), "cudaMemsetAsync");

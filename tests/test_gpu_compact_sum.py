@@ -65,6 +65,31 @@ def test_fused_sum_on_edge_masks(eb, orc, n):
         assert got.tobytes() == want.tobytes(), (n, name)
 
 
+@pytest.mark.parametrize("case", ("inf", "-inf then inf", "nan", "huge"))
+def test_fused_sum_non_finite(eb, orc, case):
+    """Infinities and NaNs among the kept values: a slot whose hi leaves the finite
+    range ends with a zero comp, exactly as the step-by-step join gives it."""
+    n = 3 * 4096 * 5 + 123
+    x = orc.corpus(n, 77)
+    keep = np.random.default_rng(78).random(n) < 0.7
+    kept_at = np.flatnonzero(keep)
+    if case == "inf":
+        x[kept_at[[5, 4096 + 300]]] = np.inf
+    elif case == "-inf then inf":
+        x[kept_at[[17, 17 + 256 * 3]]] = (-np.inf, np.inf)
+    elif case == "nan":
+        x[kept_at[[0, 9000]]] = np.nan
+    else:
+        x[kept_at[::97]] = 1.7e308
+    cs = eb.CompactSum(torch.from_numpy(keep).cuda(), torch.from_numpy(x).cuda(), pair_out=True)
+    got = cs().cpu().numpy()
+    want = orc.reduce(x[keep], pair_out=True)
+    if np.isnan(want[0]):  # a NaN's payload is the hardware's; that it is NaN, and comp 0, is the contract
+        assert np.isnan(got[0]) and got[1] == 0.0, case
+    else:
+        assert got.tobytes() == want.tobytes(), case
+
+
 def test_fused_sum_unaligned_mask(eb, orc):
     """A mask that does not start on a 16-byte boundary takes the byte-wise loads."""
     n = 200_003
