@@ -17,15 +17,20 @@
 //   leafStartKernel   a warp per tile: for every multiple of 4096 among the tile's
 //                     ranks, the sample holding it (leafStart[l]), from the tile's
 //                     512 bitmap words.
-//   keptLeavesKernel  CTAs claim groups of 2^q consecutive leaves. Per leaf: the
-//                     bitmap words over [leafStart[l], leafStart[l + 1]) are scanned
-//                     across the CTA, the kept sample indices staged in shared memory
-//                     by rank, then thread t loads the values of ranks t + 256 i,
-//                     i = 0..15, together and folds them into slot t's partial in
-//                     order -- the leaf walk, term by term -- before one warp runs the
-//                     in-leaf tree. The next leaf's words are in flight meanwhile. A
-//                     group's leaves join by the pairwise levels; the last CTA runs
-//                     the remaining levels over the group partials.
+//   keptDenseKernel   warps claim leaves. A leaf spanning at most 4 samples per
+//                     survivor is summed by the one warp: bitmap words 32 at a time,
+//                     each kept value copied by cp.async straight into a per-warp
+//                     ring at its rank (three batches in flight, no register held),
+//                     every full row of 256 ranks folded slot by slot in rank order,
+//                     and the in-leaf tree in registers and shuffles. Sparser leaves
+//                     go on a list.
+//   keptSparseKernel  CTAs take the listed leaves one at a time: a CTA scan of the
+//                     leaf's bitmap words, the kept sample indices staged in shared
+//                     memory by rank, each thread loading its slot's 16 values
+//                     together, one warp running the in-leaf tree.
+//   The warp that finishes the last leaf of an aligned chunk of 512 joins the
+//   chunk's leaves by the pairwise levels; the one that finishes the last chunk,
+//   the chunks, and stores the value. No CTA ever waits on another.
 //
 // Traffic: the mask (n bytes), the bitmap written and read (n / 4 bytes), the value
 // sectors holding a survivor; the bits are those of the two-kernel compaction +
@@ -179,64 +184,128 @@ __global__ __launch_bounds__(kThreads) void leafStartKernel(const uint32_t* __re
 }
 
 
-/** Pulls the values of samples [s0, s1) into L2 (128-byte lines spread over the
- *  warp) when the range is dense enough that nearly all of its sectors will be
- *  read: at most two samples per survivor. The lines stay inside the values. */
-__device__ __forceinline__ void prefetchLeafWarp(const double* values, int64_t n, int64_t s0, int64_t s1, int cnt)
-{
-    if (s1 - s0 > 2 * int64_t(cnt))
-        return;
-    const uintptr_t lo = reinterpret_cast<uintptr_t>(values);
-    const uintptr_t hi = lo + uintptr_t(n) * sizeof(double);
-    uintptr_t p = reinterpret_cast<uintptr_t>(values + s0) & ~uintptr_t(127);
-    const uintptr_t e = reinterpret_cast<uintptr_t>(values + s1);
-    for (p += uintptr_t(threadIdx.x & 31) * 128; p < e; p += 32 * 128)
-        if (p >= lo && p < hi)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
 struct LeafArgs {
     const uint32_t* bitmap;
     const int32_t* leafStart;
     const uint32_t* count;
     const double* values;
     int64_t n;
-    P* leafPart;          // one partial per leaf
-    P* chunkPart;         // one per aligned chunk of kChunk leaves
-    uint32_t* chunkDone;  // leaves finished per chunk, zero on entry
-    uint32_t* topDone;    // chunks finished, zero on entry
-    uint32_t* leafNext;   // the leaf claim counter, zero on entry
-    uint32_t* err;        // zero on entry
+    P* leafPart;           // one partial per leaf
+    P* chunkPart;          // one per aligned chunk of kChunk leaves
+    uint32_t* chunkDone;   // leaves finished per chunk, zero on entry
+    uint32_t* topDone;     // chunks finished, zero on entry
+    uint32_t* leafNext;    // the dense pass's claim counter over all leaves, zero on entry
+    int32_t* sparseList;   // the leaves the dense pass hands on
+    uint32_t* sparseCount; // zero on entry
+    uint32_t* sparseNext;  // the sparse pass's claim counter, zero on entry
+    uint32_t* err;         // zero on entry
     double* out;
     int pairOut;
 };
 
-constexpr int kLeafWarps = kThreads / 32;
-constexpr int kRing = 512;      // a warp's staged values: under 256 waiting + 8 words' worth
-constexpr int kBatchWords = 8;  // non-empty bitmap words whose values a lane loads together
+constexpr int kDenseThreads = 128;          // four warps, one leaf each
+constexpr int kDenseWarps = kDenseThreads / 32;
+constexpr int kRing = 1024;                 // a warp's staged values (see sumDenseLeaf)
+constexpr int kBatchWords = 8;              // non-empty bitmap words per async batch
+constexpr int kInflight = 3;                // async batches a warp keeps in flight (land0..2)
 constexpr int kSlotsPerLane = kSlots / 32;
+constexpr int kMaxK = 4;                    // bitmap words per thread per chunk (sparse pass)
+constexpr int64_t kDenseSpan = 4;           // a leaf is dense when it spans at most 4 samples per survivor
+
+/** ``cp.async`` of one float64 from global to shared memory when ``pred`` (the
+ *  copy lands asynchronously; cpWait orders it). */
+__device__ __forceinline__ void cpAsync8(double* dst, const double* src, bool pred)
+{
+    const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n @p cp.async.ca.shared.global [%0], [%1], 8;\n}\n" ::"r"(d),
+        "l"(src), "r"(int(pred))
+        : "memory");
+}
+__device__ __forceinline__ void cpCommit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+/** Waits until at most ``pending`` of this thread's committed groups are in flight. */
+__device__ __forceinline__ void cpWait(int pending)
+{
+    if (pending <= 0)
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    else if (pending == 1)
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    else
+        asm volatile("cp.async.wait_group 2;\n" ::: "memory");
+}
+
+/** One slot's fold of term ``x``: the join with (x, 0) without its non-finite test,
+ *  which the caller applies once at the end (hi, once infinite or NaN, stays so and
+ *  the comp ends zero; while hi is finite the comp is never -0, so the join's
+ *  ``comp + 0`` is exact and dropped). ``first`` starts the slot at (x, 0). */
+__device__ __forceinline__ void foldTerm(double& h, double& c, double x, bool first)
+{
+    if (first) {
+        h = x;
+        c = 0.0;
+    } else {
+        const double sum = h + x;
+        const double bb = sum - h;
+        const double e = (h - (sum - bb)) + (x - bb);
+        c = c + e;
+        h = sum;
+    }
+}
+
+/** Bitmap word ``w`` of a leaf whose samples are [s0, s1) (0 outside [w0, wEnd)),
+ *  its bits outside the leaf cleared: they belong to its neighbours. */
+__device__ __forceinline__ uint32_t leafWord(const uint32_t* __restrict__ bitmap, int64_t w, int64_t s0, int64_t s1)
+{
+    const int64_t w0 = s0 >> 5, wEnd = ((s1 - 1) >> 5) + 1;
+    uint32_t x = 0;
+    if (w >= w0 && w < wEnd) {
+        x = bitmap[w];
+        if (w == w0)
+            x &= ~0u << (s0 & 31);
+        if (w == wEnd - 1) {
+            const int e = int((s1 - 1) & 31);
+            x &= e == 31 ? ~0u : ((2u << e) - 1u);
+        }
+    }
+    return x;
+}
+
+/** A leaf's sample range, kept inside [0, n) whatever the starts hold, so that a
+ *  failed pass still reads in bounds. */
+__device__ __forceinline__ void leafRange(const LeafArgs& a, int64_t l, int64_t leaves, int64_t& s0, int64_t& s1)
+{
+    s0 = a.leafStart[l];
+    s0 = s0 < 0 ? 0 : (s0 >= a.n ? a.n - 1 : s0);
+    s1 = l + 1 < leaves ? int64_t(a.leafStart[l + 1]) : a.n;
+    s1 = s1 <= s0 ? s0 + 1 : (s1 > a.n ? a.n : s1);
+}
 
 /** Pairwise levels over ``m <= 512`` partials at ``in`` (an aligned 512-node
- *  subtree), by one warp: lane l takes nodes [16 l, 16 l + 16) and joins them in
- *  registers (offsets 1..8), then lanes pair up by shuffles (offsets 16..256): the
- *  pairs and order of ``levels``. Result in lane 0. Reads through L2, so partials
- *  that other CTAs published before their counter increment are seen. */
+ *  subtree), by one warp: lane l takes nodes [16 l, 16 l + 16) as two runs of 8,
+ *  joins each run in registers (offsets 1, 2, 4) and the two runs (offset 8), then
+ *  lanes pair up by shuffles (offsets 16..256): the pairs and order of ``levels``.
+ *  Result in lane 0. Reads through L2, so partials other CTAs published before
+ *  their counter increment are seen. */
 __device__ __forceinline__ P warpLevels(const P* in, int m)
 {
     const int lane = int(threadIdx.x & 31);
-    P x[16];
+    P run[2];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const int i = lane * 16 + j;
-        x[j] = i < m ? P{__ldcg(&in[i].h), __ldcg(&in[i].c)} : P{};
+    for (int half = 0; half < 2; ++half) {
+        const int i0 = lane * 16 + half * 8;
+        P x[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            x[j] = i0 + j < m ? P{__ldcg(&in[i0 + j].h), __ldcg(&in[i0 + j].c)} : P{};
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1)
+#pragma unroll
+            for (int j = 0; j < 8; j += 2 * off)
+                if (i0 + j + off < m)
+                    x[j] = P::join(x[j], x[j + off]);
+        run[half] = x[0];
     }
-#pragma unroll
-    for (int off = 1; off < 16; off <<= 1)
-#pragma unroll
-        for (int j = 0; j < 16; j += 2 * off)
-            if (lane * 16 + j + off < m)
-                x[j] = P::join(x[j], x[j + off]);
-    P q = x[0];
+    P q = lane * 16 + 8 < m ? P::join(run[0], run[1]) : run[0];
 #pragma unroll
     for (int lo = 1; lo < 32; lo <<= 1) {
         const P o = q.shflDown(unsigned(lo));
@@ -246,87 +315,72 @@ __device__ __forceinline__ P warpLevels(const P* in, int m)
     return q;
 }
 
-/** One warp sums one leaf: the samples [s0, s1) hold its ``cnt`` survivors. Lane l
- *  owns slots l + 32 i (i < 8). The bitmap words go 32 at a time (one per lane); the
- *  non-empty ones 8 at a time, each lane loading the value of its bit in each (one
- *  coalesced 256-byte row per word), into a ring at the value's rank; every full
- *  row of 256 ranks is folded, slot by slot, in rank order. The fold skips the
- *  non-finite test of each step and applies it once at the end: once a slot's hi
- *  is infinite or NaN it stays so, and its comp ends zero either way; while hi is
- *  finite the comp of a join with (x, 0) is never -0, so adding that 0 is exact. */
-__device__ __forceinline__ P sumLeaf(const LeafArgs& a, int64_t s0, int64_t s1, int cnt, double* ring)
+/** Called by one whole warp once leaf ``l``'s partial ``q`` (valid in lane 0) is
+ *  known: stores it, and the warp that finishes the last leaf of an aligned chunk
+ *  of 512 runs that chunk's pairwise levels; the warp that finishes the last chunk
+ *  runs the levels above and stores the value. Counters are bumped after a
+ *  __threadfence and partials read through L2, so either pass may finish a chunk. */
+__device__ __forceinline__ void finishLeaf(const LeafArgs& a, int64_t l, int64_t leaves, const P& q)
 {
     const int lane = int(threadIdx.x & 31);
-    const uint32_t below = (1u << lane) - 1u;
-    const int64_t w0 = s0 >> 5, wEnd = ((s1 - 1) >> 5) + 1;
-    double h[kSlotsPerLane], c[kSlotsPerLane];
-#pragma unroll
-    for (int i = 0; i < kSlotsPerLane; ++i)
-        h[i] = c[i] = 0.0;
-    uint32_t have = 0, used = 0;  // ranks staged, ranks folded (warp-uniform)
-    auto fold = [&](int live) {   // the row at ``used``: slots below ``live`` take a term
-        const bool first = used == 0;
-#pragma unroll
-        for (int i = 0; i < kSlotsPerLane; ++i) {
-            if (lane + 32 * i < live) {
-                const double x = ring[(used + uint32_t(lane + 32 * i)) & (kRing - 1)];
-                if (first) {
-                    h[i] = x;
-                } else {
-                    const double sum = h[i] + x;
-                    const double bb = sum - h[i];
-                    const double e = (h[i] - (sum - bb)) + (x - bb);
-                    c[i] = c[i] + e;
-                    h[i] = sum;
-                }
-            }
-        }
-    };
-    for (int64_t wb = w0; wb < wEnd; wb += 32) {
-        uint32_t word = 0;
-        const int64_t w = wb + lane;
-        if (w < wEnd) {
-            word = a.bitmap[w];
-            if (w == w0)
-                word &= ~0u << (s0 & 31);
-            if (w == wEnd - 1) {
-                const int e = int((s1 - 1) & 31);
-                word &= e == 31 ? ~0u : ((2u << e) - 1u);
-            }
-        }
-        uint32_t nz = __ballot_sync(kFull, word != 0);
-        while (nz != 0) {
-            double v[kBatchWords];
-            uint32_t r[kBatchWords];
-#pragma unroll
-            for (int b = 0; b < kBatchWords; ++b) {
-                const int src = nz != 0 ? __ffs(int(nz)) - 1 : 0;
-                const uint32_t wd = __shfl_sync(kFull, word, src) & (nz != 0 ? ~0u : 0u);
-                nz &= nz - 1u;
-                const bool mine = (wd >> lane) & 1u;
-                r[b] = mine ? have + uint32_t(__popc(wd & below)) : 0xffffffffu;
-                v[b] = mine ? __ldg(a.values + (wb + src) * 32 + lane) : 0.0;
-                have += uint32_t(__popc(wd));
-            }
-#pragma unroll
-            for (int b = 0; b < kBatchWords; ++b)
-                if (r[b] < uint32_t(kLeaf))
-                    ring[r[b] & (kRing - 1)] = v[b];
-            __syncwarp();
-            while (have - used >= uint32_t(kSlots) && used < uint32_t(kLeaf)) {
-                fold(kSlots);
-                used += kSlots;
-            }
-            __syncwarp();
-        }
+    const int64_t chunks = (leaves + kChunk - 1) / kChunk;
+    const int64_t ch = l / kChunk;
+    const int inChunk = int(leaves - ch * kChunk < kChunk ? leaves - ch * kChunk : kChunk);
+    uint32_t last = 0;
+    if (lane == 0) {
+        a.leafPart[l] = q;
+        __threadfence();
+        last = atomicAdd(&a.chunkDone[ch], 1u) == uint32_t(inChunk - 1) ? 1u : 0u;
     }
-    if (have != uint32_t(cnt) && lane == 0)
-        atomicOr(a.err, 2u);  // the bitmap and the leaf starts disagree
-    if (have > used && used < uint32_t(kLeaf))
-        fold(int(have - used));  // the last leaf's short row
-    __syncwarp();
-    // the in-leaf tree over slots l + 32 i: offsets 128, 64, 32 in registers, then shuffles
-    const int live = cnt < kSlots ? cnt : kSlots;
+    if (!__shfl_sync(kFull, last, 0))
+        return;
+    __threadfence();
+    const P cp = warpLevels(a.leafPart + ch * kChunk, inChunk);
+    uint32_t top = 0;
+    if (lane == 0) {
+        a.chunkPart[ch] = cp;
+        __threadfence();
+        top = atomicAdd(a.topDone, 1u) == uint32_t(chunks - 1) ? 1u : 0u;
+    }
+    if (!__shfl_sync(kFull, top, 0))
+        return;
+    __threadfence();
+    int64_t m = chunks;  // the levels above the chunks: aligned runs of 512, then the level above
+    P* v = a.chunkPart;
+    while (m > 1) {
+        const int64_t runs = (m + kChunk - 1) / kChunk;
+        for (int64_t rr = 0; rr < runs; ++rr) {
+            const int cnt = int(m - rr * kChunk < kChunk ? m - rr * kChunk : kChunk);
+            const P r = warpLevels(v + rr * kChunk, cnt);
+            __syncwarp();
+            if (lane == 0)
+                v[rr] = r;
+            __threadfence();
+            __syncwarp();
+        }
+        m = runs;
+    }
+    if (lane == 0) {
+        const P r{__ldcg(&v[0].h), __ldcg(&v[0].c)};
+        const bool failed = *reinterpret_cast<volatile uint32_t*>(a.err) != 0u;
+        const double nan = __longlong_as_double(0x7ff8000000000000ll);
+        if (a.pairOut) {
+            a.out[0] = failed ? nan : r.h;
+            a.out[1] = failed ? nan : (isfinite(r.h) ? r.c : 0.0);
+        } else {
+            a.out[0] = failed ? nan : r.value();
+        }
+        if (failed)
+            *const_cast<uint32_t*>(a.count) = 0xffffffffu;
+    }
+}
+
+/** The in-leaf tree over the slots a warp holds in registers (lane l: slots
+ *  l + 32 i, i < 8): offsets 128, 64, 32 inside each lane, then shuffles 16..1 --
+ *  the pairs and order of leafTree. Result in lane 0. */
+__device__ __forceinline__ P warpLeafTree(const double (&h)[kSlotsPerLane], const double (&c)[kSlotsPerLane], int live)
+{
+    const int lane = int(threadIdx.x & 31);
     P x[kSlotsPerLane];
 #pragma unroll
     for (int i = 0; i < kSlotsPerLane; ++i)
@@ -351,16 +405,89 @@ __device__ __forceinline__ P sumLeaf(const LeafArgs& a, int64_t s0, int64_t s1, 
     return q;
 }
 
-/** Warps claim leaves off a counter and sum each alone (no CTA barrier anywhere).
- *  A leaf's partial goes to leafPart; the warp that finishes the last leaf of an
- *  aligned chunk of 512 runs the chunk's pairwise levels, and the warp that
- *  finishes the last chunk the levels above, and stores the value. The next leaf's
- *  value range, when dense, is pulled toward L2 while the current one is summed. */
-__global__ __launch_bounds__(kThreads, 3) void keptLeavesKernel(LeafArgs a)
+/** One warp sums one dense leaf (samples [s0, s1) holding its ``cnt`` survivors).
+ *  The bitmap words go 32 at a time, one per lane, the next 32 already in flight;
+ *  the non-empty ones 8 at a time, each lane copying the value of its bit in each
+ *  (one coalesced row of 32 samples per word) with cp.async straight into a ring
+ *  at the value's rank -- no register holds a value in flight, so a warp keeps
+ *  three batches (up to 6 KB) under way. When the oldest batch has landed, every
+ *  full row of 256 ranks below it is folded: lane l folds slots l + 32 i in rank
+ *  order. The ring holds under 256 folded-pending ranks plus three batches of at
+ *  most 256, so 1024 entries never wrap onto a live one. */
+__device__ __forceinline__ P sumDenseLeaf(const LeafArgs& a, int64_t s0, int64_t s1, int cnt, double* ring)
 {
-    __shared__ double rings[kLeafWarps][kRing];
-    const int lane = int(threadIdx.x & 31), warp = int(threadIdx.x >> 5);
-    double* ring = rings[warp];
+    const int lane = int(threadIdx.x & 31);
+    const uint32_t below = (1u << lane) - 1u;
+    const int64_t w0 = s0 >> 5, wEnd = ((s1 - 1) >> 5) + 1;
+    double h[kSlotsPerLane], c[kSlotsPerLane];
+#pragma unroll
+    for (int i = 0; i < kSlotsPerLane; ++i)
+        h[i] = c[i] = 0.0;
+    uint32_t have = 0, used = 0;  // ranks issued, ranks folded (warp-uniform)
+    uint32_t land0 = 0, land1 = 0, land2 = 0;  // ``have`` after each batch in flight, oldest first
+    int inflight = 0;
+    auto foldUpTo = [&](uint32_t limit, int live) {
+        while (used + uint32_t(live) <= limit && used < uint32_t(kLeaf)) {
+#pragma unroll
+            for (int i = 0; i < kSlotsPerLane; ++i)
+                if (lane + 32 * i < live)
+                    foldTerm(h[i], c[i], ring[(used + uint32_t(lane + 32 * i)) & (kRing - 1)], used == 0);
+            used += uint32_t(kSlots);
+        }
+    };
+    uint32_t word = leafWord(a.bitmap, w0 + lane, s0, s1);
+    for (int64_t wb = w0; wb < wEnd; wb += 32) {
+        const uint32_t nextWord = leafWord(a.bitmap, wb + 32 + lane, s0, s1);
+        uint32_t nz = __ballot_sync(kFull, word != 0);
+        while (nz != 0) {
+#pragma unroll
+            for (int b = 0; b < kBatchWords; ++b) {
+                const int src = nz != 0 ? __ffs(int(nz)) - 1 : 0;
+                const uint32_t wd = __shfl_sync(kFull, word, src) & (nz != 0 ? ~0u : 0u);
+                nz &= nz - 1u;
+                const uint32_t r = have + uint32_t(__popc(wd & below));
+                cpAsync8(ring + (r & (kRing - 1)), a.values + (wb + src) * 32 + lane,
+                    ((wd >> lane) & 1u) != 0u && r < uint32_t(kLeaf));
+                have += uint32_t(__popc(wd));
+            }
+            cpCommit();
+            if (inflight == 0)
+                land0 = have;
+            else if (inflight == 1)
+                land1 = have;
+            else
+                land2 = have;
+            if (++inflight == kInflight) {  // the oldest batch has landed: fold below it
+                cpWait(kInflight - 1);
+                __syncwarp();
+                foldUpTo(land0, kSlots);
+                land0 = land1;
+                land1 = land2;
+                --inflight;
+                __syncwarp();
+            }
+        }
+        word = nextWord;
+    }
+    cpWait(0);
+    __syncwarp();
+    foldUpTo(have, kSlots);
+    if (have > used && used < uint32_t(kLeaf))
+        foldUpTo(have, int(have - used));  // the last leaf's short row
+    if (have != uint32_t(cnt) && lane == 0)
+        atomicOr(a.err, 2u);  // the bitmap and the leaf starts disagree
+    __syncwarp();             // the ring is rewritten by the next leaf
+    return warpLeafTree(h, c, cnt < kSlots ? cnt : kSlots);
+}
+
+/** The dense pass: warps claim leaves off a counter over all leaves; a leaf
+ *  spanning more than kDenseSpan samples per survivor goes on the sparse list for
+ *  the CTA pass, the others are summed here by one warp each. */
+__global__ __launch_bounds__(kDenseThreads, 6) void keptDenseKernel(LeafArgs a)
+{
+    __shared__ __align__(16) double rings[kDenseWarps][kRing];
+    const int lane = int(threadIdx.x & 31);
+    double* ring = rings[threadIdx.x >> 5];
     const int64_t rows = int64_t(*a.count) > a.n ? 0 : int64_t(*a.count);
     const int64_t leaves = (rows + kLeaf - 1) / kLeaf;
     if (leaves == 0) {
@@ -371,88 +498,123 @@ __global__ __launch_bounds__(kThreads, 3) void keptLeavesKernel(LeafArgs a)
         }
         return;
     }
-    const int64_t chunks = (leaves + kChunk - 1) / kChunk;
-    auto range = [&](int64_t l, int64_t& s0, int64_t& s1) {
-        // kept inside [0, n) whatever the starts hold, so a failed pass reads in bounds
-        s0 = a.leafStart[l];
-        s0 = s0 < 0 ? 0 : (s0 >= a.n ? a.n - 1 : s0);
-        s1 = l + 1 < leaves ? int64_t(a.leafStart[l + 1]) : a.n;
-        s1 = s1 <= s0 ? s0 + 1 : (s1 > a.n ? a.n : s1);
-    };
     auto claim = [&]() -> int64_t {
         uint32_t l = 0;
         if (lane == 0)
             l = atomicAdd(a.leafNext, 1u);
         return int64_t(__shfl_sync(kFull, l, 0));
     };
-    auto cntOf = [&](int64_t l) { return int(rows - l * kLeaf < kLeaf ? rows - l * kLeaf : kLeaf); };
-    int64_t l = claim();
-    if (l < leaves) {
+    int64_t next = claim();
+    while (next < leaves) {
+        const int64_t l = next;
+        next = claim();  // the next claim's round trip overlaps this leaf
         int64_t s0, s1;
-        range(l, s0, s1);
-        prefetchLeafWarp(a.values, a.n, s0, s1, cntOf(l));
+        leafRange(a, l, leaves, s0, s1);
+        const int cnt = int(rows - l * kLeaf < kLeaf ? rows - l * kLeaf : kLeaf);
+        if (s1 - s0 > kDenseSpan * int64_t(cnt)) {
+            if (lane == 0)
+                a.sparseList[atomicAdd(a.sparseCount, 1u)] = int32_t(l);
+            continue;
+        }
+        const P q = sumDenseLeaf(a, s0, s1, cnt, ring);
+        finishLeaf(a, l, leaves, q);
     }
-    while (l < leaves) {
-        const int64_t next = claim();
-        if (next < leaves) {
-            int64_t n0, n1;
-            range(next, n0, n1);
-            prefetchLeafWarp(a.values, a.n, n0, n1, cntOf(next));
+}
+
+/** Words per thread for a sparse leaf over [s0, s1): the smallest power of two up
+ *  to kMaxK whose chunk of 256 K words covers the leaf. */
+__device__ __forceinline__ int wordsPerThread(int64_t s0, int64_t s1)
+{
+    const int64_t words = ((s1 - 1) >> 5) - (s0 >> 5) + 1;
+    int K = 1;
+    while (K < kMaxK && int64_t(K) * kThreads < words)
+        K *= 2;
+    return K;
+}
+
+/** The sparse pass: CTAs take the leaves the dense pass listed, one leaf per CTA at
+ *  a time. Per chunk of 256 K bitmap words (the next chunk's words in flight): a
+ *  CTA scan of the words' counts and the kept sample indices staged in shared
+ *  memory by rank; then thread t loads the values of ranks t + 256 i, i < 16,
+ *  together (each in its own sector: the leaf is sparse) and folds them into slot
+ *  t in order; one warp runs the in-leaf tree and finishes the leaf. */
+__global__ __launch_bounds__(kThreads, 3) void keptSparseKernel(LeafArgs a)
+{
+    __shared__ __align__(16) int32_t idx[kLeaf];
+    __shared__ P s[2][kSlots];
+    __shared__ uint32_t scan[33];
+    __shared__ int64_t sLeaf;
+    const int t = int(threadIdx.x);
+    const int64_t rows = int64_t(*a.count) > a.n ? 0 : int64_t(*a.count);
+    const int64_t leaves = (rows + kLeaf - 1) / kLeaf;
+    if (leaves == 0)
+        return;
+    const uint32_t listed = *a.sparseCount;
+    int parity = 0;  // the slot buffer the next in-leaf tree takes
+    for (;;) {
+        if (t == 0) {
+            const uint32_t i = atomicAdd(a.sparseNext, 1u);
+            sLeaf = i < listed ? int64_t(a.sparseList[i]) : -1;
         }
+        __syncthreads();
+        const int64_t l = sLeaf;
+        __syncthreads();  // sLeaf is rewritten by the next claim
+        if (l < 0 || l >= leaves)
+            break;
         int64_t s0, s1;
-        range(l, s0, s1);
-        const P q = sumLeaf(a, s0, s1, cntOf(l), ring);
-        const int64_t ch = l / kChunk;
-        const int inChunk = int(leaves - ch * kChunk < kChunk ? leaves - ch * kChunk : kChunk);
-        uint32_t last = 0;
-        if (lane == 0) {
-            a.leafPart[l] = q;
-            __threadfence();
-            last = atomicAdd(&a.chunkDone[ch], 1u) == uint32_t(inChunk - 1) ? 1u : 0u;
-        }
-        if (__shfl_sync(kFull, last, 0)) {
-            __threadfence();
-            const P cp = warpLevels(a.leafPart + ch * kChunk, inChunk);
-            uint32_t top = 0;
-            if (lane == 0) {
-                a.chunkPart[ch] = cp;
-                __threadfence();
-                top = atomicAdd(a.topDone, 1u) == uint32_t(chunks - 1) ? 1u : 0u;
-            }
-            if (__shfl_sync(kFull, top, 0)) {
-                __threadfence();
-                // the levels above the chunks: aligned runs of 512, then the level above
-                int64_t m = chunks;
-                P* v = a.chunkPart;
-                while (m > 1) {
-                    const int64_t runs = (m + kChunk - 1) / kChunk;
-                    for (int64_t rr = 0; rr < runs; ++rr) {
-                        const int cnt = int(m - rr * kChunk < kChunk ? m - rr * kChunk : kChunk);
-                        const P r = warpLevels(v + rr * kChunk, cnt);
-                        __syncwarp();
-                        if (lane == 0)
-                            v[rr] = r;
-                        __threadfence();
-                        __syncwarp();
-                    }
-                    m = runs;
-                }
-                if (lane == 0) {
-                    const P r{__ldcg(&v[0].h), __ldcg(&v[0].c)};
-                    const bool failed = *reinterpret_cast<volatile uint32_t*>(a.err) != 0u;
-                    const double nan = __longlong_as_double(0x7ff8000000000000ll);
-                    if (a.pairOut) {
-                        a.out[0] = failed ? nan : r.h;
-                        a.out[1] = failed ? nan : (isfinite(r.h) ? r.c : 0.0);
-                    } else {
-                        a.out[0] = failed ? nan : r.value();
-                    }
-                    if (failed)
-                        *const_cast<uint32_t*>(a.count) = 0xffffffffu;
+        leafRange(a, l, leaves, s0, s1);
+        const int cnt = int(rows - l * kLeaf < kLeaf ? rows - l * kLeaf : kLeaf);
+        const int K = wordsPerThread(s0, s1);
+        const int64_t wEnd = ((s1 - 1) >> 5) + 1;
+        uint32_t word[kMaxK];
+#pragma unroll
+        for (int k = 0; k < kMaxK; ++k)
+            word[k] = k < K ? leafWord(a.bitmap, (s0 >> 5) + int64_t(t) * K + k, s0, s1) : 0u;
+        uint32_t base = 0;
+        for (int64_t cw = s0 >> 5; cw < wEnd; cw += int64_t(kThreads) * K) {
+            uint32_t next[kMaxK];
+#pragma unroll
+            for (int k = 0; k < kMaxK; ++k)
+                next[k] = k < K ? leafWord(a.bitmap, cw + int64_t(kThreads) * K + int64_t(t) * K + k, s0, s1) : 0u;
+            uint32_t mine = 0;
+#pragma unroll
+            for (int k = 0; k < kMaxK; ++k)
+                mine += uint32_t(__popc(word[k]));
+            uint32_t total = 0;
+            uint32_t r = base + blockExclusiveSum(mine, total, scan);
+#pragma unroll
+            for (int k = 0; k < kMaxK; ++k) {
+                uint32_t x = word[k];
+                const int64_t sample0 = (cw + int64_t(t) * K + k) * 32;
+                while (x != 0) {
+                    if (r < uint32_t(kLeaf))
+                        idx[r] = int32_t(sample0 + __ffs(int(x)) - 1);
+                    x &= x - 1u;
+                    ++r;
                 }
             }
+            base += total;
+#pragma unroll
+            for (int k = 0; k < kMaxK; ++k)
+                word[k] = next[k];
         }
-        l = next;
+        if (t == 0 && int(base) != cnt)
+            atomicOr(a.err, 2u);  // the bitmap and the leaf starts disagree
+        __syncthreads();          // idx holds the leaf
+        const int have = int(base) < cnt ? int(base) : cnt;  // staged entries only
+        double v[kTerms];
+#pragma unroll
+        for (int i = 0; i < kTerms; ++i)
+            v[i] = t + i * kSlots < have ? __ldg(a.values + idx[t + i * kSlots]) : 0.0;
+        double h = 0.0, c = 0.0;
+#pragma unroll
+        for (int i = 0; i < kTerms; ++i)
+            if (t + i * kSlots < cnt)
+                foldTerm(h, c, v[i], i == 0);
+        const P q = leafTreeWarp0(P{h, isfinite(h) ? c : 0.0}, cnt < kSlots ? cnt : kSlots, s[parity]);
+        parity ^= 1;
+        if ((t >> 5) == 0)
+            finishLeaf(a, l, leaves, q);
     }
 }
 
@@ -464,30 +626,36 @@ __global__ void compactSumEmptyKernel(uint32_t* count, double* out, int pairOut)
         out[1] = 0.0;
 }
 
-/** Scratch of one call over n samples: [leaf claim, chunks finished, error, pad |
- *  leaves finished per chunk] (zeroed by the call's memset), then the tile counts
- *  and offsets, the bitmap, the leaf starts, the leaf partials and the chunk
- *  partials. */
+/** Scratch of one call over n samples: [dense claim, chunks finished, error,
+ *  sparse listed, sparse claim, pad | leaves finished per chunk] (zeroed by the
+ *  call's memset), then the tile counts and offsets, the bitmap, the leaf starts,
+ *  the sparse list, the leaf partials and the chunk partials. */
 struct SumLayout {
     int64_t tiles = 0;
     int64_t maxLeaves = 0, maxChunks = 0;
-    size_t zeroed = 0, tileCount = 0, tileOff = 0, bitmap = 0, leafStart = 0, leafPart = 0, chunkPart = 0,
-           total = 0;
+    size_t zeroed = 0, tileCount = 0, tileOff = 0, bitmap = 0, leafStart = 0, sparseList = 0, leafPart = 0,
+           chunkPart = 0, total = 0;
 };
 
 size_t up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-int leavesGrid()
+/** Resident CTAs of the dense (which = 0) or sparse (1) pass on the current device:
+ *  both passes are persistent grids that claim their leaves. */
+int passGrid(int which)
 {
     static std::mutex mu;
-    static int perSm[64] = {};
+    static int perSm[64][2] = {};
     int dev = 0;
     cudaCheck(cudaGetDevice(&dev), "cudaGetDevice");
     std::lock_guard<std::mutex> lock(mu);
-    int& k = perSm[dev & 63];
+    int& k = perSm[dev & 63][which];
     if (k == 0) {
-        cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, keptLeavesKernel, kThreads, 0),
-            "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        if (which == 0)
+            cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, keptDenseKernel, kDenseThreads, 0),
+                "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        else
+            cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, keptSparseKernel, kThreads, 0),
+                "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
         if (k < 1)
             k = 1;
     }
@@ -500,12 +668,13 @@ SumLayout sumLayout(int64_t n)
     L.tiles = n > 0 ? (n + kTile - 1) / kTile : 1;
     L.maxLeaves = (n + kLeaf - 1) / kLeaf;
     L.maxChunks = (L.maxLeaves + kChunk - 1) / kChunk;
-    L.zeroed = up(size_t(4 + L.maxChunks) * sizeof(uint32_t), 16);
+    L.zeroed = up(size_t(8 + L.maxChunks) * sizeof(uint32_t), 16);
     L.tileCount = up(L.zeroed, 256);
     L.tileOff = up(L.tileCount + size_t(L.tiles) * sizeof(uint32_t), 256);
     L.bitmap = up(L.tileOff + size_t(L.tiles) * sizeof(uint32_t), 256);
     L.leafStart = up(L.bitmap + size_t(L.tiles) * kTileWords * sizeof(uint32_t), 256);
-    L.leafPart = up(L.leafStart + size_t(L.maxLeaves + 1) * sizeof(int32_t), 256);
+    L.sparseList = up(L.leafStart + size_t(L.maxLeaves + 1) * sizeof(int32_t), 256);
+    L.leafPart = up(L.sparseList + size_t(L.maxLeaves + 1) * sizeof(int32_t), 256);
     L.chunkPart = up(L.leafPart + size_t(L.maxLeaves > 0 ? L.maxLeaves : 1) * sizeof(P), 256);
     L.total = up(L.chunkPart + size_t(L.maxChunks > 0 ? L.maxChunks : 1) * sizeof(P), 256);
     return L;
@@ -576,7 +745,10 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
         la.leafNext = words;
         la.topDone = words + 1;
         la.err = words + 2;
-        la.chunkDone = words + 4;
+        la.sparseCount = words + 3;
+        la.sparseNext = words + 4;
+        la.chunkDone = words + 8;
+        la.sparseList = reinterpret_cast<int32_t*>(base + L.sparseList);
         la.out = reinterpret_cast<double*>(out);
         la.pairOut = pairOut;
         cudaCheck(cudaMemsetAsync(base, 0, L.zeroed, s), "cudaMemsetAsync");
@@ -598,7 +770,9 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
         leafStartKernel<<<unsigned(startCtas < startCap ? startCtas : startCap), kThreads, 0, s>>>(bitmap, tileCount,
             tileOff, L.tiles, leafStart);
         launchCheck(who);
-        keptLeavesKernel<<<unsigned(leavesGrid()), kThreads, 0, s>>>(la);
+        keptDenseKernel<<<unsigned(passGrid(0)), kDenseThreads, 0, s>>>(la);
+        launchCheck(who);
+        keptSparseKernel<<<unsigned(passGrid(1)), kThreads, 0, s>>>(la);
         launchCheck(who);
     });
 }
