@@ -17,7 +17,7 @@
 //   leafStartKernel   a warp per tile: for every multiple of 4096 among the tile's
 //                     ranks, the sample holding it (leafStart[l]), from the tile's
 //                     512 bitmap words.
-//   keptDenseKernel   warps claim leaves. A leaf spanning at most 4 samples per
+//   keptDenseKernel   warps claim leaves. A leaf spanning at most 16 samples per
 //                     survivor is summed by the one warp: bitmap words 32 at a time,
 //                     each kept value copied by cp.async straight into a per-warp
 //                     ring at its rank (three batches in flight, no register held),
@@ -210,7 +210,7 @@ constexpr int kBatchWords = 8;              // non-empty bitmap words per async 
 constexpr int kInflight = 3;                // async batches a warp keeps in flight (land0..2)
 constexpr int kSlotsPerLane = kSlots / 32;
 constexpr int kMaxK = 4;                    // bitmap words per thread per chunk (sparse pass)
-constexpr int64_t kDenseSpan = 4;           // a leaf is dense when it spans at most 4 samples per survivor
+constexpr int64_t kDenseSpan = 16;          // a leaf goes to a warp when it spans at most 16 samples per survivor
 
 /** ``cp.async`` of one float64 from global to shared memory when ``pred`` (the
  *  copy lands asynchronously; cpWait orders it). */
@@ -405,15 +405,17 @@ __device__ __forceinline__ P warpLeafTree(const double (&h)[kSlotsPerLane], cons
     return q;
 }
 
-/** One warp sums one dense leaf (samples [s0, s1) holding its ``cnt`` survivors).
- *  The bitmap words go 32 at a time, one per lane, the next 32 already in flight;
- *  the non-empty ones 8 at a time, each lane copying the value of its bit in each
- *  (one coalesced row of 32 samples per word) with cp.async straight into a ring
- *  at the value's rank -- no register holds a value in flight, so a warp keeps
- *  three batches (up to 6 KB) under way. When the oldest batch has landed, every
- *  full row of 256 ranks below it is folded: lane l folds slots l + 32 i in rank
- *  order. The ring holds under 256 folded-pending ranks plus three batches of at
- *  most 256, so 1024 entries never wrap onto a live one. */
+/** One warp sums one leaf (samples [s0, s1) holding its ``cnt`` survivors). The
+ *  bitmap words go 32 at a time, one per lane, the next two blocks already in
+ *  flight. Each kept value is copied with cp.async straight into a ring at its
+ *  rank -- no register holds a value in flight, so a warp keeps three batches of
+ *  at most 256 values under way. A block holding at most 256 survivors is one
+ *  batch, each lane walking its own word's bits; a fuller block is walked word by
+ *  word, lane l copying bit l of each (one coalesced row of 32 samples per word),
+ *  in batches of 8 words. When the oldest batch has landed, every full row of 256
+ *  ranks below it is folded: lane l folds slots l + 32 i in rank order. The ring
+ *  holds under 256 ranks waiting plus three batches of at most 256, so 1024
+ *  entries never wrap onto a live one. */
 __device__ __forceinline__ P sumDenseLeaf(const LeafArgs& a, int64_t s0, int64_t s1, int cnt, double* ring)
 {
     const int lane = int(threadIdx.x & 31);
@@ -423,57 +425,88 @@ __device__ __forceinline__ P sumDenseLeaf(const LeafArgs& a, int64_t s0, int64_t
 #pragma unroll
     for (int i = 0; i < kSlotsPerLane; ++i)
         h[i] = c[i] = 0.0;
-    uint32_t have = 0, used = 0;  // ranks issued, ranks folded (warp-uniform)
+    uint32_t have = 0, used = 0;                // ranks issued, ranks folded (warp-uniform)
     uint32_t land0 = 0, land1 = 0, land2 = 0;  // ``have`` after each batch in flight, oldest first
     int inflight = 0;
-    auto foldUpTo = [&](uint32_t limit, int live) {
-        while (used + uint32_t(live) <= limit && used < uint32_t(kLeaf)) {
+    auto foldRows = [&](uint32_t limit) {  // every full row below ``limit``
+        while (used + uint32_t(kSlots) <= limit && used < uint32_t(kLeaf)) {
+            const double* row = ring + (used & (kRing - 1)) + lane;
+            if (used == 0) {
 #pragma unroll
-            for (int i = 0; i < kSlotsPerLane; ++i)
-                if (lane + 32 * i < live)
-                    foldTerm(h[i], c[i], ring[(used + uint32_t(lane + 32 * i)) & (kRing - 1)], used == 0);
+                for (int i = 0; i < kSlotsPerLane; ++i)
+                    foldTerm(h[i], c[i], row[32 * i], true);
+            } else {
+#pragma unroll
+                for (int i = 0; i < kSlotsPerLane; ++i)
+                    foldTerm(h[i], c[i], row[32 * i], false);
+            }
             used += uint32_t(kSlots);
         }
     };
+    auto batchDone = [&]() {  // after each commit: fold below the oldest batch once three are out
+        cpCommit();
+        if (inflight == 0)
+            land0 = have;
+        else if (inflight == 1)
+            land1 = have;
+        else
+            land2 = have;
+        if (++inflight == kInflight) {
+            cpWait(kInflight - 1);
+            __syncwarp();
+            foldRows(land0);
+            land0 = land1;
+            land1 = land2;
+            --inflight;
+            __syncwarp();
+        }
+    };
     uint32_t word = leafWord(a.bitmap, w0 + lane, s0, s1);
+    uint32_t next1 = leafWord(a.bitmap, w0 + 32 + lane, s0, s1);
     for (int64_t wb = w0; wb < wEnd; wb += 32) {
-        const uint32_t nextWord = leafWord(a.bitmap, wb + 32 + lane, s0, s1);
-        uint32_t nz = __ballot_sync(kFull, word != 0);
-        while (nz != 0) {
+        const uint32_t next2 = leafWord(a.bitmap, wb + 64 + lane, s0, s1);  // two blocks ahead
+        const uint32_t pc = uint32_t(__popc(word));
+        const uint32_t incl = warpInclusiveSum(pc);
+        const uint32_t total = __shfl_sync(kFull, incl, 31);
+        if (total <= uint32_t(kSlots)) {
+            // a thin block: each lane walks its own word's bits (one batch of at most 256)
+            uint32_t r = have + incl - pc;
+            const double* src = a.values + (wb + lane) * 32;
+            for (uint32_t x = word; x != 0; x &= x - 1u, ++r)
+                cpAsync8(ring + (r & (kRing - 1)), src + (__ffs(int(x)) - 1), r < uint32_t(kLeaf));
+            __syncwarp();
+            have += total;
+            batchDone();
+        } else {
+            // a full block: the warp walks the words in order, lane l taking bit l
+            const double* src = a.values + wb * 32 + lane;
 #pragma unroll
-            for (int b = 0; b < kBatchWords; ++b) {
-                const int src = nz != 0 ? __ffs(int(nz)) - 1 : 0;
-                const uint32_t wd = __shfl_sync(kFull, word, src) & (nz != 0 ? ~0u : 0u);
-                nz &= nz - 1u;
-                const uint32_t r = have + uint32_t(__popc(wd & below));
-                cpAsync8(ring + (r & (kRing - 1)), a.values + (wb + src) * 32 + lane,
-                    ((wd >> lane) & 1u) != 0u && r < uint32_t(kLeaf));
-                have += uint32_t(__popc(wd));
-            }
-            cpCommit();
-            if (inflight == 0)
-                land0 = have;
-            else if (inflight == 1)
-                land1 = have;
-            else
-                land2 = have;
-            if (++inflight == kInflight) {  // the oldest batch has landed: fold below it
-                cpWait(kInflight - 1);
-                __syncwarp();
-                foldUpTo(land0, kSlots);
-                land0 = land1;
-                land1 = land2;
-                --inflight;
-                __syncwarp();
+            for (int k0 = 0; k0 < 32; k0 += kBatchWords) {
+#pragma unroll
+                for (int k = k0; k < k0 + kBatchWords; ++k) {
+                    const uint32_t wd = __shfl_sync(kFull, word, k);
+                    const uint32_t r = have + uint32_t(__popc(wd & below));
+                    cpAsync8(ring + (r & (kRing - 1)), src + k * 32,
+                        ((wd >> lane) & 1u) != 0u && r < uint32_t(kLeaf));
+                    have += uint32_t(__popc(wd));
+                }
+                batchDone();
             }
         }
-        word = nextWord;
+        word = next1;
+        next1 = next2;
     }
     cpWait(0);
     __syncwarp();
-    foldUpTo(have, kSlots);
-    if (have > used && used < uint32_t(kLeaf))
-        foldUpTo(have, int(have - used));  // the last leaf's short row
+    foldRows(have);
+    if (have > used && used < uint32_t(kLeaf)) {  // the last leaf's short row
+        const int live = int(have - used);
+        const double* row = ring + (used & (kRing - 1)) + lane;
+#pragma unroll
+        for (int i = 0; i < kSlotsPerLane; ++i)
+            if (lane + 32 * i < live)
+                foldTerm(h[i], c[i], row[32 * i], used == 0);
+    }
     if (have != uint32_t(cnt) && lane == 0)
         atomicOr(a.err, 2u);  // the bitmap and the leaf starts disagree
     __syncwarp();             // the ring is rewritten by the next leaf
