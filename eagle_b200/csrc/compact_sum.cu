@@ -17,7 +17,7 @@
 //   leafStartKernel   a warp per tile: for every multiple of 4096 among the tile's
 //                     ranks, the sample holding it (leafStart[l]), from the tile's
 //                     512 bitmap words.
-//   keptDenseKernel   warps claim leaves. A leaf spanning at most 16 samples per
+//   keptDenseKernel   warps claim leaves. A leaf spanning at most 4 samples per
 //                     survivor is summed by the one warp: bitmap words 32 at a time,
 //                     each kept value copied by cp.async straight into a per-warp
 //                     ring at its rank (three batches in flight, no register held),
@@ -129,6 +129,26 @@ __global__ __launch_bounds__(kScanThreads) void tileScanKernel(const uint32_t* _
         *count = carry;
 }
 
+/** The position of the ``r``-th set bit (from 0) of ``x``, which has more than r:
+ *  five halvings, each keeping the half the bit lies in. */
+__device__ __forceinline__ int selectBit(uint32_t x, uint32_t r)
+{
+    int pos = 0;
+#pragma unroll
+    for (int w = 16; w > 0; w >>= 1) {
+        const uint32_t lo = x & ((1u << w) - 1u);
+        const uint32_t c = uint32_t(__popc(lo));
+        if (r >= c) {
+            r -= c;
+            x >>= w;
+            pos += w;
+        } else {
+            x = lo;
+        }
+    }
+    return pos;
+}
+
 /** One warp per tile: every leaf whose first rank (a multiple of 4096) falls among
  *  the tile's kept samples gets that sample's index in ``leafStart``. Lane l holds
  *  the tile's words [16 l, 16 l + 16). */
@@ -168,10 +188,7 @@ __global__ __launch_bounds__(kThreads) void leafStartKernel(const uint32_t* __re
                     const uint32_t pc = uint32_t(__popc(w[k]));
                     if (at < 0) {
                         if (rem < pc) {
-                            uint32_t x = w[k];
-                            for (uint32_t d = rem; d > 0; --d)
-                                x &= x - 1u;  // drop the lowest kept sample
-                            at = (lane * 16 + k) * 32 + __ffs(int(x)) - 1;
+                            at = (lane * 16 + k) * 32 + selectBit(w[k], rem);
                         } else {
                             rem -= pc;
                         }
@@ -210,7 +227,7 @@ constexpr int kBatchWords = 8;              // non-empty bitmap words per async 
 constexpr int kInflight = 3;                // async batches a warp keeps in flight (land0..2)
 constexpr int kSlotsPerLane = kSlots / 32;
 constexpr int kMaxK = 4;                    // bitmap words per thread per chunk (sparse pass)
-constexpr int64_t kDenseSpan = 16;          // a leaf goes to a warp when it spans at most 16 samples per survivor
+constexpr int64_t kDenseSpan = 4;           // a leaf goes to a warp when it spans at most 4 samples per survivor
 
 /** ``cp.async`` of one float64 from global to shared memory when ``pred`` (the
  *  copy lands asynchronously; cpWait orders it). */
@@ -576,26 +593,35 @@ __global__ __launch_bounds__(kThreads, 3) void keptSparseKernel(LeafArgs a)
     __shared__ __align__(16) int32_t idx[kLeaf];
     __shared__ P s[2][kSlots];
     __shared__ uint32_t scan[33];
-    __shared__ int64_t sLeaf;
+    __shared__ int64_t sClaim[2][3];  // a claimed leaf and its sample range, two deep
     const int t = int(threadIdx.x);
     const int64_t rows = int64_t(*a.count) > a.n ? 0 : int64_t(*a.count);
     const int64_t leaves = (rows + kLeaf - 1) / kLeaf;
     if (leaves == 0)
         return;
     const uint32_t listed = *a.sparseCount;
+    auto claimInto = [&](int b) {  // one thread: the next listed leaf, or -1
+        const uint32_t i = atomicAdd(a.sparseNext, 1u);
+        int64_t l = i < listed ? int64_t(a.sparseList[i]) : -1;
+        l = l >= leaves ? -1 : l;
+        int64_t s0 = 0, s1 = 1;
+        if (l >= 0)
+            leafRange(a, l, leaves, s0, s1);
+        sClaim[b][0] = l;
+        sClaim[b][1] = s0;
+        sClaim[b][2] = s1;
+    };
+    if (t == 0)
+        claimInto(0);
+    __syncthreads();
     int parity = 0;  // the slot buffer the next in-leaf tree takes
-    for (;;) {
-        if (t == 0) {
-            const uint32_t i = atomicAdd(a.sparseNext, 1u);
-            sLeaf = i < listed ? int64_t(a.sparseList[i]) : -1;
-        }
-        __syncthreads();
-        const int64_t l = sLeaf;
-        __syncthreads();  // sLeaf is rewritten by the next claim
-        if (l < 0 || l >= leaves)
+    for (int cur = 0;; cur ^= 1) {
+        const int64_t l = sClaim[cur][0];
+        if (l < 0)
             break;
-        int64_t s0, s1;
-        leafRange(a, l, leaves, s0, s1);
+        const int64_t s0 = sClaim[cur][1], s1 = sClaim[cur][2];
+        if (t == 32)
+            claimInto(cur ^ 1);  // the next claim's round trips overlap this leaf
         const int cnt = int(rows - l * kLeaf < kLeaf ? rows - l * kLeaf : kLeaf);
         const int K = wordsPerThread(s0, s1);
         const int64_t wEnd = ((s1 - 1) >> 5) + 1;
@@ -648,6 +674,7 @@ __global__ __launch_bounds__(kThreads, 3) void keptSparseKernel(LeafArgs a)
         parity ^= 1;
         if ((t >> 5) == 0)
             finishLeaf(a, l, leaves, q);
+        __syncthreads();  // the next claim is visible; this one is rewritten a leaf later
     }
 }
 
