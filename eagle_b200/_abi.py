@@ -296,6 +296,7 @@ SIGNATURES = {
     "eagle_backend_x_b200_combine_partials": (_i32, [_u64, _i64, _u64, _u64, _u64]),
     "eagle_backend_x_b200_compact_gather": (_i32, [ctypes.POINTER(CompactDesc), _u64, _u64, _u32]),
     "eagle_backend_x_b200_reduce_counted": (_i32, [ctypes.POINTER(ReduceDesc), _u64]),
+    "eagle_backend_x_b200_reduce_fixed": (_i32, [ctypes.POINTER(ReduceDesc)]),
     "eagle_backend_x_b200_compact_sum": (_i32, [ctypes.POINTER(CompactDesc), _u64, _u64, _u32]),
     "eagle_backend_x_b200_engine_create": (_i32, [ctypes.POINTER(EngineDesc), ctypes.POINTER(_P)]),
     "eagle_backend_x_b200_engine_launch": (_i32, [_P, _u64]),

@@ -528,10 +528,13 @@ _POLICIES = {"compensated": _abi.REDUCE_COMPENSATED, "ordered": _abi.REDUCE_ORDE
 class Reducer:
     """A prepared canonical reduction of one (n, columns) CUDA plane: work buffers
     allocated once (the seam's query), so :meth:`__call__` only enqueues (and can be
-    captured in a CUDA graph)."""
+    captured in a CUDA graph). ``fixed=True`` sums float64 on eagle's 128-bit
+    fixed-point leaf (``eagle_backend_x_b200_reduce_fixed``), the path eagle takes on
+    devices whose FP32:FP64 ratio is 8 or worse; on such a device the plain call
+    takes it by itself."""
 
     def __init__(self, x, op: str = "sum", *, policy: str = "ordered", comp=None, pair_out: bool = False,
-                 out=None):
+                 out=None, fixed: bool = False):
         torch = _t()
         if not (isinstance(x, torch.Tensor) and x.is_cuda and x.is_contiguous()):
             raise ValueError("eagle_b200.reduce takes a contiguous CUDA tensor")
@@ -549,7 +552,11 @@ class Reducer:
         self.comp = comp
         if comp is not None:
             d.comp_in = _ptr(comp)
-        _abi.check(_abi.lib().eagle_backend_x_reduce_canonical(ctypes.byref(d)))  # query
+        if fixed and (d.dtype != _abi.REDUCE_F64 or d.op != _abi.REDUCE_OP_SUM or pair_out):
+            raise ValueError("the fixed-point leaf sums float64 and writes one value per column")
+        self._entry = _abi.lib().eagle_backend_x_b200_reduce_fixed if fixed else \
+            _abi.lib().eagle_backend_x_reduce_canonical
+        _abi.check(self._entry(ctypes.byref(d)))  # query
         elem = x.element_size()
         self.work_a = torch.empty(int(d.work_elems) * elem, dtype=torch.uint8, device=x.device)
         self.work_b = torch.empty(int(d.work_elems) * elem, dtype=torch.uint8, device=x.device)
@@ -563,14 +570,16 @@ class Reducer:
 
     def __call__(self, stream=None):
         self.desc.stream = _stream_handle(stream)
-        _abi.check(_abi.lib().eagle_backend_x_reduce_canonical(ctypes.byref(self.desc)))
+        _abi.check(self._entry(ctypes.byref(self.desc)))
         return self.out
 
 
-def reduce(x, op: str = "sum", *, policy: str = "ordered", comp=None, pair_out: bool = False, stream=None):
+def reduce(x, op: str = "sum", *, policy: str = "ordered", comp=None, pair_out: bool = False, fixed: bool = False,
+           stream=None):
     """The canonical reduction of each column of the CUDA plane ``x`` (python/eagle/_graph_reduce.py:98):
-    a tensor of ``columns`` results (``2 * columns`` with ``pair_out``: hi then comp)."""
-    return Reducer(x, op, policy=policy, comp=comp, pair_out=pair_out)(stream)
+    a tensor of ``columns`` results (``2 * columns`` with ``pair_out``: hi then comp); ``fixed``
+    takes the 128-bit fixed-point float64 leaf (eagle/reduce/canonical.h:153-313)."""
+    return Reducer(x, op, policy=policy, comp=comp, pair_out=pair_out, fixed=fixed)(stream)
 
 
 # ------------------------------------------------------------------------- filtering

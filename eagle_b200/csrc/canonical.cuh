@@ -42,6 +42,136 @@ struct CompP {  // a floating-point sum's partial (hi, comp)
     }
 };
 
+/** eagle's fixed-point partial of a float64 sum (canonical.h:153-302), the leaf it
+ *  takes on a device whose FP32:FP64 throughput ratio is 8 or worse (:304-313):
+ *  the value is v * 2^u, v a signed 128-bit integer held as (lo, hi). A term's
+ *  last mantissa bit lands at most 53 bits above the unit, kept 106 bits below the
+ *  largest term seen; a join aligns the units (floor shifts) and halves both sides
+ *  when either reaches 2^125. Infinities and NaN set sticky flags; value() rounds
+ *  once to nearest-even. All integer arithmetic: the bits do not depend on order of
+ *  evaluation beyond the tree's. */
+struct FixedP {
+    using I = __int128;
+    using U = unsigned __int128;
+    static constexpr int32_t kEmpty = -100000;  // the unit of a partial that saw no term
+    static constexpr int32_t kPosInf = 1, kNegInf = 2, kNan = 4;
+    uint64_t lo;
+    int64_t hi;
+    int32_t u, fl;
+
+    __device__ __forceinline__ I get() const { return I((U(uint64_t(hi)) << 64) | U(lo)); }
+    __device__ __forceinline__ void set(I v)
+    {
+        lo = uint64_t(U(v));
+        hi = int64_t(v >> 64);
+    }
+    static __device__ __forceinline__ I shr(I v, int32_t d) { return v >> (d < 127 ? d : 127); }
+    static __device__ __forceinline__ FixedP empty() { return FixedP{0, 0, kEmpty, 0}; }
+    static __device__ __forceinline__ FixedP of(double x)
+    {
+        FixedP p = empty();
+        p.add(x);
+        return p;
+    }
+    static __device__ __forceinline__ FixedP of(double x, double xc)
+    {
+        FixedP p = empty();
+        p.add(x);
+        p.add(xc);
+        return p;
+    }
+    __device__ __forceinline__ void add(double x, double xc)
+    {
+        add(x);
+        add(xc);
+    }
+    __device__ __forceinline__ void add(double x)
+    {
+        const uint64_t b = uint64_t(__double_as_longlong(x));
+        const int32_t e = int32_t((b >> 52) & 0x7ff);
+        if (e == 0x7ff) {
+            fl |= (b << 12) != 0 ? kNan : ((b >> 63) != 0 ? kNegInf : kPosInf);
+            return;
+        }
+        const uint64_t m = (b & 0xfffffffffffffull) | (e != 0 ? (1ull << 52) : 0ull);
+        if (m == 0)
+            return;
+        const int32_t ex = (e != 0 ? e : 1) - 1075;  // the weight of m's last bit
+        I v = get();
+        if (ex - 53 > u) {
+            v = shr(v, ex - 53 - u);
+            u = ex - 53;
+        }
+        const int32_t sh = ex - u;  // at most 53
+        const I t = sh >= 0 ? I(U(m) << sh) : (-sh < 64 ? I(m >> -sh) : I(0));
+        set((b >> 63) != 0 ? v - t : v + t);
+    }
+    static __device__ __forceinline__ bool wide(I z)
+    {
+        const I top = z >> 125;
+        return top != 0 && top != -1;
+    }
+    static __device__ __forceinline__ FixedP join(const FixedP& a, const FixedP& b)
+    {
+        I x = a.get(), y = b.get();
+        int32_t un = a.u;
+        if (b.u > un) {
+            x = shr(x, b.u - un);
+            un = b.u;
+        } else {
+            y = shr(y, un - b.u);
+        }
+        if (wide(x) || wide(y)) {
+            x >>= 1;
+            y >>= 1;
+            ++un;
+        }
+        FixedP o;
+        o.set(x + y);
+        o.u = un;
+        o.fl = a.fl | b.fl;
+        return o;
+    }
+    __device__ __forceinline__ double value() const
+    {
+        if (fl != 0) {
+            if ((fl & kNan) != 0 || (fl & (kPosInf | kNegInf)) == (kPosInf | kNegInf))
+                return __longlong_as_double(0x7ff8000000000000ll);
+            return __longlong_as_double((fl & kPosInf) != 0 ? 0x7ff0000000000000ll : int64_t(0xfff0000000000000ull));
+        }
+        const I v = get();
+        if (v == 0)
+            return 0.0;
+        const bool neg = v < 0;
+        const U mag = neg ? U(0) - U(v) : U(v);
+        const uint64_t mh = uint64_t(mag >> 64), ml = uint64_t(mag);
+        const int32_t lz = mh != 0 ? __clzll(int64_t(mh)) : 64 + __clzll(int64_t(ml));
+        const int32_t len = 128 - lz;
+        const int32_t sub = len + u + 1074;  // the bits of weight 2^-1074 and up
+        const int32_t keep = sub < 53 ? sub : 53;
+        const int32_t drop = len - keep;
+        double r;
+        if (drop <= 0) {
+            r = ldexp(double(uint64_t(mag)), u);
+        } else {
+            U q = drop < 128 ? mag >> drop : U(0);
+            const U rem = drop < 128 ? mag - (q << drop) : mag;
+            if (drop <= 128) {
+                const U half = U(1) << (drop - 1);
+                if (rem > half || (rem == half && (q & 1) != 0))
+                    ++q;
+            }
+            r = ldexp(double(uint64_t(q)), u + drop);
+        }
+        return neg ? -r : r;
+    }
+    __device__ __forceinline__ FixedP shflDown(unsigned off) const
+    {
+        return {__shfl_down_sync(kFull, lo, off), __shfl_down_sync(kFull, hi, off), __shfl_down_sync(kFull, u, off),
+            __shfl_down_sync(kFull, fl, off)};
+    }
+};
+
 /** The in-leaf tree over the slot partials (thread t < ``live`` holds slot t in
  *  ``mine``): offsets 128..32 through shared memory, 16..1 by warp shuffles, an
  *  absent partner carried. The leaf's partial is valid in thread 0. */

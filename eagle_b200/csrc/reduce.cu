@@ -345,7 +345,7 @@ void enqueueReduce(const eagle_backend_reduce_desc& d, int64_t cols, int pairOut
     for (int64_t c0 = 0; c0 < cols; c0 += 65535) {
         a.col0 = c0;
         const dim3 grid(unsigned(a.groups), unsigned(std::min<int64_t>(cols - c0, 65535)));
-        if constexpr (IsComp<P>::value) {
+        if constexpr (IsComp<P>::value || std::is_same_v<P, FixedP>) {
             if (hasComp)
                 canonicalKernel<P, T, true><<<grid, kSlots, 0, stream>>>(a);
             else
@@ -355,6 +355,18 @@ void enqueueReduce(const eagle_backend_reduce_desc& d, int64_t cols, int pairOut
         }
         launchCheck("eagle_backend_x_reduce_canonical");
     }
+}
+
+/** Whether ``dev`` runs float64 at 1/8 of the float32 rate or slower, where eagle
+ *  sums float64 on the fixed-point leaf (canonical.h:304-313, fixedLeafDevice :599-607). */
+bool slowFp64(int dev)
+{
+    int ratio = 0;
+    if (cudaDeviceGetAttribute(&ratio, cudaDevAttrSingleToDoublePrecisionPerfRatio, dev) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return false;
+    }
+    return ratio >= 8;
 }
 
 template <class T>
@@ -429,20 +441,19 @@ extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_bac
             invalid(std::string(who) + ": in, out, work_a and work_b must be device addresses");
         const int dev = resolveDevice(d.device, query ? 0 : d.in);
         DeviceScope scope(dev);
-        if (!query && d.dtype == EAGLE_BACKEND_REDUCE_F64 && d.op == EAGLE_BACKEND_REDUCE_OP_SUM && d.flags == 0) {
-            // eagle takes a 128-bit fixed-point leaf on devices whose FP32:FP64 rate
-            // is 8:1 or worse (canonical.h:304-313); this build carries the (hi, comp)
-            // leaf only, so such a device is refused rather than given other bits
-            int ratio = 0;
-            if (cudaDeviceGetAttribute(&ratio, cudaDevAttrSingleToDoublePrecisionPerfRatio, dev) == cudaSuccess
-                && ratio >= 8)
-                unsupported(std::string(who) + ": this device's FP32:FP64 ratio is " + std::to_string(ratio)
-                    + ":1; eagle reduces float64 sums there with the fixed-point leaf, which this build lacks");
-            (void)cudaGetLastError();
-        }
         const cudaStream_t stream = seamStream(d.stream);
         const int pairOut = (d.flags & EAGLE_BACKEND_REDUCE_PAIR_OUT) != 0;
         int64_t workElems = 0;
+        if (d.dtype == EAGLE_BACKEND_REDUCE_F64 && d.op == EAGLE_BACKEND_REDUCE_OP_SUM && d.flags == 0
+            && slowFp64(dev)) {
+            // a float64 sum without PAIR_OUT on a slow-FP64 device takes the fixed-point
+            // leaf under every policy, as eagle does (eagle_backend.h:896-906, canonical.h:304-313)
+            if (query)
+                desc->work_elems = workElemsFor<FixedP, double>(d.n, d.columns, smCount());
+            else
+                enqueueReduce<FixedP, double>(d, d.columns, 0, stream);
+            return;
+        }
         switch (d.dtype) {
         case EAGLE_BACKEND_REDUCE_F32: dispatchOp<float>(d, d.columns, pairOut, stream, query, &workElems); break;
         case EAGLE_BACKEND_REDUCE_F64: dispatchOp<double>(d, d.columns, pairOut, stream, query, &workElems); break;
@@ -456,6 +467,42 @@ extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_bac
         }
         if (query)
             desc->work_elems = workElems;
+    });
+}
+
+extern "C" __attribute__((visibility("default"))) eagle_backend_status eagle_backend_x_b200_reduce_fixed(
+    struct eagle_backend_reduce_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_reduce_fixed";
+        constexpr size_t base = offsetof(eagle_backend_reduce_desc, work_elems) + sizeof(int64_t);
+        if (desc == nullptr || desc->struct_size < base)
+            invalid(std::string(who) + ": null desc or struct_size too small");
+        eagle_backend_reduce_desc d{};
+        std::memcpy(&d, desc, std::min<size_t>(desc->struct_size, sizeof d));
+        const bool ext = desc->struct_size >= offsetof(eagle_backend_reduce_desc, comp_in) + sizeof(uint64_t);
+        if (!ext) {
+            d.policy = EAGLE_BACKEND_REDUCE_ORDERED;
+            d.flags = 0;
+            d.columns = 1;
+            d.comp_in = 0;
+        }
+        if (d.n < 1)
+            invalid(std::string(who) + ": n must be >= 1");
+        if (d.dtype != EAGLE_BACKEND_REDUCE_F64 || d.op != EAGLE_BACKEND_REDUCE_OP_SUM)
+            invalid(std::string(who) + ": the fixed-point leaf sums float64 (dtype F64, op SUM)");
+        if (d.flags != 0)
+            unsupported(std::string(who) + ": the fixed-point sum has no (hi, comp) pair to write (PAIR_OUT)");
+        if (d.columns < 1 || d.policy > EAGLE_BACKEND_REDUCE_AUTO)
+            invalid(std::string(who) + ": columns must be >= 1; unknown policy");
+        const bool query = d.work_a == 0;
+        if (!query && (d.in == 0 || d.out == 0 || d.work_b == 0))
+            invalid(std::string(who) + ": in, out, work_a and work_b must be device addresses");
+        DeviceScope scope(resolveDevice(d.device, query ? 0 : d.in));
+        if (query)
+            desc->work_elems = workElemsFor<FixedP, double>(d.n, d.columns, smCount());
+        else
+            enqueueReduce<FixedP, double>(d, d.columns, 0, seamStream(d.stream));
     });
 }
 

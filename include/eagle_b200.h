@@ -654,6 +654,17 @@ eagle_backend_status eagle_backend_x_b200_compact_gather(struct eagle_backend_co
  * give 0. Query with work_a == 0. One kernel after a memset; capturable. */
 eagle_backend_status eagle_backend_x_b200_reduce_counted(struct eagle_backend_reduce_desc* desc, uint64_t count);
 
+/* eagle_backend_x_b200_reduce_fixed: x_reduce_canonical of float64 sums on eagle's
+ * fixed-point leaf (eagle/reduce/canonical.h:153-302): the same tree over 128-bit
+ * fixed-point partials (v * 2^u, the unit 106 bits below the largest term; IEEE
+ * specials as sticky flags; one rounding at the end), the path eagle takes -- and
+ * x_reduce_canonical takes by itself -- on a device whose FP32:FP64 throughput ratio
+ * is 8 or worse (canonical.h:304-313). Offered here on any device so that its bits
+ * can be had and checked on B200 too. dtype F64, op SUM, any policy, columns and
+ * comp_in as x_reduce_canonical; PAIR_OUT returns UNSUPPORTED. Query with
+ * work_a == 0. One kernel per 65535 columns after a memset; capturable. */
+eagle_backend_status eagle_backend_x_b200_reduce_fixed(struct eagle_backend_reduce_desc* desc);
+
 /* eagle_backend_x_b200_compact_sum: the canonical ordered sum of the float64
  * ``values`` the mask keeps, in sample order -- the bits of compact_gather followed
  * by reduce_counted -- without writing the kept values anywhere: the mask becomes a

@@ -43,6 +43,8 @@ def lib():
         L.oracle_threads.argtypes = [ctypes.c_int]
         L.oracle_reduce.argtypes = [_P, _I64, _I64, ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int]
         L.oracle_leaf_partials_f64.argtypes = [_P, _I64, _P]
+        L.oracle_reduce_fixed.argtypes = [_P, _I64, _I64, _P, _P]
+        L.oracle_ladder.argtypes = [_I64, ctypes.c_int, ctypes.c_int, _P, _P]
         L.oracle_leaf_partials_f64.restype = _I64
         L.oracle_pairwise_f64.argtypes = [_P, _I64, _P]
         L.oracle_partial_value_f64.argtypes = [ctypes.c_double, ctypes.c_double]
@@ -187,6 +189,36 @@ def corpus(n: int, seed: int, dtype=np.float64):
     else:
         lib().oracle_corpus_f32(n, seed, _ptr(out))
     return out
+
+
+def reduce_fixed(x, *, columns: int = 1, comp=None):
+    """eagle's fixed-point float64 sum (eagle/reduce/canonical.h:153-302): the canonical
+    tree over 128-bit fixed-point partials, one value per column of the row-major
+    ``(n, columns)`` array ``x`` -- what eagle computes on a device whose FP32:FP64
+    ratio is 8 or worse (canonical.h:304-313)."""
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    n = x.size // columns
+    out = np.zeros(columns, dtype=np.float64)
+    c = None if comp is None else np.ascontiguousarray(comp, dtype=np.float64)
+    rc = lib().oracle_reduce_fixed(_ptr(x), n, columns, _ptr(c), _ptr(out))
+    if rc != 0:
+        raise ValueError(f"oracle_reduce_fixed refused (status {rc})")
+    return out
+
+
+def fixed_leaf(fp32_per_fp64: int) -> bool:
+    """Whether eagle reduces float64 sums on the fixed-point leaf on a device with
+    this FP32:FP64 throughput ratio (canonical.h:304-313: 8 or worse)."""
+    return fp32_per_fp64 >= 8
+
+
+def ladder(n: int, er: int, g: int):
+    """The cancellation ladder of eagle's fixed-point tests
+    (tests/test_CanonicalReduce.cu:88-119): returns (values, exact sum in units of 2^-10)."""
+    x = np.zeros(n, dtype=np.float64)
+    units = np.zeros(1, dtype=np.int64)
+    lib().oracle_ladder(n, int(er), int(g), _ptr(x), _ptr(units))
+    return x, int(units[0])
 
 
 def fixture(n: int, kappa: float, dtype=np.float64):

@@ -27,6 +27,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <limits>
 #include <vector>
 
 #include <omp.h>
@@ -171,6 +172,118 @@ P reduceColumn(const ColumnIn<T>& in, int64_t rows)
     return pairwise(parts);
 }
 
+// The fixed-point partial of a float64 sum that eagle takes on devices whose
+// FP32:FP64 throughput ratio is 8 or worse (canonical.h:153-313, the rule :304-313):
+// the value is v * 2^u with v a signed 128-bit integer. A term's last mantissa bit
+// lands at most 53 bits above the unit, which is kept 106 bits below the largest
+// term seen (a term, or an aligned partial, loses at most one unit); a join halves
+// both sides and raises the unit when either reaches 2^125. Infinities and NaN set
+// sticky flags; value() rounds once to nearest-even, subnormals included.
+struct Fixed {
+    using I = __int128;
+    using U = unsigned __int128;
+    static constexpr int32_t kEmpty = -100000;  // the unit of a partial that saw no term
+    static constexpr int32_t kPosInf = 1, kNegInf = 2, kNan = 4;
+    I v = 0;
+    int32_t u = kEmpty, fl = 0;
+
+    static I shr(I x, int32_t d) { return x >> (d < 127 ? d : 127); }  // floor, any d >= 0
+    static Fixed of(double x)
+    {
+        Fixed p;
+        p.add(x);
+        return p;
+    }
+    static Fixed of(double x, double xc)
+    {
+        Fixed p;
+        p.add(x);
+        p.add(xc);
+        return p;
+    }
+    void add(double x, double xc)
+    {
+        add(x);
+        add(xc);
+    }
+    void add(double x)
+    {
+        uint64_t b;
+        std::memcpy(&b, &x, sizeof b);
+        const int32_t e = int32_t((b >> 52) & 0x7ff);
+        if (e == 0x7ff) {
+            fl |= (b << 12) != 0 ? kNan : ((b >> 63) != 0 ? kNegInf : kPosInf);
+            return;
+        }
+        const uint64_t m = (b & 0xfffffffffffffull) | (e != 0 ? (1ull << 52) : 0ull);
+        if (m == 0)
+            return;
+        const int32_t ex = (e != 0 ? e : 1) - 1075;  // the weight of m's last bit
+        if (ex - 53 > u) {
+            v = shr(v, ex - 53 - u);
+            u = ex - 53;
+        }
+        const int32_t sh = ex - u;  // at most 53
+        const I t = sh >= 0 ? I(U(m) << sh) : (-sh < 64 ? I(m >> -sh) : I(0));
+        v = (b >> 63) != 0 ? v - t : v + t;
+    }
+    static Fixed join(const Fixed& a, const Fixed& b)
+    {
+        I x = a.v, y = b.v;
+        int32_t u = a.u;
+        if (b.u > u) {
+            x = shr(x, b.u - u);
+            u = b.u;
+        } else {
+            y = shr(y, u - b.u);
+        }
+        const auto wide = [](I z) { const I top = z >> 125; return top != 0 && top != -1; };
+        if (wide(x) || wide(y)) {
+            x >>= 1;
+            y >>= 1;
+            ++u;
+        }
+        Fixed o;
+        o.v = x + y;
+        o.u = u;
+        o.fl = a.fl | b.fl;
+        return o;
+    }
+    double value() const
+    {
+        if (fl != 0) {
+            if ((fl & kNan) != 0 || (fl & (kPosInf | kNegInf)) == (kPosInf | kNegInf))
+                return std::numeric_limits<double>::quiet_NaN();
+            return (fl & kPosInf) != 0 ? std::numeric_limits<double>::infinity()
+                                       : -std::numeric_limits<double>::infinity();
+        }
+        if (v == 0)
+            return 0.0;
+        const bool neg = v < 0;
+        const U mag = neg ? U(0) - U(v) : U(v);
+        int len = 0;
+        for (U z = mag; z != 0; z >>= 1)
+            ++len;
+        const int32_t sub = len + u + 1074;  // the bits of weight 2^-1074 and up
+        const int32_t keep = sub < 53 ? sub : 53;
+        const int32_t drop = len - keep;
+        double r;
+        if (drop <= 0) {
+            r = std::ldexp(double(uint64_t(mag)), u);
+        } else {
+            U q = drop < 128 ? mag >> drop : U(0);
+            const U rem = drop < 128 ? mag - (q << drop) : mag;
+            if (drop <= 128) {
+                const U half = U(1) << (drop - 1);
+                if (rem > half || (rem == half && (q & 1) != 0))
+                    ++q;
+            }
+            r = std::ldexp(double(uint64_t(q)), u + drop);
+        }
+        return neg ? -r : r;
+    }
+};
+
 template <class T, class Op>
 int reducePlainTyped(const void* in, int64_t n, int64_t cols, void* out)
 {
@@ -284,6 +397,47 @@ int oracle_reduce(const void* in, int64_t n, int64_t cols, int dtype, int op, co
     default:
         return 2;
     }
+}
+
+int oracle_reduce_fixed(const double* in, int64_t n, int64_t cols, const double* comp_in, double* out)
+{
+    if (n < 1 || cols < 1 || in == nullptr || out == nullptr)
+        return 2;
+    for (int64_t j = 0; j < cols; ++j) {
+        ColumnIn<double> ci{in, comp_in, cols, j};
+        out[j] = reduceColumn<Fixed>(ci, n).value();
+    }
+    return 0;
+}
+
+// The cancellation ladder of eagle's fixed-point tests (tests/test_CanonicalReduce.cu:88-119):
+// x at r and exactly -x at n-1-r, |x| a full 52-bit mantissa times 2^e, e uniform in
+// [G - ER, G + ER]; a quarter of the pairs (and the middle) carry v * 2^-10 on both
+// partners instead. ``units`` = the exact sum in units of 2^-10.
+void oracle_ladder(int64_t n, int ER, int G, double* x, long long* units)
+{
+    const auto mix = [](uint64_t z) {
+        z += 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    long long total = 0;
+    for (int64_t r = 0; r < n; ++r) {
+        const int64_t m = n - 1 - r, j = std::min(r, m);
+        const uint64_t h = mix(uint64_t(j) * 0x100000001B3ull ^ mix(7));
+        if (j == 0 || m == r || (h & 3) == 0) {
+            const long long v = 1 + (long long)((h >> 8) % 4096);
+            x[r] = std::ldexp(double(v), -10);
+            total += v;
+        } else {
+            const uint64_t h2 = mix(h), h3 = mix(h2);
+            const double mant = 1.0 + double(h2 & ((1ull << 52) - 1)) / double(1ull << 52);
+            const double v = std::ldexp(mant, int((h3 >> 1) % uint64_t(2 * ER + 1)) - ER + G);
+            x[r] = ((h3 & 1) != 0) == (r < m) ? -v : v;
+        }
+    }
+    *units = total;
 }
 
 int64_t oracle_leaf_partials_f64(const double* x, int64_t n, double* hc)

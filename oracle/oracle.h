@@ -22,6 +22,8 @@ extern "C" {
 int oracle_threads(int threads);
 int oracle_reduce(const void* in, int64_t n, int64_t cols, int dtype, int op, const void* comp_in, void* out,
     int pair_out);
+int oracle_reduce_fixed(const double* in, int64_t n, int64_t cols, const double* comp_in, double* out);
+void oracle_ladder(int64_t n, int ER, int G, double* x, long long* units);
 int64_t oracle_leaf_partials_f64(const double* x, int64_t n, double* hc);
 void oracle_pairwise_f64(const double* hc, int64_t m, double* root_hc);
 double oracle_partial_value_f64(double h, double c);
