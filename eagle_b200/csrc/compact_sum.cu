@@ -36,6 +36,7 @@
 // sectors holding a survivor; the bits are those of the two-kernel compaction +
 // canonical sum, which the tests check against the oracle.
 #include "canonical.cuh"
+#include "tiles.cuh"
 
 #include <mutex>
 
@@ -47,87 +48,8 @@ constexpr int kRows = 4;
 constexpr int64_t kRow = int64_t(kThreads) * 16;  // 4096 samples: 16 mask bytes per thread
 constexpr int64_t kTile = kRow * kRows;           // 16384 samples per keepCount CTA
 constexpr int64_t kTileWords = kTile / 32;        // its bitmap words
-constexpr int kScanThreads = 1024;
-constexpr int kScanPer = 16;                      // tile counts per scan thread per round
 
 using P = CompP<double>;
-
-template <bool Drop, bool Aligned>
-__global__ __launch_bounds__(kThreads) void keepCountKernel(const uint8_t* __restrict__ mask, int64_t n,
-    uint32_t* __restrict__ bitmap, uint32_t* __restrict__ tileCount)
-{
-    __shared__ uint32_t part[kThreads / 32];
-    const int t = int(threadIdx.x);
-    const int64_t tile = blockIdx.x;
-    const int64_t tile0 = tile * kTile;
-    uint32_t bits[kRows];
-    uint32_t c = 0;
-#pragma unroll
-    for (int q = 0; q < kRows; ++q) {
-        bits[q] = keepBits16<Drop, Aligned>(mask, tile0 + int64_t(q) * kRow + int64_t(t) * 16, n);
-        c += uint32_t(__popc(bits[q]));
-    }
-    // threads 2u and 2u + 1 hold the low and high halves of one 32-sample word
-#pragma unroll
-    for (int q = 0; q < kRows; ++q) {
-        const uint32_t hi = __shfl_down_sync(kFull, bits[q], 1);
-        if ((t & 1) == 0)
-            bitmap[tile * kTileWords + q * (kRow / 32) + (t >> 1)] = bits[q] | (hi << 16);
-    }
-    c = warpSum(c);
-    if ((t & 31) == 0)
-        part[t >> 5] = c;
-    __syncthreads();
-    if (t == 0) {
-        uint32_t s = 0;
-#pragma unroll
-        for (int w = 0; w < kThreads / 32; ++w)
-            s += part[w];
-        tileCount[tile] = s;
-    }
-}
-
-/** tileOff[i] = the kept samples before tile i; ``*count`` = all of them. One CTA. */
-__global__ __launch_bounds__(kScanThreads) void tileScanKernel(const uint32_t* __restrict__ tileCount,
-    uint32_t* __restrict__ tileOff, int64_t tiles, uint32_t* count)
-{
-    __shared__ uint32_t scan[33];
-    const int t = int(threadIdx.x);
-    uint32_t carry = 0;
-    for (int64_t r0 = 0; r0 < tiles; r0 += int64_t(kScanThreads) * kScanPer) {
-        const int64_t i0 = r0 + int64_t(t) * kScanPer;
-        uint32_t v[kScanPer];
-        if (i0 + kScanPer <= tiles) {  // four 16-byte loads (the counts start 256-byte aligned)
-#pragma unroll
-            for (int k = 0; k < kScanPer / 4; ++k) {
-                const uint4 x = reinterpret_cast<const uint4*>(tileCount + i0)[k];
-                v[4 * k] = x.x;
-                v[4 * k + 1] = x.y;
-                v[4 * k + 2] = x.z;
-                v[4 * k + 3] = x.w;
-            }
-        } else {
-#pragma unroll
-            for (int k = 0; k < kScanPer; ++k)
-                v[k] = i0 + k < tiles ? tileCount[i0 + k] : 0u;
-        }
-        uint32_t mine = 0;
-#pragma unroll
-        for (int k = 0; k < kScanPer; ++k)
-            mine += v[k];
-        uint32_t total = 0;
-        uint32_t run = carry + blockExclusiveSum(mine, total, scan);
-#pragma unroll
-        for (int k = 0; k < kScanPer; ++k) {
-            if (i0 + k < tiles)
-                tileOff[i0 + k] = run;
-            run += v[k];
-        }
-        carry += total;
-    }
-    if (t == 0)
-        *count = carry;
-}
 
 /** The position of the ``r``-th set bit (from 0) of ``x``, which has more than r:
  *  five halvings, each keeping the half the bit lies in. */
@@ -691,10 +613,9 @@ __global__ void compactSumEmptyKernel(uint32_t* count, double* out, int pairOut)
  *  call's memset), then the tile counts and offsets, the bitmap, the leaf starts,
  *  the sparse list, the leaf partials and the chunk partials. */
 struct SumLayout {
-    int64_t tiles = 0;
     int64_t maxLeaves = 0, maxChunks = 0;
-    size_t zeroed = 0, tileCount = 0, tileOff = 0, bitmap = 0, leafStart = 0, sparseList = 0, leafPart = 0,
-           chunkPart = 0, total = 0;
+    tiles::TileLayout t;
+    size_t zeroed = 0, leafStart = 0, sparseList = 0, leafPart = 0, chunkPart = 0, total = 0;
 };
 
 size_t up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -725,14 +646,11 @@ int passGrid(int which)
 SumLayout sumLayout(int64_t n)
 {
     SumLayout L;
-    L.tiles = n > 0 ? (n + kTile - 1) / kTile : 1;
     L.maxLeaves = (n + kLeaf - 1) / kLeaf;
     L.maxChunks = (L.maxLeaves + kChunk - 1) / kChunk;
     L.zeroed = up(size_t(8 + L.maxChunks) * sizeof(uint32_t), 16);
-    L.tileCount = up(L.zeroed, 256);
-    L.tileOff = up(L.tileCount + size_t(L.tiles) * sizeof(uint32_t), 256);
-    L.bitmap = up(L.tileOff + size_t(L.tiles) * sizeof(uint32_t), 256);
-    L.leafStart = up(L.bitmap + size_t(L.tiles) * kTileWords * sizeof(uint32_t), 256);
+    L.t = tiles::tileLayout(n, L.zeroed);
+    L.leafStart = up(L.t.end, 256);
     L.sparseList = up(L.leafStart + size_t(L.maxLeaves + 1) * sizeof(int32_t), 256);
     L.leafPart = up(L.sparseList + size_t(L.maxLeaves + 1) * sizeof(int32_t), 256);
     L.chunkPart = up(L.leafPart + size_t(L.maxLeaves > 0 ? L.maxLeaves : 1) * sizeof(P), 256);
@@ -789,9 +707,9 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
         }
         char* base = reinterpret_cast<char*>(d.scratch);
         uint32_t* words = reinterpret_cast<uint32_t*>(base);
-        uint32_t* tileCount = reinterpret_cast<uint32_t*>(base + L.tileCount);
-        uint32_t* tileOff = reinterpret_cast<uint32_t*>(base + L.tileOff);
-        uint32_t* bitmap = reinterpret_cast<uint32_t*>(base + L.bitmap);
+        uint32_t* tileCount = reinterpret_cast<uint32_t*>(base + L.t.count);
+        uint32_t* tileOff = reinterpret_cast<uint32_t*>(base + L.t.off);
+        uint32_t* bitmap = reinterpret_cast<uint32_t*>(base + L.t.bitmap);
         int32_t* leafStart = reinterpret_cast<int32_t*>(base + L.leafStart);
         uint32_t* count = reinterpret_cast<uint32_t*>(d.count);
         LeafArgs la{};
@@ -812,23 +730,13 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
         la.out = reinterpret_cast<double*>(out);
         la.pairOut = pairOut;
         cudaCheck(cudaMemsetAsync(base, 0, L.zeroed, s), "cudaMemsetAsync");
-        const auto mask = reinterpret_cast<const uint8_t*>(d.mask);
-        const unsigned tiles = unsigned(L.tiles);
-        const bool aligned = (d.mask & 15u) == 0;
-        if (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP)
-            aligned ? keepCountKernel<true, true><<<tiles, kThreads, 0, s>>>(mask, d.n, bitmap, tileCount)
-                    : keepCountKernel<true, false><<<tiles, kThreads, 0, s>>>(mask, d.n, bitmap, tileCount);
-        else
-            aligned ? keepCountKernel<false, true><<<tiles, kThreads, 0, s>>>(mask, d.n, bitmap, tileCount)
-                    : keepCountKernel<false, false><<<tiles, kThreads, 0, s>>>(mask, d.n, bitmap, tileCount);
-        launchCheck(who);
-        tileScanKernel<<<1, kScanThreads, 0, s>>>(tileCount, tileOff, L.tiles, count);
-        launchCheck(who);
+        tiles::enqueueTiles(reinterpret_cast<const uint8_t*>(d.mask), d.n,
+            (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0, base, L.t, count, tiles::ScanTrigger{}, s, who);
         const int64_t warpsPerCta = kThreads / 32;
-        const int64_t startCtas = (L.tiles + warpsPerCta - 1) / warpsPerCta;
+        const int64_t startCtas = (L.t.tiles + warpsPerCta - 1) / warpsPerCta;
         const int64_t startCap = int64_t(smCount()) * 8;
         leafStartKernel<<<unsigned(startCtas < startCap ? startCtas : startCap), kThreads, 0, s>>>(bitmap, tileCount,
-            tileOff, L.tiles, leafStart);
+            tileOff, L.t.tiles, leafStart);
         launchCheck(who);
         keptDenseKernel<<<unsigned(passGrid(0)), kDenseThreads, 0, s>>>(la);
         launchCheck(who);
