@@ -172,30 +172,53 @@ __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
     }
 }
 
-/** compact_device's second pass: one 16384-sample tile per CTA, its keep bits read
- *  back from the tile bitmap (512 words; thread t's 16 bits of row q are half
- *  t & 1 of word 128 q + t / 2), one CTA scan of the four rows' counts, and the
- *  indices written from the tile's scanned offset -- no look-back, so no tile waits
- *  on another. */
+/** compact_device's second pass: CTAs loop over 16384-sample tiles (the next
+ *  tile's bitmap words already in flight). A tile's keep bits are read back from its
+ *  512 bitmap words (thread t's 16 bits of row q are half t & 1 of word 128 q + t / 2),
+ *  scanned across the CTA, and its indices written from the tile's scanned offset --
+ *  no look-back, so no tile waits on another. */
 __global__ __launch_bounds__(kThreads) void scatterKernel(CompactArgs a, const uint32_t* __restrict__ bitmap,
     const uint32_t* __restrict__ tileOff)
 {
     __shared__ uint64_t scan64[33];
     __shared__ int32_t stage[kStage];
     const int t = int(threadIdx.x);
-    const int64_t tile = blockIdx.x;
-    const int64_t tile0 = tile * kTile;
-    uint32_t bits[kRows];
-    uint64_t packed = 0;
+    const int64_t tiles = int64_t(a.tiles);
+    auto words = [&](int64_t tile, uint32_t (&w)[kRows]) {
 #pragma unroll
-    for (int q = 0; q < kRows; ++q) {
-        const uint32_t w = bitmap[tile * (kTile / 32) + q * (kRow / 32) + (t >> 1)];
-        bits[q] = (t & 1) != 0 ? (w >> 16) : (w & 0xffffu);
-        packed |= uint64_t(__popc(bits[q])) << (16 * q);
+        for (int q = 0; q < kRows; ++q)
+            w[q] = __ldg(bitmap + tile * (kTile / 32) + q * (kRow / 32) + (t >> 1));
+    };
+    uint32_t cur[kRows] = {0u, 0u, 0u, 0u}, nxt[kRows] = {0u, 0u, 0u, 0u};
+    uint32_t off = 0;
+    int64_t tile = blockIdx.x;
+    if (tile < tiles) {
+        words(tile, cur);
+        off = __ldg(tileOff + tile);
     }
-    uint64_t rowTotals = 0;
-    const uint64_t excl = blockExclusiveSum(packed, rowTotals, scan64);
-    writeRows<false>(a, bits, excl, rowTotals, tile0, tileOff[tile], stage);
+    while (tile < tiles) {
+        const int64_t next = tile + gridDim.x;
+        uint32_t nextOff = 0;
+        if (next < tiles) {
+            words(next, nxt);
+            nextOff = __ldg(tileOff + next);
+        }
+        uint32_t bits[kRows];
+        uint64_t packed = 0;
+#pragma unroll
+        for (int q = 0; q < kRows; ++q) {
+            bits[q] = (t & 1) != 0 ? (cur[q] >> 16) : (cur[q] & 0xffffu);
+            packed |= uint64_t(__popc(bits[q])) << (16 * q);
+        }
+        uint64_t rowTotals = 0;
+        const uint64_t excl = blockExclusiveSum(packed, rowTotals, scan64);
+        writeRows<false>(a, bits, excl, rowTotals, tile * kTile, off, stage);
+#pragma unroll
+        for (int q = 0; q < kRows; ++q)
+            cur[q] = nxt[q];
+        off = nextOff;
+        tile = next;
+    }
 }
 
 __global__ void compactEmptyKernel(uint32_t* count, uint32_t* live32, uint32_t* fire)
@@ -422,7 +445,9 @@ void enqueueCompactDevice(const eagle_backend_compact_desc& d, const char* who)
     a.n = d.n;
     a.map = reinterpret_cast<int32_t*>(d.index_map);
     a.tiles = uint32_t(L.tiles);
-    scatterKernel<<<unsigned(L.tiles), kThreads, 0, s>>>(a, reinterpret_cast<const uint32_t*>(scratch + L.bitmap),
+    const int64_t cap = int64_t(smCount()) * 8;  // resident CTAs: each loops over tiles
+    scatterKernel<<<unsigned(L.tiles < cap ? L.tiles : cap), kThreads, 0, s>>>(a,
+        reinterpret_cast<const uint32_t*>(scratch + L.bitmap),
         reinterpret_cast<const uint32_t*>(scratch + L.off));
     launchCheck(who);
 }
