@@ -4,18 +4,15 @@
 // python/src/seam/eagle_backend.h:666-701): index_map[0, count) = the kept sample
 // indices, ascending; count; optionally the reorder trigger (live32, fire) of
 // Compact.h:113-118. Eagle runs predicate -> multi-level int64 scan -> scatter
-// (about 2 log256(n) + 2 launches over 8-byte planes). Here it is three kernels, none
-// of whose CTAs waits on another: the mask becomes a keep bitmap and per-tile counts
-// (one streaming pass over 16384-sample tiles, tiles.cuh), one CTA scans the counts
-// (and forms live32 and fire), and a scatter pass re-reads each tile's 2 KB of bitmap,
-// scans it across the CTA and writes the tile's indices from its offset, staged in
-// shared memory for coalesced stores. compact_gather and the allocation-free entry
-// keep the one-pass form: each CTA takes the next tile off a counter and finds its
-// offset by a decoupled look-back over the earlier tiles' status words, which needs
-// no bitmap (its scratch is one word per tile) but is bound by the look-back's
-// latency when the mask is sparse.
+// (about 2 log256(n) + 2 launches over 8-byte planes). Here it is ONE kernel
+// after a memset of its scratch: each CTA takes the next 16384-sample tile off a
+// counter (so every tile it waits on is already owned by a running CTA), turns
+// 4 x 16 mask bytes per thread into keep bit-sets, scans the counts across the CTA,
+// finds the tile's global offset by a decoupled look-back over the earlier
+// tiles' status words, stages the kept indices in shared memory and writes them
+// with coalesced stores. The trigger's live32 rides in the same status words, so
+// the last tile alone knows count and live32 and writes count, live32 and fire.
 #include "common.cuh"
-#include "tiles.cuh"
 
 #include <mutex>
 
@@ -45,53 +42,6 @@ struct CompactArgs {
     void* outValues;     // Gather: the kept samples' values, in sample order
     uint32_t elemBytes;  // Gather: 4 or 8
 };
-
-/** A tile's kept indices (its rows' keep bits ``bits``, their per-row exclusive
- *  counts packed in ``excl`` and totals in ``rowTotals``) written from output index
- *  ``first`` on: gathered in shared memory in output order and written out with
- *  coalesced stores whenever the next row would not fit (a sparse tile: once; a
- *  dense one: per row); with Gather, the kept samples' values beside them. */
-template <bool Gather>
-__device__ __forceinline__ void writeRows(const CompactArgs& a, const uint32_t (&bits)[kRows], uint64_t excl,
-    uint64_t rowTotals, int64_t tile0, uint32_t first, int32_t* stage)
-{
-    const int t = int(threadIdx.x);
-    uint32_t flushAt = first;  // the output index of stage[0]
-    uint32_t fill = 0;         // staged so far (uniform across the CTA)
-    auto flush = [&]() {
-        __syncthreads();
-        for (uint32_t r = uint32_t(t); r < fill; r += kThreads) {
-            const int32_t idx = stage[r];
-            const size_t out = size_t(flushAt) + r;
-            if (a.map != nullptr)
-                a.map[out] = idx;
-            if constexpr (Gather) {
-                if (a.elemBytes == 8)
-                    static_cast<uint64_t*>(a.outValues)[out] = static_cast<const uint64_t*>(a.values)[idx];
-                else
-                    static_cast<uint32_t*>(a.outValues)[out] = static_cast<const uint32_t*>(a.values)[idx];
-            }
-        }
-        __syncthreads();
-        flushAt += fill;
-        fill = 0;
-    };
-#pragma unroll
-    for (int q = 0; q < kRows; ++q) {
-        const uint32_t rowTotal = uint32_t(rowTotals >> (16 * q)) & 0xffffu;
-        if (fill + rowTotal > kStage)
-            flush();
-        uint32_t k = fill + (uint32_t(excl >> (16 * q)) & 0xffffu);
-        const int64_t i0 = tile0 + int64_t(q) * kRow + int64_t(t) * 16;
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if ((bits[q] >> j) & 1u)
-                stage[k++] = int32_t(i0 + j);
-        fill += rowTotal;
-    }
-    if (fill != 0)
-        flush();
-}
 
 /** One 16384-sample tile per CTA, as four rows of 4096: thread t holds the 16
  *  mask bytes at t * 16 of every row (four coalesced 16-byte loads). One CTA scan
@@ -157,7 +107,43 @@ __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
     }
     __syncthreads();
     const uint64_t prefix = sPrefix;
-    writeRows<Gather>(a, bits, excl, rowTotals, tile0, uint32_t(prefix), stage);
+    // the rows' kept indices gather in shared memory in output order; they are written
+    // out whenever the next row would not fit (a sparse tile: once; a dense one: per row)
+    uint32_t flushAt = uint32_t(prefix);  // the output index of stage[0]
+    uint32_t fill = 0;                    // staged so far (uniform across the CTA)
+    auto flush = [&]() {
+        __syncthreads();
+        for (uint32_t r = uint32_t(t); r < fill; r += kThreads) {
+            const int32_t idx = stage[r];
+            const size_t out = size_t(flushAt) + r;
+            if (a.map != nullptr)
+                a.map[out] = idx;
+            if constexpr (Gather) {
+                if (a.elemBytes == 8)
+                    static_cast<uint64_t*>(a.outValues)[out] = static_cast<const uint64_t*>(a.values)[idx];
+                else
+                    static_cast<uint32_t*>(a.outValues)[out] = static_cast<const uint32_t*>(a.values)[idx];
+            }
+        }
+        __syncthreads();
+        flushAt += fill;
+        fill = 0;
+    };
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+        const uint32_t rowTotal = uint32_t(rowTotals >> (16 * q)) & 0xffffu;
+        if (fill + rowTotal > kStage)
+            flush();
+        uint32_t k = fill + (uint32_t(excl >> (16 * q)) & 0xffffu);
+        const int64_t i0 = tile0 + int64_t(q) * kRow + int64_t(t) * 16;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if ((bits[q] >> j) & 1u)
+                stage[k++] = int32_t(i0 + j);
+        fill += rowTotal;
+    }
+    if (fill != 0)
+        flush();
     if (tile == a.tiles - 1 && t == 0) {
         const uint32_t c = uint32_t(prefix) + total;
         const bool broken = *a.err != 0u;
@@ -169,55 +155,6 @@ __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
             const double limit = double(a.theta) * 32.0 * double(live32);
             *a.fire = (double(c) < limit && c < span && span >= 4096u) ? 1u : 0u;
         }
-    }
-}
-
-/** compact_device's second pass: CTAs loop over 16384-sample tiles (the next
- *  tile's bitmap words already in flight). A tile's keep bits are read back from its
- *  512 bitmap words (thread t's 16 bits of row q are half t & 1 of word 128 q + t / 2),
- *  scanned across the CTA, and its indices written from the tile's scanned offset --
- *  no look-back, so no tile waits on another. */
-__global__ __launch_bounds__(kThreads) void scatterKernel(CompactArgs a, const uint32_t* __restrict__ bitmap,
-    const uint32_t* __restrict__ tileOff)
-{
-    __shared__ uint64_t scan64[33];
-    __shared__ int32_t stage[kStage];
-    const int t = int(threadIdx.x);
-    const int64_t tiles = int64_t(a.tiles);
-    auto words = [&](int64_t tile, uint32_t (&w)[kRows]) {
-#pragma unroll
-        for (int q = 0; q < kRows; ++q)
-            w[q] = __ldg(bitmap + tile * (kTile / 32) + q * (kRow / 32) + (t >> 1));
-    };
-    uint32_t cur[kRows] = {0u, 0u, 0u, 0u}, nxt[kRows] = {0u, 0u, 0u, 0u};
-    uint32_t off = 0;
-    int64_t tile = blockIdx.x;
-    if (tile < tiles) {
-        words(tile, cur);
-        off = __ldg(tileOff + tile);
-    }
-    while (tile < tiles) {
-        const int64_t next = tile + gridDim.x;
-        uint32_t nextOff = 0;
-        if (next < tiles) {
-            words(next, nxt);
-            nextOff = __ldg(tileOff + next);
-        }
-        uint32_t bits[kRows];
-        uint64_t packed = 0;
-#pragma unroll
-        for (int q = 0; q < kRows; ++q) {
-            bits[q] = (t & 1) != 0 ? (cur[q] >> 16) : (cur[q] & 0xffffu);
-            packed |= uint64_t(__popc(bits[q])) << (16 * q);
-        }
-        uint64_t rowTotals = 0;
-        const uint64_t excl = blockExclusiveSum(packed, rowTotals, scan64);
-        writeRows<false>(a, bits, excl, rowTotals, tile * kTile, off, stage);
-#pragma unroll
-        for (int q = 0; q < kRows; ++q)
-            cur[q] = nxt[q];
-        off = nextOff;
-        tile = next;
     }
 }
 
@@ -238,10 +175,6 @@ void launchCompact(const CompactArgs& a, bool aligned, cudaStream_t s)
     else
         compactKernel<Drop, Trigger, false, Gather><<<a.tiles, kThreads, 0, s>>>(a);
 }
-
-/** compact_device's scratch: the tile front end's counts, offsets, live groups and
- *  bitmap (n / 8 bytes). */
-size_t compactTilesScratchBytes(int64_t n) { return tiles::tileLayout(n, 0).end; }
 
 size_t compactScratchBytes(int64_t n)
 {
@@ -428,27 +361,27 @@ void enqueueCompactDevice(const eagle_backend_compact_desc& d, const char* who)
         launchCheck(who);
         return;
     }
-    static_assert(kTile == tiles::kTile && kRow == tiles::kRow, "one tile shape for both passes");
-    const tiles::TileLayout L = tiles::tileLayout(d.n, 0);
-    char* scratch = reinterpret_cast<char*>(d.scratch);
-    tiles::ScanTrigger trig{};
-    if (trigger) {
-        trig.live32 = reinterpret_cast<uint32_t*>(d.live32);
-        trig.span = reinterpret_cast<const uint32_t*>(d.span);
-        trig.fire = reinterpret_cast<uint32_t*>(d.fire);
-        trig.theta = d.theta;
-    }
-    const bool drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
-    tiles::enqueueTiles(reinterpret_cast<const uint8_t*>(d.mask), d.n, drop, scratch, L,
-        reinterpret_cast<uint32_t*>(d.count), trig, s, who);
+    const size_t scratchBytes = compactScratchBytes(d.n);
     CompactArgs a{};
+    a.mask = reinterpret_cast<const uint8_t*>(d.mask);
     a.n = d.n;
     a.map = reinterpret_cast<int32_t*>(d.index_map);
-    a.tiles = uint32_t(L.tiles);
-    const int64_t cap = int64_t(smCount()) * 8;  // resident CTAs: each loops over tiles
-    scatterKernel<<<unsigned(L.tiles < cap ? L.tiles : cap), kThreads, 0, s>>>(a,
-        reinterpret_cast<const uint32_t*>(scratch + L.bitmap),
-        reinterpret_cast<const uint32_t*>(scratch + L.off));
+    a.count = reinterpret_cast<uint32_t*>(d.count);
+    a.tiles = uint32_t((d.n + kTile - 1) / kTile);
+    a.status = reinterpret_cast<uint64_t*>(d.scratch);
+    a.tileNext = reinterpret_cast<uint32_t*>(d.scratch + size_t(a.tiles) * sizeof(uint64_t));
+    a.err = a.tileNext + 1;
+    a.live32 = reinterpret_cast<uint32_t*>(d.live32);
+    a.span = reinterpret_cast<const uint32_t*>(d.span);
+    a.fire = reinterpret_cast<uint32_t*>(d.fire);
+    a.theta = d.theta;
+    cudaCheck(cudaMemsetAsync(reinterpret_cast<void*>(d.scratch), 0, scratchBytes, s), "cudaMemsetAsync");
+    const bool aligned = (d.mask & 15u) == 0;
+    const bool drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
+    if (drop)
+        trigger ? launchCompact<true, true>(a, aligned, s) : launchCompact<true, false>(a, aligned, s);
+    else
+        trigger ? launchCompact<false, true>(a, aligned, s) : launchCompact<false, false>(a, aligned, s);
     launchCheck(who);
 }
 
@@ -518,11 +451,9 @@ EB_API eagle_backend_status eagle_backend_compact_device(struct eagle_backend_co
             constexpr size_t end = offsetof(eagle_backend_compact_desc, scratch_bytes) + sizeof(int64_t);
             if (desc->struct_size < end)
                 invalid(std::string(who) + ": the scratch query needs a desc carrying scratch_bytes");
-            desc->scratch_bytes = int64_t(compactTilesScratchBytes(d.n));
+            desc->scratch_bytes = int64_t(compactScratchBytes(d.n));
             return;
         }
-        if ((d.scratch & 255u) != 0)
-            invalid(std::string(who) + ": scratch must be 256-byte aligned");
         DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
         enqueueCompactDevice(d, who);
     });
@@ -544,11 +475,9 @@ EB_API eagle_backend_status eagle_backend_compact_classes_device(struct eagle_ba
             unsupported(std::string(who) + ": the int32 index map addresses at most 2^31-1 samples, got n = "
                 + std::to_string(d.n));
         if (d.scratch == 0) {
-            desc->scratch_bytes = int64_t(compactTilesScratchBytes(d.n));
+            desc->scratch_bytes = int64_t(compactScratchBytes(d.n));
             return;
         }
-        if ((d.scratch & 255u) != 0)
-            invalid(std::string(who) + ": scratch must be 256-byte aligned");
         if (d.live32 == 0 || d.span == 0 || d.fire == 0 || d.mixed32 == 0 || d.class_fire == 0
             || (d.n > 0 && d.class_plane == 0))
             invalid(std::string(who) + ": live32, span, fire, class_plane, mixed32 and class_fire are required");
