@@ -93,6 +93,101 @@ __global__ __launch_bounds__(256) void oscillatorRange(EB_OSC_ROLES(TEnd<Spread>
         hawkStepsum);
 }
 
+/** t after k steps of a sample that starts at t = +0: T[0] = +0, T[k + 1] = T[k] + dt,
+ *  rounded -- one sequence for every such sample, since dt is a Param. A CTA keeps
+ *  every S-th term (S a power of two, at most kTCoarse + 1 terms) in shared memory;
+ *  a sample then finds the step it stops at (the first k >= 1 with T[k] >= t_end,
+ *  the model's step-then-test) by a binary search of the coarse terms and at most S
+ *  additions from the one below, instead of adding dt and testing at every step. The
+ *  terms are the very additions the sample's own steps would make, so its t, its
+ *  stop step and its x, v are those of the step-by-step run, bit for bit. */
+constexpr int kTCoarse = 5120;          // coarse terms a CTA keeps (40 KB of shared memory)
+constexpr int64_t kTMaxBudget = 65536;  // longer runs keep the step-by-step test
+
+struct TTable {
+    const double* c;  // c[j] = T[j * stride], j <= budget / stride
+    int stride;       // 0: no table (dt negative, infinite or NaN, or a budget too long)
+    int64_t budget;
+    double perTerm;   // 1 / (dt * stride): the coarse index of a t, roughly (T[k] is close to k dt)
+};
+
+/** Built by thread 0 of the CTA; the others wait at the barrier that follows. */
+__device__ __forceinline__ int buildTTable(double* c, double dt, int64_t budget)
+{
+    if (!(dt >= 0.0 && dt <= 1.7976931348623157e308) || budget < 1 || budget > kTMaxBudget)
+        return 0;
+    int stride = 1;
+    while (int64_t(stride) * kTCoarse < budget)
+        stride *= 2;
+    double tt = 0.0;
+    c[0] = 0.0;
+    for (int64_t k = 1; k <= budget; ++k) {
+        tt = __dadd_rn(tt, dt);
+        if ((k & (stride - 1)) == 0)
+            c[k / stride] = tt;
+    }
+    return stride;
+}
+
+/** For a sample at t = +0 with end ``te``: the steps it runs within ``budget``
+ *  (``target``), whether it stops on the last of them, and its t after them. The
+ *  first coarse term at or past te is guessed from te / (dt stride) and confirmed by
+ *  its neighbour (a binary search when the guess misses by more than one), then at
+ *  most ``stride`` additions find the step. */
+__device__ __forceinline__ void tTarget(const TTable& T, double dt, double te, int64_t& target, bool& stops,
+    double& tAfter)
+{
+    const int64_t last = T.budget / T.stride;  // coarse terms 0..last
+    // j: the first index >= 1 with c[j] >= te, or last + 1
+    int64_t g = 1;
+    if (te > 0.0) {
+        const double e = te * T.perTerm;
+        g = e < double(last) ? int64_t(e) : last;
+        g = g < 1 ? 1 : g;
+    }
+    int64_t j;
+    if (T.c[g] >= te) {
+        if (g == 1 || T.c[g - 1] < te) {
+            j = g;
+        } else {
+            int64_t lo = 1, hi = g - 1;
+            while (lo < hi) {
+                const int64_t mid = (lo + hi) >> 1;
+                if (T.c[mid] >= te)
+                    hi = mid;
+                else
+                    lo = mid + 1;
+            }
+            j = lo;
+        }
+    } else if (g == last || T.c[g + 1] >= te) {
+        j = g + 1;
+    } else {
+        int64_t lo = g + 2, hi = last + 1;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (T.c[mid] >= te)
+                hi = mid;
+            else
+                lo = mid + 1;
+        }
+        j = lo;
+    }
+    int64_t k = (j - 1) * T.stride;
+    double tt = T.c[j - 1];
+    stops = false;
+    while (k < T.budget) {
+        ++k;
+        tt = __dadd_rn(tt, dt);
+        if (tt >= te) {
+            stops = true;
+            break;
+        }
+    }
+    target = k;
+    tAfter = tt;
+}
+
 /** The persistent entry. Every lane holds its current sample and, one chunk
  *  ahead, the NEXT one: at each chunk head the lanes of a warp lacking a next
  *  sample claim the following indices together off ``hawk_next`` (one atomic per
@@ -112,8 +207,18 @@ __global__ __launch_bounds__(256, 4) void oscillatorPersist(EB_OSC_ROLES(TEnd<Sp
     const int64_t budget = *static_cast<const int64_t*>(fused.data);
     const int chunk = hawkChunk == 0 ? 32 : int(hawkChunk < (1u << 20) ? hawkChunk : (1u << 20));
     uint32_t* finished_ = static_cast<uint32_t*>(finished.data);
+    __shared__ double sT[kTCoarse + 1];
+    __shared__ int sStride;
+    if (threadIdx.x == 0)
+        sStride = buildTTable(sT, dt, budget);
+    __syncthreads();
+    const TTable table{sT, sStride, budget, sStride != 0 ? 1.0 / (dt * double(sStride)) : 0.0};
     Oscillator<Fma> cur{}, nxt{};
     int64_t i = -1, ni = -1;  // the lane's current and prefetched samples (-1: none)
+    bool fast = false;        // the current sample started at t = +0: its stop is known
+    int64_t target = 0;       // fast: the steps it runs in this launch
+    bool stops = false;       // fast: it terminates on the last of them
+    double tAfter = 0.0;      // fast: its t after them
     uint8_t nterm = 0;        // the prefetched sample's mask byte
     int64_t taken = 0;        // steps of the current sample so far
     bool exhausted = false;
@@ -154,6 +259,9 @@ __global__ __launch_bounds__(256, 4) void oscillatorPersist(EB_OSC_ROLES(TEnd<Sp
                 cur.c = Oscillator<Fma>::coeff(dt, nxt.c);
                 i = ni;
                 taken = 0;
+                fast = table.stride != 0 && __double_as_longlong(cur.t) == 0;
+                if (fast)
+                    tTarget(table, dt, cur.te, target, stops, tAfter);
             }
             ni = -1;
         }
@@ -169,9 +277,20 @@ __global__ __launch_bounds__(256, 4) void oscillatorPersist(EB_OSC_ROLES(TEnd<Sp
         int ran = 0;
         bool fin = false;
         if (active) {
-            const int64_t room = budget - taken;
-            ran = cur.run(dt, int(room < chunk ? room : chunk), fin);
-            taken += ran;
+            if (fast) {
+                const int64_t room = target - taken;
+                ran = int(room < chunk ? room : chunk);
+                cur.stepsXV(dt, ran);
+                taken += ran;
+                if (taken == target) {
+                    cur.t = tAfter;
+                    fin = stops;
+                }
+            } else {
+                const int64_t room = budget - taken;
+                ran = cur.run(dt, int(room < chunk ? room : chunk), fin);
+                taken += ran;
+            }
         }
         ranSum += (unsigned long long)ran;
         slots += (unsigned long long)chunk;

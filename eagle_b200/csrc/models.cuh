@@ -24,6 +24,7 @@ namespace eb {
 template <bool Fma>
 struct Oscillator {
     double x, v, t, c, te;
+    static constexpr int kBlock = 8;
 
     static __device__ __forceinline__ double coeff(double dt, double omega)
     {
@@ -51,7 +52,19 @@ struct Oscillator {
         t = __dadd_rn(t, dt);
     }
 
-    static constexpr int kBlock = 8;
+    /** x and v ``n`` (>= 0) steps on, t untouched: for a sample whose stop step is
+     *  known in advance. */
+    __device__ __forceinline__ void stepsXV(double dt, int n)
+    {
+        int k = 0;
+        for (; k + kBlock <= n; k += kBlock) {
+#pragma unroll
+            for (int j = 0; j < kBlock; ++j)
+                stepXV(dt);
+        }
+        for (; k < n; ++k)
+            stepXV(dt);
+    }
 
     /** Run at most ``budget`` (>= 0) steps; returns the steps run, ``fin`` true if
      *  the sample terminated on the last of them.
