@@ -625,7 +625,13 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
             std::memcpy(e->iuniforms, d.iuniforms, sizeof e->iuniforms);
             std::memcpy(e->uext, d.uniforms_ext, sizeof e->uext);
             e->term = reinterpret_cast<uint8_t*>(d.terminated);
-            e->chunk = d.chunk != 0 ? d.chunk : d.model == EAGLE_B200_MODEL_LORENZ ? 8u : 256u;
+            // steps per claim head: an oscillator lane idles from its sample's end to the next
+            // head, a head costs a claim and a swap; 512 measured best for the oscillator (5.74
+            // against 5.90 ms at 256 and 6.32 ms at 1024 for 2^24 heterogeneous stops)
+            e->chunk = d.chunk != 0 ? d.chunk
+                : d.model == EAGLE_B200_MODEL_LORENZ ? 8u
+                : d.model == EAGLE_B200_MODEL_GAMBLER ? 256u
+                                                      : 512u;
             e->block = d.model == EAGLE_B200_MODEL_LORENZ ? 128u : 256u;
             cudaCheck(cudaMalloc(&e->cells, sizeof(Cells)), "cudaMalloc");
             cudaCheck(cudaMallocHost(&e->host, sizeof(Cells)), "cudaMallocHost");
