@@ -54,7 +54,7 @@ def _args():
                         "2^28, the physical reorder and the K-class sort of 2^24) for their own lines")
     p.add_argument("--no-fma", action="store_true", help="exact (uncontracted) arithmetic profile")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--e2e-chunks", type=int, default=16)
+    p.add_argument("--e2e-chunks", type=int, default=8)
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     return p.parse_args()

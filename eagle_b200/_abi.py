@@ -301,6 +301,8 @@ SIGNATURES = {
     "eagle_backend_x_b200_engine_create": (_i32, [ctypes.POINTER(EngineDesc), ctypes.POINTER(_P)]),
     "eagle_backend_x_b200_engine_launch": (_i32, [_P, _u64]),
     "eagle_backend_x_b200_engine_report": (_i32, [_P, _u64, ctypes.POINTER(Report)]),
+    "eagle_backend_x_b200_engine_report_enqueue": (_i32, [_P, _u64]),
+    "eagle_backend_x_b200_engine_report_read": (_i32, [_P, ctypes.POINTER(Report)]),
     "eagle_backend_x_b200_engine_run": (_i32, [_P, _u64, ctypes.POINTER(Report)]),
     "eagle_backend_x_b200_engine_release": (None, [_P]),
 }

@@ -416,7 +416,7 @@ class StagedRunner:
     whatever its size, and its resident CTAs wait out that tail, so narrower runs
     side by side keep the tails of one chunk under the work of the others."""
 
-    def __init__(self, model: Model, *, max_steps: int, chunks: int = 16, streams: int = 4, ctas_per_sm: int = 1,
+    def __init__(self, model: Model, *, max_steps: int, chunks: int = 8, streams: int = 4, ctas_per_sm: int = 1,
                  full_tail: int = 2, terminated=None, device=None, **kwargs):
         torch = _t()
         per_sample = {k: v for k, v in kwargs.items() if isinstance(v, torch.Tensor) and v.is_cuda and v.dim() == 1}
@@ -478,8 +478,23 @@ class StagedRunner:
             stream.wait_event(ev)
 
     def report(self, stream=None) -> RunReport:
-        """The run's report over all chunks (one small read per chunk)."""
-        reps = [r.report(stream) for r in self.runners]
+        """The run's report over all chunks: every chunk's counters copied on
+        ``stream``, one host wait, then read."""
+        torch = _t()
+        lib = _abi.lib()
+        s = _stream_handle(stream)
+        with torch.cuda.device(self.device):
+            for r in self.runners:
+                _abi.check(lib.eagle_backend_x_b200_engine_report_enqueue(r._h, s))
+            (stream if stream is not None else torch.cuda.current_stream(self.device)).synchronize()
+            reps = []
+            for r in self.runners:
+                rep = _abi.new(_abi.Report)
+                _abi.check(lib.eagle_backend_x_b200_engine_report_read(r._h, ctypes.byref(rep)))
+                reps.append(RunReport(n=int(rep.n), finished=int(rep.finished), done=bool(rep.done),
+                                      steps=int(rep.steps), launches=int(rep.launches),
+                                      compactions=int(rep.compactions), step_sum=int(rep.step_sum), mode=self.mode,
+                                      report_bytes=int(rep.report_bytes)))
         fin = sum(r.finished for r in reps)
         return RunReport(n=self.n, finished=fin, done=fin == self.n, steps=max(r.steps for r in reps),
                          launches=sum(r.launches for r in reps), compactions=sum(r.compactions for r in reps),

@@ -519,10 +519,9 @@ void launchEngine(Engine& e, cudaStream_t s)
     cudaCheck(cudaLaunchKernel(stub, dim3(grid), dim3(e.block), args.data(), 0, s), "cudaLaunchKernel");
 }
 
-void readReport(Engine& e, cudaStream_t s, eagle_b200_report* out)
+/** The report from the host copy of the cells (already landed). */
+void fillReport(const Engine& e, eagle_b200_report* out)
 {
-    cudaCheck(cudaMemcpyAsync(e.host, e.cells, sizeof(Cells), cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
-    cudaCheck(cudaStreamSynchronize(s), "cudaStreamSynchronize");
     const Cells& c = *e.host;
     eagle_b200_report r{};
     r.struct_size = sizeof r;
@@ -547,6 +546,13 @@ void readReport(Engine& e, cudaStream_t s, eagle_b200_report* out)
     const uint32_t size = out->struct_size < sizeof r ? out->struct_size : uint32_t(sizeof r);
     std::memcpy(out, &r, size);
     out->struct_size = size;
+}
+
+void readReport(Engine& e, cudaStream_t s, eagle_b200_report* out)
+{
+    cudaCheck(cudaMemcpyAsync(e.host, e.cells, sizeof(Cells), cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
+    cudaCheck(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    fillReport(e, out);
 }
 
 void destroy(Engine* e)
@@ -732,6 +738,34 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_report(eagle_b200_engine
         auto* e = reinterpret_cast<Engine*>(h);
         DeviceScope scope(e->device);
         readReport(*e, seamStream(stream), report);
+        if (report->struct_size >= offsetof(eagle_b200_report, error) + sizeof(uint32_t) && report->error != 0)
+            fail(EAGLE_BACKEND_ERROR, "eagle_b200 engine: a device-side wait gave up (error word "
+                + std::to_string(report->error) + "); the run's results are not valid");
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_engine_report_enqueue(eagle_b200_engine h, uint64_t stream)
+{
+    return guarded([&] {
+        if (h == nullptr)
+            fail(EAGLE_BACKEND_BAD_HANDLE, "eagle_backend_x_b200_engine_report_enqueue: null handle");
+        auto* e = reinterpret_cast<Engine*>(h);
+        DeviceScope scope(e->device);
+        cudaCheck(cudaMemcpyAsync(e->host, e->cells, sizeof(Cells), cudaMemcpyDeviceToHost, seamStream(stream)),
+            "cudaMemcpyAsync");
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_engine_report_read(eagle_b200_engine h,
+    struct eagle_b200_report* report)
+{
+    return guarded([&] {
+        if (h == nullptr)
+            fail(EAGLE_BACKEND_BAD_HANDLE, "eagle_backend_x_b200_engine_report_read: null handle");
+        if (report == nullptr || report->struct_size < 8)
+            invalid("eagle_backend_x_b200_engine_report_read: null or short report");
+        const auto* e = reinterpret_cast<const Engine*>(h);
+        fillReport(*e, report);
         if (report->struct_size >= offsetof(eagle_b200_report, error) + sizeof(uint32_t) && report->error != 0)
             fail(EAGLE_BACKEND_ERROR, "eagle_b200 engine: a device-side wait gave up (error word "
                 + std::to_string(report->error) + "); the run's results are not valid");

@@ -787,6 +787,12 @@ eagle_backend_status eagle_backend_x_b200_engine_launch(eagle_b200_engine h, uin
 /* Wait for ``stream`` and read the last run's report (one device-to-host copy). */
 eagle_backend_status eagle_backend_x_b200_engine_report(eagle_b200_engine h, uint64_t stream,
     struct eagle_b200_report* report);
+/* The report in two halves, so that many engines' reports cost one host wait:
+ * report_enqueue puts the device-to-host copy of the run's counters on ``stream``
+ * (no wait); report_read fills ``report`` from that copy and must follow a wait
+ * for the stream (cudaStreamSynchronize, an event, ...) that covers the copy. */
+eagle_backend_status eagle_backend_x_b200_engine_report_enqueue(eagle_b200_engine h, uint64_t stream);
+eagle_backend_status eagle_backend_x_b200_engine_report_read(eagle_b200_engine h, struct eagle_b200_report* report);
 /* launch + report. */
 eagle_backend_status eagle_backend_x_b200_engine_run(eagle_b200_engine h, uint64_t stream,
     struct eagle_b200_report* report);
