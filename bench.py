@@ -48,10 +48,12 @@ def _args():
     p.add_argument("--impl", default="engine", choices=("engine", "reference"))
     p.add_argument("--mode", default="auto", choices=("auto", "band", "band_eager", "persist", "fused"))
     p.add_argument("--n", type=int, default=None, help="samples per GPU (default: the workload's)")
-    p.add_argument("--workload", default="oscillator", choices=("oscillator", "lorenz", "gambler", "compact_sum", "reorder"),
+    p.add_argument("--workload", default="oscillator",
+                   choices=("oscillator", "lorenz", "gambler", "compact_sum", "compact", "reorder"),
                    help="oscillator: the headline 16M heterogeneous-stop run; the others time the other "
                         "configurations' kernels (Lorenz RKF7(8) 2^22, gambler's ruin 2^26, compact-then-sum "
-                        "2^28, the physical reorder and the K-class sort of 2^24) for their own lines")
+                        "2^28, the active-set compaction alone 2^28, the physical reorder and the K-class "
+                        "sort of 2^24) for their own lines")
     p.add_argument("--no-fma", action="store_true", help="exact (uncontracted) arithmetic profile")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-chunks", type=int, default=8)
@@ -620,6 +622,48 @@ def side_workload(args):
                                       "kind": "port", "sample": f"the first {m} slots, numpy stable partition "
                                                                 f"({sec:.2f} s)"},
                      "gpu_launches": (2 + 2 * 8 + 1) + (3 + 2 * 8 + 2), "clocks": clocks.summary()})
+    elif args.workload == "compact":
+        # the active-set compaction alone (compact_device: ascending index map + count),
+        # 2^28 samples, keep masks Bernoulli(p), p in {0.9, 0.5, 0.1, 0.01} (seeds 7 + i)
+        n = args.n or (1 << 28)
+        ps = (0.9, 0.5, 0.1, 0.01)
+        masks = [torch.from_numpy(np.random.default_rng(7 + i).random(n) < p).to(dev) for i, p in enumerate(ps)]
+        comps = [eb.Compactor(mk, drop=False) for mk in masks]
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MiB: evicts the 126 MB L2
+
+        def step():
+            for c in comps:
+                flush.zero_()
+                c(stream)
+
+        with _Clocks(0) as clocks:
+            ms = _timed(step, args.steps, args.warmup, stream)
+        flush_ms = _timed(lambda: [flush.zero_() for _ in ps], 3, 1, stream)
+        work_ms = max(ms - flush_ms, 1e-6)
+        counts = [int(c.count.item()) for c in comps]
+        alg = sum(n + 4 * k for k in counts)  # the mask read, the index map written
+        peak, peak_kind = _peaks()
+        m = min(n, 1 << 24)
+        t0 = time.perf_counter()
+        for i, p in enumerate(ps):
+            oracle.compact(np.random.default_rng(7 + i).random(m) < p, drop=False)
+        sec = time.perf_counter() - t0
+        kept_sample = sum(int(m * p) for p in ps)
+        line.update({"metric": "GB/s, 2^28 active-set compaction vs the HBM roofline",
+                     "value": alg / (work_ms / 1e3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+                     "dtype": "u8 mask, int32 map",
+                     "config": {"workload": "active-set-compaction", "n": n, "p": list(ps), "kept": counts,
+                                "l2": "a 256 MiB buffer is written before every compaction (its time is measured "
+                                      "apart and taken out)", "flush_ms_per_step": flush_ms},
+                     "roofline": {"bound": "hbm", "achieved": alg / (work_ms / 1e3) / 1e9, "peak": peak,
+                                  "unit": "GB/s", "frac": alg / (work_ms / 1e3) / 1e9 / peak, "traffic": None,
+                                  "peak_kind": peak_kind,
+                                  "basis": "n mask bytes read + 4 bytes per kept index written, summed over the "
+                                           "four masks / compaction time"},
+                     "cpu_baseline": {"value": (4 * m + 4 * kept_sample) / sec / 1e9, "unit": "GB/s",
+                                      "cores": 1, "kind": "port",
+                                      "sample": f"the first {m} samples of each mask ({sec:.2f} s)"},
+                     "gpu_launches": 4 * args.steps, "clocks": clocks.summary()})
     else:
         n = args.n or (1 << 28)
         rng = np.random.default_rng(4)
