@@ -189,15 +189,20 @@ __global__ __launch_bounds__(kThreads) void placeKernel(PlaceArgs a)
     // element e of the tile is the (e % 16)-th of thread e / 16's keep bits: read the
     // stage coalesced (lane-consecutive e) and put each element at its tile-local place,
     // the kept ones at [0, kept), the dropped ones at [kept, len)
-#pragma unroll 4
+    T v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {  // all sixteen loads in flight before the first is used
+        const int e = t + j * kThreads;
+        v[j] = int64_t(e) < len ? src[tile0 + e] : T{};
+    }
+#pragma unroll
     for (int j = 0; j < kPer; ++j) {
         const int e = t + j * kThreads;
         if (int64_t(e) < len) {
-            const T v = src[tile0 + e];
             const uint32_t kb = sKeep[e >> 4], bit = uint32_t(e & 15);
             const uint32_t before = sExcl[e >> 4] + __popc(kb & ((1u << bit) - 1u));  // kept before e
             const uint32_t pos = ((kb >> bit) & 1u) ? before : kept + uint32_t(e) - before;
-            out[pos] = v;
+            out[pos] = v[j];
         }
     }
     __syncthreads();
@@ -372,6 +377,7 @@ struct ClassArgs {
     uint32_t classes, nKeys;
     int drop, within;
     uint8_t* keys;   // n: each slot's key, kept while the planes move
+    uint16_t* rel;   // n: each slot's rank among its tile's slots of the same key
     uint32_t* hist;  // nKeys x tiles, key-major: counts, then the first destinations
     uint32_t tiles;
 };
@@ -423,12 +429,25 @@ __global__ __launch_bounds__(kThreads) void classHistKernel(ClassArgs a)
     uint32_t kr[kRounds];
     rankTile(a.keys, tile0, lim, cnt, kr);
     __syncthreads();
-    if (uint32_t(t) < a.nKeys) {
-        uint32_t total = 0;
+    // per key: each warp's first rank (the counts of the warps before it) and the total
+    uint32_t total = 0;
 #pragma unroll
-        for (int q = 0; q < kWarps; ++q)
-            total += cnt[q][t];
+    for (int q = 0; q < kWarps; ++q) {
+        const uint32_t c = cnt[q][t];
+        cnt[q][t] = uint16_t(total);
+        total += c;
+    }
+    if (uint32_t(t) < a.nKeys)
         a.hist[size_t(t) * a.tiles + blockIdx.x] = total;
+    __syncthreads();
+    // each slot's rank within its key's run of the tile, for every plane's place
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+        const uint32_t k = kr[r] >> 16;
+        if (k != kNoKey) {
+            const int64_t i = tile0 + int64_t(w) * (kRounds * 32) + int64_t(r) * 32 + lane;
+            a.rel[i] = uint16_t(cnt[w][k] + (kr[r] & 0xffffu));
+        }
     }
 }
 
@@ -499,6 +518,9 @@ struct ClassPlaceArgs {
     const void* stage;
     void* plane;
     const uint8_t* keys;
+    const uint16_t* rel;     // each slot's rank within its key's run of the tile
+    const uint32_t* total;   // the count matrix's total (the entry after the last)
+    uint32_t nKeys;
     const uint32_t* base;  // nKeys x tiles first destinations
     const uint32_t* lim;
     const uint32_t* fire;
@@ -516,46 +538,47 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
     if (*a.err != 0u)
         return;
     extern __shared__ __align__(16) unsigned char smem[];
-    T* out = reinterpret_cast<T*>(smem);                               // the tile in key order
+    T* out = reinterpret_cast<T*>(smem);                                     // the tile in key order
     uint8_t* outKey = reinterpret_cast<uint8_t*>(smem + kTile * sizeof(T));  // each place's key
-    __shared__ uint16_t cnt[kWarps][256];
     __shared__ uint32_t sStart[256];
     __shared__ uint32_t scan[33];
     const int t = int(threadIdx.x);
-    for (int q = t; q < kWarps * 256; q += kThreads)
-        (&cnt[0][0])[q] = 0;
-    __syncthreads();
     const int64_t lim = spanOf(a.lim, a.n);
     const int64_t tile0 = int64_t(blockIdx.x) * kTile;
     if (tile0 >= lim)
         return;
     const int64_t len = lim - tile0 < kTile ? lim - tile0 : kTile;
-    uint32_t kr[kRounds];
-    rankTile(a.keys, tile0, lim, cnt, kr);
-    __syncthreads();
-    // each warp's first rank per key (the counts of the warps before it), and the
-    // tile's count of each key
-    uint32_t total = 0;
-#pragma unroll
-    for (int q = 0; q < kWarps; ++q) {
-        const uint32_t c = cnt[q][t];
-        cnt[q][t] = uint16_t(total);
-        total += c;
+    // the tile's count of each key, from the scanned key-major matrix: the next entry's
+    // first destination (the next key's first tile, or the total after the last) less its own
+    uint32_t c = 0;
+    if (uint32_t(t) < a.nKeys) {
+        const size_t at = size_t(t) * a.tiles + blockIdx.x;
+        const size_t m = size_t(a.nKeys) * a.tiles;
+        c = (at + 1 < m ? a.base[at + 1] : *a.total) - a.base[at];
     }
     uint32_t all = 0;
-    sStart[t] = blockExclusiveSum(total, all, scan);  // the key's first place in the tile
-    __syncthreads();
-    const unsigned lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
+    sStart[t] = blockExclusiveSum(c, all, scan);  // the key's first place in the tile
+    // each slot's value, key and rank among its key's slots (the histogram pass ranked
+    // them): thread t takes slots t, t + 256, ..., all sixteen loads in flight
     const T* src = static_cast<const T*>(a.stage);
+    T v[kPer];
+    uint32_t kr[kPer];
 #pragma unroll
-    for (int r = 0; r < kRounds; ++r) {
-        const uint32_t k = kr[r] >> 16;
-        if (k == kNoKey)
-            continue;
-        const int64_t i = tile0 + int64_t(w) * (kRounds * 32) + int64_t(r) * 32 + lane;
-        const uint32_t pos = sStart[k] + cnt[w][k] + (kr[r] & 0xffffu);
-        out[pos] = src[i];
-        outKey[pos] = uint8_t(k);
+    for (int j = 0; j < kPer; ++j) {
+        const int64_t i = tile0 + t + int64_t(j) * kThreads;
+        const bool in = i - tile0 < len;
+        v[j] = in ? src[i] : T{};
+        kr[j] = in ? (uint32_t(a.keys[i]) << 16) | uint32_t(a.rel[i]) : kNoKey << 16;
+    }
+    __syncthreads();  // sStart
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const uint32_t k = kr[j] >> 16;
+        if (k != kNoKey) {
+            const uint32_t pos = sStart[k] + (kr[j] & 0xffffu);
+            out[pos] = v[j];
+            outKey[pos] = uint8_t(k);
+        }
     }
     __syncthreads();
     // each key's run of the tile is contiguous in the plane: coalesced stores
@@ -563,10 +586,10 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
     for (int q = t; q < int(len); q += kThreads) {
         const uint32_t k = outKey[q];
         const int64_t d = int64_t(a.base[size_t(k) * a.tiles + blockIdx.x]) + (q - int64_t(sStart[k]));
-        const T v = out[q];
-        dst[d] = v;
+        const T val = out[q];
+        dst[d] = val;
         if constexpr (Perm)
-            a.inv[static_cast<int32_t>(v)] = int32_t(d);
+            a.inv[static_cast<int32_t>(val)] = int32_t(d);
     }
 }
 
@@ -604,7 +627,7 @@ __global__ void classFinishKernel(const uint32_t* base, uint32_t tiles, uint32_t
 }
 
 struct ClassLayout {
-    size_t keys, hist, status, words, stage, total;
+    size_t keys, rel, hist, status, words, stage, total;
 };
 
 ClassLayout classLayoutFor(int64_t n, uint32_t elem, uint32_t classes)
@@ -616,7 +639,8 @@ ClassLayout classLayoutFor(int64_t n, uint32_t elem, uint32_t classes)
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
     ClassLayout l{};
     l.keys = 0;
-    l.hist = up(m);
+    l.rel = up(m);
+    l.hist = up(l.rel + m * sizeof(uint16_t));
     l.status = up(l.hist + histN * sizeof(uint32_t));
     l.words = up(l.status + scanTiles * sizeof(uint64_t));
     l.stage = l.words + 256;
@@ -776,6 +800,7 @@ EB_API eagle_backend_status eagle_backend_reorder_classes_device(struct eagle_ba
         c.drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
         c.within = within;
         c.keys = reinterpret_cast<uint8_t*>(raw + l.keys);
+        c.rel = reinterpret_cast<uint16_t*>(raw + l.rel);
         c.hist = reinterpret_cast<uint32_t*>(raw + l.hist);
         c.tiles = uint32_t((d.n + kTile - 1) / kTile);
         ScanU32Args sa{};
@@ -797,6 +822,9 @@ EB_API eagle_backend_status eagle_backend_reorder_classes_device(struct eagle_ba
         ClassPlaceArgs p{};
         p.stage = raw + l.stage;
         p.keys = c.keys;
+        p.rel = c.rel;
+        p.total = sa.total;
+        p.nKeys = c.nKeys;
         p.base = c.hist;
         p.lim = lim;
         p.fire = fire;
