@@ -6,14 +6,14 @@
 // survivors: leaf l holds ranks [4096 l, 4096 l + 4096), and slot t of a leaf folds
 // its ranks t, t + 256, ..., in that order. Writing the survivors out and reading
 // them back costs 16 bytes per survivor on top of the mask and the value sectors,
-// the whole gap between a compaction and its roofline. Instead, after a 16-byte
-// memset:
+// the whole gap between a compaction and its roofline. Instead, after a memset of
+// the claim and chunk counters:
 //
-//   keepCountKernel   one 16384-sample tile per CTA (four coalesced rows of 4096 mask
+//   keepCountKernel   (tiles.cuh) one 16384-sample tile per CTA (four coalesced rows of 4096 mask
 //                     bytes): the keep bits go out as a bitmap (one bit per sample)
 //                     and the tile's count as one word. No look-back: a tile never
 //                     waits on another, so the pass streams.
-//   tileScanKernel    one CTA: the exclusive scan of the tile counts, and the count.
+//   tileScanKernel    (tiles.cuh) one CTA: the exclusive scan of the tile counts, and the count.
 //   leafStartKernel   a warp per tile: for every multiple of 4096 among the tile's
 //                     ranks, the sample holding it (leafStart[l]), from the tile's
 //                     512 bitmap words.
