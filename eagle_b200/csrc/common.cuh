@@ -374,10 +374,11 @@ __device__ __forceinline__ uint32_t nonZero16(uint4 w)
     uint32_t set = 0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        const uint32_t nz = __vcmpne4(words[q], 0u);  // 0xff per non-zero byte
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-            set |= ((nz >> (8 * b)) & 1u) << (4 * q + b);
+        // 0xff per non-zero byte; the multiply moves the top bits of bytes 0..3 (bits 7,
+        // 15, 23, 31) to bits 28..31 -- every partial product lands on its own bit
+        // position, so nothing carries into them
+        const uint32_t nz = __vcmpne4(words[q], 0u) & 0x80808080u;
+        set |= ((nz * 0x00204081u) >> 28) << (4 * q);
     }
     return set;
 }
@@ -396,6 +397,31 @@ __device__ __forceinline__ uint32_t keepBits16(const uint8_t* __restrict__ mask,
             if (i0 + j < n && mask[i0 + j] != 0)
                 set |= 1u << j;
     }
+    const uint32_t valid = i0 >= n ? 0u : (i0 + 16 <= n ? 0xffffu : ((1u << uint32_t(n - i0)) - 1u));
+    return (Drop ? ~set : set) & valid;
+}
+
+/** The 16 mask bytes of samples [i0, i0 + 16) as one 16-byte word (bytes past n read
+ *  as 0): one vector load when the mask is 16-byte aligned and the run whole. Issue
+ *  all of a thread's loads before the first keepOf16, so they are in flight together. */
+template <bool Aligned>
+__device__ __forceinline__ uint4 maskBytes16(const uint8_t* __restrict__ mask, int64_t i0, int64_t n)
+{
+    if (Aligned && i0 + 16 <= n)
+        return __ldg(reinterpret_cast<const uint4*>(mask + i0));
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+        if (i0 + j < n)
+            w[j >> 2] |= uint32_t(mask[i0 + j]) << (8 * (j & 3));
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+/** Keep bits of 16 mask bytes already loaded by maskBytes16 (bit j: sample i0 + j kept). */
+template <bool Drop>
+__device__ __forceinline__ uint32_t keepOf16(uint4 raw, int64_t i0, int64_t n)
+{
+    const uint32_t set = nonZero16(raw);
     const uint32_t valid = i0 >= n ? 0u : (i0 + 16 <= n ? 0xffffu : ((1u << uint32_t(n - i0)) - 1u));
     return (Drop ? ~set : set) & valid;
 }

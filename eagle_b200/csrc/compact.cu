@@ -5,9 +5,9 @@
 // indices, ascending; count; optionally the reorder trigger (live32, fire) of
 // Compact.h:113-118. Eagle runs predicate -> multi-level int64 scan -> scatter
 // (about 2 log256(n) + 2 launches over 8-byte planes). Here it is ONE kernel
-// after a memset of its scratch: each CTA takes the next 16384-sample tile off a
+// after a memset of its scratch: each CTA takes the next 32768-sample tile off a
 // counter (so every tile it waits on is already owned by a running CTA), turns
-// 4 x 16 mask bytes per thread into keep bit-sets, scans the counts across the CTA,
+// 8 x 16 mask bytes per thread into keep bit-sets, scans the counts across the CTA,
 // finds the tile's global offset by a decoupled look-back over the earlier
 // tiles' status words, stages the kept indices in shared memory and writes them
 // with coalesced stores. The trigger's live32 rides in the same status words, so
@@ -20,9 +20,9 @@ namespace eb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kRows = 4;                               // a tile is four rows of 4096 samples
+constexpr int kRows = 8;                               // a tile is eight rows of 4096 samples
 constexpr int64_t kRow = int64_t(kThreads) * 16;       // 16 mask bytes per thread per row
-constexpr int64_t kTile = kRow * kRows;                // 16384 samples per CTA
+constexpr int64_t kTile = kRow * kRows;                // 32768 samples per CTA
 constexpr uint32_t kStage = uint32_t(kRow);            // one row's kept indices at most
 
 struct CompactArgs {
@@ -43,14 +43,16 @@ struct CompactArgs {
     uint32_t elemBytes;  // Gather: 4 or 8
 };
 
-/** One 16384-sample tile per CTA, as four rows of 4096: thread t holds the 16
- *  mask bytes at t * 16 of every row (four coalesced 16-byte loads). One CTA scan
- *  of the four rows' counts packed as 16-bit lanes of a 64-bit word gives each
- *  thread's place in every row, one decoupled look-back the tile's offset; each
- *  row's kept indices then go through shared memory to coalesced stores (the
- *  Gather values are read through the staged indices at the store). Four rows per
- *  look-back keep four times the bytes in flight per round trip, which is what a
- *  sparse mask (few kept, so little else to do) is bound by. */
+/** One 32768-sample tile per CTA, as eight rows of 4096: thread t holds the 16
+ *  mask bytes at t * 16 of every row (eight coalesced 16-byte loads, all in flight
+ *  before the first is used). Two CTA scans of the rows' counts, packed four at a
+ *  time as 16-bit lanes of a 64-bit word, give each thread's place in every row,
+ *  one decoupled look-back the tile's offset; each row's kept indices then go
+ *  through shared memory to coalesced stores (the Gather values are read through
+ *  the staged indices at the store). Eight rows per look-back keep eight times the
+ *  bytes in flight per round trip, which is what a sparse mask (few kept, so
+ *  little else to do) is bound by; a row at most a quarter kept is staged by its
+ *  set bits alone, a denser one by all 16 bits predicated. */
 template <bool Drop, bool Trigger, bool Aligned, bool Gather = false>
 __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
 {
@@ -66,18 +68,29 @@ __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
     const uint32_t tile = sTile;
     const int64_t tile0 = int64_t(tile) * kTile;
     uint32_t bits[kRows];
-    uint64_t packed = 0;  // row q's count in bits [16q, 16q + 16)
+    uint64_t packed[kRows / 4] = {};  // row q's count in bits [16 (q % 4), + 16) of word q / 4
+    uint4 raw[kRows];
+#pragma unroll
+    for (int q = 0; q < kRows; ++q)  // every row's load in flight before the first is used
+        raw[q] = maskBytes16<Aligned>(a.mask, tile0 + int64_t(q) * kRow + int64_t(t) * 16, a.n);
 #pragma unroll
     for (int q = 0; q < kRows; ++q) {
-        bits[q] = keepBits16<Drop, Aligned>(a.mask, tile0 + int64_t(q) * kRow + int64_t(t) * 16, a.n);
-        packed |= uint64_t(__popc(bits[q])) << (16 * q);
+        bits[q] = keepOf16<Drop>(raw[q], tile0 + int64_t(q) * kRow + int64_t(t) * 16, a.n);
+        packed[q / 4] |= uint64_t(__popc(bits[q])) << (16 * (q % 4));
     }
-    uint64_t rowTotals = 0;
-    const uint64_t excl = blockExclusiveSum(packed, rowTotals, scan64);
+    uint32_t exclRow[kRows], rowTotal[kRows];  // the thread's place in each row; each row's count
     uint32_t total = 0;
 #pragma unroll
-    for (int q = 0; q < kRows; ++q)
-        total += uint32_t(rowTotals >> (16 * q)) & 0xffffu;
+    for (int w = 0; w < kRows / 4; ++w) {
+        uint64_t tot = 0;
+        const uint64_t ex = blockExclusiveSum(packed[w], tot, scan64);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            exclRow[4 * w + q] = uint32_t(ex >> (16 * q)) & 0xffffu;
+            rowTotal[4 * w + q] = uint32_t(tot >> (16 * q)) & 0xffffu;
+            total += rowTotal[4 * w + q];
+        }
+    }
     uint32_t groups = 0;
     if constexpr (Trigger) {
         // a 32-sample group is two neighbouring threads of a row (rows start on a multiple of 32)
@@ -131,16 +144,20 @@ __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
     };
 #pragma unroll
     for (int q = 0; q < kRows; ++q) {
-        const uint32_t rowTotal = uint32_t(rowTotals >> (16 * q)) & 0xffffu;
-        if (fill + rowTotal > kStage)
+        if (fill + rowTotal[q] > kStage)
             flush();
-        uint32_t k = fill + (uint32_t(excl >> (16 * q)) & 0xffffu);
-        const int64_t i0 = tile0 + int64_t(q) * kRow + int64_t(t) * 16;
+        uint32_t k = fill + exclRow[q];
+        const int32_t i0 = int32_t(tile0 + int64_t(q) * kRow + int64_t(t) * 16);
+        if (rowTotal[q] > uint32_t(kRow / 4)) {  // a dense row (the choice is the CTA's): every bit, predicated
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if ((bits[q] >> j) & 1u)
-                stage[k++] = int32_t(i0 + j);
-        fill += rowTotal;
+            for (int j = 0; j < 16; ++j)
+                if ((bits[q] >> j) & 1u)
+                    stage[k++] = i0 + j;
+        } else {
+            for (uint32_t x = bits[q]; x != 0; x &= x - 1u)  // the set bits only
+                stage[k++] = i0 + (__ffs(int(x)) - 1);
+        }
+        fill += rowTotal[q];
     }
     if (fill != 0)
         flush();

@@ -38,9 +38,13 @@ __global__ __launch_bounds__(kThreads) void keepCountKernel(const uint8_t* __res
     const int64_t tile0 = tile * kTile;
     uint32_t bits[kRows];
     uint32_t c = 0, live = 0;
+    uint4 raw[kRows];
+#pragma unroll
+    for (int q = 0; q < kRows; ++q)  // every row's load in flight before the first is used
+        raw[q] = maskBytes16<Aligned>(mask, tile0 + int64_t(q) * kRow + int64_t(t) * 16, n);
 #pragma unroll
     for (int q = 0; q < kRows; ++q) {
-        bits[q] = keepBits16<Drop, Aligned>(mask, tile0 + int64_t(q) * kRow + int64_t(t) * 16, n);
+        bits[q] = keepOf16<Drop>(raw[q], tile0 + int64_t(q) * kRow + int64_t(t) * 16, n);
         c += uint32_t(__popc(bits[q]));
     }
     // threads 2u and 2u + 1 hold the low and high halves of one 32-sample word

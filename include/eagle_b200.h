@@ -615,7 +615,7 @@ eagle_backend_status eagle_backend_pointer_residency(int32_t device, uint64_t pt
  * cannot allocate device memory (no counterpart in the reference: eagle's
  * compaction always takes caller scratch). Same desc, same outputs, same flags and
  * trigger; ``scratch`` must be 0 and no query is needed. Its working memory is a
- * fixed 128 KiB + 256 B array inside this library on every device that loads it,
+ * fixed 64 KiB + 256 B array inside this library on every device that loads it,
  * enough for n <= 2^28 samples; a larger n returns UNSUPPORTED. It allocates
  * nothing: it enqueues one memset of that array and the compaction kernel. The
  * first call on a device looks the array's address up (cudaGetSymbolAddress), so

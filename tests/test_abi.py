@@ -101,7 +101,7 @@ def test_desc_layouts_match_the_header(tmp_path):
 def test_compact_query_needs_no_device():
     d = _abi.new(_abi.CompactDesc, n=100_003, flags=_abi.COMPACT_MASK_IS_DROP)
     assert _abi.lib().eagle_backend_compact_device(ctypes.byref(d)) == _abi.OK
-    assert d.scratch_bytes >= 8 * ((100_003 + 16383) // 16384)  # one status word per 16384-sample tile
+    assert d.scratch_bytes >= 8 * ((100_003 + 32767) // 32768)  # one status word per 32768-sample tile
 
 
 def test_compact_refuses_past_int32_and_negative():
