@@ -23,7 +23,15 @@ constexpr int kThreads = 256;
 constexpr int kRows = 8;                               // a tile is eight rows of 4096 samples
 constexpr int64_t kRow = int64_t(kThreads) * 16;       // 16 mask bytes per thread per row
 constexpr int64_t kTile = kRow * kRows;                // 32768 samples per CTA
-constexpr uint32_t kStage = uint32_t(kRow);            // one row's kept indices at most
+constexpr uint32_t kStage = uint32_t(kTile / 4);       // kept indices staged in the tile's mask bytes
+constexpr int kCtasPerSm = 6;                          // 33 KB of shared memory and <= 40 registers each
+
+/** 16-byte ``cp.async`` (L2 only) from global to shared memory; both addresses 16-byte aligned. */
+__device__ __forceinline__ void cpAsync16(uint8_t* dst, const uint8_t* src)
+{
+    const uint32_t d = uint32_t(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src) : "memory");
+}
 
 struct CompactArgs {
     const uint8_t* mask;
@@ -54,42 +62,52 @@ struct CompactArgs {
  *  little else to do) is bound by; a row at most a quarter kept is staged by its
  *  set bits alone, a denser one by all 16 bits predicated. */
 template <bool Drop, bool Trigger, bool Aligned, bool Gather = false>
-__global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
+__global__ __launch_bounds__(kThreads, kCtasPerSm) void compactKernel(CompactArgs a)
 {
     __shared__ uint32_t sTile;
     __shared__ uint64_t scan64[33];
     __shared__ uint32_t scan[33];
     __shared__ uint64_t sPrefix;
-    __shared__ int32_t stage[kStage];
+    // the tile's mask bytes; once every thread holds its keep bits, the staging area
+    __shared__ __align__(16) uint8_t sMask[kTile];
+    int32_t* stage = reinterpret_cast<int32_t*>(sMask);
     const int t = int(threadIdx.x);
     if (t == 0)
         sTile = atomicAdd(a.tileNext, 1u);
     __syncthreads();
     const uint32_t tile = sTile;
     const int64_t tile0 = int64_t(tile) * kTile;
+    // every row's 16 bytes copied to shared memory before the first is used: the copies
+    // are in flight together without holding registers (a thread reads back only its own)
+    if (Aligned && tile0 + kTile <= a.n) {
+#pragma unroll
+        for (int q = 0; q < kRows; ++q)
+            cpAsync16(sMask + q * kRow + t * 16, a.mask + tile0 + int64_t(q) * kRow + int64_t(t) * 16);
+        asm volatile("cp.async.commit_group;\n"
+                     "cp.async.wait_group 0;\n" ::: "memory");
+    } else {  // the last tile, or a mask not 16-byte aligned
+#pragma unroll 1
+        for (int q = 0; q < kRows; ++q)
+            *reinterpret_cast<uint4*>(sMask + q * kRow + t * 16) =
+                maskBytes16<Aligned>(a.mask, tile0 + int64_t(q) * kRow + int64_t(t) * 16, a.n);
+    }
     uint32_t bits[kRows];
     uint64_t packed[kRows / 4] = {};  // row q's count in bits [16 (q % 4), + 16) of word q / 4
-    uint4 raw[kRows];
-#pragma unroll
-    for (int q = 0; q < kRows; ++q)  // every row's load in flight before the first is used
-        raw[q] = maskBytes16<Aligned>(a.mask, tile0 + int64_t(q) * kRow + int64_t(t) * 16, a.n);
 #pragma unroll
     for (int q = 0; q < kRows; ++q) {
-        bits[q] = keepOf16<Drop>(raw[q], tile0 + int64_t(q) * kRow + int64_t(t) * 16, a.n);
+        const uint4 raw = *reinterpret_cast<const uint4*>(sMask + q * kRow + t * 16);
+        bits[q] = keepOf16<Drop>(raw, tile0 + int64_t(q) * kRow + int64_t(t) * 16, a.n);
         packed[q / 4] |= uint64_t(__popc(bits[q])) << (16 * (q % 4));
     }
-    uint32_t exclRow[kRows], rowTotal[kRows];  // the thread's place in each row; each row's count
+    // the thread's place in each row and each row's count, four rows to a 64-bit word
+    uint64_t exclRows[kRows / 4], rowTotals[kRows / 4];
     uint32_t total = 0;
 #pragma unroll
     for (int w = 0; w < kRows / 4; ++w) {
-        uint64_t tot = 0;
-        const uint64_t ex = blockExclusiveSum(packed[w], tot, scan64);
+        exclRows[w] = blockExclusiveSum(packed[w], rowTotals[w], scan64);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            exclRow[4 * w + q] = uint32_t(ex >> (16 * q)) & 0xffffu;
-            rowTotal[4 * w + q] = uint32_t(tot >> (16 * q)) & 0xffffu;
-            total += rowTotal[4 * w + q];
-        }
+        for (int q = 0; q < 4; ++q)
+            total += uint32_t(rowTotals[w] >> (16 * q)) & 0xffffu;
     }
     uint32_t groups = 0;
     if constexpr (Trigger) {
@@ -144,11 +162,12 @@ __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
     };
 #pragma unroll
     for (int q = 0; q < kRows; ++q) {
-        if (fill + rowTotal[q] > kStage)
+        const uint32_t rowTotal = uint32_t(rowTotals[q / 4] >> (16 * (q % 4))) & 0xffffu;
+        if (fill + rowTotal > kStage)
             flush();
-        uint32_t k = fill + exclRow[q];
+        uint32_t k = fill + (uint32_t(exclRows[q / 4] >> (16 * (q % 4))) & 0xffffu);
         const int32_t i0 = int32_t(tile0 + int64_t(q) * kRow + int64_t(t) * 16);
-        if (rowTotal[q] > uint32_t(kRow / 4)) {  // a dense row (the choice is the CTA's): every bit, predicated
+        if (rowTotal > uint32_t(kRow / 4)) {  // a dense row (the choice is the CTA's): every bit, predicated
 #pragma unroll
             for (int j = 0; j < 16; ++j)
                 if ((bits[q] >> j) & 1u)
@@ -157,7 +176,7 @@ __global__ __launch_bounds__(kThreads) void compactKernel(CompactArgs a)
             for (uint32_t x = bits[q]; x != 0; x &= x - 1u)  // the set bits only
                 stage[k++] = i0 + (__ffs(int(x)) - 1);
         }
-        fill += rowTotal[q];
+        fill += rowTotal;
     }
     if (fill != 0)
         flush();
