@@ -82,6 +82,20 @@ def _peaks():
         return 6650.0, "fallback"
 
 
+def _fp64_peak():
+    """FP64 lane-instructions per second of this GPU, in T/s: 64 FP64 lanes per SM per
+    cycle x SMs x the measured max SM clock (no FP64 figure is measured on this pool)."""
+    import torch
+
+    props = torch.cuda.get_device_properties(0)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            mhz = float(json.load(f)["sm_max_mhz"])
+    except Exception:
+        mhz = 1965.0
+    return 64 * props.multi_processor_count * mhz * 1e6 / 1e12
+
+
 class _Clocks:
     """SM clock and clock-event reasons sampled through NVML every 10 ms during the
     timed region (reading only; nothing is set)."""
@@ -373,6 +387,17 @@ def engine(args):
                 traffic = json.load(f).get(f"{mode}_{'fma' if fma else 'exact'}")
         except Exception:
             traffic = None
+    # the physical bounds beside the effective figure: DRAM bytes per launch (ncu) over the
+    # engine time, and FP64 issue -- 2 DFMA lane-instructions per sample-step on the known-stop
+    # path (x and v; t is not added per step), one more (the t add) on the step-by-step one;
+    # twice as many uncontracted
+    fp64_per_step = (2 if fma else 4) + (0 if mode == "persist" else 1)
+    fp64_peak = _fp64_peak()
+    fp64_rate = fp64_per_step * steps_per_run / (eng / 1e3) / 1e12
+    physical = {"dram_gbs": traffic / (eng / 1e3) / 1e9 if traffic else None,
+                "fp64": {"achieved": fp64_rate, "peak": fp64_peak, "unit": "T FP64 lane-instructions/s",
+                         "frac": fp64_rate / fp64_peak, "per_sample_step": fp64_per_step,
+                         "peak_kind": "derived: 64 FP64 lanes per SM per cycle x SMs x the measured max SM clock"}}
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -388,7 +413,8 @@ def engine(args):
                      "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                      "basis": "66 B per sample-step (eagle's unfused per-step plane traffic) x sample-steps "
                               "per run / engine time per run; the fused kernel keeps state in registers, so "
-                              "this effective figure exceeds the physical DRAM rate"},
+                              "this effective figure exceeds the physical DRAM rate",
+                     "physical": physical},
         "clocks": clocks.summary(),
     }
     res = result.cpu().numpy()
@@ -479,13 +505,7 @@ def side_workload(args):
         rep = runner.report(stream)
         instr = _profile_value("lorenz_fp64_instr_per_attempt")
         achieved = instr * rep.step_sum / (ms / 1e3) / 1e12 if instr else None
-        props = torch.cuda.get_device_properties(0)
-        try:
-            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-                mhz = float(json.load(f)["sm_max_mhz"])
-        except Exception:
-            mhz = 1965.0
-        fp64_peak = 64 * props.multi_processor_count * mhz * 1e6 / 1e12  # FP64 lanes per SM per cycle
+        fp64_peak = _fp64_peak()
         m = min(n, 1 << 15)
         host = {k: v[:m].copy() for k, v in init.items()}
         na, nr, term = np.zeros(m, np.uint32), np.zeros(m, np.uint32), np.zeros(m, np.uint8)
