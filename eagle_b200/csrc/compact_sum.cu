@@ -24,10 +24,12 @@
 //                     every full row of 256 ranks folded slot by slot in rank order,
 //                     and the in-leaf tree in registers and shuffles. Sparser leaves
 //                     go on a list.
-//   keptSparseKernel  CTAs take the listed leaves one at a time: a CTA scan of the
-//                     leaf's bitmap words, the kept sample indices staged in shared
-//                     memory by rank, each thread loading its slot's 16 values
-//                     together, one warp running the in-leaf tree.
+//   keptSparseKernel  CTAs take the listed leaves one at a time: the survivors
+//                     staged in shared memory by rank (a leaf over many bitmap tiles
+//                     by its tiles spread over the warps, each tile ranked from its
+//                     scanned offset; a denser one by a CTA scan of its bitmap words),
+//                     each thread loading its slot's 16 values together, one warp
+//                     running the in-leaf tree.
 //   The warp that finishes the last leaf of an aligned chunk of 512 joins the
 //   chunk's leaves by the pairwise levels; the one that finishes the last chunk,
 //   the chunks, and stores the value. No CTA ever waits on another.
@@ -125,6 +127,7 @@ __global__ __launch_bounds__(kThreads) void leafStartKernel(const uint32_t* __re
 
 struct LeafArgs {
     const uint32_t* bitmap;
+    const uint32_t* tileOff;  // the survivors before each bitmap tile
     const int32_t* leafStart;
     const uint32_t* count;
     const double* values;
@@ -505,16 +508,20 @@ __device__ __forceinline__ int wordsPerThread(int64_t s0, int64_t s1)
 }
 
 /** The sparse pass: CTAs take the leaves the dense pass listed, one leaf per CTA at
- *  a time. Per chunk of 256 K bitmap words (the next chunk's words in flight): a
- *  CTA scan of the words' counts and the kept sample indices staged in shared
- *  memory by rank; then thread t loads the values of ranks t + 256 i, i < 16,
- *  together (each in its own sector: the leaf is sparse) and folds them into slot
- *  t in order; one warp runs the in-leaf tree and finishes the leaf. */
+ *  a time, and stage its survivors' sample indices in shared memory by rank. A leaf
+ *  over at least eight 16384-sample bitmap tiles spreads them over the CTA's warps:
+ *  the front end's scanned tile offset gives the rank of a tile's first survivor, so
+ *  a warp stages its tiles' survivors (those ranked inside the leaf) with no wait on
+ *  the other warps. A denser leaf is walked in chunks of 256 K bitmap words, a CTA
+ *  scan of each chunk's counts giving the ranks. Then thread t loads the values
+ *  of ranks t + 256 i, i < 16, together (each in its own sector: the leaf is
+ *  sparse; every staged index is a bitmap position, so below n) and folds them
+ *  into slot t in order; one warp runs the in-leaf tree and finishes the leaf. */
 __global__ __launch_bounds__(kThreads, 3) void keptSparseKernel(LeafArgs a)
 {
     __shared__ __align__(16) int32_t idx[kLeaf];
     __shared__ P s[2][kSlots];
-    __shared__ uint32_t scan[33];
+    __shared__ uint32_t scan[33], sHits[kThreads / 32];
     __shared__ int64_t sClaim[2][3];  // a claimed leaf and its sample range, two deep
     const int t = int(threadIdx.x);
     const int64_t rows = int64_t(*a.count) > a.n ? 0 : int64_t(*a.count);
@@ -545,44 +552,90 @@ __global__ __launch_bounds__(kThreads, 3) void keptSparseKernel(LeafArgs a)
         if (t == 32)
             claimInto(cur ^ 1);  // the next claim's round trips overlap this leaf
         const int cnt = int(rows - l * kLeaf < kLeaf ? rows - l * kLeaf : kLeaf);
-        const int K = wordsPerThread(s0, s1);
-        const int64_t wEnd = ((s1 - 1) >> 5) + 1;
-        uint32_t word[kMaxK];
+        const int64_t tileEnd = (s1 - 1) / kTile + 1;
+        uint32_t staged = 0;
+        if (tileEnd - s0 / kTile >= kThreads / 32) {
+            // a leaf over at least one tile per warp (under ~3 % kept): the tiles go to the
+            // warps in turn, and a tile's scanned offset gives the rank of its first survivor,
+            // so each warp stages its tiles' survivors ranked inside the leaf with no wait on
+            // the others (lane l holds the tile's words [16 l, 16 l + 16))
+            const int warp = t >> 5, lane = t & 31;
+            const int64_t rank0 = l * int64_t(kLeaf);
+            uint32_t hits = 0;
+            for (int64_t tile = s0 / kTile + warp; tile < tileEnd; tile += kThreads / 32) {
+                const uint4* src = reinterpret_cast<const uint4*>(a.bitmap + tile * kTileWords) + lane * 4;
+                uint32_t w[16];
 #pragma unroll
-        for (int k = 0; k < kMaxK; ++k)
-            word[k] = k < K ? leafWord(a.bitmap, (s0 >> 5) + int64_t(t) * K + k, s0, s1) : 0u;
-        uint32_t base = 0;
-        for (int64_t cw = s0 >> 5; cw < wEnd; cw += int64_t(kThreads) * K) {
-            uint32_t next[kMaxK];
+                for (int k = 0; k < 4; ++k) {
+                    const uint4 x = src[k];
+                    w[4 * k] = x.x;
+                    w[4 * k + 1] = x.y;
+                    w[4 * k + 2] = x.z;
+                    w[4 * k + 3] = x.w;
+                }
+                uint32_t mine = 0;
 #pragma unroll
-            for (int k = 0; k < kMaxK; ++k)
-                next[k] = k < K ? leafWord(a.bitmap, cw + int64_t(kThreads) * K + int64_t(t) * K + k, s0, s1) : 0u;
-            uint32_t mine = 0;
+                for (int k = 0; k < 16; ++k)
+                    mine += uint32_t(__popc(w[k]));
+                const uint32_t excl = warpInclusiveSum(mine) - mine;
+                int64_t r = int64_t(a.tileOff[tile]) + int64_t(excl) - rank0;  // the lane's first rank in the leaf
+                if (r < int64_t(cnt) && r + int64_t(mine) > 0) {
 #pragma unroll
-            for (int k = 0; k < kMaxK; ++k)
-                mine += uint32_t(__popc(word[k]));
-            uint32_t total = 0;
-            uint32_t r = base + blockExclusiveSum(mine, total, scan);
-#pragma unroll
-            for (int k = 0; k < kMaxK; ++k) {
-                uint32_t x = word[k];
-                const int64_t sample0 = (cw + int64_t(t) * K + k) * 32;
-                while (x != 0) {
-                    if (r < uint32_t(kLeaf))
-                        idx[r] = int32_t(sample0 + __ffs(int(x)) - 1);
-                    x &= x - 1u;
-                    ++r;
+                    for (int k = 0; k < 16; ++k) {
+                        const int32_t sample0 = int32_t((tile * kTileWords + lane * 16 + k) * 32);
+                        for (uint32_t x = w[k]; x != 0; x &= x - 1u, ++r)
+                            if (r >= 0 && r < int64_t(cnt)) {
+                                idx[r] = sample0 + (__ffs(int(x)) - 1);
+                                ++hits;
+                            }
+                    }
                 }
             }
-            base += total;
+            hits = warpSum(hits);
+            if (lane == 0)
+                sHits[warp] = hits;
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < kThreads / 32; ++k)
+                staged += sHits[k];
+        } else {
+            // a denser leaf: chunks of 256 K bitmap words (the next chunk's words in flight),
+            // a CTA scan of each chunk's counts giving the ranks
+            const int K = wordsPerThread(s0, s1);
+            const int64_t wEnd = ((s1 - 1) >> 5) + 1;
+            uint32_t word[kMaxK];
 #pragma unroll
             for (int k = 0; k < kMaxK; ++k)
-                word[k] = next[k];
+                word[k] = k < K ? leafWord(a.bitmap, (s0 >> 5) + int64_t(t) * K + k, s0, s1) : 0u;
+            for (int64_t cw = s0 >> 5; cw < wEnd; cw += int64_t(kThreads) * K) {
+                uint32_t next[kMaxK];
+#pragma unroll
+                for (int k = 0; k < kMaxK; ++k)
+                    next[k] = k < K ? leafWord(a.bitmap, cw + int64_t(kThreads) * K + int64_t(t) * K + k, s0, s1)
+                                    : 0u;
+                uint32_t mine = 0;
+#pragma unroll
+                for (int k = 0; k < kMaxK; ++k)
+                    mine += uint32_t(__popc(word[k]));
+                uint32_t total = 0;
+                uint32_t r = staged + blockExclusiveSum(mine, total, scan);
+#pragma unroll
+                for (int k = 0; k < kMaxK; ++k) {
+                    const int32_t sample0 = int32_t((cw + int64_t(t) * K + k) * 32);
+                    for (uint32_t x = word[k]; x != 0; x &= x - 1u, ++r)
+                        if (r < uint32_t(cnt))
+                            idx[r] = sample0 + (__ffs(int(x)) - 1);
+                }
+                staged += total;
+#pragma unroll
+                for (int k = 0; k < kMaxK; ++k)
+                    word[k] = next[k];
+            }
         }
-        if (t == 0 && int(base) != cnt)
-            atomicOr(a.err, 2u);  // the bitmap and the leaf starts disagree
+        if (t == 0 && staged != uint32_t(cnt))
+            atomicOr(a.err, 2u);  // the bitmap, the tile offsets and the leaf starts disagree
         __syncthreads();          // idx holds the leaf
-        const int have = int(base) < cnt ? int(base) : cnt;  // staged entries only
+        const int have = staged == uint32_t(cnt) ? cnt : 0;  // a failed leaf reads nothing
         double v[kTerms];
 #pragma unroll
         for (int i = 0; i < kTerms; ++i)
@@ -714,6 +767,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
         uint32_t* count = reinterpret_cast<uint32_t*>(d.count);
         LeafArgs la{};
         la.bitmap = bitmap;
+        la.tileOff = tileOff;
         la.leafStart = leafStart;
         la.count = count;
         la.values = reinterpret_cast<const double*>(values);
