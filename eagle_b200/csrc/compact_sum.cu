@@ -76,7 +76,7 @@ __device__ __forceinline__ int selectBit(uint32_t x, uint32_t r)
 /** One warp per tile: every leaf whose first rank (a multiple of 4096) falls among
  *  the tile's kept samples gets that sample's index in ``leafStart``. Lane l holds
  *  the tile's words [16 l, 16 l + 16). */
-__global__ __launch_bounds__(kThreads) void leafStartKernel(const uint32_t* __restrict__ bitmap,
+__global__ __launch_bounds__(kThreads, 4) void leafStartKernel(const uint32_t* __restrict__ bitmap,
     const uint32_t* __restrict__ tileCount, const uint32_t* __restrict__ tileOff, int64_t tiles,
     int32_t* __restrict__ leafStart)
 {
@@ -105,20 +105,22 @@ __global__ __launch_bounds__(kThreads) void leafStartKernel(const uint32_t* __re
         for (uint64_t b = b0; b < o + c; b += uint64_t(kLeaf)) {
             const uint32_t r = uint32_t(b - o);  // the boundary's rank inside the tile
             if (r >= excl && r < excl + mine) {
-                uint32_t rem = r - excl;
+                // the word holding the boundary, then its bit (one select, not one per word)
+                uint32_t rem = r - excl, wd = 0;
                 int at = -1;
 #pragma unroll
                 for (int k = 0; k < 16; ++k) {
                     const uint32_t pc = uint32_t(__popc(w[k]));
                     if (at < 0) {
                         if (rem < pc) {
-                            at = (lane * 16 + k) * 32 + selectBit(w[k], rem);
+                            at = k;
+                            wd = w[k];
                         } else {
                             rem -= pc;
                         }
                     }
                 }
-                leafStart[b / uint64_t(kLeaf)] = int32_t(tile * kTile + at);
+                leafStart[b / uint64_t(kLeaf)] = int32_t(tile * kTile + (lane * 16 + at) * 32 + selectBit(wd, rem));
             }
         }
     }

@@ -24,7 +24,7 @@ constexpr int64_t kRow = int64_t(kThreads) * 16;  // 4096 samples: 16 mask bytes
 constexpr int64_t kTile = kRow * kRows;           // 16384 samples per CTA
 constexpr int64_t kWords = kTile / 32;            // a tile's bitmap words
 constexpr int kScanThreads = 1024;
-constexpr int kScanPer = 16;                      // tile counts per scan thread per round
+constexpr int kScanRound = kScanThreads * 8;     // tile counts per scan round (8 per thread)
 
 /** One 16384-sample tile per CTA (a CTA looping over several tiles held more
  *  registers and measured slower: 72-79 against 67 us for 2^28 samples). */
@@ -88,52 +88,88 @@ struct ScanTrigger {
 };
 
 /** tileOff[i] = the kept samples before tile i; ``*count`` = all of them; with a
- *  trigger, live32 and fire as the one-pass compaction writes them. One CTA. */
+ *  trigger, live32 and fire as the one-pass compaction writes them. One CTA, in
+ *  rounds of 8192 counts: the counts come in and the offsets go out as coalesced
+ *  16-byte rows through shared memory, where thread t scans its 8 neighbours (16
+ *  scattered 4-byte stores per thread throttled the load-store queue). */
 __global__ __launch_bounds__(kScanThreads) void tileScanKernel(const uint32_t* __restrict__ tileCount,
     uint32_t* __restrict__ tileOff, int64_t tiles, uint32_t* count, ScanTrigger trig)
 {
+    __shared__ __align__(16) uint32_t buf[kScanRound];
     __shared__ uint32_t scan[33];
     const int t = int(threadIdx.x);
     uint32_t carry = 0, liveSum = 0;
-    for (int64_t r0 = 0; r0 < tiles; r0 += int64_t(kScanThreads) * kScanPer) {
-        const int64_t i0 = r0 + int64_t(t) * kScanPer;
-        uint32_t v[kScanPer];
-        if (i0 + kScanPer <= tiles) {  // four 16-byte loads (the counts start 256-byte aligned)
+    for (int64_t r0 = 0; r0 < tiles; r0 += kScanRound) {
+        // coalesced rows in: thread t takes rows t and t + kScanThreads of four counts
 #pragma unroll
-            for (int k = 0; k < kScanPer / 4; ++k) {
-                const uint4 x = reinterpret_cast<const uint4*>(tileCount + i0)[k];
-                v[4 * k] = x.x;
-                v[4 * k + 1] = x.y;
-                v[4 * k + 2] = x.z;
-                v[4 * k + 3] = x.w;
+        for (int h = 0; h < 2; ++h) {
+            const int row = t + h * kScanThreads;
+            const int64_t i = r0 + int64_t(row) * 4;
+            uint4 x;
+            if (i + 4 <= tiles) {  // the counts start 256-byte aligned
+                x = *reinterpret_cast<const uint4*>(tileCount + i);
+            } else {
+                x.x = i < tiles ? tileCount[i] : 0u;
+                x.y = i + 1 < tiles ? tileCount[i + 1] : 0u;
+                x.z = i + 2 < tiles ? tileCount[i + 2] : 0u;
+                x.w = i + 3 < tiles ? tileCount[i + 3] : 0u;
             }
-        } else {
-#pragma unroll
-            for (int k = 0; k < kScanPer; ++k)
-                v[k] = i0 + k < tiles ? tileCount[i0 + k] : 0u;
+            reinterpret_cast<uint4*>(buf)[row] = x;
         }
-        uint32_t mine = 0;
-#pragma unroll
-        for (int k = 0; k < kScanPer; ++k)
-            mine += v[k];
+        __syncthreads();
+        // thread t scans counts [8 t, 8 t + 8) of the round
+        uint4 lo = reinterpret_cast<const uint4*>(buf)[2 * t], hi = reinterpret_cast<const uint4*>(buf)[2 * t + 1];
+        const uint32_t mine = lo.x + lo.y + lo.z + lo.w + hi.x + hi.y + hi.z + hi.w;
         uint32_t total = 0;
-        uint32_t run = carry + blockExclusiveSum(mine, total, scan);
-#pragma unroll
-        for (int k = 0; k < kScanPer; ++k) {
-            if (i0 + k < tiles)
-                tileOff[i0 + k] = run;
-            run += v[k];
-        }
+        uint32_t run = carry + blockExclusiveSum(mine, total, scan);  // its barriers order buf's reads
+        uint4 olo, ohi;
+        olo.x = run;
+        run += lo.x;
+        olo.y = run;
+        run += lo.y;
+        olo.z = run;
+        run += lo.z;
+        olo.w = run;
+        run += lo.w;
+        ohi.x = run;
+        run += hi.x;
+        ohi.y = run;
+        run += hi.y;
+        ohi.z = run;
+        run += hi.z;
+        ohi.w = run;
+        reinterpret_cast<uint4*>(buf)[2 * t] = olo;
+        reinterpret_cast<uint4*>(buf)[2 * t + 1] = ohi;
         carry += total;
+        __syncthreads();
+        // coalesced rows out
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int row = t + h * kScanThreads;
+            const int64_t i = r0 + int64_t(row) * 4;
+            const uint4 x = reinterpret_cast<const uint4*>(buf)[row];
+            if (i + 4 <= tiles) {
+                *reinterpret_cast<uint4*>(tileOff + i) = x;
+            } else {
+                if (i < tiles)
+                    tileOff[i] = x.x;
+                if (i + 1 < tiles)
+                    tileOff[i + 1] = x.y;
+                if (i + 2 < tiles)
+                    tileOff[i + 2] = x.z;
+                if (i + 3 < tiles)
+                    tileOff[i + 3] = x.w;
+            }
+        }
         if (trig.tileLive != nullptr) {
             uint32_t l = 0;
-#pragma unroll
-            for (int k = 0; k < kScanPer; ++k)
-                l += i0 + k < tiles ? trig.tileLive[i0 + k] : 0u;
+            for (int64_t i = r0 + t; i < r0 + kScanRound && i < tiles; i += kScanThreads)
+                l += trig.tileLive[i];
             uint32_t lt = 0;
             blockExclusiveSum(l, lt, scan);
             liveSum += lt;
         }
+        __syncthreads();  // buf is rewritten by the next round
     }
     if (t == 0) {
         *count = carry;
