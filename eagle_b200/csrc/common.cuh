@@ -312,59 +312,6 @@ __device__ __forceinline__ uint64_t lbExclusivePrefix(const uint64_t* status, ui
     return exclusive;
 }
 
-/** lbExclusivePrefix walked by the whole CTA (every thread calls it, after the
- *  tile published its aggregate): thread j inspects tile ``end - 1 - j``, so one
- *  round covers blockDim.x predecessors. When a thousand tiles are in flight,
- *  most of them still without their inclusive prefix, the warp walk needs dozens
- *  of dependent rounds per tile; this one, a few. ``firstOf`` holds 32 words and
- *  ``scratch`` 33 of shared memory. Returns the exclusive prefix in every thread. */
-template <class Codec>
-__device__ __forceinline__ uint64_t lbExclusivePrefixBlock(const uint64_t* status, uint32_t tile, uint32_t epoch,
-    uint32_t* err, uint32_t* firstOf, uint64_t* scratch)
-{
-    const unsigned lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-    uint64_t exclusive = 0;
-    int64_t end = int64_t(tile);
-    while (end > 0) {
-        const int64_t i = end - 1 - int64_t(threadIdx.x);
-        uint64_t w = 0;
-        uint32_t flag = kLbPrefix;  // before tile 0: the empty prefix
-        if (i >= 0) {
-            uint32_t spins = 0;
-            for (;;) {
-                w = lbLoad(status, i);
-                if (Codec::ready(w, epoch)) {
-                    flag = Codec::flag(w);
-                    break;
-                }
-                if (++spins > kLbSpinLimit) {
-                    atomicOr(err, 1u);
-                    w = 0;
-                    flag = kLbPrefix;
-                    break;
-                }
-                if (spins > 32)
-                    __nanosleep(64);
-            }
-        }
-        const uint64_t value = (i >= 0 && Codec::ready(w, epoch)) ? Codec::payload(w) : 0ull;
-        const unsigned prefixLanes = __ballot_sync(kFull, flag == kLbPrefix);
-        if (lane == 0)
-            firstOf[warp] = prefixLanes != 0 ? warp * 32u + unsigned(__ffs(prefixLanes)) - 1u : 0xffffffffu;
-        __syncthreads();
-        unsigned first = 0xffffffffu;  // the nearest predecessor holding a prefix
-        for (unsigned k = 0; k < warps; ++k)
-            first = firstOf[k] < first ? firstOf[k] : first;
-        uint64_t sum = 0;
-        blockExclusiveSum<uint64_t>(threadIdx.x <= first ? value : 0ull, sum, scratch);
-        exclusive += sum;
-        if (first != 0xffffffffu)
-            break;
-        end -= int64_t(blockDim.x);
-    }
-    return exclusive;
-}
-
 // ------------------------------------------------------------------ mask bytes
 
 /** Bits of the non-zero bytes among the 16 in ``w`` (bit j: byte j). */
@@ -381,24 +328,6 @@ __device__ __forceinline__ uint32_t nonZero16(uint4 w)
         set |= ((nz * 0x00204081u) >> 28) << (4 * q);
     }
     return set;
-}
-
-/** Keep bits of the 16 mask bytes of samples [i0, i0 + 16): one 16-byte load when
- *  the run is whole and the mask 16-byte aligned. */
-template <bool Drop, bool Aligned>
-__device__ __forceinline__ uint32_t keepBits16(const uint8_t* __restrict__ mask, int64_t i0, int64_t n)
-{
-    uint32_t set = 0;  // bit j: mask byte i0 + j is non-zero
-    if (Aligned && i0 + 16 <= n) {
-        set = nonZero16(__ldg(reinterpret_cast<const uint4*>(mask + i0)));
-    } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if (i0 + j < n && mask[i0 + j] != 0)
-                set |= 1u << j;
-    }
-    const uint32_t valid = i0 >= n ? 0u : (i0 + 16 <= n ? 0xffffu : ((1u << uint32_t(n - i0)) - 1u));
-    return (Drop ? ~set : set) & valid;
 }
 
 /** The 16 mask bytes of samples [i0, i0 + 16) as one 16-byte word (bytes past n read
