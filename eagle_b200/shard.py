@@ -19,7 +19,9 @@ counts are all-gathered (offsets by prefix), every rank shares its first
 ``LEAF - 1`` survivors, each rank forms the partials of the leaves that START in
 its part (completing its last leaf from the later ranks' heads), and the leaf
 partials are all-gathered and joined by the canonical pairwise levels -- the bits
-of the one-device canonical sum over the concatenated survivors.
+of the one-device canonical sum over the concatenated survivors. The compaction map
+itself needs only the counts: :func:`compact_map_sharded` gives each rank its
+survivors' global sample indices and where they start in the map over all shards.
 """
 
 from __future__ import annotations
@@ -174,6 +176,37 @@ def ragged_fold(kept, count: int, *, group=None, leaf_partials=None, combine=Non
     dist.all_gather(every, padded, group=group)
     ordered = torch.cat([every[q][:sizes[q]] for q in range(world)]).contiguous()
     return combine(ordered)
+
+
+def global_map(local_map, count: int, begin: int, *, group=None):
+    """This rank's part of the compaction map over every rank's shard in rank order:
+    ``(indices, offset, total)``. ``indices`` are ``local_map[:count]`` shifted by the
+    shard's first sample ``begin`` (int64: eight shards of 2^28 pass int32), ``offset``
+    is the survivors of the earlier ranks -- where this part starts in the
+    concatenated map -- and ``total`` all ranks' survivors, from one all-gather of the
+    counts (Compact.h:23-47's ascending map, per rank plus a rank base offset)."""
+    import torch
+    import torch.distributed as dist
+
+    dev = local_map.device
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    cnt = torch.tensor([int(count)], dtype=torch.int64, device=dev)
+    gathered = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(world)]
+    dist.all_gather(gathered, cnt, group=group)
+    counts = [int(g.item()) for g in gathered]
+    indices = local_map[:int(count)].to(torch.int64) + int(begin)
+    return indices, sum(counts[:rank]), sum(counts)
+
+
+def compact_map_sharded(mask, begin: int, *, drop: bool = True, group=None):
+    """Compact this rank's shard (``mask`` holds samples ``[begin, begin + n)``) on its
+    device and place the survivors in the map over every rank's shard:
+    ``(indices, offset, total)`` as :func:`global_map` returns them."""
+    from ._api import compact
+
+    index_map, count = compact(mask, drop=drop)
+    return global_map(index_map, int(count.item()), begin, group=group)
 
 
 def device_leaf_partials(x):

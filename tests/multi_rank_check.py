@@ -63,6 +63,16 @@ def main():
             print(f"MISMATCH ragged {got[2].item()!r} whole {want!r}", flush=True)
             sys.exit(1)
         print("RAGGED COMPACT-SUM OK", world, want, flush=True)
+    # the compaction map over every shard: each rank's global indices at its offset
+    idx, offset, total = shard.compact_map_sharded(torch.from_numpy(keep[b:b + c].copy()).cuda(), b, drop=False)
+    whole = np.flatnonzero(keep)
+    mine = idx.cpu().numpy()
+    if total != whole.size or not np.array_equal(mine, whole[offset:offset + mine.size]):
+        print(f"MISMATCH map rank {rank} offset {offset} total {total}", flush=True)
+        sys.exit(1)
+    dist.barrier()
+    if rank == 0:
+        print("SHARDED MAP OK", world, total, flush=True)
     dist.barrier()
     dist.destroy_process_group()
 

@@ -3,8 +3,9 @@ per-rank canonical partials of x are all-gathered over NCCL and folded in rank
 order on the device; the result's bits equal the one-device run over the whole
 batch (checked against the oracle); and a compaction's ragged survivors, summed
 across ranks by the head and leaf-partial exchange, give the bits of the one-device
-compact-then-sum. Runs under torchrun when two or more GPUs are visible; skipped
-otherwise."""
+compact-then-sum; and each rank's compaction map, placed by the all-gathered
+counts, is its part of the one-device map of the whole batch. Runs under
+torchrun when two or more GPUs are visible; skipped otherwise."""
 
 import os
 import subprocess
@@ -32,3 +33,4 @@ def test_shards_fold_to_the_whole(world):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "RANK-ORDER FOLD OK" in r.stdout
     assert "RAGGED COMPACT-SUM OK" in r.stdout
+    assert "SHARDED MAP OK" in r.stdout

@@ -106,3 +106,40 @@ def test_ragged_survivors_fold_to_the_whole(orc, counts):
         got = np.frombuffer(got, dtype=np.float64)
         assert got[2:3].tobytes() == want_value
         assert got[:2].tobytes() == want_pair
+
+
+def _map_rank(rank, world, port, n, p, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import oracle
+
+        keep = np.random.default_rng([17, n]).random(n) < p
+        begin, count = shard.shard_range(n, rank, world)
+        local, c = oracle.compact(keep[begin:begin + count], drop=False)
+        assert c == local.size
+        idx, offset, total = shard.global_map(torch.from_numpy(np.asarray(local, dtype=np.int32)), c, begin)
+        out[rank] = (idx.numpy().tobytes(), offset, total, str(idx.dtype))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,n,p", ((2, 100_003, 0.5), (4, 4096 * 5 + 7, 0.01), (4, 1000, 0.0), (2, 3, 1.0)))
+def test_sharded_maps_concatenate_to_the_whole(orc, world, n, p):
+    """Each rank's survivors, shifted to global sample indices and placed at the
+    survivors of the earlier ranks, make the one-rank ascending map of the batch."""
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_map_rank, args=(world, _free_port(), n, p, out), nprocs=world, join=True)
+        res = dict(out)
+    keep = np.random.default_rng([17, n]).random(n) < p
+    want, total = orc.compact(keep, drop=False)
+    got = np.zeros(total, dtype=np.int64)
+    for r in range(world):
+        idx, offset, tot, dtype = res[r]
+        part = np.frombuffer(idx, dtype=np.int64)
+        assert tot == total and dtype == "torch.int64"
+        got[offset:offset + part.size] = part
+        assert offset + part.size <= total
+    assert sum(np.frombuffer(res[r][0], dtype=np.int64).size for r in range(world)) == total
+    assert np.array_equal(got, np.asarray(want, dtype=np.int64))
