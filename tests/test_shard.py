@@ -54,7 +54,7 @@ def _rank(rank, world, port, n, out):
 @pytest.mark.parametrize("world", (2, 4))
 def test_rank_order_fold_is_the_whole(orc, world):
     n = 1 << 20
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:  # no fork of this threaded process
         out = mgr.dict()
         mp.spawn(_rank, args=(world, _free_port(), n, out), nprocs=world, join=True)
         res = dict(out)
@@ -97,7 +97,7 @@ def test_ragged_survivors_fold_to_the_whole(orc, counts):
     the exchange of heads and leaf partials gives the bits of the one-rank canonical
     sum over the concatenation."""
     world = len(counts)
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:  # no fork of this threaded process
         out = mgr.dict()
         mp.spawn(_ragged_rank, args=(world, _free_port(), counts, out), nprocs=world, join=True)
         res = dict(out)
@@ -128,7 +128,7 @@ def _map_rank(rank, world, port, n, p, out):
 def test_sharded_maps_concatenate_to_the_whole(orc, world, n, p):
     """Each rank's survivors, shifted to global sample indices and placed at the
     survivors of the earlier ranks, make the one-rank ascending map of the batch."""
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:  # no fork of this threaded process
         out = mgr.dict()
         mp.spawn(_map_rank, args=(world, _free_port(), n, p, out), nprocs=world, join=True)
         res = dict(out)
