@@ -378,7 +378,8 @@ def engine(args):
     peak, peak_kind = _peaks()
     achieved = B_STEP * steps_per_run / (eng / 1e3) / 1e9
     passes = rep.launches
-    launches_per_step = (passes + 2 if mode == "band" else 2) + 1 + 1  # engine kernels, the sum, the combine
+    # engine kernels (persist: mask count, the claim order, the persistent run), the sum, the combine
+    launches_per_step = (passes + 2 if mode == "band" else 3 if mode == "persist" else 2) + 1 + 1
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):

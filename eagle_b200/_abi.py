@@ -37,6 +37,7 @@ MEM_DEVICE, MEM_PINNED = 0, 1
 MODEL_OSCILLATOR, MODEL_OSCILLATOR_SPREAD, MODEL_GAMBLER, MODEL_LORENZ = 0, 1, 2, 3
 MODE_BAND, MODE_PERSIST, MODE_FUSED, MODE_BAND_EAGER = 0, 1, 2, 3
 FLAG_FMA = 1
+FLAG_INDEX_ORDER = 2
 
 
 class BackendError(RuntimeError):

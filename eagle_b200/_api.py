@@ -181,11 +181,15 @@ class Runner:
     schedule: ``"band"`` (one CUDA graph: WHILE over the fused step + compaction
     kernel), ``"persist"`` (one persistent launch) or ``"fused"`` (one lane per sample,
     one launch); ``"auto"`` takes ``"band"``. All modes leave identical bits. ``fma``
-    contracts the model's multiply-adds as a device compiler does by default."""
+    contracts the model's multiply-adds as a device compiler does by default. The
+    persist oscillator claims its samples longest first (their stop steps estimated
+    from ``t_end``, ``t`` and ``dt``); ``index_order=True`` claims them in index order
+    instead -- the same bits, a slower schedule."""
 
     def __init__(self, model: Model, *, max_steps: int, mode: str = "auto", fma: bool = False, terminated=None,
                  device=None, k_first: int = 0, k_min: int = 0, k_max: int = 0, chunk: int = 0,
-                 overhead_steps: float = 0.0, interval_steps: float = 0.0, ctas_per_sm: int = 0, **planes):
+                 overhead_steps: float = 0.0, interval_steps: float = 0.0, ctas_per_sm: int = 0,
+                 index_order: bool = False, **planes):
         torch = _t()
         self._ctas_per_sm = int(ctas_per_sm)
         if model not in (oscillator, gambler, lorenz):
@@ -236,7 +240,7 @@ class Runner:
             raise ValueError("terminated must be a contiguous bool/uint8 CUDA tensor")
         self.terminated = terminated
         d = _abi.new(_abi.EngineDesc)
-        d.flags = _abi.FLAG_FMA if self.fma else 0
+        d.flags = (_abi.FLAG_FMA if self.fma else 0) | (_abi.FLAG_INDEX_ORDER if index_order else 0)
         d.device = self.device.index if self.device.index is not None else -1
         d.model = _abi.MODEL_OSCILLATOR_SPREAD if spread else _abi.MODEL_OSCILLATOR
         d.mode = _MODES[mode]

@@ -30,9 +30,13 @@
 
 namespace eb {
 
-// defined in compact.cu and entries.cu
+// defined in compact.cu, entries.cu and order.cu
 void enqueueMaskCount(const uint8_t* mask, int64_t n, uint32_t* cell, cudaStream_t s, bool zeroFirst);
 const void* entryStub(const std::string& name);
+const void* orderedPersistStub(bool fma, bool spread);
+size_t stopOrderBytes(int64_t n);
+void enqueueStopOrder(const double* tEnd, double tEndU, const double* t, const uint8_t* term, int64_t n, double dt,
+    int64_t budget, int32_t* order, cudaStream_t s);
 
 namespace {
 
@@ -326,6 +330,7 @@ struct Engine {
     cudaGraphExec_t exec = nullptr;
     BandArgs band{};
     uint32_t* goHost = nullptr;  // pinned: the eager band loop's condition word
+    int32_t* order = nullptr;  // persist oscillator: the claim order, each run longest first (order.cu)
     int bandGrid = 0, persistGrid = 0;
     uint32_t chunk = 32, block = 256;
     bool fma = false, spread = false;
@@ -506,11 +511,22 @@ void launchEngine(Engine& e, cudaStream_t s)
              static_cast<void*>(&count), static_cast<void*>(&nSamples)})
         args.push_back(p);
     unsigned grid = 0;
+    const int32_t* order = nullptr;
     if (persist) {
         for (void* p : {static_cast<void*>(&next), static_cast<void*>(&util), static_cast<void*>(&steps),
                  static_cast<void*>(&stepsum), static_cast<void*>(&chunk)})
             args.push_back(p);
         grid = unsigned(e.persistGrid);
+        if (e.order != nullptr) {
+            // claims longest first (order.cu): the same samples, the same steps, fuller warps
+            const double* tEnd = e.spread ? reinterpret_cast<const double*>(e.planes[1]) : nullptr;
+            const double* tPlane = reinterpret_cast<const double*>(e.planes[e.spread ? 4 : 3]);
+            const double dt = e.spread ? e.uniforms[0] : e.uniforms[1];
+            order = e.order;
+            enqueueStopOrder(tEnd, e.spread ? 0.0 : e.uniforms[0], tPlane, e.term, e.n, dt, e.maxSteps, e.order, s);
+            args.push_back(&order);
+            stub = orderedPersistStub(e.fma, e.spread);
+        }
     } else {
         args.push_back(&steps);
         args.push_back(&stepsum);
@@ -571,6 +587,7 @@ void destroy(Engine* e)
     (void)cudaFree(e->records);
     (void)cudaFreeHost(e->host);
     (void)cudaFreeHost(e->goHost);
+    (void)cudaFree(e->order);
     (void)cudaSetDevice(prev);
     delete e;
 }
@@ -587,7 +604,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
 {
     return guarded([&] {
         constexpr const char* who = "eagle_backend_x_b200_engine_create";
-        const auto d = readDesc(desc, EAGLE_B200_FLAG_FMA, who);
+        const auto d = readDesc(desc, EAGLE_B200_FLAG_FMA | EAGLE_B200_FLAG_INDEX_ORDER, who);
         if (out == nullptr)
             invalid(std::string(who) + ": null output");
         if (d.model > EAGLE_B200_MODEL_LORENZ)
@@ -632,11 +649,16 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
             std::memcpy(e->uext, d.uniforms_ext, sizeof e->uext);
             e->term = reinterpret_cast<uint8_t*>(d.terminated);
             // steps per claim head: an oscillator lane idles from its sample's end to the next
-            // head, a head costs a claim and a swap; 512 measured best for the oscillator (5.74
-            // against 5.90 ms at 256 and 6.32 ms at 1024 for 2^24 heterogeneous stops)
+            // head, a head costs a claim and a swap. Claimed in index order, 512 measured best
+            // (5.74 against 5.90 ms at 256 and 6.32 ms at 1024 for 2^24 heterogeneous stops);
+            // claimed longest first, a warp's lanes end together, so the heads only cost:
+            // 3.84 ms at 4096 against 3.86 / 3.89 / 4.02 / 4.28 ms at 2048 / 1024 / 512 / 256
+            const bool ordered = d.mode == EAGLE_B200_MODE_PERSIST && (d.flags & EAGLE_B200_FLAG_INDEX_ORDER) == 0
+                && (d.model == EAGLE_B200_MODEL_OSCILLATOR || spread);
             e->chunk = d.chunk != 0 ? d.chunk
                 : d.model == EAGLE_B200_MODEL_LORENZ ? 8u
                 : d.model == EAGLE_B200_MODEL_GAMBLER ? 256u
+                : ordered                             ? 4096u
                                                       : 512u;
             e->block = d.model == EAGLE_B200_MODEL_LORENZ ? 128u : 256u;
             cudaCheck(cudaMalloc(&e->cells, sizeof(Cells)), "cudaMalloc");
@@ -707,6 +729,8 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
                     "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
                 const int perSm = d.ctas_per_sm > 0 ? std::min(int(d.ctas_per_sm), std::max(1, occ)) : std::max(1, occ);
                 e->persistGrid = perSm * smCount();
+                if (ordered && d.n > 0)
+                    cudaCheck(cudaMalloc(&e->order, stopOrderBytes(d.n)), "cudaMalloc");
             }
         } catch (...) {
             destroy(e);

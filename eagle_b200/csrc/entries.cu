@@ -243,8 +243,9 @@ __device__ __forceinline__ void tTarget(const TTable& T, double dt, double te, i
  *  lane runs up to ``chunk`` steps of its sample per head, within the budget; a
  *  lane whose sample ends mid-chunk waits, masked, for the next head. */
 template <bool Fma, bool Spread>
-__global__ __launch_bounds__(256, 4) void oscillatorPersist(EB_OSC_ROLES(TEnd<Spread>), uint32_t* hawkNext,
-    unsigned long long* hawkUtil, uint32_t* hawkSteps, unsigned long long* hawkStepsum, uint32_t hawkChunk)
+__device__ __forceinline__ void persistBody(EB_OSC_ROLES(TEnd<Spread>), uint32_t* hawkNext,
+    unsigned long long* hawkUtil, uint32_t* hawkSteps, unsigned long long* hawkStepsum, uint32_t hawkChunk,
+    const int32_t* __restrict__ order)
 {
     (void)nSamples;
     const unsigned lane = threadIdx.x & 31u;
@@ -296,7 +297,7 @@ __global__ __launch_bounds__(256, 4) void oscillatorPersist(EB_OSC_ROLES(TEnd<Sp
             if (k >= count) {
                 exhausted = true;
             } else {
-                ni = base + k;
+                ni = order != nullptr ? int64_t(__ldg(order + k)) : base + k;  // the claim's sample
                 nterm = term[ni];
                 nxt.x = dplane(x)[ni];
                 nxt.v = dplane(v)[ni];
@@ -371,6 +372,27 @@ __global__ __launch_bounds__(256, 4) void oscillatorPersist(EB_OSC_ROLES(TEnd<Sp
     }
 }
 
+template <bool Fma, bool Spread>
+__global__ __launch_bounds__(256, 4) void oscillatorPersist(EB_OSC_ROLES(TEnd<Spread>), uint32_t* hawkNext,
+    unsigned long long* hawkUtil, uint32_t* hawkSteps, unsigned long long* hawkStepsum, uint32_t hawkChunk)
+{
+    persistBody<Fma, Spread>(omega, tEnd, dt, terminated, x, v, t, finished, fused, base, count, nSamples,
+        hawkNext, hawkUtil, hawkSteps, hawkStepsum, hawkChunk, nullptr);
+}
+
+/** The persistent entry with the claims taken through ``order``: claim k runs sample
+ *  order[k] (a permutation of [0, count) with base 0), so that an order grouping
+ *  samples of like length keeps a warp's lanes busy together. The engine's persist
+ *  mode launches it behind its longest-first order (order.cu). */
+template <bool Fma, bool Spread>
+__global__ __launch_bounds__(256, 4) void oscillatorPersistOrdered(EB_OSC_ROLES(TEnd<Spread>), uint32_t* hawkNext,
+    unsigned long long* hawkUtil, uint32_t* hawkSteps, unsigned long long* hawkStepsum, uint32_t hawkChunk,
+    const int32_t* order)
+{
+    persistBody<Fma, Spread>(omega, tEnd, dt, terminated, x, v, t, finished, fused, base, count, nSamples,
+        hawkNext, hawkUtil, hawkSteps, hawkStepsum, hawkChunk, order);
+}
+
 void addGamblerEntries(std::map<std::string, const void*>& m);  // walks.cu
 void addLorenzEntries(std::map<std::string, const void*>& m);   // lorenz.cu
 
@@ -408,6 +430,16 @@ const void* entryStub(const std::string& name)
     const auto& t = entryTable();
     const auto it = t.find(name);
     return it == t.end() ? nullptr : it->second;
+}
+
+/** The ordered persistent oscillator entry (the engine's; not in the name table). */
+const void* orderedPersistStub(bool fma, bool spread)
+{
+    if (fma)
+        return spread ? reinterpret_cast<const void*>(&oscillatorPersistOrdered<true, true>)
+                      : reinterpret_cast<const void*>(&oscillatorPersistOrdered<true, false>);
+    return spread ? reinterpret_cast<const void*>(&oscillatorPersistOrdered<false, true>)
+                  : reinterpret_cast<const void*>(&oscillatorPersistOrdered<false, false>);
 }
 
 }  // namespace eb

@@ -1,0 +1,175 @@
+// The longest-first claim order of the persistent oscillator.
+//
+// A persistent warp runs its 32 lanes' samples in lockstep, 512 steps per claim
+// head: a lane whose sample stops early idles until the head, and the C2 batch
+// (t_end log-uniform over three decades) leaves a lane idle about a fifth of the
+// time when samples are claimed in index order. The oscillator's stop step is
+// known before it steps (about (t_end - t) / dt), so the engine first sorts the
+// samples by it, longest first, and the lanes claim them in that order: a warp's
+// lanes then hold samples of like length, and the long ones start first, which
+// also shortens the launch's tail. Only the claim order changes -- every sample
+// takes the same steps in the same order, so every plane, the mask and the run
+// counters keep their bits.
+//
+// The sort is local: each run of 32768 consecutive samples is ordered within its own
+// range by a counting sort over at most kBuckets buckets of ``width`` steps (the
+// budget spread over them), longest first, samples already terminated last -- one
+// CTA per run, all in shared memory. The lanes claim the runs one after another, so
+// a claim's loads and its results' stores stay inside a few runs at a time: the
+// gathered planes are read once from DRAM and their partly written sectors merge in
+// L2 (a global sort made every access a random one: 5.9 ms against 5.3 ms in index
+// order, where the same samples moved into sorted order beforehand took 3.6 ms).
+#include "common.cuh"
+
+#include <mutex>
+
+namespace eb {
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int64_t kTile = 32768;  // samples per run (and per CTA)
+constexpr int kBuckets = 2048;    // step buckets; bucket kBuckets: terminated
+constexpr int kSlots = kBuckets + 1;
+constexpr int kSubs = 4;          // copies of the histogram
+constexpr int kUnroll = 4;        // samples per thread whose loads go out together
+constexpr int kPerScan = (kSlots + kThreads - 1) / kThreads;
+constexpr size_t kSmem = size_t(kSubs) * kSlots * sizeof(uint32_t) + size_t(kTile) * sizeof(uint16_t);
+
+struct StopKeyArgs {
+    const double* tEnd;  // null: ``tEndU`` for every sample
+    double tEndU;
+    const double* t;
+    const uint8_t* term;
+    int64_t n;
+    double dt, perDt;  // perDt = 1 / dt
+    int64_t budget;
+    int64_t width;  // steps per bucket
+    int32_t* order;
+};
+
+/** Sample i's bucket: its estimated steps this run, ceil((t_end - t) / dt) kept in
+ *  [1, budget] (the budget for a non-finite estimate or dt not above zero), over
+ *  ``width``, counted from the longest (bucket 0) down; kBuckets for a terminated
+ *  sample. */
+__device__ __forceinline__ uint32_t stopKey(const StopKeyArgs& a, int64_t i)
+{
+    const uint8_t done = a.term[i];  // the three loads go out together
+    const double te = a.tEnd != nullptr ? a.tEnd[i] : a.tEndU;
+    const double t0 = a.t[i];
+    if (done != 0)
+        return kBuckets;
+    const double d = (te - t0) * a.perDt;  // an estimate: only the order depends on it
+    int64_t steps = a.budget;
+    if (a.dt > 0.0 && d < double(a.budget))  // false for NaN
+        steps = d <= 1.0 ? 1 : int64_t(ceil(d));
+    steps = steps < 1 ? 1 : (steps > a.budget ? a.budget : steps);
+    const int64_t k = (steps - 1) / a.width;
+    return uint32_t(kBuckets - 1) - uint32_t(k < kBuckets ? k : kBuckets - 1);
+}
+
+/** One CTA per run of kTile samples: keys into shared memory with a histogram,
+ *  the buckets' starts by a CTA scan, then each sample placed in its bucket (in no
+ *  particular order within it). The histogram is kept in kSubs copies, lane l
+ *  counting into copy l % kSubs, so that the many samples of a crowded bucket (short
+ *  stops) collide in shared memory kSubs times less; each copy gets its own range
+ *  inside the bucket. */
+__global__ __launch_bounds__(kThreads) void stopOrderKernel(StopKeyArgs a)
+{
+    extern __shared__ __align__(16) uint32_t smem[];
+    uint32_t* cnt = smem;                                          // [kSubs][kSlots]
+    uint16_t* keys = reinterpret_cast<uint16_t*>(smem + kSubs * kSlots);  // [kTile]
+    __shared__ uint32_t scan[33];
+    const int t = int(threadIdx.x);
+    const int sub = t % kSubs;
+    for (int b = t; b < kSubs * kSlots; b += kThreads)
+        cnt[b] = 0;
+    __syncthreads();
+    const int64_t i0 = int64_t(blockIdx.x) * kTile;
+    const int live = int(a.n - i0 < kTile ? a.n - i0 : kTile);
+    for (int j0 = 0; j0 < live; j0 += kThreads * kUnroll) {
+        uint32_t k[kUnroll];
+#pragma unroll
+        for (int r = 0; r < kUnroll; ++r) {  // coalesced; every round's loads issued together
+            const int j = j0 + r * kThreads + t;
+            k[r] = j < live ? stopKey(a, i0 + j) : 0u;
+        }
+#pragma unroll
+        for (int r = 0; r < kUnroll; ++r) {
+            const int j = j0 + r * kThreads + t;
+            if (j < live) {
+                keys[j] = uint16_t(k[r]);
+                atomicAdd(&cnt[sub * kSlots + int(k[r])], 1u);
+            }
+        }
+    }
+    __syncthreads();
+    // positions run bucket by bucket (longest first), and inside a bucket copy by copy:
+    // thread t owns buckets [kPerScan t, kPerScan t + kPerScan)
+    uint32_t mine = 0;
+#pragma unroll
+    for (int q = 0; q < kPerScan; ++q) {
+        const int b = t * kPerScan + q;
+#pragma unroll
+        for (int c = 0; c < kSubs; ++c)
+            mine += b < kSlots ? cnt[c * kSlots + b] : 0u;
+    }
+    uint32_t total = 0;
+    uint32_t run = blockExclusiveSum(mine, total, scan);
+#pragma unroll
+    for (int q = 0; q < kPerScan; ++q) {
+        const int b = t * kPerScan + q;
+#pragma unroll
+        for (int c = 0; c < kSubs; ++c)
+            if (b < kSlots) {
+                const uint32_t here = cnt[c * kSlots + b];
+                cnt[c * kSlots + b] = run;  // now the copy's next position in the bucket
+                run += here;
+            }
+    }
+    __syncthreads();
+    for (int j = t; j < live; j += kThreads)
+        a.order[i0 + atomicAdd(&cnt[sub * kSlots + int(keys[j])], 1u)] = int32_t(i0 + j);
+}
+
+}  // namespace
+
+/** Device bytes of the claim order over n samples. */
+size_t stopOrderBytes(int64_t n) { return (size_t(n) * sizeof(int32_t) + 255) / 256 * 256; }
+
+/** Enqueue the claim order of samples [0, n) into ``order`` (stopOrderBytes(n)
+ *  bytes): each run of 32768 samples longest first, t_end from ``tEnd`` (null:
+ *  ``tEndU`` for all), t from ``t``, the mask ``term``; stop steps estimated
+ *  against ``budget``. */
+void enqueueStopOrder(const double* tEnd, double tEndU, const double* t, const uint8_t* term, int64_t n, double dt,
+    int64_t budget, int32_t* order, cudaStream_t s)
+{
+    if (n <= 0)
+        return;
+    StopKeyArgs a{};
+    a.tEnd = tEnd;
+    a.tEndU = tEndU;
+    a.t = t;
+    a.term = term;
+    a.n = n;
+    a.dt = dt;
+    a.perDt = 1.0 / dt;
+    a.budget = budget > 0 ? budget : 1;
+    a.width = (a.budget + kBuckets - 1) / kBuckets;
+    a.order = order;
+    {  // the kernel's dynamic shared memory limit, raised once per device
+        static std::mutex mu;
+        static bool raised[64] = {};
+        int dev = 0;
+        cudaCheck(cudaGetDevice(&dev), "cudaGetDevice");
+        std::lock_guard<std::mutex> lock(mu);
+        if (!raised[dev & 63]) {
+            cudaCheck(cudaFuncSetAttribute(stopOrderKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)),
+                "cudaFuncSetAttribute");
+            raised[dev & 63] = true;
+        }
+    }
+    stopOrderKernel<<<unsigned((n + kTile - 1) / kTile), kThreads, kSmem, s>>>(a);
+    launchCheck("stop order");
+}
+
+}  // namespace eb

@@ -724,6 +724,12 @@ eagle_backend_status eagle_backend_x_b200_entry(const char* name, int32_t device
 #define EAGLE_B200_MODE_BAND_EAGER 3u /* the band passes launched from the host, one condition read per pass */
 
 #define EAGLE_B200_FLAG_FMA 1u /* contract x0 + dt*v0 and v0 - c*x0 into fused multiply-adds */
+/* persist oscillator: claim samples in index order. By default the engine first orders each
+ * run of 32768 samples by their stop steps, estimated as (t_end - t) / dt, longest first, and
+ * the lanes claim them in that order (a warp's lanes then run samples of like length); the
+ * planes, mask and report are the same bits either way. The order holds 4 bytes per sample
+ * of device memory. */
+#define EAGLE_B200_FLAG_INDEX_ORDER 2u
 
 struct eagle_b200_engine_desc {
     uint32_t struct_size;
@@ -740,7 +746,8 @@ struct eagle_b200_engine_desc {
     int64_t k_first;     /* band: steps of the first launch (0: 16) */
     int64_t k_min;       /* band: fewest steps per launch but the last (0: 8) */
     int64_t k_max;       /* band: most steps per launch (0: 4096) */
-    uint32_t chunk;      /* persist: steps between claims, a power of two (0: 256; LORENZ 8) */
+    uint32_t chunk;      /* persist: steps between claims, a power of two (0: the oscillator 4096
+                          * claimed longest first, 512 in index order; GAMBLER 256; LORENZ 8) */
     uint32_t block;      /* threads per block (0: 256) */
     double overhead_steps; /* band: a launch's fixed cost in sample-steps (0: built-in) */
     double interval_steps; /* band: a launch's per-sample memory cost in steps (0: built-in) */
