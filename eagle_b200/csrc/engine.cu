@@ -35,6 +35,7 @@ void enqueueMaskCount(const uint8_t* mask, int64_t n, uint32_t* cell, cudaStream
 const void* entryStub(const std::string& name);
 const void* orderedPersistStub(bool fma, bool spread);
 size_t stopOrderBytes(int64_t n);
+void prepareStopOrder();
 void enqueueStopOrder(const double* tEnd, double tEndU, const double* t, const uint8_t* term, int64_t n, double dt,
     int64_t budget, int32_t* order, cudaStream_t s);
 
@@ -729,8 +730,10 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_create(const struct eagl
                     "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
                 const int perSm = d.ctas_per_sm > 0 ? std::min(int(d.ctas_per_sm), std::max(1, occ)) : std::max(1, occ);
                 e->persistGrid = perSm * smCount();
-                if (ordered && d.n > 0)
+                if (ordered && d.n > 0) {
                     cudaCheck(cudaMalloc(&e->order, stopOrderBytes(d.n)), "cudaMalloc");
+                    prepareStopOrder();
+                }
             }
         } catch (...) {
             destroy(e);

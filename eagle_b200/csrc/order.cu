@@ -136,6 +136,22 @@ __global__ __launch_bounds__(kThreads) void stopOrderKernel(StopKeyArgs a)
 /** Device bytes of the claim order over n samples. */
 size_t stopOrderBytes(int64_t n) { return (size_t(n) * sizeof(int32_t) + 255) / 256 * 256; }
 
+/** Raise the order kernel's dynamic shared-memory limit on the current device, once
+ *  per device (the engine calls it at create, outside any stream capture). */
+void prepareStopOrder()
+{
+    static std::mutex mu;
+    static bool raised[64] = {};
+    int dev = 0;
+    cudaCheck(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!raised[dev & 63]) {
+        cudaCheck(cudaFuncSetAttribute(stopOrderKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)),
+            "cudaFuncSetAttribute");
+        raised[dev & 63] = true;
+    }
+}
+
 /** Enqueue the claim order of samples [0, n) into ``order`` (stopOrderBytes(n)
  *  bytes): each run of 32768 samples longest first, t_end from ``tEnd`` (null:
  *  ``tEndU`` for all), t from ``t``, the mask ``term``; stop steps estimated
@@ -156,18 +172,7 @@ void enqueueStopOrder(const double* tEnd, double tEndU, const double* t, const u
     a.budget = budget > 0 ? budget : 1;
     a.width = (a.budget + kBuckets - 1) / kBuckets;
     a.order = order;
-    {  // the kernel's dynamic shared memory limit, raised once per device
-        static std::mutex mu;
-        static bool raised[64] = {};
-        int dev = 0;
-        cudaCheck(cudaGetDevice(&dev), "cudaGetDevice");
-        std::lock_guard<std::mutex> lock(mu);
-        if (!raised[dev & 63]) {
-            cudaCheck(cudaFuncSetAttribute(stopOrderKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)),
-                "cudaFuncSetAttribute");
-            raised[dev & 63] = true;
-        }
-    }
+    prepareStopOrder();
     stopOrderKernel<<<unsigned((n + kTile - 1) / kTile), kThreads, kSmem, s>>>(a);
     launchCheck("stop order");
 }

@@ -79,3 +79,41 @@ def test_continued_runs_and_wide_buckets(eb, orc):
     om, te = rng.uniform(1, 3, n), 10.0 ** rng.uniform(-2, 1, n)
     _check(eb, orc, om, te, max_steps=1500, runs=3)  # later runs start away from t = +0
     _check(eb, orc, om, rng.uniform(0, 60.0, n), max_steps=70_000)  # 35 steps per bucket
+
+
+def test_ordered_launch_replays_in_a_cuda_graph(eb, orc):
+    """The persist launch only enqueues (mask count, the claim order, the run), so it
+    captures into a CUDA graph; each replay is a fresh run with the oracle's bits."""
+    n = 60_000
+    rng = np.random.default_rng(8)
+    om, te = rng.uniform(1, 3, n), 10.0 ** rng.uniform(-2, 1, n)
+    x0 = rng.normal(1, 0.1, n)
+    d_x0 = torch.from_numpy(x0).cuda()
+    planes = dict(omega=torch.from_numpy(om).cuda(), t_end=torch.from_numpy(te).cuda(), dt=1e-3,
+                  x=d_x0.clone(), v=torch.zeros(n, dtype=torch.float64, device="cuda"),
+                  t=torch.zeros(n, dtype=torch.float64, device="cuda"))
+    term = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    runner = eb.until_done(eb.oscillator, max_steps=10_000, mode="persist", fma=True, terminated=term, **planes)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        runner.launch(s)  # the first launch builds the device's t sequence outside the capture
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        runner.launch(s)
+    st = [x0.copy(), np.zeros(n), np.zeros(n), np.zeros(n, np.uint8)]
+    _, fin, longest, total = orc.oscillator_run(om, *st, t_end=te, dt=1e-3, max_steps=10_000, fused=True)
+    for _ in range(2):
+        planes["x"].copy_(d_x0)
+        planes["v"].zero_()
+        planes["t"].zero_()
+        term.zero_()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        dev = [planes[k].cpu().numpy() for k in ("x", "v", "t")] + [term.cpu().numpy()]
+        for a, b, name in zip(dev, st, ("x", "v", "t", "terminated")):
+            assert a.tobytes() == b.tobytes(), name
+        rep = runner.report(s)
+        assert (rep.finished, rep.steps, rep.step_sum) == (fin, longest, total)
+    del g
