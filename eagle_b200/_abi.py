@@ -291,6 +291,7 @@ SIGNATURES = {
     "eagle_backend_event_release": (None, [_u64, _i32]),
     "eagle_backend_compact_device": (_i32, [ctypes.POINTER(CompactDesc)]),
     "eagle_backend_x_b200_compact_device_noalloc": (_i32, [ctypes.POINTER(CompactDesc)]),
+    "eagle_backend_x_b200_compact_wait_check": (_i32, [ctypes.POINTER(CompactDesc), _u32]),
     "eagle_backend_reset_device": (_i32, [ctypes.POINTER(ReorderDesc)]),
     "eagle_backend_x_reduce_canonical": (_i32, [ctypes.POINTER(ReduceDesc)]),
     "eagle_backend_x_b200_entry": (_i32, [ctypes.c_char_p, _i32, ctypes.POINTER(_u64)]),
@@ -306,6 +307,9 @@ SIGNATURES = {
     "eagle_backend_x_b200_engine_report_read": (_i32, [_P, ctypes.POINTER(Report)]),
     "eagle_backend_x_b200_engine_run": (_i32, [_P, _u64, ctypes.POINTER(Report)]),
     "eagle_backend_x_b200_engine_release": (None, [_P]),
+    "eagle_backend_x_b200_engine_time_kernel": (_i32, [_P, _i32]),
+    "eagle_backend_x_b200_engine_kernel_ms": (_i32, [_P, ctypes.POINTER(_f32), _i32, ctypes.POINTER(_i32)]),
+    "eagle_backend_x_b200_probe_fp64": (_i32, [_i32, _u64, ctypes.POINTER(ctypes.c_double)]),
 }
 
 

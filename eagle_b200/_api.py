@@ -387,6 +387,23 @@ class Runner:
         self._copy_back(stream)
         return rep
 
+    def time_kernel(self, launches: int) -> None:
+        """Time the main kernel (the persistent or fused step entry; the band graph as
+        a whole) of each of the next ``launches`` launches with CUDA events on the
+        launch stream; 0 disarms. Read the times with :meth:`kernel_ms`."""
+        torch = _t()
+        with torch.cuda.device(self.device):
+            _abi.check(_abi.lib().eagle_backend_x_b200_engine_time_kernel(self._h, int(launches)))
+
+    def kernel_ms(self, cap: int = 65536) -> list:
+        """Milliseconds of each launch timed since :meth:`time_kernel` (waits for them)."""
+        torch = _t()
+        buf = (ctypes.c_float * max(1, cap))()
+        count = ctypes.c_int32()
+        with torch.cuda.device(self.device):
+            _abi.check(_abi.lib().eagle_backend_x_b200_engine_kernel_ms(self._h, buf, int(cap), ctypes.byref(count)))
+        return [float(buf[i]) for i in range(min(int(count.value), cap))]
+
     def reset(self) -> None:
         """Clear the mask: every sample is live again (its state is kept)."""
         self.terminated.zero_()

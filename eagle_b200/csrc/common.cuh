@@ -268,11 +268,12 @@ constexpr uint32_t kLbSpinLimit = 1u << 22;
 
 /** Called by one full warp of the CTA owning ``tile`` (> 0) after it published
  *  its aggregate. Returns the exclusive prefix payload of the tile in every lane.
+ *  Each lane polls a predecessor at most ``spinLimit`` times.
  *  Lane l inspects tile ``end - 1 - l``: the nearest predecessor holding an
  *  inclusive prefix ends the walk. */
 template <class Codec>
 __device__ __forceinline__ uint64_t lbExclusivePrefix(const uint64_t* status, uint32_t tile, uint32_t epoch,
-    uint32_t* err)
+    uint32_t* err, uint32_t spinLimit = kLbSpinLimit)
 {
     const unsigned lane = threadIdx.x & 31u;
     uint64_t exclusive = 0;
@@ -289,7 +290,7 @@ __device__ __forceinline__ uint64_t lbExclusivePrefix(const uint64_t* status, ui
                     flag = Codec::flag(w);
                     break;
                 }
-                if (++spins > kLbSpinLimit) {
+                if (++spins > spinLimit) {
                     atomicOr(err, 1u);
                     w = 0;
                     flag = kLbPrefix;

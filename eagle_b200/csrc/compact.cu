@@ -49,6 +49,7 @@ struct CompactArgs {
     const void* values;  // Gather: the samples' values (elemBytes each)
     void* outValues;     // Gather: the kept samples' values, in sample order
     uint32_t elemBytes;  // Gather: 4 or 8
+    uint32_t spinLimit;  // polls of one predecessor's status word before the look-back gives up
 };
 
 /** One 32768-sample tile per CTA, as eight rows of 4096: thread t holds the 16
@@ -129,7 +130,7 @@ __global__ __launch_bounds__(kThreads, kCtasPerSm) void compactKernel(CompactArg
         } else {
             if (t == 0)
                 lbPublish<PlainCodec>(a.status, tile, 0, kLbAggregate, payload);
-            prefix = lbExclusivePrefix<PlainCodec>(a.status, tile, 0, a.err);
+            prefix = lbExclusivePrefix<PlainCodec>(a.status, tile, 0, a.err, a.spinLimit);
             if (t == 0)
                 lbPublish<PlainCodec>(a.status, tile, 0, kLbPrefix, prefix + payload);
         }
@@ -203,16 +204,20 @@ __global__ void compactEmptyKernel(uint32_t* count, uint32_t* live32, uint32_t* 
     }
 }
 
+/** One CTA per tile (``grid`` fewer only when tiles are withheld on purpose). */
 template <bool Drop, bool Trigger, bool Gather = false>
-void launchCompact(const CompactArgs& a, bool aligned, cudaStream_t s)
+void launchCompact(const CompactArgs& a, bool aligned, cudaStream_t s, uint32_t grid = 0)
 {
+    const uint32_t g = grid != 0 ? grid : a.tiles;
     if (aligned)
-        compactKernel<Drop, Trigger, true, Gather><<<a.tiles, kThreads, 0, s>>>(a);
+        compactKernel<Drop, Trigger, true, Gather><<<g, kThreads, 0, s>>>(a);
     else
-        compactKernel<Drop, Trigger, false, Gather><<<a.tiles, kThreads, 0, s>>>(a);
+        compactKernel<Drop, Trigger, false, Gather><<<g, kThreads, 0, s>>>(a);
 }
 
-size_t compactScratchBytes(int64_t n)
+__global__ void setWordKernel(uint32_t* w, uint32_t value) { *w = value; }
+
+constexpr size_t compactScratchBytes(int64_t n)
 {
     const int64_t tiles = n > 0 ? (n + kTile - 1) / kTile : 1;
     const size_t bytes = size_t(tiles) * sizeof(uint64_t) + 2 * sizeof(uint32_t);
@@ -375,8 +380,13 @@ using namespace eb;
 namespace eb {
 namespace {
 
-/** compact_device's whole enqueue (after the query), shared with the class trigger entry. */
-void enqueueCompactDevice(const eagle_backend_compact_desc& d, const char* who)
+/** compact_device's whole enqueue (after the query) over the scratch at ``scratch``
+ *  (compactScratchBytes(n) bytes, zeroed here on the stream): shared by compact_device,
+ *  the class trigger entry, the allocation-free entry and the wait check. The wait
+ *  check passes ``withholdFirst``: the tile counter starts at 1, so no CTA takes
+ *  tile 0 and every look-back that reaches it polls ``spinLimit`` times and gives up. */
+void enqueueCompactOn(const eagle_backend_compact_desc& d, char* scratch, const char* who,
+    uint32_t spinLimit = kLbSpinLimit, bool withholdFirst = false)
 {
     if (d.count == 0 || (d.n > 0 && (d.mask == 0 || d.index_map == 0)))
         invalid(std::string(who) + ": mask, index_map and count must be device addresses");
@@ -397,28 +407,40 @@ void enqueueCompactDevice(const eagle_backend_compact_desc& d, const char* who)
         launchCheck(who);
         return;
     }
-    const size_t scratchBytes = compactScratchBytes(d.n);
     CompactArgs a{};
     a.mask = reinterpret_cast<const uint8_t*>(d.mask);
     a.n = d.n;
     a.map = reinterpret_cast<int32_t*>(d.index_map);
     a.count = reinterpret_cast<uint32_t*>(d.count);
     a.tiles = uint32_t((d.n + kTile - 1) / kTile);
-    a.status = reinterpret_cast<uint64_t*>(d.scratch);
-    a.tileNext = reinterpret_cast<uint32_t*>(d.scratch + size_t(a.tiles) * sizeof(uint64_t));
+    a.status = reinterpret_cast<uint64_t*>(scratch);
+    a.tileNext = reinterpret_cast<uint32_t*>(scratch + size_t(a.tiles) * sizeof(uint64_t));
     a.err = a.tileNext + 1;
     a.live32 = reinterpret_cast<uint32_t*>(d.live32);
     a.span = reinterpret_cast<const uint32_t*>(d.span);
     a.fire = reinterpret_cast<uint32_t*>(d.fire);
     a.theta = d.theta;
-    cudaCheck(cudaMemsetAsync(reinterpret_cast<void*>(d.scratch), 0, scratchBytes, s), "cudaMemsetAsync");
+    a.spinLimit = spinLimit;
+    // the status words, the tile counter and the error word start at zero on every call
+    cudaCheck(cudaMemsetAsync(scratch, 0, compactScratchBytes(d.n), s), "cudaMemsetAsync");
+    uint32_t grid = a.tiles;
+    if (withholdFirst) {
+        setWordKernel<<<1, 1, 0, s>>>(a.tileNext, 1u);
+        launchCheck(who);
+        grid = a.tiles - 1;
+    }
     const bool aligned = (d.mask & 15u) == 0;
     const bool drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
     if (drop)
-        trigger ? launchCompact<true, true>(a, aligned, s) : launchCompact<true, false>(a, aligned, s);
+        trigger ? launchCompact<true, true>(a, aligned, s, grid) : launchCompact<true, false>(a, aligned, s, grid);
     else
-        trigger ? launchCompact<false, true>(a, aligned, s) : launchCompact<false, false>(a, aligned, s);
+        trigger ? launchCompact<false, true>(a, aligned, s, grid) : launchCompact<false, false>(a, aligned, s, grid);
     launchCheck(who);
+}
+
+void enqueueCompactDevice(const eagle_backend_compact_desc& d, const char* who)
+{
+    enqueueCompactOn(d, reinterpret_cast<char*>(d.scratch), who);
 }
 
 /** Per 32-slot group of [0, n): does it hold two or more live classes
@@ -492,6 +514,24 @@ EB_API eagle_backend_status eagle_backend_compact_device(struct eagle_backend_co
         }
         DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
         enqueueCompactDevice(d, who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_compact_wait_check(struct eagle_backend_compact_desc* desc,
+    uint32_t spin_limit)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_compact_wait_check";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        if (d.n <= kTile || d.n > INT64_C(2147483647))
+            invalid(std::string(who) + ": n must lie in (" + std::to_string(kTile) + ", 2^31 - 1]: the check "
+                "withholds the first tile and needs a later one to wait for it");
+        if (spin_limit == 0 || spin_limit > kLbSpinLimit)
+            invalid(std::string(who) + ": spin_limit must lie in [1, 2^22]");
+        if (d.scratch == 0)
+            invalid(std::string(who) + ": needs compact_device's scratch (query it there)");
+        DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
+        enqueueCompactOn(d, reinterpret_cast<char*>(d.scratch), who, spin_limit, true);
     });
 }
 
@@ -669,6 +709,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_gather(struct eagle_bac
         a.values = reinterpret_cast<const void*>(values);
         a.outValues = reinterpret_cast<void*>(out_values);
         a.elemBytes = elem_bytes;
+        a.spinLimit = kLbSpinLimit;
         cudaCheck(cudaMemsetAsync(reinterpret_cast<void*>(d.scratch), 0, compactScratchBytes(d.n), s),
             "cudaMemsetAsync");
         const bool aligned = (d.mask & 15u) == 0;
@@ -694,16 +735,21 @@ namespace {
 
 /** The largest batch the allocation-free compaction serves (2^28 samples). */
 constexpr int64_t kNoAllocMaxSamples = INT64_C(1) << 28;
-/** One status word per 4096-sample tile, then the tile counter and the error word. */
+/** One status word per 32768-sample (kTile) tile, then the tile counter and the error word,
+ *  rounded up to 256 bytes: compactScratchBytes of the largest batch. */
 constexpr size_t kNoAllocScratchBytes = size_t(kNoAllocMaxSamples / kTile) * sizeof(uint64_t) + 256;
 
 /** The scratch every allocation-free call shares (each device that loads this
  *  library holds its own copy until the process exits). Host code must not use
  *  this name as an address: see noAllocScratch. */
 static __device__ __align__(256) unsigned char g_noAllocScratch[kNoAllocScratchBytes];
+static_assert(compactScratchBytes(kNoAllocMaxSamples) <= kNoAllocScratchBytes,
+    "the built-in scratch must hold the largest batch's status words, tile counter and error word");
 
 /** The device address of g_noAllocScratch on ``device`` (current when called),
- *  looked up on the first call for that device and kept. */
+ *  looked up on the first call for that device and kept for the life of the
+ *  process: a cudaDeviceReset of that device afterwards would leave the kept
+ *  address stale, so the entry does not support one. */
 void* noAllocScratch(int device)
 {
     static std::mutex mu;
@@ -737,48 +783,9 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_device_noalloc(struct e
             invalid(std::string(who) + ": takes no scratch (leave the field 0)");
         if (d.count == 0 || (d.n > 0 && (d.mask == 0 || d.index_map == 0)))
             invalid(std::string(who) + ": mask, index_map and count must be device addresses");
-        const bool trigger = d.live32 != 0;
-        if (trigger) {
-            if (d.span == 0 || d.fire == 0)
-                invalid(std::string(who) + ": a trigger needs live32, span and fire");
-            if (d.reserved2 != 0)
-                invalid(std::string(who) + ": reserved2 must be zero");
-            if (!(d.theta > 0.0f && d.theta < 1.0f))
-                invalid(std::string(who) + ": the trigger's theta must lie in (0, 1)");
-        }
         const int dev = resolveDevice(d.device, d.mask != 0 ? d.mask : d.count);
         DeviceScope scope(dev);
-        const cudaStream_t s = seamStream(d.stream);
-        if (d.n == 0) {
-            compactEmptyKernel<<<1, 1, 0, s>>>(reinterpret_cast<uint32_t*>(d.count),
-                trigger ? reinterpret_cast<uint32_t*>(d.live32) : nullptr,
-                trigger ? reinterpret_cast<uint32_t*>(d.fire) : nullptr);
-            launchCheck(who);
-            return;
-        }
-        char* scratch = static_cast<char*>(noAllocScratch(dev));
-        CompactArgs a{};
-        a.mask = reinterpret_cast<const uint8_t*>(d.mask);
-        a.n = d.n;
-        a.map = reinterpret_cast<int32_t*>(d.index_map);
-        a.count = reinterpret_cast<uint32_t*>(d.count);
-        a.tiles = uint32_t((d.n + kTile - 1) / kTile);
-        a.status = reinterpret_cast<uint64_t*>(scratch);
-        a.tileNext = reinterpret_cast<uint32_t*>(scratch + size_t(a.tiles) * sizeof(uint64_t));
-        a.err = a.tileNext + 1;
-        a.live32 = reinterpret_cast<uint32_t*>(d.live32);
-        a.span = reinterpret_cast<const uint32_t*>(d.span);
-        a.fire = reinterpret_cast<uint32_t*>(d.fire);
-        a.theta = d.theta;
-        // the status words, the tile counter and the error word start at zero on every call
-        cudaCheck(cudaMemsetAsync(scratch, 0, size_t(a.tiles) * sizeof(uint64_t) + 2 * sizeof(uint32_t), s),
-            "cudaMemsetAsync");
-        const bool aligned = (d.mask & 15u) == 0;
-        const bool drop = (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0;
-        if (drop)
-            trigger ? launchCompact<true, true>(a, aligned, s) : launchCompact<true, false>(a, aligned, s);
-        else
-            trigger ? launchCompact<false, true>(a, aligned, s) : launchCompact<false, false>(a, aligned, s);
-        launchCheck(who);
+        char* scratch = d.n > 0 ? static_cast<char*>(noAllocScratch(dev)) : nullptr;
+        enqueueCompactOn(d, scratch, who);
     });
 }

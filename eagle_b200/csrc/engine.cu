@@ -335,7 +335,34 @@ struct Engine {
     int bandGrid = 0, persistGrid = 0;
     uint32_t chunk = 32, block = 256;
     bool fma = false, spread = false;
+    // armed by engine_time_kernel: events recorded around the main kernel of the next launches
+    std::vector<cudaEvent_t> evStart, evStop;
+    size_t evUsed = 0;
 };
+
+/** Record the next armed start (``stop`` false) or stop event of ``e`` on ``s``. */
+void markKernel(Engine& e, cudaStream_t s, bool stop)
+{
+    if (e.evUsed >= e.evStart.size())
+        return;
+    if (!stop) {
+        cudaCheck(cudaEventRecord(e.evStart[e.evUsed], s), "cudaEventRecord");
+        return;
+    }
+    cudaCheck(cudaEventRecord(e.evStop[e.evUsed], s), "cudaEventRecord");
+    ++e.evUsed;
+}
+
+void releaseTimers(Engine& e)
+{
+    for (cudaEvent_t ev : e.evStart)
+        (void)cudaEventDestroy(ev);
+    for (cudaEvent_t ev : e.evStop)
+        (void)cudaEventDestroy(ev);
+    e.evStart.clear();
+    e.evStop.clear();
+    e.evUsed = 0;
+}
 
 template <bool Fma, bool Spread, bool Graph>
 void* bandKernelPtr()
@@ -422,7 +449,9 @@ ScalarHandle handle(uint64_t p, int64_t n, int dev)
 void launchEngine(Engine& e, cudaStream_t s)
 {
     if (e.mode == EAGLE_B200_MODE_BAND) {
+        markKernel(e, s, false);
         cudaCheck(cudaGraphLaunch(e.exec, s), "cudaGraphLaunch");
+        markKernel(e, s, true);
         return;
     }
     if (e.mode == EAGLE_B200_MODE_BAND_EAGER) {
@@ -533,7 +562,9 @@ void launchEngine(Engine& e, cudaStream_t s)
         args.push_back(&stepsum);
         grid = unsigned((e.n + e.block - 1) / e.block);
     }
+    markKernel(e, s, false);
     cudaCheck(cudaLaunchKernel(stub, dim3(grid), dim3(e.block), args.data(), 0, s), "cudaLaunchKernel");
+    markKernel(e, s, true);
 }
 
 /** The report from the host copy of the cells (already landed). */
@@ -589,6 +620,7 @@ void destroy(Engine* e)
     (void)cudaFreeHost(e->host);
     (void)cudaFreeHost(e->goHost);
     (void)cudaFree(e->order);
+    releaseTimers(*e);
     (void)cudaSetDevice(prev);
     delete e;
 }
@@ -806,6 +838,47 @@ EB_API eagle_backend_status eagle_backend_x_b200_engine_run(eagle_b200_engine h,
     if (s != EAGLE_BACKEND_OK)
         return s;
     return eagle_backend_x_b200_engine_report(h, stream, report);
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_engine_time_kernel(eagle_b200_engine h, int32_t launches)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_engine_time_kernel";
+        if (h == nullptr)
+            fail(EAGLE_BACKEND_BAD_HANDLE, std::string(who) + ": null handle");
+        if (launches < 0 || launches > 65536)
+            invalid(std::string(who) + ": launches must lie in [0, 65536]");
+        auto* e = reinterpret_cast<Engine*>(h);
+        DeviceScope scope(e->device);
+        releaseTimers(*e);
+        for (int32_t i = 0; i < launches; ++i) {
+            cudaEvent_t a = nullptr, b = nullptr;
+            cudaCheck(cudaEventCreate(&a), "cudaEventCreate");
+            e->evStart.push_back(a);
+            cudaCheck(cudaEventCreate(&b), "cudaEventCreate");
+            e->evStop.push_back(b);
+        }
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_engine_kernel_ms(eagle_b200_engine h, float* ms, int32_t cap,
+    int32_t* count)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_engine_kernel_ms";
+        if (h == nullptr)
+            fail(EAGLE_BACKEND_BAD_HANDLE, std::string(who) + ": null handle");
+        if (count == nullptr || cap < 0 || (cap > 0 && ms == nullptr))
+            invalid(std::string(who) + ": null output");
+        auto* e = reinterpret_cast<Engine*>(h);
+        DeviceScope scope(e->device);
+        const size_t m = std::min(e->evUsed, size_t(cap));
+        for (size_t i = 0; i < m; ++i) {
+            cudaCheck(cudaEventSynchronize(e->evStop[i]), "cudaEventSynchronize");
+            cudaCheck(cudaEventElapsedTime(&ms[i], e->evStart[i], e->evStop[i]), "cudaEventElapsedTime");
+        }
+        *count = int32_t(e->evUsed);
+    });
 }
 
 EB_API void eagle_backend_x_b200_engine_release(eagle_b200_engine h)

@@ -231,3 +231,22 @@ def compact_sum_sharded(mask, values, *, drop: bool = False, group=None):
     cs.gather()
     count = int(cs.count.item())
     return ragged_fold(cs.kept, count, group=group)
+
+
+class ShardedCompactSum:
+    """:func:`compact_sum_sharded` prepared once per shard: the compaction's buffers
+    are allocated at construction, so each call enqueues the gather of this rank's
+    survivors, reads their count (one host wait: the exchange is planned on the
+    host) and makes the exchange. Returns ``(hi, comp, value)`` on every rank."""
+
+    def __init__(self, mask, values, *, drop: bool = False, group=None):
+        from ._api import CompactSum
+
+        self.cs = CompactSum(mask, values, drop=drop)
+        self.group = group
+        self.count = 0
+
+    def __call__(self):
+        self.cs.gather()
+        self.count = int(self.cs.count.item())
+        return ragged_fold(self.cs.kept, self.count, group=self.group)

@@ -611,6 +611,17 @@ eagle_backend_status eagle_backend_reorder_classes_device(struct eagle_backend_r
 /* eagle_backend.h:847: classify ``ptr`` as seen from ``device`` (-1: the current one) */
 eagle_backend_status eagle_backend_pointer_residency(int32_t device, uint64_t ptr, int32_t* cls);
 
+/* eagle_backend_x_b200_compact_wait_check: compact_device with its first tile withheld,
+ * to exercise the bounded look-back wait (this backend's addition; eagle's multi-level
+ * scan has no wait to bound, eagle/cuda/Scan.h:32-141). No CTA takes tile 0, so every
+ * tile whose look-back reaches tile 0 polls its status word ``spin_limit`` times (in
+ * [1, 2^22]; compact_device uses 2^22), gives up, sets the error word and goes on; the
+ * last tile then writes a count of 0xffffffff, above any n, as compact_device does
+ * after any wait that gave up. The map's contents are unspecified. Same desc and
+ * caller scratch as compact_device; n must exceed one 32768-sample tile. */
+eagle_backend_status eagle_backend_x_b200_compact_wait_check(struct eagle_backend_compact_desc* desc,
+    uint32_t spin_limit);
+
 /* eagle_backend_x_b200_compact_device_noalloc: compact_device for callers that
  * cannot allocate device memory (no counterpart in the reference: eagle's
  * compaction always takes caller scratch). Same desc, same outputs, same flags and
@@ -618,8 +629,9 @@ eagle_backend_status eagle_backend_pointer_residency(int32_t device, uint64_t pt
  * fixed 64 KiB + 256 B array inside this library on every device that loads it,
  * enough for n <= 2^28 samples; a larger n returns UNSUPPORTED. It allocates
  * nothing: it enqueues one memset of that array and the compaction kernel. The
- * first call on a device looks the array's address up (cudaGetSymbolAddress), so
- * make that first call before any stream capture. Every call shares the one array:
+ * first call on a device looks the array's address up (cudaGetSymbolAddress) and
+ * keeps it, so make that first call before any stream capture, and do not reset the
+ * device (cudaDeviceReset) after it. Every call shares the one array:
  * calls that may overlap on the GPU (other streams, other threads) race and must
  * be serialised by the caller. */
 eagle_backend_status eagle_backend_x_b200_compact_device_noalloc(struct eagle_backend_compact_desc* desc);
@@ -804,6 +816,24 @@ eagle_backend_status eagle_backend_x_b200_engine_report_read(eagle_b200_engine h
 eagle_backend_status eagle_backend_x_b200_engine_run(eagle_b200_engine h, uint64_t stream,
     struct eagle_b200_report* report);
 void eagle_backend_x_b200_engine_release(eagle_b200_engine h);
+/* Timing of the engine's main kernel (this backend's addition, for measurement; eagle
+ * times whole launches from Python, python/eagle/_until_done.py:1322-1460): arm CUDA
+ * events recorded on the launch stream just before and just after the main kernel
+ * (the persistent or fused step entry; the band graph as a whole) of each of the
+ * next ``launches`` launches, in [0, 65536]; 0 disarms. Re-arming drops earlier
+ * times. Creates events: call outside any stream capture. */
+eagle_backend_status eagle_backend_x_b200_engine_time_kernel(eagle_b200_engine h, int32_t launches);
+/* Wait for the timed launches' events and write the first min(cap, timed) kernel
+ * times in milliseconds to ``ms``; ``*count`` = launches timed since arming. */
+eagle_backend_status eagle_backend_x_b200_engine_kernel_ms(eagle_b200_engine h, float* ms, int32_t cap,
+    int32_t* count);
+
+/* The FP64 issue probe (this backend's addition, for measurement; no counterpart in
+ * eagle): times a kernel whose every lane runs eight independent chains of fused
+ * double-precision multiply-adds on ``device`` (-1: the current one) and writes the
+ * best rate of five launches, in lane multiply-adds per second. Synchronises
+ * ``stream`` and allocates stream-ordered memory: not for use inside a capture. */
+eagle_backend_status eagle_backend_x_b200_probe_fp64(int32_t device, uint64_t stream, double* fma_per_s);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -154,3 +154,39 @@ def test_reset_device(eb):
     ar = torch.arange(n, dtype=torch.int32)
     assert torch.equal(perm.cpu(), ar) and torch.equal(inv.cpu(), ar) and torch.equal(imap.cpu(), ar)
     assert words.tolist() == [n, n]
+
+
+@pytest.mark.parametrize("tiles", (2, 5, 40))
+def test_bounded_wait_gives_up(eb, tiles):
+    """The look-back's bounded wait (eagle_b200/csrc/common.cuh lbExclusivePrefix):
+    with the first tile withheld nothing ever publishes its status word, so each
+    tile whose look-back reaches it polls ``spin_limit`` times, gives up and sets the
+    error word; the count comes back 0xffffffff (above n) instead of a hang. The
+    same scratch then serves a normal compaction bit for bit."""
+    from eagle_b200 import _abi
+
+    n = tiles * 32768 + 123
+    mask = _mask(n, 21, 0.5)
+    comp = eb.Compactor(torch.from_numpy(mask).cuda())
+    d = _abi.new(_abi.CompactDesc)
+    ctypes.memmove(ctypes.byref(d), ctypes.byref(comp.desc), ctypes.sizeof(d))
+    d.stream = torch.cuda.current_stream().cuda_stream
+    comp.count.fill_(7)
+    _abi.check(_abi.lib().eagle_backend_x_b200_compact_wait_check(ctypes.byref(d), 1024))
+    torch.cuda.synchronize()
+    assert int(comp.count.item()) & 0xffffffff == 0xffffffff
+    index_map, count = comp()
+    c = int(count.item())
+    want = np.flatnonzero(~mask)
+    assert c == want.size and np.array_equal(index_map[:c].cpu().numpy(), want)
+
+
+def test_bounded_wait_check_refusals(eb):
+    from eagle_b200 import _abi
+
+    d = _abi.new(_abi.CompactDesc, n=32768, mask=1, index_map=1, count=1, scratch=1)
+    assert _abi.lib().eagle_backend_x_b200_compact_wait_check(ctypes.byref(d), 1024) == _abi.INVALID_ARGUMENT
+    d.n = 70000
+    assert _abi.lib().eagle_backend_x_b200_compact_wait_check(ctypes.byref(d), 0) == _abi.INVALID_ARGUMENT
+    assert _abi.lib().eagle_backend_x_b200_compact_wait_check(ctypes.byref(d), (1 << 22) + 1) == \
+        _abi.INVALID_ARGUMENT

@@ -1,8 +1,9 @@
 """The allocation-free compaction (eagle_backend_x_b200_compact_device_noalloc),
 for callers that cannot allocate device memory: through the C-ABI it must give
 the same index map and count as the regular entry (eagle_backend_compact_device,
-which takes caller scratch), on two calls in a row, since every call reuses the
-one built-in scratch array; and it must refuse a batch past its 2^28-sample limit.
+which takes caller scratch) and as numpy's flatnonzero of the kept samples, on two
+calls in a row, since every call reuses the one built-in scratch array; and it
+must refuse a batch past its 2^28-sample limit.
 
 This file is collected last so that a failure here stops a -x run only after
 every other test has run."""
@@ -48,6 +49,9 @@ def test_matches_the_scratch_entry_twice(eb, n, drop):
         c = int(c1.item())
         assert int(c0.item()) == c
         assert torch.equal(m0[:c], m1[:c])
+        keep = mask.cpu().numpy()
+        want = np.flatnonzero(~keep if drop else keep)
+        assert c == want.size and np.array_equal(m0[:c].cpu().numpy(), want)
 
 
 def test_trigger_matches(eb):
@@ -70,6 +74,10 @@ def test_largest_batch_and_refusal(eb):
     torch.cuda.synchronize()
     c = int(c1.item())
     assert int(c0.item()) == c and torch.equal(m0[:c], m1[:c])
+    want = np.flatnonzero(~mask[: 1 << 20].cpu().numpy())
+    assert c == 256 * want.size
+    assert np.array_equal(m0[:want.size].cpu().numpy(), want)
+    assert np.array_equal(m0[c - want.size:c].cpu().numpy(), want + (255 << 20))
     del m0, m1, mask
     d = _abi.new(_abi.CompactDesc, flags=_abi.COMPACT_MASK_IS_DROP, mask=1, index_map=1, count=1, n=n + 1)
     assert _abi.lib().eagle_backend_x_b200_compact_device_noalloc(ctypes.byref(d)) == _abi.UNSUPPORTED
