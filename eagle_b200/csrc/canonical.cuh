@@ -42,40 +42,59 @@ struct CompP {  // a floating-point sum's partial (hi, comp)
     }
 };
 
-/** eagle's fixed-point partial of a float64 sum (canonical.h:153-302), the leaf it
- *  takes on a device whose FP32:FP64 throughput ratio is 8 or worse (:304-313):
- *  the value is v * 2^u, v a signed 128-bit integer held as (lo, hi). A term's
- *  last mantissa bit lands at most 53 bits above the unit, kept 106 bits below the
- *  largest term seen; a join aligns the units (floor shifts) and halves both sides
- *  when either reaches 2^125. Infinities and NaN set sticky flags; value() rounds
- *  once to nearest-even. All integer arithmetic: the bits do not depend on order of
- *  evaluation beyond the tree's. */
+/** eagle's exact fixed-point partial of a float64 sum: the leaf eagle takes on a
+ *  device whose FP32:FP64 throughput ratio is 8 or worse (canonical.h:153-313). It
+ *  stands for A * 2^unit, A a signed 128-bit integer held as two 64-bit words. The
+ *  rules that decide its bits are eagle's (its tests pin them through exact known
+ *  sums):
+ *   (1) before any finite non-zero term: A = 0 and unit = kNoTerm, below every real
+ *       unit;
+ *   (2) a finite non-zero term (-1)^s * m * 2^e (m its integer significand, at most
+ *       53 bits; e the weight of m's last bit): when unit < e - 53 the unit rises to
+ *       e - 53 and A is divided by 2^(the rise), rounding toward -infinity; then
+ *       A += (-1)^s * floor(m * 2^(e - unit));
+ *   (3) a join lifts the lower unit to the higher as in (2); if either accumulator
+ *       then lies outside [-2^125, 2^125), both are halved toward -infinity and the
+ *       unit rises by one; then the accumulators add and the flags combine;
+ *   (4) an infinity or NaN only sets a sticky flag: NaN, or infinities of both
+ *       signs, make the value NaN; infinities of one sign make it that infinity.
+ *  A stays below 2^127 in magnitude: a leaf folds at most 32 terms of at most 2^106
+ *  units each, and (3) keeps a join's sum below 2^127. value() rounds A * 2^unit
+ *  once to the nearest double, ties to even, subnormals included. */
 struct FixedP {
     using I = __int128;
     using U = unsigned __int128;
-    static constexpr int32_t kEmpty = -100000;  // the unit of a partial that saw no term
-    static constexpr int32_t kPosInf = 1, kNegInf = 2, kNan = 4;
-    uint64_t lo;
-    int64_t hi;
-    int32_t u, fl;
+    static constexpr int32_t kNoTerm = -100000;
+    static constexpr int32_t kInfUp = 1, kInfDown = 2, kNaN = 4;
+    uint64_t accLo;  // A, low word
+    int64_t accHi;   // A, high word (carries the sign)
+    int32_t unit;
+    int32_t sticky;  // kInfUp | kInfDown | kNaN
 
-    __device__ __forceinline__ I get() const { return I((U(uint64_t(hi)) << 64) | U(lo)); }
-    __device__ __forceinline__ void set(I v)
+    __device__ __forceinline__ I acc() const { return I((U(uint64_t(accHi)) << 64) | U(accLo)); }
+    __device__ __forceinline__ void store(I a)
     {
-        lo = uint64_t(U(v));
-        hi = int64_t(v >> 64);
+        accLo = uint64_t(U(a));
+        accHi = int64_t(a >> 64);
     }
-    static __device__ __forceinline__ I shr(I v, int32_t d) { return v >> (d < 127 ? d : 127); }
-    static __device__ __forceinline__ FixedP empty() { return FixedP{0, 0, kEmpty, 0}; }
+    /** floor(a / 2^k) for any k >= 0: the arithmetic shift, whose result is already 0
+     *  or -1 for every 128-bit a once k reaches 127. */
+    static __device__ __forceinline__ I floorDiv2k(I a, int32_t k) { return a >> (k < 127 ? k : 127); }
+    static __device__ __forceinline__ bool outside125(I a)
+    {
+        const I lim = I(1) << 125;
+        return a < -lim || a >= lim;
+    }
+    static __device__ __forceinline__ FixedP none() { return FixedP{0ull, 0ll, kNoTerm, 0}; }
     static __device__ __forceinline__ FixedP of(double x)
     {
-        FixedP p = empty();
+        FixedP p = none();
         p.add(x);
         return p;
     }
     static __device__ __forceinline__ FixedP of(double x, double xc)
     {
-        FixedP p = empty();
+        FixedP p = none();
         p.add(x);
         p.add(xc);
         return p;
@@ -85,90 +104,108 @@ struct FixedP {
         add(x);
         add(xc);
     }
+    /** Rule (2), or (4) for a non-finite term. */
     __device__ __forceinline__ void add(double x)
     {
-        const uint64_t b = uint64_t(__double_as_longlong(x));
-        const int32_t e = int32_t((b >> 52) & 0x7ff);
-        if (e == 0x7ff) {
-            fl |= (b << 12) != 0 ? kNan : ((b >> 63) != 0 ? kNegInf : kPosInf);
+        const uint64_t w = uint64_t(__double_as_longlong(x));
+        const uint32_t field = uint32_t(w >> 52) & 0x7ffu;
+        const bool minus = (w >> 63) != 0;
+        uint64_t m = w & ((1ull << 52) - 1);
+        if (field == 0x7ffu) {
+            sticky |= m != 0 ? kNaN : (minus ? kInfDown : kInfUp);
             return;
         }
-        const uint64_t m = (b & 0xfffffffffffffull) | (e != 0 ? (1ull << 52) : 0ull);
-        if (m == 0)
-            return;
-        const int32_t ex = (e != 0 ? e : 1) - 1075;  // the weight of m's last bit
-        I v = get();
-        if (ex - 53 > u) {
-            v = shr(v, ex - 53 - u);
-            u = ex - 53;
-        }
-        const int32_t sh = ex - u;  // at most 53
-        const I t = sh >= 0 ? I(U(m) << sh) : (-sh < 64 ? I(m >> -sh) : I(0));
-        set((b >> 63) != 0 ? v - t : v + t);
-    }
-    static __device__ __forceinline__ bool wide(I z)
-    {
-        const I top = z >> 125;
-        return top != 0 && top != -1;
-    }
-    static __device__ __forceinline__ FixedP join(const FixedP& a, const FixedP& b)
-    {
-        I x = a.get(), y = b.get();
-        int32_t un = a.u;
-        if (b.u > un) {
-            x = shr(x, b.u - un);
-            un = b.u;
+        int32_t e;  // the weight of m's last bit
+        if (field == 0) {
+            if (m == 0)
+                return;  // a signed zero adds nothing
+            e = -1074;
         } else {
-            y = shr(y, un - b.u);
+            m |= 1ull << 52;
+            e = int32_t(field) - 1075;
         }
-        if (wide(x) || wide(y)) {
-            x >>= 1;
-            y >>= 1;
-            ++un;
+        I a = acc();
+        if (unit < e - 53) {
+            a = floorDiv2k(a, e - 53 - unit);
+            unit = e - 53;
         }
-        FixedP o;
-        o.set(x + y);
-        o.u = un;
-        o.fl = a.fl | b.fl;
-        return o;
+        const int32_t lift = e - unit;  // at most 53
+        const U term = lift >= 0 ? U(m) << lift : (lift > -64 ? U(m >> -lift) : U(0));
+        store(minus ? a - I(term) : a + I(term));
     }
+    /** Rule (3); the flags of either side carry over. */
+    static __device__ __forceinline__ FixedP join(const FixedP& p, const FixedP& q)
+    {
+        int32_t unit = p.unit > q.unit ? p.unit : q.unit;
+        I a = floorDiv2k(p.acc(), unit - p.unit);
+        I b = floorDiv2k(q.acc(), unit - q.unit);
+        if (outside125(a) || outside125(b)) {
+            a >>= 1;
+            b >>= 1;
+            ++unit;
+        }
+        FixedP r;
+        r.store(a + b);
+        r.unit = unit;
+        r.sticky = p.sticky | q.sticky;
+        return r;
+    }
+    /** A * 2^unit to the nearest double (ties to even). |A| is cut to its top 64 bits
+     *  plus a sticky bit for everything below them; those 64 bits hold the 53 the
+     *  double keeps (fewer for a subnormal) and at least 11 below, so one
+     *  round-to-nearest-even on them, with the sticky bit breaking a tie, is the
+     *  correctly rounded result. */
     __device__ __forceinline__ double value() const
     {
-        if (fl != 0) {
-            if ((fl & kNan) != 0 || (fl & (kPosInf | kNegInf)) == (kPosInf | kNegInf))
+        if (sticky != 0) {
+            if ((sticky & kNaN) != 0 || (sticky & (kInfUp | kInfDown)) == (kInfUp | kInfDown))
                 return __longlong_as_double(0x7ff8000000000000ll);
-            return __longlong_as_double((fl & kPosInf) != 0 ? 0x7ff0000000000000ll : int64_t(0xfff0000000000000ull));
+            return (sticky & kInfUp) != 0 ? __longlong_as_double(0x7ff0000000000000ll)
+                                          : __longlong_as_double(int64_t(0xfff0000000000000ull));
         }
-        const I v = get();
-        if (v == 0)
+        const I a = acc();
+        if (a == 0)
             return 0.0;
-        const bool neg = v < 0;
-        const U mag = neg ? U(0) - U(v) : U(v);
-        const uint64_t mh = uint64_t(mag >> 64), ml = uint64_t(mag);
-        const int32_t lz = mh != 0 ? __clzll(int64_t(mh)) : 64 + __clzll(int64_t(ml));
-        const int32_t len = 128 - lz;
-        const int32_t sub = len + u + 1074;  // the bits of weight 2^-1074 and up
-        const int32_t keep = sub < 53 ? sub : 53;
-        const int32_t drop = len - keep;
-        double r;
-        if (drop <= 0) {
-            r = ldexp(double(uint64_t(mag)), u);
+        const bool minus = a < 0;
+        const U mag = minus ? U(0) - U(a) : U(a);
+        const uint64_t w1 = uint64_t(mag >> 64), w0 = uint64_t(mag);
+        uint64_t top;  // |A|'s leading 64 bits, its highest set bit at bit 63
+        bool below;    // any set bit of |A| under them
+        int32_t len;   // |A|'s bit length
+        if (w1 != 0) {
+            const int32_t z = __clzll(int64_t(w1));
+            len = 128 - z;
+            top = z == 0 ? w1 : (w1 << z) | (w0 >> (64 - z));
+            below = (z == 0 ? w0 : w0 << z) != 0;
         } else {
-            U q = drop < 128 ? mag >> drop : U(0);
-            const U rem = drop < 128 ? mag - (q << drop) : mag;
-            if (drop <= 128) {
-                const U half = U(1) << (drop - 1);
-                if (rem > half || (rem == half && (q & 1) != 0))
-                    ++q;
-            }
-            r = ldexp(double(uint64_t(q)), u + drop);
+            const int32_t z = __clzll(int64_t(w0));
+            len = 64 - z;
+            top = w0 << z;
+            below = false;
         }
-        return neg ? -r : r;
+        const int32_t lead = unit + len - 1;  // the weight of the leading bit
+        // bits at weights >= 2^-1074 survive: 53 for a normal result, fewer for a subnormal
+        const int32_t keep = lead + 1075 < 53 ? lead + 1075 : 53;
+        double r;
+        if (keep <= 0) {
+            // under the smallest subnormal 2^-1074: above its half (2^-1075) rounds up to it,
+            // exactly its half ties to the even 0, anything smaller is 0
+            r = (keep == 0 && (below || top != (1ull << 63))) ? __longlong_as_double(1ll) : 0.0;
+        } else {
+            const int32_t cut = 64 - keep;  // 11..63 low bits of top go
+            uint64_t q = top >> cut;
+            const uint64_t rest = top & ((1ull << cut) - 1);
+            const uint64_t half = 1ull << (cut - 1);
+            if (rest > half || (rest == half && (below || (q & 1) != 0)))
+                ++q;  // a carry to 2^keep is still exact in a double
+            r = ldexp(double(q), lead - keep + 1);
+        }
+        return minus ? -r : r;
     }
     __device__ __forceinline__ FixedP shflDown(unsigned off) const
     {
-        return {__shfl_down_sync(kFull, lo, off), __shfl_down_sync(kFull, hi, off), __shfl_down_sync(kFull, u, off),
-            __shfl_down_sync(kFull, fl, off)};
+        return {__shfl_down_sync(kFull, accLo, off), __shfl_down_sync(kFull, accHi, off),
+            __shfl_down_sync(kFull, unit, off), __shfl_down_sync(kFull, sticky, off)};
     }
 };
 

@@ -313,6 +313,54 @@ __device__ __forceinline__ uint64_t lbExclusivePrefix(const uint64_t* status, ui
     return exclusive;
 }
 
+// ------------------------------------------------------------------ bulk copies
+//
+// One thread asks the copy engine for a contiguous global -> shared copy that
+// completes on an mbarrier (cp.async.bulk, no tensor map, never multicast: the
+// source is always this GPU's own memory). Every wait on the barrier is bounded.
+
+__device__ __forceinline__ uint32_t sharedAddr(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
+
+/** One-thread init of a CTA-local mbarrier expecting ``arrivals`` arrivals, made
+ *  visible to the copy engine; the CTA must pass a barrier before using it. */
+__device__ __forceinline__ void mbarInit(uint64_t* bar, uint32_t arrivals)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n"
+                 "fence.mbarrier_init.release.cluster;\n" ::"r"(sharedAddr(bar)),
+        "r"(arrivals)
+        : "memory");
+}
+
+/** Arrive on ``bar`` announcing ``bytes`` still to land, then copy ``bytes`` (a
+ *  multiple of 16, both addresses 16-byte aligned) from global ``src`` to this
+ *  CTA's shared ``dst``; the copy engine counts them off the barrier's phase. */
+__device__ __forceinline__ void bulkLoad(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n"
+                 "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%2], [%3], %1, [%0];\n" ::"r"(
+                     sharedAddr(bar)),
+        "r"(bytes), "r"(sharedAddr(dst)), "l"(src)
+        : "memory");
+}
+
+/** Wait for phase ``parity`` of ``bar`` to complete, at most ``limit`` polls (each
+ *  may suspend the thread for a while in hardware). False if it gave up. */
+__device__ __forceinline__ bool mbarWait(uint64_t* bar, uint32_t parity, uint32_t limit)
+{
+    for (uint32_t i = 0; i < limit; ++i) {
+        uint32_t done = 0;
+        asm volatile("{\n .reg .pred p;\n"
+                     " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                     " selp.u32 %0, 1, 0, p;\n}\n"
+                     : "=r"(done)
+                     : "r"(sharedAddr(bar)), "r"(parity)
+                     : "memory");
+        if (done != 0)
+            return true;
+    }
+    return false;
+}
+
 // ------------------------------------------------------------------ mask bytes
 
 /** Bits of the non-zero bytes among the 16 in ``w`` (bit j: byte j). */

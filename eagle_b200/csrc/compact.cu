@@ -26,13 +26,6 @@ constexpr int64_t kTile = kRow * kRows;                // 32768 samples per CTA
 constexpr uint32_t kStage = uint32_t(kTile / 4);       // kept indices staged in the tile's mask bytes
 constexpr int kCtasPerSm = 6;                          // 33 KB of shared memory and <= 40 registers each
 
-/** 16-byte ``cp.async`` (L2 only) from global to shared memory; both addresses 16-byte aligned. */
-__device__ __forceinline__ void cpAsync16(uint8_t* dst, const uint8_t* src)
-{
-    const uint32_t d = uint32_t(__cvta_generic_to_shared(dst));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src) : "memory");
-}
-
 struct CompactArgs {
     const uint8_t* mask;
     int64_t n;
@@ -69,23 +62,26 @@ __global__ __launch_bounds__(kThreads, kCtasPerSm) void compactKernel(CompactArg
     __shared__ uint64_t scan64[33];
     __shared__ uint32_t scan[33];
     __shared__ uint64_t sPrefix;
+    __shared__ uint64_t sBar;  // completes when the tile's mask bytes have landed
     // the tile's mask bytes; once every thread holds its keep bits, the staging area
-    __shared__ __align__(16) uint8_t sMask[kTile];
+    __shared__ __align__(128) uint8_t sMask[kTile];
     int32_t* stage = reinterpret_cast<int32_t*>(sMask);
     const int t = int(threadIdx.x);
-    if (t == 0)
+    if (t == 0) {
         sTile = atomicAdd(a.tileNext, 1u);
+        mbarInit(&sBar, 1);
+    }
     __syncthreads();
     const uint32_t tile = sTile;
     const int64_t tile0 = int64_t(tile) * kTile;
-    // every row's 16 bytes copied to shared memory before the first is used: the copies
-    // are in flight together without holding registers (a thread reads back only its own)
     if (Aligned && tile0 + kTile <= a.n) {
-#pragma unroll
-        for (int q = 0; q < kRows; ++q)
-            cpAsync16(sMask + q * kRow + t * 16, a.mask + tile0 + int64_t(q) * kRow + int64_t(t) * 16);
-        asm volatile("cp.async.commit_group;\n"
-                     "cp.async.wait_group 0;\n" ::: "memory");
+        // the whole tile in one bulk copy by the copy engine, issued by one thread
+        if (t == 0)
+            bulkLoad(sMask, a.mask + tile0, uint32_t(kTile), &sBar);
+        if (!mbarWait(&sBar, 0, kLbSpinLimit)) {
+            atomicOr(a.err, 2u);  // reported as a failed compaction; wait out the copy before going on
+            (void)mbarWait(&sBar, 0, kLbSpinLimit);
+        }
     } else {  // the last tile, or a mask not 16-byte aligned
 #pragma unroll 1
         for (int q = 0; q < kRows; ++q)

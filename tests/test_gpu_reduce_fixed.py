@@ -95,3 +95,44 @@ def test_refusals(eb):
     d.op = _abi.REDUCE_OP_MAX
     with pytest.raises(ValueError):
         _abi.check(_abi.lib().eagle_backend_x_b200_reduce_fixed(ctypes.byref(d)))
+
+
+def _exact_cases():
+    """Sums the fixed-point partial holds exactly (terms within 2^40 of each other,
+    at most 4096 of them, so no unit lift or halving drops a bit): its rounded value
+    must then be the correctly rounded exact sum, which math.fsum gives. Ties to even,
+    a sticky bit past a tie, cancellation down to subnormals."""
+    e = np.ldexp
+    cases = [
+        [1.0, e(1.0, -53)],                       # exactly half an ulp above 1: ties to 1
+        [1.0, e(3.0, -53)],                       # 1.5 ulp: ties up to the even 1 + 2 ulp
+        [1.0 + e(1.0, -52), e(1.0, -53)],         # odd significand: the tie goes up
+        [1.0, e(1.0, -53), e(1.0, -100)],         # a sticky bit past the tie: up
+        [1.0, -e(1.0, -53), -e(1.0, -100)],       # below 1: the other side
+        [e(1.0, -1022), -e(1.0, -1074)],          # a subnormal result
+        [e(3.0, -1074), e(5.0, -1074), -e(1.0, -1073)],
+        [-e(1.0, 600), e(1.0, 600), e(1.0, 550)],
+        [np.finfo(np.float64).max, e(1.0, 970)],  # exactly half an ulp above max: ties to even (max is odd)
+    ]
+    rng = np.random.default_rng(99)
+    for n in (3, 100, 4096):
+        for scale in (0, 300, -900):
+            x = rng.uniform(-1, 1, n) * np.ldexp(1.0, rng.integers(-20, 21, n) + scale)
+            cases.append(list(x))
+    return cases
+
+
+def test_value_is_the_correctly_rounded_exact_sum(eb, orc):
+    import math
+
+    from fractions import Fraction
+
+    for x in _exact_cases():
+        a = np.array(x, dtype=np.float64)
+        try:
+            want = np.float64(math.fsum(a))
+        except OverflowError:  # rounds past the largest double
+            want = np.float64(np.inf if sum(Fraction(v) for v in a) > 0 else -np.inf)
+        got = fixed(eb, a)
+        assert got.tobytes() == want.tobytes(), (x[:4], got, want)
+        assert orc.reduce_fixed(a).tobytes() == want.tobytes()

@@ -70,3 +70,20 @@ def test_columns_and_companion(orc):
 def test_rule_from_ratio(orc):
     assert orc.fixed_leaf(32) and orc.fixed_leaf(64) and orc.fixed_leaf(8)
     assert not orc.fixed_leaf(2) and not orc.fixed_leaf(1)
+
+
+def test_oracle_value_is_the_correctly_rounded_exact_sum(orc):
+    """The oracle's fixed-point sum rounds an exactly held sum as math.fsum does
+    (ties to even, a sticky bit past a tie, subnormal results, overflow to inf)."""
+    import math
+    from fractions import Fraction
+
+    from test_gpu_reduce_fixed import _exact_cases
+
+    for x in _exact_cases():
+        a = np.array(x, dtype=np.float64)
+        try:
+            want = np.float64(math.fsum(a))
+        except OverflowError:
+            want = np.float64(np.inf if sum(Fraction(v) for v in a) > 0 else -np.inf)
+        assert orc.reduce_fixed(a).tobytes() == want.tobytes(), x[:4]
