@@ -60,7 +60,7 @@ def _args():
     p.add_argument("--mode", default="auto", choices=("auto", "band", "band_eager", "persist", "fused"))
     p.add_argument("--n", type=int, default=None, help="samples of the batch (default: the workload's)")
     p.add_argument("--workload", default="oscillator",
-                   choices=("oscillator", "lorenz", "gambler", "compact_sum", "compact", "reorder"),
+                   choices=("oscillator", "lorenz", "gambler", "compact_sum", "compact", "reorder", "probe"),
                    help="oscillator: the headline line with the other configurations in extra_configs; the "
                         "others print one configuration alone (reorder: the physical reorder and the K-class "
                         "sort of 2^24 slots, one GPU)")
@@ -108,8 +108,13 @@ def _fp64_lane_peak():
     return 64 * props.multi_processor_count * mhz * 1e6 / 1e12
 
 
-def _fp64_probe():
-    """The measured FP64 multiply-add rate of this GPU (the library's probe kernel), T/s."""
+PROBE_KINDS = {0: "1 chain", 1: "2 chains", 2: "4 chains", 3: "8 chains", 4: "oscillator step, 1 sample/lane",
+               5: "oscillator step, 2 samples/lane", 6: "oscillator step, 3 samples/lane"}
+
+
+def _fp64_probe(kind: int = 3, ctas_per_sm: int = 0):
+    """The measured FP64 multiply-add rate of this GPU (the library's probe kernel), T/s:
+    kinds 0-3 independent chains per lane, 4-6 the oscillator's coupled step (PROBE_KINDS)."""
     import ctypes
 
     import torch
@@ -117,8 +122,8 @@ def _fp64_probe():
     from eagle_b200 import _abi
 
     out = ctypes.c_double()
-    _abi.check(_abi.lib().eagle_backend_x_b200_probe_fp64(-1, torch.cuda.current_stream().cuda_stream,
-                                                          ctypes.byref(out)))
+    _abi.check(_abi.lib().eagle_backend_x_b200_probe_fp64(-1, kind, ctas_per_sm,
+                                                          torch.cuda.current_stream().cuda_stream, ctypes.byref(out)))
     return out.value / 1e12
 
 
@@ -434,7 +439,8 @@ def headline(ctx, args):
         # added per step), one more (the t add) step by step; twice as many uncontracted
         fp64_per_step = (2 if fma else 4) + (0 if mode == "persist" else 1)
         lane_peak = _fp64_lane_peak()
-        probe = _fp64_probe()
+        probe = _fp64_probe(3)
+        probe_step = _fp64_probe(4, 4)  # one sample per lane at the kernel's own 4 CTAs of 256 per SM
         achieved = fp64_per_step * steps0 / (kmean / 1e3) / 1e12
         traffic_full = _profile_value(f"{mode}_{'fma' if fma else 'exact'}")
         traffic = traffic_full * per_rank[0]["samples"] / N_TOTAL if traffic_full else None
@@ -449,7 +455,12 @@ def headline(ctx, args):
                      "persistent kernel's mean CUDA-event time inside the timed region",
             "probe": {"value": probe, "frac": achieved / probe,
                       "what": "measured live: the library's FP64 probe (eight independent multiply-add chains per "
-                              "lane, best of five launches)"},
+                              "lane, full occupancy, best of five launches)"},
+            "probe_step": {"value": probe_step, "frac": achieved / probe_step,
+                           "what": "measured live: the same probe running the oscillator's own step (x' = fma(dt, "
+                                   "v, x), v' = fma(-c, x, v), both results needed by the next step: two coupled "
+                                   "chains, three register operands each), one sample per lane, at the kernel's "
+                                   "occupancy (4 CTAs of 256 threads per SM) -- the ceiling of this instruction mix"},
             "dram_gbs": traffic / (kmean / 1e3) / 1e9 if traffic else None,
             "dram_frac": traffic / (kmean / 1e3) / 1e9 / peak_hbm if traffic else None,
             "traffic_kind": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full 2^24-sample launch "
@@ -736,14 +747,21 @@ def extra_compact_sum(ctx, args, data):
             return call
         calls = [make(i) for i in range(len(sharded))]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=ctx.dev)  # 256 MiB: evicts the 126 MB L2
+    marks = []
 
     def step():
         for call in calls:
             flush.zero_()
+            e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            e[0].record(ctx.stream)
             call()
+            e[1].record(ctx.stream)
+            marks.append(e)
 
     with _Clocks(ctx.local) as clocks:
         ms, _ = _timed(ctx, step, 5, 3)
+    torch.cuda.synchronize()
+    per_p = [statistics.mean(m[0].elapsed_time(m[1]) for m in marks[-20:][i::4]) for i in range(4)]
     flush_ms, _ = _timed(ctx, lambda: [flush.zero_() for _ in DENSITIES], 3, 1)
     work_ms = max(ms - flush_ms, 1e-6)
     got = [float(o[-1].item()) if ctx.dist is None else float(o[2].item()) for o in outs]
@@ -757,7 +775,8 @@ def extra_compact_sum(ctx, args, data):
                               "ShardedCompactSum: each rank gathers its survivors, the ragged leaves are exchanged "
                               "once (counts, heads, leaf partials) and folded in rank order",
                       "l2": "a 256 MiB buffer is written before every call (its time is measured apart and taken "
-                            "out)", "flush_ms_per_step": flush_ms},
+                            "out)", "flush_ms_per_step": flush_ms,
+                      "us_per_call": [round(1e3 * v, 1) for v in per_p]},
            "result": {"sums": got, "sum_bits": [_bits(v) for v in got]},
            "roofline": {"bound": "hbm", "achieved": gbs / ctx.world, "peak": peak, "unit": "GB/s",
                         "frac": gbs / ctx.world / peak, "traffic": None, "peak_kind": peak_kind,
@@ -780,16 +799,23 @@ def extra_compact(ctx, args, data):
     comps = [eb.Compactor(mk, drop=False) for mk in d_masks]
     placed = [None] * len(comps)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=ctx.dev)
+    marks = []
 
     def step():
         for i, c in enumerate(comps):
             flush.zero_()
+            e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            e[0].record(ctx.stream)
             c(ctx.stream)
+            e[1].record(ctx.stream)
+            marks.append(e)
             if ctx.dist is not None:
                 placed[i] = global_map(c.index_map, int(c.count.item()), begin)
 
     with _Clocks(ctx.local) as clocks:
         ms, _ = _timed(ctx, step, 5, 3)
+    torch.cuda.synchronize()
+    per_p = [statistics.mean(m[0].elapsed_time(m[1]) for m in marks[-20:][i::4]) for i in range(4)]
     flush_ms, _ = _timed(ctx, lambda: [flush.zero_() for _ in DENSITIES], 3, 1)
     work_ms = max(ms - flush_ms, 1e-6)
     counts = [int(c.count.item()) for c in comps]
@@ -815,7 +841,8 @@ def extra_compact(ctx, args, data):
                       "path": "compact_device per shard" + ("" if ctx.dist is None else
                                                            ", global map offsets from one all-gather of the counts"),
                       "l2": "a 256 MiB buffer is written before every compaction (its time is measured apart and "
-                            "taken out)", "flush_ms_per_step": flush_ms},
+                            "taken out)", "flush_ms_per_step": flush_ms,
+                      "us_per_call": [round(1e3 * v, 1) for v in per_p]},
            "roofline": {"bound": "hbm", "kernel": "compactKernel", "achieved": gbs / ctx.world, "peak": peak,
                         "unit": "GB/s", "frac": gbs / ctx.world / peak, "traffic": None, "peak_kind": peak_kind,
                         "basis": "n mask bytes read + 4 bytes per kept index written, summed over the four masks "
@@ -988,8 +1015,24 @@ def reorder_line(ctx, args):
             "gpu_launches": (2 + 2 * 8 + 1) + (3 + 2 * 8 + 2), "clocks": clocks.summary()}
 
 
+def probe_line(ctx, args):
+    """The FP64 issue probe over its patterns and occupancies (one GPU)."""
+    rows = {}
+    lane_peak = _fp64_lane_peak()
+    with _Clocks(ctx.local) as clocks:
+        for per_sm in (1, 2, 4, 6, 8):
+            rows[f"{per_sm * 8} warps/SM"] = {PROBE_KINDS[k]: round(_fp64_probe(k, per_sm) / lane_peak, 4)
+                                              for k in PROBE_KINDS}
+    return {"metric": "FP64 multiply-adds per second as a fraction of the derived lane peak", "value": None,
+            "unit": "fraction of 64 FP64 lanes x SMs x the max SM clock", "lane_peak_T": lane_peak,
+            "config": {"workload": "fp64-issue-probe", "threads_per_cta": 256}, "rows": rows,
+            "clocks": clocks.summary()}
+
+
 def one_workload(ctx, args):
-    if args.workload == "lorenz":
+    if args.workload == "probe":
+        out = probe_line(ctx, args)
+    elif args.workload == "lorenz":
         out = extra_lorenz(ctx, args)
     elif args.workload == "gambler":
         out = extra_gambler(ctx, args)

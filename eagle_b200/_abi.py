@@ -309,7 +309,7 @@ SIGNATURES = {
     "eagle_backend_x_b200_engine_release": (None, [_P]),
     "eagle_backend_x_b200_engine_time_kernel": (_i32, [_P, _i32]),
     "eagle_backend_x_b200_engine_kernel_ms": (_i32, [_P, ctypes.POINTER(_f32), _i32, ctypes.POINTER(_i32)]),
-    "eagle_backend_x_b200_probe_fp64": (_i32, [_i32, _u64, ctypes.POINTER(ctypes.c_double)]),
+    "eagle_backend_x_b200_probe_fp64": (_i32, [_i32, _u32, _u32, _u64, ctypes.POINTER(ctypes.c_double)]),
 }
 
 

@@ -159,7 +159,7 @@ struct PlaceArgs {
  *  is perm: inv[v] = new slot for each moved value v, and index_map is the
  *  identity over the tile's part of [0, count). */
 template <class T, bool Perm>
-__global__ __launch_bounds__(kThreads) void placeKernel(PlaceArgs a)
+__global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : 4) void placeKernel(PlaceArgs a)
 {
     if (a.fire != nullptr && *a.fire == 0u)
         return;
@@ -177,24 +177,25 @@ __global__ __launch_bounds__(kThreads) void placeKernel(PlaceArgs a)
     const int64_t len = sp - tile0 < kTile ? sp - tile0 : kTile;
     __shared__ uint16_t sKeep[kThreads];
     __shared__ uint32_t sExcl[kThreads];
+    const T* src = static_cast<const T*>(a.stage);
+    // element e of the tile is the (e % 16)-th of thread e / 16's keep bits: read the
+    // stage coalesced (lane-consecutive e) and put each element at its tile-local place,
+    // the kept ones at [0, kept), the dropped ones at [kept, len). The sixteen loads go
+    // out first, so that they are in flight while the tile's keep counts are scanned.
+    T v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int e = t + j * kThreads;
+        v[j] = int64_t(e) < len ? src[tile0 + e] : T{};
+    }
     const uint32_t keep = a.bits[size_t(tile) * kThreads + size_t(t)];
+    const int64_t pre = int64_t(a.prefix[tile]);  // kept slots before the tile
+    const int64_t cnt = int64_t(*a.cnt);
     uint32_t kept = 0;
     const uint32_t excl = blockExclusiveSum(uint32_t(__popc(keep)), kept, scan);
     sKeep[t] = uint16_t(keep);
     sExcl[t] = excl;
     __syncthreads();
-    const int64_t pre = int64_t(a.prefix[tile]);  // kept slots before the tile
-    const int64_t cnt = int64_t(*a.cnt);
-    const T* src = static_cast<const T*>(a.stage);
-    // element e of the tile is the (e % 16)-th of thread e / 16's keep bits: read the
-    // stage coalesced (lane-consecutive e) and put each element at its tile-local place,
-    // the kept ones at [0, kept), the dropped ones at [kept, len)
-    T v[kPer];
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {  // all sixteen loads in flight before the first is used
-        const int e = t + j * kThreads;
-        v[j] = int64_t(e) < len ? src[tile0 + e] : T{};
-    }
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
         const int e = t + j * kThreads;
@@ -548,18 +549,9 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
     if (tile0 >= lim)
         return;
     const int64_t len = lim - tile0 < kTile ? lim - tile0 : kTile;
-    // the tile's count of each key, from the scanned key-major matrix: the next entry's
-    // first destination (the next key's first tile, or the total after the last) less its own
-    uint32_t c = 0;
-    if (uint32_t(t) < a.nKeys) {
-        const size_t at = size_t(t) * a.tiles + blockIdx.x;
-        const size_t m = size_t(a.nKeys) * a.tiles;
-        c = (at + 1 < m ? a.base[at + 1] : *a.total) - a.base[at];
-    }
-    uint32_t all = 0;
-    sStart[t] = blockExclusiveSum(c, all, scan);  // the key's first place in the tile
     // each slot's value, key and rank among its key's slots (the histogram pass ranked
-    // them): thread t takes slots t, t + 256, ..., all sixteen loads in flight
+    // them): thread t takes slots t, t + 256, ..., all sixteen loads in flight while the
+    // tile's key counts below are scanned
     const T* src = static_cast<const T*>(a.stage);
     T v[kPer];
     uint32_t kr[kPer];
@@ -570,6 +562,16 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
         v[j] = in ? src[i] : T{};
         kr[j] = in ? (uint32_t(a.keys[i]) << 16) | uint32_t(a.rel[i]) : kNoKey << 16;
     }
+    // the tile's count of each key, from the scanned key-major matrix: the next entry's
+    // first destination (the next key's first tile, or the total after the last) less its own
+    uint32_t c = 0;
+    if (uint32_t(t) < a.nKeys) {
+        const size_t at = size_t(t) * a.tiles + blockIdx.x;
+        const size_t m = size_t(a.nKeys) * a.tiles;
+        c = (at + 1 < m ? a.base[at + 1] : *a.total) - a.base[at];
+    }
+    uint32_t all = 0;
+    sStart[t] = blockExclusiveSum(c, all, scan);  // the key's first place in the tile
     __syncthreads();  // sStart
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {

@@ -829,11 +829,16 @@ eagle_backend_status eagle_backend_x_b200_engine_kernel_ms(eagle_b200_engine h, 
     int32_t* count);
 
 /* The FP64 issue probe (this backend's addition, for measurement; no counterpart in
- * eagle): times a kernel whose every lane runs eight independent chains of fused
- * double-precision multiply-adds on ``device`` (-1: the current one) and writes the
- * best rate of five launches, in lane multiply-adds per second. Synchronises
- * ``stream`` and allocates stream-ordered memory: not for use inside a capture. */
-eagle_backend_status eagle_backend_x_b200_probe_fp64(int32_t device, uint64_t stream, double* fma_per_s);
+ * eagle): times a kernel of fused double-precision multiply-adds on ``device`` (-1:
+ * the current one) and writes the best rate of five launches, in lane multiply-adds
+ * per second. ``kind`` 0..3: 1, 2, 4 or 8 independent chains per lane, c = fma(c, a,
+ * b) with a and b arguments; 4..6: the oscillator's step on 1, 2 or 3 samples per
+ * lane, x' = fma(dt, v, x) and v' = fma(-c, x, v), whose two multiply-adds need both
+ * results of the step before. ``ctas_per_sm``: resident CTAs of 256 threads per SM (0:
+ * as many as fit). Synchronises ``stream`` and allocates stream-ordered memory: not
+ * for use inside a capture. */
+eagle_backend_status eagle_backend_x_b200_probe_fp64(int32_t device, uint32_t kind, uint32_t ctas_per_sm,
+    uint64_t stream, double* fma_per_s);
 
 #ifdef __cplusplus
 } /* extern "C" */
