@@ -127,6 +127,15 @@ def _fp64_probe(kind: int = 3, ctas_per_sm: int = 0):
     return out.value / 1e12
 
 
+_T0 = time.time()
+
+
+def _log(msg: str) -> None:
+    """A progress line on stderr (rank and seconds since start), so a slow phase shows."""
+    sys.stderr.write(f"[bench rank {os.environ.get('RANK', '0')} +{time.time() - _T0:.1f}s] {msg}\n")
+    sys.stderr.flush()
+
+
 def _host_cores() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -390,6 +399,7 @@ def headline(ctx, args):
                  "persist_kernel_ms": r[1], "launch_ms": r[2], "reduce_ms": r[3], "allgather_us": 1e3 * r[4],
                  "combine_us": 1e3 * r[5], "sample_steps": int(r[6])} for q, r in enumerate(rows)]
 
+    _log("headline timed; end-to-end leg")
     # e2e: the same runs through the C-ABI with this rank's shard in pinned host memory
     e2e = None
     if not args.no_e2e:
@@ -491,6 +501,7 @@ def headline(ctx, args):
                        "finished": finished, "steps": longest, "sample_steps": int(all_steps)},
         }
         if not args.no_cpu:
+            _log("oracle over the whole batch")
             orc = _oracle()
             st = [x0_all.copy(), np.zeros(n_total), np.zeros(n_total), np.zeros(n_total, np.uint8)]
             t0 = time.perf_counter()
@@ -881,19 +892,26 @@ def extras(ctx, args):
     import torch
 
     out = {}
+    _log("lorenz")
     out["lorenz"] = extra_lorenz(ctx, args)
     torch.cuda.empty_cache()
+    _log("gambler")
     out["gambler"] = extra_gambler(ctx, args)
     torch.cuda.empty_cache()
+    _log("compaction data")
     n_total = 1 << 28
     begin, n, vals, masks = _c5_shard(ctx, n_total)
     data = (n_total, begin, n, vals, masks)
+    _log("compact-then-sum")
     out["compact_sum"] = extra_compact_sum(ctx, args, data)
     torch.cuda.empty_cache()
+    _log("compaction")
     out["compact"] = extra_compact(ctx, args, data)
     torch.cuda.empty_cache()
+    _log("compact-then-sum parity")
     c5_parity(ctx, args, data, out["compact_sum"])
     ctx.barrier()
+    _log("extras done")
     return out
 
 
@@ -1064,12 +1082,15 @@ def main():
             raise SystemExit("--impl reference times the headline workload")
         reference(args)
         return
+    _log("start")
     ctx = Ctx()
+    _log(f"process group ready ({ctx.world} ranks)")
     if args.workload != "oscillator":
         one_workload(ctx, args)
         ctx.close()
         return
     line = headline(ctx, args)
+    _log("headline done")
     if not args.no_extra:
         ext = extras(ctx, args)
         if line is not None:
