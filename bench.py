@@ -783,8 +783,9 @@ def extra_compact_sum(ctx, args, data):
            "ms_per_step": ms, "steps": 5, "warmup": 3, "dtype": "f64 values, u8 mask",
            "config": {"workload": "compact-then-sum", "n_total": n_total, "p": list(DENSITIES),
                       "path": "CompactSum (fused: the kept values are never written)" if ctx.dist is None else
-                              "ShardedCompactSum: each rank gathers its survivors, the ragged leaves are exchanged "
-                              "once (counts, heads, leaf partials) and folded in rank order",
+                              "ShardedCompactSum: each rank gathers its survivors; fixed-size device all-gathers "
+                              "of the counts, every rank's first 4095 survivors and the leaf partials, with the "
+                              "leaves and the rank-order fold formed on the device (no host read)",
                       "l2": "a 256 MiB buffer is written before every call (its time is measured apart and taken "
                             "out)", "flush_ms_per_step": flush_ms,
                       "us_per_call": [round(1e3 * v, 1) for v in per_p]},
@@ -803,25 +804,28 @@ def extra_compact(ctx, args, data):
     import torch
 
     import eagle_b200 as eb
-    from eagle_b200.shard import global_map
+    from eagle_b200.shard import ShardedCompactor
 
     n_total, begin, n, vals, masks = data
     d_masks = [torch.from_numpy(mk).to(ctx.dev) for mk in masks]
-    comps = [eb.Compactor(mk, drop=False) for mk in d_masks]
-    placed = [None] * len(comps)
+    if ctx.dist is None:
+        comps = [eb.Compactor(mk, drop=False) for mk in d_masks]
+        calls = comps
+    else:  # each rank's map placed in the map over every shard by one device all-gather of the counts
+        placed = [ShardedCompactor(mk, begin, drop=False) for mk in d_masks]
+        comps = [pc.comp for pc in placed]
+        calls = placed
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=ctx.dev)
     marks = []
 
     def step():
-        for i, c in enumerate(comps):
+        for call in calls:
             flush.zero_()
             e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             e[0].record(ctx.stream)
-            c(ctx.stream)
+            call(ctx.stream)
             e[1].record(ctx.stream)
             marks.append(e)
-            if ctx.dist is not None:
-                placed[i] = global_map(c.index_map, int(c.count.item()), begin)
 
     with _Clocks(ctx.local) as clocks:
         ms, _ = _timed(ctx, step, 5, 3)
@@ -842,15 +846,17 @@ def extra_compact(ctx, args, data):
             got = c.index_map[:counts[i]].cpu().numpy()
             ok_local &= counts[i] == want.size and np.array_equal(got, want)
             if ctx.dist is not None:
-                idx, offset, total = placed[i]
+                pc = placed[i]
+                offset, total = int(pc.offset.item()), int(pc.total.item())
                 ok_local &= total == totals[i] and offset == int(sum(r[i] for r in rows[:ctx.rank]))
-                ok_local &= np.array_equal(idx[:min(4096, want.size)].cpu().numpy(), want[:4096] + begin)
+                ok_local &= np.array_equal(pc.indices()[:4096].cpu().numpy(), want[:4096] + begin)
     ok_all = ctx.all_true(ok_local)
     out = {"metric": "GB/s, 2^28 active-set compaction vs the HBM roofline", "value": gbs, "unit": "GB/s",
            "ms_per_step": ms, "steps": 5, "warmup": 3, "dtype": "u8 mask, int32 map",
            "config": {"workload": "active-set-compaction", "n_total": n_total, "p": list(DENSITIES), "kept": totals,
                       "path": "compact_device per shard" + ("" if ctx.dist is None else
-                                                           ", global map offsets from one all-gather of the counts"),
+                                                           ", each rank's place in the map over all shards from one "
+                                                           "device all-gather of the counts (no host read)"),
                       "l2": "a 256 MiB buffer is written before every compaction (its time is measured apart and "
                             "taken out)", "flush_ms_per_step": flush_ms,
                       "us_per_call": [round(1e3 * v, 1) for v in per_p]},

@@ -745,7 +745,8 @@ class CompactSum:
         torch = _t()
         if self._gdesc is None:
             dev = self.mask.device
-            self.kept = torch.empty(max(self.n, 1), dtype=torch.float64, device=dev)
+            # at least one leaf's worth, so that a rank can always share its first 4095 survivors
+            self.kept = torch.empty(max(self.n, 4096), dtype=torch.float64, device=dev)
             d = _abi.new(_abi.CompactDesc, flags=_abi.COMPACT_MASK_IS_DROP if self.drop else 0, device=dev.index,
                          n=self.n)
             _abi.check(_abi.lib().eagle_backend_x_b200_compact_gather(ctypes.byref(d), 0, 0, 8))  # query

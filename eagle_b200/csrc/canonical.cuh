@@ -313,6 +313,31 @@ __device__ __forceinline__ P leafPartial(const T* __restrict__ in, const T* __re
     return leafTree(p, live, s);
 }
 
+/** leafPartial of a leaf whose i-th element (i < ``cnt``) is ``at(i)``, for leaves
+ *  whose elements do not sit in one plane; the same slots, terms and order, so the
+ *  same bits as leafPartial over those elements. No companion. */
+template <class P, class T, class At>
+__device__ __forceinline__ P leafPartialAt(At at, int64_t cnt, P* s)
+{
+    const int t = int(threadIdx.x);
+    const int live = cnt < kSlots ? int(cnt) : kSlots;
+    P p{};
+    if (t < live) {
+        T v[kTerms];
+#pragma unroll
+        for (int k = 0; k < kTerms; ++k) {
+            const int64_t i = int64_t(t) + int64_t(k) * kSlots;
+            v[k] = i < cnt ? at(i) : T(0);
+        }
+        p = P::of(v[0]);
+#pragma unroll
+        for (int k = 1; k < kTerms; ++k)
+            if (int64_t(t) + int64_t(k) * kSlots < cnt)
+                p.add(v[k]);
+    }
+    return leafTree(p, live, s);
+}
+
 /** Pairwise levels over ``v[0, m)`` in shared memory (an aligned subtree): node i
  *  of level L sits at i * 2^L; its right child, if present, at + 2^(L-1). */
 template <class P>

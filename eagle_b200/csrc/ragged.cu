@@ -1,0 +1,190 @@
+// The canonical sum of a compaction's survivors spread over several ranks, with no
+// host round trip.
+//
+// After a compaction on every rank, rank r holds c_r survivors in sample order; the
+// survivors of all ranks, concatenated in rank order, are the one-device compaction
+// of the whole batch, and its canonical sum is the pairwise tree over 4096-survivor
+// leaves of that concatenation (eagle/reduce/canonical.h:10-32). Rank r starts at
+// o_r = c_0 + ... + c_{r-1}, which no rank knows before the counts are exchanged, so
+// a rank's leaves are not aligned to its own survivors. The exchange here is three
+// fixed-size all-gathers (every rank's count, its first 4095 survivors, its leaf
+// partials) around two kernels that read the gathered counts on the device:
+//
+//   raggedLeavesKernel  one CTA per leaf that STARTS in this rank's part: the leaf's
+//                       survivors come from this rank, and past its end from the
+//                       next ranks' gathered heads (a leaf that starts here ends
+//                       within 4095 survivors of this rank's end);
+//   raggedFoldKernel    one CTA: every rank's leaf partials, in rank order (the
+//                       order of the leaves), through the pairwise levels.
+//
+// Every rank runs the same fold over the same gathered partials, so every rank gets
+// the bits of the one-device compact-then-sum, at any rank count.
+#include "canonical.cuh"
+
+#define EB_API extern "C" __attribute__((visibility("default")))
+
+namespace eb {
+namespace {
+
+constexpr int kHead = int(kLeaf) - 1;  // survivors a rank shares with the earlier ranks
+constexpr int kMaxRanks = 256;
+
+struct RaggedLeavesArgs {
+    const double* kept;      // this rank's survivors, sample order
+    const uint32_t* counts;  // every rank's survivor count (gathered)
+    const double* heads;     // every rank's first kHead survivors (gathered), [world][kHead]
+    int32_t rank, world;
+    double* partials;        // out: (hi, comp) of each leaf starting in this rank's part
+    int64_t cap;             // leaves ``partials`` holds
+    uint32_t* leafCount;     // out: leaves starting in this rank's part
+};
+
+__global__ __launch_bounds__(kSlots) void raggedLeavesKernel(RaggedLeavesArgs a)
+{
+    __shared__ int64_t sOff[kMaxRanks + 1];  // sOff[q] = first survivor of rank q; sOff[world] = total
+    __shared__ CompP<double> s[kSlots];
+    if (threadIdx.x == 0) {
+        int64_t o = 0;
+        for (int q = 0; q < a.world; ++q) {
+            sOff[q] = o;
+            o += int64_t(a.counts[q]);
+        }
+        sOff[a.world] = o;
+    }
+    __syncthreads();
+    const int64_t mine = sOff[a.rank], end = sOff[a.rank + 1], total = sOff[a.world];
+    const int64_t first = (mine + kLeaf - 1) / kLeaf;  // the first leaf starting at or after ``mine``
+    const int64_t leaves = end > first * kLeaf ? (end - first * kLeaf + kLeaf - 1) / kLeaf : 0;
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+        *a.leafCount = uint32_t(leaves < a.cap ? leaves : a.cap);
+    const int64_t k = blockIdx.x;
+    if (k >= leaves || k >= a.cap)
+        return;
+    const int64_t start = (first + k) * kLeaf;  // global position of the leaf's first survivor
+    const int64_t cnt = total - start < kLeaf ? total - start : kLeaf;
+    const double* kept = a.kept;
+    const double* heads = a.heads;
+    const int32_t rank = a.rank, world = a.world;
+    auto at = [&](int64_t i) -> double {
+        const int64_t g = start + i;
+        if (g < end)
+            return kept[g - mine];
+        int q = rank + 1;  // a later rank's head: g - sOff[q] < kHead for the rank holding g
+        while (q + 1 < world && g >= sOff[q + 1])
+            ++q;
+        return heads[int64_t(q) * kHead + (g - sOff[q])];
+    };
+    const CompP<double> p = leafPartialAt<CompP<double>, double>(at, cnt, s);
+    if (threadIdx.x == 0) {
+        a.partials[2 * k] = p.h;
+        a.partials[2 * k + 1] = p.c;
+    }
+}
+
+/** The pairwise levels over every rank's leaf partials in rank order: rank q's
+ *  ``leafCounts[q]`` partials sit at ``gathered + 2 cap q``. One CTA; ``work`` holds
+ *  2 ceil(leaves / kChunk) doubles. out = {hi, comp, value}; no leaves: zeros. */
+__global__ __launch_bounds__(kSlots) void raggedFoldKernel(const double* __restrict__ gathered,
+    const uint32_t* __restrict__ leafCounts, int32_t world, int64_t cap, double* __restrict__ work,
+    double* __restrict__ out)
+{
+    __shared__ CompP<double> v[kChunk];
+    __shared__ int64_t sFirst[kMaxRanks + 1];  // sFirst[q] = rank q's first leaf in the whole order
+    if (threadIdx.x == 0) {
+        int64_t o = 0;
+        for (int q = 0; q < world; ++q) {
+            sFirst[q] = o;
+            o += int64_t(leafCounts[q]);
+        }
+        sFirst[world] = o;
+    }
+    __syncthreads();
+    int64_t count = sFirst[world];
+    if (count == 0) {
+        if (threadIdx.x == 0)
+            out[0] = out[1] = out[2] = 0.0;
+        return;
+    }
+    bool firstLevel = true;
+    while (firstLevel || count > 1) {
+        const int64_t chunks = (count + kChunk - 1) / kChunk;
+        for (int64_t c = 0; c < chunks; ++c) {
+            const int cnt = int(count - c * kChunk < kChunk ? count - c * kChunk : kChunk);
+            for (int i = int(threadIdx.x); i < cnt; i += int(blockDim.x)) {
+                const int64_t j = c * kChunk + i;
+                if (firstLevel) {
+                    int q = 0;  // the rank whose leaves hold j
+                    while (q + 1 < world && j >= sFirst[q + 1])
+                        ++q;
+                    const double* src = gathered + 2 * (cap * q + (j - sFirst[q]));
+                    v[i] = CompP<double>{src[0], src[1]};
+                } else {
+                    v[i] = CompP<double>{work[2 * j], work[2 * j + 1]};
+                }
+            }
+            __syncthreads();
+            levels(v, cnt);
+            if (threadIdx.x == 0) {
+                work[2 * c] = v[0].h;
+                work[2 * c + 1] = v[0].c;
+            }
+            __syncthreads();
+        }
+        count = chunks;
+        firstLevel = false;
+    }
+    if (threadIdx.x == 0) {
+        const CompP<double> r{work[0], work[1]};
+        out[0] = r.h;
+        out[1] = r.c;
+        out[2] = r.value();
+    }
+}
+
+}  // namespace
+}  // namespace eb
+
+using namespace eb;
+
+EB_API eagle_backend_status eagle_backend_x_b200_ragged_leaves(uint64_t kept, uint64_t counts, uint64_t heads,
+    int32_t rank, int32_t world, uint64_t partials, int64_t cap, uint64_t leaf_count, uint64_t stream)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_ragged_leaves";
+        if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+            invalid(std::string(who) + ": need 0 <= rank < world <= 256");
+        if (cap < 1 || cap > (INT64_C(1) << 31))
+            invalid(std::string(who) + ": cap must lie in [1, 2^31]");
+        if (counts == 0 || heads == 0 || partials == 0 || leaf_count == 0)
+            invalid(std::string(who) + ": counts, heads, partials and leaf_count must be device addresses");
+        RaggedLeavesArgs a{};
+        a.kept = reinterpret_cast<const double*>(kept);
+        a.counts = reinterpret_cast<const uint32_t*>(counts);
+        a.heads = reinterpret_cast<const double*>(heads);
+        a.rank = rank;
+        a.world = world;
+        a.partials = reinterpret_cast<double*>(partials);
+        a.cap = cap;
+        a.leafCount = reinterpret_cast<uint32_t*>(leaf_count);
+        raggedLeavesKernel<<<unsigned(cap), kSlots, 0, seamStream(stream)>>>(a);
+        launchCheck(who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, uint64_t leaf_counts, int32_t world,
+    int64_t cap, uint64_t work, uint64_t out, uint64_t stream)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_ragged_fold";
+        if (world < 1 || world > kMaxRanks)
+            invalid(std::string(who) + ": world must lie in [1, 256]");
+        if (cap < 1)
+            invalid(std::string(who) + ": cap must be >= 1");
+        if (gathered == 0 || leaf_counts == 0 || work == 0 || out == 0)
+            invalid(std::string(who) + ": gathered, leaf_counts, work and out must be device addresses");
+        raggedFoldKernel<<<1, kSlots, 0, seamStream(stream)>>>(reinterpret_cast<const double*>(gathered),
+            reinterpret_cast<const uint32_t*>(leaf_counts), world, cap, reinterpret_cast<double*>(work),
+            reinterpret_cast<double*>(out));
+        launchCheck(who);
+    });
+}

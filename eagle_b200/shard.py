@@ -234,19 +234,93 @@ def compact_sum_sharded(mask, values, *, drop: bool = False, group=None):
 
 
 class ShardedCompactSum:
-    """:func:`compact_sum_sharded` prepared once per shard: the compaction's buffers
-    are allocated at construction, so each call enqueues the gather of this rank's
-    survivors, reads their count (one host wait: the exchange is planned on the
-    host) and makes the exchange. Returns ``(hi, comp, value)`` on every rank."""
+    """The canonical sum of every rank's survivors as ONE concatenation in rank order,
+    prepared once per shard and run with no host round trip: each call gathers this
+    rank's survivors on its device, all-gathers the survivor counts and every rank's
+    first ``LEAF - 1`` survivors, forms the partial of each leaf that starts in this
+    rank's part (``eagle_backend_x_b200_ragged_leaves``, which reads the gathered counts
+    on the device), all-gathers the leaf partials and folds them in rank order
+    (``eagle_backend_x_b200_ragged_fold``). Every collective moves a fixed number of
+    bytes, so nothing waits on the host. Returns ``(hi, comp, value)`` on every rank:
+    the bits of the one-device compact-then-sum of the concatenated shards."""
 
     def __init__(self, mask, values, *, drop: bool = False, group=None):
+        import torch
+        import torch.distributed as dist
+
         from ._api import CompactSum
 
         self.cs = CompactSum(mask, values, drop=drop)
         self.group = group
-        self.count = 0
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        dev = mask.device
+        n = mask.numel()
+        self.cap = (n + LEAF - 1) // LEAF + 1
+        self.counts = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        self.heads = torch.zeros(self.world * (LEAF - 1), dtype=torch.float64, device=dev)
+        self.partials = torch.zeros(2 * self.cap, dtype=torch.float64, device=dev)
+        self.leaf_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.all_partials = torch.zeros(self.world * 2 * self.cap, dtype=torch.float64, device=dev)
+        self.all_leaf_counts = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        self.work = torch.zeros(2 * ((self.world * self.cap + 511) // 512) + 2, dtype=torch.float64, device=dev)
+        self.out = torch.zeros(3, dtype=torch.float64, device=dev)
 
-    def __call__(self):
-        self.cs.gather()
-        self.count = int(self.cs.count.item())
-        return ragged_fold(self.cs.kept, self.count, group=self.group)
+    def __call__(self, stream=None):
+        import torch
+        import torch.distributed as dist
+
+        s = (stream or torch.cuda.current_stream()).cuda_stream
+        lib = _abi.lib()
+        self.cs.gather(stream)
+        dist.all_gather_into_tensor(self.counts, self.cs.count, group=self.group)
+        dist.all_gather_into_tensor(self.heads, self.cs.kept[:LEAF - 1], group=self.group)
+        _abi.check(lib.eagle_backend_x_b200_ragged_leaves(
+            self.cs.kept.data_ptr(), self.counts.data_ptr(), self.heads.data_ptr(), self.rank, self.world,
+            self.partials.data_ptr(), self.cap, self.leaf_count.data_ptr(), s))
+        dist.all_gather_into_tensor(self.all_partials, self.partials, group=self.group)
+        dist.all_gather_into_tensor(self.all_leaf_counts, self.leaf_count, group=self.group)
+        _abi.check(lib.eagle_backend_x_b200_ragged_fold(
+            self.all_partials.data_ptr(), self.all_leaf_counts.data_ptr(), self.world, self.cap,
+            self.work.data_ptr(), self.out.data_ptr(), s))
+        return self.out
+
+
+class ShardedCompactor:
+    """This rank's compaction, placed in the map over every rank's shard with no host
+    round trip: each call compacts the shard (``begin`` is its first sample) and
+    all-gathers the counts on the device; ``offset`` (this rank's first place in the
+    concatenated map) and ``total`` are then device tensors. The rank's part of the
+    map is ``index_map[:count] + begin`` (:meth:`indices` forms it, int64)."""
+
+    def __init__(self, mask, begin: int, *, drop: bool = True, group=None):
+        import torch
+        import torch.distributed as dist
+
+        from ._api import Compactor
+
+        self.comp = Compactor(mask, drop=drop)
+        self.begin = int(begin)
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.counts = torch.zeros(dist.get_world_size(group), dtype=torch.int32, device=mask.device)
+        self.offset = None
+        self.total = None
+
+    def __call__(self, stream=None):
+        import torch
+        import torch.distributed as dist
+
+        self.comp(stream)
+        dist.all_gather_into_tensor(self.counts, self.comp.count, group=self.group)
+        c = self.counts.to(torch.int64)
+        self.offset = c[:self.rank].sum()
+        self.total = c.sum()
+        return self.offset, self.total
+
+    def indices(self):
+        """This rank's survivors as global sample indices (int64), in map order."""
+        import torch
+
+        count = int(self.comp.count.item())
+        return self.comp.index_map[:count].to(torch.int64) + self.begin

@@ -611,6 +611,25 @@ eagle_backend_status eagle_backend_reorder_classes_device(struct eagle_backend_r
 /* eagle_backend.h:847: classify ``ptr`` as seen from ``device`` (-1: the current one) */
 eagle_backend_status eagle_backend_pointer_residency(int32_t device, uint64_t ptr, int32_t* cls);
 
+/* The canonical sum of a compaction's survivors over several ranks with no host round
+ * trip (this backend's addition; eagle folds per-rank partials of aligned shards in
+ * rank order, eagle/exec/RankPartition.h:222-241, and has no ragged case). Rank r
+ * holds ``kept`` = its c_r survivors in sample order; ``counts`` = every rank's
+ * uint32 count and ``heads`` = every rank's first 4095 survivors ([world][4095]
+ * float64), both all-gathered in rank order. ragged_leaves writes the (hi, comp)
+ * partial of each 4096-survivor leaf of the concatenation that STARTS in rank r's
+ * part (its survivors past rank r's end taken from the later ranks' heads) into
+ * ``partials`` (2 * cap doubles) and their number into ``leaf_count`` (uint32). */
+eagle_backend_status eagle_backend_x_b200_ragged_leaves(uint64_t kept, uint64_t counts, uint64_t heads,
+    int32_t rank, int32_t world, uint64_t partials, int64_t cap, uint64_t leaf_count, uint64_t stream);
+/* ragged_fold: every rank's leaf partials (``gathered`` = [world][cap][2], all-gathered)
+ * and leaf counts (``leaf_counts``, uint32[world]) through the canonical pairwise
+ * levels, in rank order, into ``out`` = {hi, comp, value} (zeros for no survivors):
+ * the bits of the one-device compact-then-sum of the concatenated shards. ``work``
+ * holds 2 * ceil(world * cap / 512) + 2 doubles. One CTA. */
+eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, uint64_t leaf_counts, int32_t world,
+    int64_t cap, uint64_t work, uint64_t out, uint64_t stream);
+
 /* eagle_backend_x_b200_compact_wait_check: compact_device with its first tile withheld,
  * to exercise the bounded look-back wait (this backend's addition; eagle's multi-level
  * scan has no wait to bound, eagle/cuda/Scan.h:32-141). No CTA takes tile 0, so every

@@ -63,6 +63,32 @@ def main():
             print(f"MISMATCH ragged {got[2].item()!r} whole {want!r}", flush=True)
             sys.exit(1)
         print("RAGGED COMPACT-SUM OK", world, want, flush=True)
+    # the same survivors through the device-side exchange (no host round trip), and a
+    # batch whose shards keep few survivors, so that one leaf spans several ranks' heads
+    for frac, label in ((0.37, "dense"), (0.0003, "sparse")):
+        keep2 = keep if label == "dense" else g.random(nv) < frac
+        sc = shard.ShardedCompactSum(torch.from_numpy(keep2[b:b + c].copy()).cuda(),
+                                     torch.from_numpy(vals[b:b + c].copy()).cuda())
+        for _ in range(2):  # twice: the prepared buffers are reused
+            out = sc()
+        torch.cuda.synchronize()
+        if rank == 0:
+            import oracle
+
+            want = oracle.reduce(vals[keep2])[0]
+            if np.float64(out[2].item()).tobytes() != np.float64(want).tobytes():
+                print(f"MISMATCH device ragged ({label}) {out[2].item()!r} whole {want!r}", flush=True)
+                sys.exit(1)
+    if rank == 0:
+        print("DEVICE RAGGED COMPACT-SUM OK", world, flush=True)
+    sm = shard.ShardedCompactor(torch.from_numpy(keep[b:b + c].copy()).cuda(), b, drop=False)
+    offset_d, total_d = sm()
+    whole = np.flatnonzero(keep)
+    mine = sm.indices().cpu().numpy()
+    off = int(offset_d.item())
+    if int(total_d.item()) != whole.size or not np.array_equal(mine, whole[off:off + mine.size]):
+        print(f"MISMATCH device map rank {rank} offset {off}", flush=True)
+        sys.exit(1)
     # the compaction map over every shard: each rank's global indices at its offset
     idx, offset, total = shard.compact_map_sharded(torch.from_numpy(keep[b:b + c].copy()).cuda(), b, drop=False)
     whole = np.flatnonzero(keep)

@@ -34,3 +34,4 @@ def test_shards_fold_to_the_whole(world):
     assert "RANK-ORDER FOLD OK" in r.stdout
     assert "RAGGED COMPACT-SUM OK" in r.stdout
     assert "SHARDED MAP OK" in r.stdout
+    assert "DEVICE RAGGED COMPACT-SUM OK" in r.stdout

@@ -1,0 +1,70 @@
+"""The device-side ragged exchange of compact-then-sum on one GPU, with the ranks
+emulated: the batch is split into W shards, each shard compacted on its own, the
+counts and heads stacked as the all-gathers would stack them, then every rank's
+leaves (eagle_backend_x_b200_ragged_leaves) and the rank-order fold
+(eagle_backend_x_b200_ragged_fold) -- bit for bit the one-device compact-then-sum
+of the whole batch and the oracle's compaction + canonical sum, for even and uneven
+splits, empty shards, and shards so sparse that one leaf spans many ranks."""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+LEAF = 4096
+
+
+def _emulated(eb, vals, keep, bounds):
+    from eagle_b200 import _abi
+
+    lib = _abi.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    world = len(bounds) - 1
+    sums = []
+    for r in range(world):
+        b, e = bounds[r], bounds[r + 1]
+        cs = eb.CompactSum(torch.from_numpy(keep[b:e].copy()).cuda(), torch.from_numpy(vals[b:e].copy()).cuda())
+        cs.gather()
+        sums.append(cs)
+    cap = max((bounds[r + 1] - bounds[r] + LEAF - 1) // LEAF + 1 for r in range(world))
+    counts = torch.cat([cs.count for cs in sums]).contiguous()
+    heads = torch.cat([cs.kept[:LEAF - 1] for cs in sums]).contiguous()
+    gathered = torch.zeros(world * 2 * cap, dtype=torch.float64, device="cuda")
+    leaf_counts = torch.zeros(world, dtype=torch.int32, device="cuda")
+    for r, cs in enumerate(sums):
+        _abi.check(lib.eagle_backend_x_b200_ragged_leaves(
+            cs.kept.data_ptr(), counts.data_ptr(), heads.data_ptr(), r, world,
+            gathered.data_ptr() + 8 * 2 * cap * r, cap, leaf_counts.data_ptr() + 4 * r, s))
+    work = torch.zeros(2 * ((world * cap + 511) // 512) + 2, dtype=torch.float64, device="cuda")
+    out = torch.zeros(3, dtype=torch.float64, device="cuda")
+    _abi.check(lib.eagle_backend_x_b200_ragged_fold(gathered.data_ptr(), leaf_counts.data_ptr(), world, cap,
+                                                    work.data_ptr(), out.data_ptr(), s))
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+CASES = [
+    (1 << 20, 0.37, (0, 1 << 19, 1 << 20)),                    # two even shards
+    ((1 << 20) + 777, 0.61, None),                             # four uneven shards
+    (300_000, 0.002, None),                                    # sparse: leaves span many ranks
+    (200_000, 0.5, (0, 0, 100_000, 100_000, 200_000)),         # empty shards
+    (100_000, 0.0, None),                                      # nothing kept
+    (65_536, 1.0, (0, 1, 2, 3, 65_536)),                       # one-survivor shards
+]
+
+
+@pytest.mark.parametrize("n,p,bounds", CASES)
+def test_emulated_ranks_equal_the_whole(eb, orc, n, p, bounds):
+    g = np.random.default_rng([n, int(p * 1000)])
+    vals = orc.corpus(n, 91)
+    keep = g.random(n) < p
+    if bounds is None:
+        w = 8 if p < 0.01 else 4
+        cuts = np.sort(g.integers(0, n, w - 1))
+        bounds = (0, *[int(c) for c in cuts], n)
+    got = _emulated(eb, vals, keep, list(bounds))
+    whole = eb.CompactSum(torch.from_numpy(keep).cuda(), torch.from_numpy(vals).cuda())().cpu().numpy()
+    want = orc.reduce(vals[keep])[0] if keep.any() else np.float64(0.0)  # the oracle refuses an empty sum
+    assert np.float64(got[2]).tobytes() == np.float64(want).tobytes() == whole[-1].tobytes()
