@@ -679,10 +679,7 @@ def extra_gambler(ctx, args):
                       "status": "finished" if sum(r[1] for r in rows) == n_total else "max_steps",
                       "l2": "inputs 768 MiB over all shards, re-initialised every step"},
            "result": {"sum_time": total, "mean_time": total / n_total},
-           "roofline": {"bound": "integer issue", "kernel": "gamblerPersist", "achieved": None, "peak": None,
-                        "unit": None, "frac": None, "traffic": None, "kernel_ms": rows[0][3],
-                        "basis": "Philox-4x32-10 per 128 steps plus a compare per step: integer-issue bound; "
-                                 "the ncu pipe shares are in profiles/gamblerPersist_16M_philox.md"},
+           "roofline": _issue_roofline(rows[0][0], rows[0][3]),
            "gpu_launches": 4 * steps, "clocks": clocks.summary()}
     ok_local = True
     if not args.no_cpu:
@@ -702,6 +699,29 @@ def extra_gambler(ctx, args):
                                  "shard's device int64 sum equal to the exact sum of its time plane; the total is "
                                  "the exact sum of the shard sums"}
     return out
+
+
+def _issue_roofline(sample_steps, kernel_ms):
+    """The gambler kernel's roofline: warp instructions issued per second (its ncu count per
+    sample-step x the rank's sample-steps / its kernel time) against 4 schedulers per SM x
+    SMs x the max SM clock."""
+    import torch
+
+    per = _profile_value("gambler_warp_instr_per_sample_step")
+    props = torch.cuda.get_device_properties(torch.cuda.current_device())
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            mhz = float(json.load(f)["sm_max_mhz"])
+    except Exception:
+        mhz = 1965.0
+    peak = 4 * props.multi_processor_count * mhz * 1e6 / 1e12
+    achieved = per * sample_steps / (kernel_ms / 1e3) / 1e12 if per else None
+    return {"bound": "integer issue", "kernel": "gamblerPersist", "achieved": achieved, "peak": peak,
+            "unit": "T warp instructions/s", "frac": achieved / peak if achieved else None, "traffic": None,
+            "kernel_ms": kernel_ms, "peak_kind": "derived: 4 schedulers per SM x SMs x the max SM clock",
+            "basis": "warp instructions per sample-step counted by ncu (profiles/traffic.json) x rank 0's "
+                     "sample-steps / its kernel time; Philox-4x32-10 per 128 steps plus a compare per step keep "
+                     "the integer pipes busy (profiles/gamblerPersist_16M_philox.md)"}
 
 
 def _c5_block(b: int):
