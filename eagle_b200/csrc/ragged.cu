@@ -56,25 +56,31 @@ __global__ __launch_bounds__(kSlots) void raggedLeavesKernel(RaggedLeavesArgs a)
     const int64_t first = (mine + kLeaf - 1) / kLeaf;  // the first leaf starting at or after ``mine``
     const int64_t leaves = end > first * kLeaf ? (end - first * kLeaf + kLeaf - 1) / kLeaf : 0;
     if (blockIdx.x == 0 && threadIdx.x == 0)
-        *a.leafCount = uint32_t(leaves < a.cap ? leaves : a.cap);
+        *a.leafCount = uint32_t(leaves);  // above cap: the fold reports the overflow
     const int64_t k = blockIdx.x;
     if (k >= leaves || k >= a.cap)
         return;
     const int64_t start = (first + k) * kLeaf;  // global position of the leaf's first survivor
     const int64_t cnt = total - start < kLeaf ? total - start : kLeaf;
-    const double* kept = a.kept;
     const double* heads = a.heads;
     const int32_t rank = a.rank, world = a.world;
-    auto at = [&](int64_t i) -> double {
-        const int64_t g = start + i;
-        if (g < end)
-            return kept[g - mine];
-        int q = rank + 1;  // a later rank's head: g - sOff[q] < kHead for the rank holding g
-        while (q + 1 < world && g >= sOff[q + 1])
-            ++q;
-        return heads[int64_t(q) * kHead + (g - sOff[q])];
-    };
-    const CompP<double> p = leafPartialAt<CompP<double>, double>(at, cnt, s);
+    CompP<double> p;
+    if (start + cnt <= end) {  // the whole leaf is this rank's (every leaf but the last)
+        const double* mineLeaf = a.kept + (start - mine);
+        p = leafPartialAt<CompP<double>, double>([&](int64_t i) { return mineLeaf[i]; }, cnt, s);
+    } else {
+        const double* kept = a.kept;
+        auto at = [&](int64_t i) -> double {
+            const int64_t g = start + i;
+            if (g < end)
+                return kept[g - mine];
+            int q = rank + 1;  // a later rank's head: g - sOff[q] < kHead for the rank holding g
+            while (q + 1 < world && g >= sOff[q + 1])
+                ++q;
+            return heads[int64_t(q) * kHead + (g - sOff[q])];
+        };
+        p = leafPartialAt<CompP<double>, double>(at, cnt, s);
+    }
     if (threadIdx.x == 0) {
         a.partials[2 * k] = p.h;
         a.partials[2 * k + 1] = p.c;
@@ -98,7 +104,18 @@ __global__ __launch_bounds__(kSlots) void raggedFoldKernel(const double* __restr
         }
         sFirst[world] = o;
     }
+    __shared__ int sOver;
+    if (threadIdx.x == 0) {
+        sOver = 0;
+        for (int q = 0; q < world; ++q)
+            sOver |= int64_t(leafCounts[q]) > cap ? 1 : 0;
+    }
     __syncthreads();
+    if (sOver != 0) {  // some rank formed more leaves than ``cap`` holds: no valid sum
+        if (threadIdx.x == 0)
+            out[0] = out[1] = out[2] = __longlong_as_double(0x7ff8000000000000ll);
+        return;
+    }
     int64_t count = sFirst[world];
     if (count == 0) {
         if (threadIdx.x == 0)

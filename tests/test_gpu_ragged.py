@@ -68,3 +68,28 @@ def test_emulated_ranks_equal_the_whole(eb, orc, n, p, bounds):
     whole = eb.CompactSum(torch.from_numpy(keep).cuda(), torch.from_numpy(vals).cuda())().cpu().numpy()
     want = orc.reduce(vals[keep])[0] if keep.any() else np.float64(0.0)  # the oracle refuses an empty sum
     assert np.float64(got[2]).tobytes() == np.float64(want).tobytes() == whole[-1].tobytes()
+
+
+def test_leaf_capacity_overflow_is_reported(eb):
+    """A rank handed too small a ``cap`` for its leaves: every rank's fold gives NaN
+    instead of a sum missing leaves."""
+    from eagle_b200 import _abi
+
+    lib = _abi.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    n = 5 * LEAF
+    cs = eb.CompactSum(torch.ones(n, dtype=torch.bool, device="cuda"),
+                       torch.ones(n, dtype=torch.float64, device="cuda"))
+    cs.gather()
+    heads = cs.kept[:LEAF - 1].contiguous()
+    partials = torch.zeros(2 * 2, dtype=torch.float64, device="cuda")
+    leaf_counts = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _abi.check(lib.eagle_backend_x_b200_ragged_leaves(cs.kept.data_ptr(), cs.count.data_ptr(), heads.data_ptr(),
+                                                      0, 1, partials.data_ptr(), 2, leaf_counts.data_ptr(), s))
+    work = torch.zeros(8, dtype=torch.float64, device="cuda")
+    out = torch.zeros(3, dtype=torch.float64, device="cuda")
+    _abi.check(lib.eagle_backend_x_b200_ragged_fold(partials.data_ptr(), leaf_counts.data_ptr(), 1, 2,
+                                                    work.data_ptr(), out.data_ptr(), s))
+    torch.cuda.synchronize()
+    assert int(leaf_counts.item()) == 5
+    assert torch.isnan(out).all()
