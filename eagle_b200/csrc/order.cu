@@ -63,15 +63,12 @@ __device__ __forceinline__ int64_t claimOf(const StopKeyArgs& a, int64_t r, int6
     return (pos / kWeave) * (kWeave * a.woven) + r * kWeave + pos % kWeave;
 }
 
-/** Sample i's bucket: its estimated steps this run, ceil((t_end - t) / dt) kept in
- *  [1, budget] (the budget for a non-finite estimate or dt not above zero), over
- *  ``width``, counted from the longest (bucket 0) down; kBuckets for a terminated
- *  sample. */
-__device__ __forceinline__ uint32_t stopKey(const StopKeyArgs& a, int64_t i)
+/** Sample i's bucket from its mask byte, t_end and t: its estimated steps this run,
+ *  ceil((t_end - t) / dt) kept in [1, budget] (the budget for a non-finite estimate
+ *  or dt not above zero), over ``width``, counted from the longest (bucket 0) down;
+ *  kBuckets for a terminated sample. */
+__device__ __forceinline__ uint32_t stopKeyOf(const StopKeyArgs& a, uint8_t done, double te, double t0)
 {
-    const uint8_t done = a.term[i];  // the three loads go out together
-    const double te = a.tEnd != nullptr ? a.tEnd[i] : a.tEndU;
-    const double t0 = a.t[i];
     if (done != 0)
         return kBuckets;
     const double d = (te - t0) * a.perDt;  // an estimate: only the order depends on it
@@ -103,12 +100,21 @@ __global__ __launch_bounds__(kThreads) void stopOrderKernel(StopKeyArgs a)
     const int64_t i0 = int64_t(blockIdx.x) * a.run;
     const int live = int(a.n - i0 < a.run ? a.n - i0 : a.run);
     for (int j0 = 0; j0 < live; j0 += kThreads * kUnroll) {
+        // coalesced; every load of the round issued before any key is formed
+        uint8_t done[kUnroll];
+        double te[kUnroll], t0[kUnroll];
+#pragma unroll
+        for (int r = 0; r < kUnroll; ++r) {
+            const int j = j0 + r * kThreads + t;
+            const int64_t i = i0 + (j < live ? j : 0);
+            done[r] = a.term[i];
+            te[r] = a.tEnd != nullptr ? a.tEnd[i] : a.tEndU;
+            t0[r] = a.t[i];
+        }
         uint32_t k[kUnroll];
 #pragma unroll
-        for (int r = 0; r < kUnroll; ++r) {  // coalesced; every round's loads issued together
-            const int j = j0 + r * kThreads + t;
-            k[r] = j < live ? stopKey(a, i0 + j) : 0u;
-        }
+        for (int r = 0; r < kUnroll; ++r)
+            k[r] = stopKeyOf(a, done[r], te[r], t0[r]);
 #pragma unroll
         for (int r = 0; r < kUnroll; ++r) {
             const int j = j0 + r * kThreads + t;
