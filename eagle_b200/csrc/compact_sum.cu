@@ -73,17 +73,33 @@ __device__ __forceinline__ int selectBit(uint32_t x, uint32_t r)
     return pos;
 }
 
+/** One rank's share of the leaves of the concatenation of every rank's survivors
+ *  (compact-then-sum across ranks), formed on the device from the gathered counts.
+ *  This rank's survivors are ranks [offset, offset + count) of the concatenation;
+ *  counting ``shift`` = offset mod 4096 phantom survivors in front of them makes the
+ *  concatenation's leaves this rank's leaves of shifted ranks (leaf L: shifted ranks
+ *  [4096 L, 4096 L + 4096), local ranks from 4096 L - shift). Leaves [first, full)
+ *  start and end here; with ``straddle`` the leaf starting at local rank
+ *  ``tailStart`` runs on into the later ranks (or to the end of all survivors). */
+struct RaggedPlan {
+    int64_t offset, total, count, shift;
+    int64_t first, full;
+    int64_t tailStart, tailLen, headLen;
+    int32_t straddle, pad;
+};
+
 /** One warp per tile: every leaf whose first rank (a multiple of 4096) falls among
  *  the tile's kept samples gets that sample's index in ``leafStart``. Lane l holds
  *  the tile's words [16 l, 16 l + 16). */
 __global__ __launch_bounds__(kThreads, 4) void leafStartKernel(const uint32_t* __restrict__ bitmap,
     const uint32_t* __restrict__ tileCount, const uint32_t* __restrict__ tileOff, int64_t tiles,
-    int32_t* __restrict__ leafStart)
+    int32_t* __restrict__ leafStart, const RaggedPlan* __restrict__ plan)
 {
     const int lane = int(threadIdx.x & 31);
     const int64_t warps = int64_t(gridDim.x) * (kThreads / 32);
+    const uint64_t shift = plan != nullptr ? uint64_t(plan->shift) : 0u;  // ranks counted as shifted ones
     for (int64_t tile = int64_t(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5); tile < tiles; tile += warps) {
-        const uint64_t o = tileOff[tile], c = tileCount[tile];
+        const uint64_t o = tileOff[tile] + shift, c = tileCount[tile];
         const uint64_t b0 = (o + uint64_t(kLeaf) - 1) / uint64_t(kLeaf) * uint64_t(kLeaf);
         if (c == 0 || b0 >= o + c)
             continue;  // warp-uniform
@@ -145,7 +161,26 @@ struct LeafArgs {
     uint32_t* err;         // zero on entry
     double* out;
     int pairOut;
+    const RaggedPlan* plan;  // null: one device's sum; else this rank's leaves of the concatenation
+    double* partOut;         // with a plan: (hi, comp) of leaves [first, full), from index 0
 };
+
+/** The leaves a pass walks: shifted survivor count, all leaves, and the range to sum. */
+struct LeafSpan {
+    int64_t rows, leaves, first, end, shift;
+};
+
+__device__ __forceinline__ LeafSpan leafSpan(const LeafArgs& a)
+{
+    LeafSpan sp;
+    const int64_t c = int64_t(*a.count) > a.n ? 0 : int64_t(*a.count);
+    sp.shift = a.plan != nullptr ? a.plan->shift : 0;
+    sp.rows = c + sp.shift;
+    sp.leaves = (sp.rows + kLeaf - 1) / kLeaf;
+    sp.first = a.plan != nullptr ? a.plan->first : 0;
+    sp.end = a.plan != nullptr ? a.plan->full : sp.leaves;
+    return sp;
+}
 
 constexpr int kDenseThreads = 128;          // four warps, one leaf each
 constexpr int kDenseWarps = kDenseThreads / 32;
@@ -267,6 +302,13 @@ __device__ __forceinline__ P warpLevels(const P* in, int m)
 __device__ __forceinline__ void finishLeaf(const LeafArgs& a, int64_t l, int64_t leaves, const P& q)
 {
     const int lane = int(threadIdx.x & 31);
+    if (a.plan != nullptr) {  // one rank's leaves: stored for the exchange, joined elsewhere
+        if (lane == 0) {
+            a.partOut[2 * (l - a.plan->first)] = q.h;
+            a.partOut[2 * (l - a.plan->first) + 1] = q.c;
+        }
+        return;
+    }
     const int64_t chunks = (leaves + kChunk - 1) / kChunk;
     const int64_t ch = l / kChunk;
     const int inChunk = int(leaves - ch * kChunk < kChunk ? leaves - ch * kChunk : kChunk);
@@ -465,9 +507,9 @@ __global__ __launch_bounds__(kDenseThreads, 6) void keptDenseKernel(LeafArgs a)
     __shared__ __align__(16) double rings[kDenseWarps][kRing];
     const int lane = int(threadIdx.x & 31);
     double* ring = rings[threadIdx.x >> 5];
-    const int64_t rows = int64_t(*a.count) > a.n ? 0 : int64_t(*a.count);
-    const int64_t leaves = (rows + kLeaf - 1) / kLeaf;
-    if (leaves == 0) {
+    const LeafSpan sp = leafSpan(a);
+    const int64_t rows = sp.rows, leaves = sp.leaves;
+    if (leaves == 0 && a.plan == nullptr) {
         if (blockIdx.x == 0 && threadIdx.x == 0) {
             a.out[0] = 0.0;
             if (a.pairOut)
@@ -481,10 +523,10 @@ __global__ __launch_bounds__(kDenseThreads, 6) void keptDenseKernel(LeafArgs a)
             l = atomicAdd(a.leafNext, 1u);
         return int64_t(__shfl_sync(kFull, l, 0));
     };
-    int64_t next = claim();
-    while (next < leaves) {
+    int64_t next = sp.first + claim();
+    while (next < sp.end) {
         const int64_t l = next;
-        next = claim();  // the next claim's round trip overlaps this leaf
+        next = sp.first + claim();  // the next claim's round trip overlaps this leaf
         int64_t s0, s1;
         leafRange(a, l, leaves, s0, s1);
         const int cnt = int(rows - l * kLeaf < kLeaf ? rows - l * kLeaf : kLeaf);
@@ -526,15 +568,15 @@ __global__ __launch_bounds__(kThreads, 3) void keptSparseKernel(LeafArgs a)
     __shared__ uint32_t scan[33], sHits[kThreads / 32];
     __shared__ int64_t sClaim[2][3];  // a claimed leaf and its sample range, two deep
     const int t = int(threadIdx.x);
-    const int64_t rows = int64_t(*a.count) > a.n ? 0 : int64_t(*a.count);
-    const int64_t leaves = (rows + kLeaf - 1) / kLeaf;
-    if (leaves == 0)
+    const LeafSpan sp = leafSpan(a);
+    const int64_t rows = sp.rows, leaves = sp.leaves;
+    if (sp.end <= sp.first)
         return;
     const uint32_t listed = *a.sparseCount;
     auto claimInto = [&](int b) {  // one thread: the next listed leaf, or -1
         const uint32_t i = atomicAdd(a.sparseNext, 1u);
         int64_t l = i < listed ? int64_t(a.sparseList[i]) : -1;
-        l = l >= leaves ? -1 : l;
+        l = l >= sp.end ? -1 : l;
         int64_t s0 = 0, s1 = 1;
         if (l >= 0)
             leafRange(a, l, leaves, s0, s1);
@@ -562,7 +604,7 @@ __global__ __launch_bounds__(kThreads, 3) void keptSparseKernel(LeafArgs a)
             // so each warp stages its tiles' survivors ranked inside the leaf with no wait on
             // the others (lane l holds the tile's words [16 l, 16 l + 16))
             const int warp = t >> 5, lane = t & 31;
-            const int64_t rank0 = l * int64_t(kLeaf);
+            const int64_t rank0 = l * int64_t(kLeaf) - sp.shift;  // the leaf's first survivor's local rank
             uint32_t hits = 0;
             for (int64_t tile = s0 / kTile + warp; tile < tileEnd; tile += kThreads / 32) {
                 const uint4* src = reinterpret_cast<const uint4*>(a.bitmap + tile * kTileWords) + lane * 4;
@@ -670,7 +712,7 @@ __global__ void compactSumEmptyKernel(uint32_t* count, double* out, int pairOut)
 struct SumLayout {
     int64_t maxLeaves = 0, maxChunks = 0;
     tiles::TileLayout t;
-    size_t zeroed = 0, leafStart = 0, sparseList = 0, leafPart = 0, chunkPart = 0, total = 0;
+    size_t zeroed = 0, leafStart = 0, sparseList = 0, leafPart = 0, chunkPart = 0, plan = 0, tail = 0, total = 0;
 };
 
 size_t up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -709,8 +751,143 @@ SumLayout sumLayout(int64_t n)
     L.sparseList = up(L.leafStart + size_t(L.maxLeaves + 1) * sizeof(int32_t), 256);
     L.leafPart = up(L.sparseList + size_t(L.maxLeaves + 1) * sizeof(int32_t), 256);
     L.chunkPart = up(L.leafPart + size_t(L.maxLeaves > 0 ? L.maxLeaves : 1) * sizeof(P), 256);
-    L.total = up(L.chunkPart + size_t(L.maxChunks > 0 ? L.maxChunks : 1) * sizeof(P), 256);
+    L.plan = up(L.chunkPart + size_t(L.maxChunks > 0 ? L.maxChunks : 1) * sizeof(P), 256);
+    L.tail = up(L.plan + sizeof(RaggedPlan), 256);
+    L.total = up(L.tail + size_t(kLeaf) * sizeof(double), 256);
     return L;
+}
+
+// ------------------------------------------------- the same leaves across ranks
+
+constexpr int kMaxRanks = 256;
+constexpr int64_t kHead = kLeaf - 1;  // survivors a rank shares with the earlier ranks
+
+/** One thread: this rank's RaggedPlan from every rank's count. */
+__global__ void raggedPlanKernel(const uint32_t* __restrict__ counts, int32_t rank, int32_t world,
+    const uint32_t* __restrict__ count, int64_t n, RaggedPlan* plan)
+{
+    int64_t o = 0, total = 0;
+    for (int q = 0; q < world; ++q) {
+        if (q < rank)
+            o += int64_t(counts[q]);
+        total += int64_t(counts[q]);
+    }
+    const int64_t c = int64_t(*count) > n ? 0 : int64_t(*count);  // this rank's own, as its passes read it
+    RaggedPlan r{};
+    r.offset = o;
+    r.total = total;
+    r.count = c;
+    r.shift = o % kLeaf;
+    r.first = r.shift > 0 ? 1 : 0;
+    r.full = (c + r.shift) / kLeaf;  // leaf L ends by local rank 4096 (L + 1) - shift <= c
+    if (r.full < r.first)
+        r.full = r.first;
+    const int64_t s0 = r.full * kLeaf - r.shift;  // where the next leaf would start
+    r.straddle = (s0 >= 0 && s0 < c) ? 1 : 0;
+    r.tailStart = r.straddle ? s0 : c;
+    r.tailLen = r.straddle ? c - s0 : 0;
+    r.headLen = c < kHead ? c : kHead;
+    *plan = r;
+}
+
+/** The values of this rank's survivors of local ranks [r0, r1) (at most 4096) into
+ *  ``out[0, r1 - r0)``: CTA 0 the head (ranks [0, headLen)), CTA 1 the straddling
+ *  leaf's part here (ranks [tailStart, count)). The first tile holding rank r0 is
+ *  found by a binary search over the scanned tile offsets; each warp then takes one
+ *  16384-sample tile at a time and ranks its survivors from the tile's offset. */
+__global__ __launch_bounds__(kThreads) void rankSelectKernel(const uint32_t* __restrict__ bitmap,
+    const uint32_t* __restrict__ tileOff, int64_t tiles, const double* __restrict__ values,
+    const RaggedPlan* __restrict__ plan, double* __restrict__ head, double* __restrict__ tail)
+{
+    __shared__ int64_t sFirst;
+    const int64_t r0 = blockIdx.x == 0 ? 0 : plan->tailStart;
+    const int64_t r1 = blockIdx.x == 0 ? plan->headLen : plan->tailStart + plan->tailLen;
+    double* out = blockIdx.x == 0 ? head : tail;
+    if (r1 <= r0)
+        return;
+    if (threadIdx.x == 0) {  // the last tile whose first survivor's rank is <= r0
+        int64_t lo = 0, hi = tiles - 1;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi + 1) / 2;
+            if (int64_t(tileOff[mid]) <= r0)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        sFirst = lo;
+    }
+    __syncthreads();
+    const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
+    for (int64_t tile = sFirst + warp; tile < tiles && int64_t(tileOff[tile]) < r1; tile += kThreads / 32) {
+        const uint4* src = reinterpret_cast<const uint4*>(bitmap + tile * kTileWords) + lane * 4;
+        uint32_t w[16];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 x = src[k];
+            w[4 * k] = x.x;
+            w[4 * k + 1] = x.y;
+            w[4 * k + 2] = x.z;
+            w[4 * k + 3] = x.w;
+        }
+        uint32_t mine = 0;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+            mine += uint32_t(__popc(w[k]));
+        int64_t r = int64_t(tileOff[tile]) + int64_t(warpInclusiveSum(mine) - mine);  // the lane's first rank
+        if (r >= r1 || r + int64_t(mine) <= r0)
+            continue;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int64_t sample0 = (tile * kTileWords + lane * 16 + k) * 32;
+            for (uint32_t x = w[k]; x != 0; x &= x - 1u, ++r)
+                if (r >= r0 && r < r1)
+                    out[r - r0] = values[sample0 + (__ffs(int(x)) - 1)];
+        }
+    }
+}
+
+/** One CTA: the leaf that starts here and runs into the later ranks, from this
+ *  rank's part (``tail``) and the later ranks' gathered heads, at partials index
+ *  full - first; then this rank's leaf count (all of 0xffffffff when a pass reported
+ *  an error, so that the fold gives NaN). */
+__global__ __launch_bounds__(kSlots) void straddleKernel(const RaggedPlan* __restrict__ plan,
+    const uint32_t* __restrict__ counts, const double* __restrict__ heads, int32_t rank, int32_t world,
+    const double* __restrict__ tail, const uint32_t* __restrict__ err, double* __restrict__ partials,
+    uint32_t* __restrict__ leafCount)
+{
+    __shared__ int64_t sOff[kMaxRanks + 1];
+    __shared__ P s[kSlots];
+    if (threadIdx.x == 0) {
+        int64_t o = 0;
+        for (int q = 0; q < world; ++q) {
+            sOff[q] = o;
+            o += int64_t(counts[q]);
+        }
+        sOff[world] = o;
+    }
+    __syncthreads();
+    const RaggedPlan r = *plan;
+    const int64_t own = r.full - r.first;
+    if (r.straddle) {
+        const int64_t start = r.offset + r.tailStart;  // the leaf's first survivor in the concatenation
+        const int64_t cnt = r.total - start < kLeaf ? r.total - start : kLeaf;
+        auto at = [&](int64_t i) -> double {
+            if (i < r.tailLen)
+                return tail[i];
+            const int64_t g = start + i;
+            int q = rank + 1;  // the later rank holding g: g - sOff[q] < kHead
+            while (q + 1 < world && g >= sOff[q + 1])
+                ++q;
+            return heads[int64_t(q) * kHead + (g - sOff[q])];
+        };
+        const P q = leafPartialAt<P, double>(at, cnt, s);
+        if (threadIdx.x == 0) {
+            partials[2 * own] = q.h;
+            partials[2 * own + 1] = q.c;
+        }
+    }
+    if (threadIdx.x == 0)
+        *leafCount = *err != 0u ? 0xffffffffu : uint32_t(own + r.straddle);
 }
 
 }  // namespace
@@ -792,11 +969,152 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
         const int64_t startCtas = (L.t.tiles + warpsPerCta - 1) / warpsPerCta;
         const int64_t startCap = int64_t(smCount()) * 8;
         leafStartKernel<<<unsigned(startCtas < startCap ? startCtas : startCap), kThreads, 0, s>>>(bitmap, tileCount,
-            tileOff, L.t.tiles, leafStart);
+            tileOff, L.t.tiles, leafStart, nullptr);
         launchCheck(who);
         keptDenseKernel<<<unsigned(passGrid(0)), kDenseThreads, 0, s>>>(la);
         launchCheck(who);
         keptSparseKernel<<<unsigned(passGrid(1)), kThreads, 0, s>>>(la);
+        launchCheck(who);
+    });
+}
+
+// ---------------------------------------------- compact-then-sum across ranks
+//
+// The one-device call above, cut where the ranks must exchange: _count runs the
+// front end (keep bitmap, tile counts and offsets, this rank's count); the caller
+// all-gathers the counts; _leaves forms this rank's plan from them on the device,
+// places the leaf starts in the concatenation's leaves, sums every leaf that starts
+// and ends here with the same dense and sparse passes (their partials written out,
+// not joined), and copies out this rank's first 4095 survivors and the part of the
+// leaf that straddles into the next ranks; the caller all-gathers the heads;
+// _straddle sums that leaf from its part here and the later ranks' heads. The leaf
+// partials and counts then go through eagle_backend_x_b200_ragged_fold. The kept
+// values are never written out, as in the one-device call.
+
+namespace eb {
+namespace {
+
+/** The split entries' common checks (the desc is compact_sum's, with its scratch). */
+SumLayout checkSplit(const eagle_backend_compact_desc& d, const char* who)
+{
+    if (d.n < 0)
+        invalid(std::string(who) + ": n must be >= 0");
+    if (d.n > INT64_C(2147483647))
+        unsupported(std::string(who) + ": at most 2^31-1 samples, got n = " + std::to_string(d.n));
+    if (d.index_map != 0 || d.live32 != 0)
+        unsupported(std::string(who) + ": writes no index map and offers no trigger");
+    if (d.scratch == 0 || d.count == 0 || (d.n > 0 && d.mask == 0))
+        invalid(std::string(who) + ": mask, count and scratch (queried from compact_sum) must be device addresses");
+    if ((d.scratch & 255u) != 0)
+        invalid(std::string(who) + ": scratch must be 256-byte aligned");
+    return sumLayout(d.n);
+}
+
+}  // namespace
+}  // namespace eb
+
+EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_count(struct eagle_backend_compact_desc* desc)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_compact_sum_count";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        const SumLayout L = checkSplit(d, who);
+        DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
+        const cudaStream_t s = seamStream(d.stream);
+        char* base = reinterpret_cast<char*>(d.scratch);
+        cudaCheck(cudaMemsetAsync(base, 0, L.zeroed, s), "cudaMemsetAsync");
+        if (d.n == 0) {
+            cudaCheck(cudaMemsetAsync(reinterpret_cast<void*>(d.count), 0, sizeof(uint32_t), s), "cudaMemsetAsync");
+            return;
+        }
+        tiles::enqueueTiles(reinterpret_cast<const uint8_t*>(d.mask), d.n,
+            (d.flags & EAGLE_BACKEND_COMPACT_MASK_IS_DROP) != 0, base, L.t, reinterpret_cast<uint32_t*>(d.count),
+            tiles::ScanTrigger{}, s, who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_leaves(struct eagle_backend_compact_desc* desc,
+    uint64_t values, uint64_t counts, int32_t rank, int32_t world, uint64_t head, uint64_t partials, int64_t cap)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_compact_sum_leaves";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        const SumLayout L = checkSplit(d, who);
+        if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+            invalid(std::string(who) + ": need 0 <= rank < world <= 256");
+        if (counts == 0 || head == 0 || partials == 0 || (d.n > 0 && values == 0))
+            invalid(std::string(who) + ": values, counts, head and partials must be device addresses");
+        if ((values & 7u) != 0)
+            invalid(std::string(who) + ": values must be an 8-byte aligned float64 array");
+        if (cap < L.maxLeaves + 1)
+            invalid(std::string(who) + ": cap must be at least ceil(n / 4096) + 1 leaves");
+        DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
+        const cudaStream_t s = seamStream(d.stream);
+        char* base = reinterpret_cast<char*>(d.scratch);
+        auto* plan = reinterpret_cast<RaggedPlan*>(base + L.plan);
+        raggedPlanKernel<<<1, 1, 0, s>>>(reinterpret_cast<const uint32_t*>(counts), rank, world,
+            reinterpret_cast<const uint32_t*>(d.count), d.n, plan);
+        launchCheck(who);
+        if (d.n == 0)
+            return;
+        uint32_t* words = reinterpret_cast<uint32_t*>(base);
+        const uint32_t* tileCount = reinterpret_cast<const uint32_t*>(base + L.t.count);
+        const uint32_t* tileOff = reinterpret_cast<const uint32_t*>(base + L.t.off);
+        const uint32_t* bitmap = reinterpret_cast<const uint32_t*>(base + L.t.bitmap);
+        int32_t* leafStart = reinterpret_cast<int32_t*>(base + L.leafStart);
+        LeafArgs la{};
+        la.bitmap = bitmap;
+        la.tileOff = tileOff;
+        la.leafStart = leafStart;
+        la.count = reinterpret_cast<const uint32_t*>(d.count);
+        la.values = reinterpret_cast<const double*>(values);
+        la.n = d.n;
+        la.leafPart = reinterpret_cast<P*>(base + L.leafPart);
+        la.chunkPart = reinterpret_cast<P*>(base + L.chunkPart);
+        la.leafNext = words;
+        la.topDone = words + 1;
+        la.err = words + 2;
+        la.sparseCount = words + 3;
+        la.sparseNext = words + 4;
+        la.chunkDone = words + 8;
+        la.sparseList = reinterpret_cast<int32_t*>(base + L.sparseList);
+        la.out = nullptr;
+        la.plan = plan;
+        la.partOut = reinterpret_cast<double*>(partials);
+        const int64_t warpsPerCta = kThreads / 32;
+        const int64_t startCtas = (L.t.tiles + warpsPerCta - 1) / warpsPerCta;
+        const int64_t startCap = int64_t(smCount()) * 8;
+        leafStartKernel<<<unsigned(startCtas < startCap ? startCtas : startCap), kThreads, 0, s>>>(bitmap, tileCount,
+            tileOff, L.t.tiles, leafStart, plan);
+        launchCheck(who);
+        keptDenseKernel<<<unsigned(passGrid(0)), kDenseThreads, 0, s>>>(la);
+        launchCheck(who);
+        keptSparseKernel<<<unsigned(passGrid(1)), kThreads, 0, s>>>(la);
+        launchCheck(who);
+        rankSelectKernel<<<2, kThreads, 0, s>>>(bitmap, tileOff, L.t.tiles, reinterpret_cast<const double*>(values),
+            plan, reinterpret_cast<double*>(head), reinterpret_cast<double*>(base + L.tail));
+        launchCheck(who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_straddle(struct eagle_backend_compact_desc* desc,
+    uint64_t counts, uint64_t heads, int32_t rank, int32_t world, uint64_t partials, uint64_t leaf_count)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_compact_sum_straddle";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        const SumLayout L = checkSplit(d, who);
+        if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+            invalid(std::string(who) + ": need 0 <= rank < world <= 256");
+        if (counts == 0 || heads == 0 || partials == 0 || leaf_count == 0)
+            invalid(std::string(who) + ": counts, heads, partials and leaf_count must be device addresses");
+        DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
+        const cudaStream_t s = seamStream(d.stream);
+        char* base = reinterpret_cast<char*>(d.scratch);
+        straddleKernel<<<1, kSlots, 0, s>>>(reinterpret_cast<const RaggedPlan*>(base + L.plan),
+            reinterpret_cast<const uint32_t*>(counts), reinterpret_cast<const double*>(heads), rank, world,
+            reinterpret_cast<const double*>(base + L.tail), reinterpret_cast<const uint32_t*>(base) + 2,
+            reinterpret_cast<double*>(partials), reinterpret_cast<uint32_t*>(leaf_count));
         launchCheck(who);
     });
 }

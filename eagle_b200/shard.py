@@ -235,14 +235,16 @@ def compact_sum_sharded(mask, values, *, drop: bool = False, group=None):
 
 class ShardedCompactSum:
     """The canonical sum of every rank's survivors as ONE concatenation in rank order,
-    prepared once per shard and run with no host round trip: each call gathers this
-    rank's survivors on its device, all-gathers the survivor counts and every rank's
-    first ``LEAF - 1`` survivors, forms the partial of each leaf that starts in this
-    rank's part (``eagle_backend_x_b200_ragged_leaves``, which reads the gathered counts
-    on the device), all-gathers the leaf partials and folds them in rank order
-    (``eagle_backend_x_b200_ragged_fold``). Every collective moves a fixed number of
-    bytes, so nothing waits on the host. Returns ``(hi, comp, value)`` on every rank:
-    the bits of the one-device compact-then-sum of the concatenated shards."""
+    prepared once per shard and run with no host round trip and without writing the
+    survivors out: each call runs the fused compact-then-sum's front end on this
+    rank's shard (``eagle_backend_x_b200_compact_sum_count``), all-gathers the
+    survivor counts, sums every leaf of the concatenation that starts and ends here
+    straight from the values (``_compact_sum_leaves``, planned on the device from the
+    gathered counts), all-gathers every rank's first ``LEAF - 1`` survivors, sums the
+    leaf that straddles into the later ranks (``_compact_sum_straddle``), all-gathers
+    the leaf partials and folds them in rank order (``eagle_backend_x_b200_ragged_fold``).
+    Every collective moves a fixed number of bytes. Returns ``(hi, comp, value)`` on
+    every rank: the bits of the one-device compact-then-sum of the concatenated shards."""
 
     def __init__(self, mask, values, *, drop: bool = False, group=None):
         import torch
@@ -251,6 +253,7 @@ class ShardedCompactSum:
         from ._api import CompactSum
 
         self.cs = CompactSum(mask, values, drop=drop)
+        self.values = values
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -258,6 +261,7 @@ class ShardedCompactSum:
         n = mask.numel()
         self.cap = (n + LEAF - 1) // LEAF + 1
         self.counts = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        self.head = torch.zeros(LEAF - 1, dtype=torch.float64, device=dev)
         self.heads = torch.zeros(self.world * (LEAF - 1), dtype=torch.float64, device=dev)
         self.partials = torch.zeros(2 * self.cap, dtype=torch.float64, device=dev)
         self.leaf_count = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -267,17 +271,24 @@ class ShardedCompactSum:
         self.out = torch.zeros(3, dtype=torch.float64, device=dev)
 
     def __call__(self, stream=None):
+        import ctypes
+
         import torch
         import torch.distributed as dist
 
         s = (stream or torch.cuda.current_stream()).cuda_stream
         lib = _abi.lib()
-        self.cs.gather(stream)
+        d = self.cs.sdesc
+        d.stream = s
+        _abi.check(lib.eagle_backend_x_b200_compact_sum_count(ctypes.byref(d)))
         dist.all_gather_into_tensor(self.counts, self.cs.count, group=self.group)
-        dist.all_gather_into_tensor(self.heads, self.cs.kept[:LEAF - 1], group=self.group)
-        _abi.check(lib.eagle_backend_x_b200_ragged_leaves(
-            self.cs.kept.data_ptr(), self.counts.data_ptr(), self.heads.data_ptr(), self.rank, self.world,
-            self.partials.data_ptr(), self.cap, self.leaf_count.data_ptr(), s))
+        _abi.check(lib.eagle_backend_x_b200_compact_sum_leaves(
+            ctypes.byref(d), self.values.data_ptr(), self.counts.data_ptr(), self.rank, self.world,
+            self.head.data_ptr(), self.partials.data_ptr(), self.cap))
+        dist.all_gather_into_tensor(self.heads, self.head, group=self.group)
+        _abi.check(lib.eagle_backend_x_b200_compact_sum_straddle(
+            ctypes.byref(d), self.counts.data_ptr(), self.heads.data_ptr(), self.rank, self.world,
+            self.partials.data_ptr(), self.leaf_count.data_ptr()))
         dist.all_gather_into_tensor(self.all_partials, self.partials, group=self.group)
         dist.all_gather_into_tensor(self.all_leaf_counts, self.leaf_count, group=self.group)
         _abi.check(lib.eagle_backend_x_b200_ragged_fold(

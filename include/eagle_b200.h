@@ -631,6 +631,25 @@ eagle_backend_status eagle_backend_x_b200_ragged_leaves(uint64_t kept, uint64_t 
 eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, uint64_t leaf_counts, int32_t world,
     int64_t cap, uint64_t work, uint64_t out, uint64_t stream);
 
+/* compact-then-sum across ranks without writing the survivors (this backend's addition,
+ * the fused form of ragged_leaves): x_b200_compact_sum cut where the ranks exchange.
+ * Same desc and scratch as x_b200_compact_sum (query there). _count: the keep bitmap,
+ * the tile counts and this rank's count (to ``count``); the caller all-gathers the
+ * counts into ``counts`` (uint32[world], rank order). _leaves (once per _count): from
+ * ``counts`` on the device, the (hi, comp) partial of every leaf of the concatenated
+ * survivors that starts and ends in this rank, into ``partials`` (2 * cap doubles, cap
+ * >= ceil(n / 4096) + 1) from index 0, and this rank's first min(count, 4095)
+ * survivors into ``head`` (4095 doubles); the caller all-gathers the heads into
+ * ``heads`` ([world][4095]). _straddle: the leaf that starts here and runs into the
+ * later ranks, from this rank's part and ``heads``, after those partials, and the
+ * rank's leaf count into ``leaf_count`` (uint32; 0xffffffff after a pass error). The
+ * partials and counts then go through eagle_backend_x_b200_ragged_fold. */
+eagle_backend_status eagle_backend_x_b200_compact_sum_count(struct eagle_backend_compact_desc* desc);
+eagle_backend_status eagle_backend_x_b200_compact_sum_leaves(struct eagle_backend_compact_desc* desc,
+    uint64_t values, uint64_t counts, int32_t rank, int32_t world, uint64_t head, uint64_t partials, int64_t cap);
+eagle_backend_status eagle_backend_x_b200_compact_sum_straddle(struct eagle_backend_compact_desc* desc,
+    uint64_t counts, uint64_t heads, int32_t rank, int32_t world, uint64_t partials, uint64_t leaf_count);
+
 /* eagle_backend_x_b200_compact_wait_check: compact_device with its first tile withheld,
  * to exercise the bounded look-back wait (this backend's addition; eagle's multi-level
  * scan has no wait to bound, eagle/cuda/Scan.h:32-141). No CTA takes tile 0, so every

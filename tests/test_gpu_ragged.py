@@ -1,10 +1,12 @@
 """The device-side ragged exchange of compact-then-sum on one GPU, with the ranks
 emulated: the batch is split into W shards, each shard compacted on its own, the
 counts and heads stacked as the all-gathers would stack them, then every rank's
-leaves (eagle_backend_x_b200_ragged_leaves) and the rank-order fold
-(eagle_backend_x_b200_ragged_fold) -- bit for bit the one-device compact-then-sum
-of the whole batch and the oracle's compaction + canonical sum, for even and uneven
-splits, empty shards, and shards so sparse that one leaf spans many ranks."""
+leaves and the rank-order fold (eagle_backend_x_b200_ragged_fold) -- bit for bit the
+one-device compact-then-sum of the whole batch and the oracle's compaction +
+canonical sum, for even and uneven splits, empty shards, and shards so sparse that
+one leaf spans many ranks. Both forms of the leaves: from the gathered survivors
+(eagle_backend_x_b200_ragged_leaves) and fused, straight from the values
+(eagle_backend_x_b200_compact_sum_count / _leaves / _straddle)."""
 
 import numpy as np
 import pytest
@@ -45,6 +47,44 @@ def _emulated(eb, vals, keep, bounds):
     return out.cpu().numpy()
 
 
+def _emulated_fused(eb, vals, keep, bounds):
+    import ctypes
+
+    from eagle_b200 import _abi
+
+    lib = _abi.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    world = len(bounds) - 1
+    sums, vdev = [], []
+    for r in range(world):
+        b, e = bounds[r], bounds[r + 1]
+        v = torch.from_numpy(vals[b:e].copy()).cuda()
+        cs = eb.CompactSum(torch.from_numpy(keep[b:e].copy()).cuda(), v)
+        cs.sdesc.stream = s
+        _abi.check(lib.eagle_backend_x_b200_compact_sum_count(ctypes.byref(cs.sdesc)))
+        sums.append(cs)
+        vdev.append(v)
+    cap = max((bounds[r + 1] - bounds[r] + LEAF - 1) // LEAF + 1 for r in range(world))
+    counts = torch.cat([cs.count for cs in sums]).contiguous()
+    heads = torch.zeros(world * (LEAF - 1), dtype=torch.float64, device="cuda")
+    gathered = torch.zeros(world * 2 * cap, dtype=torch.float64, device="cuda")
+    leaf_counts = torch.zeros(world, dtype=torch.int32, device="cuda")
+    for r, cs in enumerate(sums):
+        _abi.check(lib.eagle_backend_x_b200_compact_sum_leaves(
+            ctypes.byref(cs.sdesc), vdev[r].data_ptr(), counts.data_ptr(), r, world,
+            heads.data_ptr() + 8 * (LEAF - 1) * r, gathered.data_ptr() + 8 * 2 * cap * r, cap))
+    for r, cs in enumerate(sums):
+        _abi.check(lib.eagle_backend_x_b200_compact_sum_straddle(
+            ctypes.byref(cs.sdesc), counts.data_ptr(), heads.data_ptr(), r, world,
+            gathered.data_ptr() + 8 * 2 * cap * r, leaf_counts.data_ptr() + 4 * r))
+    work = torch.zeros(2 * ((world * cap + 511) // 512) + 2, dtype=torch.float64, device="cuda")
+    out = torch.zeros(3, dtype=torch.float64, device="cuda")
+    _abi.check(lib.eagle_backend_x_b200_ragged_fold(gathered.data_ptr(), leaf_counts.data_ptr(), world, cap,
+                                                    work.data_ptr(), out.data_ptr(), s))
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
 CASES = [
     (1 << 20, 0.37, (0, 1 << 19, 1 << 20)),                    # two even shards
     ((1 << 20) + 777, 0.61, None),                             # four uneven shards
@@ -52,6 +92,9 @@ CASES = [
     (200_000, 0.5, (0, 0, 100_000, 100_000, 200_000)),         # empty shards
     (100_000, 0.0, None),                                      # nothing kept
     (65_536, 1.0, (0, 1, 2, 3, 65_536)),                       # one-survivor shards
+    (1 << 22, 0.9, (0, 1 << 20, 2 << 20, 3 << 20, 4 << 20)),  # dense: leaves on the warp path
+    (1 << 22, 0.004, (0, 1 << 21, 1 << 22)),                   # sparse: leaves over many bitmap tiles
+    (3 * 4096 + 17, 1.0, (0, 4096, 8192, 3 * 4096 + 17)),      # shards of exactly one leaf, then a ragged one
 ]
 
 
@@ -65,9 +108,11 @@ def test_emulated_ranks_equal_the_whole(eb, orc, n, p, bounds):
         cuts = np.sort(g.integers(0, n, w - 1))
         bounds = (0, *[int(c) for c in cuts], n)
     got = _emulated(eb, vals, keep, list(bounds))
+    fused = _emulated_fused(eb, vals, keep, list(bounds))
     whole = eb.CompactSum(torch.from_numpy(keep).cuda(), torch.from_numpy(vals).cuda())().cpu().numpy()
     want = orc.reduce(vals[keep])[0] if keep.any() else np.float64(0.0)  # the oracle refuses an empty sum
     assert np.float64(got[2]).tobytes() == np.float64(want).tobytes() == whole[-1].tobytes()
+    assert np.float64(fused[2]).tobytes() == np.float64(want).tobytes()
 
 
 def test_leaf_capacity_overflow_is_reported(eb):
