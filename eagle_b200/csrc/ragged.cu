@@ -14,8 +14,9 @@
 //                       survivors come from this rank, and past its end from the
 //                       next ranks' gathered heads (a leaf that starts here ends
 //                       within 4095 survivors of this rank's end);
-//   raggedFoldKernel    one CTA: every rank's leaf partials, in rank order (the
-//                       order of the leaves), through the pairwise levels.
+//   raggedChunkKernel   every rank's leaf partials, in rank order (the order of the
+//   raggedTopKernel     leaves), through the pairwise levels: aligned chunks of 512
+//                       leaves by one CTA each, then the levels above by one CTA.
 //
 // Every rank runs the same fold over the same gathered partials, so every rank gets
 // the bits of the one-device compact-then-sum, at any rank count.
@@ -87,58 +88,82 @@ __global__ __launch_bounds__(kSlots) void raggedLeavesKernel(RaggedLeavesArgs a)
     }
 }
 
-/** The pairwise levels over every rank's leaf partials in rank order: rank q's
- *  ``leafCounts[q]`` partials sit at ``gathered + 2 cap q``. One CTA; ``work`` holds
- *  2 ceil(leaves / kChunk) doubles. out = {hi, comp, value}; no leaves: zeros. */
-__global__ __launch_bounds__(kSlots) void raggedFoldKernel(const double* __restrict__ gathered,
-    const uint32_t* __restrict__ leafCounts, int32_t world, int64_t cap, double* __restrict__ work,
-    double* __restrict__ out)
+/** Rank q's first leaf in the whole order (sFirst[q]; sFirst[world] = all leaves) and
+ *  whether some rank formed more leaves than ``cap`` holds, in shared memory. */
+__device__ __forceinline__ void leafOrigins(const uint32_t* __restrict__ leafCounts, int32_t world, int64_t cap,
+    int64_t* sFirst, int* sOver)
 {
-    __shared__ CompP<double> v[kChunk];
-    __shared__ int64_t sFirst[kMaxRanks + 1];  // sFirst[q] = rank q's first leaf in the whole order
     if (threadIdx.x == 0) {
         int64_t o = 0;
+        int over = 0;
         for (int q = 0; q < world; ++q) {
             sFirst[q] = o;
             o += int64_t(leafCounts[q]);
+            over |= int64_t(leafCounts[q]) > cap ? 1 : 0;
         }
         sFirst[world] = o;
-    }
-    __shared__ int sOver;
-    if (threadIdx.x == 0) {
-        sOver = 0;
-        for (int q = 0; q < world; ++q)
-            sOver |= int64_t(leafCounts[q]) > cap ? 1 : 0;
+        *sOver = over;
     }
     __syncthreads();
+}
+
+/** The first level of the fold: CTA c joins leaves [512 c, 512 c + 512) of the whole
+ *  order (rank q's ``leafCounts[q]`` partials sit at ``gathered + 2 cap q``) by the
+ *  pairwise levels into work[2 c, 2 c + 1]. */
+__global__ __launch_bounds__(kSlots) void raggedChunkKernel(const double* __restrict__ gathered,
+    const uint32_t* __restrict__ leafCounts, int32_t world, int64_t cap, double* __restrict__ work)
+{
+    __shared__ CompP<double> v[kChunk];
+    __shared__ int64_t sFirst[kMaxRanks + 1];
+    __shared__ int sOver;
+    leafOrigins(leafCounts, world, cap, sFirst, &sOver);
+    const int64_t count = sFirst[world];
+    const int64_t c = blockIdx.x;
+    if (sOver != 0 || c * kChunk >= count)
+        return;
+    const int cnt = int(count - c * kChunk < kChunk ? count - c * kChunk : kChunk);
+    for (int i = int(threadIdx.x); i < cnt; i += int(blockDim.x)) {
+        const int64_t j = c * kChunk + i;
+        int q = 0;  // the rank whose leaves hold j
+        while (q + 1 < world && j >= sFirst[q + 1])
+            ++q;
+        const double* src = gathered + 2 * (cap * q + (j - sFirst[q]));
+        v[i] = CompP<double>{src[0], src[1]};
+    }
+    __syncthreads();
+    levels(v, cnt);
+    if (threadIdx.x == 0) {
+        work[2 * c] = v[0].h;
+        work[2 * c + 1] = v[0].c;
+    }
+}
+
+/** The levels above the chunks, one CTA: out = {hi, comp, value}; no leaves: zeros;
+ *  some rank's leaves past ``cap``: NaN. */
+__global__ __launch_bounds__(kSlots) void raggedTopKernel(const uint32_t* __restrict__ leafCounts, int32_t world,
+    int64_t cap, double* __restrict__ work, double* __restrict__ out)
+{
+    __shared__ CompP<double> v[kChunk];
+    __shared__ int64_t sFirst[kMaxRanks + 1];
+    __shared__ int sOver;
+    leafOrigins(leafCounts, world, cap, sFirst, &sOver);
     if (sOver != 0) {  // some rank formed more leaves than ``cap`` holds: no valid sum
         if (threadIdx.x == 0)
             out[0] = out[1] = out[2] = __longlong_as_double(0x7ff8000000000000ll);
         return;
     }
-    int64_t count = sFirst[world];
-    if (count == 0) {
+    if (sFirst[world] == 0) {
         if (threadIdx.x == 0)
             out[0] = out[1] = out[2] = 0.0;
         return;
     }
-    bool firstLevel = true;
-    while (firstLevel || count > 1) {
+    int64_t count = (sFirst[world] + kChunk - 1) / kChunk;  // the chunk partials
+    while (count > 1) {
         const int64_t chunks = (count + kChunk - 1) / kChunk;
         for (int64_t c = 0; c < chunks; ++c) {
             const int cnt = int(count - c * kChunk < kChunk ? count - c * kChunk : kChunk);
-            for (int i = int(threadIdx.x); i < cnt; i += int(blockDim.x)) {
-                const int64_t j = c * kChunk + i;
-                if (firstLevel) {
-                    int q = 0;  // the rank whose leaves hold j
-                    while (q + 1 < world && j >= sFirst[q + 1])
-                        ++q;
-                    const double* src = gathered + 2 * (cap * q + (j - sFirst[q]));
-                    v[i] = CompP<double>{src[0], src[1]};
-                } else {
-                    v[i] = CompP<double>{work[2 * j], work[2 * j + 1]};
-                }
-            }
+            for (int i = int(threadIdx.x); i < cnt; i += int(blockDim.x))
+                v[i] = CompP<double>{work[2 * (c * kChunk + i)], work[2 * (c * kChunk + i) + 1]};
             __syncthreads();
             levels(v, cnt);
             if (threadIdx.x == 0) {
@@ -148,7 +173,6 @@ __global__ __launch_bounds__(kSlots) void raggedFoldKernel(const double* __restr
             __syncthreads();
         }
         count = chunks;
-        firstLevel = false;
     }
     if (threadIdx.x == 0) {
         const CompP<double> r{work[0], work[1]};
@@ -199,9 +223,13 @@ EB_API eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, 
             invalid(std::string(who) + ": cap must be >= 1");
         if (gathered == 0 || leaf_counts == 0 || work == 0 || out == 0)
             invalid(std::string(who) + ": gathered, leaf_counts, work and out must be device addresses");
-        raggedFoldKernel<<<1, kSlots, 0, seamStream(stream)>>>(reinterpret_cast<const double*>(gathered),
-            reinterpret_cast<const uint32_t*>(leaf_counts), world, cap, reinterpret_cast<double*>(work),
-            reinterpret_cast<double*>(out));
+        const cudaStream_t s = seamStream(stream);
+        const int64_t chunks = (int64_t(world) * cap + kChunk - 1) / kChunk;  // at most; idle CTAs leave at once
+        raggedChunkKernel<<<unsigned(chunks), kSlots, 0, s>>>(reinterpret_cast<const double*>(gathered),
+            reinterpret_cast<const uint32_t*>(leaf_counts), world, cap, reinterpret_cast<double*>(work));
+        launchCheck(who);
+        raggedTopKernel<<<1, kSlots, 0, s>>>(reinterpret_cast<const uint32_t*>(leaf_counts), world, cap,
+            reinterpret_cast<double*>(work), reinterpret_cast<double*>(out));
         launchCheck(who);
     });
 }

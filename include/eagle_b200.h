@@ -627,7 +627,7 @@ eagle_backend_status eagle_backend_x_b200_ragged_leaves(uint64_t kept, uint64_t 
  * levels, in rank order, into ``out`` = {hi, comp, value} (zeros for no survivors):
  * the bits of the one-device compact-then-sum of the concatenated shards. A rank whose
  * leaves did not fit its ``cap`` (ceil(shard samples / 4096) always fit) makes every
- * rank's ``out`` NaN. ``work`` holds 2 * ceil(world * cap / 512) + 2 doubles. One CTA. */
+ * rank's ``out`` NaN. ``work`` holds 2 * ceil(world * cap / 512) + 2 doubles. */
 eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, uint64_t leaf_counts, int32_t world,
     int64_t cap, uint64_t work, uint64_t out, uint64_t stream);
 
