@@ -502,12 +502,26 @@ class StagedRunner:
         """The run's report over all chunks: every chunk's counters copied on
         ``stream``, one host wait, then read."""
         torch = _t()
+        self.report_enqueue(stream)
+        (stream if stream is not None else torch.cuda.current_stream(self.device)).synchronize()
+        return self.report_read()
+
+    def report_enqueue(self, stream=None) -> None:
+        """Put the device-to-host copies of every chunk's counters on ``stream`` (no
+        wait): :meth:`report_read` reads them once a wait covers the copies, so the
+        host can enqueue the next run meanwhile."""
+        torch = _t()
         lib = _abi.lib()
         s = _stream_handle(stream)
         with torch.cuda.device(self.device):
             for r in self.runners:
                 _abi.check(lib.eagle_backend_x_b200_engine_report_enqueue(r._h, s))
-            (stream if stream is not None else torch.cuda.current_stream(self.device)).synchronize()
+
+    def report_read(self) -> RunReport:
+        """The report from the copies :meth:`report_enqueue` made (after a wait for them)."""
+        torch = _t()
+        lib = _abi.lib()
+        with torch.cuda.device(self.device):
             reps = []
             for r in self.runners:
                 rep = _abi.new(_abi.Report)
