@@ -47,7 +47,7 @@ MAX_STEPS = 10_000
 DT = 1e-3
 B_STEP = 66  # bytes one sample-step of eagle's unfused kernel reads and writes (omega, t_end, x, v, t, mask)
 WORKLOAD = "euler-oscillator-heterogeneous-stop"
-C5_BLOCK = 1 << 24  # compaction data are drawn per block of this many samples, so every shard draws its own
+MASK_BLOCK = 1 << 24  # compaction data are drawn per block of this many samples, so every shard draws its own
 DENSITIES = (0.9, 0.5, 0.1, 0.01)
 
 
@@ -72,8 +72,8 @@ def _args():
     return p.parse_args()
 
 
-def _c2_inputs(n: int):
-    """The whole C2 batch (every rank draws all of it and takes its shard)."""
+def _oscillator_inputs(n: int):
+    """The whole 2^24-sample heterogeneous-stop oscillator batch (every rank draws all of it and takes its shard)."""
     omega = np.random.default_rng(1).uniform(1.0, 3.0, n)
     x0 = np.random.default_rng(2).normal(1.0, 0.1, n)
     t_end = 10.0 ** np.random.default_rng(3).uniform(-2.0, 1.0, n)
@@ -322,7 +322,7 @@ def headline(ctx, args):
     begin, n = ctx.shard(n_total)
     mode = "persist" if args.mode == "auto" else args.mode
     fma = not args.no_fma
-    omega_all, x0_all, tend_all = _c2_inputs(n_total)
+    omega_all, x0_all, tend_all = _oscillator_inputs(n_total)
     omega, x0, t_end = (a[begin:begin + n] for a in (omega_all, x0_all, tend_all))
     dev, stream = ctx.dev, ctx.stream
     d_om = torch.from_numpy(omega).to(dev)
@@ -592,7 +592,7 @@ def headline(ctx, args):
 # ------------------------------------------------------------------------------ extras
 
 def extra_lorenz(ctx, args):
-    """C3: Lorenz-63 under adaptive RKF7(8), 2^22 samples, contiguous shards."""
+    """Lorenz-63 under adaptive RKF7(8), 2^22 samples, contiguous shards."""
     import torch
 
     import eagle_b200 as eb
@@ -694,7 +694,7 @@ def extra_lorenz(ctx, args):
 
 
 def extra_gambler(ctx, args):
-    """C4: the gambler's-ruin walk, 2^26 samples, shards keyed by their global ids."""
+    """The gambler's-ruin walk, 2^26 samples, shards keyed by their global ids."""
     import torch
 
     import eagle_b200 as eb
@@ -790,38 +790,38 @@ def _issue_roofline(sample_steps, kernel_ms):
                      "the integer pipes busy (profiles/gamblerPersist_16M_philox.md)"}
 
 
-def _c5_block(b: int):
-    """Block ``b`` (C5_BLOCK samples) of the 2^28-sample compaction data: N(0, 1) values
+def _masked_block(b: int):
+    """Block ``b`` (MASK_BLOCK samples) of the 2^28-sample compaction data: N(0, 1) values
     with 1 in 10^6 replaced by +-1e12, and one keep mask per density."""
-    vals = np.random.default_rng([4, b]).standard_normal(C5_BLOCK)
-    k = round(C5_BLOCK / 1e6)
-    where = np.random.default_rng([5, b]).choice(C5_BLOCK, size=k, replace=False)
+    vals = np.random.default_rng([4, b]).standard_normal(MASK_BLOCK)
+    k = round(MASK_BLOCK / 1e6)
+    where = np.random.default_rng([5, b]).choice(MASK_BLOCK, size=k, replace=False)
     vals[where] = np.where(np.random.default_rng([6, b]).random(k) < 0.5, -1.0, 1.0) * 1e12
-    masks = [np.random.default_rng([7 + i, b]).random(C5_BLOCK, dtype=np.float32) < p
+    masks = [np.random.default_rng([7 + i, b]).random(MASK_BLOCK, dtype=np.float32) < p
              for i, p in enumerate(DENSITIES)]
     return vals, masks
 
 
-def _c5_blocks(first: int, last: int):
+def _masked_blocks(first: int, last: int):
     """Blocks [first, last), drawn on a thread pool (numpy's generators fill without the GIL)."""
     import concurrent.futures
 
     with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(16, _host_cores()))) as ex:
-        return list(ex.map(_c5_block, range(first, last)))
+        return list(ex.map(_masked_block, range(first, last)))
 
 
-def _c5_shard(ctx, n_total):
+def _masked_shard(ctx, n_total):
     begin, n = ctx.shard(n_total)
-    if begin % C5_BLOCK or n % C5_BLOCK:
-        raise ValueError(f"the compaction workload shards by blocks of {C5_BLOCK} samples")
-    blocks = _c5_blocks(begin // C5_BLOCK, (begin + n) // C5_BLOCK)
+    if begin % MASK_BLOCK or n % MASK_BLOCK:
+        raise ValueError(f"the compaction workload shards by blocks of {MASK_BLOCK} samples")
+    blocks = _masked_blocks(begin // MASK_BLOCK, (begin + n) // MASK_BLOCK)
     vals = np.concatenate([bl[0] for bl in blocks])
     masks = [np.concatenate([bl[1][i] for bl in blocks]) for i in range(len(DENSITIES))]
     return begin, n, vals, masks
 
 
 def extra_compact_sum(ctx, args, data):
-    """C5: compact-then-sum of 2^28 values under four keep densities."""
+    """Compact-then-sum of 2^28 values under four keep densities."""
     import torch
 
     import eagle_b200 as eb
@@ -886,7 +886,7 @@ def extra_compact_sum(ctx, args, data):
 
 
 def extra_compact(ctx, args, data):
-    """The active-set compaction alone (ascending index map + count), the C5 masks."""
+    """The active-set compaction alone (ascending index map + count), over the compact-then-sum masks."""
     import torch
 
     import eagle_b200 as eb
@@ -957,7 +957,7 @@ def extra_compact(ctx, args, data):
     return out
 
 
-def c5_parity(ctx, args, data, c5):
+def compact_sum_parity(ctx, args, data, line):
     """Rank 0: the oracle's compaction + canonical sum of the whole 2^28 batch."""
     if ctx.rank != 0 or args.no_cpu:
         return
@@ -967,17 +967,17 @@ def c5_parity(ctx, args, data, c5):
     if n == n_total:
         full_vals, full_masks = vals, masks
     else:
-        blocks = _c5_blocks(0, n_total // C5_BLOCK)
+        blocks = _masked_blocks(0, n_total // MASK_BLOCK)
         full_vals = np.concatenate([bl[0] for bl in blocks])
         full_masks = [np.concatenate([bl[1][i] for bl in blocks]) for i in range(len(DENSITIES))]
     want = []
     for mk in full_masks:
         idx, _ = orc.compact(mk, drop=False)
         want.append(_bits(orc.reduce(full_vals[idx])[0]))
-    c5["parity"] = {"ok": want == c5["result"]["sum_bits"], "oracle_sum_bits": want,
-                    "seconds": time.perf_counter() - t0,
-                    "what": "the oracle's ascending compaction of the whole batch's mask, then its canonical sum "
-                            "of the kept values, per density"}
+    line["parity"] = {"ok": want == line["result"]["sum_bits"], "oracle_sum_bits": want,
+                      "seconds": time.perf_counter() - t0,
+                      "what": "the oracle's ascending compaction of the whole batch's mask, then its canonical sum "
+                              "of the kept values, per density"}
 
 
 def extras(ctx, args):
@@ -992,7 +992,7 @@ def extras(ctx, args):
     torch.cuda.empty_cache()
     _log("compaction data")
     n_total = 1 << 28
-    begin, n, vals, masks = _c5_shard(ctx, n_total)
+    begin, n, vals, masks = _masked_shard(ctx, n_total)
     data = (n_total, begin, n, vals, masks)
     _log("compact-then-sum")
     out["compact_sum"] = extra_compact_sum(ctx, args, data)
@@ -1001,7 +1001,7 @@ def extras(ctx, args):
     out["compact"] = extra_compact(ctx, args, data)
     torch.cuda.empty_cache()
     _log("compact-then-sum parity")
-    c5_parity(ctx, args, data, out["compact_sum"])
+    compact_sum_parity(ctx, args, data, out["compact_sum"])
     ctx.barrier()
     _log("extras done")
     return out
@@ -1017,7 +1017,7 @@ def reference(args):
     if rank != 0:
         return
     n_total = args.n or N_TOTAL
-    omega, x0, t_end = _c2_inputs(n_total)
+    omega, x0, t_end = _oscillator_inputs(n_total)
     orc = _oracle()
     cores = orc.threads()
     fma = not args.no_fma
@@ -1148,13 +1148,13 @@ def one_workload(ctx, args):
         out = extra_gambler(ctx, args)
     elif args.workload in ("compact_sum", "compact"):
         n_total = args.n or (1 << 28)
-        begin, n, vals, masks = _c5_shard(ctx, n_total)
+        begin, n, vals, masks = _masked_shard(ctx, n_total)
         data = (n_total, begin, n, vals, masks)
         if args.workload == "compact":
             out = extra_compact(ctx, args, data)
         else:
             out = extra_compact_sum(ctx, args, data)
-            c5_parity(ctx, args, data, out)
+            compact_sum_parity(ctx, args, data, out)
     else:
         if ctx.world != 1:
             raise SystemExit("--workload reorder runs on one GPU")

@@ -37,7 +37,7 @@ const void* orderedPersistStub(bool fma, bool spread);
 size_t stopOrderBytes(int64_t n);
 void prepareStopOrder();
 void enqueueStopOrder(const double* tEnd, double tEndU, const double* t, const uint8_t* term, int64_t n, double dt,
-    int64_t budget, int32_t* order, cudaStream_t s);
+    int64_t budget, int32_t* order, uint32_t* finished, cudaStream_t s);
 
 namespace {
 
@@ -478,10 +478,13 @@ void launchEngine(Engine& e, cudaStream_t s)
     cudaCheck(cudaMemsetAsync(&c->finished, 0, sizeof(uint32_t), s), "cudaMemsetAsync");
     cudaCheck(cudaMemsetAsync(&c->next, 0, offsetof(Cells, stepsum64) + sizeof(c->stepsum64) - offsetof(Cells, next), s),
         "cudaMemsetAsync");
-    enqueueMaskCount(e.term, e.n, &c->finished, s, false);
+    const bool persist = e.mode == EAGLE_B200_MODE_PERSIST;
+    // the ordered persist launch counts the mask in its claim order's key pass
+    const bool ordered = persist && e.order != nullptr && e.n > 0 && e.maxSteps > 0;
+    if (!ordered)
+        enqueueMaskCount(e.term, e.n, &c->finished, s, false);
     if (e.n == 0 || e.maxSteps == 0)
         return;
-    const bool persist = e.mode == EAGLE_B200_MODE_PERSIST;
     const std::string name = entryName(e, persist);
     const void* stub = entryStub(name);
     const int dev = e.device;
@@ -553,7 +556,8 @@ void launchEngine(Engine& e, cudaStream_t s)
             const double* tPlane = reinterpret_cast<const double*>(e.planes[e.spread ? 4 : 3]);
             const double dt = e.spread ? e.uniforms[0] : e.uniforms[1];
             order = e.order;
-            enqueueStopOrder(tEnd, e.spread ? 0.0 : e.uniforms[0], tPlane, e.term, e.n, dt, e.maxSteps, e.order, s);
+            enqueueStopOrder(tEnd, e.spread ? 0.0 : e.uniforms[0], tPlane, e.term, e.n, dt, e.maxSteps, e.order,
+                &c->finished, s);
             args.push_back(&order);
             stub = orderedPersistStub(e.fma, e.spread);
         }

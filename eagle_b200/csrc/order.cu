@@ -1,8 +1,8 @@
 // The longest-first claim order of the persistent oscillator.
 //
 // A persistent warp runs its 32 lanes' samples in lockstep, 512 steps per claim
-// head: a lane whose sample stops early idles until the head, and the C2 batch
-// (t_end log-uniform over three decades) leaves a lane idle about a fifth of the
+// head: a lane whose sample stops early idles until the head, and a batch with
+// t_end log-uniform over three decades leaves a lane idle about a fifth of the
 // time when samples are claimed in index order. The oscillator's stop step is
 // known before it steps (about (t_end - t) / dt), so the engine first sorts the
 // samples by it, longest first, and the lanes claim them in that order: a warp's
@@ -12,13 +12,20 @@
 // counters keep their bits.
 //
 // The sort is local: each run of 32768 consecutive samples (fewer for a small batch,
-// down to 4096) is ordered within its own
-// range by a counting sort over at most kBuckets buckets of ``width`` steps (the
-// budget spread over them), longest first, samples already terminated last -- one
-// CTA per run, all in shared memory. The lanes claim the runs one after another, so
-// a claim's loads and its results' stores stay inside a few runs at a time: the
-// gathered planes are read once from DRAM and their partly written sectors merge in
-// L2 (a global sort made every access a random one: 5.9 ms against 5.3 ms in index
+// down to 4096) is ordered within its own range by a counting sort over at most
+// kBuckets buckets of ``width`` steps (the budget spread over them), longest first,
+// samples already terminated last. Two launches: stopKeyKernel streams the mask,
+// t_end and t (17 bytes a sample) near the rate of a copy and writes each sample's
+// 2-byte bucket; stopSortKernel then sorts each run in one CTA, all in shared
+// memory, from keys that are still in L2, builds the run's order in shared memory
+// and writes it out coalesced, and counts the run's terminated samples for the run
+// report (so the launch needs no mask count of its own). At 2^24 samples: 58 + 44
+// us, where one kernel doing both per run (its loads, then its scattered 4-byte
+// order stores) took 149 us and the mask count 6.5 more.
+//
+// The lanes claim the runs one after another, so a claim's loads and its results'
+// stores stay inside a few runs at a time: the gathered planes are read once from
+// DRAM and their partly written sectors merge in L2 (a global sort made every access a random one: 5.9 ms against 5.3 ms in index
 // order, where the same samples moved into sorted order beforehand took 3.6 ms).
 #include "common.cuh"
 
@@ -33,9 +40,12 @@ constexpr int64_t kMinRun = 4096;  // the shortest run a small batch is cut into
 constexpr int kBuckets = 2048;    // step buckets; bucket kBuckets: terminated
 constexpr int kSlots = kBuckets + 1;
 constexpr int kSubs = 4;          // copies of the histogram
-constexpr int kUnroll = 4;        // samples per thread whose loads go out together
 constexpr int kPerScan = (kSlots + kThreads - 1) / kThreads;
 constexpr size_t kSmem = size_t(kSubs) * kSlots * sizeof(uint32_t) + size_t(kTile) * sizeof(uint16_t);
+
+constexpr int kKeyThreads = 256;
+constexpr int kKeyPer = 8;  // samples per thread of the key pass, their loads issued together
+constexpr int kVecPer = int(kTile / 8 / kThreads);  // 16-byte key loads per thread of a full run
 
 struct StopKeyArgs {
     const double* tEnd;  // null: ``tEndU`` for every sample
@@ -48,7 +58,9 @@ struct StopKeyArgs {
     int64_t width;  // steps per bucket
     int64_t run;    // samples per run, a power of two in [kMinRun, kTile]
     int64_t woven;  // runs whose claims are interleaved (the full runs, or 0: runs claimed one after another)
+    uint16_t* keys;  // n bucket keys, 16-byte aligned
     int32_t* order;
+    uint32_t* finished;  // += the samples already terminated (the mask's set bytes, counted by the sort); null: not counted
 };
 
 constexpr int64_t kWeave = 32;  // claims a run gives before the next run's turn (one warp's worth)
@@ -80,51 +92,97 @@ __device__ __forceinline__ uint32_t stopKeyOf(const StopKeyArgs& a, uint8_t done
     return uint32_t(kBuckets - 1) - uint32_t(k < kBuckets ? k : kBuckets - 1);
 }
 
-/** One CTA per run of ``a.run`` samples: keys into shared memory with a histogram,
- *  the buckets' starts by a CTA scan, then each sample placed in its bucket (in no
- *  particular order within it). The histogram is kept in kSubs copies, lane l
- *  counting into copy l % kSubs, so that the many samples of a crowded bucket (short
- *  stops) collide in shared memory kSubs times less; each copy gets its own range
- *  inside the bucket. */
-__global__ __launch_bounds__(kThreads) void stopOrderKernel(StopKeyArgs a)
+/** Sample i's bucket key for every i < n: the mask byte, t_end and t of kKeyPer
+ *  samples a thread (a stride of kKeyThreads apart, so every load is coalesced), all
+ *  loads out before any key is formed. */
+__global__ __launch_bounds__(kKeyThreads) void stopKeyKernel(StopKeyArgs a)
+{
+    const int64_t i0 = int64_t(blockIdx.x) * (kKeyThreads * kKeyPer) + threadIdx.x;
+    uint8_t done[kKeyPer];
+    double te[kKeyPer], t0[kKeyPer];
+#pragma unroll
+    for (int r = 0; r < kKeyPer; ++r) {
+        const int64_t i = i0 + int64_t(r) * kKeyThreads;
+        const int64_t at = i < a.n ? i : 0;
+        done[r] = a.term[at];
+        te[r] = a.tEnd != nullptr ? a.tEnd[at] : a.tEndU;
+        t0[r] = a.t[at];
+    }
+#pragma unroll
+    for (int r = 0; r < kKeyPer; ++r) {
+        const int64_t i = i0 + int64_t(r) * kKeyThreads;
+        if (i < a.n)
+            a.keys[i] = uint16_t(stopKeyOf(a, done[r], te[r], t0[r]));
+    }
+}
+
+/** The histogram copy that sample j of a run counts into: copies alternate every 8
+ *  samples, so the lanes of one shared-memory atomic (8 or 32 samples apart) spread
+ *  over all kSubs copies and the many samples of a crowded bucket (short stops)
+ *  collide kSubs times less. */
+__device__ __forceinline__ int subOf(int j) { return (j >> 3) & (kSubs - 1); }
+
+/** The run's keys of whole 16-byte groups (8 keys each) that thread t takes: group
+ *  t + q kThreads, zeros past ``vecs``; the loads all go out together. */
+__device__ __forceinline__ void loadKeyGroups(const uint4* src, int vecs, uint4 (&w)[kVecPer])
+{
+#pragma unroll
+    for (int q = 0; q < kVecPer; ++q) {
+        const int v = int(threadIdx.x) + q * kThreads;
+        w[q] = v < vecs ? src[v] : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+__device__ __forceinline__ uint32_t keyAt(const uint4& w, int e)
+{
+    const uint32_t word = e < 2 ? w.x : e < 4 ? w.y : e < 6 ? w.z : w.w;
+    return (word >> (16 * (e & 1))) & 0xffffu;
+}
+
+/** One CTA per run of ``a.run`` samples, from the keys the key pass left in L2: a
+ *  histogram of the run's keys, the buckets' starts by a CTA scan, then each sample's
+ *  place in its bucket (in no particular order within it) taken by a shared-memory
+ *  atomic. The run's order is built in shared memory (2-byte offsets into the run)
+ *  and written out in place order, coalesced: writing each sample's claim straight
+ *  to global memory scattered 4-byte stores over the run's 128 KB, one L1 wavefront
+ *  per lane (104 us at 2^24 against about 30). Each of the kSubs histogram copies
+ *  gets its own range inside the bucket. */
+__global__ __launch_bounds__(kThreads, 2) void stopSortKernel(StopKeyArgs a)
 {
     extern __shared__ __align__(16) uint32_t smem[];
-    uint32_t* cnt = smem;                                          // [kSubs][kSlots]
-    uint16_t* keys = reinterpret_cast<uint16_t*>(smem + kSubs * kSlots);  // [kTile]
+    uint32_t* cnt = smem;                                                  // [kSubs][kSlots]
+    uint16_t* ord = reinterpret_cast<uint16_t*>(smem + kSubs * kSlots);   // [kTile]: place -> offset
     __shared__ uint32_t scan[33];
     const int t = int(threadIdx.x);
-    const int sub = t % kSubs;
+    const int64_t i0 = int64_t(blockIdx.x) * a.run;
+    const int live = int(a.n - i0 < a.run ? a.n - i0 : a.run);
+    const int vecs = live / 8;  // whole 16-byte groups of keys (i0 is a multiple of 8)
+    const uint4* src = reinterpret_cast<const uint4*>(a.keys + i0);
+    uint4 w[kVecPer];
+    loadKeyGroups(src, vecs, w);
     for (int b = t; b < kSubs * kSlots; b += kThreads)
         cnt[b] = 0;
     __syncthreads();
-    const int64_t i0 = int64_t(blockIdx.x) * a.run;
-    const int live = int(a.n - i0 < a.run ? a.n - i0 : a.run);
-    for (int j0 = 0; j0 < live; j0 += kThreads * kUnroll) {
-        // coalesced; every load of the round issued before any key is formed
-        uint8_t done[kUnroll];
-        double te[kUnroll], t0[kUnroll];
 #pragma unroll
-        for (int r = 0; r < kUnroll; ++r) {
-            const int j = j0 + r * kThreads + t;
-            const int64_t i = i0 + (j < live ? j : 0);
-            done[r] = a.term[i];
-            te[r] = a.tEnd != nullptr ? a.tEnd[i] : a.tEndU;
-            t0[r] = a.t[i];
-        }
-        uint32_t k[kUnroll];
+    for (int q = 0; q < kVecPer; ++q) {
+        const int v = t + q * kThreads;
+        if (v < vecs) {
 #pragma unroll
-        for (int r = 0; r < kUnroll; ++r)
-            k[r] = stopKeyOf(a, done[r], te[r], t0[r]);
-#pragma unroll
-        for (int r = 0; r < kUnroll; ++r) {
-            const int j = j0 + r * kThreads + t;
-            if (j < live) {
-                keys[j] = uint16_t(k[r]);
-                atomicAdd(&cnt[sub * kSlots + int(k[r])], 1u);
-            }
+            for (int e = 0; e < 8; ++e)
+                atomicAdd(&cnt[subOf(v * 8 + e) * kSlots + int(keyAt(w[q], e))], 1u);
         }
     }
+    for (int j = vecs * 8 + t; j < live; j += kThreads)  // the last run's ragged end
+        atomicAdd(&cnt[subOf(j) * kSlots + int(a.keys[i0 + j])], 1u);
     __syncthreads();
+    if (a.finished != nullptr && t == kThreads - 1) {  // the run's terminated samples: bucket kBuckets
+        uint32_t c = 0;
+#pragma unroll
+        for (int q = 0; q < kSubs; ++q)
+            c += cnt[q * kSlots + kBuckets];
+        if (c != 0)
+            atomicAdd(a.finished, c);
+    }
     // positions run bucket by bucket (longest first), and inside a bucket copy by copy:
     // thread t owns buckets [kPerScan t, kPerScan t + kPerScan)
     uint32_t mine = 0;
@@ -149,8 +207,23 @@ __global__ __launch_bounds__(kThreads) void stopOrderKernel(StopKeyArgs a)
             }
     }
     __syncthreads();
-    for (int j = t; j < live; j += kThreads)
-        a.order[claimOf(a, blockIdx.x, atomicAdd(&cnt[sub * kSlots + int(keys[j])], 1u))] = int32_t(i0 + j);
+    loadKeyGroups(src, vecs, w);  // again from L2: holding them through the scan costs a CTA per SM
+#pragma unroll
+    for (int q = 0; q < kVecPer; ++q) {
+        const int v = t + q * kThreads;
+        if (v < vecs) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int j = v * 8 + e;
+                ord[atomicAdd(&cnt[subOf(j) * kSlots + int(keyAt(w[q], e))], 1u)] = uint16_t(j);
+            }
+        }
+    }
+    for (int j = vecs * 8 + t; j < live; j += kThreads)
+        ord[atomicAdd(&cnt[subOf(j) * kSlots + int(a.keys[i0 + j])], 1u)] = uint16_t(j);
+    __syncthreads();
+    for (int p = t; p < live; p += kThreads)
+        a.order[claimOf(a, blockIdx.x, p)] = int32_t(i0 + int64_t(ord[p]));
 }
 
 }  // namespace
@@ -173,10 +246,14 @@ int l2Bytes()
 
 }  // namespace
 
-/** Device bytes of the claim order over n samples. */
-size_t stopOrderBytes(int64_t n) { return (size_t(n) * sizeof(int32_t) + 255) / 256 * 256; }
+/** Bytes of the claim order proper (n int32), rounded to 256. */
+size_t orderPart(int64_t n) { return (size_t(n) * sizeof(int32_t) + 255) / 256 * 256; }
 
-/** Raise the order kernel's dynamic shared-memory limit on the current device, once
+/** Device bytes of the claim order over n samples: the order, then the n 2-byte
+ *  bucket keys the sort reads. */
+size_t stopOrderBytes(int64_t n) { return orderPart(n) + (size_t(n) * sizeof(uint16_t) + 255) / 256 * 256; }
+
+/** Raise the sort kernel's dynamic shared-memory limit on the current device, once
  *  per device (the engine calls it at create, outside any stream capture). */
 void prepareStopOrder()
 {
@@ -186,18 +263,19 @@ void prepareStopOrder()
     cudaCheck(cudaGetDevice(&dev), "cudaGetDevice");
     std::lock_guard<std::mutex> lock(mu);
     if (!raised[dev & 63]) {
-        cudaCheck(cudaFuncSetAttribute(stopOrderKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)),
+        cudaCheck(cudaFuncSetAttribute(stopSortKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)),
             "cudaFuncSetAttribute");
         raised[dev & 63] = true;
     }
 }
 
 /** Enqueue the claim order of samples [0, n) into ``order`` (stopOrderBytes(n)
- *  bytes): each run of up to 32768 samples longest first, t_end from ``tEnd`` (null:
- *  ``tEndU`` for all), t from ``t``, the mask ``term``; stop steps estimated
- *  against ``budget``. */
+ *  bytes, 16-byte aligned): each run of up to 32768 samples longest first, t_end
+ *  from ``tEnd`` (null: ``tEndU`` for all), t from ``t``, the mask ``term``; stop
+ *  steps estimated against ``budget``. The mask's set bytes are added to
+ *  ``finished`` unless it is null. */
 void enqueueStopOrder(const double* tEnd, double tEndU, const double* t, const uint8_t* term, int64_t n, double dt,
-    int64_t budget, int32_t* order, cudaStream_t s)
+    int64_t budget, int32_t* order, uint32_t* finished, cudaStream_t s)
 {
     if (n <= 0)
         return;
@@ -212,6 +290,8 @@ void enqueueStopOrder(const double* tEnd, double tEndU, const double* t, const u
     a.budget = budget > 0 ? budget : 1;
     a.width = (a.budget + kBuckets - 1) / kBuckets;
     a.order = order;
+    a.keys = reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(order) + orderPart(n));
+    a.finished = finished;
     // A run's sort takes one CTA the same time whatever else runs, so a batch too small
     // to give every SM two runs of kTile is cut into shorter runs (down to kMinRun):
     // the order then groups lengths a little less finely, but its launch no longer
@@ -230,7 +310,9 @@ void enqueueStopOrder(const double* tEnd, double tEndU, const double* t, const u
     // 2^24: 5.71 against 3.64 ms), so larger batches claim run after run.
     a.woven = n * 48 <= int64_t(l2Bytes()) ? n / a.run : 0;
     prepareStopOrder();
-    stopOrderKernel<<<unsigned((n + a.run - 1) / a.run), kThreads, kSmem, s>>>(a);
+    stopKeyKernel<<<unsigned((n + kKeyThreads * kKeyPer - 1) / (kKeyThreads * kKeyPer)), kKeyThreads, 0, s>>>(a);
+    launchCheck("stop order");
+    stopSortKernel<<<unsigned((n + a.run - 1) / a.run), kThreads, kSmem, s>>>(a);
     launchCheck("stop order");
 }
 

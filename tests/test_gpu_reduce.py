@@ -57,6 +57,21 @@ def test_large_and_tiny_sums(eb, orc, n):
     assert _same(eb.reduce(_dev(x)).cpu().numpy(), orc.reduce(x))
 
 
+@pytest.mark.parametrize("n", (8192, 12289, (1 << 23) + 12345))
+def test_staged_and_direct_leaf_loads(eb, orc, n):
+    """A float64 plane gives the oracle's bits whether it starts on a 16-byte boundary
+    or 8 bytes off one (a view one element into its buffer), at sizes whose CTAs own
+    one leaf each and whose CTAs own groups of several."""
+    x = orc.corpus(n, 77 + n)
+    want = orc.reduce(x)
+    assert _same(eb.reduce(_dev(x)).cpu().numpy(), want)
+    base = torch.empty(n + 1, dtype=torch.float64, device="cuda")
+    base[1:].copy_(torch.from_numpy(x))
+    off = base[1:]
+    assert off.data_ptr() % 16 == 8
+    assert _same(eb.reduce(off).cpu().numpy(), want)
+
+
 @pytest.mark.parametrize("dtype", [np.int32, np.int64])
 def test_integer_sums_min_max(eb, orc, dtype):
     rng = np.random.default_rng(1)
