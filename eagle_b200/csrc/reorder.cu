@@ -15,11 +15,18 @@
 // Here: ONE scan kernel (16 mask bytes per thread, CTA scan, decoupled look-back
 // over 4096-slot tiles) records each tile's keep bits and its exclusive kept
 // prefix in the scratch, since the mask itself is one of the planes that move.
-// Each plane then takes two kernels: a copy of [0, *span) into the stage, and a
-// tile kernel that reads its 4096 staged elements, places them in shared memory
-// in their new order (kept run first, dropped run after) and writes both runs
-// with coalesced stores. Nothing reads *span or *fire on the host, so every
-// launch is capturable.
+// Each plane then takes two kernels. The place kernel reads a tile of the plane
+// itself, orders it in shared memory (kept run first, dropped run after), writes
+// the kept run straight to its final slots and the dropped run to the stage, both
+// with coalesced stores; a copy then puts the staged dropped run at [count, span).
+// In place works for the kept run because a kept slot only moves down (slot i to
+// incl(i) - 1 <= i): a tile's kept run lands in its own slots or in the tiles just
+// before it, and it waits only until those tiles have been read (a per-tile flag;
+// tiles are claimed in order, and a tile's read never waits, so the wait always
+// ends; it is bounded all the same). The plane is read once and written once, the
+// dropped run twice more: (4 - 2p) element bytes a slot at keep fraction p where a
+// copy of the whole span to the stage and a place back cost 4. Nothing reads
+// *span or *fire on the host, so every launch is capturable.
 #include "common.cuh"
 
 #include <cstdlib>
@@ -42,21 +49,24 @@ struct alignas(16) Elem16 {
     uint64_t lo, hi;
 };
 
-/** The scratch layout of a reorder of n samples whose widest moved element is
- *  ``elem`` bytes: tile status words, three counters, tile prefixes, tile keep
- *  bits (one uint16 per thread), then the stage. */
+/** The scratch layout of a reorder of n samples over ``planes`` planes whose
+ *  widest moved element is ``elem`` bytes: tile status words, three counters, each
+ *  tile's read flag, one tile counter per moved plane (perm included; all zeroed per
+ *  call), tile prefixes, tile keep bits (one uint16 per thread), then the stage. */
 struct Layout {
-    size_t status, words, prefix, bits, stage, total;
+    size_t status, words, done, claims, prefix, bits, stage, total;
 };
 
-Layout layoutFor(int64_t n, uint32_t elem)
+Layout layoutFor(int64_t n, uint32_t elem, size_t planes = 0)
 {
     const size_t tiles = size_t(n > 0 ? (n + kTile - 1) / kTile : 1);
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
     Layout l{};
     l.status = 0;
     l.words = up(tiles * sizeof(uint64_t));
-    l.prefix = l.words + 256;
+    l.done = l.words + 256;
+    l.claims = up(l.done + tiles * sizeof(uint32_t));
+    l.prefix = up(l.claims + (planes + 1) * sizeof(uint32_t));
     l.bits = up(l.prefix + tiles * sizeof(uint32_t));
     l.stage = up(l.bits + tiles * kThreads * sizeof(uint16_t));
     l.total = up(l.stage + size_t(n > 0 ? n : 1) * (elem > 4 ? elem : 4));
@@ -141,85 +151,210 @@ __global__ __launch_bounds__(kThreads) void copySpanKernel(const T* __restrict__
         dst[i] = src[i];
 }
 
-struct PlaceArgs {
-    const void* stage;
+struct InPlaceArgs {
     void* plane;
+    void* stage;
     const uint16_t* bits;
     const uint32_t* prefix;
     const uint32_t* cnt;
     const uint32_t* span;
     const uint32_t* fire;
-    const uint32_t* err;
-    int32_t* inv;       // Perm only
-    int32_t* indexMap;  // Perm only
+    uint32_t* err;
+    uint32_t* claim;     // this plane's tile counter (zero on entry)
+    uint32_t* readDone;  // per tile: the epoch of the latest plane whose tile has been read
+    int32_t* inv;        // Perm only
+    int32_t* indexMap;   // Perm only
     int64_t n;
+    uint32_t epoch, tiles;
 };
 
-/** One 4096-slot tile of one plane into its new places. With ``Perm`` the plane
- *  is perm: inv[v] = new slot for each moved value v, and index_map is the
- *  identity over the tile's part of [0, count). */
+__device__ __forceinline__ uint32_t readFlag(const uint32_t* readDone, int64_t w)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(readDone + w) : "memory");
+    return v;
+}
+
+/** Whether tile ``w`` of the plane with ``epoch`` has been read, polled at most
+ *  kLbSpinLimit times (acquire: the tile's slots may be overwritten after it). */
+__device__ __forceinline__ bool waitTileRead(const uint32_t* readDone, int64_t w, uint32_t epoch)
+{
+    for (uint32_t i = 0; i < kLbSpinLimit; ++i) {
+        if (readFlag(readDone, w) >= epoch)
+            return true;
+        if (i > 32)
+            __nanosleep(64);
+    }
+    return false;
+}
+
+/** 4096-slot tiles of one plane moved in place, one CTA per resident slot: each
+ *  tile (claimed in order; the next claim goes out while the tile is worked on) is
+ *  read, ordered in shared memory and its read published, then its kept run written
+ *  to [pre, pre + kept) once the earlier tiles that range covers have been read, and
+ *  its dropped run to the stage at its rank among the dropped slots. With ``Perm``
+ *  the plane is perm: inv[v] = the new slot of each moved value v (a dropped one's
+ *  is count + its rank), and index_map is the identity over the tile's part of
+ *  [0, count). A wait that gives up sets bit 2 of ``*err`` and leaves the tile's
+ *  kept run unwritten: the count then reports the failure. No wait is on a tile
+ *  whose read cannot finish: the lowest tile not yet read is being read (reads
+ *  wait on nothing) or is claimed by a CTA writing an earlier tile, whose waits are
+ *  on tiles lower still, all read. */
 template <class T, bool Perm>
-__global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : 4) void placeKernel(PlaceArgs a)
+__global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : 4) void placeInPlaceKernel(InPlaceArgs a)
 {
     if (a.fire != nullptr && *a.fire == 0u)
         return;
     if (*a.err != 0u)
-        return;  // the scan gave up: leave the planes as they were
+        return;  // the scan gave up (the planes stay as they were), or an earlier plane's wait did
     extern __shared__ __align__(16) unsigned char smem[];
     T* out = reinterpret_cast<T*>(smem);
     __shared__ uint32_t scan[33];
-    const int t = int(threadIdx.x);
-    const uint32_t tile = blockIdx.x;
-    const int64_t sp = spanOf(a.span, a.n);
-    const int64_t tile0 = int64_t(tile) * kTile;
-    if (tile0 >= sp)
-        return;  // the whole CTA: nothing of this tile moves
-    const int64_t len = sp - tile0 < kTile ? sp - tile0 : kTile;
     __shared__ uint16_t sKeep[kThreads];
     __shared__ uint32_t sExcl[kThreads];
-    const T* src = static_cast<const T*>(a.stage);
-    // element e of the tile is the (e % 16)-th of thread e / 16's keep bits: read the
-    // stage coalesced (lane-consecutive e) and put each element at its tile-local place,
-    // the kept ones at [0, kept), the dropped ones at [kept, len). The sixteen loads go
-    // out first, so that they are in flight while the tile's keep counts are scanned.
-    T v[kPer];
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-        const int e = t + j * kThreads;
-        v[j] = int64_t(e) < len ? src[tile0 + e] : T{};
-    }
-    const uint32_t keep = a.bits[size_t(tile) * kThreads + size_t(t)];
-    const int64_t pre = int64_t(a.prefix[tile]);  // kept slots before the tile
+    __shared__ uint32_t sTile;
+    __shared__ int sOk;
+    const int t = int(threadIdx.x);
+    if (t == 0)
+        sTile = atomicAdd(a.claim, 1u);
+    __syncthreads();
+    uint32_t tile = sTile;
+    const int64_t sp = spanOf(a.span, a.n);
     const int64_t cnt = int64_t(*a.cnt);
-    uint32_t kept = 0;
-    const uint32_t excl = blockExclusiveSum(uint32_t(__popc(keep)), kept, scan);
-    sKeep[t] = uint16_t(keep);
-    sExcl[t] = excl;
-    __syncthreads();
+    T* plane = static_cast<T*>(a.plane);
+    T* stage = static_cast<T*>(a.stage);
+    constexpr bool kNarrow = sizeof(T) <= 2;
+    const bool vecOk = (reinterpret_cast<uintptr_t>(plane) & 15u) == 0;
+    while (tile < a.tiles) {
+        const int64_t tile0 = int64_t(tile) * kTile;
+        if (tile0 >= sp)
+            break;  // nothing of this tile moves, nor of any later claim; no kept slot lands here
+        const int64_t len = sp - tile0 < kTile ? sp - tile0 : kTile;
+        // Elements 1 or 2 bytes wide: thread t takes the tile's elements [16 t, 16 t + 16)
+        // -- exactly its own keep bits -- in one or two 16-byte loads. Wider ones: element
+        // e is the (e % 16)-th of thread e / 16's keep bits, read coalesced
+        // (lane-consecutive e). All loads go out before the keep counts are scanned.
+        T v[kPer];
+        if constexpr (kNarrow) {
+            const int64_t e0 = int64_t(t) * kPer;
+            if (vecOk && e0 + kPer <= len) {
+                union {
+                    uint4 q[sizeof(T)];
+                    T x[kPer];
+                } u;
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-        const int e = t + j * kThreads;
-        if (int64_t(e) < len) {
-            const uint32_t kb = sKeep[e >> 4], bit = uint32_t(e & 15);
-            const uint32_t before = sExcl[e >> 4] + __popc(kb & ((1u << bit) - 1u));  // kept before e
-            const uint32_t pos = ((kb >> bit) & 1u) ? before : kept + uint32_t(e) - before;
-            out[pos] = v[j];
+                for (int k = 0; k < int(sizeof(T)); ++k)
+                    u.q[k] = reinterpret_cast<const uint4*>(plane + tile0 + e0)[k];
+#pragma unroll
+                for (int j = 0; j < kPer; ++j)
+                    v[j] = u.x[j];
+            } else {
+#pragma unroll
+                for (int j = 0; j < kPer; ++j)
+                    v[j] = e0 + j < len ? plane[tile0 + e0 + j] : T{};
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int e = t + j * kThreads;
+                v[j] = int64_t(e) < len ? plane[tile0 + e] : T{};
+            }
         }
-    }
-    __syncthreads();
-    T* dst = static_cast<T*>(a.plane);
-    // the kept run lands at [pre, pre + kept), the dropped run at [cnt + tile0 - pre, ...)
-    const int64_t dropAt = cnt + tile0 - pre;
-    for (int q = t; q < int(len); q += kThreads) {
-        const int64_t d = q < int(kept) ? pre + q : dropAt + (q - int(kept));
-        const T v = out[q];
-        dst[d] = v;
-        if constexpr (Perm) {
-            a.inv[static_cast<int32_t>(v)] = int32_t(d);
-            if (q < int(kept))
-                a.indexMap[d] = int32_t(d);
+        uint32_t next = 0;
+        if (t == 0)
+            next = atomicAdd(a.claim, 1u);  // used at the end of the tile
+        const uint32_t keep = a.bits[size_t(tile) * kThreads + size_t(t)];
+        const int64_t pre = int64_t(a.prefix[tile]);  // kept slots before the tile
+        // the read flags of the (at most two) earlier tiles the kept run may land in,
+        // fetched now so that the check after the scan seldom waits
+        const int64_t first = pre / kTile;
+        uint32_t seen = 0;
+        if (t < 2 && first + t < int64_t(tile))
+            seen = readFlag(a.readDone, first + t);
+        uint32_t kept = 0;
+        const uint32_t excl = blockExclusiveSum(uint32_t(__popc(keep)), kept, scan);
+        if (t == 0)
+            sOk = 1;
+        if constexpr (kNarrow) {
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int64_t e = int64_t(t) * kPer + j;
+                if (e < len) {
+                    const uint32_t before = excl + __popc(keep & ((1u << j) - 1u));  // kept before e
+                    const uint32_t pos = ((keep >> j) & 1u) ? before : kept + uint32_t(e) - before;
+                    out[pos] = v[j];
+                }
+            }
+        } else {
+            sKeep[t] = uint16_t(keep);
+            sExcl[t] = excl;
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int e = t + j * kThreads;
+                if (int64_t(e) < len) {
+                    const uint32_t kb = sKeep[e >> 4], bit = uint32_t(e & 15);
+                    const uint32_t before = sExcl[e >> 4] + __popc(kb & ((1u << bit) - 1u));  // kept before e
+                    const uint32_t pos = ((kb >> bit) & 1u) ? before : kept + uint32_t(e) - before;
+                    out[pos] = v[j];
+                }
+            }
         }
+        __syncthreads();  // every load of the tile has landed (its value is in shared memory)
+        if (t == 0)  // so its slots may be overwritten: reads that have returned need no fence
+            asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.readDone + tile), "r"(a.epoch) : "memory");
+        if (kept > 0) {
+            // [pre, pre + kept) covers at most two tiles, the last of them this one at most
+            const int64_t last = (pre + int64_t(kept) - 1) / kTile;
+            if (t < 2) {
+                const int64_t w = first + t;
+                if (w <= last && w < int64_t(tile) && seen < a.epoch && !waitTileRead(a.readDone, w, a.epoch)) {
+                    atomicOr(a.err, 4u);
+                    sOk = 0;
+                }
+            }
+            __syncthreads();
+        }
+        const int64_t dropBase = tile0 - pre;  // dropped slots before the tile
+        const bool ok = sOk != 0;
+        for (int q = t; q < int(len); q += kThreads) {
+            const T x = out[q];
+            if (q < int(kept)) {
+                if (!ok)
+                    continue;
+                const int64_t d = pre + q;
+                plane[d] = x;
+                if constexpr (Perm) {
+                    a.inv[static_cast<int32_t>(x)] = int32_t(d);
+                    a.indexMap[d] = int32_t(d);
+                }
+            } else {
+                const int64_t r = dropBase + (q - int(kept));
+                stage[r] = x;
+                if constexpr (Perm)
+                    a.inv[static_cast<int32_t>(x)] = int32_t(cnt + r);
+            }
+        }
+        if (t == 0)
+            sTile = next;
+        __syncthreads();  // out, sKeep and sExcl are free again; sTile holds the next claim
+        tile = sTile;
     }
+}
+
+/** plane[count + r] = stage[r] for the staged dropped run, r < span - count. */
+template <class T>
+__global__ __launch_bounds__(kThreads) void dropBackKernel(const T* __restrict__ stage, T* __restrict__ plane,
+    const uint32_t* cnt, const uint32_t* span, const uint32_t* fire, const uint32_t* err, int64_t n)
+{
+    if (fire != nullptr && *fire == 0u)
+        return;
+    if (*err != 0u)
+        return;
+    const int64_t c = int64_t(*cnt);
+    const int64_t end = spanOf(span, n) - c;
+    for (int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; r < end; r += int64_t(gridDim.x) * blockDim.x)
+        plane[c + r] = stage[r];
 }
 
 __global__ void reorderFinishKernel(const uint32_t* cnt, const uint32_t* err, uint32_t* count, uint32_t* span,
@@ -283,6 +418,34 @@ unsigned streamGrid(int64_t n)
     const int64_t want = (n + kThreads - 1) / kThreads;
     const int64_t cap = int64_t(smCount()) * 8;
     return unsigned(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+/** The in-place place kernel's grid for ``tiles`` tiles: one CTA per resident slot
+ *  (the kernel's occupancy, looked up once per device), at most one per tile. Also
+ *  opts the kernel into ``shared`` bytes of dynamic shared memory. */
+template <class T, bool Perm>
+unsigned placeGrid(uint32_t tiles, size_t shared)
+{
+    static std::mutex mu;
+    static int perSm[64] = {};
+    const void* kernel = reinterpret_cast<const void*>(&placeInPlaceKernel<T, Perm>);
+    allowShared(kernel, shared);
+    int dev = 0;
+    cudaCheck(cudaGetDevice(&dev), "cudaGetDevice");
+    int occ = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (perSm[dev & 63] == 0) {
+            cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&perSm[dev & 63], placeInPlaceKernel<T, Perm>,
+                          kThreads, shared),
+                "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+            if (perSm[dev & 63] < 1)
+                perSm[dev & 63] = 1;
+        }
+        occ = perSm[dev & 63];
+    }
+    const int64_t slots = int64_t(occ) * smCount();
+    return unsigned(int64_t(tiles) < slots ? int64_t(tiles) : slots);
 }
 
 template <class F>
@@ -665,7 +828,7 @@ EB_API eagle_backend_status eagle_backend_reorder_device(struct eagle_backend_re
             unsupported(std::string(who) + ": the int32 perm addresses at most 2^31-1 samples, got n = "
                 + std::to_string(d.n));
         const auto planes = planesOf(d, who, true);
-        const Layout l = layoutFor(d.n, widestOf(planes));
+        const Layout l = layoutFor(d.n, widestOf(planes), planes.size());
         if (d.scratch == 0) {
             constexpr size_t end = offsetof(eagle_backend_reorder_desc, scratch_bytes) + sizeof(int64_t);
             if (desc->struct_size < end)
@@ -704,7 +867,7 @@ EB_API eagle_backend_status eagle_backend_reorder_device(struct eagle_backend_re
         else
             reorderScanKernel<false><<<a.tiles, kThreads, 0, s>>>(a);
         launchCheck(who);
-        PlaceArgs p{};
+        InPlaceArgs p{};
         p.stage = base + l.stage;
         p.bits = a.bits;
         p.prefix = a.prefix;
@@ -712,24 +875,28 @@ EB_API eagle_backend_status eagle_backend_reorder_device(struct eagle_backend_re
         p.span = span;
         p.fire = fire;
         p.err = a.err;
+        p.readDone = reinterpret_cast<uint32_t*>(base + l.done);
         p.n = d.n;
+        p.tiles = a.tiles;
+        uint32_t epoch = 0;
         auto move = [&](uint64_t data, uint32_t elem, bool perm) {
+            p.claim = reinterpret_cast<uint32_t*>(base + l.claims) + epoch;
+            ++epoch;
+            p.epoch = epoch;
             withElem(elem, [&](auto tag) {
                 using T = decltype(tag);
-                copySpanKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(data),
-                    reinterpret_cast<T*>(base + l.stage), span, fire, d.n);
-                launchCheck(who);
                 p.plane = reinterpret_cast<void*>(data);
                 const size_t shared = size_t(kTile) * sizeof(T);
                 if (perm) {
                     p.inv = reinterpret_cast<int32_t*>(d.inv);
                     p.indexMap = reinterpret_cast<int32_t*>(d.index_map);
-                    allowShared(reinterpret_cast<const void*>(&placeKernel<int32_t, true>), shared);
-                    placeKernel<int32_t, true><<<a.tiles, kThreads, shared, s>>>(p);
+                    placeInPlaceKernel<int32_t, true><<<placeGrid<int32_t, true>(a.tiles, shared), kThreads, shared, s>>>(p);
                 } else {
-                    allowShared(reinterpret_cast<const void*>(&placeKernel<T, false>), shared);
-                    placeKernel<T, false><<<a.tiles, kThreads, shared, s>>>(p);
+                    placeInPlaceKernel<T, false><<<placeGrid<T, false>(a.tiles, shared), kThreads, shared, s>>>(p);
                 }
+                launchCheck(who);
+                dropBackKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(base + l.stage),
+                    reinterpret_cast<T*>(data), a.cnt, span, fire, a.err, d.n);
                 launchCheck(who);
             });
         };

@@ -72,6 +72,32 @@ def test_reorder_matches_oracle(eb, orc, n, drop):
     del keep_alive
 
 
+@pytest.mark.parametrize("pattern", ("keep_most", "keep_few", "all", "none", "runs", "front"))
+def test_reorder_densities_and_runs(eb, orc, pattern):
+    """Masks that move the kept runs by little (a tile's kept run then lands in its
+    own tile and the one before, which it has to wait on) and by much, with the
+    dropped runs staged and copied back: every plane, perm, inv and the count bit
+    for bit against the oracle, on 2^21 + 123 slots (513 tiles)."""
+    n = (1 << 21) + 123
+    host = _host(n, 99, 0.5)
+    g = np.random.default_rng(7)
+    drop = {"keep_most": g.random(n) < 0.001, "keep_few": g.random(n) < 0.999, "all": np.zeros(n, bool),
+            "none": np.ones(n, bool), "runs": (np.arange(n) // 5000) % 2 == 1,
+            "front": np.arange(n) >= n // 3}[pattern]
+    host[MASK] = drop.astype(np.uint8)
+    dev = _dev(host)
+    perm, inv, im, count, span = _cells(n, n)
+    hp, hi, him = np.arange(n, dtype=np.int32), np.arange(n, dtype=np.int32), np.zeros(n, np.int32)
+    keep_alive = eb.reorder(dev, dev[MASK], perm, inv, im, count, span, drop=True)
+    c, sp, _ = orc.reorder(host, MASK, hp, hi, him, n, drop=True)
+    torch.cuda.synchronize()
+    _same(dev, host)
+    assert perm.cpu().numpy().tobytes() == hp.tobytes() and inv.cpu().numpy().tobytes() == hi.tobytes()
+    assert int(count.item()) == c and int(span.item()) == sp
+    assert im.cpu().numpy()[:c].tobytes() == him[:c].tobytes()
+    del keep_alive
+
+
 def test_partial_span_leaves_the_tail(eb, orc):
     n = 50_001
     host = _host(n, 3, 0.5)
