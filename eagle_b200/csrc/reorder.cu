@@ -201,7 +201,7 @@ __device__ __forceinline__ bool waitTileRead(const uint32_t* readDone, int64_t w
  *  wait on nothing) or is claimed by a CTA writing an earlier tile, whose waits are
  *  on tiles lower still, all read. */
 template <class T, bool Perm>
-__global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : 4) void placeInPlaceKernel(InPlaceArgs a)
+__global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : (sizeof(T) <= 2 ? 8 : 4)) void placeInPlaceKernel(InPlaceArgs a)
 {
     if (a.fire != nullptr && *a.fire == 0u)
         return;
