@@ -869,9 +869,11 @@ def extra_compact_sum(ctx, args, data):
            "ms_per_step": ms, "steps": 5, "warmup": 3, "dtype": "f64 values, u8 mask",
            "config": {"workload": "compact-then-sum", "n_total": n_total, "p": list(DENSITIES),
                       "path": "CompactSum (fused: the kept values are never written)" if ctx.dist is None else
-                              "ShardedCompactSum: each rank gathers its survivors; fixed-size device all-gathers "
-                              "of the counts, every rank's first 4095 survivors and the leaf partials, with the "
-                              "leaves and the rank-order fold formed on the device (no host read)",
+                              "ShardedCompactSum: each rank sums its leaves straight from the values (the "
+                              "survivors are never written); two fixed-size device all-gathers, of every rank's "
+                              "head block (its first 4095 survivors and its count) and of its partial block (its "
+                              "leaf partials and their number), with the leaves and the rank-order fold formed on "
+                              "the device (no host read)",
                       "l2": "a 256 MiB buffer is written before every call (its time is measured apart and taken "
                             "out)", "flush_ms_per_step": flush_ms,
                       "us_per_call": [round(1e3 * v, 1) for v in per_p]},

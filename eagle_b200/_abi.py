@@ -292,13 +292,15 @@ SIGNATURES = {
     "eagle_backend_compact_device": (_i32, [ctypes.POINTER(CompactDesc)]),
     "eagle_backend_x_b200_compact_device_noalloc": (_i32, [ctypes.POINTER(CompactDesc)]),
     "eagle_backend_x_b200_compact_wait_check": (_i32, [ctypes.POINTER(CompactDesc), _u32]),
-    "eagle_backend_x_b200_ragged_leaves": (_i32, [_u64, _u64, _u64, _i32, _i32, _u64, _i64, _u64, _u64]),
-    "eagle_backend_x_b200_ragged_fold": (_i32, [_u64, _u64, _i32, _i64, _u64, _u64, _u64]),
+    "eagle_backend_x_b200_ragged_head": (_i32, [_u64, _u64, _u64, _u64]),
+    "eagle_backend_x_b200_ragged_leaves": (_i32, [_u64, _u64, _i32, _i32, _u64, _i64, _u64]),
+    "eagle_backend_x_b200_ragged_fold": (_i32, [_u64, _i32, _i64, _u64, _u64, _u64]),
     "eagle_backend_x_b200_compact_sum_count": (_i32, [ctypes.POINTER(CompactDesc)]),
-    "eagle_backend_x_b200_compact_sum_leaves": (_i32, [ctypes.POINTER(CompactDesc), _u64, _u64, _i32, _i32, _u64, _u64,
+    "eagle_backend_x_b200_compact_sum_head": (_i32, [ctypes.POINTER(CompactDesc), _u64, _u64]),
+    "eagle_backend_x_b200_compact_sum_leaves": (_i32, [ctypes.POINTER(CompactDesc), _u64, _u64, _i32, _i32, _u64,
                                                        _i64]),
-    "eagle_backend_x_b200_compact_sum_straddle": (_i32, [ctypes.POINTER(CompactDesc), _u64, _u64, _i32, _i32, _u64,
-                                                         _u64]),
+    "eagle_backend_x_b200_compact_sum_straddle": (_i32, [ctypes.POINTER(CompactDesc), _u64, _i32, _i32, _u64,
+                                                         _i64]),
     "eagle_backend_reset_device": (_i32, [ctypes.POINTER(ReorderDesc)]),
     "eagle_backend_x_reduce_canonical": (_i32, [ctypes.POINTER(ReduceDesc)]),
     "eagle_backend_x_b200_entry": (_i32, [ctypes.c_char_p, _i32, ctypes.POINTER(_u64)]),

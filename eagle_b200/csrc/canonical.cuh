@@ -338,6 +338,37 @@ __device__ __forceinline__ P leafPartialAt(At at, int64_t cnt, P* s)
     return leafTree(p, live, s);
 }
 
+// ------------------------------------------------ exchange blocks across ranks
+//
+// A sum over survivors spread across ranks exchanges two fixed-size blocks per rank,
+// each in one all-gather:
+//   the head block, kLeaf doubles: the rank's first min(count, kHead) survivors at
+//     [0, kHead), its survivor count in the low 32 bits of slot kHead;
+//   the partial block, 2 cap + 2 doubles: (hi, comp) of each leaf starting in the
+//     rank's part at [2 k, 2 k + 1], the number of those leaves in the low 32 bits of
+//     slot 2 cap (all ones: a pass failed), slot 2 cap + 1 unused.
+
+constexpr int kMaxRanks = 256;
+constexpr int64_t kHead = kLeaf - 1;   // survivors a rank shares with the earlier ranks
+constexpr int64_t kHeadBlock = kLeaf;  // doubles per head block
+
+__device__ __forceinline__ uint32_t blockCount(const double* __restrict__ blocks, int q)
+{
+    return uint32_t(__double_as_longlong(blocks[int64_t(q) * kHeadBlock + kHead]));
+}
+
+__device__ __forceinline__ double blockHead(const double* __restrict__ blocks, int q, int64_t i)
+{
+    return blocks[int64_t(q) * kHeadBlock + i];
+}
+
+__device__ __forceinline__ double countSlot(uint32_t c)
+{
+    return __longlong_as_double(static_cast<long long>(c));
+}
+
+__host__ __device__ __forceinline__ int64_t partialBlock(int64_t cap) { return 2 * cap + 2; }
+
 /** Pairwise levels over ``v[0, m)`` in shared memory (an aligned subtree): node i
  *  of level L sits at i * 2^L; its right child, if present, at + 2^(L-1). */
 template <class P>

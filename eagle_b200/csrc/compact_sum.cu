@@ -759,20 +759,32 @@ SumLayout sumLayout(int64_t n)
 
 // ------------------------------------------------- the same leaves across ranks
 
-constexpr int kMaxRanks = 256;
-constexpr int64_t kHead = kLeaf - 1;  // survivors a rank shares with the earlier ranks
+/** This rank's survivor count as its passes read it (a count above n: a failed scan, none). */
+__device__ __forceinline__ int64_t ownCount(const uint32_t* count, int64_t n)
+{
+    return int64_t(*count) > n ? 0 : int64_t(*count);
+}
 
-/** One thread: this rank's RaggedPlan from every rank's count. */
-__global__ void raggedPlanKernel(const uint32_t* __restrict__ counts, int32_t rank, int32_t world,
+/** One thread: the head's length in ``plan`` (the rest of the plan needs every
+ *  rank's count) and this rank's count in its head block. */
+__global__ void headPlanKernel(const uint32_t* __restrict__ count, int64_t n, RaggedPlan* plan, double* block)
+{
+    const int64_t c = ownCount(count, n);
+    plan->headLen = c < kHead ? c : kHead;
+    block[kHead] = countSlot(uint32_t(c));
+}
+
+/** One thread: this rank's RaggedPlan from every rank's gathered head block. */
+__global__ void raggedPlanKernel(const double* __restrict__ blocks, int32_t rank, int32_t world,
     const uint32_t* __restrict__ count, int64_t n, RaggedPlan* plan)
 {
     int64_t o = 0, total = 0;
     for (int q = 0; q < world; ++q) {
         if (q < rank)
-            o += int64_t(counts[q]);
-        total += int64_t(counts[q]);
+            o += int64_t(blockCount(blocks, q));
+        total += int64_t(blockCount(blocks, q));
     }
-    const int64_t c = int64_t(*count) > n ? 0 : int64_t(*count);  // this rank's own, as its passes read it
+    const int64_t c = ownCount(count, n);
     RaggedPlan r{};
     r.offset = o;
     r.total = total;
@@ -790,70 +802,100 @@ __global__ void raggedPlanKernel(const uint32_t* __restrict__ counts, int32_t ra
     *plan = r;
 }
 
+constexpr int kSelectCtas = 32;  // CTAs of rankSelectKernel: a sparse range's tiles in one round
+
 /** The values of this rank's survivors of local ranks [r0, r1) (at most 4096) into
- *  ``out[0, r1 - r0)``: CTA 0 the head (ranks [0, headLen)), CTA 1 the straddling
- *  leaf's part here (ranks [tailStart, count)). The first tile holding rank r0 is
- *  found by a binary search over the scanned tile offsets; each warp then takes one
- *  16384-sample tile at a time and ranks its survivors from the tile's offset. */
+ *  ``out[0, r1 - r0)``: the head (``tail`` false: ranks [0, headLen)) or the
+ *  straddling leaf's part here (ranks [tailStart, count)). The first tile holding
+ *  rank r0 is found by a binary search over the scanned tile offsets; CTA b then
+ *  takes that tile + b, + b + kSelectCtas, ... while the tile starts below r1. In a
+ *  tile, thread t holds bitmap words 2t and 2t + 1 (64 samples), ranks them by a CTA
+ *  scan from the tile's offset, and loads each word's survivors in the range with 32
+ *  predicated loads issued together. */
 __global__ __launch_bounds__(kThreads) void rankSelectKernel(const uint32_t* __restrict__ bitmap,
     const uint32_t* __restrict__ tileOff, int64_t tiles, const double* __restrict__ values,
-    const RaggedPlan* __restrict__ plan, double* __restrict__ head, double* __restrict__ tail)
+    const RaggedPlan* __restrict__ plan, const uint32_t* __restrict__ count, int64_t n, bool tail,
+    double* __restrict__ out)
 {
-    __shared__ int64_t sFirst;
-    const int64_t r0 = blockIdx.x == 0 ? 0 : plan->tailStart;
-    const int64_t r1 = blockIdx.x == 0 ? plan->headLen : plan->tailStart + plan->tailLen;
-    double* out = blockIdx.x == 0 ? head : tail;
+    static_assert(kTileWords == 2 * kThreads, "two bitmap words per thread cover a tile");
+    __shared__ int64_t sLo, sHi;
+    __shared__ int sBest;
+    __shared__ uint32_t scan[33];
+    const int t = int(threadIdx.x);
+    int64_t r0 = 0, r1 = 0;
+    if (tail) {
+        r0 = plan->tailStart;
+        r1 = plan->tailStart + plan->tailLen;
+    } else {  // the head block: its length from the count, and the count into its slot
+        const int64_t c = ownCount(count, n);
+        r1 = c < kHead ? c : kHead;
+        if (blockIdx.x == 0 && t == 0)
+            out[kHead] = countSlot(uint32_t(c));
+    }
     if (r1 <= r0)
         return;
-    if (threadIdx.x == 0) {  // the last tile whose first survivor's rank is <= r0
-        int64_t lo = 0, hi = tiles - 1;
-        while (lo < hi) {
-            const int64_t mid = (lo + hi + 1) / 2;
-            if (int64_t(tileOff[mid]) <= r0)
-                lo = mid;
-            else
-                hi = mid - 1;
-        }
-        sFirst = lo;
+    // the last tile whose first survivor's rank is <= r0 (tile 0's is 0): kThreads probes
+    // per round over [lo, hi], each round narrowing it to one stride. The head (r0 = 0)
+    // starts at tile 0: any empty tiles before its first survivor are passed over below.
+    if (t == 0) {
+        sLo = 0;
+        sHi = r0 == 0 ? 0 : tiles - 1;
     }
     __syncthreads();
-    const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
-    for (int64_t tile = sFirst + warp; tile < tiles && int64_t(tileOff[tile]) < r1; tile += kThreads / 32) {
-        const uint4* src = reinterpret_cast<const uint4*>(bitmap + tile * kTileWords) + lane * 4;
-        uint32_t w[16];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint4 x = src[k];
-            w[4 * k] = x.x;
-            w[4 * k + 1] = x.y;
-            w[4 * k + 2] = x.z;
-            w[4 * k + 3] = x.w;
+    while (sHi > sLo) {
+        const int64_t lo = sLo, hi = sHi;
+        const int64_t step = (hi - lo + kThreads) / kThreads;  // ceil((hi - lo + 1) / kThreads)
+        if (t == 0)
+            sBest = 0;
+        __syncthreads();
+        const int64_t at = lo + int64_t(t) * step;
+        if (t > 0 && at <= hi && int64_t(tileOff[at]) <= r0)
+            atomicMax(&sBest, t);
+        __syncthreads();
+        if (t == 0) {
+            sLo = lo + int64_t(sBest) * step;
+            sHi = sLo + step - 1 < hi ? sLo + step - 1 : hi;
         }
-        uint32_t mine = 0;
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-            mine += uint32_t(__popc(w[k]));
-        int64_t r = int64_t(tileOff[tile]) + int64_t(warpInclusiveSum(mine) - mine);  // the lane's first rank
+        __syncthreads();
+    }
+    const int64_t first = sLo;
+    for (int64_t tile = first + blockIdx.x; tile < tiles && int64_t(tileOff[tile]) < r1; tile += gridDim.x) {
+        const uint2 w = reinterpret_cast<const uint2*>(bitmap + tile * kTileWords)[t];
+        const uint32_t mine = uint32_t(__popc(w.x) + __popc(w.y));
+        uint32_t total = 0;
+        const uint32_t excl = blockExclusiveSum(mine, total, scan);
+        int64_t r = int64_t(tileOff[tile]) + int64_t(excl);  // the thread's first survivor's rank
         if (r >= r1 || r + int64_t(mine) <= r0)
             continue;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const int64_t sample0 = (tile * kTileWords + lane * 16 + k) * 32;
-            for (uint32_t x = w[k]; x != 0; x &= x - 1u, ++r)
-                if (r >= r0 && r < r1)
-                    out[r - r0] = values[sample0 + (__ffs(int(x)) - 1)];
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t x = k == 0 ? w.x : w.y;
+            const int64_t sample0 = (tile * kTileWords + 2 * t + k) * 32;
+            double v[32];
+#pragma unroll
+            for (int b = 0; b < 32; ++b) {
+                const int64_t rb = r + __popc(x & ((1u << b) - 1u));
+                v[b] = ((x >> b) & 1u) && rb >= r0 && rb < r1 ? values[sample0 + b] : 0.0;
+            }
+#pragma unroll
+            for (int b = 0; b < 32; ++b) {
+                const int64_t rb = r + __popc(x & ((1u << b) - 1u));
+                if (((x >> b) & 1u) && rb >= r0 && rb < r1)
+                    out[rb - r0] = v[b];
+            }
+            r += __popc(x);
         }
     }
 }
 
 /** One CTA: the leaf that starts here and runs into the later ranks, from this
- *  rank's part (``tail``) and the later ranks' gathered heads, at partials index
- *  full - first; then this rank's leaf count (all of 0xffffffff when a pass reported
- *  an error, so that the fold gives NaN). */
+ *  rank's part (``tail``) and the later ranks' gathered head blocks, at partials
+ *  index full - first; then this rank's leaf count into the partial block's count
+ *  slot (all of 0xffffffff when a pass reported an error, so that the fold gives
+ *  NaN). */
 __global__ __launch_bounds__(kSlots) void straddleKernel(const RaggedPlan* __restrict__ plan,
-    const uint32_t* __restrict__ counts, const double* __restrict__ heads, int32_t rank, int32_t world,
-    const double* __restrict__ tail, const uint32_t* __restrict__ err, double* __restrict__ partials,
-    uint32_t* __restrict__ leafCount)
+    const double* __restrict__ blocks, int32_t rank, int32_t world, const double* __restrict__ tail,
+    const uint32_t* __restrict__ err, double* __restrict__ partials, int64_t cap)
 {
     __shared__ int64_t sOff[kMaxRanks + 1];
     __shared__ P s[kSlots];
@@ -861,7 +903,7 @@ __global__ __launch_bounds__(kSlots) void straddleKernel(const RaggedPlan* __res
         int64_t o = 0;
         for (int q = 0; q < world; ++q) {
             sOff[q] = o;
-            o += int64_t(counts[q]);
+            o += int64_t(blockCount(blocks, q));
         }
         sOff[world] = o;
     }
@@ -878,7 +920,7 @@ __global__ __launch_bounds__(kSlots) void straddleKernel(const RaggedPlan* __res
             int q = rank + 1;  // the later rank holding g: g - sOff[q] < kHead
             while (q + 1 < world && g >= sOff[q + 1])
                 ++q;
-            return heads[int64_t(q) * kHead + (g - sOff[q])];
+            return blockHead(blocks, q, g - sOff[q]);
         };
         const P q = leafPartialAt<P, double>(at, cnt, s);
         if (threadIdx.x == 0) {
@@ -887,7 +929,7 @@ __global__ __launch_bounds__(kSlots) void straddleKernel(const RaggedPlan* __res
         }
     }
     if (threadIdx.x == 0)
-        *leafCount = *err != 0u ? 0xffffffffu : uint32_t(own + r.straddle);
+        partials[2 * cap] = countSlot(*err != 0u ? 0xffffffffu : uint32_t(own + r.straddle));
 }
 
 }  // namespace
@@ -1033,8 +1075,36 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_count(struct eagle_
     });
 }
 
+EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_head(struct eagle_backend_compact_desc* desc,
+    uint64_t values, uint64_t block)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_compact_sum_head";
+        const auto d = readDesc(desc, EAGLE_BACKEND_COMPACT_MASK_IS_DROP, who);
+        const SumLayout L = checkSplit(d, who);
+        if (block == 0 || (d.n > 0 && values == 0))
+            invalid(std::string(who) + ": values and block must be device addresses");
+        if ((values & 7u) != 0 || (block & 7u) != 0)
+            invalid(std::string(who) + ": values and block must be 8-byte aligned float64 arrays");
+        DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
+        const cudaStream_t s = seamStream(d.stream);
+        char* base = reinterpret_cast<char*>(d.scratch);
+        auto* plan = reinterpret_cast<RaggedPlan*>(base + L.plan);
+        if (d.n == 0) {
+            headPlanKernel<<<1, 1, 0, s>>>(reinterpret_cast<const uint32_t*>(d.count), d.n, plan,
+                reinterpret_cast<double*>(block));
+            launchCheck(who);
+            return;
+        }
+        rankSelectKernel<<<kSelectCtas, kThreads, 0, s>>>(reinterpret_cast<const uint32_t*>(base + L.t.bitmap),
+            reinterpret_cast<const uint32_t*>(base + L.t.off), L.t.tiles, reinterpret_cast<const double*>(values),
+            plan, reinterpret_cast<const uint32_t*>(d.count), d.n, false, reinterpret_cast<double*>(block));
+        launchCheck(who);
+    });
+}
+
 EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_leaves(struct eagle_backend_compact_desc* desc,
-    uint64_t values, uint64_t counts, int32_t rank, int32_t world, uint64_t head, uint64_t partials, int64_t cap)
+    uint64_t values, uint64_t blocks, int32_t rank, int32_t world, uint64_t partials, int64_t cap)
 {
     return guarded([&] {
         constexpr const char* who = "eagle_backend_x_b200_compact_sum_leaves";
@@ -1042,8 +1112,8 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_leaves(struct eagle
         const SumLayout L = checkSplit(d, who);
         if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
             invalid(std::string(who) + ": need 0 <= rank < world <= 256");
-        if (counts == 0 || head == 0 || partials == 0 || (d.n > 0 && values == 0))
-            invalid(std::string(who) + ": values, counts, head and partials must be device addresses");
+        if (blocks == 0 || partials == 0 || (d.n > 0 && values == 0))
+            invalid(std::string(who) + ": values, blocks and partials must be device addresses");
         if ((values & 7u) != 0)
             invalid(std::string(who) + ": values must be an 8-byte aligned float64 array");
         if (cap < L.maxLeaves + 1)
@@ -1052,7 +1122,7 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_leaves(struct eagle
         const cudaStream_t s = seamStream(d.stream);
         char* base = reinterpret_cast<char*>(d.scratch);
         auto* plan = reinterpret_cast<RaggedPlan*>(base + L.plan);
-        raggedPlanKernel<<<1, 1, 0, s>>>(reinterpret_cast<const uint32_t*>(counts), rank, world,
+        raggedPlanKernel<<<1, 1, 0, s>>>(reinterpret_cast<const double*>(blocks), rank, world,
             reinterpret_cast<const uint32_t*>(d.count), d.n, plan);
         launchCheck(who);
         if (d.n == 0)
@@ -1091,14 +1161,15 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_leaves(struct eagle
         launchCheck(who);
         keptSparseKernel<<<unsigned(passGrid(1)), kThreads, 0, s>>>(la);
         launchCheck(who);
-        rankSelectKernel<<<2, kThreads, 0, s>>>(bitmap, tileOff, L.t.tiles, reinterpret_cast<const double*>(values),
-            plan, reinterpret_cast<double*>(head), reinterpret_cast<double*>(base + L.tail));
+        rankSelectKernel<<<kSelectCtas, kThreads, 0, s>>>(bitmap, tileOff, L.t.tiles,
+            reinterpret_cast<const double*>(values), plan, la.count, d.n, true,
+            reinterpret_cast<double*>(base + L.tail));
         launchCheck(who);
     });
 }
 
 EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_straddle(struct eagle_backend_compact_desc* desc,
-    uint64_t counts, uint64_t heads, int32_t rank, int32_t world, uint64_t partials, uint64_t leaf_count)
+    uint64_t blocks, int32_t rank, int32_t world, uint64_t partials, int64_t cap)
 {
     return guarded([&] {
         constexpr const char* who = "eagle_backend_x_b200_compact_sum_straddle";
@@ -1106,15 +1177,16 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum_straddle(struct eag
         const SumLayout L = checkSplit(d, who);
         if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
             invalid(std::string(who) + ": need 0 <= rank < world <= 256");
-        if (counts == 0 || heads == 0 || partials == 0 || leaf_count == 0)
-            invalid(std::string(who) + ": counts, heads, partials and leaf_count must be device addresses");
+        if (blocks == 0 || partials == 0)
+            invalid(std::string(who) + ": blocks and partials must be device addresses");
+        if (cap < L.maxLeaves + 1)
+            invalid(std::string(who) + ": cap must be at least ceil(n / 4096) + 1 leaves");
         DeviceScope scope(resolveDevice(d.device, d.mask != 0 ? d.mask : d.count));
         const cudaStream_t s = seamStream(d.stream);
         char* base = reinterpret_cast<char*>(d.scratch);
         straddleKernel<<<1, kSlots, 0, s>>>(reinterpret_cast<const RaggedPlan*>(base + L.plan),
-            reinterpret_cast<const uint32_t*>(counts), reinterpret_cast<const double*>(heads), rank, world,
-            reinterpret_cast<const double*>(base + L.tail), reinterpret_cast<const uint32_t*>(base) + 2,
-            reinterpret_cast<double*>(partials), reinterpret_cast<uint32_t*>(leaf_count));
+            reinterpret_cast<const double*>(blocks), rank, world, reinterpret_cast<const double*>(base + L.tail),
+            reinterpret_cast<const uint32_t*>(base) + 2, reinterpret_cast<double*>(partials), cap);
         launchCheck(who);
     });
 }

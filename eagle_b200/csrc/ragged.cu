@@ -6,10 +6,12 @@
 // of the whole batch, and its canonical sum is the pairwise tree over 4096-survivor
 // leaves of that concatenation (eagle/reduce/canonical.h:10-32). Rank r starts at
 // o_r = c_0 + ... + c_{r-1}, which no rank knows before the counts are exchanged, so
-// a rank's leaves are not aligned to its own survivors. The exchange here is three
-// fixed-size all-gathers (every rank's count, its first 4095 survivors, its leaf
-// partials) around two kernels that read the gathered counts on the device:
+// a rank's leaves are not aligned to its own survivors. The exchange here is two
+// fixed-size all-gathers -- every rank's head block (its first 4095 survivors and its
+// count), then its partial block (its leaf partials and their number) -- around
+// kernels that read the gathered blocks on the device:
 //
+//   raggedHeadKernel    this rank's head block from its survivors;
 //   raggedLeavesKernel  one CTA per leaf that STARTS in this rank's part: the leaf's
 //                       survivors come from this rank, and past its end from the
 //                       next ranks' gathered heads (a leaf that starts here ends
@@ -27,18 +29,25 @@
 namespace eb {
 namespace {
 
-constexpr int kHead = int(kLeaf) - 1;  // survivors a rank shares with the earlier ranks
-constexpr int kMaxRanks = 256;
-
 struct RaggedLeavesArgs {
-    const double* kept;      // this rank's survivors, sample order
-    const uint32_t* counts;  // every rank's survivor count (gathered)
-    const double* heads;     // every rank's first kHead survivors (gathered), [world][kHead]
+    const double* kept;    // this rank's survivors, sample order
+    const double* blocks;  // every rank's head block (gathered), [world][kHeadBlock]
     int32_t rank, world;
-    double* partials;        // out: (hi, comp) of each leaf starting in this rank's part
-    int64_t cap;             // leaves ``partials`` holds
-    uint32_t* leafCount;     // out: leaves starting in this rank's part
+    double* partials;      // out: this rank's partial block (partialBlock(cap) doubles)
+    int64_t cap;           // leaves the partial block holds
 };
+
+/** This rank's head block: its first min(count, kHead) survivors and its count. */
+__global__ __launch_bounds__(256) void raggedHeadKernel(const double* __restrict__ kept,
+    const uint32_t* __restrict__ count, double* __restrict__ block)
+{
+    const uint32_t c = *count;
+    const int64_t len = int64_t(c) < kHead ? int64_t(c) : kHead;
+    for (int64_t i = threadIdx.x; i < len; i += blockDim.x)
+        block[i] = kept[i];
+    if (threadIdx.x == 0)
+        block[kHead] = countSlot(c);
+}
 
 __global__ __launch_bounds__(kSlots) void raggedLeavesKernel(RaggedLeavesArgs a)
 {
@@ -48,7 +57,7 @@ __global__ __launch_bounds__(kSlots) void raggedLeavesKernel(RaggedLeavesArgs a)
         int64_t o = 0;
         for (int q = 0; q < a.world; ++q) {
             sOff[q] = o;
-            o += int64_t(a.counts[q]);
+            o += int64_t(blockCount(a.blocks, q));
         }
         sOff[a.world] = o;
     }
@@ -57,13 +66,13 @@ __global__ __launch_bounds__(kSlots) void raggedLeavesKernel(RaggedLeavesArgs a)
     const int64_t first = (mine + kLeaf - 1) / kLeaf;  // the first leaf starting at or after ``mine``
     const int64_t leaves = end > first * kLeaf ? (end - first * kLeaf + kLeaf - 1) / kLeaf : 0;
     if (blockIdx.x == 0 && threadIdx.x == 0)
-        *a.leafCount = uint32_t(leaves);  // above cap: the fold reports the overflow
+        a.partials[2 * a.cap] = countSlot(uint32_t(leaves));  // above cap: the fold reports the overflow
     const int64_t k = blockIdx.x;
     if (k >= leaves || k >= a.cap)
         return;
     const int64_t start = (first + k) * kLeaf;  // global position of the leaf's first survivor
     const int64_t cnt = total - start < kLeaf ? total - start : kLeaf;
-    const double* heads = a.heads;
+    const double* blocks = a.blocks;
     const int32_t rank = a.rank, world = a.world;
     CompP<double> p;
     if (start + cnt <= end) {  // the whole leaf is this rank's (every leaf but the last)
@@ -78,7 +87,7 @@ __global__ __launch_bounds__(kSlots) void raggedLeavesKernel(RaggedLeavesArgs a)
             int q = rank + 1;  // a later rank's head: g - sOff[q] < kHead for the rank holding g
             while (q + 1 < world && g >= sOff[q + 1])
                 ++q;
-            return heads[int64_t(q) * kHead + (g - sOff[q])];
+            return blockHead(blocks, q, g - sOff[q]);
         };
         p = leafPartialAt<CompP<double>, double>(at, cnt, s);
     }
@@ -88,18 +97,25 @@ __global__ __launch_bounds__(kSlots) void raggedLeavesKernel(RaggedLeavesArgs a)
     }
 }
 
+/** Rank q's leaf count from the gathered partial blocks. */
+__device__ __forceinline__ int64_t leafCountOf(const double* __restrict__ gathered, int q, int64_t cap)
+{
+    return int64_t(uint32_t(__double_as_longlong(gathered[int64_t(q) * partialBlock(cap) + 2 * cap])));
+}
+
 /** Rank q's first leaf in the whole order (sFirst[q]; sFirst[world] = all leaves) and
  *  whether some rank formed more leaves than ``cap`` holds, in shared memory. */
-__device__ __forceinline__ void leafOrigins(const uint32_t* __restrict__ leafCounts, int32_t world, int64_t cap,
+__device__ __forceinline__ void leafOrigins(const double* __restrict__ gathered, int32_t world, int64_t cap,
     int64_t* sFirst, int* sOver)
 {
     if (threadIdx.x == 0) {
         int64_t o = 0;
         int over = 0;
         for (int q = 0; q < world; ++q) {
+            const int64_t k = leafCountOf(gathered, q, cap);
             sFirst[q] = o;
-            o += int64_t(leafCounts[q]);
-            over |= int64_t(leafCounts[q]) > cap ? 1 : 0;
+            o += k;
+            over |= k > cap ? 1 : 0;
         }
         sFirst[world] = o;
         *sOver = over;
@@ -108,15 +124,15 @@ __device__ __forceinline__ void leafOrigins(const uint32_t* __restrict__ leafCou
 }
 
 /** The first level of the fold: CTA c joins leaves [512 c, 512 c + 512) of the whole
- *  order (rank q's ``leafCounts[q]`` partials sit at ``gathered + 2 cap q``) by the
- *  pairwise levels into work[2 c, 2 c + 1]. */
-__global__ __launch_bounds__(kSlots) void raggedChunkKernel(const double* __restrict__ gathered,
-    const uint32_t* __restrict__ leafCounts, int32_t world, int64_t cap, double* __restrict__ work)
+ *  order (rank q's partials lead its block at ``gathered + partialBlock(cap) q``) by
+ *  the pairwise levels into work[2 c, 2 c + 1]. */
+__global__ __launch_bounds__(kSlots) void raggedChunkKernel(const double* __restrict__ gathered, int32_t world,
+    int64_t cap, double* __restrict__ work)
 {
     __shared__ CompP<double> v[kChunk];
     __shared__ int64_t sFirst[kMaxRanks + 1];
     __shared__ int sOver;
-    leafOrigins(leafCounts, world, cap, sFirst, &sOver);
+    leafOrigins(gathered, world, cap, sFirst, &sOver);
     const int64_t count = sFirst[world];
     const int64_t c = blockIdx.x;
     if (sOver != 0 || c * kChunk >= count)
@@ -127,7 +143,7 @@ __global__ __launch_bounds__(kSlots) void raggedChunkKernel(const double* __rest
         int q = 0;  // the rank whose leaves hold j
         while (q + 1 < world && j >= sFirst[q + 1])
             ++q;
-        const double* src = gathered + 2 * (cap * q + (j - sFirst[q]));
+        const double* src = gathered + partialBlock(cap) * q + 2 * (j - sFirst[q]);
         v[i] = CompP<double>{src[0], src[1]};
     }
     __syncthreads();
@@ -140,13 +156,13 @@ __global__ __launch_bounds__(kSlots) void raggedChunkKernel(const double* __rest
 
 /** The levels above the chunks, one CTA: out = {hi, comp, value}; no leaves: zeros;
  *  some rank's leaves past ``cap``: NaN. */
-__global__ __launch_bounds__(kSlots) void raggedTopKernel(const uint32_t* __restrict__ leafCounts, int32_t world,
+__global__ __launch_bounds__(kSlots) void raggedTopKernel(const double* __restrict__ gathered, int32_t world,
     int64_t cap, double* __restrict__ work, double* __restrict__ out)
 {
     __shared__ CompP<double> v[kChunk];
     __shared__ int64_t sFirst[kMaxRanks + 1];
     __shared__ int sOver;
-    leafOrigins(leafCounts, world, cap, sFirst, &sOver);
+    leafOrigins(gathered, world, cap, sFirst, &sOver);
     if (sOver != 0) {  // some rank formed more leaves than ``cap`` holds: no valid sum
         if (threadIdx.x == 0)
             out[0] = out[1] = out[2] = __longlong_as_double(0x7ff8000000000000ll);
@@ -187,8 +203,23 @@ __global__ __launch_bounds__(kSlots) void raggedTopKernel(const uint32_t* __rest
 
 using namespace eb;
 
-EB_API eagle_backend_status eagle_backend_x_b200_ragged_leaves(uint64_t kept, uint64_t counts, uint64_t heads,
-    int32_t rank, int32_t world, uint64_t partials, int64_t cap, uint64_t leaf_count, uint64_t stream)
+EB_API eagle_backend_status eagle_backend_x_b200_ragged_head(uint64_t kept, uint64_t count, uint64_t block,
+    uint64_t stream)
+{
+    return guarded([&] {
+        constexpr const char* who = "eagle_backend_x_b200_ragged_head";
+        if (count == 0 || block == 0)
+            invalid(std::string(who) + ": count and block must be device addresses");
+        if ((kept & 7u) != 0 || (block & 7u) != 0)
+            invalid(std::string(who) + ": kept and block must be 8-byte aligned float64 arrays");
+        raggedHeadKernel<<<1, 256, 0, seamStream(stream)>>>(reinterpret_cast<const double*>(kept),
+            reinterpret_cast<const uint32_t*>(count), reinterpret_cast<double*>(block));
+        launchCheck(who);
+    });
+}
+
+EB_API eagle_backend_status eagle_backend_x_b200_ragged_leaves(uint64_t kept, uint64_t blocks, int32_t rank,
+    int32_t world, uint64_t partials, int64_t cap, uint64_t stream)
 {
     return guarded([&] {
         constexpr const char* who = "eagle_backend_x_b200_ragged_leaves";
@@ -196,24 +227,22 @@ EB_API eagle_backend_status eagle_backend_x_b200_ragged_leaves(uint64_t kept, ui
             invalid(std::string(who) + ": need 0 <= rank < world <= 256");
         if (cap < 1 || cap > (INT64_C(1) << 31))
             invalid(std::string(who) + ": cap must lie in [1, 2^31]");
-        if (counts == 0 || heads == 0 || partials == 0 || leaf_count == 0)
-            invalid(std::string(who) + ": counts, heads, partials and leaf_count must be device addresses");
+        if (blocks == 0 || partials == 0)
+            invalid(std::string(who) + ": blocks and partials must be device addresses");
         RaggedLeavesArgs a{};
         a.kept = reinterpret_cast<const double*>(kept);
-        a.counts = reinterpret_cast<const uint32_t*>(counts);
-        a.heads = reinterpret_cast<const double*>(heads);
+        a.blocks = reinterpret_cast<const double*>(blocks);
         a.rank = rank;
         a.world = world;
         a.partials = reinterpret_cast<double*>(partials);
         a.cap = cap;
-        a.leafCount = reinterpret_cast<uint32_t*>(leaf_count);
         raggedLeavesKernel<<<unsigned(cap), kSlots, 0, seamStream(stream)>>>(a);
         launchCheck(who);
     });
 }
 
-EB_API eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, uint64_t leaf_counts, int32_t world,
-    int64_t cap, uint64_t work, uint64_t out, uint64_t stream)
+EB_API eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, int32_t world, int64_t cap,
+    uint64_t work, uint64_t out, uint64_t stream)
 {
     return guarded([&] {
         constexpr const char* who = "eagle_backend_x_b200_ragged_fold";
@@ -221,14 +250,14 @@ EB_API eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, 
             invalid(std::string(who) + ": world must lie in [1, 256]");
         if (cap < 1)
             invalid(std::string(who) + ": cap must be >= 1");
-        if (gathered == 0 || leaf_counts == 0 || work == 0 || out == 0)
-            invalid(std::string(who) + ": gathered, leaf_counts, work and out must be device addresses");
+        if (gathered == 0 || work == 0 || out == 0)
+            invalid(std::string(who) + ": gathered, work and out must be device addresses");
         const cudaStream_t s = seamStream(stream);
         const int64_t chunks = (int64_t(world) * cap + kChunk - 1) / kChunk;  // at most; idle CTAs leave at once
-        raggedChunkKernel<<<unsigned(chunks), kSlots, 0, s>>>(reinterpret_cast<const double*>(gathered),
-            reinterpret_cast<const uint32_t*>(leaf_counts), world, cap, reinterpret_cast<double*>(work));
+        raggedChunkKernel<<<unsigned(chunks), kSlots, 0, s>>>(reinterpret_cast<const double*>(gathered), world, cap,
+            reinterpret_cast<double*>(work));
         launchCheck(who);
-        raggedTopKernel<<<1, kSlots, 0, s>>>(reinterpret_cast<const uint32_t*>(leaf_counts), world, cap,
+        raggedTopKernel<<<1, kSlots, 0, s>>>(reinterpret_cast<const double*>(gathered), world, cap,
             reinterpret_cast<double*>(work), reinterpret_cast<double*>(out));
         launchCheck(who);
     });

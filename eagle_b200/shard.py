@@ -236,15 +236,17 @@ def compact_sum_sharded(mask, values, *, drop: bool = False, group=None):
 class ShardedCompactSum:
     """The canonical sum of every rank's survivors as ONE concatenation in rank order,
     prepared once per shard and run with no host round trip and without writing the
-    survivors out: each call runs the fused compact-then-sum's front end on this
-    rank's shard (``eagle_backend_x_b200_compact_sum_count``), all-gathers the
-    survivor counts, sums every leaf of the concatenation that starts and ends here
-    straight from the values (``_compact_sum_leaves``, planned on the device from the
-    gathered counts), all-gathers every rank's first ``LEAF - 1`` survivors, sums the
-    leaf that straddles into the later ranks (``_compact_sum_straddle``), all-gathers
-    the leaf partials and folds them in rank order (``eagle_backend_x_b200_ragged_fold``).
-    Every collective moves a fixed number of bytes. Returns ``(hi, comp, value)`` on
-    every rank: the bits of the one-device compact-then-sum of the concatenated shards."""
+    survivors out. Each call runs the fused compact-then-sum's front end on this rank's
+    shard (``eagle_backend_x_b200_compact_sum_count``) and forms the rank's head block
+    -- its first ``LEAF - 1`` survivors and its count (``_compact_sum_head``) -- then
+    all-gathers the head blocks; sums every leaf of the concatenation that starts here
+    straight from the values, the one running into the later ranks from their heads
+    (``_compact_sum_leaves``, ``_compact_sum_straddle``, planned on the device from
+    the gathered counts); all-gathers the partial blocks (the leaf partials and their
+    number) and folds them in rank order (``eagle_backend_x_b200_ragged_fold``). Two
+    collectives per call, each of a fixed number of bytes. Returns ``(hi, comp,
+    value)`` on every rank: the bits of the one-device compact-then-sum of the
+    concatenated shards."""
 
     def __init__(self, mask, values, *, drop: bool = False, group=None):
         import torch
@@ -260,13 +262,10 @@ class ShardedCompactSum:
         dev = mask.device
         n = mask.numel()
         self.cap = (n + LEAF - 1) // LEAF + 1
-        self.counts = torch.zeros(self.world, dtype=torch.int32, device=dev)
-        self.head = torch.zeros(LEAF - 1, dtype=torch.float64, device=dev)
-        self.heads = torch.zeros(self.world * (LEAF - 1), dtype=torch.float64, device=dev)
-        self.partials = torch.zeros(2 * self.cap, dtype=torch.float64, device=dev)
-        self.leaf_count = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.all_partials = torch.zeros(self.world * 2 * self.cap, dtype=torch.float64, device=dev)
-        self.all_leaf_counts = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        self.block = torch.zeros(LEAF, dtype=torch.float64, device=dev)
+        self.blocks = torch.zeros(self.world * LEAF, dtype=torch.float64, device=dev)
+        self.partials = torch.zeros(2 * self.cap + 2, dtype=torch.float64, device=dev)
+        self.all_partials = torch.zeros(self.world * (2 * self.cap + 2), dtype=torch.float64, device=dev)
         self.work = torch.zeros(2 * ((self.world * self.cap + 511) // 512) + 2, dtype=torch.float64, device=dev)
         self.out = torch.zeros(3, dtype=torch.float64, device=dev)
 
@@ -281,19 +280,17 @@ class ShardedCompactSum:
         d = self.cs.sdesc
         d.stream = s
         _abi.check(lib.eagle_backend_x_b200_compact_sum_count(ctypes.byref(d)))
-        dist.all_gather_into_tensor(self.counts, self.cs.count, group=self.group)
+        _abi.check(lib.eagle_backend_x_b200_compact_sum_head(ctypes.byref(d), self.values.data_ptr(),
+                                                              self.block.data_ptr()))
+        dist.all_gather_into_tensor(self.blocks, self.block, group=self.group)
         _abi.check(lib.eagle_backend_x_b200_compact_sum_leaves(
-            ctypes.byref(d), self.values.data_ptr(), self.counts.data_ptr(), self.rank, self.world,
-            self.head.data_ptr(), self.partials.data_ptr(), self.cap))
-        dist.all_gather_into_tensor(self.heads, self.head, group=self.group)
+            ctypes.byref(d), self.values.data_ptr(), self.blocks.data_ptr(), self.rank, self.world,
+            self.partials.data_ptr(), self.cap))
         _abi.check(lib.eagle_backend_x_b200_compact_sum_straddle(
-            ctypes.byref(d), self.counts.data_ptr(), self.heads.data_ptr(), self.rank, self.world,
-            self.partials.data_ptr(), self.leaf_count.data_ptr()))
+            ctypes.byref(d), self.blocks.data_ptr(), self.rank, self.world, self.partials.data_ptr(), self.cap))
         dist.all_gather_into_tensor(self.all_partials, self.partials, group=self.group)
-        dist.all_gather_into_tensor(self.all_leaf_counts, self.leaf_count, group=self.group)
         _abi.check(lib.eagle_backend_x_b200_ragged_fold(
-            self.all_partials.data_ptr(), self.all_leaf_counts.data_ptr(), self.world, self.cap,
-            self.work.data_ptr(), self.out.data_ptr(), s))
+            self.all_partials.data_ptr(), self.world, self.cap, self.work.data_ptr(), self.out.data_ptr(), s))
         return self.out
 
 

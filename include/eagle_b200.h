@@ -614,41 +614,50 @@ eagle_backend_status eagle_backend_pointer_residency(int32_t device, uint64_t pt
 /* The canonical sum of a compaction's survivors over several ranks with no host round
  * trip (this backend's addition; eagle folds per-rank partials of aligned shards in
  * rank order, eagle/exec/RankPartition.h:222-241, and has no ragged case). Rank r
- * holds ``kept`` = its c_r survivors in sample order; ``counts`` = every rank's
- * uint32 count and ``heads`` = every rank's first 4095 survivors ([world][4095]
- * float64), both all-gathered in rank order. ragged_leaves writes the (hi, comp)
- * partial of each 4096-survivor leaf of the concatenation that STARTS in rank r's
- * part (its survivors past rank r's end taken from the later ranks' heads) into
- * ``partials`` (2 * cap doubles) and their number into ``leaf_count`` (uint32). */
-eagle_backend_status eagle_backend_x_b200_ragged_leaves(uint64_t kept, uint64_t counts, uint64_t heads,
-    int32_t rank, int32_t world, uint64_t partials, int64_t cap, uint64_t leaf_count, uint64_t stream);
-/* ragged_fold: every rank's leaf partials (``gathered`` = [world][cap][2], all-gathered)
- * and leaf counts (``leaf_counts``, uint32[world]) through the canonical pairwise
- * levels, in rank order, into ``out`` = {hi, comp, value} (zeros for no survivors):
- * the bits of the one-device compact-then-sum of the concatenated shards. A rank whose
- * leaves did not fit its ``cap`` (ceil(shard samples / 4096) always fit) makes every
- * rank's ``out`` NaN. ``work`` holds 2 * ceil(world * cap / 512) + 2 doubles. */
-eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, uint64_t leaf_counts, int32_t world,
-    int64_t cap, uint64_t work, uint64_t out, uint64_t stream);
+ * holds ``kept`` = its c_r survivors in sample order. Two fixed-size blocks per rank
+ * cross the ranks, each in one all-gather in rank order:
+ *   the head block, 4096 float64: the rank's first min(c_r, 4095) survivors, then
+ *     c_r as a uint32 in the low 32 bits of element 4095;
+ *   the partial block, 2 * cap + 2 float64: the (hi, comp) partial of each leaf that
+ *     starts in the rank's part, then their number as a uint32 in the low 32 bits of
+ *     element 2 * cap (0xffffffff: a pass failed), element 2 * cap + 1 unused.
+ * ragged_head writes rank r's head block (``count`` = c_r, uint32, on the device).
+ * ragged_leaves reads ``blocks`` = every rank's head block ([world][4096]) and writes
+ * rank r's partial block: every 4096-survivor leaf of the concatenation that STARTS in
+ * rank r's part, its survivors past rank r's end taken from the later ranks' heads. */
+eagle_backend_status eagle_backend_x_b200_ragged_head(uint64_t kept, uint64_t count, uint64_t block,
+    uint64_t stream);
+eagle_backend_status eagle_backend_x_b200_ragged_leaves(uint64_t kept, uint64_t blocks, int32_t rank,
+    int32_t world, uint64_t partials, int64_t cap, uint64_t stream);
+/* ragged_fold: every rank's partial block (``gathered`` = [world][2 * cap + 2],
+ * all-gathered) through the canonical pairwise levels, in rank order, into ``out`` =
+ * {hi, comp, value} (zeros for no survivors): the bits of the one-device
+ * compact-then-sum of the concatenated shards. A rank whose leaves did not fit its
+ * ``cap`` (ceil(shard samples / 4096) + 1 always fit) makes every rank's ``out`` NaN.
+ * ``work`` holds 2 * ceil(world * cap / 512) + 2 doubles. */
+eagle_backend_status eagle_backend_x_b200_ragged_fold(uint64_t gathered, int32_t world, int64_t cap,
+    uint64_t work, uint64_t out, uint64_t stream);
 
 /* compact-then-sum across ranks without writing the survivors (this backend's addition,
- * the fused form of ragged_leaves): x_b200_compact_sum cut where the ranks exchange.
- * Same desc and scratch as x_b200_compact_sum (query there). _count: the keep bitmap,
- * the tile counts and this rank's count (to ``count``); the caller all-gathers the
- * counts into ``counts`` (uint32[world], rank order). _leaves (once per _count): from
- * ``counts`` on the device, the (hi, comp) partial of every leaf of the concatenated
- * survivors that starts and ends in this rank, into ``partials`` (2 * cap doubles, cap
- * >= ceil(n / 4096) + 1) from index 0, and this rank's first min(count, 4095)
- * survivors into ``head`` (4095 doubles); the caller all-gathers the heads into
- * ``heads`` ([world][4095]). _straddle: the leaf that starts here and runs into the
- * later ranks, from this rank's part and ``heads``, after those partials, and the
- * rank's leaf count into ``leaf_count`` (uint32; 0xffffffff after a pass error). The
- * partials and counts then go through eagle_backend_x_b200_ragged_fold. */
+ * the fused form of ragged_head / ragged_leaves): x_b200_compact_sum cut where the ranks
+ * exchange, with the same two blocks. Same desc and scratch as x_b200_compact_sum
+ * (query there). _count: the keep bitmap, the tile counts and this rank's count (to
+ * ``count``). _head (after _count): this rank's head block into ``block`` (4096
+ * doubles); the caller all-gathers the head blocks into ``blocks`` ([world][4096],
+ * rank order). _leaves (once per _count): from ``blocks`` on the device, the (hi, comp)
+ * partial of every leaf of the concatenated survivors that starts and ends in this
+ * rank, into ``partials`` (the partial block, 2 * cap + 2 doubles, cap >=
+ * ceil(n / 4096) + 1) from index 0. _straddle: the leaf that starts here and runs into
+ * the later ranks, from this rank's part and the later ranks' heads, after those
+ * partials, and the block's leaf count. The partial blocks then go through
+ * eagle_backend_x_b200_ragged_fold. */
 eagle_backend_status eagle_backend_x_b200_compact_sum_count(struct eagle_backend_compact_desc* desc);
+eagle_backend_status eagle_backend_x_b200_compact_sum_head(struct eagle_backend_compact_desc* desc,
+    uint64_t values, uint64_t block);
 eagle_backend_status eagle_backend_x_b200_compact_sum_leaves(struct eagle_backend_compact_desc* desc,
-    uint64_t values, uint64_t counts, int32_t rank, int32_t world, uint64_t head, uint64_t partials, int64_t cap);
+    uint64_t values, uint64_t blocks, int32_t rank, int32_t world, uint64_t partials, int64_t cap);
 eagle_backend_status eagle_backend_x_b200_compact_sum_straddle(struct eagle_backend_compact_desc* desc,
-    uint64_t counts, uint64_t heads, int32_t rank, int32_t world, uint64_t partials, uint64_t leaf_count);
+    uint64_t blocks, int32_t rank, int32_t world, uint64_t partials, int64_t cap);
 
 /* eagle_backend_x_b200_compact_wait_check: compact_device with its first tile withheld,
  * to exercise the bounded look-back wait (this backend's addition; eagle's multi-level

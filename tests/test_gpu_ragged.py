@@ -1,12 +1,12 @@
 """The device-side ragged exchange of compact-then-sum on one GPU, with the ranks
 emulated: the batch is split into W shards, each shard compacted on its own, the
-counts and heads stacked as the all-gathers would stack them, then every rank's
-leaves and the rank-order fold (eagle_backend_x_b200_ragged_fold) -- bit for bit the
+head blocks (first 4095 survivors and the count) stacked as the first all-gather
+would stack them, then every rank's partial block and the rank-order fold (eagle_backend_x_b200_ragged_fold) -- bit for bit the
 one-device compact-then-sum of the whole batch and the oracle's compaction +
 canonical sum, for even and uneven splits, empty shards, and shards so sparse that
 one leaf spans many ranks. Both forms of the leaves: from the gathered survivors
 (eagle_backend_x_b200_ragged_leaves) and fused, straight from the values
-(eagle_backend_x_b200_compact_sum_count / _leaves / _straddle)."""
+(eagle_backend_x_b200_compact_sum_count / _head / _leaves / _straddle)."""
 
 import numpy as np
 import pytest
@@ -18,7 +18,20 @@ torch = pytest.importorskip("torch")
 LEAF = 4096
 
 
+def _fold(lib, gathered, world, cap, s):
+    from eagle_b200 import _abi
+
+    work = torch.zeros(2 * ((world * cap + 511) // 512) + 2, dtype=torch.float64, device="cuda")
+    out = torch.zeros(3, dtype=torch.float64, device="cuda")
+    _abi.check(lib.eagle_backend_x_b200_ragged_fold(gathered.data_ptr(), world, cap, work.data_ptr(),
+                                                    out.data_ptr(), s))
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
 def _emulated(eb, vals, keep, bounds):
+    """Every rank's head block stacked as the first all-gather stacks them, every
+    rank's partial block as the second does."""
     from eagle_b200 import _abi
 
     lib = _abi.lib()
@@ -31,20 +44,16 @@ def _emulated(eb, vals, keep, bounds):
         cs.gather()
         sums.append(cs)
     cap = max((bounds[r + 1] - bounds[r] + LEAF - 1) // LEAF + 1 for r in range(world))
-    counts = torch.cat([cs.count for cs in sums]).contiguous()
-    heads = torch.cat([cs.kept[:LEAF - 1] for cs in sums]).contiguous()
-    gathered = torch.zeros(world * 2 * cap, dtype=torch.float64, device="cuda")
-    leaf_counts = torch.zeros(world, dtype=torch.int32, device="cuda")
+    pb = 2 * cap + 2
+    blocks = torch.zeros(world * LEAF, dtype=torch.float64, device="cuda")
+    for r, cs in enumerate(sums):
+        _abi.check(lib.eagle_backend_x_b200_ragged_head(cs.kept.data_ptr(), cs.count.data_ptr(),
+                                                        blocks.data_ptr() + 8 * LEAF * r, s))
+    gathered = torch.zeros(world * pb, dtype=torch.float64, device="cuda")
     for r, cs in enumerate(sums):
         _abi.check(lib.eagle_backend_x_b200_ragged_leaves(
-            cs.kept.data_ptr(), counts.data_ptr(), heads.data_ptr(), r, world,
-            gathered.data_ptr() + 8 * 2 * cap * r, cap, leaf_counts.data_ptr() + 4 * r, s))
-    work = torch.zeros(2 * ((world * cap + 511) // 512) + 2, dtype=torch.float64, device="cuda")
-    out = torch.zeros(3, dtype=torch.float64, device="cuda")
-    _abi.check(lib.eagle_backend_x_b200_ragged_fold(gathered.data_ptr(), leaf_counts.data_ptr(), world, cap,
-                                                    work.data_ptr(), out.data_ptr(), s))
-    torch.cuda.synchronize()
-    return out.cpu().numpy()
+            cs.kept.data_ptr(), blocks.data_ptr(), r, world, gathered.data_ptr() + 8 * pb * r, cap, s))
+    return _fold(lib, gathered, world, cap, s)
 
 
 def _emulated_fused(eb, vals, keep, bounds):
@@ -55,6 +64,9 @@ def _emulated_fused(eb, vals, keep, bounds):
     lib = _abi.lib()
     s = torch.cuda.current_stream().cuda_stream
     world = len(bounds) - 1
+    cap = max((bounds[r + 1] - bounds[r] + LEAF - 1) // LEAF + 1 for r in range(world))
+    pb = 2 * cap + 2
+    blocks = torch.zeros(world * LEAF, dtype=torch.float64, device="cuda")
     sums, vdev = [], []
     for r in range(world):
         b, e = bounds[r], bounds[r + 1]
@@ -62,27 +74,18 @@ def _emulated_fused(eb, vals, keep, bounds):
         cs = eb.CompactSum(torch.from_numpy(keep[b:e].copy()).cuda(), v)
         cs.sdesc.stream = s
         _abi.check(lib.eagle_backend_x_b200_compact_sum_count(ctypes.byref(cs.sdesc)))
+        _abi.check(lib.eagle_backend_x_b200_compact_sum_head(ctypes.byref(cs.sdesc), v.data_ptr(),
+                                                              blocks.data_ptr() + 8 * LEAF * r))
         sums.append(cs)
         vdev.append(v)
-    cap = max((bounds[r + 1] - bounds[r] + LEAF - 1) // LEAF + 1 for r in range(world))
-    counts = torch.cat([cs.count for cs in sums]).contiguous()
-    heads = torch.zeros(world * (LEAF - 1), dtype=torch.float64, device="cuda")
-    gathered = torch.zeros(world * 2 * cap, dtype=torch.float64, device="cuda")
-    leaf_counts = torch.zeros(world, dtype=torch.int32, device="cuda")
+    gathered = torch.zeros(world * pb, dtype=torch.float64, device="cuda")
     for r, cs in enumerate(sums):
         _abi.check(lib.eagle_backend_x_b200_compact_sum_leaves(
-            ctypes.byref(cs.sdesc), vdev[r].data_ptr(), counts.data_ptr(), r, world,
-            heads.data_ptr() + 8 * (LEAF - 1) * r, gathered.data_ptr() + 8 * 2 * cap * r, cap))
-    for r, cs in enumerate(sums):
+            ctypes.byref(cs.sdesc), vdev[r].data_ptr(), blocks.data_ptr(), r, world,
+            gathered.data_ptr() + 8 * pb * r, cap))
         _abi.check(lib.eagle_backend_x_b200_compact_sum_straddle(
-            ctypes.byref(cs.sdesc), counts.data_ptr(), heads.data_ptr(), r, world,
-            gathered.data_ptr() + 8 * 2 * cap * r, leaf_counts.data_ptr() + 4 * r))
-    work = torch.zeros(2 * ((world * cap + 511) // 512) + 2, dtype=torch.float64, device="cuda")
-    out = torch.zeros(3, dtype=torch.float64, device="cuda")
-    _abi.check(lib.eagle_backend_x_b200_ragged_fold(gathered.data_ptr(), leaf_counts.data_ptr(), world, cap,
-                                                    work.data_ptr(), out.data_ptr(), s))
-    torch.cuda.synchronize()
-    return out.cpu().numpy()
+            ctypes.byref(cs.sdesc), blocks.data_ptr(), r, world, gathered.data_ptr() + 8 * pb * r, cap))
+    return _fold(lib, gathered, world, cap, s)
 
 
 CASES = [
@@ -126,15 +129,11 @@ def test_leaf_capacity_overflow_is_reported(eb):
     cs = eb.CompactSum(torch.ones(n, dtype=torch.bool, device="cuda"),
                        torch.ones(n, dtype=torch.float64, device="cuda"))
     cs.gather()
-    heads = cs.kept[:LEAF - 1].contiguous()
-    partials = torch.zeros(2 * 2, dtype=torch.float64, device="cuda")
-    leaf_counts = torch.zeros(1, dtype=torch.int32, device="cuda")
-    _abi.check(lib.eagle_backend_x_b200_ragged_leaves(cs.kept.data_ptr(), cs.count.data_ptr(), heads.data_ptr(),
-                                                      0, 1, partials.data_ptr(), 2, leaf_counts.data_ptr(), s))
-    work = torch.zeros(8, dtype=torch.float64, device="cuda")
-    out = torch.zeros(3, dtype=torch.float64, device="cuda")
-    _abi.check(lib.eagle_backend_x_b200_ragged_fold(partials.data_ptr(), leaf_counts.data_ptr(), 1, 2,
-                                                    work.data_ptr(), out.data_ptr(), s))
-    torch.cuda.synchronize()
-    assert int(leaf_counts.item()) == 5
-    assert torch.isnan(out).all()
+    block = torch.zeros(LEAF, dtype=torch.float64, device="cuda")
+    _abi.check(lib.eagle_backend_x_b200_ragged_head(cs.kept.data_ptr(), cs.count.data_ptr(), block.data_ptr(), s))
+    partials = torch.zeros(2 * 2 + 2, dtype=torch.float64, device="cuda")
+    _abi.check(lib.eagle_backend_x_b200_ragged_leaves(cs.kept.data_ptr(), block.data_ptr(), 0, 1,
+                                                      partials.data_ptr(), 2, s))
+    out = _fold(lib, partials, 1, 2, s)
+    assert int(partials[4:5].view(torch.int64).item()) & 0xffffffff == 5
+    assert np.isnan(out).all()
