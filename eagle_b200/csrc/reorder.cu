@@ -705,6 +705,7 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
     T* out = reinterpret_cast<T*>(smem);                                     // the tile in key order
     uint8_t* outKey = reinterpret_cast<uint8_t*>(smem + kTile * sizeof(T));  // each place's key
     __shared__ uint32_t sStart[256];
+    __shared__ int64_t sShift[256];  // a key's first destination less its first place in the tile
     __shared__ uint32_t scan[33];
     const int t = int(threadIdx.x);
     const int64_t lim = spanOf(a.lim, a.n);
@@ -727,15 +728,18 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
     }
     // the tile's count of each key, from the scanned key-major matrix: the next entry's
     // first destination (the next key's first tile, or the total after the last) less its own
-    uint32_t c = 0;
+    uint32_t c = 0, first = 0;
     if (uint32_t(t) < a.nKeys) {
         const size_t at = size_t(t) * a.tiles + blockIdx.x;
         const size_t m = size_t(a.nKeys) * a.tiles;
-        c = (at + 1 < m ? a.base[at + 1] : *a.total) - a.base[at];
+        first = a.base[at];
+        c = (at + 1 < m ? a.base[at + 1] : *a.total) - first;
     }
     uint32_t all = 0;
-    sStart[t] = blockExclusiveSum(c, all, scan);  // the key's first place in the tile
-    __syncthreads();  // sStart
+    const uint32_t start = blockExclusiveSum(c, all, scan);  // the key's first place in the tile
+    sStart[t] = start;
+    sShift[t] = int64_t(first) - int64_t(start);
+    __syncthreads();  // sStart, sShift
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
         const uint32_t k = kr[j] >> 16;
@@ -749,8 +753,7 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
     // each key's run of the tile is contiguous in the plane: coalesced stores
     T* dst = static_cast<T*>(a.plane);
     for (int q = t; q < int(len); q += kThreads) {
-        const uint32_t k = outKey[q];
-        const int64_t d = int64_t(a.base[size_t(k) * a.tiles + blockIdx.x]) + (q - int64_t(sStart[k]));
+        const int64_t d = sShift[outKey[q]] + q;
         const T val = out[q];
         dst[d] = val;
         if constexpr (Perm)
