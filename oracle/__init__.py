@@ -239,6 +239,27 @@ def philox4x32_10(counter, seed: int):
     return out
 
 
+def curand_philox4x32_10(counters, keys):
+    """cuRAND's Philox-4x32-10 (``curand_Philox4x32_10`` of its device API) of each
+    row of ``counters`` (n x 4 uint32) under the key in the same row of ``keys``
+    (n x 2 uint32), computed on the GPU: the check of :func:`philox4x32_10`. Needs a
+    CUDA device."""
+    c = np.ascontiguousarray(counters, dtype=np.uint32).reshape(-1, 4)
+    k = np.ascontiguousarray(keys, dtype=np.uint32).reshape(-1, 2)
+    if c.shape[0] != k.shape[0]:
+        raise ValueError("one key per counter")
+    path = os.path.join(_HERE, "libcurand_philox.so")
+    if not os.path.exists(path):
+        build()
+    L = ctypes.CDLL(path)
+    L.curand_philox_ref.argtypes = [_P, _P, _P, ctypes.c_int]
+    out = np.zeros_like(c)
+    err = L.curand_philox_ref(_ptr(c), _ptr(k), _ptr(out), int(c.shape[0]))
+    if err != 0:
+        raise RuntimeError(f"curand_philox_ref: CUDA error {err}")
+    return out
+
+
 def gambler_run(pos, time, terminated, *, seed: int, max_steps: int, id_base: int = 0):
     """Every live sample's walk until it reaches 0 or 100 or has taken ``max_steps``
     steps in this run, in place. Returns ``(finished, longest, total)``."""

@@ -3,7 +3,7 @@ steps, absorbing at 0 and 100) on the GPU against the oracle: positions, int64
 absorption times and the mask bit for bit, the report exactly, the canonical
 int64 sum of the times exact; both schedules; the cap and a continued run; shards
 keyed by id_base draw the numbers of the whole; the hawk-ABI entry through
-launch_raw."""
+launch_raw; and the oracle's Philox itself against cuRAND's."""
 
 import ctypes
 
@@ -110,3 +110,25 @@ def test_hawk_abi_persist_entry(eb, orc):
     rp, rt, rm, ((f, longest, total),) = _oracle(orc, pos0, 1_000_000)
     assert time.cpu().numpy().tobytes() == rt.tobytes() and int(fin.item()) == f
     assert int(words.cpu().numpy()[1]) == total
+
+
+def test_oracle_philox_is_curands(orc):
+    """The oracle's Philox-4x32-10 -- the generator the walk's steps come from, and
+    the check of the GPU walk above -- against cuRAND's own block function
+    (curand_Philox4x32_10) on the same counters and keys: random ones, the walk's own
+    (step / 128 and the sample id as two words each, under the seed used above), and
+    the all-zero and all-ones edges."""
+    g = np.random.default_rng(3)
+    n = 4096
+    counters = g.integers(0, 1 << 32, (n, 4), dtype=np.uint64).astype(np.uint32)
+    keys = g.integers(0, 1 << 32, (n, 2), dtype=np.uint64).astype(np.uint32)
+    blocks = g.integers(0, 1 << 20, 256, dtype=np.uint64)
+    ids = g.integers(0, 1 << 26, 256, dtype=np.uint64)
+    walk = np.stack([blocks & 0xffffffff, blocks >> 32, ids & 0xffffffff, ids >> 32], axis=1).astype(np.uint32)
+    counters = np.concatenate([counters, walk, np.zeros((1, 4), np.uint32), np.full((1, 4), 0xffffffff, np.uint32)])
+    seed_words = np.array([SEED & 0xffffffff, SEED >> 32], np.uint32)
+    keys = np.concatenate([keys, np.tile(seed_words, (256, 1)), np.zeros((1, 2), np.uint32),
+                           np.full((1, 2), 0xffffffff, np.uint32)])
+    want = orc.curand_philox4x32_10(counters, keys)
+    got = np.stack([orc.philox4x32_10(c, int(k[0]) | (int(k[1]) << 32)) for c, k in zip(counters, keys)])
+    assert got.dtype == want.dtype and (got == want).all()
