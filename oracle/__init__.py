@@ -62,6 +62,8 @@ def lib():
         L.oracle_gambler_run.argtypes = [_I64, _P, _P, _P, _I64, ctypes.c_uint64, _I64, _P]
         L.oracle_det_pow.argtypes = [ctypes.c_double, ctypes.c_double]
         L.oracle_det_pow.restype = ctypes.c_double
+        L.oracle_lorenz_stages.argtypes = [_P, ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                           ctypes.c_double, ctypes.c_double, _P, _P, _P]
         L.oracle_lorenz_run.argtypes = [_I64, _P] + [ctypes.c_double] * 5 + [_P] * 8 + [_I64, _P]
         L.oracle_corpus_f64.argtypes = [_I64, ctypes.c_uint64, _P]
         L.oracle_corpus_f32.argtypes = [_I64, ctypes.c_uint64, _P]
@@ -237,6 +239,19 @@ def philox4x32_10(counter, seed: int):
     out = np.zeros(4, dtype=np.uint32)
     lib().oracle_philox4x32_10(_ptr(c), int(seed), _ptr(out))
     return out
+
+
+def lorenz_stages(s0, step, *, rho, sigma, beta, rtol, atol):
+    """The scheme of one RKF7(8) attempt of Lorenz-63 from ``s0`` with ``step``
+    (benchmarks/perf_card/perf_card.py:289-309 rkf78_stages and error_ratio, with
+    Lorenz's right-hand side): ``(s8, err, ratio)``."""
+    s = np.ascontiguousarray(s0, dtype=np.float64)
+    s8 = np.zeros(3)
+    err = np.zeros(3)
+    ratio = np.zeros(1)
+    lib().oracle_lorenz_stages(_ptr(s), float(step), float(rho), float(sigma), float(beta), float(rtol),
+                               float(atol), _ptr(s8), _ptr(err), _ptr(ratio))
+    return s8, err, float(ratio[0])
 
 
 def curand_philox4x32_10(counters, keys):

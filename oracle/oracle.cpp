@@ -840,14 +840,11 @@ inline double termSum(const double* coef, int count, double k[][3], int d)
     return total;
 }
 
-// One attempt; returns true when it was accepted.
-bool lorenzAttempt(double s[3], double& t, double& h, double rho, double sigma, double beta, double tFinal,
-    double rtol, double atol)
+// The scheme of one attempt of step h from s0: the 8th-order state, the error vector
+// and the mixed max-norm ratio (the attempt below, before its controller).
+void lorenzStages(const double s0[3], double step, double rho, double sigma, double beta, double rtol,
+    double atol, double s8[3], double err[3], double* ratioOut)
 {
-    const double s0[3] = {s[0], s[1], s[2]};
-    const double t0 = t;
-    const bool last = h >= tFinal - t0;
-    const double step = last ? tFinal - t0 : h;
     double k[13][3];
     lorenzRhs(s0, sigma, rho, beta, k[0]);
     for (int i = 0; i < 12; ++i) {
@@ -856,7 +853,6 @@ bool lorenzAttempt(double s[3], double& t, double& h, double rho, double sigma, 
             si[d] = s0[d] + step * termSum(kA[i], i + 1, k, d);
         lorenzRhs(si, sigma, rho, beta, k[i + 1]);
     }
-    double s8[3], err[3];
     for (int d = 0; d < 3; ++d) {
         s8[d] = s0[d] + step * termSum(kB, 13, k, d);
         err[d] = step * termSum(kBE, 13, k, d);
@@ -866,6 +862,19 @@ bool lorenzAttempt(double s[3], double& t, double& h, double rho, double sigma, 
         const double r = std::fabs(err[d]) / (atol + rtol * std::fmax(std::fabs(s8[d]), std::fabs(s0[d])));
         ratio = d == 0 ? r : std::fmax(ratio, r);
     }
+    *ratioOut = ratio;
+}
+
+// One attempt; returns true when it was accepted.
+bool lorenzAttempt(double s[3], double& t, double& h, double rho, double sigma, double beta, double tFinal,
+    double rtol, double atol)
+{
+    const double s0[3] = {s[0], s[1], s[2]};
+    const double t0 = t;
+    const bool last = h >= tFinal - t0;
+    const double step = last ? tFinal - t0 : h;
+    double s8[3], err[3], ratio = 0.0;
+    lorenzStages(s0, step, rho, sigma, beta, rtol, atol, s8, err, &ratio);
     const bool accept = ratio < 1.0;
     const double expo = accept ? -1.0 / 9.0 : -1.0 / 8.0;
     h = step * std::fmin(5.0, std::fmax(0.2, 0.9 * detPow(ratio, expo)));
@@ -883,6 +892,12 @@ bool lorenzAttempt(double s[3], double& t, double& h, double rho, double sigma, 
 extern "C" {
 
 double oracle_det_pow(double r, double e) { return detPow(r, e); }
+
+void oracle_lorenz_stages(const double s0[3], double step, double rho, double sigma, double beta, double rtol,
+    double atol, double s8[3], double err[3], double* ratio)
+{
+    lorenzStages(s0, step, rho, sigma, beta, rtol, atol, s8, err, ratio);
+}
 
 int oracle_lorenz_run(int64_t n, const double* rho, double sigma, double beta, double t_final, double rtol,
     double atol, double* x, double* y, double* z, double* t, double* h, uint32_t* n_acc, uint32_t* n_rej,

@@ -41,6 +41,9 @@ void oracle_philox4x32_10(const uint32_t counter[4], uint64_t seed, uint32_t out
 int oracle_gambler_run(int64_t n, int32_t* pos, int64_t* time, uint8_t* term, int64_t id_base, uint64_t seed,
     int64_t max_steps, int64_t* stats);
 double oracle_det_pow(double r, double e);
+/* one RKF7(8) attempt's scheme for Lorenz-63: 8th-order state, error vector, mixed max-norm ratio */
+void oracle_lorenz_stages(const double s0[3], double step, double rho, double sigma, double beta, double rtol,
+    double atol, double s8[3], double err[3], double* ratio);
 int oracle_lorenz_run(int64_t n, const double* rho, double sigma, double beta, double t_final, double rtol,
     double atol, double* x, double* y, double* z, double* t, double* h, uint32_t* n_acc, uint32_t* n_rej,
     uint8_t* term, int64_t max_steps, int64_t* stats);

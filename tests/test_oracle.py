@@ -13,7 +13,10 @@ Pins (paths relative to the eagle source tree):
 * python/tests/test_active_set.py:49-56: the map is flatnonzero(~mask) over the
   sizes (0, 1, 7, 256, 257, 4096, 100_003);
 * python/tests/test_until_done_auto.py:160-184: bandK and the policy sequence,
-  restated independently.
+  restated independently;
+* benchmarks/perf_card/perf_card.py:255-317: one RKF7(8) attempt (tableau, stage
+  sums, error ratio) against the card's own functions run with Lorenz's right-hand
+  side (tests/golden/rkf78_lorenz.json).
 """
 
 import json
@@ -396,3 +399,33 @@ def test_lorenz_reaches_t_final_and_counts(orc):
     att = na.astype(np.int64) + nr
     assert int(att.sum()) == total and int(att.max()) == longest
     assert 100 < att.mean() < 2000 and np.all(np.isfinite(z))
+
+
+def test_rkf78_attempt_matches_the_perf_cards_code():
+    """The oracle's RKF7(8) attempt of Lorenz-63 (the scheme the Lorenz configuration
+    runs: Fehlberg's tableau, left-to-right term sums skipping zero coefficients, the
+    mixed max-norm error ratio) bit for bit against the same attempt computed by eagle's
+    own perf-card functions (tests/golden/rkf78_lorenz.json, written by
+    tests/golden/make_rkf78_golden.py from benchmarks/perf_card/perf_card.py), on 96
+    states, steps and rho values, accepted and rejected."""
+    import json
+    import os
+
+    import oracle
+
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "rkf78_lorenz.json")
+    with open(path) as f:
+        g = json.load(f)
+
+    def f64(h):
+        return np.array([int(h, 16)], dtype=np.uint64).view(np.float64)[0]
+
+    rejected = 0
+    for c in g["cases"]:
+        s8, err, ratio = oracle.lorenz_stages([f64(v) for v in c["s0"]], f64(c["step"]), rho=f64(c["rho"]),
+                                              sigma=g["sigma"], beta=g["beta"], rtol=g["rtol"], atol=g["atol"])
+        assert [int(np.float64(v).view(np.uint64)) for v in s8] == [int(v, 16) for v in c["s8"]], c
+        assert [int(np.float64(v).view(np.uint64)) for v in err] == [int(v, 16) for v in c["err"]], c
+        assert int(np.float64(ratio).view(np.uint64)) == int(c["ratio"], 16), c
+        rejected += ratio >= 1.0
+    assert 0 < rejected < len(g["cases"])
