@@ -72,6 +72,27 @@ def test_staged_and_direct_leaf_loads(eb, orc, n):
     assert _same(eb.reduce(off).cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("n", ((1 << 22) + 37, 700 * 4096 + 1, 8000 * 4096 - 5))
+def test_leaf_by_leaf_kernel_every_kind(eb, orc, n):
+    """One column with more leaves than the device holds CTAs takes the leaf-by-leaf
+    kernel (leaves claimed in order, each 512-leaf chunk joined by the CTA completing
+    it, the chunk partials by the last): the oracle's bits for float64 (also with a
+    companion and PAIR_OUT), float32, int64 sums, min, max and all, with a ragged last
+    leaf and chunk."""
+    x = orc.corpus(n, 5 + n)
+    assert _same(eb.reduce(_dev(x)).cpu().numpy(), orc.reduce(x))
+    c = orc.corpus(n, 6 + n) * 1e-17
+    assert _same(eb.reduce(_dev(x), comp=_dev(c), pair_out=True).cpu().numpy(),
+                 orc.reduce(x, comp=c, pair_out=True))
+    xf = orc.corpus(n, 7 + n, np.float32)
+    assert _same(eb.reduce(_dev(xf)).cpu().numpy(), orc.reduce(xf))
+    xi = np.random.default_rng(n).integers(-10 ** 9, 10 ** 9, size=n)
+    for op in ("sum", "max", "min"):
+        assert _same(eb.reduce(_dev(xi), op).cpu().numpy(), orc.reduce(xi, op)), op
+    m = (np.random.default_rng(n + 1).random(n) < 0.9999999).astype(np.uint8)
+    assert _same(eb.reduce(_dev(m), "all").cpu().numpy(), orc.reduce(m, "all"))
+
+
 @pytest.mark.parametrize("dtype", [np.int32, np.int64])
 def test_integer_sums_min_max(eb, orc, dtype):
     rng = np.random.default_rng(1)
