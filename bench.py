@@ -1180,7 +1180,7 @@ def reorder_line(ctx, args):
                                             "kept run written in place, its dropped run staged and copied back "
                                             "((4 - 2p) element bytes a slot), perm likewise with inv and "
                                             "index_map written, the mask read by the scan"}},
-            "gpu_launches": (1 + 2 * 8 + 1) + (3 + 2 * 8 + 2), "clocks": clocks.summary()}
+            "gpu_launches": (1 + 2 * 7 + 1) + (3 + 2 * 8 + 2), "clocks": clocks.summary()}
 
 
 def probe_line(ctx, args):

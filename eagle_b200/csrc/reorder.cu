@@ -154,6 +154,8 @@ __global__ __launch_bounds__(kThreads) void copySpanKernel(const T* __restrict__
 struct InPlaceArgs {
     void* plane;
     void* stage;
+    void* plane2;  // the second plane of a pair (G = 2), its dropped run staged at stage2
+    void* stage2;
     const uint16_t* bits;
     const uint32_t* prefix;
     const uint32_t* cnt;
@@ -188,27 +190,30 @@ __device__ __forceinline__ bool waitTileRead(const uint32_t* readDone, int64_t w
     return false;
 }
 
-/** 4096-slot tiles of one plane moved in place, one CTA per resident slot: each
- *  tile (claimed in order; the next claim goes out while the tile is worked on) is
- *  read, ordered in shared memory and its read published, then its kept run written
- *  to [pre, pre + kept) once the earlier tiles that range covers have been read, and
- *  its dropped run to the stage at its rank among the dropped slots. With ``Perm``
- *  the plane is perm: inv[v] = the new slot of each moved value v (a dropped one's
- *  is count + its rank), and index_map is the identity over the tile's part of
- *  [0, count). A wait that gives up sets bit 2 of ``*err`` and leaves the tile's
- *  kept run unwritten: the count then reports the failure. No wait is on a tile
- *  whose read cannot finish: the lowest tile not yet read is being read (reads
- *  wait on nothing) or is claimed by a CTA writing an earlier tile, whose waits are
- *  on tiles lower still, all read. */
-template <class T, bool Perm>
-__global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : (sizeof(T) <= 2 ? 8 : 4)) void placeInPlaceKernel(InPlaceArgs a)
+/** 4096-slot tiles of ``G`` planes (1, or 2 of the same element size) moved in
+ *  place, one CTA per resident slot: each tile (claimed in order; the next claim goes
+ *  out while the tile is worked on) is read, ordered in shared memory and its read
+ *  published, then its kept run written to [pre, pre + kept) once the earlier tiles
+ *  that range covers have been read, and its dropped run to the stage at its rank
+ *  among the dropped slots. Two planes share the tile's scan, read flag and wait.
+ *  With ``Perm`` the plane is perm: inv[v] = the new slot of each moved value v (a
+ *  dropped one's is count + its rank), and index_map is the identity over the
+ *  tile's part of [0, count). A wait that gives up sets bit 2 of ``*err`` and
+ *  leaves the tile's kept run unwritten: the count then reports the failure. No
+ *  wait is on a tile whose read cannot finish: the lowest tile not yet read is being
+ *  read (reads wait on nothing) or is claimed by a CTA writing an earlier tile, whose
+ *  waits are on tiles lower still, all read. */
+template <class T, bool Perm, int G>
+__global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : (sizeof(T) <= 2 && G == 1 ? 8 : 4)) void placeInPlaceKernel(
+    InPlaceArgs a)
 {
+    static_assert(G == 1 || (G == 2 && !Perm), "perm moves alone");
     if (a.fire != nullptr && *a.fire == 0u)
         return;
     if (*a.err != 0u)
         return;  // the scan gave up (the planes stay as they were), or an earlier plane's wait did
     extern __shared__ __align__(16) unsigned char smem[];
-    T* out = reinterpret_cast<T*>(smem);
+    T* out = reinterpret_cast<T*>(smem);  // [G][kTile]
     __shared__ uint32_t scan[33];
     __shared__ uint16_t sKeep[kThreads];
     __shared__ uint32_t sExcl[kThreads];
@@ -221,10 +226,19 @@ __global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : (sizeof(T) <= 2 ? 8 :
     uint32_t tile = sTile;
     const int64_t sp = spanOf(a.span, a.n);
     const int64_t cnt = int64_t(*a.cnt);
-    T* plane = static_cast<T*>(a.plane);
-    T* stage = static_cast<T*>(a.stage);
+    T* planes[G];
+    T* stages[G];
+    planes[0] = static_cast<T*>(a.plane);
+    stages[0] = static_cast<T*>(a.stage);
+    if constexpr (G == 2) {
+        planes[1] = static_cast<T*>(a.plane2);
+        stages[1] = static_cast<T*>(a.stage2);
+    }
     constexpr bool kNarrow = sizeof(T) <= 2;
-    const bool vecOk = (reinterpret_cast<uintptr_t>(plane) & 15u) == 0;
+    bool vecOk = true;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+        vecOk = vecOk && (reinterpret_cast<uintptr_t>(planes[g]) & 15u) == 0;
     while (tile < a.tiles) {
         const int64_t tile0 = int64_t(tile) * kTile;
         if (tile0 >= sp)
@@ -234,30 +248,34 @@ __global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : (sizeof(T) <= 2 ? 8 :
         // -- exactly its own keep bits -- in one or two 16-byte loads. Wider ones: element
         // e is the (e % 16)-th of thread e / 16's keep bits, read coalesced
         // (lane-consecutive e). All loads go out before the keep counts are scanned.
-        T v[kPer];
-        if constexpr (kNarrow) {
-            const int64_t e0 = int64_t(t) * kPer;
-            if (vecOk && e0 + kPer <= len) {
-                union {
-                    uint4 q[sizeof(T)];
-                    T x[kPer];
-                } u;
+        T v[G][kPer];
 #pragma unroll
-                for (int k = 0; k < int(sizeof(T)); ++k)
-                    u.q[k] = reinterpret_cast<const uint4*>(plane + tile0 + e0)[k];
+        for (int g = 0; g < G; ++g) {
+            const T* plane = planes[g];
+            if constexpr (kNarrow) {
+                const int64_t e0 = int64_t(t) * kPer;
+                if (vecOk && e0 + kPer <= len) {
+                    union {
+                        uint4 q[sizeof(T)];
+                        T x[kPer];
+                    } u;
 #pragma unroll
-                for (int j = 0; j < kPer; ++j)
-                    v[j] = u.x[j];
+                    for (int k = 0; k < int(sizeof(T)); ++k)
+                        u.q[k] = reinterpret_cast<const uint4*>(plane + tile0 + e0)[k];
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j)
+                        v[g][j] = u.x[j];
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j)
+                        v[g][j] = e0 + j < len ? plane[tile0 + e0 + j] : T{};
+                }
             } else {
 #pragma unroll
-                for (int j = 0; j < kPer; ++j)
-                    v[j] = e0 + j < len ? plane[tile0 + e0 + j] : T{};
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < kPer; ++j) {
-                const int e = t + j * kThreads;
-                v[j] = int64_t(e) < len ? plane[tile0 + e] : T{};
+                for (int j = 0; j < kPer; ++j) {
+                    const int e = t + j * kThreads;
+                    v[g][j] = int64_t(e) < len ? plane[tile0 + e] : T{};
+                }
             }
         }
         uint32_t next = 0;
@@ -282,7 +300,9 @@ __global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : (sizeof(T) <= 2 ? 8 :
                 if (e < len) {
                     const uint32_t before = excl + __popc(keep & ((1u << j) - 1u));  // kept before e
                     const uint32_t pos = ((keep >> j) & 1u) ? before : kept + uint32_t(e) - before;
-                    out[pos] = v[j];
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+                        out[g * kTile + pos] = v[g][j];
                 }
             }
         } else {
@@ -296,7 +316,9 @@ __global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : (sizeof(T) <= 2 ? 8 :
                     const uint32_t kb = sKeep[e >> 4], bit = uint32_t(e & 15);
                     const uint32_t before = sExcl[e >> 4] + __popc(kb & ((1u << bit) - 1u));  // kept before e
                     const uint32_t pos = ((kb >> bit) & 1u) ? before : kept + uint32_t(e) - before;
-                    out[pos] = v[j];
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+                        out[g * kTile + pos] = v[g][j];
                 }
             }
         }
@@ -318,21 +340,25 @@ __global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : (sizeof(T) <= 2 ? 8 :
         const int64_t dropBase = tile0 - pre;  // dropped slots before the tile
         const bool ok = sOk != 0;
         for (int q = t; q < int(len); q += kThreads) {
-            const T x = out[q];
             if (q < int(kept)) {
                 if (!ok)
                     continue;
                 const int64_t d = pre + q;
-                plane[d] = x;
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    planes[g][d] = out[g * kTile + q];
                 if constexpr (Perm) {
+                    const T x = out[q];
                     a.inv[static_cast<int32_t>(x)] = int32_t(d);
                     a.indexMap[d] = int32_t(d);
                 }
             } else {
                 const int64_t r = dropBase + (q - int(kept));
-                stage[r] = x;
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    stages[g][r] = out[g * kTile + q];
                 if constexpr (Perm)
-                    a.inv[static_cast<int32_t>(x)] = int32_t(cnt + r);
+                    a.inv[static_cast<int32_t>(out[q])] = int32_t(cnt + r);
             }
         }
         if (t == 0)
@@ -342,10 +368,12 @@ __global__ __launch_bounds__(kThreads, sizeof(T) > 8 ? 2 : (sizeof(T) <= 2 ? 8 :
     }
 }
 
-/** plane[count + r] = stage[r] for the staged dropped run, r < span - count. */
+/** plane[count + r] = stage[r] for the staged dropped run, r < span - count, and the
+ *  same for a second plane (plane2, stage2) when it is not null. */
 template <class T>
 __global__ __launch_bounds__(kThreads) void dropBackKernel(const T* __restrict__ stage, T* __restrict__ plane,
-    const uint32_t* cnt, const uint32_t* span, const uint32_t* fire, const uint32_t* err, int64_t n)
+    const T* __restrict__ stage2, T* __restrict__ plane2, const uint32_t* cnt, const uint32_t* span,
+    const uint32_t* fire, const uint32_t* err, int64_t n)
 {
     if (fire != nullptr && *fire == 0u)
         return;
@@ -353,8 +381,11 @@ __global__ __launch_bounds__(kThreads) void dropBackKernel(const T* __restrict__
         return;
     const int64_t c = int64_t(*cnt);
     const int64_t end = spanOf(span, n) - c;
-    for (int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; r < end; r += int64_t(gridDim.x) * blockDim.x)
+    for (int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; r < end; r += int64_t(gridDim.x) * blockDim.x) {
         plane[c + r] = stage[r];
+        if (plane2 != nullptr)
+            plane2[c + r] = stage2[r];
+    }
 }
 
 __global__ void reorderFinishKernel(const uint32_t* cnt, const uint32_t* err, uint32_t* count, uint32_t* span,
@@ -423,12 +454,12 @@ unsigned streamGrid(int64_t n)
 /** The in-place place kernel's grid for ``tiles`` tiles: one CTA per resident slot
  *  (the kernel's occupancy, looked up once per device), at most one per tile. Also
  *  opts the kernel into ``shared`` bytes of dynamic shared memory. */
-template <class T, bool Perm>
+template <class T, bool Perm, int G>
 unsigned placeGrid(uint32_t tiles, size_t shared)
 {
     static std::mutex mu;
     static int perSm[64] = {};
-    const void* kernel = reinterpret_cast<const void*>(&placeInPlaceKernel<T, Perm>);
+    const void* kernel = reinterpret_cast<const void*>(&placeInPlaceKernel<T, Perm, G>);
     allowShared(kernel, shared);
     int dev = 0;
     cudaCheck(cudaGetDevice(&dev), "cudaGetDevice");
@@ -436,7 +467,7 @@ unsigned placeGrid(uint32_t tiles, size_t shared)
     {
         std::lock_guard<std::mutex> lock(mu);
         if (perSm[dev & 63] == 0) {
-            cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&perSm[dev & 63], placeInPlaceKernel<T, Perm>,
+            cudaCheck(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&perSm[dev & 63], placeInPlaceKernel<T, Perm, G>,
                           kThreads, shared),
                 "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
             if (perSm[dev & 63] < 1)
@@ -882,30 +913,59 @@ EB_API eagle_backend_status eagle_backend_reorder_device(struct eagle_backend_re
         p.n = d.n;
         p.tiles = a.tiles;
         uint32_t epoch = 0;
-        auto move = [&](uint64_t data, uint32_t elem, bool perm) {
+        // planes of one element size up to 4 bytes move two at a time when both dropped
+        // runs fit the stage one after the other, sharing each tile's scan, read flag and
+        // wait; perm moves alone (it also writes inv and index_map)
+        char* stage = base + l.stage;
+        auto move = [&](uint64_t data, uint64_t data2, uint32_t elem, bool perm) {
             p.claim = reinterpret_cast<uint32_t*>(base + l.claims) + epoch;
             ++epoch;
             p.epoch = epoch;
             withElem(elem, [&](auto tag) {
                 using T = decltype(tag);
                 p.plane = reinterpret_cast<void*>(data);
-                const size_t shared = size_t(kTile) * sizeof(T);
+                p.stage = stage;
+                p.plane2 = reinterpret_cast<void*>(data2);
+                p.stage2 = stage + size_t(d.n) * sizeof(T);
                 if (perm) {
+                    const size_t shared = size_t(kTile) * sizeof(int32_t);
                     p.inv = reinterpret_cast<int32_t*>(d.inv);
                     p.indexMap = reinterpret_cast<int32_t*>(d.index_map);
-                    placeInPlaceKernel<int32_t, true><<<placeGrid<int32_t, true>(a.tiles, shared), kThreads, shared, s>>>(p);
+                    placeInPlaceKernel<int32_t, true, 1>
+                        <<<placeGrid<int32_t, true, 1>(a.tiles, shared), kThreads, shared, s>>>(p);
+                } else if (data2 != 0) {
+                    if constexpr (sizeof(T) <= 4) {
+                        const size_t shared = 2 * size_t(kTile) * sizeof(T);
+                        placeInPlaceKernel<T, false, 2><<<placeGrid<T, false, 2>(a.tiles, shared), kThreads, shared, s>>>(p);
+                    }
                 } else {
-                    placeInPlaceKernel<T, false><<<placeGrid<T, false>(a.tiles, shared), kThreads, shared, s>>>(p);
+                    const size_t shared = size_t(kTile) * sizeof(T);
+                    placeInPlaceKernel<T, false, 1><<<placeGrid<T, false, 1>(a.tiles, shared), kThreads, shared, s>>>(p);
                 }
                 launchCheck(who);
-                dropBackKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(base + l.stage),
-                    reinterpret_cast<T*>(data), a.cnt, span, fire, a.err, d.n);
+                dropBackKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(p.stage),
+                    reinterpret_cast<T*>(data), reinterpret_cast<const T*>(p.stage2), reinterpret_cast<T*>(data2),
+                    a.cnt, span, fire, a.err, d.n);
                 launchCheck(who);
             });
         };
-        for (const auto& q : planes)
-            move(q.data, q.elem_bytes, false);
-        move(d.perm, 4, true);
+        const uint32_t stageWidth = std::max<uint32_t>(widestOf(planes), 4u);  // stage bytes per slot
+        std::vector<bool> done(planes.size(), false);
+        for (size_t k = 0; k < planes.size(); ++k) {
+            if (done[k])
+                continue;
+            done[k] = true;
+            uint64_t pair = 0;
+            if (planes[k].elem_bytes <= 4 && 2 * planes[k].elem_bytes <= stageWidth)
+                for (size_t q = k + 1; q < planes.size(); ++q)
+                    if (!done[q] && planes[q].elem_bytes == planes[k].elem_bytes) {
+                        pair = planes[q].data;
+                        done[q] = true;
+                        break;
+                    }
+            move(planes[k].data, pair, planes[k].elem_bytes, false);
+        }
+        move(d.perm, 0, 4, true);
         reorderFinishKernel<<<1, 1, 0, s>>>(a.cnt, a.err, count, span, fire);
         launchCheck(who);
     });

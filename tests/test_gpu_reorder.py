@@ -98,6 +98,35 @@ def test_reorder_densities_and_runs(eb, orc, pattern):
     del keep_alive
 
 
+@pytest.mark.parametrize("n", (4097, (1 << 20) + 3))
+def test_reorder_paired_planes_and_a_narrow_stage(eb, orc, n):
+    """Planes of one element size move two at a time when both dropped runs fit the
+    stage: with no plane wider than 4 bytes the stage holds 4 bytes a slot, so the two
+    byte planes pair and the int32 and float32 planes move alone; every plane, perm, inv
+    and the count bit for bit against the oracle, a second reorder after it too."""
+    g = np.random.default_rng(n)
+    host = [(g.random(n) < 0.4).astype(np.uint8),                            # the mask
+            g.integers(0, 256, n, dtype=np.int64).astype(np.uint8),
+            g.integers(-2**31, 2**31 - 1, n, dtype=np.int64).astype(np.int32),
+            g.standard_normal(n).astype(np.float32),
+            g.integers(-2**15, 2**15 - 1, n, dtype=np.int64).astype(np.int16)]
+    dev = _dev(host)
+    perm, inv, im, count, span = _cells(n, n)
+    hp, hi, him = np.arange(n, dtype=np.int32), np.arange(n, dtype=np.int32), np.zeros(n, np.int32)
+    for r in range(2):
+        keep_alive = eb.reorder(dev, dev[0], perm, inv, im, count, span, drop=True)
+        c, sp, _ = orc.reorder(host, 0, hp, hi, him, n if r == 0 else sp, drop=True)
+        torch.cuda.synchronize()
+        _same(dev, host)
+        assert perm.cpu().numpy().tobytes() == hp.tobytes() and inv.cpu().numpy().tobytes() == hi.tobytes()
+        assert int(count.item()) == c and int(span.item()) == sp
+        m2 = host[0].copy()
+        m2[:c][::3] = 1
+        host[0][:] = m2
+        dev[0].copy_(torch.from_numpy(m2))
+        del keep_alive
+
+
 def test_partial_span_leaves_the_tail(eb, orc):
     n = 50_001
     host = _host(n, 3, 0.5)
