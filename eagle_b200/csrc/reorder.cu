@@ -712,6 +712,8 @@ __global__ __launch_bounds__(kThreads) void scanU32Kernel(ScanU32Args a)
 struct ClassPlaceArgs {
     const void* stage;
     void* plane;
+    const void* stage2;  // the second plane of a pair (G = 2) and its staged copy
+    void* plane2;
     const uint8_t* keys;
     const uint16_t* rel;     // each slot's rank within its key's run of the tile
     const uint32_t* total;   // the count matrix's total (the entry after the last)
@@ -725,16 +727,22 @@ struct ClassPlaceArgs {
     uint32_t tiles;
 };
 
-template <class T, bool Perm>
+/** One tile of ``G`` planes (1, or 2 of the same element size, sharing the tile's
+ *  keys, ranks and scan) placed in key order: each slot to its key's run of the
+ *  destination at its rank, the tile staged in shared memory in key order first so
+ *  that each key's run is written with coalesced stores. With ``Perm`` the plane is
+ *  perm and inv follows it. */
+template <class T, bool Perm, int G>
 __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
 {
+    static_assert(G == 1 || (G == 2 && !Perm), "perm moves alone");
     if (a.fire != nullptr && *a.fire == 0u)
         return;
     if (*a.err != 0u)
         return;
     extern __shared__ __align__(16) unsigned char smem[];
-    T* out = reinterpret_cast<T*>(smem);                                     // the tile in key order
-    uint8_t* outKey = reinterpret_cast<uint8_t*>(smem + kTile * sizeof(T));  // each place's key
+    T* out = reinterpret_cast<T*>(smem);                                         // [G][kTile], key order
+    uint8_t* outKey = reinterpret_cast<uint8_t*>(smem + G * kTile * sizeof(T));  // each place's key
     __shared__ uint32_t sStart[256];
     __shared__ int64_t sShift[256];  // a key's first destination less its first place in the tile
     __shared__ uint32_t scan[33];
@@ -745,16 +753,25 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
         return;
     const int64_t len = lim - tile0 < kTile ? lim - tile0 : kTile;
     // each slot's value, key and rank among its key's slots (the histogram pass ranked
-    // them): thread t takes slots t, t + 256, ..., all sixteen loads in flight while the
-    // tile's key counts below are scanned
-    const T* src = static_cast<const T*>(a.stage);
-    T v[kPer];
+    // them): thread t takes slots t, t + 256, ..., all loads in flight while the tile's
+    // key counts below are scanned
+    const T* src[G];
+    T* dst[G];
+    src[0] = static_cast<const T*>(a.stage);
+    dst[0] = static_cast<T*>(a.plane);
+    if constexpr (G == 2) {
+        src[1] = static_cast<const T*>(a.stage2);
+        dst[1] = static_cast<T*>(a.plane2);
+    }
+    T v[G][kPer];
     uint32_t kr[kPer];
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
         const int64_t i = tile0 + t + int64_t(j) * kThreads;
         const bool in = i - tile0 < len;
-        v[j] = in ? src[i] : T{};
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            v[g][j] = in ? src[g][i] : T{};
         kr[j] = in ? (uint32_t(a.keys[i]) << 16) | uint32_t(a.rel[i]) : kNoKey << 16;
     }
     // the tile's count of each key, from the scanned key-major matrix: the next entry's
@@ -776,19 +793,21 @@ __global__ __launch_bounds__(kThreads) void classPlaceKernel(ClassPlaceArgs a)
         const uint32_t k = kr[j] >> 16;
         if (k != kNoKey) {
             const uint32_t pos = sStart[k] + (kr[j] & 0xffffu);
-            out[pos] = v[j];
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                out[g * kTile + pos] = v[g][j];
             outKey[pos] = uint8_t(k);
         }
     }
     __syncthreads();
     // each key's run of the tile is contiguous in the plane: coalesced stores
-    T* dst = static_cast<T*>(a.plane);
     for (int q = t; q < int(len); q += kThreads) {
         const int64_t d = sShift[outKey[q]] + q;
-        const T val = out[q];
-        dst[d] = val;
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            dst[g][d] = out[g * kTile + q];
         if constexpr (Perm)
-            a.inv[static_cast<int32_t>(val)] = int32_t(d);
+            a.inv[static_cast<int32_t>(out[q])] = int32_t(d);
     }
 }
 
@@ -1063,28 +1082,63 @@ EB_API eagle_backend_status eagle_backend_reorder_classes_device(struct eagle_ba
         p.err = sa.err;
         p.n = d.n;
         p.tiles = c.tiles;
-        auto move = [&](uint64_t data, uint32_t elem, bool perm) {
+        // planes of one element size up to 4 bytes move two at a time when both fit the
+        // stage one after the other (they share the tile's keys, ranks and scan); perm
+        // moves alone
+        char* stage = raw + l.stage;
+        auto move = [&](uint64_t data, uint64_t data2, uint32_t elem, bool perm) {
             withElem(elem, [&](auto tag) {
                 using T = decltype(tag);
-                copySpanKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(data),
-                    reinterpret_cast<T*>(raw + l.stage), lim, fire, d.n);
+                T* st = reinterpret_cast<T*>(stage);
+                T* st2 = st + d.n;
+                copySpanKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(data), st, lim,
+                    fire, d.n);
                 launchCheck(who);
+                if (data2 != 0) {
+                    copySpanKernel<T><<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<const T*>(data2), st2, lim,
+                        fire, d.n);
+                    launchCheck(who);
+                }
+                p.stage = st;
                 p.plane = reinterpret_cast<void*>(data);
-                const size_t shared = size_t(kTile) * (sizeof(T) + 1);
+                p.stage2 = st2;
+                p.plane2 = reinterpret_cast<void*>(data2);
                 if (perm) {
+                    const size_t shared = size_t(kTile) * (sizeof(int32_t) + 1);
                     p.inv = reinterpret_cast<int32_t*>(d.inv);
-                    allowShared(reinterpret_cast<const void*>(&classPlaceKernel<int32_t, true>), shared);
-                    classPlaceKernel<int32_t, true><<<c.tiles, kThreads, shared, s>>>(p);
+                    allowShared(reinterpret_cast<const void*>(&classPlaceKernel<int32_t, true, 1>), shared);
+                    classPlaceKernel<int32_t, true, 1><<<c.tiles, kThreads, shared, s>>>(p);
+                } else if (data2 != 0) {
+                    if constexpr (sizeof(T) <= 4) {
+                        const size_t shared = size_t(kTile) * (2 * sizeof(T) + 1);
+                        allowShared(reinterpret_cast<const void*>(&classPlaceKernel<T, false, 2>), shared);
+                        classPlaceKernel<T, false, 2><<<c.tiles, kThreads, shared, s>>>(p);
+                    }
                 } else {
-                    allowShared(reinterpret_cast<const void*>(&classPlaceKernel<T, false>), shared);
-                    classPlaceKernel<T, false><<<c.tiles, kThreads, shared, s>>>(p);
+                    const size_t shared = size_t(kTile) * (sizeof(T) + 1);
+                    allowShared(reinterpret_cast<const void*>(&classPlaceKernel<T, false, 1>), shared);
+                    classPlaceKernel<T, false, 1><<<c.tiles, kThreads, shared, s>>>(p);
                 }
                 launchCheck(who);
             });
         };
-        for (const auto& q : planes)
-            move(q.data, q.elem_bytes, false);
-        move(d.perm, 4, true);
+        const uint32_t stageWidth = std::max<uint32_t>(widestOf(planes), 4u);  // stage bytes per slot
+        std::vector<bool> done(planes.size(), false);
+        for (size_t k = 0; k < planes.size(); ++k) {
+            if (done[k])
+                continue;
+            done[k] = true;
+            uint64_t pair = 0;
+            if (planes[k].elem_bytes <= 4 && 2 * planes[k].elem_bytes <= stageWidth)
+                for (size_t q = k + 1; q < planes.size(); ++q)
+                    if (!done[q] && planes[q].elem_bytes == planes[k].elem_bytes) {
+                        pair = planes[q].data;
+                        done[q] = true;
+                        break;
+                    }
+            move(planes[k].data, pair, planes[k].elem_bytes, false);
+        }
+        move(d.perm, 0, 4, true);
         // the live count: *count within the live prefix, else the dead key's first slot
         const uint32_t* live = within ? count : c.hist + size_t(d.classes) * c.tiles;
         classIdentityKernel<<<streamGrid(d.n), kThreads, 0, s>>>(reinterpret_cast<int32_t*>(d.index_map), live, fire,

@@ -25,7 +25,9 @@ def _host(n, K, seed, p_drop):
     cls = g.integers(0, K + 2, n).astype(np.uint8)  # some past K: clamped to K - 1
     return [g.standard_normal(n), (g.random(n) < p_drop).astype(np.uint8), cls,
             g.integers(-2**15, 2**15 - 1, n, dtype=np.int64).astype(np.int16),
-            g.standard_normal(n) + 1j * g.standard_normal(n)]
+            g.standard_normal(n) + 1j * g.standard_normal(n),
+            g.standard_normal(n).astype(np.float32),                            # a pair of 4-byte planes,
+            g.integers(-2**31, 2**31 - 1, n, dtype=np.int64).astype(np.int32)]  # moved together
 
 
 def _cells(n, count, span, K):
