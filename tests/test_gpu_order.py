@@ -117,3 +117,52 @@ def test_ordered_launch_replays_in_a_cuda_graph(eb, orc):
         rep = runner.report(s)
         assert (rep.finished, rep.steps, rep.step_sum) == (fin, longest, total)
     del g
+
+
+def test_large_ordered_launch_eager_and_captured(eb, orc):
+    """A batch of 2^22 + 12345 samples (128 full runs of 32768 and a ragged one, some
+    samples terminated before the run): the oracle's bits for every plane, the mask and
+    the report, called eagerly and replayed twice from a CUDA graph."""
+    n = (1 << 22) + 12345
+    rng = np.random.default_rng(12)
+    om, te = rng.uniform(1, 3, n), 10.0 ** rng.uniform(-2, 0.3, n)
+    x0 = rng.normal(1, 0.1, n)
+    mask0 = (rng.random(n) < 0.02).astype(np.uint8)
+    d_x0 = torch.from_numpy(x0).cuda()
+    d_m0 = torch.from_numpy(mask0).cuda()
+    planes = dict(omega=torch.from_numpy(om).cuda(), t_end=torch.from_numpy(te).cuda(), dt=1e-3,
+                  x=d_x0.clone(), v=torch.zeros(n, dtype=torch.float64, device="cuda"),
+                  t=torch.zeros(n, dtype=torch.float64, device="cuda"))
+    term = d_m0.clone()
+    runner = eb.until_done(eb.oscillator, max_steps=2500, mode="persist", fma=True, terminated=term, **planes)
+    st = [x0.copy(), np.zeros(n), np.zeros(n), mask0.copy()]
+    _, fin, longest, total = orc.oscillator_run(om, *st, t_end=te, dt=1e-3, max_steps=2500, fused=True)
+
+    def reset():
+        planes["x"].copy_(d_x0)
+        planes["v"].zero_()
+        planes["t"].zero_()
+        term.copy_(d_m0)
+
+    def check(rep):
+        dev = [planes[k].cpu().numpy() for k in ("x", "v", "t")] + [term.cpu().numpy()]
+        for a, b, name in zip(dev, st, ("x", "v", "t", "terminated")):
+            assert a.tobytes() == b.tobytes(), name
+        assert (rep.finished, rep.steps, rep.step_sum) == (fin, longest, total)
+
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        reset()
+        runner.launch(s)
+    s.synchronize()
+    check(runner.report(s))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        runner.launch(s)
+    for _ in range(2):
+        reset()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        check(runner.report(s))
+    del g
