@@ -1023,15 +1023,16 @@ EB_API eagle_backend_status eagle_backend_x_b200_compact_sum(struct eagle_backen
 // ---------------------------------------------- compact-then-sum across ranks
 //
 // The one-device call above, cut where the ranks must exchange: _count runs the
-// front end (keep bitmap, tile counts and offsets, this rank's count); the caller
-// all-gathers the counts; _leaves forms this rank's plan from them on the device,
-// places the leaf starts in the concatenation's leaves, sums every leaf that starts
-// and ends here with the same dense and sparse passes (their partials written out,
-// not joined), and copies out this rank's first 4095 survivors and the part of the
-// leaf that straddles into the next ranks; the caller all-gathers the heads;
-// _straddle sums that leaf from its part here and the later ranks' heads. The leaf
-// partials and counts then go through eagle_backend_x_b200_ragged_fold. The kept
-// values are never written out, as in the one-device call.
+// front end (keep bitmap, tile counts and offsets, this rank's count); _head writes
+// this rank's head block (its first 4095 survivors, selected by a CTA per bitmap tile,
+// and its count); the caller all-gathers the head blocks; _leaves forms this rank's
+// plan from the gathered counts on the device, places the leaf starts in the
+// concatenation's leaves, sums every leaf that starts and ends here with the same
+// dense and sparse passes (their partials written out, not joined) and selects the
+// part of the leaf that straddles into the next ranks; _straddle sums that leaf from
+// its part here and the later ranks' heads and closes the partial block with the leaf
+// count. The caller all-gathers the partial blocks, and eagle_backend_x_b200_ragged_fold
+// joins them. The kept values are never written out, as in the one-device call.
 
 namespace eb {
 namespace {
