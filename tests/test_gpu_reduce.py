@@ -170,6 +170,29 @@ def test_captured_replay_follows_the_input(eb, orc):
         assert _same(red.out.cpu().numpy(), orc.reduce(y))
 
 
+def test_leaf_by_leaf_replay_follows_the_input(eb, orc):
+    """The leaf-by-leaf kernel (one column of more leaves than the device holds CTAs)
+    captured in a CUDA graph: each replay zeroes its chunk counters first and gives the
+    oracle's bits for the plane's current values."""
+    n = (1 << 22) + 37
+    xd = _dev(orc.corpus(n, 21))
+    red = eb.Reducer(xd, pair_out=True)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        red(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        red(s)
+    for seed in (22, 23, 24):
+        y = orc.corpus(n, seed)
+        xd.copy_(torch.from_numpy(y))
+        g.replay()
+        torch.cuda.synchronize()
+        assert _same(red.out.cpu().numpy(), orc.reduce(y, pair_out=True)), seed
+    del g
+
+
 def test_chunk_partials_combine_to_the_whole(eb, orc):
     """Aligned chunks (leafSize * 2^q) are subtrees: their PAIR_OUT partials combined
     by the pairwise levels give the bits of the whole (canonical.h:30-32, :424-439)."""
