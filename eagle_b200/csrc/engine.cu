@@ -475,8 +475,11 @@ void launchEngine(Engine& e, cudaStream_t s)
     }
     // persist / fused: zero the run words, count the mask, one launch
     Cells* c = e.cells;
-    cudaCheck(cudaMemsetAsync(&c->finished, 0, sizeof(uint32_t), s), "cudaMemsetAsync");
-    cudaCheck(cudaMemsetAsync(&c->next, 0, offsetof(Cells, stepsum64) + sizeof(c->stepsum64) - offsetof(Cells, next), s),
+    // one memset from finished through stepsum64 (newly, err and total between them are
+    // the band schedule's; the persist and fused report reads none of them)
+    static_assert(offsetof(Cells, finished) < offsetof(Cells, next), "finished precedes the run words");
+    cudaCheck(cudaMemsetAsync(&c->finished, 0,
+                  offsetof(Cells, stepsum64) + sizeof(c->stepsum64) - offsetof(Cells, finished), s),
         "cudaMemsetAsync");
     const bool persist = e.mode == EAGLE_B200_MODE_PERSIST;
     // the ordered persist launch counts the mask in its claim order's key pass
