@@ -1180,7 +1180,10 @@ def reorder_line(ctx, args):
                                             "kept run written in place, its dropped run staged and copied back "
                                             "((4 - 2p) element bytes a slot), perm likewise with inv and "
                                             "index_map written, the mask read by the scan"}},
-            "gpu_launches": (1 + 2 * 7 + 1) + (3 + 2 * 8 + 2), "clocks": clocks.summary()}
+            # reorder: scan, 5 float64 planes x (place, copy back), the uint8 pair, perm, finish;
+            # class sort: histogram, scan, 5 x (copy, place), the uint8 pair (2 copies, 1 place),
+            # perm (copy, place), identity, finish
+            "gpu_launches": (1 + 2 * 5 + 2 + 2 + 1) + (2 + 2 * 5 + 3 + 2 + 2), "clocks": clocks.summary()}
 
 
 def probe_line(ctx, args):
