@@ -491,6 +491,40 @@ void withElem(uint32_t bytes, F&& f)
     }
 }
 
+/** One move of the reorder: a plane, or two planes of one element size (``second``
+ *  nonzero) moved together. */
+struct PlaneMove {
+    uint64_t first, second;
+    uint32_t elem;
+};
+
+uint32_t widestOf(const std::vector<eagle_backend_reorder_plane>& p);
+
+/** The planes' moves: planes of one element size up to 4 bytes paired (in table
+ *  order) when both fit the stage one after the other, which holds n x max(widest
+ *  element, 4) bytes; the rest one by one. */
+std::vector<PlaneMove> pairPlanes(const std::vector<eagle_backend_reorder_plane>& planes)
+{
+    const uint32_t stageWidth = std::max<uint32_t>(widestOf(planes), 4u);
+    std::vector<bool> done(planes.size(), false);
+    std::vector<PlaneMove> moves;
+    for (size_t k = 0; k < planes.size(); ++k) {
+        if (done[k])
+            continue;
+        done[k] = true;
+        PlaneMove m{planes[k].data, 0, planes[k].elem_bytes};
+        if (m.elem <= 4 && 2 * m.elem <= stageWidth)
+            for (size_t q = k + 1; q < planes.size(); ++q)
+                if (!done[q] && planes[q].elem_bytes == m.elem) {
+                    m.second = planes[q].data;
+                    done[q] = true;
+                    break;
+                }
+        moves.push_back(m);
+    }
+    return moves;
+}
+
 /** The plane table, checked as eagle checks it (Reorder.h checkReorder). */
 std::vector<eagle_backend_reorder_plane> planesOf(const eagle_backend_reorder_desc& d, const char* who,
     bool needMask)
@@ -968,22 +1002,8 @@ EB_API eagle_backend_status eagle_backend_reorder_device(struct eagle_backend_re
                 launchCheck(who);
             });
         };
-        const uint32_t stageWidth = std::max<uint32_t>(widestOf(planes), 4u);  // stage bytes per slot
-        std::vector<bool> done(planes.size(), false);
-        for (size_t k = 0; k < planes.size(); ++k) {
-            if (done[k])
-                continue;
-            done[k] = true;
-            uint64_t pair = 0;
-            if (planes[k].elem_bytes <= 4 && 2 * planes[k].elem_bytes <= stageWidth)
-                for (size_t q = k + 1; q < planes.size(); ++q)
-                    if (!done[q] && planes[q].elem_bytes == planes[k].elem_bytes) {
-                        pair = planes[q].data;
-                        done[q] = true;
-                        break;
-                    }
-            move(planes[k].data, pair, planes[k].elem_bytes, false);
-        }
+        for (const auto& m : pairPlanes(planes))
+            move(m.first, m.second, m.elem, false);
         move(d.perm, 0, 4, true);
         reorderFinishKernel<<<1, 1, 0, s>>>(a.cnt, a.err, count, span, fire);
         launchCheck(who);
@@ -1122,22 +1142,8 @@ EB_API eagle_backend_status eagle_backend_reorder_classes_device(struct eagle_ba
                 launchCheck(who);
             });
         };
-        const uint32_t stageWidth = std::max<uint32_t>(widestOf(planes), 4u);  // stage bytes per slot
-        std::vector<bool> done(planes.size(), false);
-        for (size_t k = 0; k < planes.size(); ++k) {
-            if (done[k])
-                continue;
-            done[k] = true;
-            uint64_t pair = 0;
-            if (planes[k].elem_bytes <= 4 && 2 * planes[k].elem_bytes <= stageWidth)
-                for (size_t q = k + 1; q < planes.size(); ++q)
-                    if (!done[q] && planes[q].elem_bytes == planes[k].elem_bytes) {
-                        pair = planes[q].data;
-                        done[q] = true;
-                        break;
-                    }
-            move(planes[k].data, pair, planes[k].elem_bytes, false);
-        }
+        for (const auto& m : pairPlanes(planes))
+            move(m.first, m.second, m.elem, false);
         move(d.perm, 0, 4, true);
         // the live count: *count within the live prefix, else the dead key's first slot
         const uint32_t* live = within ? count : c.hist + size_t(d.classes) * c.tiles;
