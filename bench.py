@@ -69,6 +69,9 @@ def _args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-chunks", type=int, default=8)
     p.add_argument("--no-cpu", action="store_true", help="skip the oracle runs (parity and CPU baseline)")
+    p.add_argument("--exchange", action="store_true",
+                   help="at one GPU, run the multi-rank paths through a one-rank NCCL group (to time and profile "
+                        "their exchanges)")
     return p.parse_args()
 
 
@@ -211,9 +214,12 @@ class _Clocks:
 
 
 class Ctx:
-    """One rank's view: its device, stream and process group (None at N = 1)."""
+    """One rank's view: its device, stream and process group (None at N = 1, unless
+    ``exchange``: then a one-rank NCCL group, so that the multi-rank paths -- their
+    collectives and device-side exchanges -- run, and can be timed and profiled, on
+    one GPU)."""
 
-    def __init__(self):
+    def __init__(self, exchange: bool = False):
         import torch
 
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -222,9 +228,13 @@ class Ctx:
         torch.cuda.set_device(self.local)
         self.dev = torch.device("cuda", self.local)
         self.dist = None
-        if self.world > 1:
+        if self.world > 1 or exchange:
             import torch.distributed as dist
 
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29541")
+            os.environ.setdefault("RANK", str(self.rank))
+            os.environ.setdefault("WORLD_SIZE", str(self.world))
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=self.dev)
             self.dist = dist
         self.stream = torch.cuda.current_stream()
@@ -1236,7 +1246,7 @@ def main():
         reference(args)
         return
     _log("start")
-    ctx = Ctx()
+    ctx = Ctx(exchange=args.exchange)
     _log(f"process group ready ({ctx.world} ranks)")
     if args.workload != "oscillator":
         one_workload(ctx, args)
